@@ -1,0 +1,518 @@
+// f32 model primitives on sm_100a, one device kernel per entry of the
+// reference's C ABI (kernels/kernels.h:12-28, Vx bodies in kernels/kernels.vx).
+// Exported with device pointers as glmvx_<op>(..., stream).
+//
+// Numerics: element-wise ops use the reference's operation order with IEEE
+// division and square root (no fast-math).  Reductions (dot products, norms,
+// softmax sums) run as parallel trees in f32, so they agree with the
+// reference's ordered sums to rounding, not bit for bit.  The router's
+// selection and top-k's ordering are exact functions of their scores.
+#include <algorithm>
+#include <cfloat>
+
+#include "common.cuh"
+
+namespace glmvx {
+
+__device__ __forceinline__ float sigmoid_ref(float x) {  // kernels/kernels.vx:8-15
+    if (x >= 0.0f) return 1.0f / (1.0f + expf(0.0f - x));
+    const float z = expf(x);
+    return z / (1.0f + z);
+}
+
+// Block-wide sum for blockDim.x == 256 (8 warps); result broadcast to all.
+__device__ __forceinline__ float block_sum_256(float v, float *scratch) {
+    v = warp_sum(v);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    __syncthreads();
+    if (lane == 0) scratch[warp] = v;
+    __syncthreads();
+    float t = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) t += scratch[i];
+    return t;
+}
+
+__device__ __forceinline__ float block_max_256(float v, float *scratch) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    __syncthreads();
+    if (lane == 0) scratch[warp] = v;
+    __syncthreads();
+    float t = scratch[0];
+#pragma unroll
+    for (int i = 1; i < 8; ++i) t = fmaxf(t, scratch[i]);
+    return t;
+}
+
+// ---- f32 matvec / matmul_nt: one warp per weight row, TB tokens per slice.
+template <int TB>
+__global__ void __launch_bounds__(256)
+    f32_rows_kernel(float *__restrict__ out, const float *__restrict__ wt, const float *__restrict__ x, int rows,
+                    int cols, int batch, int out_row_major_tokens) {
+    const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (row >= rows) return;
+    const int t0 = blockIdx.y * TB, nt = min(TB, batch - t0);
+    const float *wr = wt + static_cast<size_t>(row) * cols;
+    float acc[TB];
+#pragma unroll
+    for (int t = 0; t < TB; ++t) acc[t] = 0.0f;
+    const bool vec = ((reinterpret_cast<uintptr_t>(wr) | reinterpret_cast<uintptr_t>(x)) & 15) == 0 && (cols & 3) == 0;
+    if (vec) {
+        for (int c = lane * 4; c < cols; c += 128) {
+            const float4 wv = __ldg(reinterpret_cast<const float4 *>(wr + c));
+#pragma unroll
+            for (int t = 0; t < TB; ++t)
+                if (t < nt) {
+                    const float4 xv = __ldg(reinterpret_cast<const float4 *>(x + static_cast<size_t>(t0 + t) * cols + c));
+                    acc[t] = fmaf(wv.x, xv.x, acc[t]);
+                    acc[t] = fmaf(wv.y, xv.y, acc[t]);
+                    acc[t] = fmaf(wv.z, xv.z, acc[t]);
+                    acc[t] = fmaf(wv.w, xv.w, acc[t]);
+                }
+        }
+    } else {
+        for (int c = lane; c < cols; c += 32) {
+            const float wv = __ldg(wr + c);
+#pragma unroll
+            for (int t = 0; t < TB; ++t)
+                if (t < nt) acc[t] = fmaf(wv, __ldg(x + static_cast<size_t>(t0 + t) * cols + c), acc[t]);
+        }
+    }
+#pragma unroll
+    for (int t = 0; t < TB; ++t) {
+        const float v = warp_sum(acc[t]);
+        if (lane == 0 && t < nt) {
+            if (out_row_major_tokens) out[static_cast<size_t>(t0 + t) * rows + row] = v;
+            else out[static_cast<size_t>(row) * batch + t0 + t] = v;
+        }
+    }
+}
+
+int32_t f32_rows(float *out, const float *w, const float *x, int rows, int cols, int batch, bool token_major,
+                 cudaStream_t s) {
+    if (rows == 0 || batch == 0) return kOk;
+    if (batch <= 1) {
+        f32_rows_kernel<1><<<dim3((rows + 7) / 8, 1), 256, 0, s>>>(out, w, x, rows, cols, batch, token_major);
+    } else {
+        f32_rows_kernel<8><<<dim3((rows + 7) / 8, (batch + 7) / 8), 256, 0, s>>>(out, w, x, rows, cols, batch,
+                                                                                token_major);
+    }
+    return launch_status("f32_rows_kernel");
+}
+
+// ---- row-wise norms and softmax: one 256-thread CTA per row.
+__global__ void __launch_bounds__(256) rmsnorm_kernel(float *out, const float *x, const float *w, int n, float eps) {
+    __shared__ float scratch[8];
+    const float *xr = x + static_cast<size_t>(blockIdx.x) * n;
+    float *orow = out + static_cast<size_t>(blockIdx.x) * n;
+    float ss = 0.0f;
+    for (int i = threadIdx.x; i < n; i += 256) ss = fmaf(xr[i], xr[i], ss);
+    ss = block_sum_256(ss, scratch);
+    const float inv = 1.0f / sqrtf(ss / static_cast<float>(n) + eps);
+    for (int i = threadIdx.x; i < n; i += 256) orow[i] = __fmul_rn(__fmul_rn(xr[i], inv), w[i]);
+}
+
+__global__ void __launch_bounds__(256)
+    layernorm_kernel(float *out, const float *x, const float *w, const float *b, int n, float eps) {
+    __shared__ float scratch[8];
+    const float *xr = x + static_cast<size_t>(blockIdx.x) * n;
+    float *orow = out + static_cast<size_t>(blockIdx.x) * n;
+    float s = 0.0f;
+    for (int i = threadIdx.x; i < n; i += 256) s += xr[i];
+    const float mean = block_sum_256(s, scratch) / static_cast<float>(n);
+    float v = 0.0f;
+    for (int i = threadIdx.x; i < n; i += 256) {
+        const float d = xr[i] - mean;
+        v = fmaf(d, d, v);
+    }
+    const float inv = 1.0f / sqrtf(block_sum_256(v, scratch) / static_cast<float>(n) + eps);
+    for (int i = threadIdx.x; i < n; i += 256)
+        orow[i] = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(xr[i], mean), inv), w[i]), b[i]);
+}
+
+__global__ void __launch_bounds__(256) softmax_kernel(float *out, const float *x, int n) {
+    __shared__ float scratch[8];
+    const float *xr = x + static_cast<size_t>(blockIdx.x) * n;
+    float *orow = out + static_cast<size_t>(blockIdx.x) * n;
+    float m = -INFINITY;
+    for (int i = threadIdx.x; i < n; i += 256) m = fmaxf(m, xr[i]);
+    m = block_max_256(m, scratch);
+    float s = 0.0f;
+    for (int i = threadIdx.x; i < n; i += 256) {
+        const float e = expf(xr[i] - m);
+        orow[i] = e;
+        s += e;
+    }
+    s = block_sum_256(s, scratch);
+    for (int i = threadIdx.x; i < n; i += 256) orow[i] = orow[i] / s;
+}
+
+// ---- element-wise
+__global__ void swiglu_kernel(float *out, const float *g, const float *u, int64_t n) {
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const float gv = g[i];
+        out[i] = __fmul_rn(__fmul_rn(gv, sigmoid_ref(gv)), u[i]);  // kernels/kernels.vx:58
+    }
+}
+
+__global__ void add_kernel(float *out, const float *a, const float *b, int64_t n) {
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+        out[i] = __fadd_rn(a[i], b[i]);
+}
+
+__global__ void axpy_kernel(float *out, const float *x, float alpha, int64_t n) {
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+        out[i] = __fadd_rn(out[i], __fmul_rn(alpha, x[i]));
+}
+
+// kernels/kernels.vx:226-248: rotate adjacent pairs at [offset, offset+rope_dim).
+// One thread owns a whole pair (reads both, then writes both), so out == x
+// (in place, allowed by kernels/kernels.h:17) is race-free.
+__global__ void rope_offset_kernel(float *out, const float *x, const float *cs, const float *sn, int heads,
+                                   int head_dim, int rope_dim, int offset) {
+    const int64_t total = static_cast<int64_t>(heads) * head_dim;
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int d = static_cast<int>(i % head_dim);
+        if (d < offset || d >= offset + rope_dim) {
+            out[i] = x[i];
+        } else if (((d - offset) & 1) == 0) {
+            const int p = (d - offset) >> 1;
+            const float a = x[i], b = x[i + 1];
+            out[i] = __fsub_rn(__fmul_rn(a, cs[p]), __fmul_rn(b, sn[p]));
+            out[i + 1] = __fadd_rn(__fmul_rn(a, sn[p]), __fmul_rn(b, cs[p]));
+        }
+    }
+}
+
+// kernels/kernels.vx:425-441: interleaved pairs -> [even half | odd half].
+__global__ void rope_glm_kernel(float *out, const float *x, const float *cs, const float *sn, int heads, int dim) {
+    const int half = dim / 2;
+    const int64_t total = static_cast<int64_t>(heads) * half;
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t h = i / half;
+        const int p = static_cast<int>(i % half);
+        const float a = x[h * dim + 2 * p], b = x[h * dim + 2 * p + 1];
+        out[h * dim + p] = __fsub_rn(__fmul_rn(a, cs[p]), __fmul_rn(b, sn[p]));
+        out[h * dim + half + p] = __fadd_rn(__fmul_rn(b, cs[p]), __fmul_rn(a, sn[p]));
+    }
+}
+
+// ---- router (kernels/kernels.vx:252-279): one 256-thread CTA per token.
+// score = sigmoid(logit)+bias picks experts (ties -> lower id); weights are
+// the picked sigmoids / (ordered sum + 1e-20) * scale.
+constexpr int kMaxRouterExperts = 4096, kMaxRouterK = 64;
+
+__global__ void __launch_bounds__(256)
+    router_kernel(int32_t *ids, float *weights, const float *logits, const float *bias, int experts, int k,
+                  float scale) {
+    __shared__ float score[kMaxRouterExperts];
+    __shared__ float wbest[8];
+    __shared__ int ibest[8];
+    __shared__ int chosen[kMaxRouterK];
+    const float *lr = logits + static_cast<size_t>(blockIdx.x) * experts;
+    for (int e = threadIdx.x; e < experts; e += 256) score[e] = sigmoid_ref(lr[e]) + bias[e];
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int slot = 0; slot < k; ++slot) {
+        float bv = -INFINITY;
+        int bi = INT_MAX;
+        for (int e = threadIdx.x; e < experts; e += 256) {
+            const float v = score[e];
+            if (v > bv || (v == bv && e < bi)) {  // strict >, lower id wins ties
+                bv = v;
+                bi = e;
+            }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (ov > bv || (ov == bv && oi < bi)) {
+                bv = ov;
+                bi = oi;
+            }
+        }
+        if (lane == 0) {
+            wbest[warp] = bv;
+            ibest[warp] = bi;
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            float v = wbest[0];
+            int i = ibest[0];
+            for (int q = 1; q < 8; ++q)
+                if (wbest[q] > v || (wbest[q] == v && ibest[q] < i)) {
+                    v = wbest[q];
+                    i = ibest[q];
+                }
+            chosen[slot] = i;
+            score[i] = -INFINITY;  // exclude from later slots
+        }
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) {
+        float probs[kMaxRouterK];
+        float total = 0.0f;
+        for (int slot = 0; slot < k; ++slot) {
+            probs[slot] = sigmoid_ref(lr[chosen[slot]]);
+            total = total + probs[slot];
+        }
+        total = total + 1e-20f;
+        for (int slot = 0; slot < k; ++slot) {
+            ids[static_cast<size_t>(blockIdx.x) * k + slot] = chosen[slot];
+            weights[static_cast<size_t>(blockIdx.x) * k + slot] = probs[slot] / total * scale;
+        }
+    }
+}
+
+// ---- exact stable top-k (kernels/kernels.vx:281-355) by sorting composite
+// keys: descending score (with -0 folded onto +0), then ascending index.
+__device__ __forceinline__ uint64_t topk_key(float v, int32_t i) {
+    uint32_t b = __float_as_uint(v == 0.0f ? 0.0f : v);
+    b = (b & 0x80000000u) ? ~b : (b | 0x80000000u);  // ascending float order
+    return (static_cast<uint64_t>(~b) << 32) | static_cast<uint32_t>(i);  // ascending key = descending score
+}
+
+// Single-CTA bitonic sort of n2 (power of two) keys in `keys` (shared or global).
+__device__ void bitonic_sort(uint64_t *keys, int n2) {
+    for (int size = 2; size <= n2; size <<= 1) {
+        for (int stride = size >> 1; stride > 0; stride >>= 1) {
+            for (int i = threadIdx.x; i < n2 / 2; i += blockDim.x) {
+                const int lo = 2 * i - (i & (stride - 1));
+                const int hi = lo + stride;
+                const bool up = (lo & size) == 0;
+                const uint64_t a = keys[lo], b = keys[hi];
+                if ((a > b) == up) {
+                    keys[lo] = b;
+                    keys[hi] = a;
+                }
+            }
+            __syncthreads();
+        }
+    }
+}
+
+constexpr int kTopkSmemKeys = 4096;  // 32 KB of static shared memory
+
+__global__ void __launch_bounds__(1024)
+    topk_kernel(int32_t *indices, const float *scores, int n, int k, uint64_t *global_keys, int n2) {
+    __shared__ uint64_t skeys[kTopkSmemKeys];
+    uint64_t *keys = n2 <= kTopkSmemKeys ? skeys : global_keys;
+    for (int i = threadIdx.x; i < n2; i += blockDim.x) keys[i] = i < n ? topk_key(scores[i], i) : ~0ull;
+    __syncthreads();
+    bitonic_sort(keys, n2);
+    for (int i = threadIdx.x; i < k; i += blockDim.x) indices[i] = static_cast<int32_t>(keys[i] & 0xffffffffu);
+}
+
+// ---- DSA index scores (kernels/kernels.vx:404-421): one warp per token.
+__global__ void __launch_bounds__(256)
+    index_scores_kernel(float *out, const float *q, const float *keys, const float *w, int tokens, int heads,
+                        int dim, float qk_scale) {
+    const int t = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (t >= tokens) return;
+    const float *kr = keys + static_cast<size_t>(t) * dim;
+    float total = 0.0f;
+    for (int h = 0; h < heads; ++h) {
+        const float *qh = q + static_cast<size_t>(h) * dim;
+        float dot = 0.0f;
+        for (int d = lane; d < dim; d += 32) dot = fmaf(qh[d], kr[d], dot);
+        dot = warp_sum(dot);
+        const float s = dot * qk_scale;
+        if (s > 0.0f) total = fmaf(w[h], s, total);
+    }
+    if (lane == 0) out[t] = total;
+}
+
+// ---- single-query attention over all or selected tokens
+// (kernels/kernels.vx:358-400): scores -> softmax -> weighted value sum, one
+// CTA.  `scratch` holds one f32 per attended token.  A selected id outside
+// [0, tokens) is never dereferenced: it sets *bad and the host rejects the
+// call, as the reference does before touching memory (kernels/kernels.vx:385).
+__global__ void __launch_bounds__(256)
+    attention_kernel(float *out, float *scratch, const float *q, const float *keys, const float *values,
+                     const int32_t *selected, int count, int tokens, int dim, int value_dim, float scale,
+                     int32_t *bad) {
+    __shared__ float red[8];
+    __shared__ int any_bad;
+    if (threadIdx.x == 0) any_bad = 0;
+    __syncthreads();
+    if (selected)
+        for (int j = threadIdx.x; j < count; j += 256)
+            if (selected[j] < 0 || selected[j] >= tokens) any_bad = 1;
+    __syncthreads();
+    if (any_bad) {
+        if (threadIdx.x == 0 && bad) *bad = 1;
+        return;
+    }
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int j = warp; j < count; j += 8) {
+        const int t = selected ? selected[j] : j;
+        const float *kr = keys + static_cast<size_t>(t) * dim;
+        float dot = 0.0f;
+        for (int d = lane; d < dim; d += 32) dot = fmaf(q[d], kr[d], dot);
+        dot = warp_sum(dot);
+        if (lane == 0) scratch[j] = dot * scale;
+    }
+    __syncthreads();
+    float m = -INFINITY;
+    for (int j = threadIdx.x; j < count; j += 256) m = fmaxf(m, scratch[j]);
+    m = block_max_256(m, red);
+    float s = 0.0f;
+    for (int j = threadIdx.x; j < count; j += 256) {
+        const float e = expf(scratch[j] - m);
+        scratch[j] = e;
+        s += e;
+    }
+    s = block_sum_256(s, red);
+    for (int j = threadIdx.x; j < count; j += 256) scratch[j] = scratch[j] / s;
+    __syncthreads();
+    for (int d = threadIdx.x; d < value_dim; d += 256) {
+        float acc = 0.0f;
+        for (int j = 0; j < count; ++j) {
+            const int t = selected ? selected[j] : j;
+            acc = fmaf(scratch[j], values[static_cast<size_t>(t) * value_dim + d], acc);
+        }
+        out[d] = acc;
+    }
+}
+
+static int ew_grid(int64_t n) { return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, 4 * 148 * 8))); }
+
+}  // namespace glmvx
+
+using namespace glmvx;
+#define S_ (cudaStream_t) stream
+
+GLMVX_EXPORT int32_t glmvx_matvec_f32(float *out, const float *w, const float *x, int32_t rows, int32_t cols,
+                                      void *stream) {
+    if (rows < 0 || cols < 0) return set_error("matvec dims"), kInvalid;
+    if (cols == 0) {
+        if (rows) GLMVX_CUDA(cudaMemsetAsync(out, 0, sizeof(float) * rows, S_));
+        return kOk;
+    }
+    return f32_rows(out, w, x, rows, cols, 1, true, S_);
+}
+
+// out[m,n] = a[m,k] . b[n,k]^T (kernels/kernels.vx:135-218).
+GLMVX_EXPORT int32_t glmvx_matmul_nt(float *out, const float *a, const float *b, int32_t m, int32_t n, int32_t k,
+                                     void *stream) {
+    if (m < 0 || n < 0 || k < 0) return set_error("matmul_nt dims"), kInvalid;
+    if (k == 0) {
+        if (m && n) GLMVX_CUDA(cudaMemsetAsync(out, 0, sizeof(float) * m * n, S_));
+        return kOk;
+    }
+    return f32_rows(out, b, a, n, k, m, true, S_);
+}
+
+GLMVX_EXPORT int32_t glmvx_rmsnorm(float *out, const float *x, const float *w, int32_t rows, int32_t n, float eps,
+                                   void *stream) {
+    if (n <= 0 || eps <= 0.0f || rows < 0) return set_error("rmsnorm dims/eps"), kInvalid;
+    if (rows) rmsnorm_kernel<<<rows, 256, 0, S_>>>(out, x, w, n, eps);
+    return launch_status("rmsnorm_kernel");
+}
+
+GLMVX_EXPORT int32_t glmvx_layernorm(float *out, const float *x, const float *w, const float *b, int32_t rows,
+                                     int32_t n, float eps, void *stream) {
+    if (n <= 0 || eps <= 0.0f || rows < 0) return set_error("layernorm dims/eps"), kInvalid;
+    if (rows) layernorm_kernel<<<rows, 256, 0, S_>>>(out, x, w, b, n, eps);
+    return launch_status("layernorm_kernel");
+}
+
+GLMVX_EXPORT int32_t glmvx_softmax(float *out, const float *x, int32_t rows, int32_t n, void *stream) {
+    if (n <= 0 || rows < 0) return set_error("softmax dims"), kInvalid;
+    if (rows) softmax_kernel<<<rows, 256, 0, S_>>>(out, x, n);
+    return launch_status("softmax_kernel");
+}
+
+GLMVX_EXPORT int32_t glmvx_swiglu(float *out, const float *gate, const float *up, int64_t n, void *stream) {
+    if (n < 0) return set_error("swiglu n"), kInvalid;
+    if (n) swiglu_kernel<<<ew_grid(n), 256, 0, S_>>>(out, gate, up, n);
+    return launch_status("swiglu_kernel");
+}
+
+GLMVX_EXPORT int32_t glmvx_add(float *out, const float *a, const float *b, int64_t n, void *stream) {
+    if (n < 0) return set_error("add n"), kInvalid;
+    if (n) add_kernel<<<ew_grid(n), 256, 0, S_>>>(out, a, b, n);
+    return launch_status("add_kernel");
+}
+
+GLMVX_EXPORT int32_t glmvx_axpy(float *out, const float *x, float alpha, int64_t n, void *stream) {
+    if (n < 0) return set_error("axpy n"), kInvalid;
+    if (n) axpy_kernel<<<ew_grid(n), 256, 0, S_>>>(out, x, alpha, n);
+    return launch_status("axpy_kernel");
+}
+
+GLMVX_EXPORT int32_t glmvx_rope_offset(float *out, const float *x, const float *cs, const float *sn, int32_t heads,
+                                       int32_t head_dim, int32_t rope_dim, int32_t offset, void *stream) {
+    if (heads < 0 || rope_dim < 0 || offset < 0 || head_dim < rope_dim || offset > head_dim - rope_dim ||
+        rope_dim % 2 != 0)
+        return set_error("rope dims"), kInvalid;
+    const int64_t n = static_cast<int64_t>(heads) * head_dim;
+    if (n) rope_offset_kernel<<<ew_grid(n), 256, 0, S_>>>(out, x, cs, sn, heads, head_dim, rope_dim, offset);
+    return launch_status("rope_offset_kernel");
+}
+
+GLMVX_EXPORT int32_t glmvx_rope_glm(float *out, const float *x, const float *cs, const float *sn, int32_t heads,
+                                    int32_t dim, void *stream) {
+    if (heads < 0 || dim <= 0 || dim % 2 != 0) return set_error("rope_glm dims"), kInvalid;
+    const int64_t n = static_cast<int64_t>(heads) * (dim / 2);
+    if (n) rope_glm_kernel<<<ew_grid(n), 256, 0, S_>>>(out, x, cs, sn, heads, dim);
+    return launch_status("rope_glm_kernel");
+}
+
+// tokens x experts logits -> ids/weights [tokens, k].
+GLMVX_EXPORT int32_t glmvx_router(int32_t *ids, float *weights, const float *logits, const float *bias,
+                                  int32_t tokens, int32_t experts, int32_t k, float scale, void *stream) {
+    if (k <= 0 || experts < k || tokens < 0) return set_error("router k/experts"), kInvalid;
+    if (experts > kMaxRouterExperts || k > kMaxRouterK)
+        return set_error("GPU router supports at most %d experts and k <= %d", kMaxRouterExperts, kMaxRouterK),
+               kUnsupported;
+    if (tokens) router_kernel<<<tokens, 256, 0, S_>>>(ids, weights, logits, bias, experts, k, scale);
+    return launch_status("router_kernel");
+}
+
+// Scratch bytes glmvx_topk needs for n scores (0 when it sorts in shared memory).
+GLMVX_EXPORT int64_t glmvx_topk_scratch_bytes(int32_t n) {
+    int64_t n2 = 1;
+    while (n2 < n) n2 <<= 1;
+    return n2 <= kTopkSmemKeys ? 0 : n2 * 8;
+}
+
+GLMVX_EXPORT int32_t glmvx_topk(int32_t *indices, const float *scores, int32_t n, int32_t k, void *scratch,
+                                void *stream) {
+    if (n < 0 || k < 0 || n < k) return set_error("topk n/k"), kInvalid;
+    if (k == 0) return kOk;
+    int n2 = 1;
+    while (n2 < n) n2 <<= 1;
+    if (n2 > kTopkSmemKeys && !scratch) return set_error("topk needs scratch for n > %d", kTopkSmemKeys), kInvalid;
+    topk_kernel<<<1, 1024, 0, S_>>>(indices, scores, n, k, static_cast<uint64_t *>(scratch), n2);
+    return launch_status("topk_kernel");
+}
+
+GLMVX_EXPORT int32_t glmvx_index_scores(float *out, const float *q, const float *keys, const float *w,
+                                        int32_t tokens, int32_t heads, int32_t dim, float qk_scale, void *stream) {
+    if (tokens < 0 || heads <= 0 || dim <= 0) return set_error("index_scores dims"), kInvalid;
+    if (tokens) index_scores_kernel<<<(tokens + 7) / 8, 256, 0, S_>>>(out, q, keys, w, tokens, heads, dim, qk_scale);
+    return launch_status("index_scores_kernel");
+}
+
+// selected == nullptr attends to the first `count` tokens.  `bad` (device
+// int32, required when `selected` is given) is set to 1 when a selected id is
+// out of range; the kernel then writes nothing and the host must reject.
+GLMVX_EXPORT int32_t glmvx_attention(float *out, float *scratch, const float *q, const float *keys,
+                                     const float *values, const int32_t *selected, int32_t count, int32_t tokens,
+                                     int32_t dim, int32_t value_dim, float scale, int32_t *bad, void *stream) {
+    if (count <= 0 || tokens <= 0 || dim <= 0 || value_dim <= 0) return set_error("attention dims"), kInvalid;
+    if (!selected && count > tokens) return set_error("attention count > tokens"), kInvalid;
+    if (selected && !bad) return set_error("attention with selected ids needs a status word"), kInvalid;
+    attention_kernel<<<1, 256, 0, S_>>>(out, scratch, q, keys, values, selected, count, tokens, dim, value_dim,
+                                        scale, bad);
+    return launch_status("attention_kernel");
+}

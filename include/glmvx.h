@@ -1,0 +1,175 @@
+/*
+ * libglmvx_cuda.so -- B200 (sm_100a) packed-GGUF dequant GEMV/GEMM library.
+ *
+ * Two C ABIs, no C++ types, no exceptions across the boundary:
+ *
+ *  1. The reference's CPU kernel ABI, unchanged (kernels/kernels.h:12-53 of
+ *     gakonst/glm-vx).  HOST pointers; each call stages its inputs on the
+ *     GPU, runs the kernel and copies the result back.  Loading this library
+ *     with GLM_VX_LIBRARY=.../libglmvx_cuda.so makes the reference's own
+ *     kernels/packed.py and kernels/backend.py run on the B200.
+ *     Status: 0 ok, -1 rejected arguments (as the reference), -2 CUDA error,
+ *     -3 a kernel's bounded wait expired.  Message: glmvx_last_error().
+ *
+ *  2. A resident DEVICE-pointer ABI (glmvx_*), the one the GPU backend and the
+ *     benchmarks use: weights live in HBM, calls are asynchronous on the given
+ *     stream (NULL = legacy default stream).  It replaces the reference's
+ *     ctypes CUDA Driver API runtime and PTX entry points (gpu/runtime.py,
+ *     gpu/kernels.h, gpu/gemm.vx, gpu/fp8.vx).
+ *
+ * GGML kinds: 1 F16, 8 Q8_0, 10 Q2_K, 11 Q3_K, 12 Q4_K, 13 Q5_K, 14 Q6_K,
+ * 16 IQ2_XXS, 18 IQ3_XXS, 19 IQ1_S, 23 IQ4_XS (kernels/packed.py:14-19).
+ */
+#ifndef GLMVX_H
+#define GLMVX_H
+#include <stdint.h>
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ====================================================================== *
+ * 1. Reference CPU ABI served by the GPU (host pointers)                  *
+ * ====================================================================== */
+
+/* Packed weights.  Replaces kernels/kernels.h:193-207 (GLM_VX_PACKED_DECL),
+ * bodies kernels/packed.vx:154-470 and the generated batch_v2 exports
+ * (kernels/packed.vx:473ff).  half/table must be the reference's exact
+ * lookup tables (kernels/packed.py:27-37); they are verified, not used. */
+#define GLMVX_REFERENCE_PACKED_DECL(kind)                                                          \
+    int32_t glm_vx_packed_##kind(float *out, const uint8_t *w, const float *x, const float *half,   \
+                                 const uint8_t *table, int32_t rows, int32_t cols);                \
+    int32_t glm_vx_packed_batch_v2_##kind(float *out, const uint8_t *w, const float *x,            \
+                                          const float *half, const uint8_t *table, int32_t rows,  \
+                                          int32_t cols, int32_t batch);                            \
+    int32_t glm_vx_unpack_##kind(float *out, const uint8_t *w, const float *half,                   \
+                                 const uint8_t *table, int32_t blocks);
+GLMVX_REFERENCE_PACKED_DECL(f16)
+GLMVX_REFERENCE_PACKED_DECL(q8_0)
+GLMVX_REFERENCE_PACKED_DECL(q2_k)
+GLMVX_REFERENCE_PACKED_DECL(q3_k)
+GLMVX_REFERENCE_PACKED_DECL(q4_k)
+GLMVX_REFERENCE_PACKED_DECL(q5_k)
+GLMVX_REFERENCE_PACKED_DECL(q6_k)
+GLMVX_REFERENCE_PACKED_DECL(iq2_xxs)
+GLMVX_REFERENCE_PACKED_DECL(iq3_xxs)
+GLMVX_REFERENCE_PACKED_DECL(iq1_s)
+GLMVX_REFERENCE_PACKED_DECL(iq4_xs)
+#undef GLMVX_REFERENCE_PACKED_DECL
+
+/* f32 primitives.  Replace kernels/kernels.h:168-184 one for one
+ * (bodies kernels/kernels.vx:17-441). */
+int32_t glm_vx_rmsnorm(float *out, const float *x, const float *weight, int32_t n, float eps);
+int32_t glm_vx_layernorm(float *out, const float *x, const float *weight, const float *bias, int32_t n, float eps);
+int32_t glm_vx_softmax(float *out, const float *x, int32_t n);
+int32_t glm_vx_swiglu(float *out, const float *gate, const float *up, int32_t n);
+int32_t glm_vx_add(float *out, const float *a, const float *b, int32_t n);
+int32_t glm_vx_axpy(float *out, const float *x, float alpha, int32_t n);
+int32_t glm_vx_matvec(float *out, const float *weight, const float *x, int32_t rows, int32_t cols);
+int32_t glm_vx_matmul_nt(float *out, const float *a, const float *b, int32_t m, int32_t n, int32_t k);
+int32_t glm_vx_rope(float *out, const float *x, const float *cosine, const float *sine, int32_t heads,
+                    int32_t head_dim, int32_t rope_dim);
+int32_t glm_vx_router(int32_t *indices, float *weights, const float *logits, const float *bias, int32_t experts,
+                      int32_t k, float scale);
+int32_t glm_vx_topk(int32_t *indices, const float *scores, int32_t n, int32_t k);
+int32_t glm_vx_attention(float *out, float *scratch, const float *q, const float *keys, const float *values,
+                         int32_t tokens, int32_t dim, int32_t value_dim, float scale);
+int32_t glm_vx_sparse_attention(float *out, float *scratch, const float *q, const float *keys, const float *values,
+                                const int32_t *selected, int32_t count, int32_t tokens, int32_t dim,
+                                int32_t value_dim, float scale);
+int32_t glm_vx_rope_offset(float *out, const float *x, const float *cosine, const float *sine, int32_t heads,
+                           int32_t head_dim, int32_t rope_dim, int32_t offset);
+int32_t glm_vx_index_scores(float *out, const float *q, const float *keys, const float *weights, int32_t tokens,
+                            int32_t heads, int32_t dim, float qk_scale);
+int32_t glm_vx_rope_glm(float *out, const float *x, const float *cosine, const float *sine, int32_t heads,
+                        int32_t dim);
+
+/* ====================================================================== *
+ * 2. Resident device-pointer ABI                                          *
+ * ====================================================================== */
+
+/* Last error message of the calling thread ("" when none). */
+const char *glmvx_last_error(void);
+int32_t glmvx_version(void);
+
+/* Device, memory, streams, events, graphs.  Replace the ctypes Driver API
+ * runtime: CUDAContext (gpu/runtime.py:150-292), DeviceBuffer (:330-380),
+ * Stream (:564-600), Event (:611-663). */
+int32_t glmvx_device_count(int32_t *count);
+int32_t glmvx_set_device(int32_t device);
+int32_t glmvx_get_device(int32_t *device);
+int32_t glmvx_device_info(int32_t device, char *name, int32_t name_len, int32_t *cc, int32_t *sms,
+                          int64_t *l2_bytes, int64_t *total_mem, int32_t *smem_optin);
+int32_t glmvx_malloc(void **ptr, uint64_t bytes);
+int32_t glmvx_free(void *ptr);
+int32_t glmvx_host_alloc(void **ptr, uint64_t bytes); /* pinned host memory */
+int32_t glmvx_host_free(void *ptr);
+int32_t glmvx_memcpy_htod(void *dst, const void *src, uint64_t bytes, void *stream);
+int32_t glmvx_memcpy_dtoh(void *dst, const void *src, uint64_t bytes, void *stream);
+int32_t glmvx_memcpy_dtod(void *dst, const void *src, uint64_t bytes, void *stream);
+int32_t glmvx_memset(void *dst, int32_t value, uint64_t bytes, void *stream);
+int32_t glmvx_device_synchronize(void);
+int32_t glmvx_stream_create(void **stream);
+int32_t glmvx_stream_destroy(void *stream);
+int32_t glmvx_stream_synchronize(void *stream);
+int32_t glmvx_stream_wait_event(void *stream, void *event);
+int32_t glmvx_event_create(void **event);
+int32_t glmvx_event_destroy(void *event);
+int32_t glmvx_event_record(void *event, void *stream);
+int32_t glmvx_event_synchronize(void *event);
+int32_t glmvx_event_elapsed_ms(void *start, void *end, float *ms);
+int32_t glmvx_graph_begin(void *stream);
+int32_t glmvx_graph_end(void *stream, void **graph_exec);
+int32_t glmvx_graph_launch(void *graph_exec, void *stream);
+int32_t glmvx_graph_destroy(void *graph_exec);
+/* Reads and clears the device word kernels set when a bounded wait expires. */
+int32_t glmvx_check_device_error(int32_t *code);
+
+/* Fused packed dequant + matvec: out[rows] = W[rows,cols] . x[cols].
+ * Replaces glm_vx_packed_<kind> (kernels/packed.vx:154-470) for resident
+ * weights; the reference GPU backend had no packed entry (gpu/backend.py:56). */
+int32_t glmvx_packed_gemv(int32_t kind, float *out, const uint8_t *w, const float *x, int32_t rows, int32_t cols,
+                          void *stream);
+/* Small-batch: out[batch,rows] = x[batch,cols] . W^T, x row-major, batch <= 64.
+ * Replaces glm_vx_packed_batch_v2_<kind> (kernels/packed.vx:473ff). */
+int32_t glmvx_packed_gemm(int32_t kind, float *out, const uint8_t *w, const float *x, int32_t rows, int32_t cols,
+                          int32_t batch, void *stream);
+/* As glmvx_packed_gemm; *path reports the kernel taken
+ * (1 stream GEMV, 2 generic, 3 F16 element path). */
+int32_t glmvx_packed_gemm_path(int32_t kind, float *out, const uint8_t *w, const float *x, int32_t rows,
+                               int32_t cols, int32_t batch, void *stream, int32_t *path);
+/* Diagnostic decode of `blocks` reference blocks (F16: elements) to f32.
+ * Replaces glm_vx_unpack_<kind> (kernels/packed.vx:175-181 and siblings). */
+int32_t glmvx_unpack(int32_t kind, float *out, const uint8_t *w, int64_t blocks, void *stream);
+
+/* f32 primitives on device pointers.  Replace the reference PTX entries in
+ * gpu/kernels.h:7-115 (matvec, rmsnorm(_rows), softmax(_rows), swiglu,
+ * rope_glm, router, index_scores) and the CPU ones in kernels/kernels.h. */
+int32_t glmvx_matvec_f32(float *out, const float *w, const float *x, int32_t rows, int32_t cols, void *stream);
+int32_t glmvx_matmul_nt(float *out, const float *a, const float *b, int32_t m, int32_t n, int32_t k, void *stream);
+int32_t glmvx_rmsnorm(float *out, const float *x, const float *w, int32_t rows, int32_t n, float eps, void *stream);
+int32_t glmvx_layernorm(float *out, const float *x, const float *w, const float *b, int32_t rows, int32_t n,
+                        float eps, void *stream);
+int32_t glmvx_softmax(float *out, const float *x, int32_t rows, int32_t n, void *stream);
+int32_t glmvx_swiglu(float *out, const float *gate, const float *up, int64_t n, void *stream);
+int32_t glmvx_add(float *out, const float *a, const float *b, int64_t n, void *stream);
+int32_t glmvx_axpy(float *out, const float *x, float alpha, int64_t n, void *stream);
+int32_t glmvx_rope_offset(float *out, const float *x, const float *cosine, const float *sine, int32_t heads,
+                          int32_t head_dim, int32_t rope_dim, int32_t offset, void *stream);
+int32_t glmvx_rope_glm(float *out, const float *x, const float *cosine, const float *sine, int32_t heads,
+                       int32_t dim, void *stream);
+/* tokens rows of expert logits -> ids/weights [tokens,k]
+ * (kernels/kernels.vx:252-279, gpu/kernels.vx:452-490). */
+int32_t glmvx_router(int32_t *ids, float *weights, const float *logits, const float *bias, int32_t tokens,
+                     int32_t experts, int32_t k, float scale, void *stream);
+int64_t glmvx_topk_scratch_bytes(int32_t n);
+int32_t glmvx_topk(int32_t *indices, const float *scores, int32_t n, int32_t k, void *scratch, void *stream);
+int32_t glmvx_index_scores(float *out, const float *q, const float *keys, const float *w, int32_t tokens,
+                           int32_t heads, int32_t dim, float qk_scale, void *stream);
+int32_t glmvx_attention(float *out, float *scratch, const float *q, const float *keys, const float *values,
+                        const int32_t *selected, int32_t count, int32_t tokens, int32_t dim, int32_t value_dim,
+                        float scale, int32_t *bad, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* GLMVX_H */
