@@ -222,48 +222,67 @@ def run_ours(args, ranks):
                                                      stream.handle, C.byref(path)), 'glmvx_packed_gemm')
             paths[b] = path.value
 
-    def record(ev):
-        rt.call('glmvx_event_record', ev.handle, stream.handle)
+    def capture(fn):
+        g = rt.Graph(stream)
+        g.begin()
+        fn()
+        g.end()
+        g.launch()  # untimed replay: the first launch of a graph is not timed
+        stream.synchronize()
+        return g
 
-    # warm-up, then the timed region captured as one graph with an event
-    # before the sweep and after each kernel of every step.
+    def sweep_steps():
+        for s in range(args.steps):
+            for i, b in enumerate(BATCHES):
+                w = wbuf.ptr + ((s * len(BATCHES) + i) % copies) * stride
+                rt.check(lib, lib.glmvx_packed_gemm(KIND, obuf[b].ptr, w, xbuf[b].ptr, ROWS, COLS, b,
+                                                    stream.handle), 'glmvx_packed_gemm')
+
+    def one_batch(i, b):
+        def fn():
+            for s in range(args.steps):
+                w = wbuf.ptr + ((s * len(BATCHES) + i) % copies) * stride
+                rt.check(lib, lib.glmvx_packed_gemm(KIND, obuf[b].ptr, w, xbuf[b].ptr, ROWS, COLS, b,
+                                                    stream.handle), 'glmvx_packed_gemm')
+        return fn
+
+    start, end = rt.Event(), rt.Event()
+
+    def timed(graph):
+        ranks.barrier()
+        dev.synchronize()
+        t0 = time.time()
+        start.record(stream)
+        graph.launch()
+        end.record(stream)
+        end.synchronize()
+        t1 = time.time()
+        ranks.barrier()
+        clocks.window(t0, t1)
+        return start.elapsed_ms(end)
+
+    # warm-up, then the timed region: K steps captured as one CUDA graph,
+    # bracketed by events on the launching stream.
     for s in range(args.warmup):
         launch(s)
     stream.synchronize()
-    events = [[rt.Event() for _ in range(len(BATCHES) + 1)] for _ in range(args.steps)]
-    graph = rt.Graph(stream)
-    graph.begin()
-    for s in range(args.steps):
-        record(events[s][0])
-        for i, b in enumerate(BATCHES):
-            w = wbuf.ptr + ((s * len(BATCHES) + i) % copies) * stride
-            rt.check(lib, lib.glmvx_packed_gemm(KIND, obuf[b].ptr, w, xbuf[b].ptr, ROWS, COLS, b, stream.handle),
-                     'glmvx_packed_gemm')
-            record(events[s][i + 1])
-    graph.end()
-    graph.launch()  # untimed replay so the graph's first-launch cost is not timed
-    stream.synchronize()
-
+    graph = capture(sweep_steps)
     clocks = ClockSampler(int(os.environ.get('CUDA_VISIBLE_DEVICES', str(ranks.local)).split(',')[0])
                           if os.environ.get('CUDA_VISIBLE_DEVICES', '').split(',')[0].isdigit() else ranks.local)
     time.sleep(0.3)
-    ranks.barrier()
-    dev.synchronize()
-    t0 = time.time()
-    graph.launch()
-    dev.synchronize()
-    t1 = time.time()
-    ranks.barrier()
-    clocks.window(t0, t1)
+    total_ms = ranks.max(timed(graph))
+    graph.close()
     dev.check_device_error()
-    per_kernel = np.array([[events[s][i].elapsed_ms(events[s][i + 1]) for i in range(len(BATCHES))]
-                           for s in range(args.steps)])
-    total_ms = events[0][0].elapsed_ms(events[-1][-1])
-    total_ms = ranks.max(total_ms)
     step_bytes = sum(algorithmic_bytes(b) for b in BATCHES)
     value = ranks.world * step_bytes * args.steps / (total_ms * 1e-3) / 1e9
-    avg = per_kernel.mean(axis=0)
-    graph.close()
+    # Per-kernel durations: each batch size alone, K back-to-back launches.
+    avg = []
+    for i, b in enumerate(BATCHES):
+        g = capture(one_batch(i, b))
+        avg.append(ranks.max(timed(g)) / args.steps)
+        g.close()
+    avg = np.array(avg)
+    dev.check_device_error()
 
     # e2e through the public API: resident weights, host activations/outputs.
     backend = GPUBackend(ranks.local)

@@ -62,7 +62,7 @@ __device__ __forceinline__ int32_t k4_min(const uint8_t *s, int g) {
 
 struct FmtF16 {  // kernels/packed.vx:24-27 (pseudo-block of 8 halves)
     static constexpr int kKind = 1, kBlk = 8, kBytes = 16;
-    __device__ static void octet(const uint8_t *blk, int, float w[8]) {
+    __device__ __forceinline__ static void octet(const uint8_t *blk, int, float w[8]) {
 #pragma unroll
         for (int k = 0; k < 8; ++k) w[k] = h2f(u16(blk + 2 * k));
     }
@@ -70,7 +70,7 @@ struct FmtF16 {  // kernels/packed.vx:24-27 (pseudo-block of 8 halves)
 
 struct FmtQ8_0 {  // kernels/packed.vx:28-31: d*q
     static constexpr int kKind = 8, kBlk = 32, kBytes = 34;
-    __device__ static void octet(const uint8_t *blk, int j0, float w[8]) {
+    __device__ __forceinline__ static void octet(const uint8_t *blk, int j0, float w[8]) {
         const float d = h2f(u16(blk));
         uint32_t lo, hi;
         ld8_a2(blk + 2 + j0, lo, hi);
@@ -81,7 +81,7 @@ struct FmtQ8_0 {  // kernels/packed.vx:28-31: d*q
 
 struct FmtQ2_K {  // kernels/packed.vx:85-94: (d*sc)*q - (dmin*m)
     static constexpr int kKind = 10, kBlk = 256, kBytes = 84;
-    __device__ static void octet(const uint8_t *blk, int j0, float w[8]) {
+    __device__ __forceinline__ static void octet(const uint8_t *blk, int j0, float w[8]) {
         const uint32_t sc = u8(blk + j0 / 16);
         const float dl = __fmul_rn(h2f(u16(blk + 80)), static_cast<float>(sc & 15));
         const float ml = __fmul_rn(h2f(u16(blk + 82)), static_cast<float>(sc >> 4));
@@ -98,7 +98,7 @@ struct FmtQ2_K {  // kernels/packed.vx:85-94: (d*sc)*q - (dmin*m)
 
 struct FmtQ3_K {  // kernels/packed.vx:95-106: (d*sc)*q, q -= 4 when the hmask bit is clear
     static constexpr int kKind = 11, kBlk = 256, kBytes = 110;
-    __device__ static void octet(const uint8_t *blk, int j0, float w[8]) {
+    __device__ __forceinline__ static void octet(const uint8_t *blk, int j0, float w[8]) {
         const int g = j0 / 16;
         const int32_t low = (u8(blk + 96 + g % 8) >> (4 * (g / 8))) & 15;
         const int32_t high = (u8(blk + 104 + g % 4) >> (2 * (g / 4))) & 3;
@@ -118,7 +118,7 @@ struct FmtQ3_K {  // kernels/packed.vx:95-106: (d*sc)*q, q -= 4 when the hmask b
 
 struct FmtQ4_K {  // kernels/packed.vx:121-130: (d*sc)*q - (dmin*m)
     static constexpr int kKind = 12, kBlk = 256, kBytes = 144;
-    __device__ static void octet(const uint8_t *blk, int j0, float w[8]) {
+    __device__ __forceinline__ static void octet(const uint8_t *blk, int j0, float w[8]) {
         const int g = j0 / 32;
         const float dl = __fmul_rn(h2f(u16(blk)), static_cast<float>(k4_scale(blk + 4, g)));
         const float ml = __fmul_rn(h2f(u16(blk + 2)), static_cast<float>(k4_min(blk + 4, g)));
@@ -135,7 +135,7 @@ struct FmtQ4_K {  // kernels/packed.vx:121-130: (d*sc)*q - (dmin*m)
 
 struct FmtQ5_K {  // kernels/packed.vx:131-141
     static constexpr int kKind = 13, kBlk = 256, kBytes = 176;
-    __device__ static void octet(const uint8_t *blk, int j0, float w[8]) {
+    __device__ __forceinline__ static void octet(const uint8_t *blk, int j0, float w[8]) {
         const int g = j0 / 32;
         const float dl = __fmul_rn(h2f(u16(blk)), static_cast<float>(k4_scale(blk + 4, g)));
         const float ml = __fmul_rn(h2f(u16(blk + 2)), static_cast<float>(k4_min(blk + 4, g)));
@@ -153,7 +153,7 @@ struct FmtQ5_K {  // kernels/packed.vx:131-141
 
 struct FmtQ6_K {  // kernels/packed.vx:142-152: (d*sc)*q
     static constexpr int kKind = 14, kBlk = 256, kBytes = 210;
-    __device__ static void octet(const uint8_t *blk, int j0, float w[8]) {
+    __device__ __forceinline__ static void octet(const uint8_t *blk, int j0, float w[8]) {
         const int g = (j0 % 128) / 32;
         const float dsc = __fmul_rn(h2f(u16(blk + 208)), static_cast<float>(s8(u8(blk + 192 + j0 / 16))));
         uint32_t lo, hi, hlo, hhi;
@@ -170,7 +170,7 @@ struct FmtQ6_K {  // kernels/packed.vx:142-152: (d*sc)*q
 
 struct FmtIQ2_XXS {  // kernels/packed.vx:45-59
     static constexpr int kKind = 16, kBlk = 256, kBytes = 66;
-    __device__ static void octet(const uint8_t *blk, int j0, float w[8]) {
+    __device__ __forceinline__ static void octet(const uint8_t *blk, int j0, float w[8]) {
         const int g = j0 / 32, l = (j0 % 32) / 8;
         const uint8_t *p = blk + 2 + 8 * g;
         const int32_t bits = low28(p + 4);
@@ -188,7 +188,7 @@ struct FmtIQ2_XXS {  // kernels/packed.vx:45-59
 
 struct FmtIQ3_XXS {  // kernels/packed.vx:60-74
     static constexpr int kKind = 18, kBlk = 256, kBytes = 98;
-    __device__ static void octet(const uint8_t *blk, int j0, float w[8]) {
+    __device__ __forceinline__ static void octet(const uint8_t *blk, int j0, float w[8]) {
         const int g = j0 / 32, l = (j0 % 32) / 8;
         const uint8_t *p = blk + 66 + 4 * g;
         const int32_t bits = low28(p);
@@ -207,7 +207,7 @@ struct FmtIQ3_XXS {  // kernels/packed.vx:60-74
 
 struct FmtIQ1_S {  // kernels/packed.vx:32-44: d*(2s+1) * (grid + delta)
     static constexpr int kKind = 19, kBlk = 256, kBytes = 50;
-    __device__ static void octet(const uint8_t *blk, int j0, float w[8]) {
+    __device__ __forceinline__ static void octet(const uint8_t *blk, int j0, float w[8]) {
         const int g = j0 / 32, l = (j0 % 32) / 8;
         const uint32_t high = u16(blk + 34 + 2 * g);
         const uint32_t index = u8(blk + 2 + 4 * g + l) | (((high >> (3 * l)) & 7) << 8);
@@ -222,7 +222,7 @@ struct FmtIQ1_S {  // kernels/packed.vx:32-44: d*(2s+1) * (grid + delta)
 
 struct FmtIQ4_XS {  // kernels/packed.vx:75-84
     static constexpr int kKind = 23, kBlk = 256, kBytes = 136;
-    __device__ static void octet(const uint8_t *blk, int j0, float w[8]) {
+    __device__ __forceinline__ static void octet(const uint8_t *blk, int j0, float w[8]) {
         const int g = j0 / 32;
         const int32_t sc = ((u8(blk + 4 + g / 2) >> (4 * (g % 2))) & 15) | (((u16(blk + 2) >> (2 * g)) & 3) << 4);
         const float dl = __fmul_rn(h2f(u16(blk)), static_cast<float>(sc - 32));
