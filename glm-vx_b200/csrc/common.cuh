@@ -50,7 +50,7 @@ int sm_count();
 // ---------------------------------------------------------------- device ---
 
 // Error codes written into the device error word.
-enum DeviceError : int { kDevErrNone = 0, kDevErrFullWait = 1, kDevErrEmptyWait = 2 };
+enum DeviceError : int { kDevErrNone = 0, kDevErrFullWait = 1, kDevErrEmptyWait = 2, kDevErrBadIndex = 3 };
 
 __device__ __forceinline__ uint64_t globaltimer_ns() {
     uint64_t t;

@@ -1,0 +1,203 @@
+// Routed + shared MoE feed-forward layer on sm_100a (decode and small batches).
+//
+// Semantics follow the reference model exactly (glm_vx/model.py:289-324 and
+// glm_vx/prefill.py:44-81):
+//   logits  = router_w . x                          (F32 matvec)
+//   ids, w  = top-k of sigmoid(logits)+bias, w = sigmoid/(sum+1e-20)*scale
+//             (kernels/kernels.vx:252-279)
+//   y       = sum over the token's experts in ascending expert id of
+//             down_e(SwiGLU(gate_e x, up_e x)) * w, then + shared(x)
+//
+// Device pipeline, six launches and no host round trip:
+//   1. router logits     f32 GEMV/GEMM                     (ops.cu)
+//   2. top-k routing     one CTA per token                 (ops.cu)
+//   3. grouping          one CTA: assignments sorted by (expert, token), the
+//                        gate/up/down job descriptors and each token's
+//                        ascending-id combine order        (this file)
+//   4. gate+up           streaming GEMV over 2P jobs       (packed_gemv.cu)
+//   5. down              streaming GEMV over P jobs, SwiGLU fused into the
+//                        activation load                   (packed_gemv.cu)
+//   6. combine           weighted sum in reference order   (this file)
+// P = tokens*top_k (+ tokens for the shared expert).  Jobs are ordered by
+// expert so tokens sharing an expert stream its rows close together in time
+// (L2 reuse).
+#include "codecs.cuh"
+#include "gemv_jobs.cuh"
+
+namespace glmvx {
+
+struct MoeWorkspace {
+    float *logits;
+    int32_t *ids;
+    float *wts;
+    GemvJob *gu_jobs, *dn_jobs;
+    int32_t *comb;
+    float *combw;
+    float *g_out, *u_out, *pair_out;
+    size_t bytes;
+};
+
+static MoeWorkspace carve(char *base, int T, int hidden, int inter, int E, int k, bool shared) {
+    MoeWorkspace w{};
+    size_t off = 0;
+    auto take = [&](size_t n) {
+        char *p = base ? base + off : nullptr;
+        off += (n + 255) & ~static_cast<size_t>(255);
+        return p;
+    };
+    const size_t P = static_cast<size_t>(T) * k + (shared ? T : 0);
+    w.logits = reinterpret_cast<float *>(take(4ull * T * E));
+    w.ids = reinterpret_cast<int32_t *>(take(4ull * T * k));
+    w.wts = reinterpret_cast<float *>(take(4ull * T * k));
+    w.gu_jobs = reinterpret_cast<GemvJob *>(take(sizeof(GemvJob) * 2 * P));
+    w.dn_jobs = reinterpret_cast<GemvJob *>(take(sizeof(GemvJob) * P));
+    w.comb = reinterpret_cast<int32_t *>(take(4ull * T * k));
+    w.combw = reinterpret_cast<float *>(take(4ull * T * k));
+    w.g_out = reinterpret_cast<float *>(take(4ull * P * inter));
+    w.u_out = reinterpret_cast<float *>(take(4ull * P * inter));
+    w.pair_out = reinterpret_cast<float *>(take(4ull * P * hidden));
+    w.bytes = off;
+    return w;
+}
+
+constexpr int kGroupThreads = 512, kMaxAssignments = 4096;
+
+// Rank each (token, slot) assignment by (expert id, token): the rank is its
+// pair index, so pairs of one expert are contiguous and ordered by token.
+__global__ void __launch_bounds__(kGroupThreads)
+    moe_group_kernel(const int32_t *ids, const float *wts, int T, int k, int E, int shared, const uint8_t *gate,
+                     const uint8_t *up, const uint8_t *down, size_t gu_stride, size_t dn_stride, const uint8_t *sgate,
+                     const uint8_t *sup, const uint8_t *sdown, const float *x, int hidden, int inter, float *g_out,
+                     float *u_out, float *pair_out, GemvJob *gu_jobs, GemvJob *dn_jobs, int32_t *comb, float *combw,
+                     int *bad) {
+    __shared__ int32_t s_ids[kMaxAssignments];
+    __shared__ int32_t s_pair[kMaxAssignments];
+    const int n = T * k;
+    const int P = n + (shared ? T : 0);
+    for (int a = threadIdx.x; a < n; a += blockDim.x) {
+        const int e = ids[a];
+        s_ids[a] = e;
+        if (e < 0 || e >= E) report_device_error(bad, kDevErrBadIndex);
+    }
+    __syncthreads();
+    for (int a = threadIdx.x; a < n; a += blockDim.x) {
+        const int e = s_ids[a];
+        int rank = 0;
+        for (int b = 0; b < n; ++b) {
+            const int eb = s_ids[b];
+            rank += (eb < e) | ((eb == e) & (b < a));
+        }
+        s_pair[a] = rank;
+        const int t = a / k;
+        const int ec = min(max(e, 0), E - 1);  // never form an out-of-range pointer
+        gu_jobs[rank] = GemvJob{gate + ec * gu_stride, x + static_cast<size_t>(t) * hidden, nullptr,
+                                g_out + static_cast<size_t>(rank) * inter};
+        gu_jobs[P + rank] = GemvJob{up + ec * gu_stride, x + static_cast<size_t>(t) * hidden, nullptr,
+                                    u_out + static_cast<size_t>(rank) * inter};
+        dn_jobs[rank] = GemvJob{down + ec * dn_stride, g_out + static_cast<size_t>(rank) * inter,
+                                u_out + static_cast<size_t>(rank) * inter, pair_out + static_cast<size_t>(rank) * hidden};
+    }
+    if (shared) {
+        for (int t = threadIdx.x; t < T; t += blockDim.x) {
+            const int p = n + t;
+            gu_jobs[p] = GemvJob{sgate, x + static_cast<size_t>(t) * hidden, nullptr, g_out + static_cast<size_t>(p) * inter};
+            gu_jobs[P + p] = GemvJob{sup, x + static_cast<size_t>(t) * hidden, nullptr, u_out + static_cast<size_t>(p) * inter};
+            dn_jobs[p] = GemvJob{sdown, g_out + static_cast<size_t>(p) * inter, u_out + static_cast<size_t>(p) * inter,
+                                 pair_out + static_cast<size_t>(p) * hidden};
+        }
+    }
+    __syncthreads();
+    // Each token's slots in ascending expert id (glm_vx/model.py:305-316).
+    for (int t = threadIdx.x; t < T; t += blockDim.x) {
+        for (int i = 0; i < k; ++i) {
+            const int a = t * k + i, e = s_ids[a];
+            int pos = 0;
+            for (int j = 0; j < k; ++j) pos += s_ids[t * k + j] < e;
+            comb[t * k + pos] = s_pair[a];
+            combw[t * k + pos] = wts[a];
+        }
+    }
+}
+
+// y[t] = ((0 + o_0*w_0) + o_1*w_1 + ...) + shared_t, each product and sum
+// rounded separately as the reference's f32 array arithmetic does.
+__global__ void moe_combine_kernel(float *y, const float *pair_out, const int32_t *comb, const float *combw, int T,
+                                   int k, int hidden, int shared) {
+    const int t = blockIdx.y;
+    const int h = blockIdx.x * blockDim.x + threadIdx.x;
+    if (h >= hidden) return;
+    float r = 0.0f;
+    for (int i = 0; i < k; ++i) {
+        const int p = comb[t * k + i];
+        r = __fadd_rn(r, __fmul_rn(pair_out[static_cast<size_t>(p) * hidden + h], combw[t * k + i]));
+    }
+    if (shared) r = __fadd_rn(r, pair_out[static_cast<size_t>(T * k + t) * hidden + h]);
+    y[static_cast<size_t>(t) * hidden + h] = r;
+}
+
+}  // namespace glmvx
+
+using namespace glmvx;
+
+GLMVX_EXPORT int64_t glmvx_moe_workspace_bytes(int32_t tokens, int32_t hidden, int32_t inter, int32_t experts,
+                                               int32_t top_k, int32_t has_shared) {
+    if (tokens < 0 || hidden <= 0 || inter <= 0 || experts <= 0 || top_k <= 0) return -1;
+    return static_cast<int64_t>(carve(nullptr, tokens, hidden, inter, experts, top_k, has_shared != 0).bytes + 256);
+}
+
+GLMVX_EXPORT int32_t glmvx_moe_ffn(float *y, const float *x, int32_t tokens, int32_t hidden, int32_t inter,
+                                   const float *router_w, const float *router_bias, int32_t experts, int32_t top_k,
+                                   float scale, int32_t kind, const uint8_t *gate, const uint8_t *up,
+                                   const uint8_t *down, const uint8_t *shared_gate, const uint8_t *shared_up,
+                                   const uint8_t *shared_down, void *workspace, uint64_t workspace_bytes,
+                                   int32_t *ids_out, float *weights_out, void *stream) {
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (tokens < 0 || hidden <= 0 || inter <= 0 || experts <= 0 || top_k <= 0 || top_k > experts) {
+        set_error("moe: invalid dimensions");
+        return kInvalid;
+    }
+    if (static_cast<int64_t>(tokens) * top_k > kMaxAssignments) {
+        set_error("moe: at most %d token-expert assignments per call", kMaxAssignments);
+        return kInvalid;
+    }
+    const bool shared = shared_gate && shared_up && shared_down;
+    if (!shared && (shared_gate || shared_up || shared_down)) {
+        set_error("moe: shared expert needs gate, up and down");
+        return kInvalid;
+    }
+    if (tokens == 0) return kOk;
+    int blk = 0, bytes = 0;
+    if (!reference_layout(kind, blk, bytes) || hidden % blk || inter % blk) {
+        set_error("moe: unsupported expert format or block-misaligned dims");
+        return kUnsupported;
+    }
+    char *base = static_cast<char *>(workspace);
+    const uintptr_t mis = (256 - (reinterpret_cast<uintptr_t>(base) & 255)) & 255;
+    base += mis;
+    MoeWorkspace w = carve(base, tokens, hidden, inter, experts, top_k, shared);
+    if (!workspace || w.bytes + mis > workspace_bytes) {
+        set_error("moe: workspace needs %zu bytes", static_cast<size_t>(w.bytes + mis));
+        return kInvalid;
+    }
+    const size_t gu_stride = static_cast<size_t>(inter) * (hidden / blk) * bytes;
+    const size_t dn_stride = static_cast<size_t>(hidden) * (inter / blk) * bytes;
+    const int P = tokens * top_k + (shared ? tokens : 0);
+    int32_t st_ = glmvx_matmul_nt(w.logits, x, router_w, tokens, experts, hidden, st);
+    if (st_) return st_;
+    st_ = glmvx_router(w.ids, w.wts, w.logits, router_bias, tokens, experts, top_k, scale, st);
+    if (st_) return st_;
+    moe_group_kernel<<<1, kGroupThreads, 0, st>>>(w.ids, w.wts, tokens, top_k, experts, shared, gate, up, down,
+                                                  gu_stride, dn_stride, shared_gate, shared_up, shared_down, x,
+                                                  hidden, inter, w.g_out, w.u_out, w.pair_out, w.gu_jobs, w.dn_jobs,
+                                                  w.comb, w.combw, device_error_word());
+    if ((st_ = launch_status("moe_group_kernel"))) return st_;
+    if ((st_ = gemv_jobs_device(kind, w.gu_jobs, 2 * P, inter, hidden, gate, x, st))) return st_;
+    if ((st_ = gemv_jobs_device(kind, w.dn_jobs, P, hidden, inter, down, w.g_out, st))) return st_;
+    moe_combine_kernel<<<dim3((hidden + 255) / 256, tokens), 256, 0, st>>>(y, w.pair_out, w.comb, w.combw, tokens,
+                                                                           top_k, hidden, shared);
+    if ((st_ = launch_status("moe_combine_kernel"))) return st_;
+    if (ids_out) GLMVX_CUDA(cudaMemcpyAsync(ids_out, w.ids, 4ull * tokens * top_k, cudaMemcpyDeviceToDevice, st));
+    if (weights_out)
+        GLMVX_CUDA(cudaMemcpyAsync(weights_out, w.wts, 4ull * tokens * top_k, cudaMemcpyDeviceToDevice, st));
+    return kOk;
+}

@@ -169,6 +169,26 @@ int32_t glmvx_attention(float *out, float *scratch, const float *q, const float 
                         const int32_t *selected, int32_t count, int32_t tokens, int32_t dim, int32_t value_dim,
                         float scale, int32_t *bad, void *stream);
 
+/* Routed + shared MoE feed-forward layer (decode / small batches), device
+ * pointers.  Replaces the per-expert Python loop of glm_vx/model.py:289-324
+ * (and its grouped prefill form, glm_vx/prefill.py:44-81) for resident
+ * experts: router logits (F32), sigmoid+bias top-k (kernels/kernels.vx:252-279),
+ * grouping by expert, gate/up GEMVs, SwiGLU fused into the down GEMV's
+ * activation load, and the ascending-expert-id weighted combine with the
+ * shared expert added last.  Expert weights are packed GGML `kind` arrays
+ * [experts][inter][hidden] (gate, up) and [experts][hidden][inter] (down);
+ * the shared expert (all three pointers, or all NULL) has one such matrix
+ * each.  `workspace` is caller scratch of glmvx_moe_workspace_bytes(...)
+ * bytes; ids_out/weights_out (NULL or [tokens,top_k] device arrays) receive
+ * the routing.  tokens*top_k <= 4096. */
+int64_t glmvx_moe_workspace_bytes(int32_t tokens, int32_t hidden, int32_t inter, int32_t experts, int32_t top_k,
+                                  int32_t has_shared);
+int32_t glmvx_moe_ffn(float *y, const float *x, int32_t tokens, int32_t hidden, int32_t inter, const float *router_w,
+                      const float *router_bias, int32_t experts, int32_t top_k, float scale, int32_t kind,
+                      const uint8_t *gate, const uint8_t *up, const uint8_t *down, const uint8_t *shared_gate,
+                      const uint8_t *shared_up, const uint8_t *shared_down, void *workspace, uint64_t workspace_bytes,
+                      int32_t *ids_out, float *weights_out, void *stream);
+
 #ifdef __cplusplus
 }
 #endif
