@@ -1,31 +1,40 @@
-"""Benchmark: fused packed-GGUF dequant GEMV / small-batch GEMM on B200.
+"""Benchmark: IQ1_S routed-MoE decode layer on B200 (+ fused dequant-GEMV GB/s).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-Workload: one Q4_K weight matrix of 6144 rows x 2048 cols
-(256-element superblocks of 144 bytes: fp16 d and dmin = |N(0,1)|*0.01,
-12 random sub-scale bytes, 128 random nibble bytes), f32 activations N(0,1),
-token batch swept over 1, 4, 16 and 64.  One step = one pass of the sweep:
-four launches, each over a different resident copy of the weights (the
-copies rotate through more than twice the L2 capacity, so every launch
-streams its weights from HBM).  The metric is algorithmic bytes (packed
-weights + f32 activations + f32 outputs) per second.
+Headline workload (the largest configuration that fits
+one GPU): one GLM-MoE-DSA sparse feed-forward layer -- 256 routed experts +
+1 shared expert, hidden 6144, moe_intermediate 2048, all IQ1_S (fp16
+d = |N(0,1)|*0.02, uniform random qs/qh bytes); F32 router 6144x256
+~ N(0, 0.02) with correction bias ~ N(0, 0.01); sigmoid top-8, renormalised,
+scale 2.5; SwiGLU.  One step = one layer forward for a decode batch of
+TOKENS=32 token rows ~ N(0,1) (the top of the config's 1-32 range).  The
+metric is decode tokens per second through the layer; the layer streams its
+1.9 GB of experts from HBM (far more than L2), so every step reads weights
+from DRAM.  Synthetic, seeded data: the reference publishes no dataset.
+
+Also reported (key `fused_gemv`): BASELINE config 0 (Q8_0 2048x6144, batch 1)
+and config 1 (Q4_K 6144x2048, batch 1/4/16/64) fused dequant-GEMV GB/s,
+rotating weight copies beyond L2.
 
 Arms:
-  ours       device-resident timing of the CUDA library (CUDA graph of the K
-             timed steps, CUDA events between kernels), plus `e2e` through
-             the public gpu.backend.GPUBackend API with host activations and
-             host outputs, and (rank 0, N=1) the single-thread CPU oracle on a
-             bounded row sample as `cpu_baseline`.
-  reference  the reference's CPU implementation of the path -- its Vx
-             kernels cannot be compiled here, so the C restatement in
-             oracle/ (OpenMP build, all host cores) -- on a row sample.
+  ours       device-resident timing (CUDA graph of the K timed steps, CUDA
+             events on the launching stream), `e2e` through the public
+             gpu.moe.MoELayer.forward API (host activations in, host outputs
+             out), and (rank 0, N=1) the single-thread C oracle on a bounded
+             token sample as `cpu_baseline`.
+  reference  the reference's own Python path for the layer
+             (glm_vx GlmMoeDsaModel._feed_forward with its kernels/backend.py
+             VxBackend and kernels/packed.py, installed unmodified in
+             baseline/_ref) over the OpenMP C restatement of its uncompilable
+             Vx kernels, one token per step, all host cores.
 
-Multi-GPU: the path does not shard (a single projection), so N GPUs run N
-independent replicas ("replicas only"); torch.distributed over gloo carries
-only the barrier and the max-over-ranks of the device times.
+Multi-GPU: each rank runs an independent replica of the layer on its own
+token batch ("replicas"; expert parallelism is a later step);
+torch.distributed over gloo carries only barriers and the max of device times.
 """
 import argparse
+import ctypes as C
 import json
 import math
 import os
@@ -39,29 +48,17 @@ from pathlib import Path
 import numpy as np
 
 ROOT = Path(__file__).resolve().parent
-sys.path[:0] = [str(ROOT), str(ROOT / 'glm-vx_b200')]
-
-METRIC = 'fused dequant-GEMV HBM GB/s vs 8 TB/s peak'
-KIND, ROWS, COLS = 12, 6144, 2048           # Q4_K
-BATCHES = (1, 4, 16, 64)
-BLOCK, BLOCK_BYTES = 256, 144
-WEIGHT_BYTES = ROWS * (COLS // BLOCK) * BLOCK_BYTES  # 7,077,888
-# dram bytes per launch from the committed ncu capture (profiles/), None until captured.
-NCU_TRAFFIC = {}
+METRIC = 'decode tok/s (1/2/4/8 B200) + fused dequant-GEMV HBM GB/s vs 8 TB/s peak'
+EXPERTS, HIDDEN, INTER, TOPK, SCALE, KIND = 256, 6144, 2048, 8, 2.5, 19
+TOKENS = 32
+IQ1_BLOCK, IQ1_BYTES = 256, 50
+EXPERT_MATRIX_BYTES = INTER * (HIDDEN // IQ1_BLOCK) * IQ1_BYTES  # 2,457,600; gate, up and down are equal
+# dram bytes per launch of the dominant kernel from the committed ncu capture, None until captured.
+NCU_TRAFFIC = None
 
 
-def algorithmic_bytes(batch, rows=ROWS):
-    return rows * (COLS // BLOCK) * BLOCK_BYTES + batch * COLS * 4 + batch * rows * 4
-
-
-def synthetic_q4k(rows, seed=0):
-    """Config-1 synthetic Q4_K superblocks."""
-    rng = np.random.default_rng(seed)
-    blocks = rows * (COLS // BLOCK)
-    raw = rng.integers(0, 256, size=(blocks, BLOCK_BYTES), dtype=np.uint8)
-    d = (np.abs(rng.normal(size=(blocks, 2))) * 0.01).astype(np.float16)
-    raw[:, 0:4] = d.view(np.uint8).reshape(blocks, 4)
-    return raw.reshape(-1)
+def use_ours():
+    sys.path[:0] = [str(ROOT), str(ROOT / 'glm-vx_b200')]
 
 
 def peaks():
@@ -70,6 +67,29 @@ def peaks():
         return float(data['hbm_gbs']), 'measured'
     except (OSError, KeyError, ValueError):
         return 6650.0, 'fallback'
+
+
+def synthetic_layer(seed=0):
+    """BASELINE config-2 weights as host arrays (about 1.9 GB)."""
+    rng = np.random.default_rng(seed)
+
+    def iq1(count, rows, cols):
+        blocks = count * rows * cols // IQ1_BLOCK
+        raw = rng.integers(0, 256, size=(blocks, IQ1_BYTES), dtype=np.uint8)
+        raw[:, :2] = (np.abs(rng.normal(size=(blocks, 1))) * 0.02).astype(np.float16).view(np.uint8)
+        return raw.reshape(-1)
+
+    return dict(router=(rng.normal(size=(EXPERTS, HIDDEN)) * 0.02).astype(np.float32),
+                bias=(rng.normal(size=EXPERTS) * 0.01).astype(np.float32),
+                gate=iq1(EXPERTS, INTER, HIDDEN), up=iq1(EXPERTS, INTER, HIDDEN), down=iq1(EXPERTS, HIDDEN, INTER),
+                shared=(iq1(1, INTER, HIDDEN), iq1(1, INTER, HIDDEN), iq1(1, HIDDEN, INTER)))
+
+
+def layer_bytes(unique_experts, tokens):
+    """Algorithmic bytes of one layer forward: every routed expert used at
+    least once plus the shared expert (gate, up, down each), the F32 router,
+    token rows in and out."""
+    return (unique_experts + 1) * 3 * EXPERT_MATRIX_BYTES + EXPERTS * HIDDEN * 4 + 2 * tokens * HIDDEN * 4
 
 
 # ----------------------------------------------------------------- clocks
@@ -115,6 +135,11 @@ class ClockSampler:
                 'reasons': reasons, 'samples': len(picked)}
 
 
+def gpu_index(local):
+    vis = os.environ.get('CUDA_VISIBLE_DEVICES', '').split(',')
+    return int(vis[local]) if local < len(vis) and vis[local].strip().isdigit() else local
+
+
 # ------------------------------------------------------------ distributed
 class Ranks:
     def __init__(self):
@@ -145,223 +170,313 @@ class Ranks:
             self.dist.destroy_process_group()
 
 
-# ------------------------------------------------------------ CPU oracle
-def oracle_sweep(lib_path, rows, deadline_s, steps=None):
-    """Run the config-1 sweep on a `rows`-row prefix through the oracle's
-    reference C ABI.  Returns (bytes processed, seconds, steps)."""
+# --------------------------------------------------------- reference arm
+class _PackedLayerWeights:
+    """The object glm_vx.model expects for packed weights (.linear and a name
+    lookup), over host arrays of one synthetic layer."""
+
+    def __init__(self, layer):
+        self.layer = layer
+        self.gu = INTER * (HIDDEN // IQ1_BLOCK) * IQ1_BYTES
+        self.dn = HIDDEN * (INTER // IQ1_BLOCK) * IQ1_BYTES
+
+    def _packed(self, name):
+        p = 'model.layers.0.mlp.'
+        rest = name[len(p):]
+        if rest == 'gate.weight':
+            return self.layer['router'].reshape(-1).view(np.uint8), 0, (EXPERTS, HIDDEN)
+        shared = rest.startswith('shared_experts.')
+        proj = rest.split('.')[-2]
+        if shared:
+            i = {'gate_proj': 0, 'up_proj': 1, 'down_proj': 2}[proj]
+            raw = self.layer['shared'][i]
+        else:
+            e = int(rest.split('.')[1])
+            src = {'gate_proj': 'gate', 'up_proj': 'up', 'down_proj': 'down'}[proj]
+            n = self.dn if proj == 'down_proj' else self.gu
+            raw = self.layer[src][e * n:(e + 1) * n]
+        shape = (HIDDEN, INTER) if proj == 'down_proj' else (INTER, HIDDEN)
+        return raw, KIND, shape
+
+    def linear(self, name, x, backend):
+        raw, kind, shape = self._packed(name)
+        return backend.packed_matvec(raw, kind, shape, x)
+
+    def __call__(self, name):
+        if name.endswith('e_score_correction_bias'):
+            return self.layer['bias']
+        raise KeyError(name)
+
+
+def reference_model(layer, library):
+    """One sparse layer of the reference model class, stock code path."""
+    from glm_vx.model import GlmMoeDsaModel
     from kernels.backend import VxBackend
-    cpu = VxBackend(str(lib_path))
-    raw = synthetic_q4k(rows, seed=0)
-    xs = {b: np.random.default_rng(b).normal(size=(b, COLS)).astype(np.float32) for b in BATCHES}
-    done, nbytes, t0 = 0, 0, time.perf_counter()
-    while (steps is None and (done == 0 or time.perf_counter() - t0 < deadline_s)) or (steps is not None and done < steps):
-        for b in BATCHES:
-            if b == 1:
-                cpu.packed_matvec(raw, KIND, (rows, COLS), xs[b][0])
-            else:
-                cpu.packed_linear_batch(raw, KIND, (rows, COLS), xs[b])
-            nbytes += algorithmic_bytes(b, rows)
-        done += 1
-    return nbytes, time.perf_counter() - t0, done
+    config = dict(num_hidden_layers=1, hidden_size=HIDDEN, num_attention_heads=1, kv_lora_rank=1,
+                  qk_nope_head_dim=1, qk_rope_head_dim=2, v_head_dim=1, index_n_heads=1, index_head_dim=2,
+                  index_topk=1, mlp_layer_types=['sparse'], indexer_types=['full'], num_experts_per_tok=TOPK,
+                  routed_scaling_factor=SCALE, n_shared_experts=1, vocab_size=1)
+    return GlmMoeDsaModel(config, _PackedLayerWeights(layer), VxBackend(str(library)), packed_weights=True)
+
+
+def oracle_ffn(cpu, layer, x):
+    """One token through the layer with the reference's semantics
+    (glm_vx/model.py:289-324), every primitive on the C oracle `cpu`."""
+    gu = INTER * (HIDDEN // IQ1_BLOCK) * IQ1_BYTES
+    dn = HIDDEN * (INTER // IQ1_BLOCK) * IQ1_BYTES
+
+    def mlp(g, u, d):
+        a = cpu.swiglu(cpu.packed_matvec(g, KIND, (INTER, HIDDEN), x), cpu.packed_matvec(u, KIND, (INTER, HIDDEN), x))
+        return cpu.packed_matvec(d, KIND, (HIDDEN, INTER), a)
+
+    ids, w = cpu.route(cpu.matvec(layer['router'], x), layer['bias'], TOPK, SCALE)
+    result = np.zeros(HIDDEN, np.float32)
+    for slot in np.argsort(ids, kind='stable'):
+        e = int(ids[slot])
+        result += mlp(layer['gate'][e * gu:(e + 1) * gu], layer['up'][e * gu:(e + 1) * gu],
+                      layer['down'][e * dn:(e + 1) * dn]) * float(w[slot])
+    return result + mlp(*layer['shared'])
 
 
 def run_reference(args, ranks):
-    """The reference arm: the CPU implementation of the path on host cores."""
+    """The reference arm: the reference's own Python over the C oracle, host cores."""
     if ranks.rank != 0:
         return 0
-    from oracle import loader
+    ref_root = ROOT / 'baseline' / '_ref'
+    have_ref = (ref_root / 'glm_vx').exists()
+    sys.path[:0] = ([str(ref_root)] if have_ref else []) + [str(ROOT)]
+    if not have_ref:
+        sys.path.insert(1, str(ROOT / 'glm-vx_b200'))
     cores = len(os.sched_getaffinity(0))
     os.environ['OMP_NUM_THREADS'] = str(cores)
+    from oracle import loader
     lib = loader.parallel()
-    sample_rows = 768  # 1/8 of the matrix per step keeps K steps within minutes
-    oracle_sweep(lib, sample_rows, 0, steps=args.warmup)
-    nbytes, secs, steps = oracle_sweep(lib, sample_rows, 0, steps=args.steps)
-    value = nbytes / secs / 1e9
-    sample = f'{sample_rows} of {ROWS} rows per step, batches {list(BATCHES)}; C restatement of the Vx kernels (OpenMP)'
+    layer = synthetic_layer(0)
+    if have_ref:
+        model = reference_model(layer, lib)
+        run = lambda v: model._feed_forward(0, v)
+    else:  # reference Python not installed: the same semantics composed here
+        from kernels.backend import VxBackend
+        cpu = VxBackend(str(lib))
+        run = lambda v: oracle_ffn(cpu, layer, v)
+    x = np.random.default_rng(1).normal(size=(args.steps + args.warmup, HIDDEN)).astype(np.float32)
+    for i in range(args.warmup):
+        run(x[i])
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        run(x[args.warmup + i])
+    secs = time.perf_counter() - t0
+    value = args.steps / secs
+    source = ('baseline/_ref glm_vx + kernels (GlmMoeDsaModel._feed_forward, VxBackend)' if have_ref
+              else 'reference semantics composed over the oracle (baseline/_ref not installed)')
     line = {
-        'impl': 'reference', 'metric': METRIC, 'value': value, 'unit': 'GB/s', 'n_gpus': args.gpus,
-        'steps': args.steps, 'warmup': args.warmup, 'ms_per_step': secs / steps * 1e3, 'higher_is_better': True,
+        'impl': 'reference', 'metric': METRIC, 'value': value, 'unit': 'tok/s', 'n_gpus': args.gpus,
+        'steps': args.steps, 'warmup': args.warmup, 'ms_per_step': secs / args.steps * 1e3, 'higher_is_better': True,
         'scaling': 'weak', 'vs_baseline': None, 'dtype': 'f32', 'data': 'synthetic',
-        'config': {'workload': 'config1_q4_k_6144x2048_batch_sweep', 'rows_sampled': sample_rows,
-                   'batches': list(BATCHES), 'parallelism': 'host cores'},
-        'cpu_baseline': {'value': value, 'unit': 'GB/s', 'cores': cores, 'kind': 'port', 'sample': sample},
-        'e2e': {'value': value, 'unit': 'GB/s', 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0},
+        'config': {'workload': 'config2_iq1_s_moe_decode_layer', 'tokens_per_step': 1, 'parallelism': 'host cores'},
+        'cpu_baseline': {'value': value, 'unit': 'tok/s', 'cores': cores, 'kind': 'port',
+                         'sample': f'1 token per step through one full config-2 layer: {source} '
+                                   'over the OpenMP C restatement of the Vx kernels'},
+        'e2e': {'value': value, 'unit': 'tok/s', 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0},
     }
     print(json.dumps(line), flush=True)
     return 0
 
 
 # ---------------------------------------------------------------- ours
+def graph_time(rt, stream, fn, reps, ranks=None, clocks=None):
+    """Capture `fn` (issuing work on `stream`) `reps` times into a graph, run
+    it once untimed, then time one launch with events on the stream."""
+    g = rt.Graph(stream)
+    g.begin()
+    for i in range(reps):
+        fn(i)
+    g.end()
+    g.launch()
+    stream.synchronize()
+    e0, e1 = rt.Event(), rt.Event()
+    if ranks:
+        ranks.barrier()
+    rt.call('glmvx_device_synchronize')
+    t0 = time.time()
+    e0.record(stream)
+    g.launch()
+    e1.record(stream)
+    e1.synchronize()
+    if clocks:
+        clocks.window(t0, time.time())
+    if ranks:
+        ranks.barrier()
+    ms = e0.elapsed_ms(e1)
+    g.close()
+    return ms
+
+
+def fused_gemv_sweep(rt, lib, dev, stream, steps, peak):
+    """Configs 0 and 1: GB/s of the fused dequant-GEMV/GEMM per launch."""
+    res = {}
+    rng = np.random.default_rng(0)
+    for name, kind, rows, cols, blk, size, batches in (('config0_q8_0_2048x6144', 8, 2048, 6144, 32, 34, (1,)),
+                                                       ('config1_q4_k_6144x2048', 12, 6144, 2048, 256, 144,
+                                                        (1, 4, 16, 64))):
+        wbytes = rows * (cols // blk) * size
+        nblocks = rows * cols // blk
+        raw = rng.integers(0, 256, size=(nblocks, size), dtype=np.uint8)
+        sc = (np.abs(rng.normal(size=(nblocks, 2))) * 0.01).astype(np.float16).view(np.uint8)
+        raw[:, :2 if kind == 8 else 4] = sc[:, :2 if kind == 8 else 4]
+        raw = raw.reshape(-1)
+        copies = max(4, math.ceil(2.5 * dev.l2_bytes / wbytes))
+        stride = (wbytes + 255) // 256 * 256
+        wbuf = rt.DeviceBuffer(stride * copies)
+        for c in range(copies):
+            wbuf.upload(raw, stream.handle, offset=c * stride)
+        for b in batches:
+            x = rng.normal(size=(b, cols)).astype(np.float32)
+            xd, od = rt.DeviceBuffer(x.nbytes), rt.DeviceBuffer(4 * b * rows)
+            xd.upload(x, stream.handle)
+
+            def launch(i, b=b, xd=xd, od=od):
+                rt.check(lib, lib.glmvx_packed_gemm(kind, od.ptr, wbuf.ptr + (i % copies) * stride, xd.ptr, rows,
+                                                    cols, b, stream.handle), 'glmvx_packed_gemm')
+            reps = max(20, min(steps, 400))
+            for i in range(3):
+                launch(i)
+            us = graph_time(rt, stream, launch, reps) / reps * 1e3
+            alg = wbytes + x.nbytes + 4 * b * rows
+            res[f'{name}_b{b}'] = {'us': us, 'gbs': alg / us / 1e3, 'frac_of_measured_hbm': alg / us / 1e3 / peak}
+            xd.close()
+            od.close()
+        wbuf.close()
+    return res
+
+
 def run_ours(args, ranks):
-    import ctypes as C
+    use_ours()
     from gpu import runtime as rt
-    from gpu.backend import GPUBackend, PackedWeight
+    from gpu.backend import GPUBackend
+    from gpu.moe import MoELayer
 
-    dev = rt.Device(ranks.local)
-    lib = rt.library()
-    stream = rt.Stream()
-    copies = max(4, math.ceil(2.5 * dev.l2_bytes / WEIGHT_BYTES))
-    stride = (WEIGHT_BYTES + 255) // 256 * 256
-    raw = synthetic_q4k(ROWS, seed=0)
-    wbuf = rt.DeviceBuffer(stride * copies)
-    for c in range(copies):
-        wbuf.upload(raw, stream.handle, offset=c * stride)
-    xs = {b: np.random.default_rng(b).normal(size=(b, COLS)).astype(np.float32) for b in BATCHES}
-    xbuf = {b: rt.DeviceBuffer(xs[b].nbytes) for b in BATCHES}
-    obuf = {b: rt.DeviceBuffer(4 * b * ROWS) for b in BATCHES}
-    for b in BATCHES:
-        xbuf[b].upload(xs[b], stream.handle)
-    stream.synchronize()
-    paths = {}
-
-    def launch(step):
-        for i, b in enumerate(BATCHES):
-            w = wbuf.ptr + ((step * len(BATCHES) + i) % copies) * stride
-            path = C.c_int32()
-            rt.check(lib, lib.glmvx_packed_gemm_path(KIND, obuf[b].ptr, w, xbuf[b].ptr, ROWS, COLS, b,
-                                                     stream.handle, C.byref(path)), 'glmvx_packed_gemm')
-            paths[b] = path.value
-
-    def capture(fn):
-        g = rt.Graph(stream)
-        g.begin()
-        fn()
-        g.end()
-        g.launch()  # untimed replay: the first launch of a graph is not timed
-        stream.synchronize()
-        return g
-
-    def sweep_steps():
-        for s in range(args.steps):
-            for i, b in enumerate(BATCHES):
-                w = wbuf.ptr + ((s * len(BATCHES) + i) % copies) * stride
-                rt.check(lib, lib.glmvx_packed_gemm(KIND, obuf[b].ptr, w, xbuf[b].ptr, ROWS, COLS, b,
-                                                    stream.handle), 'glmvx_packed_gemm')
-
-    def one_batch(i, b):
-        def fn():
-            for s in range(args.steps):
-                w = wbuf.ptr + ((s * len(BATCHES) + i) % copies) * stride
-                rt.check(lib, lib.glmvx_packed_gemm(KIND, obuf[b].ptr, w, xbuf[b].ptr, ROWS, COLS, b,
-                                                    stream.handle), 'glmvx_packed_gemm')
-        return fn
-
-    start, end = rt.Event(), rt.Event()
-
-    def timed(graph):
-        ranks.barrier()
-        dev.synchronize()
-        t0 = time.time()
-        start.record(stream)
-        graph.launch()
-        end.record(stream)
-        end.synchronize()
-        t1 = time.time()
-        ranks.barrier()
-        clocks.window(t0, t1)
-        return start.elapsed_ms(end)
-
-    # warm-up, then the timed region: K steps captured as one CUDA graph,
-    # bracketed by events on the launching stream.
-    for s in range(args.warmup):
-        launch(s)
-    stream.synchronize()
-    graph = capture(sweep_steps)
-    clocks = ClockSampler(int(os.environ.get('CUDA_VISIBLE_DEVICES', str(ranks.local)).split(',')[0])
-                          if os.environ.get('CUDA_VISIBLE_DEVICES', '').split(',')[0].isdigit() else ranks.local)
-    time.sleep(0.3)
-    total_ms = ranks.max(timed(graph))
-    graph.close()
-    dev.check_device_error()
-    step_bytes = sum(algorithmic_bytes(b) for b in BATCHES)
-    value = ranks.world * step_bytes * args.steps / (total_ms * 1e-3) / 1e9
-    # Per-kernel durations: each batch size alone, K back-to-back launches.
-    avg = []
-    for i, b in enumerate(BATCHES):
-        g = capture(one_batch(i, b))
-        avg.append(ranks.max(timed(g)) / args.steps)
-        g.close()
-    avg = np.array(avg)
-    dev.check_device_error()
-
-    # e2e through the public API: resident weights, host activations/outputs.
     backend = GPUBackend(ranks.local)
-    handles = [PackedWeight(wbuf, KIND, (ROWS, COLS), WEIGHT_BYTES, offset=c * stride, owner=False)
-               for c in range(copies)]
-    e2e_steps = max(1, min(args.steps, 2000))
+    dev, lib, stream = backend.device, backend.lib, backend.stream
+    layer = synthetic_layer(0)
+    moe = MoELayer(backend, layer['router'], layer['bias'], KIND, layer['gate'], layer['up'], layer['down'],
+                   HIDDEN, INTER, TOPK, SCALE, shared=layer['shared'])
+    rng = np.random.default_rng(100 + ranks.rank)
+    xs = {t: rng.normal(size=(t, HIDDEN)).astype(np.float32) for t in (1, 8, TOKENS)}
+    bufs = {}
+    for t, x in xs.items():
+        xd, yd, idd = rt.DeviceBuffer(x.nbytes), rt.DeviceBuffer(x.nbytes), rt.DeviceBuffer(4 * t * TOPK)
+        xd.upload(x, stream.handle)
+        bufs[t] = (xd, yd, idd)
+    stream.synchronize()
 
-    def api_step(s):
-        for i, b in enumerate(BATCHES):
-            h = handles[(s * len(BATCHES) + i) % copies]
-            if b == 1:
-                backend.packed_matvec(h, KIND, (ROWS, COLS), xs[b][0])
-            else:
-                backend.packed_linear_batch(h, KIND, (ROWS, COLS), xs[b])
+    def step(t):
+        xd, yd, _ = bufs[t]
+        return lambda i: moe.forward_device(yd.ptr, xd.ptr, t)
 
-    for s in range(args.warmup):
-        api_step(s)
-    ranks.barrier()
-    t2 = time.perf_counter()
-    w2 = time.time()
-    for s in range(e2e_steps):
-        api_step(s)
-    e2e_s = time.perf_counter() - t2
-    clocks.window(w2, time.time())
-    e2e_s = ranks.max(e2e_s)
-    ranks.barrier()
-    e2e_value = ranks.world * step_bytes * e2e_steps / e2e_s / 1e9
-    backend.close()
+    clocks = ClockSampler(gpu_index(ranks.local))
+    for i in range(args.warmup):
+        step(TOKENS)(i)
+    stream.synchronize()
+    time.sleep(0.3)
+    total_ms = ranks.max(graph_time(rt, stream, step(TOKENS), args.steps, ranks, clocks))
+    dev.check_device_error()
+    value = ranks.world * TOKENS * args.steps / (total_ms * 1e-3)
 
+    # Per decode-batch size: layer time, unique experts, stage breakdown.
     peak, peak_kind = peaks()
-    dom = int(np.argmax(avg))
-    b_dom = BATCHES[dom]
+    per_tokens, stage_names = {}, ['router_logits', 'routing', 'grouping', 'gate_up', 'down', 'combine']
+    for t in xs:
+        xd, yd, idd = bufs[t]
+        moe.forward_device(yd.ptr, xd.ptr, t, idd.ptr)
+        ids = np.empty(t * TOPK, np.int32)
+        stream.synchronize()
+        idd.download(ids)
+        unique = len(np.unique(ids))
+        reps = max(5, min(args.steps, 100))
+        ms = graph_time(rt, stream, step(t), reps) / reps
+        # stage durations (events between the six launches, no graph)
+        events = [rt.Event() for _ in range(7)]
+        ev_arr = C.cast((C.c_void_p * 7)(*[e.handle for e in events]), C.c_void_p)
+        sums = np.zeros(6)
+        ws = moe._workspace(t)
+        for _ in range(reps):
+            rt.check(lib, lib.glmvx_moe_ffn_profiled(
+                yd.ptr, xd.ptr, t, HIDDEN, INTER, moe.router_w, moe.router_bias, EXPERTS, TOPK, SCALE, KIND,
+                moe.gate, moe.up, moe.down, *moe.shared, ws, moe._ws_bytes, ev_arr, stream.handle), 'moe profiled')
+            events[-1].synchronize()
+            sums += [events[i].elapsed_ms(events[i + 1]) for i in range(6)]
+        stages = dict(zip(stage_names, (sums / reps * 1e3).tolist()))
+        alg = layer_bytes(unique, t)
+        per_tokens[str(t)] = {'us_per_layer': ms * 1e3, 'tok_s': t / (ms * 1e-3), 'unique_experts': unique,
+                              'layer_gbs': alg / (ms * 1e-3) / 1e9, 'stage_us': stages}
+    dom_t = per_tokens[str(TOKENS)]
+    gu_us = dom_t['stage_us']['gate_up']
+    gu_bytes = (dom_t['unique_experts'] + 1) * 2 * EXPERT_MATRIX_BYTES + (TOKENS * TOPK + TOKENS) * 2 * INTER * 4
+    achieved = gu_bytes / (gu_us * 1e-6) / 1e9
+    dev.check_device_error()
 
-    def roof(i):
-        b = BATCHES[i]
-        achieved = algorithmic_bytes(b) / (avg[i] * 1e-3) / 1e9
-        return {'bound': 'hbm', 'achieved': achieved, 'peak': peak, 'unit': 'GB/s', 'frac': achieved / peak,
-                'traffic': NCU_TRAFFIC.get(b), 'kernel_batch': b, 'peak_source': peak_kind,
-                'avg_launch_us': float(avg[i] * 1e3)}
+    # e2e through the public API: host token rows in, host outputs out.
+    e2e_steps = max(1, min(args.steps, 200))
+    for i in range(min(args.warmup, 3)):
+        moe.forward(xs[TOKENS])
+    ranks.barrier()
+    t0 = time.perf_counter()
+    w0 = time.time()
+    for _ in range(e2e_steps):
+        moe.forward(xs[TOKENS])
+    e2e_s = ranks.max(time.perf_counter() - t0)
+    clocks.window(w0, time.time())
+    e2e_value = ranks.world * TOKENS * e2e_steps / e2e_s
 
+    gemv = fused_gemv_sweep(rt, lib, dev, stream, args.steps, peak)
     line = {
-        'metric': METRIC, 'value': value, 'unit': 'GB/s', 'n_gpus': ranks.world, 'steps': args.steps,
+        'metric': METRIC, 'value': value, 'unit': 'tok/s', 'n_gpus': ranks.world, 'steps': args.steps,
         'warmup': args.warmup, 'ms_per_step': total_ms / args.steps, 'higher_is_better': True, 'scaling': 'weak',
         'vs_baseline': None, 'dtype': 'f32', 'data': 'synthetic',
-        'config': {'workload': 'config1_q4_k_6144x2048_batch_sweep', 'format': 'Q4_K', 'rows': ROWS, 'cols': COLS,
-                   'batches': list(BATCHES), 'global_batch': sum(BATCHES), 'parallelism': f'replicas x{ranks.world}',
-                   'l2_policy': f'inputs larger than L2: {copies} rotating weight copies, '
-                                f'{copies * WEIGHT_BYTES / 1e6:.0f} MB vs {dev.l2_bytes / 1e6:.0f} MB L2',
-                   'kernel_paths': {str(b): paths.get(b) for b in BATCHES},
-                   'per_batch_us': {str(b): float(avg[i] * 1e3) for i, b in enumerate(BATCHES)},
-                   'per_batch_gbs': {str(b): algorithmic_bytes(b) / (avg[i] * 1e-3) / 1e9
-                                     for i, b in enumerate(BATCHES)}},
-        'roofline': roof(dom),
-        'roofline_gemv_b1': roof(0),
-        'e2e': {'value': e2e_value, 'unit': 'GB/s', 'steps': e2e_steps,
-                'h2d_bytes_per_step': sum(b * COLS * 4 for b in BATCHES),
-                'd2h_bytes_per_step': sum(b * ROWS * 4 for b in BATCHES),
-                'api': 'gpu.backend.GPUBackend.packed_matvec / packed_linear_batch (resident PackedWeight)'},
-        'gpu_launches': len(BATCHES) * args.steps,
+        'config': {'workload': 'config2_iq1_s_moe_decode_layer', 'experts': EXPERTS, 'shared_experts': 1,
+                   'hidden': HIDDEN, 'moe_intermediate': INTER, 'top_k': TOPK, 'routed_scale': SCALE,
+                   'format': 'IQ1_S', 'tokens_per_step': TOKENS, 'global_batch': TOKENS * ranks.world,
+                   'parallelism': f'replicas x{ranks.world}',
+                   'l2_policy': 'inputs larger than L2: the layer streams 1.9 GB of resident experts',
+                   'per_tokens': per_tokens},
+        'roofline': {'bound': 'hbm', 'achieved': achieved, 'peak': peak, 'unit': 'GB/s', 'frac': achieved / peak,
+                     'traffic': NCU_TRAFFIC, 'kernel': 'gemv_rows_kernel<IQ1_S> gate+up job list',
+                     'algorithmic_bytes_per_launch': gu_bytes, 'avg_launch_us': gu_us, 'peak_source': peak_kind},
+        'fused_gemv': gemv,
+        'e2e': {'value': e2e_value, 'unit': 'tok/s', 'steps': e2e_steps,
+                'h2d_bytes_per_step': TOKENS * HIDDEN * 4, 'd2h_bytes_per_step': TOKENS * HIDDEN * 4 + 2 * TOKENS * TOPK * 4,
+                'api': 'gpu.moe.MoELayer.forward (host rows in, host rows + routing out)'},
+        'gpu_launches': 6 * args.steps,
         'clocks': clocks.summary(),
     }
     if ranks.rank == 0 and ranks.world == 1 and not args.no_cpu_baseline:
         from oracle import loader
-        sample_rows = 256
-        nbytes, secs, steps = oracle_sweep(loader.serial(), sample_rows, args.cpu_seconds)
-        line['cpu_baseline'] = {'value': nbytes / secs / 1e9, 'unit': 'GB/s', 'cores': 1, 'kind': 'port',
-                                'sample': f'{steps} sweeps (batches {list(BATCHES)}) over a {sample_rows}-row '
-                                          f'prefix of the {ROWS}x{COLS} Q4_K matrix, single-thread C oracle'}
+        from kernels.backend import VxBackend
+        cpu = VxBackend(str(loader.serial()))  # the checker's library, here as the timed CPU baseline
+        n, t0 = 0, time.perf_counter()
+        while n == 0 or (time.perf_counter() - t0 < args.cpu_seconds and n < 8):
+            oracle_ffn(cpu, layer, xs[1][0])
+            n += 1
+        secs = time.perf_counter() - t0
+        line['cpu_baseline'] = {'value': n / secs, 'unit': 'tok/s', 'cores': 1, 'kind': 'port',
+                                'sample': f'{n} token(s) through the full config-2 layer, reference semantics '
+                                          '(glm_vx/model.py:289-324) on the single-thread C oracle'}
     if ranks.rank == 0:
         print(json.dumps(line), flush=True)
-    wbuf.close()
+    moe.close()
+    for t in bufs:
+        for b in bufs[t]:
+            b.close()
+    backend.close()
     return 0
 
 
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument('--gpus', type=int, default=1)
-    ap.add_argument('--steps', type=int, default=2000)
-    ap.add_argument('--warmup', type=int, default=20)
+    ap.add_argument('--steps', type=int, default=200)
+    ap.add_argument('--warmup', type=int, default=5)
     ap.add_argument('--impl', choices=('ours', 'reference'), default='ours')
     ap.add_argument('--cpu-seconds', type=float, default=10.0)
     ap.add_argument('--no-cpu-baseline', action='store_true')

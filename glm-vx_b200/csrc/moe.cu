@@ -145,12 +145,11 @@ GLMVX_EXPORT int64_t glmvx_moe_workspace_bytes(int32_t tokens, int32_t hidden, i
     return static_cast<int64_t>(carve(nullptr, tokens, hidden, inter, experts, top_k, has_shared != 0).bytes + 256);
 }
 
-GLMVX_EXPORT int32_t glmvx_moe_ffn(float *y, const float *x, int32_t tokens, int32_t hidden, int32_t inter,
-                                   const float *router_w, const float *router_bias, int32_t experts, int32_t top_k,
-                                   float scale, int32_t kind, const uint8_t *gate, const uint8_t *up,
-                                   const uint8_t *down, const uint8_t *shared_gate, const uint8_t *shared_up,
-                                   const uint8_t *shared_down, void *workspace, uint64_t workspace_bytes,
-                                   int32_t *ids_out, float *weights_out, void *stream) {
+static int32_t moe_ffn(float *y, const float *x, int32_t tokens, int32_t hidden, int32_t inter, const float *router_w,
+                       const float *router_bias, int32_t experts, int32_t top_k, float scale, int32_t kind,
+                       const uint8_t *gate, const uint8_t *up, const uint8_t *down, const uint8_t *shared_gate,
+                       const uint8_t *shared_up, const uint8_t *shared_down, void *workspace, uint64_t workspace_bytes,
+                       int32_t *ids_out, float *weights_out, void *stream, void *const *events) {
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     if (tokens < 0 || hidden <= 0 || inter <= 0 || experts <= 0 || top_k <= 0 || top_k > experts) {
         set_error("moe: invalid dimensions");
@@ -182,22 +181,51 @@ GLMVX_EXPORT int32_t glmvx_moe_ffn(float *y, const float *x, int32_t tokens, int
     const size_t gu_stride = static_cast<size_t>(inter) * (hidden / blk) * bytes;
     const size_t dn_stride = static_cast<size_t>(hidden) * (inter / blk) * bytes;
     const int P = tokens * top_k + (shared ? tokens : 0);
-    int32_t st_ = glmvx_matmul_nt(w.logits, x, router_w, tokens, experts, hidden, st);
+    auto mark = [&](int i) -> int32_t {
+        if (events) GLMVX_CUDA(cudaEventRecord(static_cast<cudaEvent_t>(events[i]), st));
+        return kOk;
+    };
+    int32_t st_ = mark(0);
     if (st_) return st_;
+    st_ = glmvx_matmul_nt(w.logits, x, router_w, tokens, experts, hidden, st);
+    if (st_ || (st_ = mark(1))) return st_;
     st_ = glmvx_router(w.ids, w.wts, w.logits, router_bias, tokens, experts, top_k, scale, st);
-    if (st_) return st_;
+    if (st_ || (st_ = mark(2))) return st_;
     moe_group_kernel<<<1, kGroupThreads, 0, st>>>(w.ids, w.wts, tokens, top_k, experts, shared, gate, up, down,
                                                   gu_stride, dn_stride, shared_gate, shared_up, shared_down, x,
                                                   hidden, inter, w.g_out, w.u_out, w.pair_out, w.gu_jobs, w.dn_jobs,
                                                   w.comb, w.combw, device_error_word());
-    if ((st_ = launch_status("moe_group_kernel"))) return st_;
-    if ((st_ = gemv_jobs_device(kind, w.gu_jobs, 2 * P, inter, hidden, gate, x, st))) return st_;
-    if ((st_ = gemv_jobs_device(kind, w.dn_jobs, P, hidden, inter, down, w.g_out, st))) return st_;
+    if ((st_ = launch_status("moe_group_kernel")) || (st_ = mark(3))) return st_;
+    if ((st_ = gemv_jobs_device(kind, w.gu_jobs, 2 * P, inter, hidden, gate, x, st)) || (st_ = mark(4))) return st_;
+    if ((st_ = gemv_jobs_device(kind, w.dn_jobs, P, hidden, inter, down, w.g_out, st)) || (st_ = mark(5))) return st_;
     moe_combine_kernel<<<dim3((hidden + 255) / 256, tokens), 256, 0, st>>>(y, w.pair_out, w.comb, w.combw, tokens,
                                                                            top_k, hidden, shared);
-    if ((st_ = launch_status("moe_combine_kernel"))) return st_;
+    if ((st_ = launch_status("moe_combine_kernel")) || (st_ = mark(6))) return st_;
     if (ids_out) GLMVX_CUDA(cudaMemcpyAsync(ids_out, w.ids, 4ull * tokens * top_k, cudaMemcpyDeviceToDevice, st));
     if (weights_out)
         GLMVX_CUDA(cudaMemcpyAsync(weights_out, w.wts, 4ull * tokens * top_k, cudaMemcpyDeviceToDevice, st));
     return kOk;
+}
+
+GLMVX_EXPORT int32_t glmvx_moe_ffn(float *y, const float *x, int32_t tokens, int32_t hidden, int32_t inter,
+                                   const float *router_w, const float *router_bias, int32_t experts, int32_t top_k,
+                                   float scale, int32_t kind, const uint8_t *gate, const uint8_t *up,
+                                   const uint8_t *down, const uint8_t *shared_gate, const uint8_t *shared_up,
+                                   const uint8_t *shared_down, void *workspace, uint64_t workspace_bytes,
+                                   int32_t *ids_out, float *weights_out, void *stream) {
+    return moe_ffn(y, x, tokens, hidden, inter, router_w, router_bias, experts, top_k, scale, kind, gate, up, down,
+                   shared_gate, shared_up, shared_down, workspace, workspace_bytes, ids_out, weights_out, stream,
+                   nullptr);
+}
+
+// As glmvx_moe_ffn, also recording events[0..6] on the stream around its six
+// stages (router logits, routing, grouping, gate+up, down, combine).
+GLMVX_EXPORT int32_t glmvx_moe_ffn_profiled(float *y, const float *x, int32_t tokens, int32_t hidden, int32_t inter,
+                                            const float *router_w, const float *router_bias, int32_t experts,
+                                            int32_t top_k, float scale, int32_t kind, const uint8_t *gate,
+                                            const uint8_t *up, const uint8_t *down, const uint8_t *shared_gate,
+                                            const uint8_t *shared_up, const uint8_t *shared_down, void *workspace,
+                                            uint64_t workspace_bytes, void *const *events, void *stream) {
+    return moe_ffn(y, x, tokens, hidden, inter, router_w, router_bias, experts, top_k, scale, kind, gate, up, down,
+                   shared_gate, shared_up, shared_down, workspace, workspace_bytes, nullptr, nullptr, stream, events);
 }

@@ -81,6 +81,8 @@ SIGNATURES = {
     'glmvx_moe_workspace_bytes': ([_I32, _I32, _I32, _I32, _I32, _I32], _I64),
     'glmvx_moe_ffn': ([_P, _P, _I32, _I32, _I32, _P, _P, _I32, _I32, _F32, _I32, _P, _P, _P, _P, _P, _P, _P, _U64,
                        _P, _P, _P], _I32),
+    'glmvx_moe_ffn_profiled': ([_P, _P, _I32, _I32, _I32, _P, _P, _I32, _I32, _F32, _I32, _P, _P, _P, _P, _P, _P, _P,
+                                _U64, _P, _P], _I32),
 }
 
 

@@ -188,6 +188,14 @@ int32_t glmvx_moe_ffn(float *y, const float *x, int32_t tokens, int32_t hidden, 
                       const uint8_t *gate, const uint8_t *up, const uint8_t *down, const uint8_t *shared_gate,
                       const uint8_t *shared_up, const uint8_t *shared_down, void *workspace, uint64_t workspace_bytes,
                       int32_t *ids_out, float *weights_out, void *stream);
+/* glmvx_moe_ffn that also records events[0..6] (cudaEvent_t) on the stream
+ * around its six stages: router logits, routing, grouping, gate+up, down,
+ * combine.  For profiling; no counterpart in the reference. */
+int32_t glmvx_moe_ffn_profiled(float *y, const float *x, int32_t tokens, int32_t hidden, int32_t inter,
+                               const float *router_w, const float *router_bias, int32_t experts, int32_t top_k,
+                               float scale, int32_t kind, const uint8_t *gate, const uint8_t *up, const uint8_t *down,
+                               const uint8_t *shared_gate, const uint8_t *shared_up, const uint8_t *shared_down,
+                               void *workspace, uint64_t workspace_bytes, void *const *events, void *stream);
 
 #ifdef __cplusplus
 }
