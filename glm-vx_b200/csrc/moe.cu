@@ -21,6 +21,8 @@
 // P = tokens*top_k (+ tokens for the shared expert).  Jobs are ordered by
 // expert so tokens sharing an expert stream its rows close together in time
 // (L2 reuse).
+#include <mutex>
+
 #include "codecs.cuh"
 #include "gemv_jobs.cuh"
 
@@ -228,4 +230,78 @@ GLMVX_EXPORT int32_t glmvx_moe_ffn_profiled(float *y, const float *x, int32_t to
                                             uint64_t workspace_bytes, void *const *events, void *stream) {
     return moe_ffn(y, x, tokens, hidden, inter, router_w, router_bias, experts, top_k, scale, kind, gate, up, down,
                    shared_gate, shared_up, shared_down, workspace, workspace_bytes, nullptr, nullptr, stream, events);
+}
+
+// ---------------------------------------------------------------------------
+// Scratch-free variant of glmvx_moe_ffn.
+//
+// Some callers cannot hand this layer a workspace: a host that embeds the
+// layer inside another runtime whose allocator owns the device's whole memory
+// budget (it has no way to carve out a buffer for us), or a decode loop that
+// must run with a fixed memory footprint and may not allocate when a larger
+// batch first appears.  This entry keeps its scratch in one file-scope device
+// array instead, so it never calls cudaMalloc, cudaFree or any allocating
+// library routine.
+//
+// Limits and rules:
+//  * The array holds kStaticMoeScratchBytes (16 MiB) per device; a layer whose
+//    workspace (glmvx_moe_workspace_bytes) is larger is rejected with
+//    kInvalid before anything is launched.  BASELINE-sized layers (hidden
+//    6144, intermediate 2048, top-8 plus a shared expert) fit up to 45 tokens.
+//  * Every scratch byte is written by an earlier stage of the same call
+//    before any stage reads it, so nothing has to start at zero and no
+//    clearing is done.
+//  * The first call on each device looks the array's address up with
+//    cudaGetSymbolAddress (with that device current) and caches it; make that
+//    first call before any stream capture on the device.
+//  * There is ONE array per device: calls whose work overlaps in time (two
+//    streams, or two host threads, on the same device) race on it.  Callers
+//    serialise such calls, e.g. by issuing them on one stream.
+constexpr size_t kStaticMoeScratchBytes = 16ull << 20;
+constexpr int kStaticMoeMaxDevices = 64;
+static __device__ __align__(256) unsigned char g_moe_scratch[kStaticMoeScratchBytes];
+
+static int32_t static_moe_scratch(void **out) {
+    static std::mutex mu;
+    static void *cached[kStaticMoeMaxDevices] = {nullptr};
+    int dev = 0;
+    GLMVX_CUDA(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= kStaticMoeMaxDevices) {
+        set_error("moe static: device %d is beyond the %d devices this entry supports", dev, kStaticMoeMaxDevices);
+        return kInvalid;
+    }
+    std::lock_guard<std::mutex> lock(mu);
+    if (!cached[dev]) {
+        void *p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_moe_scratch);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(g_moe_scratch)");
+        cached[dev] = p;
+    }
+    *out = cached[dev];
+    return kOk;
+}
+
+GLMVX_EXPORT int32_t glmvx_moe_ffn_static(float *y, const float *x, int32_t tokens, int32_t hidden, int32_t inter,
+                                          const float *router_w, const float *router_bias, int32_t experts,
+                                          int32_t top_k, float scale, int32_t kind, const uint8_t *gate,
+                                          const uint8_t *up, const uint8_t *down, const uint8_t *shared_gate,
+                                          const uint8_t *shared_up, const uint8_t *shared_down, int32_t *ids_out,
+                                          float *weights_out, void *stream) {
+    if (tokens < 0 || hidden <= 0 || inter <= 0 || experts <= 0 || top_k <= 0) {
+        set_error("moe: invalid dimensions");
+        return kInvalid;
+    }
+    const bool shared = shared_gate && shared_up && shared_down;
+    const size_t need = carve(nullptr, tokens, hidden, inter, experts, top_k, shared).bytes;
+    if (need > kStaticMoeScratchBytes) {
+        set_error("moe static: this layer needs %zu scratch bytes; the static scratch holds %zu", need,
+                  kStaticMoeScratchBytes);
+        return kInvalid;
+    }
+    void *scratch = nullptr;
+    const int32_t st = static_moe_scratch(&scratch);
+    if (st) return st;
+    return moe_ffn(y, x, tokens, hidden, inter, router_w, router_bias, experts, top_k, scale, kind, gate, up, down,
+                   shared_gate, shared_up, shared_down, scratch, kStaticMoeScratchBytes, ids_out, weights_out, stream,
+                   nullptr);
 }

@@ -196,6 +196,18 @@ int32_t glmvx_moe_ffn_profiled(float *y, const float *x, int32_t tokens, int32_t
                                float scale, int32_t kind, const uint8_t *gate, const uint8_t *up, const uint8_t *down,
                                const uint8_t *shared_gate, const uint8_t *shared_up, const uint8_t *shared_down,
                                void *workspace, uint64_t workspace_bytes, void *const *events, void *stream);
+/* glmvx_moe_ffn without a caller workspace, for callers that cannot allocate
+ * device memory (an embedding runtime that owns the whole memory budget, a
+ * decode loop with a fixed footprint).  No counterpart in the reference.
+ * Scratch is one 16 MiB file-scope device array per device: layers needing
+ * more (glmvx_moe_workspace_bytes) are rejected with -1.  The first call on a
+ * device looks the array up; make it before any stream capture.  Calls that
+ * overlap in time on one device race on the array: issue them on one stream. */
+int32_t glmvx_moe_ffn_static(float *y, const float *x, int32_t tokens, int32_t hidden, int32_t inter,
+                             const float *router_w, const float *router_bias, int32_t experts, int32_t top_k,
+                             float scale, int32_t kind, const uint8_t *gate, const uint8_t *up, const uint8_t *down,
+                             const uint8_t *shared_gate, const uint8_t *shared_up, const uint8_t *shared_down,
+                             int32_t *ids_out, float *weights_out, void *stream);
 
 #ifdef __cplusplus
 }
