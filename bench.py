@@ -51,6 +51,7 @@ ROOT = Path(__file__).resolve().parent
 METRIC = 'decode tok/s (1/2/4/8 B200) + fused dequant-GEMV HBM GB/s vs 8 TB/s peak'
 EXPERTS, HIDDEN, INTER, TOPK, SCALE, KIND = 256, 6144, 2048, 8, 2.5, 19
 TOKENS = 32
+PROFILE_EXPERTS = 32
 IQ1_BLOCK, IQ1_BYTES = 256, 50
 EXPERT_MATRIX_BYTES = INTER * (HIDDEN // IQ1_BLOCK) * IQ1_BYTES  # 2,457,600; gate, up and down are equal
 # dram bytes per launch of the dominant kernel from the committed ncu capture, None until captured.
@@ -69,8 +70,8 @@ def peaks():
         return 6650.0, 'fallback'
 
 
-def synthetic_layer(seed=0):
-    """BASELINE config-2 weights as host arrays (about 1.9 GB)."""
+def synthetic_layer(seed=0, experts=EXPERTS):
+    """BASELINE config-2 weights as host arrays (about 1.9 GB at 256 experts)."""
     rng = np.random.default_rng(seed)
 
     def iq1(count, rows, cols):
@@ -79,9 +80,9 @@ def synthetic_layer(seed=0):
         raw[:, :2] = (np.abs(rng.normal(size=(blocks, 1))) * 0.02).astype(np.float16).view(np.uint8)
         return raw.reshape(-1)
 
-    return dict(router=(rng.normal(size=(EXPERTS, HIDDEN)) * 0.02).astype(np.float32),
-                bias=(rng.normal(size=EXPERTS) * 0.01).astype(np.float32),
-                gate=iq1(EXPERTS, INTER, HIDDEN), up=iq1(EXPERTS, INTER, HIDDEN), down=iq1(EXPERTS, HIDDEN, INTER),
+    return dict(router=(rng.normal(size=(experts, HIDDEN)) * 0.02).astype(np.float32),
+                bias=(rng.normal(size=experts) * 0.01).astype(np.float32),
+                gate=iq1(experts, INTER, HIDDEN), up=iq1(experts, INTER, HIDDEN), down=iq1(experts, HIDDEN, INTER),
                 shared=(iq1(1, INTER, HIDDEN), iq1(1, INTER, HIDDEN), iq1(1, HIDDEN, INTER)))
 
 
@@ -472,6 +473,34 @@ def run_ours(args, ranks):
     return 0
 
 
+def run_profile_case(args):
+    """Small case for kernel captures: the config-2 layer shapes with only
+    PROFILE_EXPERTS experts (about 240 MB of IQ1_S, still above L2), TOKENS
+    rows, three untimed warm-up forwards then three more.  Prints one status
+    line; no benchmark numbers."""
+    use_ours()
+    from gpu.backend import GPUBackend
+    from gpu import runtime as rt
+    from gpu.moe import MoELayer
+    backend = GPUBackend(0)
+    layer = synthetic_layer(0, PROFILE_EXPERTS)
+    moe = MoELayer(backend, layer['router'], layer['bias'], KIND, layer['gate'], layer['up'], layer['down'],
+                   HIDDEN, INTER, TOPK, SCALE, shared=layer['shared'])
+    x = np.random.default_rng(100).normal(size=(TOKENS, HIDDEN)).astype(np.float32)
+    xd, yd = rt.DeviceBuffer(x.nbytes), rt.DeviceBuffer(x.nbytes)
+    xd.upload(x, backend.stream.handle)
+    for _ in range(6):
+        moe.forward_device(yd.ptr, xd.ptr, TOKENS)
+    backend.stream.synchronize()
+    backend.device.check_device_error()
+    print(f'profile case ok: {PROFILE_EXPERTS} experts, {TOKENS} tokens, 6 forwards', flush=True)
+    xd.close()
+    yd.close()
+    moe.close()
+    backend.close()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument('--gpus', type=int, default=1)
@@ -480,7 +509,11 @@ def main():
     ap.add_argument('--impl', choices=('ours', 'reference'), default='ours')
     ap.add_argument('--cpu-seconds', type=float, default=10.0)
     ap.add_argument('--no-cpu-baseline', action='store_true')
+    ap.add_argument('--profile-case', action='store_true',
+                    help='run the small kernel-capture case (one GPU) instead of the benchmark')
     args = ap.parse_args()
+    if args.profile_case:
+        return run_profile_case(args)
     if args.warmup < 3:
         ap.error('--warmup must be >= 3')
     ranks = Ranks()
