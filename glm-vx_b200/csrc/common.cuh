@@ -123,6 +123,18 @@ __device__ __forceinline__ void report_device_error(int *err, int code) {
     if (err) atomicCAS(err, 0, code);
 }
 
+// Programmatic dependent launch: let the next kernel on the stream start its
+// prologue / wait until the previous kernel's writes are visible.
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void allow_dependent_launch() { asm volatile("griddepcontrol.launch_dependents;"); }
+
+// SwiGLU element x*sigmoid(x)*u with the reference's branch-stable sigmoid
+// and rounding order (kernels/kernels.vx:8-15,56-60).
+__device__ __forceinline__ float silu_mul(float g, float u) {
+    const float sg = g >= 0.0f ? 1.0f / (1.0f + expf(0.0f - g)) : expf(g) / (1.0f + expf(g));
+    return __fmul_rn(__fmul_rn(g, sg), u);
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

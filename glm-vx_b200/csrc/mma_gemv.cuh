@@ -1,0 +1,59 @@
+// Integer tensor-core path of the packed GEMV/GEMM (packed_mma.cu), shared
+// with the MoE layer (moe.cu).
+//
+// The packed weights are multiplied in their integer form (Q8_0 bytes, Q4_K
+// nibbles, IQ1_S codebook entries) by int8 `mma.sync` instructions.  The f32
+// activations enter as exact integers: a "prepared row" holds, per 256-column
+// chunk, a power-of-two exponent E and the rounded integer x*2^E (|x*2^E| <
+// 2^30) split into four signed int8 limbs, so that
+//     x*2^E = limb0*2^24 + limb1*2^16 + limb2*2^8 + limb3
+// and every product sum inside the tensor core is exact int32 arithmetic.
+// The block scales are applied in f32 afterwards.  Rounding x*2^E to an
+// integer changes each activation by at most 2^-31 of the largest magnitude
+// in its chunk; everything else is ordinary f32 accumulation.
+#pragma once
+
+#include "common.cuh"
+
+namespace glmvx {
+
+// Prepared activation row of K columns (K % 256 == 0):
+//   [0, 4K)                 int8 limbs [4][K], limb 0 most significant
+//   [4K, +4*K/256)          int32 E per 256-column chunk, in [-98, 156], or
+//                           kPrepNonFinite when the chunk holds a non-finite value
+//   [align16(..), +4*K/32)  f32 sum of each 32-column sub-block of the activations
+// Rows are 256-byte aligned.
+constexpr int32_t kPrepNonFinite = 0x7fffffff;
+__host__ __device__ inline size_t prep_scale_offset(int K) { return 4ull * K; }
+__host__ __device__ inline size_t prep_sums_offset(int K) {
+    return (4ull * K + 4ull * (K / 256) + 15) & ~static_cast<size_t>(15);
+}
+__host__ __device__ inline size_t prep_stride(int K) {
+    return (prep_sums_offset(K) + 4ull * (K / 32) + 255) & ~static_cast<size_t>(255);
+}
+
+// One weight matrix applied to up to two prepared activation rows.
+struct MmaJob {
+    const uint8_t *w;      // packed rows [rows_per_job][row_bytes], 16-byte aligned
+    const uint8_t *xp[2];  // prepared rows; nullptr marks an unused slot
+    float *out[2];         // out[s][r] for r < rows_per_job
+};
+
+// True when `kind` and the column count take the tensor-core path.
+bool mma_supported(int kind, int cols);
+
+// Prepare `rows` activation rows x[r][0..cols) (x2 set: SwiGLU(x, x2) =
+// x*sigmoid(x)*x2 per element) into prep + r*prep_stride(cols).
+int32_t prep_rows_device(uint8_t *prep, const float *x, const float *x2, int rows, int cols, cudaStream_t stream);
+
+// Tensor-core packed GEMV over a job list.
+//  * jobs != nullptr: device-resident descriptors; the job count is
+//    *njobs_dev when njobs_dev is set (read on the device after the previous
+//    kernel completes, clamped to max_jobs), else max_jobs.
+//  * jobs == nullptr: `batch` tokens against one matrix: job j applies job0.w
+//    to prepared rows 2j and 2j+1 of job0.xp[0] (stride prep_stride(cols))
+//    and writes rows of job0.out[0] (stride rows_per_job floats).
+int32_t mma_gemv_device(int32_t kind, const MmaJob &job0, const MmaJob *jobs, const int *njobs_dev, int max_jobs,
+                        int batch, int rows_per_job, int cols, cudaStream_t stream);
+
+}  // namespace glmvx

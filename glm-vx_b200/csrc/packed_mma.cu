@@ -1,0 +1,616 @@
+// Packed-GGUF GEMV / small-batch GEMM on the sm_100a tensor cores (int8 mma).
+//
+// Same contract as the reference's fused dequantise+dot kernels
+// (glm_vx_packed_<fmt>, kernels/packed.vx:154-470, and the batch_v2 forms,
+// kernels/packed.vx:473ff): out[t][r] = sum_j w[r][j] * x[t][j] in f32 with
+// the weights decoded per GGML block.  Here the decode stops at the block's
+// integers and the multiply runs on the tensor cores:
+//
+//   Q8_0   w = d * q                      A = q (s8), per 32-column block
+//   Q4_K   w = d*sc * q - dmin*m          A = q (u8, 0..15); the min term
+//                                         dmin*m*sum(x) uses the prepared
+//                                         sub-block sums of x
+//   IQ1_S  w = d*(2s+1) * (grid + delta)  A = 8*grid +/- 1 (s8) from a shared
+//                                         table of 4096 entries (sign of delta
+//                                         selects the half); the odd
+//                                         multiplier 2s+1 is applied to the
+//                                         int32 result, d/8 in f32
+//
+// The activations come as prepared rows (mma_gemv.cuh): four int8 limbs of
+// x*2^E.  One m16n8k32 instruction takes 16 weight rows x 32 columns against
+// 8 columns = 2 tokens x 4 limbs, so each weight byte is decoded once for
+// both tokens of a job and every product is exact; the four limb partial
+// sums are recombined in f32 at the end of the tile.
+//
+// Thread/fragment layout (m16n8k32, A row-major, B column-major): lane
+// (g = lane/4, t = lane%4) holds A rows g and g+8 and B column g, each for the
+// logical k = 4t..4t+3 and 4t+16..4t+19.  Those eight logical k are mapped to
+// the eight physical columns 8t..8t+7 of the 32-column sub-block, for A and B
+// alike, so a lane's A bytes are the 8 consecutive weights its group holds in
+// the GGML block and its B bytes are 8 consecutive limb bytes.
+//
+// Kernel structure (mma_rows_kernel): a persistent grid, one CTA per SM, each
+// CTA owning a balanced range of the job list's rows.  A producer warp
+// streams tiles of 16*RG rows into a ring of shared-memory stages with one
+// 1-D bulk copy (TMA) per row (rows are padded in shared memory so the 8 row
+// groups of a fragment fall in distinct banks); S*RG consumer warps each take
+// 16 rows x 512 columns of a tile (S = cols/512 column slices, RG row
+// groups), keep the B fragments of their slice in registers, and reduce the S
+// slice partials of a row in fixed order through shared memory after every
+// tile.  Waits on mbarriers are bounded (2 s) and report through the device
+// error word.
+#include <algorithm>
+#include <type_traits>
+
+#include "codecs.cuh"
+#include "mma_gemv.cuh"
+
+namespace glmvx {
+
+// ------------------------------------------------------------- fragments ---
+
+__device__ __forceinline__ void mma_s8s8(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                         uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};"
+        : "=r"(c[0]), "=r"(c[1]), "=r"(c[2]), "=r"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
+}
+
+__device__ __forceinline__ void mma_u8s8(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                         uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};"
+        : "=r"(c[0]), "=r"(c[1]), "=r"(c[2]), "=r"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
+}
+
+// 2^e for e in [-126, 127], exactly.
+__device__ __forceinline__ float pow2(int e) { return __int_as_float((127 + e) << 23); }
+
+__device__ __forceinline__ uint32_t lds32(const uint8_t *p) { return *reinterpret_cast<const uint32_t *>(p); }
+__device__ __forceinline__ uint2 lds64(const uint8_t *p) { return *reinterpret_cast<const uint2 *>(p); }
+
+// Per-format work on one 256-column chunk of a 16-row fragment.  p0/p1 point
+// at rows g and g+8 of the warp's column slice in shared memory, b[] are the
+// slice's B fragments (16 sub-blocks), xs is the chunk's scale relative to
+// the slice's larger-magnitude chunk (for this lane's accumulator token), sums the slice's
+// sub-block activation sums.  af[] are the f32 accumulators (rows g, g+8 x
+// this lane's two limb columns), am[] the min-term accumulators of rows g, g+8.
+template <class F>
+struct MmaFmt;
+
+template <>
+struct MmaFmt<FmtIQ1_S> {
+    static constexpr int kTableBytes = 4096 * 8, kSubPerBlock = 8, kBlockBytes = 50;
+    static constexpr bool kMins = false;
+    // Entry e: the 8 grid values g of index e & 2047 as int8 8*g+1 (e < 2048,
+    // delta = +1/8) or 8*g-1 (delta = -1/8).
+    __device__ static void init_table(uint8_t *table, int tid, int nthreads) {
+        const uint2 *grid = reinterpret_cast<const uint2 *>(g_codebooks + kTabIq1sGrid);
+        for (int e = tid; e < 4096; e += nthreads) {
+            const uint2 src = grid[e & 2047];
+            const int delta = (e & 2048) ? -1 : 1;
+            uint32_t lo = 0, hi = 0;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                lo |= (static_cast<uint32_t>(8 * s8(src.x >> (8 * k)) + delta) & 0xffu) << (8 * k);
+                hi |= (static_cast<uint32_t>(8 * s8(src.y >> (8 * k)) + delta) & 0xffu) << (8 * k);
+            }
+            reinterpret_cast<uint2 *>(table)[e] = make_uint2(lo, hi);
+        }
+    }
+    template <int C>
+    __device__ __forceinline__ static void chunk(const uint8_t *p0, const uint8_t *p1, int t, const uint32_t (&b)[16][2],
+                                                 float xs, const float *, const uint8_t *table, float (&af)[4],
+                                                 float (&)[2]) {
+        const uint8_t *q0 = p0 + C * kBlockBytes, *q1 = p1 + C * kBlockBytes;
+        int ai[4] = {0, 0, 0, 0};
+#pragma unroll
+        for (int s = 0; s < 8; ++s) {
+            const uint32_t h0 = u16(q0 + 34 + 2 * s), h1 = u16(q1 + 34 + 2 * s);
+            const uint32_t i0 = q0[2 + 4 * s + t] | (((h0 >> (3 * t)) & 7u) << 8) | ((h0 >> 4) & 0x800u);
+            const uint32_t i1 = q1[2 + 4 * s + t] | (((h1 >> (3 * t)) & 7u) << 8) | ((h1 >> 4) & 0x800u);
+            const uint2 a0 = lds64(table + 8 * i0), a1 = lds64(table + 8 * i1);
+            int c[4];
+            mma_s8s8(c, a0.x, a1.x, a0.y, a1.y, b[8 * C + s][0], b[8 * C + s][1]);
+            const int dl0 = 2 * static_cast<int>((h0 >> 12) & 7u) + 1, dl1 = 2 * static_cast<int>((h1 >> 12) & 7u) + 1;
+            ai[0] += dl0 * c[0];
+            ai[1] += dl0 * c[1];
+            ai[2] += dl1 * c[2];
+            ai[3] += dl1 * c[3];
+        }
+        const float s0 = h2f(u16(q0)) * (0.125f * xs), s1 = h2f(u16(q1)) * (0.125f * xs);
+        af[0] = fmaf(s0, static_cast<float>(ai[0]), af[0]);
+        af[1] = fmaf(s0, static_cast<float>(ai[1]), af[1]);
+        af[2] = fmaf(s1, static_cast<float>(ai[2]), af[2]);
+        af[3] = fmaf(s1, static_cast<float>(ai[3]), af[3]);
+    }
+};
+
+template <>
+struct MmaFmt<FmtQ8_0> {
+    static constexpr int kTableBytes = 0, kSubPerBlock = 1, kBlockBytes = 34;
+    static constexpr bool kMins = false;
+    __device__ static void init_table(uint8_t *, int, int) {}
+    // Eight 34-byte blocks.  A block at an even index within the slice starts
+    // 4-byte aligned (its bytes follow a 2-byte scale), one at an odd index
+    // 2 bytes past alignment, so its bytes are.
+    template <int C>
+    __device__ __forceinline__ static void chunk(const uint8_t *p0, const uint8_t *p1, int t, const uint32_t (&b)[16][2],
+                                                 float xs, const float *, const uint8_t *, float (&af)[4],
+                                                 float (&)[2]) {
+#pragma unroll
+        for (int s = 0; s < 8; ++s) {
+            const int i = 8 * C + s;
+            const uint8_t *q0 = p0 + i * kBlockBytes, *q1 = p1 + i * kBlockBytes;
+            uint32_t a0, a1, a2, a3;
+            if ((i & 1) == 0) {
+                const uint32_t w0 = lds32(q0 + 8 * t), w1 = lds32(q0 + 8 * t + 4), w2 = lds32(q0 + 8 * t + 8);
+                const uint32_t v0 = lds32(q1 + 8 * t), v1 = lds32(q1 + 8 * t + 4), v2 = lds32(q1 + 8 * t + 8);
+                a0 = __funnelshift_r(w0, w1, 16);
+                a2 = __funnelshift_r(w1, w2, 16);
+                a1 = __funnelshift_r(v0, v1, 16);
+                a3 = __funnelshift_r(v1, v2, 16);
+            } else {
+                a0 = lds32(q0 + 2 + 8 * t);
+                a2 = lds32(q0 + 6 + 8 * t);
+                a1 = lds32(q1 + 2 + 8 * t);
+                a3 = lds32(q1 + 6 + 8 * t);
+            }
+            int c[4];
+            mma_s8s8(c, a0, a1, a2, a3, b[i][0], b[i][1]);
+            const float s0 = h2f(u16(q0)) * xs, s1 = h2f(u16(q1)) * xs;
+            af[0] = fmaf(s0, static_cast<float>(c[0]), af[0]);
+            af[1] = fmaf(s0, static_cast<float>(c[1]), af[1]);
+            af[2] = fmaf(s1, static_cast<float>(c[2]), af[2]);
+            af[3] = fmaf(s1, static_cast<float>(c[3]), af[3]);
+        }
+    }
+};
+
+template <>
+struct MmaFmt<FmtQ4_K> {
+    static constexpr int kTableBytes = 0, kSubPerBlock = 8, kBlockBytes = 144;
+    static constexpr bool kMins = true;
+    __device__ static void init_table(uint8_t *, int, int) {}
+    // Byte j of the 6-bit scale (or min) words of a K-quant head, sub-blocks
+    // 0..3 in `lo`, 4..7 in `hi` (kernels/packed.vx:107-120 on packed words).
+    __device__ __forceinline__ static int sel6(uint32_t lo, uint32_t hi, int j) {
+        return static_cast<int>(((j < 4 ? lo : hi) >> (8 * (j & 3))) & 0xffu);
+    }
+    template <int C>
+    __device__ __forceinline__ static void chunk(const uint8_t *p0, const uint8_t *p1, int t, const uint32_t (&b)[16][2],
+                                                 float xs, const float *sums, const uint8_t *, float (&af)[4],
+                                                 float (&am)[2]) {
+        const uint8_t *q0 = p0 + C * kBlockBytes, *q1 = p1 + C * kBlockBytes;
+        const uint4 h0 = *reinterpret_cast<const uint4 *>(q0), h1 = *reinterpret_cast<const uint4 *>(q1);
+        const uint32_t sl0 = h0.y & 0x3F3F3F3Fu, sh0 = (h0.w & 0x0F0F0F0Fu) | ((h0.y >> 2) & 0x30303030u);
+        const uint32_t sl1 = h1.y & 0x3F3F3F3Fu, sh1 = (h1.w & 0x0F0F0F0Fu) | ((h1.y >> 2) & 0x30303030u);
+        int ai[4] = {0, 0, 0, 0};
+#pragma unroll
+        for (int m = 0; m < 4; ++m) {
+            const uint2 w0 = lds64(q0 + 16 + 32 * m + 8 * t), w1 = lds64(q1 + 16 + 32 * m + 8 * t);
+            int c[4];
+            mma_u8s8(c, w0.x & 0x0F0F0F0Fu, w1.x & 0x0F0F0F0Fu, w0.y & 0x0F0F0F0Fu, w1.y & 0x0F0F0F0Fu,
+                     b[8 * C + 2 * m][0], b[8 * C + 2 * m][1]);
+            int sc0 = sel6(sl0, sh0, 2 * m), sc1 = sel6(sl1, sh1, 2 * m);
+            ai[0] += sc0 * c[0];
+            ai[1] += sc0 * c[1];
+            ai[2] += sc1 * c[2];
+            ai[3] += sc1 * c[3];
+            mma_u8s8(c, (w0.x >> 4) & 0x0F0F0F0Fu, (w1.x >> 4) & 0x0F0F0F0Fu, (w0.y >> 4) & 0x0F0F0F0Fu,
+                     (w1.y >> 4) & 0x0F0F0F0Fu, b[8 * C + 2 * m + 1][0], b[8 * C + 2 * m + 1][1]);
+            sc0 = sel6(sl0, sh0, 2 * m + 1);
+            sc1 = sel6(sl1, sh1, 2 * m + 1);
+            ai[0] += sc0 * c[0];
+            ai[1] += sc0 * c[1];
+            ai[2] += sc1 * c[2];
+            ai[3] += sc1 * c[3];
+        }
+        const float s0 = h2f(h0.x & 0xffffu) * xs, s1 = h2f(h1.x & 0xffffu) * xs;
+        af[0] = fmaf(s0, static_cast<float>(ai[0]), af[0]);
+        af[1] = fmaf(s0, static_cast<float>(ai[1]), af[1]);
+        af[2] = fmaf(s1, static_cast<float>(ai[2]), af[2]);
+        af[3] = fmaf(s1, static_cast<float>(ai[3]), af[3]);
+        if (sums) {
+            const uint32_t ml0 = h0.z & 0x3F3F3F3Fu, mh0 = ((h0.w >> 4) & 0x0F0F0F0Fu) | ((h0.z >> 2) & 0x30303030u);
+            const uint32_t ml1 = h1.z & 0x3F3F3F3Fu, mh1 = ((h1.w >> 4) & 0x0F0F0F0Fu) | ((h1.z >> 2) & 0x30303030u);
+            const float4 xa = __ldg(reinterpret_cast<const float4 *>(sums + 8 * C));
+            const float4 xb = __ldg(reinterpret_cast<const float4 *>(sums + 8 * C) + 1);
+            const float xv[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
+            float m0 = 0.0f, m1 = 0.0f;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                m0 = fmaf(static_cast<float>(sel6(ml0, mh0, j)), xv[j], m0);
+                m1 = fmaf(static_cast<float>(sel6(ml1, mh1, j)), xv[j], m1);
+            }
+            am[0] = fmaf(h2f(h0.x >> 16), m0, am[0]);
+            am[1] = fmaf(h2f(h1.x >> 16), m1, am[1]);
+        }
+    }
+};
+
+// ----------------------------------------------------------------- kernel ---
+
+constexpr int kSliceSub = 16;  // 32-column sub-blocks per warp column slice (512 columns)
+
+__device__ __forceinline__ MmaJob job_at(const MmaJob &job0, const MmaJob *jobs, int j, int batch, int rows_per_job,
+                                         size_t pstride) {
+    if (jobs) return jobs[j];
+    MmaJob r;
+    r.w = job0.w;
+#pragma unroll
+    for (int s = 0; s < 2; ++s) {
+        const int tok = 2 * j + s;
+        const bool on = tok < batch;
+        r.xp[s] = on ? job0.xp[0] + static_cast<size_t>(tok) * pstride : nullptr;
+        r.out[s] = on ? job0.out[0] + static_cast<size_t>(tok) * rows_per_job : nullptr;
+    }
+    return r;
+}
+
+template <class F, int S, int RG>
+__global__ void __launch_bounds__((S * RG + 1) * 32, 1)
+    mma_rows_kernel(MmaJob job0, const MmaJob *__restrict__ jobs, const int *njobs_dev, int max_jobs, int batch,
+                    int rows_per_job, int cols, int row_bytes, int srow, int stages, int stage_stride, int *err) {
+    using MF = MmaFmt<F>;
+    constexpr int NW = S * RG, R = 16 * RG;
+    extern __shared__ __align__(128) uint8_t smem[];
+    uint8_t *table = smem + static_cast<size_t>(stages) * stage_stride;
+    float *red = reinterpret_cast<float *>(table + MF::kTableBytes);  // [2][R][S][2]
+    uint64_t *full = reinterpret_cast<uint64_t *>(red + 2 * R * S * 2);
+    uint64_t *empty = full + stages;
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(empty + stages);  // [RG]
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const size_t pstride = prep_stride(cols);
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < stages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], NW);
+        }
+        for (int i = 0; i < RG; ++i) abort_flag[i] = 0;
+        fence_mbar_init();
+    }
+    __syncthreads();
+    allow_dependent_launch();
+
+    // The job count and, for device-built lists, the descriptors come from
+    // the previous kernel: read them only after the grid dependency.
+    auto range = [&](int &r_begin, int &r_end) {
+        int nj = max_jobs;
+        if (njobs_dev) nj = min(max(*njobs_dev, 0), max_jobs);
+        const int64_t rows = static_cast<int64_t>(rows_per_job) * nj;
+        r_begin = static_cast<int>(rows * blockIdx.x / gridDim.x);
+        r_end = static_cast<int>(rows * (blockIdx.x + 1) / gridDim.x);
+    };
+    auto tile_end = [&](int r0, int r_end) {
+        return min(min(r0 + R, r_end), (r0 / rows_per_job + 1) * rows_per_job);
+    };
+
+    if (warp == NW) {  // producer: one bulk copy per row, issued by the 32 lanes
+        if (jobs) grid_dependency_wait();
+        int r_begin, r_end;
+        range(r_begin, r_end);
+        int k = 0;
+        for (int r0 = r_begin; r0 < r_end; r0 = tile_end(r0, r_end), ++k) {
+            const int s = k % stages;
+            int ok = 1;
+            if (lane == 0) ok = mbar_wait_bounded(&empty[s], ((k / stages) & 1) ^ 1);
+            ok = __shfl_sync(0xffffffffu, ok, 0);
+            if (!ok) {
+                if (lane == 0) report_device_error(err, kDevErrEmptyWait);
+                break;
+            }
+            const int nr = tile_end(r0, r_end) - r0;
+            const MmaJob j = job_at(job0, jobs, r0 / rows_per_job, batch, rows_per_job, pstride);
+            if (lane == 0) mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(nr) * row_bytes);
+            __syncwarp();
+            uint8_t *stage = smem + static_cast<size_t>(s) * stage_stride;
+            for (int i = lane; i < nr; i += 32)
+                bulk_g2s(stage + static_cast<size_t>(i) * srow,
+                         j.w + static_cast<size_t>((r0 + i) % rows_per_job) * row_bytes, row_bytes, &full[s]);
+        }
+        return;
+    }
+
+    MF::init_table(table, threadIdx.x, NW * 32);
+    grid_dependency_wait();  // prepared activations come from the previous kernel
+    int r_begin, r_end;
+    range(r_begin, r_end);
+    if (MF::kTableBytes) named_barrier_sync(1, NW * 32);
+
+    const int sw = warp % S, rg = warp / S;
+    const int g = lane >> 2, t = lane & 3;
+    const int u0 = sw * kSliceSub;  // first sub-block of the slice
+    const size_t slice_off = static_cast<size_t>(u0 / MF::kSubPerBlock) * MF::kBlockBytes;
+    const size_t scale_off = prep_scale_offset(cols), sums_off = prep_sums_offset(cols);
+    uint32_t b[kSliceSub][2];
+    float xs[2] = {0.0f, 0.0f}, down[2] = {0.0f, 0.0f};
+    const float *sums = nullptr;
+    MmaJob J{};
+    int loaded = -1;
+    int k = 0;
+    for (int r0 = r_begin; r0 < r_end; r0 = tile_end(r0, r_end), ++k) {
+        const int job = r0 / rows_per_job;
+        if (job != loaded) {  // uniform across the CTA
+            loaded = job;
+            J = job_at(job0, jobs, job, batch, rows_per_job, pstride);
+            const uint8_t *xb = (g >> 2) ? J.xp[1] : J.xp[0];  // B column g: token g/4, limb g%4
+#pragma unroll
+            for (int u = 0; u < kSliceSub; ++u) {
+                uint2 v = make_uint2(0u, 0u);
+                if (xb)
+                    v = __ldg(reinterpret_cast<const uint2 *>(xb + static_cast<size_t>(g & 3) * cols + 32 * (u0 + u) +
+                                                              8 * t));
+                b[u][0] = v.x;
+                b[u][1] = v.y;
+            }
+            const uint8_t *xa = (t >> 1) ? J.xp[1] : J.xp[0];  // accumulator columns 2t, 2t+1: token t/2
+            // Chunk c holds x*2^E_c.  Relative to Eref = min(E_0, E_1) (the
+            // chunk of larger magnitude) its scale is 2^(Eref - E_c) <= 1;
+            // the absolute 2^-Eref is applied once per tile in two exact steps.
+            // A chunk more than 2^126 below the other contributes nothing.
+            int e0 = 0, e1 = 0;
+            if (xa) {
+                e0 = __ldg(reinterpret_cast<const int *>(xa + scale_off) + u0 / 8);
+                e1 = __ldg(reinterpret_cast<const int *>(xa + scale_off) + u0 / 8 + 1);
+            }
+            const bool bad = e0 == kPrepNonFinite || e1 == kPrepNonFinite;
+            const int eref = bad ? 0 : min(e0, e1);
+            xs[0] = (xa && !bad && eref - e0 >= -126) ? pow2(eref - e0) : 0.0f;
+            xs[1] = (xa && !bad && eref - e1 >= -126) ? pow2(eref - e1) : 0.0f;
+            down[0] = bad ? __int_as_float(0x7fc00000) : pow2(-(eref / 2));
+            down[1] = pow2(-(eref - eref / 2));
+            sums = (MF::kMins && xa) ? reinterpret_cast<const float *>(xa + sums_off) + u0 : nullptr;
+        }
+        const int s = k % stages;
+        const bool ok = mbar_wait_bounded(&full[s], (k / stages) & 1);
+        if (!ok) {
+            if (lane == 0) report_device_error(err, kDevErrFullWait);
+            abort_flag[rg] = 1;
+        }
+        const int nr = tile_end(r0, r_end) - r0;
+        float af[4] = {0.0f, 0.0f, 0.0f, 0.0f}, am[2] = {0.0f, 0.0f};
+        if (ok) {
+            const uint8_t *p0 =
+                smem + static_cast<size_t>(s) * stage_stride + static_cast<size_t>(16 * rg + g) * srow + slice_off;
+            const uint8_t *p1 = p0 + 8 * static_cast<size_t>(srow);
+            MF::template chunk<0>(p0, p1, t, b, xs[0], sums, table, af, am);
+            MF::template chunk<1>(p0, p1, t, b, xs[1], sums, table, af, am);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[s]);
+        }
+        // Recombine the limbs: lanes with even t hold limbs 0,1 (x 2^24, 2^16)
+        // and subtract the min term, odd t limbs 2,3 (x 2^8, 1).
+        const float whi = (t & 1) ? 256.0f : 16777216.0f, wlo = (t & 1) ? 1.0f : 65536.0f;
+        float v0 = fmaf(af[0], whi, af[1] * wlo) * down[0] * down[1];
+        float v1 = fmaf(af[2], whi, af[3] * wlo) * down[0] * down[1];
+        if (MF::kMins && !(t & 1)) {
+            v0 -= am[0];
+            v1 -= am[1];
+        }
+        v0 += __shfl_xor_sync(0xffffffffu, v0, 1);
+        v1 += __shfl_xor_sync(0xffffffffu, v1, 1);
+        float *rb = red + static_cast<size_t>(k & 1) * R * S * 2;
+        if (!(t & 1)) {
+            rb[((16 * rg + g) * S + sw) * 2 + (t >> 1)] = v0;
+            rb[((16 * rg + g + 8) * S + sw) * 2 + (t >> 1)] = v1;
+        }
+        named_barrier_sync(2 + rg, S * 32);
+        if (abort_flag[rg]) break;
+        if (sw == 0) {  // 16 rows x 2 tokens: S partials each, in fixed order
+            const int i = lane >> 1, slot = lane & 1;
+            float v = 0.0f;
+#pragma unroll
+            for (int q = 0; q < S; ++q) v += rb[((16 * rg + i) * S + q) * 2 + slot];
+            float *o = slot ? J.out[1] : J.out[0];
+            if (16 * rg + i < nr && o) o[(r0 + 16 * rg + i) % rows_per_job] = v;
+        }
+    }
+}
+
+// --------------------------------------------------------------- prepare ---
+
+// One warp per (row, 256-column chunk): 8 columns per lane.
+__global__ void __launch_bounds__(256)
+    prep_rows_kernel(uint8_t *__restrict__ prep, const float *__restrict__ x, const float *__restrict__ x2, int rows,
+                     int cols) {
+    grid_dependency_wait();
+    allow_dependent_launch();
+    const int chunks = cols >> 8;
+    const int64_t wid = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (wid >= static_cast<int64_t>(rows) * chunks) return;  // warp-uniform
+    const int row = static_cast<int>(wid / chunks), chunk = static_cast<int>(wid % chunks);
+    const int c0 = chunk * 256 + lane * 8;
+    const float4 *xr = reinterpret_cast<const float4 *>(x + static_cast<size_t>(row) * cols + c0);
+    float4 lo = __ldg(xr), hi = __ldg(xr + 1);
+    if (x2) {
+        const float4 *ur = reinterpret_cast<const float4 *>(x2 + static_cast<size_t>(row) * cols + c0);
+        const float4 ulo = __ldg(ur), uhi = __ldg(ur + 1);
+        lo = make_float4(silu_mul(lo.x, ulo.x), silu_mul(lo.y, ulo.y), silu_mul(lo.z, ulo.z), silu_mul(lo.w, ulo.w));
+        hi = make_float4(silu_mul(hi.x, uhi.x), silu_mul(hi.y, uhi.y), silu_mul(hi.z, uhi.z), silu_mul(hi.w, uhi.w));
+    }
+    const float v[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+    float mx = 0.0f;
+    bool finite = true;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        mx = fmaxf(mx, fabsf(v[i]));
+        finite &= isfinite(v[i]);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    finite = __all_sync(0xffffffffu, finite);
+    // 2^E puts the chunk's largest magnitude in [2^29, 2^30) (below 2^30 for
+    // subnormal maxima, E = 156); applied as two exact power-of-two factors.
+    const int ebits = (__float_as_int(mx) >> 23) & 0xff;
+    const int E = mx == 0.0f ? 0 : 156 - ebits;
+    const float up0 = pow2(E / 2), up1 = pow2(E - E / 2);
+    uint32_t qq[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+        qq[i] = static_cast<uint32_t>(__float2int_rn(finite ? (v[i] * up0) * up1 : 0.0f)) + 0x808080u;
+    // Balanced base-256 digits: the low three bytes of q + 0x808080 are
+    // digit + 128, the top byte is the (signed) top digit.
+    uint8_t *out = prep + static_cast<size_t>(row) * prep_stride(cols);
+#pragma unroll
+    for (int l = 0; l < 4; ++l) {
+        const int p = 3 - l;  // byte position of limb l
+        const uint32_t sel = static_cast<uint32_t>(p | ((p + 4) << 4));
+        const uint32_t flip = l ? 0x80808080u : 0u;
+        const uint32_t w0 = __byte_perm(__byte_perm(qq[0], qq[1], sel), __byte_perm(qq[2], qq[3], sel), 0x5410) ^ flip;
+        const uint32_t w1 = __byte_perm(__byte_perm(qq[4], qq[5], sel), __byte_perm(qq[6], qq[7], sel), 0x5410) ^ flip;
+        *reinterpret_cast<uint2 *>(out + static_cast<size_t>(l) * cols + c0) = make_uint2(w0, w1);
+    }
+    float sum = ((v[0] + v[1]) + (v[2] + v[3])) + ((v[4] + v[5]) + (v[6] + v[7]));
+    sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+    sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+    if ((lane & 3) == 0) reinterpret_cast<float *>(out + prep_sums_offset(cols))[c0 / 32] = sum;
+    if (lane == 0) reinterpret_cast<int *>(out + prep_scale_offset(cols))[chunk] = finite ? E : kPrepNonFinite;
+}
+
+// ------------------------------------------------------------------- host ---
+
+struct MmaPlan {
+    int S = 0, RG = 0, srow = 0, stages = 0, stage_stride = 0, grid = 0;
+    size_t smem = 0;
+};
+
+constexpr size_t kMmaSmemBudget = 220 * 1024;
+
+// Row groups per CTA for S column slices: about twelve consumer warps.
+constexpr int mma_row_groups(int S) { return S >= 12 ? 1 : 12 / S; }
+
+constexpr bool mma_slices_ok(int S) {
+    return S == 1 || S == 2 || S == 3 || S == 4 || S == 6 || S == 8 || S == 12 || S == 16;
+}
+
+template <class F>
+static bool plan_mma(int64_t max_rows, int64_t max_tiles_extra, int cols, int row_bytes, MmaPlan &p) {
+    using MF = MmaFmt<F>;
+    if (cols % 512 || row_bytes % 16) return false;
+    p.S = cols / 512;
+    if (!mma_slices_ok(p.S)) return false;
+    p.RG = mma_row_groups(p.S);
+    const int R = 16 * p.RG;
+    // Padded shared-memory rows: >= 16 spare bytes (the Q8_0 fragment loads
+    // read up to 2 bytes past a block) and an odd number of 16-byte units, so
+    // rows g = 0..7 of a fragment start in 8 different 4-bank groups.
+    p.srow = (row_bytes + 16 + 15) & ~15;
+    if (((p.srow >> 4) & 1) == 0) p.srow += 16;
+    p.stage_stride = (R * p.srow + 127) & ~127;
+    const size_t fixed = MF::kTableBytes + 2ull * R * p.S * 2 * 4 + 16 * 8 + 64;
+    const int fit = static_cast<int>((kMmaSmemBudget - std::min(fixed, kMmaSmemBudget)) / p.stage_stride);
+    if (fit < 1) return false;
+    const int64_t tiles = (max_rows + R - 1) / R + max_tiles_extra;
+    p.stages = static_cast<int>(std::min<int64_t>(std::min(fit, 4), std::max<int64_t>(1, tiles)));
+    p.grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(sm_count(), tiles)));
+    p.smem = static_cast<size_t>(p.stages) * p.stage_stride + fixed;
+    return true;
+}
+
+template <class F, int S>
+static int32_t launch_mma(const MmaPlan &p, const MmaJob &job0, const MmaJob *jobs, const int *njobs_dev,
+                          int max_jobs, int batch, int rows_per_job, int cols, int row_bytes, cudaStream_t stream) {
+    constexpr int RG = mma_row_groups(S);
+    auto kern = mma_rows_kernel<F, S, RG>;
+    static size_t configured = 0;  // per instantiation
+    if (p.smem > configured) {
+        GLMVX_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(p.smem)));
+        configured = p.smem;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(p.grid);
+    cfg.blockDim = dim3((S * RG + 1) * 32);
+    cfg.dynamicSmemBytes = p.smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    GLMVX_CUDA(cudaLaunchKernelEx(&cfg, kern, job0, jobs, njobs_dev, max_jobs, batch, rows_per_job, cols, row_bytes,
+                                  p.srow, p.stages, p.stage_stride, device_error_word()));
+    return kOk;
+}
+
+template <class F>
+static int32_t launch_mma_s(const MmaPlan &p, const MmaJob &job0, const MmaJob *jobs, const int *njobs_dev,
+                            int max_jobs, int batch, int rows_per_job, int cols, int row_bytes, cudaStream_t stream) {
+#define GLMVX_MMA_CASE(s) \
+    case s: return launch_mma<F, s>(p, job0, jobs, njobs_dev, max_jobs, batch, rows_per_job, cols, row_bytes, stream);
+    switch (p.S) {
+        GLMVX_MMA_CASE(1)
+        GLMVX_MMA_CASE(2)
+        GLMVX_MMA_CASE(3)
+        GLMVX_MMA_CASE(4)
+        GLMVX_MMA_CASE(6)
+        GLMVX_MMA_CASE(8)
+        GLMVX_MMA_CASE(12)
+        GLMVX_MMA_CASE(16)
+    default: set_error("mma: unsupported column count"); return kUnsupported;
+    }
+#undef GLMVX_MMA_CASE
+}
+
+// Rows must be whole 16-byte units for the per-row bulk copies: always for
+// Q8_0 (cols % 256) and Q4_K, for IQ1_S when cols % 2048 == 0.
+bool mma_supported(int kind, int cols) {
+    if (cols <= 0 || cols % 512 || !mma_slices_ok(cols / 512)) return false;
+    return kind == 8 || kind == 12 || (kind == 19 && cols % 2048 == 0);
+}
+
+int32_t prep_rows_device(uint8_t *prep, const float *x, const float *x2, int rows, int cols, cudaStream_t stream) {
+    if (rows <= 0) return kOk;
+    if (cols % 256 || (reinterpret_cast<uintptr_t>(prep) & 15) || (reinterpret_cast<uintptr_t>(x) & 15) ||
+        (reinterpret_cast<uintptr_t>(x2) & 15)) {
+        set_error("prep: columns must be a multiple of 256 and buffers 16-byte aligned");
+        return kInvalid;
+    }
+    const int64_t warps = static_cast<int64_t>(rows) * (cols / 256);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>((warps + 7) / 8));
+    cfg.blockDim = dim3(256);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    GLMVX_CUDA(cudaLaunchKernelEx(&cfg, prep_rows_kernel, prep, x, x2, rows, cols));
+    return kOk;
+}
+
+int32_t mma_gemv_device(int32_t kind, const MmaJob &job0, const MmaJob *jobs, const int *njobs_dev, int max_jobs,
+                        int batch, int rows_per_job, int cols, cudaStream_t stream) {
+    if (!mma_supported(kind, cols) || rows_per_job <= 0 || max_jobs <= 0) {
+        set_error("mma: unsupported format or shape");
+        return kUnsupported;
+    }
+    if (!jobs && (reinterpret_cast<uintptr_t>(job0.w) & 15)) {
+        set_error("mma: weights must be 16-byte aligned");
+        return kInvalid;
+    }
+    int blk = 0, bytes = 0;
+    reference_layout(kind, blk, bytes);
+    const int row_bytes = cols / blk * bytes;
+    const int64_t max_rows = static_cast<int64_t>(rows_per_job) * max_jobs;
+    int32_t st = kUnsupported;
+    dispatch_format(kind, [&]<class F>() {
+        if constexpr (std::is_same_v<F, FmtQ8_0> || std::is_same_v<F, FmtQ4_K> || std::is_same_v<F, FmtIQ1_S>) {
+            MmaPlan p;
+            if (!plan_mma<F>(max_rows, max_jobs, cols, row_bytes, p)) {
+                set_error("mma: no launch plan for this shape");
+                st = kUnsupported;
+                return;
+            }
+            st = launch_mma_s<F>(p, job0, jobs, njobs_dev, max_jobs, batch, rows_per_job, cols, row_bytes, stream);
+        }
+    });
+    return st;
+}
+
+}  // namespace glmvx

@@ -134,7 +134,7 @@ int32_t glmvx_packed_gemv(int32_t kind, float *out, const uint8_t *w, const floa
 int32_t glmvx_packed_gemm(int32_t kind, float *out, const uint8_t *w, const float *x, int32_t rows, int32_t cols,
                           int32_t batch, void *stream);
 /* As glmvx_packed_gemm; *path reports the kernel taken
- * (1 stream GEMV, 2 generic, 3 F16 element path). */
+ * (1 stream GEMV, 2 generic, 3 F16 element path, 5 tensor-core int8 path). */
 int32_t glmvx_packed_gemm_path(int32_t kind, float *out, const uint8_t *w, const float *x, int32_t rows,
                                int32_t cols, int32_t batch, void *stream, int32_t *path);
 /* Diagnostic decode of `blocks` reference blocks (F16: elements) to f32.
