@@ -442,7 +442,7 @@ def run_ours(args, ranks):
                    'l2_policy': 'inputs larger than L2: the layer streams 1.9 GB of resident experts',
                    'per_tokens': per_tokens},
         'roofline': {'bound': 'hbm', 'achieved': achieved, 'peak': peak, 'unit': 'GB/s', 'frac': achieved / peak,
-                     'traffic': NCU_TRAFFIC, 'kernel': 'gemv_rows_kernel<IQ1_S> gate+up job list',
+                     'traffic': NCU_TRAFFIC, 'kernel': 'mma_rows_kernel<IQ1_S> gate+up job list (tensor-core int8)',
                      'algorithmic_bytes_per_launch': gu_bytes, 'avg_launch_us': gu_us, 'peak_source': peak_kind},
         'fused_gemv': gemv,
         'e2e': {'value': e2e_value, 'unit': 'tok/s', 'steps': e2e_steps,

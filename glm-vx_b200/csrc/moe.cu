@@ -8,23 +8,30 @@
 //   y       = sum over the token's experts in ascending expert id of
 //             down_e(SwiGLU(gate_e x, up_e x)) * w, then + shared(x)
 //
-// Device pipeline, six launches and no host round trip:
+// Device pipeline, no host round trip:
 //   1. router logits     f32 GEMV/GEMM                     (ops.cu)
 //   2. top-k routing     one CTA per token                 (ops.cu)
 //   3. grouping          one CTA: assignments sorted by (expert, token), the
 //                        gate/up/down job descriptors and each token's
 //                        ascending-id combine order        (this file)
-//   4. gate+up           streaming GEMV over 2P jobs       (packed_gemv.cu)
-//   5. down              streaming GEMV over P jobs, SwiGLU fused into the
-//                        activation load                   (packed_gemv.cu)
+//   4. gate+up           packed GEMV over the gate and up jobs
+//   5. down              packed GEMV over the down jobs, input SwiGLU(g, u)
 //   6. combine           weighted sum in reference order   (this file)
-// P = tokens*top_k (+ tokens for the shared expert).  Jobs are ordered by
-// expert so tokens sharing an expert stream its rows close together in time
-// (L2 reuse).
+// P = tokens*top_k (+ tokens for the shared expert) (token, expert) pairs.
+//
+// Formats and widths the tensor-core path takes (mma_gemv.cuh) use it: the
+// token rows are prepared once (limbs) before step 1, the SwiGLU of each
+// pair's gate/up outputs is prepared after step 4, and each job applies one
+// expert matrix to TWO tokens routed to it, so an expert's weights are
+// decoded once per pair of its tokens.  Other formats run one streaming GEMV
+// job per pair (packed_gemv.cu) with SwiGLU fused into the activation load.
+// Jobs are ordered by expert so tokens sharing an expert stream its rows
+// close together in time (L2 reuse).
 #include <mutex>
 
 #include "codecs.cuh"
 #include "gemv_jobs.cuh"
+#include "mma_gemv.cuh"
 
 namespace glmvx {
 
@@ -36,6 +43,9 @@ struct MoeWorkspace {
     int32_t *comb;
     float *combw;
     float *g_out, *u_out, *pair_out;
+    uint8_t *xprep, *hprep;      // prepared token rows / SwiGLU inputs (tensor-core path)
+    MmaJob *gu_mjobs, *dn_mjobs;
+    int *counts;                 // [gate+up jobs, down jobs], written by the grouping kernel
     size_t bytes;
 };
 
@@ -58,24 +68,61 @@ static MoeWorkspace carve(char *base, int T, int hidden, int inter, int E, int k
     w.g_out = reinterpret_cast<float *>(take(4ull * P * inter));
     w.u_out = reinterpret_cast<float *>(take(4ull * P * inter));
     w.pair_out = reinterpret_cast<float *>(take(4ull * P * hidden));
+    w.xprep = reinterpret_cast<uint8_t *>(take(T * prep_stride(hidden)));
+    w.hprep = reinterpret_cast<uint8_t *>(take(P * prep_stride(inter)));
+    w.gu_mjobs = reinterpret_cast<MmaJob *>(take(sizeof(MmaJob) * 2 * P));
+    w.dn_mjobs = reinterpret_cast<MmaJob *>(take(sizeof(MmaJob) * P));
+    w.counts = reinterpret_cast<int *>(take(2 * sizeof(int)));
     w.bytes = off;
     return w;
 }
 
 constexpr int kGroupThreads = 512, kMaxAssignments = 4096;
 
+// Inclusive prefix sum of v[0..n) in place (n <= kMaxAssignments), whole CTA.
+__device__ void block_inclusive_scan(int16_t *v, int n, int32_t *s_warp) {
+    const int per = (n + kGroupThreads - 1) / kGroupThreads;
+    const int b0 = min(static_cast<int>(threadIdx.x) * per, n), b1 = min(b0 + per, n);
+    int sum = 0;
+    for (int i = b0; i < b1; ++i) sum += v[i];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    int incl = sum;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += y;
+    }
+    if (lane == 31) s_warp[warp] = incl;
+    __syncthreads();
+    int before = 0;
+    for (int w = 0; w < warp; ++w) before += s_warp[w];
+    int run = before + incl - sum;
+    for (int i = b0; i < b1; ++i) {
+        run += v[i];
+        v[i] = static_cast<int16_t>(run);
+    }
+    __syncthreads();
+}
+
 // Rank each (token, slot) assignment by (expert id, token): the rank is its
 // pair index, so pairs of one expert are contiguous and ordered by token.
+// With mjobs set (tensor-core path), consecutive pairs of one expert share a
+// job: the pair whose index within its expert's run is even opens a job,
+// the next one (if any) takes the job's second slot.
 __global__ void __launch_bounds__(kGroupThreads)
     moe_group_kernel(const int32_t *ids, const float *wts, int T, int k, int E, int shared, const uint8_t *gate,
                      const uint8_t *up, const uint8_t *down, size_t gu_stride, size_t dn_stride, const uint8_t *sgate,
                      const uint8_t *sup, const uint8_t *sdown, const float *x, int hidden, int inter, float *g_out,
                      float *u_out, float *pair_out, GemvJob *gu_jobs, GemvJob *dn_jobs, int32_t *comb, float *combw,
-                     int *bad) {
+                     int *bad, MmaJob *gu_m, MmaJob *dn_m, int *counts, const uint8_t *xprep, size_t xstride,
+                     const uint8_t *hprep, size_t hstride) {
     __shared__ int32_t s_ids[kMaxAssignments];
     __shared__ int32_t s_pair[kMaxAssignments];
+    __shared__ int16_t s_job[kMaxAssignments];  // per rank: opens a job (0/1), then the job id
+    __shared__ int32_t s_warp[kGroupThreads / 32];
     const int n = T * k;
     const int P = n + (shared ? T : 0);
+    const bool mma = gu_m != nullptr;
     for (int a = threadIdx.x; a < n; a += blockDim.x) {
         const int e = ids[a];
         s_ids[a] = e;
@@ -84,12 +131,18 @@ __global__ void __launch_bounds__(kGroupThreads)
     __syncthreads();
     for (int a = threadIdx.x; a < n; a += blockDim.x) {
         const int e = s_ids[a];
-        int rank = 0;
+        int lt = 0, eq = 0;
         for (int b = 0; b < n; ++b) {
             const int eb = s_ids[b];
-            rank += (eb < e) | ((eb == e) & (b < a));
+            lt += eb < e;
+            eq += (eb == e) & (b < a);
         }
+        const int rank = lt + eq;
         s_pair[a] = rank;
+        if (mma) {
+            s_job[rank] = static_cast<int16_t>((eq & 1) == 0);
+            continue;
+        }
         const int t = a / k;
         const int ec = min(max(e, 0), E - 1);  // never form an out-of-range pointer
         gu_jobs[rank] = GemvJob{gate + ec * gu_stride, x + static_cast<size_t>(t) * hidden, nullptr,
@@ -99,7 +152,7 @@ __global__ void __launch_bounds__(kGroupThreads)
         dn_jobs[rank] = GemvJob{down + ec * dn_stride, g_out + static_cast<size_t>(rank) * inter,
                                 u_out + static_cast<size_t>(rank) * inter, pair_out + static_cast<size_t>(rank) * hidden};
     }
-    if (shared) {
+    if (shared && !mma) {
         for (int t = threadIdx.x; t < T; t += blockDim.x) {
             const int p = n + t;
             gu_jobs[p] = GemvJob{sgate, x + static_cast<size_t>(t) * hidden, nullptr, g_out + static_cast<size_t>(p) * inter};
@@ -109,6 +162,59 @@ __global__ void __launch_bounds__(kGroupThreads)
         }
     }
     __syncthreads();
+    if (mma) {
+        block_inclusive_scan(s_job, n, s_warp);  // s_job[r] = 1 + id of the job holding rank r
+        const int routed = n ? s_job[n - 1] : 0;
+        const int J = routed + (shared ? (T + 1) / 2 : 0);
+        // Pass 0 writes whole jobs from the pair in slot 0 (slot 1 empty),
+        // pass 1 fills slot 1.
+        for (int pass = 0; pass < 2; ++pass) {
+            for (int a = threadIdx.x; a < n + (shared ? T : 0); a += blockDim.x) {
+                int e, t, r, j, slot;
+                const uint8_t *wg, *wu, *wd;
+                if (a < n) {
+                    e = min(max(s_ids[a], 0), E - 1);
+                    t = a / k;
+                    r = s_pair[a];
+                    j = s_job[r] - 1;
+                    slot = (r > 0 && s_job[r - 1] == s_job[r]) ? 1 : 0;
+                    wg = gate + e * gu_stride;
+                    wu = up + e * gu_stride;
+                    wd = down + e * dn_stride;
+                } else {
+                    t = a - n;
+                    r = n + t;
+                    j = routed + t / 2;
+                    slot = t & 1;
+                    wg = sgate;
+                    wu = sup;
+                    wd = sdown;
+                }
+                if (slot != pass) continue;
+                const uint8_t *xp = xprep + static_cast<size_t>(t) * xstride;
+                const uint8_t *hp = hprep + static_cast<size_t>(r) * hstride;
+                float *go = g_out + static_cast<size_t>(r) * inter, *uo = u_out + static_cast<size_t>(r) * inter;
+                float *po = pair_out + static_cast<size_t>(r) * hidden;
+                if (slot == 0) {
+                    gu_m[j] = MmaJob{wg, {xp, nullptr}, {go, nullptr}};
+                    gu_m[J + j] = MmaJob{wu, {xp, nullptr}, {uo, nullptr}};
+                    dn_m[j] = MmaJob{wd, {hp, nullptr}, {po, nullptr}};
+                } else {
+                    gu_m[j].xp[1] = xp;
+                    gu_m[j].out[1] = go;
+                    gu_m[J + j].xp[1] = xp;
+                    gu_m[J + j].out[1] = uo;
+                    dn_m[j].xp[1] = hp;
+                    dn_m[j].out[1] = po;
+                }
+            }
+            __syncthreads();
+        }
+        if (threadIdx.x == 0) {
+            counts[0] = 2 * J;
+            counts[1] = J;
+        }
+    }
     // Each token's slots in ascending expert id (glm_vx/model.py:305-316).
     for (int t = threadIdx.x; t < T; t += blockDim.x) {
         for (int i = 0; i < k; ++i) {
@@ -187,19 +293,36 @@ static int32_t moe_ffn(float *y, const float *x, int32_t tokens, int32_t hidden,
         if (events) GLMVX_CUDA(cudaEventRecord(static_cast<cudaEvent_t>(events[i]), st));
         return kOk;
     };
+    auto a16 = [](const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+    const bool mma = mma_supported(kind, hidden) && mma_supported(kind, inter) && a16(x) && a16(gate) && a16(up) &&
+                     a16(down) && (!shared || (a16(shared_gate) && a16(shared_up) && a16(shared_down)));
     int32_t st_ = mark(0);
     if (st_) return st_;
+    if (mma && (st_ = prep_rows_device(w.xprep, x, nullptr, tokens, hidden, st))) return st_;
     st_ = glmvx_matmul_nt(w.logits, x, router_w, tokens, experts, hidden, st);
     if (st_ || (st_ = mark(1))) return st_;
     st_ = glmvx_router(w.ids, w.wts, w.logits, router_bias, tokens, experts, top_k, scale, st);
     if (st_ || (st_ = mark(2))) return st_;
-    moe_group_kernel<<<1, kGroupThreads, 0, st>>>(w.ids, w.wts, tokens, top_k, experts, shared, gate, up, down,
-                                                  gu_stride, dn_stride, shared_gate, shared_up, shared_down, x,
-                                                  hidden, inter, w.g_out, w.u_out, w.pair_out, w.gu_jobs, w.dn_jobs,
-                                                  w.comb, w.combw, device_error_word());
+    moe_group_kernel<<<1, kGroupThreads, 0, st>>>(
+        w.ids, w.wts, tokens, top_k, experts, shared, gate, up, down, gu_stride, dn_stride, shared_gate, shared_up,
+        shared_down, x, hidden, inter, w.g_out, w.u_out, w.pair_out, w.gu_jobs, w.dn_jobs, w.comb, w.combw,
+        device_error_word(), mma ? w.gu_mjobs : nullptr, w.dn_mjobs, w.counts, w.xprep, prep_stride(hidden), w.hprep,
+        prep_stride(inter));
     if ((st_ = launch_status("moe_group_kernel")) || (st_ = mark(3))) return st_;
-    if ((st_ = gemv_jobs_device(kind, w.gu_jobs, 2 * P, inter, hidden, gate, x, st)) || (st_ = mark(4))) return st_;
-    if ((st_ = gemv_jobs_device(kind, w.dn_jobs, P, hidden, inter, down, w.g_out, st)) || (st_ = mark(5))) return st_;
+    if (mma) {
+        const MmaJob none{};
+        if ((st_ = mma_gemv_device(kind, none, w.gu_mjobs, w.counts, 2 * P, 0, inter, hidden, st)) ||
+            (st_ = mark(4)))
+            return st_;
+        if ((st_ = prep_rows_device(w.hprep, w.g_out, w.u_out, P, inter, st)) ||
+            (st_ = mma_gemv_device(kind, none, w.dn_mjobs, w.counts + 1, P, 0, hidden, inter, st)) || (st_ = mark(5)))
+            return st_;
+    } else {
+        if ((st_ = gemv_jobs_device(kind, w.gu_jobs, 2 * P, inter, hidden, gate, x, st)) || (st_ = mark(4)))
+            return st_;
+        if ((st_ = gemv_jobs_device(kind, w.dn_jobs, P, hidden, inter, down, w.g_out, st)) || (st_ = mark(5)))
+            return st_;
+    }
     moe_combine_kernel<<<dim3((hidden + 255) / 256, tokens), 256, 0, st>>>(y, w.pair_out, w.comb, w.combw, tokens,
                                                                            top_k, hidden, shared);
     if ((st_ = launch_status("moe_combine_kernel")) || (st_ = mark(6))) return st_;
@@ -247,7 +370,7 @@ GLMVX_EXPORT int32_t glmvx_moe_ffn_profiled(float *y, const float *x, int32_t to
 //  * The array holds kStaticMoeScratchBytes (16 MiB) per device; a layer whose
 //    workspace (glmvx_moe_workspace_bytes) is larger is rejected with
 //    kInvalid before anything is launched.  BASELINE-sized layers (hidden
-//    6144, intermediate 2048, top-8 plus a shared expert) fit up to 45 tokens.
+//    6144, intermediate 2048, top-8 plus a shared expert) fit up to 35 tokens.
 //  * Every scratch byte is written by an earlier stage of the same call
 //    before any stage reads it, so nothing has to start at zero and no
 //    clearing is done.

@@ -20,6 +20,8 @@ def synthetic_layer(experts, hidden, inter, kind=19, seed=0):
         blocks = count * n_rows * cols // block
         raw = rng.integers(0, 256, size=(blocks, size), dtype=np.uint8)
         raw[:, :2] = (np.abs(rng.normal(size=(blocks, 1))) * 0.02).astype(np.float16).view(np.uint8)
+        if kind == 12:  # Q4_K dmin
+            raw[:, 2:4] = (np.abs(rng.normal(size=(blocks, 1))) * 0.02).astype(np.float16).view(np.uint8)
         return raw.reshape(-1)
 
     layer = dict(router=(rng.normal(size=(experts, hidden)) * 0.02).astype(np.float32),
@@ -97,3 +99,32 @@ def test_moe_config2_full_width(gpu_backend):
         assert y2.tobytes() == y.tobytes()
     finally:
         moe.close()
+
+
+def _check_layer(gpu_backend, oracle, E, H, I, K, T, kind, seed):
+    from gpu.moe import MoELayer
+    layer = synthetic_layer(E, H, I, kind=kind, seed=seed)
+    moe = MoELayer(gpu_backend, layer['router'], layer['bias'], kind, layer['gate'], layer['up'], layer['down'],
+                   H, I, K, 2.5, shared=layer['shared'])
+    try:
+        x = np.random.default_rng(seed).normal(size=(T, H)).astype(np.float32)
+        y, ids, _ = moe.forward(x)
+        want, want_ids = reference_ffn(oracle, layer, x, E, H, I, K, 2.5, kind=kind)
+        assert ids.tolist() == want_ids.tolist()
+        err = np.linalg.norm(y - want) / np.linalg.norm(want)
+        assert err <= RTOL, err
+    finally:
+        moe.close()
+
+
+@pytest.mark.parametrize('T', [1, 2, 5, 9])
+def test_moe_tokens_share_experts(gpu_backend, oracle, T):
+    """4 experts, top-2: most experts serve several tokens, with odd and even
+    counts, so expert jobs take two tokens and some a single one."""
+    _check_layer(gpu_backend, oracle, 4, 2048, 2048, 2, T, 19, seed=30 + T)
+
+
+@pytest.mark.parametrize('kind', [8, 12])
+def test_moe_other_formats(gpu_backend, oracle, kind):
+    """Q8_0 and Q4_K expert stacks through the same layer (tensor-core path)."""
+    _check_layer(gpu_backend, oracle, 8, 2048, 2048, 3, 4, kind, seed=kind)
