@@ -90,9 +90,80 @@ __global__ void __launch_bounds__(256)
     }
 }
 
+// ---- f32 matvec / matmul_nt, aligned rows: a CTA owns EB weight rows x TB
+// tokens; its 8 warps split the columns (float4 per lane, coalesced), every
+// loaded weight quad serves TB tokens and every activation quad EB rows.  The
+// 8 warp partials of an output are summed in fixed order (deterministic).
+template <int EB, int TB>
+__global__ void __launch_bounds__(256)
+    f32_tile_kernel(float *__restrict__ out, const float *__restrict__ wt, const float *__restrict__ x, int rows,
+                    int cols, int batch, int out_row_major_tokens) {
+    __shared__ float red[8][EB][TB];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int r0 = blockIdx.x * EB, t0 = blockIdx.y * TB;
+    const int nr = min(EB, rows - r0), nt = min(TB, batch - t0);
+    float acc[EB][TB];
+#pragma unroll
+    for (int e = 0; e < EB; ++e)
+#pragma unroll
+        for (int t = 0; t < TB; ++t) acc[e][t] = 0.0f;
+    const int quads = cols >> 2;
+    for (int f = lane + 32 * warp; f < quads; f += 256) {
+        float4 wv[EB], xv[TB];
+#pragma unroll
+        for (int e = 0; e < EB; ++e)
+            wv[e] = e < nr ? __ldg(reinterpret_cast<const float4 *>(wt + static_cast<size_t>(r0 + e) * cols) + f)
+                           : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int t = 0; t < TB; ++t)
+            xv[t] = t < nt ? __ldg(reinterpret_cast<const float4 *>(x + static_cast<size_t>(t0 + t) * cols) + f)
+                           : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int e = 0; e < EB; ++e)
+#pragma unroll
+            for (int t = 0; t < TB; ++t) {
+                acc[e][t] = fmaf(wv[e].x, xv[t].x, acc[e][t]);
+                acc[e][t] = fmaf(wv[e].y, xv[t].y, acc[e][t]);
+                acc[e][t] = fmaf(wv[e].z, xv[t].z, acc[e][t]);
+                acc[e][t] = fmaf(wv[e].w, xv[t].w, acc[e][t]);
+            }
+    }
+#pragma unroll
+    for (int e = 0; e < EB; ++e)
+#pragma unroll
+        for (int t = 0; t < TB; ++t) {
+            const float v = warp_sum(acc[e][t]);
+            if (lane == 0) red[warp][e][t] = v;
+        }
+    __syncthreads();
+    for (int i = threadIdx.x; i < EB * TB; i += 256) {
+        const int e = i / TB, t = i % TB;
+        if (e >= nr || t >= nt) continue;
+        float v = 0.0f;
+#pragma unroll
+        for (int w = 0; w < 8; ++w) v += red[w][e][t];
+        if (out_row_major_tokens) out[static_cast<size_t>(t0 + t) * rows + r0 + e] = v;
+        else out[static_cast<size_t>(r0 + e) * batch + t0 + t] = v;
+    }
+}
+
 int32_t f32_rows(float *out, const float *w, const float *x, int rows, int cols, int batch, bool token_major,
                  cudaStream_t s) {
     if (rows == 0 || batch == 0) return kOk;
+    const bool vec = ((reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(x)) & 15) == 0 && (cols & 3) == 0;
+    if (vec && batch <= 1) {
+        f32_tile_kernel<2, 1><<<dim3((rows + 1) / 2, 1), 256, 0, s>>>(out, w, x, rows, cols, batch, token_major);
+        return launch_status("f32_tile_kernel");
+    }
+    if (vec && batch <= 8) {
+        f32_tile_kernel<4, 8><<<dim3((rows + 3) / 4, 1), 256, 0, s>>>(out, w, x, rows, cols, batch, token_major);
+        return launch_status("f32_tile_kernel");
+    }
+    if (vec) {
+        f32_tile_kernel<8, 8><<<dim3((rows + 7) / 8, (batch + 7) / 8), 256, 0, s>>>(out, w, x, rows, cols, batch,
+                                                                                  token_major);
+        return launch_status("f32_tile_kernel");
+    }
     if (batch <= 1) {
         f32_rows_kernel<1><<<dim3((rows + 7) / 8, 1), 256, 0, s>>>(out, w, x, rows, cols, batch, token_major);
     } else {

@@ -10,11 +10,12 @@
 //   Q4_K   w = d*sc * q - dmin*m          A = q (u8, 0..15); the min term
 //                                         dmin*m*sum(x) uses the prepared
 //                                         sub-block sums of x
-//   IQ1_S  w = d*(2s+1) * (grid + delta)  A = 8*grid +/- 1 (s8) from a shared
-//                                         table of 4096 entries (sign of delta
-//                                         selects the half); the odd
-//                                         multiplier 2s+1 is applied to the
-//                                         int32 result, d/8 in f32
+//   IQ1_S  w = d*(2s+1) * (grid + delta)  A = 8*grid +/- 1 (s8): a nibble
+//                                         codebook in shared memory, expanded
+//                                         with one byte permute (the sign of
+//                                         delta picks the byte table); the
+//                                         odd multiplier 2s+1 is applied to
+//                                         the int32 result, d/8 in f32
 //
 // The activations come as prepared rows (mma_gemv.cuh): four int8 limbs of
 // x*2^E.  One m16n8k32 instruction takes 16 weight rows x 32 columns against
@@ -82,22 +83,25 @@ struct MmaFmt;
 
 template <>
 struct MmaFmt<FmtIQ1_S> {
-    static constexpr int kTableBytes = 4096 * 8, kSubPerBlock = 8, kBlockBytes = 50;
+    // Codebook as 8 nibbles g+1 (0..2) per entry, four interleaved copies:
+    // copy c of entry i at byte 16*i + 4*c.  Lane t of a quad reads copy t,
+    // so the 32 lanes of a lookup fall in four disjoint groups of 8 banks.
+    static constexpr int kTableBytes = 2048 * 16, kSubPerBlock = 8, kBlockBytes = 50;
     static constexpr bool kMins = false;
-    // Entry e: the 8 grid values g of index e & 2047 as int8 8*g+1 (e < 2048,
-    // delta = +1/8) or 8*g-1 (delta = -1/8).
+    // Byte lookup words for PRMT: nibble n = g+1 selects 8*g+1 (delta = +1/8)
+    // or 8*g-1 (delta = -1/8) as int8.
+    static constexpr uint32_t kLutPlus = 0x000901F9u, kLutMinus = 0x0007FFF7u;
     __device__ static void init_table(uint8_t *table, int tid, int nthreads) {
         const uint2 *grid = reinterpret_cast<const uint2 *>(g_codebooks + kTabIq1sGrid);
-        for (int e = tid; e < 4096; e += nthreads) {
-            const uint2 src = grid[e & 2047];
-            const int delta = (e & 2048) ? -1 : 1;
-            uint32_t lo = 0, hi = 0;
+        for (int i = tid; i < 2048; i += nthreads) {
+            const uint2 src = grid[i];
+            uint32_t v = 0;
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
-                lo |= (static_cast<uint32_t>(8 * s8(src.x >> (8 * k)) + delta) & 0xffu) << (8 * k);
-                hi |= (static_cast<uint32_t>(8 * s8(src.y >> (8 * k)) + delta) & 0xffu) << (8 * k);
+                v |= (static_cast<uint32_t>(s8(src.x >> (8 * k)) + 1) & 0xfu) << (4 * k);
+                v |= (static_cast<uint32_t>(s8(src.y >> (8 * k)) + 1) & 0xfu) << (4 * k + 16);
             }
-            reinterpret_cast<uint2 *>(table)[e] = make_uint2(lo, hi);
+            *reinterpret_cast<uint4 *>(table + 16 * i) = make_uint4(v, v, v, v);
         }
     }
     template <int C>
@@ -105,15 +109,18 @@ struct MmaFmt<FmtIQ1_S> {
                                                  float xs, const float *, const uint8_t *table, float (&af)[4],
                                                  float (&)[2]) {
         const uint8_t *q0 = p0 + C * kBlockBytes, *q1 = p1 + C * kBlockBytes;
+        const uint8_t *tab = table + 4 * t;
         int ai[4] = {0, 0, 0, 0};
 #pragma unroll
         for (int s = 0; s < 8; ++s) {
             const uint32_t h0 = u16(q0 + 34 + 2 * s), h1 = u16(q1 + 34 + 2 * s);
-            const uint32_t i0 = q0[2 + 4 * s + t] | (((h0 >> (3 * t)) & 7u) << 8) | ((h0 >> 4) & 0x800u);
-            const uint32_t i1 = q1[2 + 4 * s + t] | (((h1 >> (3 * t)) & 7u) << 8) | ((h1 >> 4) & 0x800u);
-            const uint2 a0 = lds64(table + 8 * i0), a1 = lds64(table + 8 * i1);
+            const uint32_t i0 = q0[2 + 4 * s + t] | (((h0 >> (3 * t)) & 7u) << 8);
+            const uint32_t i1 = q1[2 + 4 * s + t] | (((h1 >> (3 * t)) & 7u) << 8);
+            const uint32_t e0 = lds32(tab + 16 * i0), e1 = lds32(tab + 16 * i1);
+            const uint32_t l0 = (h0 & 0x8000u) ? kLutMinus : kLutPlus, l1 = (h1 & 0x8000u) ? kLutMinus : kLutPlus;
             int c[4];
-            mma_s8s8(c, a0.x, a1.x, a0.y, a1.y, b[8 * C + s][0], b[8 * C + s][1]);
+            mma_s8s8(c, __byte_perm(l0, 0, e0), __byte_perm(l1, 0, e1), __byte_perm(l0, 0, e0 >> 16),
+                     __byte_perm(l1, 0, e1 >> 16), b[8 * C + s][0], b[8 * C + s][1]);
             const int dl0 = 2 * static_cast<int>((h0 >> 12) & 7u) + 1, dl1 = 2 * static_cast<int>((h1 >> 12) & 7u) + 1;
             ai[0] += dl0 * c[0];
             ai[1] += dl0 * c[1];
