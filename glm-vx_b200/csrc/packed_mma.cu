@@ -32,9 +32,10 @@
 //
 // Kernel structure (mma_rows_kernel): a persistent grid, one CTA per SM, each
 // CTA owning a balanced range of the job list's rows.  A producer warp
-// streams tiles of 16*RG rows into a ring of shared-memory stages with one
-// 1-D bulk copy (TMA) per row (rows are padded in shared memory so the 8 row
-// groups of a fragment fall in distinct banks); S*RG consumer warps each take
+// streams tiles of 16*RG rows into a ring of shared-memory stages with 1-D
+// bulk copies (TMA): one per tile when the row length already spreads the 8
+// row groups of a fragment over distinct banks, else one per row into padded
+// rows; S*RG consumer warps each take
 // 16 rows x 512 columns of a tile (S = cols/512 column slices, RG row
 // groups), keep the B fragments of their slice in registers, and reduce the S
 // slice partials of a row in fixed order through shared memory after every
@@ -312,12 +313,20 @@ __global__ void __launch_bounds__((S * RG + 1) * 32, 1)
             }
             const int nr = tile_end(r0, r_end) - r0;
             const MmaJob j = job_at(job0, jobs, r0 / rows_per_job, batch, rows_per_job, pstride);
-            if (lane == 0) mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(nr) * row_bytes);
-            __syncwarp();
             uint8_t *stage = smem + static_cast<size_t>(s) * stage_stride;
-            for (int i = lane; i < nr; i += 32)
-                bulk_g2s(stage + static_cast<size_t>(i) * srow,
-                         j.w + static_cast<size_t>((r0 + i) % rows_per_job) * row_bytes, row_bytes, &full[s]);
+            const uint8_t *src = j.w + static_cast<size_t>(r0 % rows_per_job) * row_bytes;
+            if (srow == row_bytes) {  // rows already bank-spread: the tile is one contiguous copy
+                if (lane == 0) {
+                    mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(nr) * row_bytes);
+                    bulk_g2s(stage, src, static_cast<uint32_t>(nr) * row_bytes, &full[s]);
+                }
+            } else {
+                if (lane == 0) mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(nr) * row_bytes);
+                __syncwarp();
+                for (int i = lane; i < nr; i += 32)
+                    bulk_g2s(stage + static_cast<size_t>(i) * srow, src + static_cast<size_t>(i) * row_bytes, row_bytes,
+                             &full[s]);
+            }
         }
         return;
     }
@@ -503,17 +512,19 @@ static bool plan_mma(int64_t max_rows, int64_t max_tiles_extra, int cols, int ro
     if (!mma_slices_ok(p.S)) return false;
     p.RG = mma_row_groups(p.S);
     const int R = 16 * p.RG;
-    // Padded shared-memory rows: >= 16 spare bytes (the Q8_0 fragment loads
-    // read up to 2 bytes past a block) and an odd number of 16-byte units, so
-    // rows g = 0..7 of a fragment start in 8 different 4-bank groups.
-    p.srow = (row_bytes + 16 + 15) & ~15;
-    if (((p.srow >> 4) & 1) == 0) p.srow += 16;
+    // Shared-memory rows span an odd number of 16-byte units, so rows g = 0..7
+    // of a fragment start in 8 different 4-bank groups.  Rows that already do
+    // (IQ1_S: 400 or 1200 bytes) keep the global stride and arrive with one
+    // bulk copy per tile; others are padded by 16 bytes, one copy per row.
+    // (The Q8_0 fragment loads read at most 2 bytes past a block, never past
+    // a row: the last block of a row has an odd index.)
+    p.srow = ((row_bytes >> 4) & 1) ? row_bytes : row_bytes + 16;
     p.stage_stride = (R * p.srow + 127) & ~127;
     const size_t fixed = MF::kTableBytes + 2ull * R * p.S * 2 * 4 + 16 * 8 + 64;
     const int fit = static_cast<int>((kMmaSmemBudget - std::min(fixed, kMmaSmemBudget)) / p.stage_stride);
     if (fit < 1) return false;
     const int64_t tiles = (max_rows + R - 1) / R + max_tiles_extra;
-    p.stages = static_cast<int>(std::min<int64_t>(std::min(fit, 4), std::max<int64_t>(1, tiles)));
+    p.stages = static_cast<int>(std::min<int64_t>(std::min(fit, 8), std::max<int64_t>(1, tiles)));
     p.grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(sm_count(), tiles)));
     p.smem = static_cast<size_t>(p.stages) * p.stage_stride + fixed;
     return true;
