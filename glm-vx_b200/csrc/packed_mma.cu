@@ -37,7 +37,8 @@
 // row groups of a fragment over distinct banks, else one per row into padded
 // rows; S*RG consumer warps each take
 // 16 rows x 512 columns of a tile (S = cols/512 column slices, RG row
-// groups), keep the B fragments of their slice in registers, and reduce the S
+// groups; IQ1_S warps take two 16-row fragments for more independent work),
+// keep the B fragments of their slice in registers, and reduce the S
 // slice partials of a row in fixed order through shared memory after every
 // tile.  Waits on mbarriers are bounded (2 s) and report through the device
 // error word.
@@ -89,6 +90,7 @@ struct MmaFmt<FmtIQ1_S> {
     // so the 32 lanes of a lookup fall in four disjoint groups of 8 banks.
     static constexpr int kTableBytes = 2048 * 16, kSubPerBlock = 8, kBlockBytes = 50;
     static constexpr bool kMins = false;
+    static constexpr int kFR = 2;  // 16-row fragments per warp (independent work to hide latency)
     // Byte lookup words for PRMT: nibble n = g+1 selects 8*g+1 (delta = +1/8)
     // or 8*g-1 (delta = -1/8) as int8.
     static constexpr uint32_t kLutPlus = 0x000901F9u, kLutMinus = 0x0007FFF7u;
@@ -106,33 +108,45 @@ struct MmaFmt<FmtIQ1_S> {
         }
     }
     template <int C>
-    __device__ __forceinline__ static void chunk(const uint8_t *p0, const uint8_t *p1, int t, const uint32_t (&b)[16][2],
-                                                 float xs, const float *, const uint8_t *table, float (&af)[4],
-                                                 float (&)[2]) {
-        const uint8_t *q0 = p0 + C * kBlockBytes, *q1 = p1 + C * kBlockBytes;
+    __device__ __forceinline__ static void chunk(const uint8_t *const (&p)[kFR][2], int t, const uint32_t (&b)[16][2],
+                                                 float xs, const float *, const uint8_t *table, float (&af)[kFR][4],
+                                                 float (&)[kFR][2]) {
         const uint8_t *tab = table + 4 * t;
-        int ai[4] = {0, 0, 0, 0};
+        const int sh = 3 * t;
+        int ai[kFR][4] = {};
 #pragma unroll
-        for (int s = 0; s < 8; ++s) {
+        for (int s = 0; s < 8; ++s)
+#pragma unroll
+        for (int f = 0; f < kFR; ++f) {
+            const uint8_t *q0 = p[f][0] + C * kBlockBytes, *q1 = p[f][1] + C * kBlockBytes;
             const uint32_t h0 = u16(q0 + 34 + 2 * s), h1 = u16(q1 + 34 + 2 * s);
-            const uint32_t i0 = q0[2 + 4 * s + t] | (((h0 >> (3 * t)) & 7u) << 8);
-            const uint32_t i1 = q1[2 + 4 * s + t] | (((h1 >> (3 * t)) & 7u) << 8);
+            // index = qs | grid bits 3t..3t+2 of h at bits 8..10; h*256 moves
+            // the field next to the byte (a multiply, off the logic pipe).
+            const uint32_t i0 = (((h0 * 256u) >> sh) & 0x700u) | q0[2 + 4 * s + t];
+            const uint32_t i1 = (((h1 * 256u) >> sh) & 0x700u) | q1[2 + 4 * s + t];
             const uint32_t e0 = lds32(tab + 16 * i0), e1 = lds32(tab + 16 * i1);
-            const uint32_t l0 = (h0 & 0x8000u) ? kLutMinus : kLutPlus, l1 = (h1 & 0x8000u) ? kLutMinus : kLutPlus;
+            // delta sign (bit 15) picks the byte table: P + sign * (M - P).
+            const uint32_t l0 = kLutPlus + (h0 >> 15) * (kLutMinus - kLutPlus);
+            const uint32_t l1 = kLutPlus + (h1 >> 15) * (kLutMinus - kLutPlus);
             int c[4];
-            mma_s8s8(c, __byte_perm(l0, 0, e0), __byte_perm(l1, 0, e1), __byte_perm(l0, 0, e0 >> 16),
-                     __byte_perm(l1, 0, e1 >> 16), b[8 * C + s][0], b[8 * C + s][1]);
-            const int dl0 = 2 * static_cast<int>((h0 >> 12) & 7u) + 1, dl1 = 2 * static_cast<int>((h1 >> 12) & 7u) + 1;
-            ai[0] += dl0 * c[0];
-            ai[1] += dl0 * c[1];
-            ai[2] += dl1 * c[2];
-            ai[3] += dl1 * c[3];
+            mma_s8s8(c, __byte_perm(l0, 0, e0), __byte_perm(l1, 0, e1), __byte_perm(l0, 0, __umulhi(e0, 65536u)),
+                     __byte_perm(l1, 0, __umulhi(e1, 65536u)), b[8 * C + s][0], b[8 * C + s][1]);
+            // 2s+1 from bits 12..14: ((h >> 11) & 14) | 1.
+            const int dl0 = static_cast<int>(((h0 >> 11) & 14u) | 1u), dl1 = static_cast<int>(((h1 >> 11) & 14u) | 1u);
+            ai[f][0] += dl0 * c[0];
+            ai[f][1] += dl0 * c[1];
+            ai[f][2] += dl1 * c[2];
+            ai[f][3] += dl1 * c[3];
         }
-        const float s0 = h2f(u16(q0)) * (0.125f * xs), s1 = h2f(u16(q1)) * (0.125f * xs);
-        af[0] = fmaf(s0, static_cast<float>(ai[0]), af[0]);
-        af[1] = fmaf(s0, static_cast<float>(ai[1]), af[1]);
-        af[2] = fmaf(s1, static_cast<float>(ai[2]), af[2]);
-        af[3] = fmaf(s1, static_cast<float>(ai[3]), af[3]);
+#pragma unroll
+        for (int f = 0; f < kFR; ++f) {
+            const float s0 = h2f(u16(p[f][0] + C * kBlockBytes)) * (0.125f * xs);
+            const float s1 = h2f(u16(p[f][1] + C * kBlockBytes)) * (0.125f * xs);
+            af[f][0] = fmaf(s0, static_cast<float>(ai[f][0]), af[f][0]);
+            af[f][1] = fmaf(s0, static_cast<float>(ai[f][1]), af[f][1]);
+            af[f][2] = fmaf(s1, static_cast<float>(ai[f][2]), af[f][2]);
+            af[f][3] = fmaf(s1, static_cast<float>(ai[f][3]), af[f][3]);
+        }
     }
 };
 
@@ -140,14 +154,17 @@ template <>
 struct MmaFmt<FmtQ8_0> {
     static constexpr int kTableBytes = 0, kSubPerBlock = 1, kBlockBytes = 34;
     static constexpr bool kMins = false;
+    static constexpr int kFR = 1;
     __device__ static void init_table(uint8_t *, int, int) {}
     // Eight 34-byte blocks.  A block at an even index within the slice starts
     // 4-byte aligned (its bytes follow a 2-byte scale), one at an odd index
     // 2 bytes past alignment, so its bytes are.
     template <int C>
-    __device__ __forceinline__ static void chunk(const uint8_t *p0, const uint8_t *p1, int t, const uint32_t (&b)[16][2],
-                                                 float xs, const float *, const uint8_t *, float (&af)[4],
-                                                 float (&)[2]) {
+    __device__ __forceinline__ static void chunk(const uint8_t *const (&p)[kFR][2], int t, const uint32_t (&b)[16][2],
+                                                 float xs, const float *, const uint8_t *, float (&afr)[kFR][4],
+                                                 float (&)[kFR][2]) {
+        const uint8_t *p0 = p[0][0], *p1 = p[0][1];
+        float(&af)[4] = afr[0];
 #pragma unroll
         for (int s = 0; s < 8; ++s) {
             const int i = 8 * C + s;
@@ -181,6 +198,7 @@ template <>
 struct MmaFmt<FmtQ4_K> {
     static constexpr int kTableBytes = 0, kSubPerBlock = 8, kBlockBytes = 144;
     static constexpr bool kMins = true;
+    static constexpr int kFR = 1;
     __device__ static void init_table(uint8_t *, int, int) {}
     // Byte j of the 6-bit scale (or min) words of a K-quant head, sub-blocks
     // 0..3 in `lo`, 4..7 in `hi` (kernels/packed.vx:107-120 on packed words).
@@ -188,10 +206,12 @@ struct MmaFmt<FmtQ4_K> {
         return static_cast<int>(((j < 4 ? lo : hi) >> (8 * (j & 3))) & 0xffu);
     }
     template <int C>
-    __device__ __forceinline__ static void chunk(const uint8_t *p0, const uint8_t *p1, int t, const uint32_t (&b)[16][2],
-                                                 float xs, const float *sums, const uint8_t *, float (&af)[4],
-                                                 float (&am)[2]) {
-        const uint8_t *q0 = p0 + C * kBlockBytes, *q1 = p1 + C * kBlockBytes;
+    __device__ __forceinline__ static void chunk(const uint8_t *const (&p)[kFR][2], int t, const uint32_t (&b)[16][2],
+                                                 float xs, const float *sums, const uint8_t *, float (&afr)[kFR][4],
+                                                 float (&amr)[kFR][2]) {
+        float(&af)[4] = afr[0];
+        float(&am)[2] = amr[0];
+        const uint8_t *q0 = p[0][0] + C * kBlockBytes, *q1 = p[0][1] + C * kBlockBytes;
         const uint4 h0 = *reinterpret_cast<const uint4 *>(q0), h1 = *reinterpret_cast<const uint4 *>(q1);
         const uint32_t sl0 = h0.y & 0x3F3F3F3Fu, sh0 = (h0.w & 0x0F0F0F0Fu) | ((h0.y >> 2) & 0x30303030u);
         const uint32_t sl1 = h1.y & 0x3F3F3F3Fu, sh1 = (h1.w & 0x0F0F0F0Fu) | ((h1.y >> 2) & 0x30303030u);
@@ -263,7 +283,8 @@ __global__ void __launch_bounds__((S * RG + 1) * 32, 1)
     mma_rows_kernel(MmaJob job0, const MmaJob *__restrict__ jobs, const int *njobs_dev, int max_jobs, int batch,
                     int rows_per_job, int cols, int row_bytes, int srow, int stages, int stage_stride, int *err) {
     using MF = MmaFmt<F>;
-    constexpr int NW = S * RG, R = 16 * RG;
+    constexpr int FR = MF::kFR;
+    constexpr int NW = S * RG, R = 16 * FR * RG;  // a warp owns FR 16-row fragments of the tile
     extern __shared__ __align__(128) uint8_t smem[];
     uint8_t *table = smem + static_cast<size_t>(stages) * stage_stride;
     float *red = reinterpret_cast<float *>(table + MF::kTableBytes);  // [2][R][S][2]
@@ -388,41 +409,52 @@ __global__ void __launch_bounds__((S * RG + 1) * 32, 1)
             abort_flag[rg] = 1;
         }
         const int nr = tile_end(r0, r_end) - r0;
-        float af[4] = {0.0f, 0.0f, 0.0f, 0.0f}, am[2] = {0.0f, 0.0f};
+        float af[FR][4] = {}, am[FR][2] = {};
+        const int rbase = 16 * FR * rg;  // first tile row of this warp's fragments
         if (ok) {
-            const uint8_t *p0 =
-                smem + static_cast<size_t>(s) * stage_stride + static_cast<size_t>(16 * rg + g) * srow + slice_off;
-            const uint8_t *p1 = p0 + 8 * static_cast<size_t>(srow);
-            MF::template chunk<0>(p0, p1, t, b, xs[0], sums, table, af, am);
-            MF::template chunk<1>(p0, p1, t, b, xs[1], sums, table, af, am);
+            const uint8_t *p[FR][2];
+#pragma unroll
+            for (int f = 0; f < FR; ++f) {
+                p[f][0] = smem + static_cast<size_t>(s) * stage_stride + static_cast<size_t>(rbase + 16 * f + g) * srow +
+                          slice_off;
+                p[f][1] = p[f][0] + 8 * static_cast<size_t>(srow);
+            }
+            MF::template chunk<0>(p, t, b, xs[0], sums, table, af, am);
+            MF::template chunk<1>(p, t, b, xs[1], sums, table, af, am);
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[s]);
         }
         // Recombine the limbs: lanes with even t hold limbs 0,1 (x 2^24, 2^16)
         // and subtract the min term, odd t limbs 2,3 (x 2^8, 1).
         const float whi = (t & 1) ? 256.0f : 16777216.0f, wlo = (t & 1) ? 1.0f : 65536.0f;
-        float v0 = fmaf(af[0], whi, af[1] * wlo) * down[0] * down[1];
-        float v1 = fmaf(af[2], whi, af[3] * wlo) * down[0] * down[1];
-        if (MF::kMins && !(t & 1)) {
-            v0 -= am[0];
-            v1 -= am[1];
-        }
-        v0 += __shfl_xor_sync(0xffffffffu, v0, 1);
-        v1 += __shfl_xor_sync(0xffffffffu, v1, 1);
         float *rb = red + static_cast<size_t>(k & 1) * R * S * 2;
-        if (!(t & 1)) {
-            rb[((16 * rg + g) * S + sw) * 2 + (t >> 1)] = v0;
-            rb[((16 * rg + g + 8) * S + sw) * 2 + (t >> 1)] = v1;
+#pragma unroll
+        for (int f = 0; f < FR; ++f) {
+            float v0 = fmaf(af[f][0], whi, af[f][1] * wlo) * down[0] * down[1];
+            float v1 = fmaf(af[f][2], whi, af[f][3] * wlo) * down[0] * down[1];
+            if (MF::kMins && !(t & 1)) {
+                v0 -= am[f][0];
+                v1 -= am[f][1];
+            }
+            v0 += __shfl_xor_sync(0xffffffffu, v0, 1);
+            v1 += __shfl_xor_sync(0xffffffffu, v1, 1);
+            if (!(t & 1)) {
+                rb[((rbase + 16 * f + g) * S + sw) * 2 + (t >> 1)] = v0;
+                rb[((rbase + 16 * f + g + 8) * S + sw) * 2 + (t >> 1)] = v1;
+            }
         }
         named_barrier_sync(2 + rg, S * 32);
         if (abort_flag[rg]) break;
-        if (sw == 0) {  // 16 rows x 2 tokens: S partials each, in fixed order
-            const int i = lane >> 1, slot = lane & 1;
-            float v = 0.0f;
+        if (sw == 0) {  // 16*FR rows x 2 tokens: S partials each, in fixed order
 #pragma unroll
-            for (int q = 0; q < S; ++q) v += rb[((16 * rg + i) * S + q) * 2 + slot];
-            float *o = slot ? J.out[1] : J.out[0];
-            if (16 * rg + i < nr && o) o[(r0 + 16 * rg + i) % rows_per_job] = v;
+            for (int o2 = lane; o2 < 32 * FR; o2 += 32) {
+                const int i = rbase + (o2 >> 1), slot = o2 & 1;
+                float v = 0.0f;
+#pragma unroll
+                for (int q = 0; q < S; ++q) v += rb[(i * S + q) * 2 + slot];
+                float *o = slot ? J.out[1] : J.out[0];
+                if (i < nr && o) o[(r0 + i) % rows_per_job] = v;
+            }
         }
     }
 }
@@ -511,7 +543,7 @@ static bool plan_mma(int64_t max_rows, int64_t max_tiles_extra, int cols, int ro
     p.S = cols / 512;
     if (!mma_slices_ok(p.S)) return false;
     p.RG = mma_row_groups(p.S);
-    const int R = 16 * p.RG;
+    const int R = 16 * MF::kFR * p.RG;
     // Shared-memory rows span an odd number of 16-byte units, so rows g = 0..7
     // of a fragment start in 8 different 4-bank groups.  Rows that already do
     // (IQ1_S: 400 or 1200 bytes) keep the global stride and arrive with one
