@@ -54,8 +54,9 @@ TOKENS = 32
 PROFILE_EXPERTS = 32
 IQ1_BLOCK, IQ1_BYTES = 256, 50
 EXPERT_MATRIX_BYTES = INTER * (HIDDEN // IQ1_BLOCK) * IQ1_BYTES  # 2,457,600; gate, up and down are equal
-# dram bytes per launch of the dominant kernel from the committed ncu capture, None until captured.
-NCU_TRAFFIC = None
+# dram bytes (read + write) per launch of the dominant kernel (gate+up), from the one-pass ncu
+# capture at this workload summarised in profiles/mma_rows_iq1_s_dram_full_config2.md.
+NCU_TRAFFIC = 906.5e6
 
 
 def use_ours():
