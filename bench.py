@@ -14,8 +14,9 @@ metric is decode tokens per second through the layer; the layer streams its
 from DRAM.  Synthetic, seeded data: the reference publishes no dataset.
 
 Also reported (key `fused_gemv`): BASELINE config 0 (Q8_0 2048x6144, batch 1)
-and config 1 (Q4_K 6144x2048, batch 1/4/16/64) fused dequant-GEMV GB/s,
-rotating weight copies beyond L2.
+and config 1 (Q4_K 6144x2048, batch 1/4/16/64) fused dequant-GEMV GB/s, and
+the FP8 E4M3 block-scaled projection (6144x6144, batch 1), rotating weight
+copies beyond L2.
 
 Arms:
   ours       device-resident timing (CUDA graph of the K timed steps, CUDA
@@ -349,6 +350,33 @@ def fused_gemv_sweep(rt, lib, dev, stream, steps, peak):
             xd.close()
             od.close()
         wbuf.close()
+    # FP8 E4M3 block-scaled projection (gpu/fp8.vx contract), 6144x6144, batch 1.
+    rows = cols = 6144
+    w8 = rng.integers(0, 256, size=rows * cols, dtype=np.uint8)
+    w8[(w8 & 0x7F) == 0x7F] = 0x3C
+    sc = (np.abs(rng.normal(size=(rows // 128) * (cols // 128))) * 0.02 + 1e-3).astype(np.float32)
+    x = rng.normal(size=cols).astype(np.float32)
+    wbytes = w8.nbytes
+    copies = max(4, math.ceil(2.5 * dev.l2_bytes / wbytes))
+    stride = (wbytes + 255) // 256 * 256
+    wbuf, sd, xd, od = rt.DeviceBuffer(stride * copies), rt.DeviceBuffer(sc.nbytes), rt.DeviceBuffer(x.nbytes), \
+        rt.DeviceBuffer(4 * rows)
+    for c in range(copies):
+        wbuf.upload(w8, stream.handle, offset=c * stride)
+    sd.upload(sc, stream.handle)
+    xd.upload(x, stream.handle)
+
+    def launch8(i):
+        rt.check(lib, lib.glmvx_fp8_matvec(od.ptr, wbuf.ptr + (i % copies) * stride, sd.ptr, xd.ptr, rows, cols,
+                                           stream.handle), 'glmvx_fp8_matvec')
+    reps = max(20, min(steps, 400))
+    for i in range(3):
+        launch8(i)
+    us = graph_time(rt, stream, launch8, reps) / reps * 1e3
+    alg = wbytes + sc.nbytes + x.nbytes + 4 * rows
+    res['fp8_e4m3_6144x6144_b1'] = {'us': us, 'gbs': alg / us / 1e3, 'frac_of_measured_hbm': alg / us / 1e3 / peak}
+    for b in (wbuf, sd, xd, od):
+        b.close()
     return res
 
 

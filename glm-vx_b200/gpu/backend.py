@@ -372,6 +372,35 @@ class GPUBackend:
         self._call('glmvx_index_scores', od, qd, kd, wd, tokens, heads, dim, scale, self.stream.handle)
         return self._fetch(offs, [out])[0]
 
+    def fp8_matvec(self, weight, scales, x):
+        """FP8 E4M3FN block-scaled projection with the contract of the
+        reference's GLMKernels.fp8_matvec (gpu/runtime.py:1031-1053):
+        weight uint8 [rows, cols], scales float32 [ceil(rows/128),
+        ceil(cols/128)], x float32 [cols] -> float32 [rows],
+        out[r] = sum_c (decode(w[r,c]) * scales[r//128, c//128]) * x[c].
+        As there, non-finite inputs and the E4M3 NaN encodings are outside the
+        finite-input contract and are not screened."""
+        self._begin()
+        weight, scales, x = np.asarray(weight), np.asarray(scales), np.asarray(x)
+        for name, arr, dtype in (('weight', weight, np.uint8), ('scales', scales, np.float32), ('x', x, np.float32)):
+            if arr.dtype != dtype:
+                raise ValueError(f'{name} must have dtype {np.dtype(dtype).name}')
+        if weight.ndim != 2:
+            raise ValueError(f'weight has incompatible shape {weight.shape}')
+        rows, cols = weight.shape
+        for name, value, minimum in (('rows', rows, 1), ('cols', cols, 0)):
+            if not minimum <= value <= _MAX:
+                raise ValueError(f'{name} must be between {minimum} and {_MAX}')
+        if scales.shape != ((rows + 127) // 128, (cols + 127) // 128):
+            raise ValueError(f'scales has incompatible shape {scales.shape}')
+        if x.shape != (cols,):
+            raise ValueError(f'x has incompatible shape {x.shape}')
+        weight, scales, x = (np.ascontiguousarray(a) for a in (weight, scales, x))
+        out = np.empty(rows, np.float32)
+        (wd, sd, xd), (od,), offs = self._stage([weight, scales, x], [out.nbytes])
+        self._call('glmvx_fp8_matvec', od, wd, sd, xd, rows, cols, self.stream.handle)
+        return self._fetch(offs, [out])[0]
+
     def mlp(self, gate, up, down, x):
         """down(SwiGLU(gate x, up x)) on expanded f32 weights, resident intermediates."""
         gate, up, down, x = _f32(gate, 'gate weight'), _f32(up, 'up weight'), _f32(down, 'down weight'), _f32(x)

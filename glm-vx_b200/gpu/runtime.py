@@ -83,6 +83,7 @@ SIGNATURES = {
                        _P, _P, _P], _I32),
     'glmvx_moe_ffn_profiled': ([_P, _P, _I32, _I32, _I32, _P, _P, _I32, _I32, _F32, _I32, _P, _P, _P, _P, _P, _P, _P,
                                 _U64, _P, _P], _I32),
+    'glmvx_fp8_matvec': ([_P, _P, _P, _P, _I32, _I32, _P], _I32),
 }
 
 

@@ -196,6 +196,13 @@ int32_t glmvx_moe_ffn_profiled(float *y, const float *x, int32_t tokens, int32_t
                                float scale, int32_t kind, const uint8_t *gate, const uint8_t *up, const uint8_t *down,
                                const uint8_t *shared_gate, const uint8_t *shared_up, const uint8_t *shared_down,
                                void *workspace, uint64_t workspace_bytes, void *const *events, void *stream);
+/* FP8 E4M3FN block-scaled projection, device pointers: out[rows] =
+ * sum_c (decode(weight[r,c]) * scales[r/128, c/128]) * x[c], weight u8
+ * [rows, cols], scales f32 [ceil(rows/128), ceil(cols/128)].  Replaces the
+ * reference's glm_vx_gpu_fp8_matvec (gpu/fp8.vx:50-89) launched by
+ * GLMKernels.fp8_matvec (gpu/runtime.py:1031-1053).  rows >= 1, cols >= 0. */
+int32_t glmvx_fp8_matvec(float *out, const uint8_t *weight, const float *scales, const float *x, int32_t rows,
+                         int32_t cols, void *stream);
 /* glmvx_moe_ffn without a caller workspace, for callers that cannot allocate
  * device memory (an embedding runtime that owns the whole memory budget, a
  * decode loop with a fixed footprint).  No counterpart in the reference.
