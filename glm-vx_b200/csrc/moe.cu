@@ -229,8 +229,9 @@ __global__ void __launch_bounds__(kGroupThreads)
 
 // y[t] = ((0 + o_0*w_0) + o_1*w_1 + ...) + shared_t, each product and sum
 // rounded separately as the reference's f32 array arithmetic does.
+// shared_rows (nullable) holds the shared expert's output of each token.
 __global__ void moe_combine_kernel(float *y, const float *pair_out, const int32_t *comb, const float *combw, int T,
-                                   int k, int hidden, int shared) {
+                                   int k, int hidden, const float *shared_rows) {
     const int t = blockIdx.y;
     const int h = blockIdx.x * blockDim.x + threadIdx.x;
     if (h >= hidden) return;
@@ -239,8 +240,12 @@ __global__ void moe_combine_kernel(float *y, const float *pair_out, const int32_
         const int p = comb[t * k + i];
         r = __fadd_rn(r, __fmul_rn(pair_out[static_cast<size_t>(p) * hidden + h], combw[t * k + i]));
     }
-    if (shared) r = __fadd_rn(r, pair_out[static_cast<size_t>(T * k + t) * hidden + h]);
+    if (shared_rows) r = __fadd_rn(r, shared_rows[static_cast<size_t>(t) * hidden + h]);
     y[static_cast<size_t>(t) * hidden + h] = r;
+}
+
+__global__ void fill_kernel(float *p, float v, int n) {
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) p[i] = v;
 }
 
 }  // namespace glmvx
@@ -257,7 +262,8 @@ static int32_t moe_ffn(float *y, const float *x, int32_t tokens, int32_t hidden,
                        const float *router_bias, int32_t experts, int32_t top_k, float scale, int32_t kind,
                        const uint8_t *gate, const uint8_t *up, const uint8_t *down, const uint8_t *shared_gate,
                        const uint8_t *shared_up, const uint8_t *shared_down, void *workspace, uint64_t workspace_bytes,
-                       int32_t *ids_out, float *weights_out, void *stream, void *const *events) {
+                       int32_t *ids_out, float *weights_out, void *stream, void *const *events,
+                       const int32_t *given_ids = nullptr) {
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     if (tokens < 0 || hidden <= 0 || inter <= 0 || experts <= 0 || top_k <= 0 || top_k > experts) {
         set_error("moe: invalid dimensions");
@@ -299,10 +305,16 @@ static int32_t moe_ffn(float *y, const float *x, int32_t tokens, int32_t hidden,
     int32_t st_ = mark(0);
     if (st_) return st_;
     if (mma && (st_ = prep_rows_device(w.xprep, x, nullptr, tokens, hidden, st))) return st_;
-    st_ = glmvx_matmul_nt(w.logits, x, router_w, tokens, experts, hidden, st);
-    if (st_ || (st_ = mark(1))) return st_;
-    st_ = glmvx_router(w.ids, w.wts, w.logits, router_bias, tokens, experts, top_k, scale, st);
-    if (st_ || (st_ = mark(2))) return st_;
+    if (given_ids) {  // routing supplied by the caller: unit combine weights
+        GLMVX_CUDA(cudaMemcpyAsync(w.ids, given_ids, 4ull * tokens * top_k, cudaMemcpyDeviceToDevice, st));
+        fill_kernel<<<(tokens * top_k + 255) / 256, 256, 0, st>>>(w.wts, 1.0f, tokens * top_k);
+        if ((st_ = launch_status("fill_kernel")) || (st_ = mark(1)) || (st_ = mark(2))) return st_;
+    } else {
+        st_ = glmvx_matmul_nt(w.logits, x, router_w, tokens, experts, hidden, st);
+        if (st_ || (st_ = mark(1))) return st_;
+        st_ = glmvx_router(w.ids, w.wts, w.logits, router_bias, tokens, experts, top_k, scale, st);
+        if (st_ || (st_ = mark(2))) return st_;
+    }
     moe_group_kernel<<<1, kGroupThreads, 0, st>>>(
         w.ids, w.wts, tokens, top_k, experts, shared, gate, up, down, gu_stride, dn_stride, shared_gate, shared_up,
         shared_down, x, hidden, inter, w.g_out, w.u_out, w.pair_out, w.gu_jobs, w.dn_jobs, w.comb, w.combw,
@@ -323,8 +335,9 @@ static int32_t moe_ffn(float *y, const float *x, int32_t tokens, int32_t hidden,
         if ((st_ = gemv_jobs_device(kind, w.dn_jobs, P, hidden, inter, down, w.g_out, st)) || (st_ = mark(5)))
             return st_;
     }
-    moe_combine_kernel<<<dim3((hidden + 255) / 256, tokens), 256, 0, st>>>(y, w.pair_out, w.comb, w.combw, tokens,
-                                                                           top_k, hidden, shared);
+    moe_combine_kernel<<<dim3((hidden + 255) / 256, tokens), 256, 0, st>>>(
+        y, w.pair_out, w.comb, w.combw, tokens, top_k, hidden,
+        shared ? w.pair_out + static_cast<size_t>(tokens) * top_k * hidden : nullptr);
     if ((st_ = launch_status("moe_combine_kernel")) || (st_ = mark(6))) return st_;
     if (ids_out) GLMVX_CUDA(cudaMemcpyAsync(ids_out, w.ids, 4ull * tokens * top_k, cudaMemcpyDeviceToDevice, st));
     if (weights_out)
@@ -353,6 +366,40 @@ GLMVX_EXPORT int32_t glmvx_moe_ffn_profiled(float *y, const float *x, int32_t to
                                             uint64_t workspace_bytes, void *const *events, void *stream) {
     return moe_ffn(y, x, tokens, hidden, inter, router_w, router_bias, experts, top_k, scale, kind, gate, up, down,
                    shared_gate, shared_up, shared_down, workspace, workspace_bytes, nullptr, nullptr, stream, events);
+}
+
+// Routed experts only, for rows whose experts are already chosen (the owner
+// rank's half of expert parallelism): y[i] = down_e(SwiGLU(gate_e x_i,
+// up_e x_i)) with e = expert_ids[i] in [0, experts).  The same grouping,
+// tensor-core jobs and ordering as glmvx_moe_ffn with one slot per row and no
+// router; workspace = glmvx_moe_workspace_bytes(rows, hidden, inter, experts,
+// 1, 0).  Out-of-range ids set the device error word (kDevErrBadIndex).
+GLMVX_EXPORT int32_t glmvx_moe_experts(float *y, const float *x, const int32_t *expert_ids, int32_t rows,
+                                       int32_t hidden, int32_t inter, int32_t experts, int32_t kind,
+                                       const uint8_t *gate, const uint8_t *up, const uint8_t *down, void *workspace,
+                                       uint64_t workspace_bytes, void *stream) {
+    if (rows > 0 && !expert_ids) {
+        set_error("moe experts: expert ids required");
+        return kInvalid;
+    }
+    return moe_ffn(y, x, rows, hidden, inter, nullptr, nullptr, experts, 1, 1.0f, kind, gate, up, down, nullptr,
+                   nullptr, nullptr, workspace, workspace_bytes, nullptr, nullptr, stream, nullptr, expert_ids);
+}
+
+// y[t] = ((0 + pair_out[comb[t,0]]*combw[t,0]) + ...) + shared_rows[t]: the
+// reference's ascending-expert-id combine (glm_vx/model.py:305-316) over pair
+// outputs gathered from elsewhere; shared_rows may be NULL.
+GLMVX_EXPORT int32_t glmvx_moe_combine(float *y, const float *pair_out, const int32_t *comb, const float *combw,
+                                       const float *shared_rows, int32_t tokens, int32_t top_k, int32_t hidden,
+                                       void *stream) {
+    if (tokens < 0 || top_k <= 0 || hidden <= 0) {
+        set_error("moe combine: invalid dimensions");
+        return kInvalid;
+    }
+    if (!tokens) return kOk;
+    moe_combine_kernel<<<dim3((hidden + 255) / 256, tokens), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        y, pair_out, comb, combw, tokens, top_k, hidden, shared_rows);
+    return launch_status("moe_combine_kernel");
 }
 
 // ---------------------------------------------------------------------------

@@ -461,6 +461,22 @@ static int ew_grid(int64_t n) { return static_cast<int>(std::max<int64_t>(1, std
 using namespace glmvx;
 #define S_ (cudaStream_t) stream
 
+__global__ void gather_rows_kernel(float *out, const float *x, const int32_t *idx, int n, int cols) {
+    const int r = blockIdx.y;
+    const float *src = x + static_cast<size_t>(idx[r]) * cols;
+    float *dst = out + static_cast<size_t>(r) * cols;
+    for (int c = blockIdx.x * blockDim.x + threadIdx.x; c < cols; c += gridDim.x * blockDim.x) dst[c] = src[c];
+}
+
+// out[i, :] = x[idx[i], :] for i < n (device pointers; idx must be in range).
+GLMVX_EXPORT int32_t glmvx_gather_rows(float *out, const float *x, const int32_t *idx, int32_t n, int32_t cols,
+                                       void *stream) {
+    if (n < 0 || cols < 0) return set_error("gather rows dims"), kInvalid;
+    if (!n || !cols) return kOk;
+    gather_rows_kernel<<<dim3((cols + 255) / 256, n), 256, 0, S_>>>(out, x, idx, n, cols);
+    return launch_status("gather_rows_kernel");
+}
+
 GLMVX_EXPORT int32_t glmvx_matvec_f32(float *out, const float *w, const float *x, int32_t rows, int32_t cols,
                                       void *stream) {
     if (rows < 0 || cols < 0) return set_error("matvec dims"), kInvalid;

@@ -196,6 +196,20 @@ int32_t glmvx_moe_ffn_profiled(float *y, const float *x, int32_t tokens, int32_t
                                float scale, int32_t kind, const uint8_t *gate, const uint8_t *up, const uint8_t *down,
                                const uint8_t *shared_gate, const uint8_t *shared_up, const uint8_t *shared_down,
                                void *workspace, uint64_t workspace_bytes, void *const *events, void *stream);
+/* Expert-parallel building blocks (the reference runs all experts in one
+ * process; these split glm_vx/model.py:289-324 between the rank that routes a
+ * token and the rank that owns its expert).  glmvx_moe_experts: routed experts
+ * for rows whose expert ids are given, y[i] = down_e(SwiGLU(gate_e x_i,
+ * up_e x_i)), workspace glmvx_moe_workspace_bytes(rows, hidden, inter,
+ * experts, 1, 0).  glmvx_moe_combine: ascending-expert-id weighted sum of pair
+ * outputs plus optional shared-expert rows (glm_vx/model.py:305-316).
+ * glmvx_gather_rows: out[i] = x[idx[i]]. */
+int32_t glmvx_moe_experts(float *y, const float *x, const int32_t *expert_ids, int32_t rows, int32_t hidden,
+                          int32_t inter, int32_t experts, int32_t kind, const uint8_t *gate, const uint8_t *up,
+                          const uint8_t *down, void *workspace, uint64_t workspace_bytes, void *stream);
+int32_t glmvx_moe_combine(float *y, const float *pair_out, const int32_t *comb, const float *combw,
+                          const float *shared_rows, int32_t tokens, int32_t top_k, int32_t hidden, void *stream);
+int32_t glmvx_gather_rows(float *out, const float *x, const int32_t *idx, int32_t n, int32_t cols, void *stream);
 /* FP8 E4M3FN block-scaled projection, device pointers: out[rows] =
  * sum_c (decode(weight[r,c]) * scales[r/128, c/128]) * x[c], weight u8
  * [rows, cols], scales f32 [ceil(rows/128), ceil(cols/128)].  Replaces the
