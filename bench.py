@@ -31,8 +31,10 @@ Arms:
              Vx kernels, one token per step, all host cores.
 
 Multi-GPU: each rank runs an independent replica of the layer on its own
-token batch ("replicas"; expert parallelism is a later step);
-torch.distributed over gloo carries only barriers and the max of device times.
+token batch (the headline, "replicas"); torch.distributed over gloo carries
+only barriers and the max of device times.  With N>1 the line also carries
+`expert_parallel`: the same layer with its experts sharded over the N GPUs
+(gpu/ep.py), exchanging (token, expert) rows with NCCL all-to-all.
 """
 import argparse
 import ctypes as C
@@ -167,6 +169,13 @@ class Ranks:
         t = torch.tensor([float(value)], dtype=torch.float64)
         self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
         return float(t.item())
+
+    def nccl_group(self):
+        """A second group over NCCL (the expert-parallel exchange); the
+        default gloo group keeps carrying barriers and max-reductions."""
+        import torch
+        torch.cuda.set_device(self.local)
+        return self.dist.new_group(backend='nccl')
 
     def close(self):
         if self.dist:
@@ -380,6 +389,47 @@ def fused_gemv_sweep(rt, lib, dev, stream, steps, peak):
     return res
 
 
+def expert_parallel_step(args, ranks, layer):
+    """N>1: the same layer with its 256 experts sharded over the ranks
+    (gpu/ep.py), TOKENS rows per rank; device time of the step (CUDA events on
+    the launching stream, host routing sync and NCCL exchanges inside), max
+    over ranks."""
+    import torch
+    from gpu.ep import ExpertParallelMoE
+    from kernels.packed import LAYOUTS
+    group = ranks.nccl_group()
+    per = EXPERTS // ranks.world
+    sl = slice(ranks.rank * per * EXPERT_MATRIX_BYTES, (ranks.rank + 1) * per * EXPERT_MATRIX_BYTES)
+    moe = ExpertParallelMoE(layer['router'], layer['bias'], KIND, layer['gate'][sl], layer['up'][sl],
+                            layer['down'][sl], EXPERTS, HIDDEN, INTER, TOPK, SCALE, shared=layer['shared'],
+                            group=group)
+    x = np.random.default_rng(300 + ranks.rank).normal(size=(TOKENS, HIDDEN)).astype(np.float32)
+    xd = torch.from_numpy(x).cuda()
+    from gpu.ep import ep_step
+
+    def step():
+        ids, wts = moe.route(xd)
+        return ep_step(xd, ids, wts, moe.per_rank, moe.exchange, moe.ops)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    steps = max(5, min(args.steps, 50))
+    ranks.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = ranks.max(e0.elapsed_time(e1))
+    ranks.barrier()
+    del moe
+    return {'tok_s': ranks.world * TOKENS * steps / (ms * 1e-3), 'ms_per_step': ms / steps, 'steps': steps,
+            'experts_per_gpu': per, 'tokens_per_rank': TOKENS,
+            'exchange': 'NCCL all_to_all_single: pair counts, token rows + expert ids out, pair outputs back'}
+
+
 def run_ours(args, ranks):
     use_ours()
     from gpu import runtime as rt
@@ -460,6 +510,7 @@ def run_ours(args, ranks):
     e2e_value = ranks.world * TOKENS * e2e_steps / e2e_s
 
     gemv = fused_gemv_sweep(rt, lib, dev, stream, args.steps, peak)
+    ep = expert_parallel_step(args, ranks, layer) if ranks.world > 1 and EXPERTS % ranks.world == 0 else None
     line = {
         'metric': METRIC, 'value': value, 'unit': 'tok/s', 'n_gpus': ranks.world, 'steps': args.steps,
         'warmup': args.warmup, 'ms_per_step': total_ms / args.steps, 'higher_is_better': True, 'scaling': 'weak',
@@ -474,6 +525,7 @@ def run_ours(args, ranks):
                      'traffic': NCU_TRAFFIC, 'kernel': 'mma_rows_kernel<IQ1_S> gate+up job list (tensor-core int8)',
                      'algorithmic_bytes_per_launch': gu_bytes, 'avg_launch_us': gu_us, 'peak_source': peak_kind},
         'fused_gemv': gemv,
+        **({'expert_parallel': ep} if ep else {}),
         'e2e': {'value': e2e_value, 'unit': 'tok/s', 'steps': e2e_steps,
                 'h2d_bytes_per_step': TOKENS * HIDDEN * 4, 'd2h_bytes_per_step': TOKENS * HIDDEN * 4 + 2 * TOKENS * TOPK * 4,
                 'api': 'gpu.moe.MoELayer.forward (host rows in, host rows + routing out)'},

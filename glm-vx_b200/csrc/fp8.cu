@@ -7,13 +7,14 @@
 // [cols] -> out f32 [rows], out[r] = sum_c (decode(w[r,c]) * s[r/128, c/128])
 // * x[c] (gpu/fp8.vx:20-38).
 //
-// One warp per row; per step a lane takes four consecutive weights from each
-// of four 128-column scale tiles (each load instruction of the warp reads 128
-// contiguous bytes), converts pairs with the hardware E4M3x2 -> f16x2
-// conversion (exact: every E4M3 value, subnormals included, is an f16 value;
-// NaN encodings become NaN), widens to f32 and multiplies by the activations
-// held in shared memory; the tile scale multiplies each 4-weight partial sum.
-// The row sum is a fixed shuffle tree (deterministic).
+// A CTA of 8 warps owns 16 rows (two per warp, interleaved for independent
+// loads); the activations are read through L1.  Per step a lane loads
+// 16 consecutive weight bytes of a row (a warp reads 512 contiguous bytes),
+// converts pairs with the hardware E4M3x2 -> f16x2 conversion (exact: every
+// E4M3 value, subnormals included, is an f16 value; NaN encodings become
+// NaN), widens to f32 and multiplies by the activations; the 16 columns lie
+// in one 128-column scale tile, whose scale multiplies the partial sum.  The
+// row sum is a fixed shuffle tree (deterministic).
 // HBM-bound: 1 byte per weight.
 #include <cuda_fp8.h>
 
@@ -21,61 +22,74 @@
 
 namespace glmvx {
 
-constexpr int kFp8Threads = 256, kFp8MaxSmemCols = 12288;
+constexpr int kFp8Threads = 256, kFp8RowsPerWarp = 2;
+constexpr int kFp8RowsPerCta = kFp8Threads / 32 * kFp8RowsPerWarp;
 
 __device__ __forceinline__ float2 e4m3x2_to_float2(uint32_t two) {
     const __half2_raw h = __nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(two & 0xffffu), __NV_E4M3);
     return __half22float2(*reinterpret_cast<const __half2 *>(&h));
 }
 
-template <bool SmemX>
+// 16 weights (one 16-byte word) against 16 activations of the same columns;
+// the four float4 activation reads go in a lane-rotated order.
+__device__ __forceinline__ float dot16(const uint4 q, const float *x16, int rot) {
+    const uint32_t words[4] = {q.x, q.y, q.z, q.w};
+    float part = 0.0f;
+#pragma unroll
+    for (int jj = 0; jj < 4; ++jj) {
+        const int j = (jj + rot) & 3;
+        const uint32_t wj = j == 0 ? words[0] : (j == 1 ? words[1] : (j == 2 ? words[2] : words[3]));
+        const float4 xq = __ldg(reinterpret_cast<const float4 *>(x16 + 4 * j));
+        const float2 a = e4m3x2_to_float2(wj), b = e4m3x2_to_float2(wj >> 16);
+        part = fmaf(a.x, xq.x, part);
+        part = fmaf(a.y, xq.y, part);
+        part = fmaf(b.x, xq.z, part);
+        part = fmaf(b.y, xq.w, part);
+    }
+    return part;
+}
+
 __global__ void __launch_bounds__(kFp8Threads)
     fp8_matvec_kernel(float *__restrict__ out, const uint8_t *__restrict__ w, const float *__restrict__ scales,
                       const float *__restrict__ x, int rows, int cols) {
-    extern __shared__ __align__(16) float xs[];
     const float *xv = x;
-    if constexpr (SmemX) {
-        for (int c = threadIdx.x; c < cols; c += kFp8Threads) xs[c] = x[c];
-        __syncthreads();
-        xv = xs;
-    }
     const int lane = threadIdx.x & 31;
-    const int64_t row = static_cast<int64_t>(blockIdx.x) * (kFp8Threads / 32) + (threadIdx.x >> 5);
-    if (row >= rows) return;
+    const int64_t row0 = static_cast<int64_t>(blockIdx.x) * kFp8RowsPerCta + (threadIdx.x >> 5) * kFp8RowsPerWarp;
+    if (row0 >= rows) return;
     const int64_t scale_cols = (static_cast<int64_t>(cols) + 127) / 128;
-    const float *srow = scales + (row / 128) * scale_cols;
-    const uint8_t *wr = w + row * static_cast<int64_t>(cols);
-    float sum = 0.0f;
-    const bool vec = (cols & 3) == 0 && (reinterpret_cast<uintptr_t>(w) & 3) == 0 &&
-                     (SmemX || (reinterpret_cast<uintptr_t>(x) & 15) == 0);
+    const bool vec = (cols & 15) == 0 && (reinterpret_cast<uintptr_t>(w) & 15) == 0 &&
+                     (reinterpret_cast<uintptr_t>(x) & 15) == 0;
+    float sum[kFp8RowsPerWarp] = {};
     if (vec) {
-        // Step of 512 columns = four 128-column scale tiles; lane l takes
-        // columns 4l..4l+3 of each tile (coalesced weight words, conflict-free
-        // float4 activation reads).
-        for (int c0 = 0; c0 < cols; c0 += 512) {
+        // A step covers 512 columns: lane l owns columns 16l..16l+15, inside
+        // the 128-column scale tile l/8.
+#pragma unroll 2
+        for (int c = 16 * lane; c < cols; c += 512) {
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const int c = c0 + 128 * i + 4 * lane;
-                if (c < cols) {
-                    const uint32_t q = __ldg(reinterpret_cast<const uint32_t *>(wr + c));
-                    const float4 xq = *reinterpret_cast<const float4 *>(xv + c);
-                    const float2 a = e4m3x2_to_float2(q), b = e4m3x2_to_float2(q >> 16);
-                    float part = a.x * xq.x;
-                    part = fmaf(a.y, xq.y, part);
-                    part = fmaf(b.x, xq.z, part);
-                    part = fmaf(b.y, xq.w, part);
-                    sum = fmaf(__ldg(srow + c / 128), part, sum);
+            for (int r = 0; r < kFp8RowsPerWarp; ++r) {
+                const int64_t row = row0 + r;
+                if (row < rows) {
+                    const uint4 q = __ldg(reinterpret_cast<const uint4 *>(w + row * cols + c));
+                    const float s = __ldg(scales + (row / 128) * scale_cols + c / 128);
+                    sum[r] = fmaf(s, dot16(q, xv + c, lane >> 1), sum[r]);
                 }
             }
         }
     } else {  // any width / alignment: one byte per lane per step
-        for (int c = lane; c < cols; c += 32) {
-            const float v = e4m3x2_to_float2(wr[c]).x;
-            sum = fmaf(v * __ldg(srow + c / 128), xv[c], sum);
+        for (int r = 0; r < kFp8RowsPerWarp; ++r) {
+            const int64_t row = row0 + r;
+            if (row >= rows) break;
+            for (int c = lane; c < cols; c += 32) {
+                const float v = e4m3x2_to_float2(w[row * cols + c]).x;
+                sum[r] = fmaf(v * __ldg(scales + (row / 128) * scale_cols + c / 128), xv[c], sum[r]);
+            }
         }
     }
-    sum = warp_sum(sum);
-    if (lane == 0) out[row] = sum;
+#pragma unroll
+    for (int r = 0; r < kFp8RowsPerWarp; ++r) {
+        const float v = warp_sum(sum[r]);
+        if (lane == 0 && row0 + r < rows) out[row0 + r] = v;
+    }
 }
 
 }  // namespace glmvx
@@ -91,18 +105,9 @@ GLMVX_EXPORT int32_t glmvx_fp8_matvec(float *out, const uint8_t *weight, const f
         return kInvalid;
     }
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    const dim3 grid(static_cast<unsigned>((rows + 7) / 8));
-    if (cols <= kFp8MaxSmemCols) {
-        const size_t smem = sizeof(float) * static_cast<size_t>(cols);
-        static bool configured = false;
-        if (!configured) {
-            GLMVX_CUDA(cudaFuncSetAttribute(fp8_matvec_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                            static_cast<int>(sizeof(float) * kFp8MaxSmemCols)));
-            configured = true;
-        }
-        fp8_matvec_kernel<true><<<grid, kFp8Threads, smem, st>>>(out, weight, scales, x, rows, cols);
-    } else {
-        fp8_matvec_kernel<false><<<grid, kFp8Threads, 0, st>>>(out, weight, scales, x, rows, cols);
-    }
+    const dim3 grid(static_cast<unsigned>((rows + kFp8RowsPerCta - 1) / kFp8RowsPerCta));
+    // Activations are read through L1 (they fit, and every warp of an SM
+    // reuses them); no shared-memory staging, so weight loads start at once.
+    fp8_matvec_kernel<<<grid, kFp8Threads, 0, st>>>(out, weight, scales, x, rows, cols);
     return launch_status("fp8_matvec_kernel");
 }
