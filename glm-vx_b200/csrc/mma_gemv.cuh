@@ -52,8 +52,12 @@ int32_t prep_rows_device(uint8_t *prep, const float *x, const float *x2, int row
 //    kernel completes, clamped to max_jobs), else max_jobs.
 //  * jobs == nullptr: `batch` tokens against one matrix: job j applies job0.w
 //    to prepared rows 2j and 2j+1 of job0.xp[0] (stride prep_stride(cols))
-//    and writes rows of job0.out[0] (stride rows_per_job floats).
+//    and writes rows of job0.out[0] (stride rows_per_job floats).  With
+//    x_raw set instead (f32 rows [batch][cols], 16-byte aligned), each CTA
+//    prepares the rows of the jobs it reaches in shared memory, so no
+//    separate preparation or scratch is needed; returns kUnsupported when the
+//    shape leaves no room for that (use the prepared-row form then).
 int32_t mma_gemv_device(int32_t kind, const MmaJob &job0, const MmaJob *jobs, const int *njobs_dev, int max_jobs,
-                        int batch, int rows_per_job, int cols, cudaStream_t stream);
+                        int batch, int rows_per_job, int cols, cudaStream_t stream, const float *x_raw = nullptr);
 
 }  // namespace glmvx

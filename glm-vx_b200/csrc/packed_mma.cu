@@ -244,8 +244,9 @@ struct MmaFmt<FmtQ4_K> {
         if (sums) {
             const uint32_t ml0 = h0.z & 0x3F3F3F3Fu, mh0 = ((h0.w >> 4) & 0x0F0F0F0Fu) | ((h0.z >> 2) & 0x30303030u);
             const uint32_t ml1 = h1.z & 0x3F3F3F3Fu, mh1 = ((h1.w >> 4) & 0x0F0F0F0Fu) | ((h1.z >> 2) & 0x30303030u);
-            const float4 xa = __ldg(reinterpret_cast<const float4 *>(sums + 8 * C));
-            const float4 xb = __ldg(reinterpret_cast<const float4 *>(sums + 8 * C) + 1);
+            // generic loads: the sums live in global or (fused preparation) shared memory
+            const float4 xa = *reinterpret_cast<const float4 *>(sums + 8 * C);
+            const float4 xb = *(reinterpret_cast<const float4 *>(sums + 8 * C) + 1);
             const float xv[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
             float m0 = 0.0f, m1 = 0.0f;
 #pragma unroll
@@ -258,6 +259,75 @@ struct MmaFmt<FmtQ4_K> {
         }
     }
 };
+
+// --------------------------------------------------------------- prepare ---
+
+// One warp prepares one 256-column chunk of one activation row (8 columns
+// per lane): x (or SwiGLU(x, x2)) -> four int8 limb planes, the chunk's
+// exponent and its 32-column sums, into the prepared row at `out`.
+__device__ __forceinline__ void prep_chunk(uint8_t *out, const float *x, const float *x2, int cols, int chunk,
+                                           int lane) {
+    const int c0 = chunk * 256 + lane * 8;
+    const float4 *xr = reinterpret_cast<const float4 *>(x + c0);
+    float4 lo = __ldg(xr), hi = __ldg(xr + 1);
+    if (x2) {
+        const float4 *ur = reinterpret_cast<const float4 *>(x2 + c0);
+        const float4 ulo = __ldg(ur), uhi = __ldg(ur + 1);
+        lo = make_float4(silu_mul(lo.x, ulo.x), silu_mul(lo.y, ulo.y), silu_mul(lo.z, ulo.z), silu_mul(lo.w, ulo.w));
+        hi = make_float4(silu_mul(hi.x, uhi.x), silu_mul(hi.y, uhi.y), silu_mul(hi.z, uhi.z), silu_mul(hi.w, uhi.w));
+    }
+    const float v[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+    float mx = 0.0f;
+    bool finite = true;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        mx = fmaxf(mx, fabsf(v[i]));
+        finite &= isfinite(v[i]);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    finite = __all_sync(0xffffffffu, finite);
+    // 2^E puts the chunk's largest magnitude in [2^29, 2^30) (below 2^30 for
+    // subnormal maxima, E = 156); applied as two exact power-of-two factors.
+    const int ebits = (__float_as_int(mx) >> 23) & 0xff;
+    const int E = mx == 0.0f ? 0 : 156 - ebits;
+    const float up0 = pow2(E / 2), up1 = pow2(E - E / 2);
+    uint32_t qq[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+        qq[i] = static_cast<uint32_t>(__float2int_rn(finite ? (v[i] * up0) * up1 : 0.0f)) + 0x808080u;
+    // Balanced base-256 digits: the low three bytes of q + 0x808080 are
+    // digit + 128, the top byte is the (signed) top digit.
+#pragma unroll
+    for (int l = 0; l < 4; ++l) {
+        const int p = 3 - l;  // byte position of limb l
+        const uint32_t sel = static_cast<uint32_t>(p | ((p + 4) << 4));
+        const uint32_t flip = l ? 0x80808080u : 0u;
+        const uint32_t w0 = __byte_perm(__byte_perm(qq[0], qq[1], sel), __byte_perm(qq[2], qq[3], sel), 0x5410) ^ flip;
+        const uint32_t w1 = __byte_perm(__byte_perm(qq[4], qq[5], sel), __byte_perm(qq[6], qq[7], sel), 0x5410) ^ flip;
+        *reinterpret_cast<uint2 *>(out + static_cast<size_t>(l) * cols + c0) = make_uint2(w0, w1);
+    }
+    float sum = ((v[0] + v[1]) + (v[2] + v[3])) + ((v[4] + v[5]) + (v[6] + v[7]));
+    sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+    sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+    if ((lane & 3) == 0) reinterpret_cast<float *>(out + prep_sums_offset(cols))[c0 / 32] = sum;
+    if (lane == 0) reinterpret_cast<int *>(out + prep_scale_offset(cols))[chunk] = finite ? E : kPrepNonFinite;
+}
+
+// One warp per (row, 256-column chunk).
+__global__ void __launch_bounds__(256)
+    prep_rows_kernel(uint8_t *__restrict__ prep, const float *__restrict__ x, const float *__restrict__ x2, int rows,
+                     int cols) {
+    grid_dependency_wait();
+    allow_dependent_launch();
+    const int chunks = cols >> 8;
+    const int64_t wid = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (wid >= static_cast<int64_t>(rows) * chunks) return;  // warp-uniform
+    const int row = static_cast<int>(wid / chunks), chunk = static_cast<int>(wid % chunks);
+    prep_chunk(prep + static_cast<size_t>(row) * prep_stride(cols), x + static_cast<size_t>(row) * cols,
+               x2 ? x2 + static_cast<size_t>(row) * cols : nullptr, cols, chunk, lane);
+}
 
 // ----------------------------------------------------------------- kernel ---
 
@@ -281,24 +351,30 @@ __device__ __forceinline__ MmaJob job_at(const MmaJob &job0, const MmaJob *jobs,
 template <class F, int S, int RG>
 __global__ void __launch_bounds__((S * RG + 1) * 32, 1)
     mma_rows_kernel(MmaJob job0, const MmaJob *__restrict__ jobs, const int *njobs_dev, int max_jobs, int batch,
-                    int rows_per_job, int cols, int row_bytes, int srow, int stages, int stage_stride, int *err) {
+                    int rows_per_job, int cols, int row_bytes, int srow, int stages, int stage_stride,
+                    const float *__restrict__ x_raw, int *err) {
     using MF = MmaFmt<F>;
     constexpr int FR = MF::kFR;
     constexpr int NW = S * RG, R = 16 * FR * RG;  // a warp owns FR 16-row fragments of the tile
     extern __shared__ __align__(128) uint8_t smem[];
-    uint8_t *table = smem + static_cast<size_t>(stages) * stage_stride;
+    const size_t pstride = prep_stride(cols);
+    // x_raw set (single matrix, `batch` token rows of f32): the CTA prepares
+    // the two rows of each job it reaches into `bsm` itself.
+    uint8_t *bsm = smem + static_cast<size_t>(stages) * stage_stride;
+    uint8_t *table = bsm + (x_raw ? 2 * pstride : 0);
     float *red = reinterpret_cast<float *>(table + MF::kTableBytes);  // [2][R][S][2]
     uint64_t *full = reinterpret_cast<uint64_t *>(red + 2 * R * S * 2);
     uint64_t *empty = full + stages;
-    volatile int *abort_flag = reinterpret_cast<volatile int *>(empty + stages);  // [RG]
+    uint64_t *jobbar = empty + stages;  // consumer warps meet here around a job's preparation
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(jobbar + 1);  // [RG]
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const size_t pstride = prep_stride(cols);
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < stages; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], NW);
         }
+        mbar_init(jobbar, NW);
         for (int i = 0; i < RG; ++i) abort_flag[i] = 0;
         fence_mbar_init();
     }
@@ -368,19 +444,46 @@ __global__ void __launch_bounds__((S * RG + 1) * 32, 1)
     const float *sums = nullptr;
     MmaJob J{};
     int loaded = -1;
+    uint32_t jb_phase = 0;
+    // Every consumer warp arrives; false if the others did not arrive in time.
+    auto job_sync = [&]() -> bool {
+        __syncwarp();
+        if (lane == 0) mbar_arrive(jobbar);
+        const bool ok = mbar_wait_bounded(jobbar, jb_phase & 1);
+        ++jb_phase;
+        return __all_sync(0xffffffffu, ok);
+    };
     int k = 0;
     for (int r0 = r_begin; r0 < r_end; r0 = tile_end(r0, r_end), ++k) {
         const int job = r0 / rows_per_job;
         if (job != loaded) {  // uniform across the CTA
             loaded = job;
             J = job_at(job0, jobs, job, batch, rows_per_job, pstride);
+            if (x_raw) {
+                // The previous job's rows are in use until every warp is here.
+                if (!job_sync()) {
+                    if (lane == 0) report_device_error(err, kDevErrFullWait);
+                    break;
+                }
+                const int chunks = cols >> 8;
+                for (int c = warp; c < 2 * chunks; c += NW) {
+                    const int slot = c / chunks, tok = 2 * job + slot;
+                    if (tok < batch)
+                        prep_chunk(bsm + slot * pstride, x_raw + static_cast<size_t>(tok) * cols, nullptr, cols,
+                                   c % chunks, lane);
+                }
+                if (!job_sync()) {
+                    if (lane == 0) report_device_error(err, kDevErrFullWait);
+                    break;
+                }
+                J.xp[0] = bsm;
+                J.xp[1] = 2 * job + 1 < batch ? bsm + pstride : nullptr;
+            }
             const uint8_t *xb = (g >> 2) ? J.xp[1] : J.xp[0];  // B column g: token g/4, limb g%4
 #pragma unroll
             for (int u = 0; u < kSliceSub; ++u) {
                 uint2 v = make_uint2(0u, 0u);
-                if (xb)
-                    v = __ldg(reinterpret_cast<const uint2 *>(xb + static_cast<size_t>(g & 3) * cols + 32 * (u0 + u) +
-                                                              8 * t));
+                if (xb) v = *reinterpret_cast<const uint2 *>(xb + static_cast<size_t>(g & 3) * cols + 32 * (u0 + u) + 8 * t);
                 b[u][0] = v.x;
                 b[u][1] = v.y;
             }
@@ -391,8 +494,8 @@ __global__ void __launch_bounds__((S * RG + 1) * 32, 1)
             // A chunk more than 2^126 below the other contributes nothing.
             int e0 = 0, e1 = 0;
             if (xa) {
-                e0 = __ldg(reinterpret_cast<const int *>(xa + scale_off) + u0 / 8);
-                e1 = __ldg(reinterpret_cast<const int *>(xa + scale_off) + u0 / 8 + 1);
+                e0 = reinterpret_cast<const int *>(xa + scale_off)[u0 / 8];
+                e1 = reinterpret_cast<const int *>(xa + scale_off)[u0 / 8 + 1];
             }
             const bool bad = e0 == kPrepNonFinite || e1 == kPrepNonFinite;
             const int eref = bad ? 0 : min(e0, e1);
@@ -459,67 +562,6 @@ __global__ void __launch_bounds__((S * RG + 1) * 32, 1)
     }
 }
 
-// --------------------------------------------------------------- prepare ---
-
-// One warp per (row, 256-column chunk): 8 columns per lane.
-__global__ void __launch_bounds__(256)
-    prep_rows_kernel(uint8_t *__restrict__ prep, const float *__restrict__ x, const float *__restrict__ x2, int rows,
-                     int cols) {
-    grid_dependency_wait();
-    allow_dependent_launch();
-    const int chunks = cols >> 8;
-    const int64_t wid = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
-    const int lane = threadIdx.x & 31;
-    if (wid >= static_cast<int64_t>(rows) * chunks) return;  // warp-uniform
-    const int row = static_cast<int>(wid / chunks), chunk = static_cast<int>(wid % chunks);
-    const int c0 = chunk * 256 + lane * 8;
-    const float4 *xr = reinterpret_cast<const float4 *>(x + static_cast<size_t>(row) * cols + c0);
-    float4 lo = __ldg(xr), hi = __ldg(xr + 1);
-    if (x2) {
-        const float4 *ur = reinterpret_cast<const float4 *>(x2 + static_cast<size_t>(row) * cols + c0);
-        const float4 ulo = __ldg(ur), uhi = __ldg(ur + 1);
-        lo = make_float4(silu_mul(lo.x, ulo.x), silu_mul(lo.y, ulo.y), silu_mul(lo.z, ulo.z), silu_mul(lo.w, ulo.w));
-        hi = make_float4(silu_mul(hi.x, uhi.x), silu_mul(hi.y, uhi.y), silu_mul(hi.z, uhi.z), silu_mul(hi.w, uhi.w));
-    }
-    const float v[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
-    float mx = 0.0f;
-    bool finite = true;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        mx = fmaxf(mx, fabsf(v[i]));
-        finite &= isfinite(v[i]);
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    finite = __all_sync(0xffffffffu, finite);
-    // 2^E puts the chunk's largest magnitude in [2^29, 2^30) (below 2^30 for
-    // subnormal maxima, E = 156); applied as two exact power-of-two factors.
-    const int ebits = (__float_as_int(mx) >> 23) & 0xff;
-    const int E = mx == 0.0f ? 0 : 156 - ebits;
-    const float up0 = pow2(E / 2), up1 = pow2(E - E / 2);
-    uint32_t qq[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i)
-        qq[i] = static_cast<uint32_t>(__float2int_rn(finite ? (v[i] * up0) * up1 : 0.0f)) + 0x808080u;
-    // Balanced base-256 digits: the low three bytes of q + 0x808080 are
-    // digit + 128, the top byte is the (signed) top digit.
-    uint8_t *out = prep + static_cast<size_t>(row) * prep_stride(cols);
-#pragma unroll
-    for (int l = 0; l < 4; ++l) {
-        const int p = 3 - l;  // byte position of limb l
-        const uint32_t sel = static_cast<uint32_t>(p | ((p + 4) << 4));
-        const uint32_t flip = l ? 0x80808080u : 0u;
-        const uint32_t w0 = __byte_perm(__byte_perm(qq[0], qq[1], sel), __byte_perm(qq[2], qq[3], sel), 0x5410) ^ flip;
-        const uint32_t w1 = __byte_perm(__byte_perm(qq[4], qq[5], sel), __byte_perm(qq[6], qq[7], sel), 0x5410) ^ flip;
-        *reinterpret_cast<uint2 *>(out + static_cast<size_t>(l) * cols + c0) = make_uint2(w0, w1);
-    }
-    float sum = ((v[0] + v[1]) + (v[2] + v[3])) + ((v[4] + v[5]) + (v[6] + v[7]));
-    sum += __shfl_xor_sync(0xffffffffu, sum, 1);
-    sum += __shfl_xor_sync(0xffffffffu, sum, 2);
-    if ((lane & 3) == 0) reinterpret_cast<float *>(out + prep_sums_offset(cols))[c0 / 32] = sum;
-    if (lane == 0) reinterpret_cast<int *>(out + prep_scale_offset(cols))[chunk] = finite ? E : kPrepNonFinite;
-}
-
 // ------------------------------------------------------------------- host ---
 
 struct MmaPlan {
@@ -537,7 +579,7 @@ constexpr bool mma_slices_ok(int S) {
 }
 
 template <class F>
-static bool plan_mma(int64_t max_rows, int64_t max_tiles_extra, int cols, int row_bytes, MmaPlan &p) {
+static bool plan_mma(int64_t max_rows, int64_t max_tiles_extra, int cols, int row_bytes, bool fused, MmaPlan &p) {
     using MF = MmaFmt<F>;
     if (cols % 512 || row_bytes % 16) return false;
     p.S = cols / 512;
@@ -552,11 +594,14 @@ static bool plan_mma(int64_t max_rows, int64_t max_tiles_extra, int cols, int ro
     // a row: the last block of a row has an odd index.)
     p.srow = ((row_bytes >> 4) & 1) ? row_bytes : row_bytes + 16;
     p.stage_stride = (R * p.srow + 127) & ~127;
-    const size_t fixed = MF::kTableBytes + 2ull * R * p.S * 2 * 4 + 16 * 8 + 64;
+    const size_t fixed = (fused ? 2 * prep_stride(cols) : 0) + MF::kTableBytes + 2ull * R * p.S * 2 * 4 + 16 * 8 + 64;
     const int fit = static_cast<int>((kMmaSmemBudget - std::min(fixed, kMmaSmemBudget)) / p.stage_stride);
     if (fit < 1) return false;
     const int64_t tiles = (max_rows + R - 1) / R + max_tiles_extra;
     p.stages = static_cast<int>(std::min<int64_t>(std::min(fit, 8), std::max<int64_t>(1, tiles)));
+    // In-kernel preparation trades stages for its rows; keep it only while
+    // every CTA still overlaps loading with compute, or has one tile anyway.
+    if (fused && p.stages < 2 && tiles > sm_count()) return false;
     p.grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(sm_count(), tiles)));
     p.smem = static_cast<size_t>(p.stages) * p.stage_stride + fixed;
     return true;
@@ -564,7 +609,8 @@ static bool plan_mma(int64_t max_rows, int64_t max_tiles_extra, int cols, int ro
 
 template <class F, int S>
 static int32_t launch_mma(const MmaPlan &p, const MmaJob &job0, const MmaJob *jobs, const int *njobs_dev,
-                          int max_jobs, int batch, int rows_per_job, int cols, int row_bytes, cudaStream_t stream) {
+                          int max_jobs, int batch, int rows_per_job, int cols, int row_bytes, const float *x_raw,
+                          cudaStream_t stream) {
     constexpr int RG = mma_row_groups(S);
     auto kern = mma_rows_kernel<F, S, RG>;
     static size_t configured = 0;  // per instantiation
@@ -583,15 +629,18 @@ static int32_t launch_mma(const MmaPlan &p, const MmaJob &job0, const MmaJob *jo
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     GLMVX_CUDA(cudaLaunchKernelEx(&cfg, kern, job0, jobs, njobs_dev, max_jobs, batch, rows_per_job, cols, row_bytes,
-                                  p.srow, p.stages, p.stage_stride, device_error_word()));
+                                  p.srow, p.stages, p.stage_stride, x_raw, device_error_word()));
     return kOk;
 }
 
 template <class F>
 static int32_t launch_mma_s(const MmaPlan &p, const MmaJob &job0, const MmaJob *jobs, const int *njobs_dev,
-                            int max_jobs, int batch, int rows_per_job, int cols, int row_bytes, cudaStream_t stream) {
-#define GLMVX_MMA_CASE(s) \
-    case s: return launch_mma<F, s>(p, job0, jobs, njobs_dev, max_jobs, batch, rows_per_job, cols, row_bytes, stream);
+                            int max_jobs, int batch, int rows_per_job, int cols, int row_bytes, const float *x_raw,
+                            cudaStream_t stream) {
+#define GLMVX_MMA_CASE(s)                                                                                       \
+    case s:                                                                                                    \
+        return launch_mma<F, s>(p, job0, jobs, njobs_dev, max_jobs, batch, rows_per_job, cols, row_bytes, x_raw, \
+                                stream);
     switch (p.S) {
         GLMVX_MMA_CASE(1)
         GLMVX_MMA_CASE(2)
@@ -635,7 +684,11 @@ int32_t prep_rows_device(uint8_t *prep, const float *x, const float *x2, int row
 }
 
 int32_t mma_gemv_device(int32_t kind, const MmaJob &job0, const MmaJob *jobs, const int *njobs_dev, int max_jobs,
-                        int batch, int rows_per_job, int cols, cudaStream_t stream) {
+                        int batch, int rows_per_job, int cols, cudaStream_t stream, const float *x_raw) {
+    if (x_raw && (jobs || (reinterpret_cast<uintptr_t>(x_raw) & 15))) {
+        set_error("mma: in-kernel preparation needs a single matrix and 16-byte aligned activations");
+        return kInvalid;
+    }
     if (!mma_supported(kind, cols) || rows_per_job <= 0 || max_jobs <= 0) {
         set_error("mma: unsupported format or shape");
         return kUnsupported;
@@ -652,12 +705,13 @@ int32_t mma_gemv_device(int32_t kind, const MmaJob &job0, const MmaJob *jobs, co
     dispatch_format(kind, [&]<class F>() {
         if constexpr (std::is_same_v<F, FmtQ8_0> || std::is_same_v<F, FmtQ4_K> || std::is_same_v<F, FmtIQ1_S>) {
             MmaPlan p;
-            if (!plan_mma<F>(max_rows, max_jobs, cols, row_bytes, p)) {
+            if (!plan_mma<F>(max_rows, max_jobs, cols, row_bytes, x_raw != nullptr, p)) {
                 set_error("mma: no launch plan for this shape");
                 st = kUnsupported;
                 return;
             }
-            st = launch_mma_s<F>(p, job0, jobs, njobs_dev, max_jobs, batch, rows_per_job, cols, row_bytes, stream);
+            st = launch_mma_s<F>(p, job0, jobs, njobs_dev, max_jobs, batch, rows_per_job, cols, row_bytes, x_raw,
+                                 stream);
         }
     });
     return st;
