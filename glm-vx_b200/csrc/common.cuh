@@ -91,6 +91,21 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
     return done != 0;
 }
 
+// try_wait with a suspend-time hint: the thread sleeps in the barrier until
+// the phase completes or about `hint_ns` pass, instead of re-issuing the test
+// (a spinning warp takes issue slots from the warps doing the work).
+__device__ __forceinline__ bool mbar_try_wait_suspend(uint64_t *bar, uint32_t parity, uint32_t hint_ns) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(smem_addr(bar)), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return done != 0;
+}
+
 // Wait for the phase with the given parity to complete, giving up after
 // `limit_ns` of wall time.  Returns false on timeout (the caller records the
 // error and returns; it never traps).
@@ -98,9 +113,9 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity
                                                   uint64_t limit_ns = 2000000000ull) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t start = globaltimer_ns();
-    for (uint32_t spin = 0;; ++spin) {
-        if (mbar_try_wait(bar, parity)) return true;
-        if ((spin & 255u) == 255u && globaltimer_ns() - start > limit_ns) return false;
+    for (;;) {
+        if (mbar_try_wait_suspend(bar, parity, 100000u)) return true;
+        if (globaltimer_ns() - start > limit_ns) return false;
     }
 }
 

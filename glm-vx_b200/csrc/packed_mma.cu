@@ -74,20 +74,49 @@ __device__ __forceinline__ float pow2(int e) { return __int_as_float((127 + e) <
 __device__ __forceinline__ uint32_t lds32(const uint8_t *p) { return *reinterpret_cast<const uint32_t *>(p); }
 __device__ __forceinline__ uint2 lds64(const uint8_t *p) { return *reinterpret_cast<const uint2 *>(p); }
 
-// Per-format work on one 256-column chunk of a 16-row fragment.  p0/p1 point
-// at rows g and g+8 of the warp's column slice in shared memory, b[] are the
-// slice's B fragments (16 sub-blocks), xs is the chunk's scale relative to
-// the slice's larger-magnitude chunk (for this lane's accumulator token), sums the slice's
-// sub-block activation sums.  af[] are the f32 accumulators (rows g, g+8 x
-// this lane's two limb columns), am[] the min-term accumulators of rows g, g+8.
+// Per-format work on one 256-column chunk (chunk C of the warp's column
+// slice) of kFR 16-row fragments.  p[f][0]/p[f][1] point at rows g and g+8
+// of fragment f at the slice start in shared memory, b[] are the slice's B
+// fragments (NB sub-blocks), xs is the chunk's scale relative to the slice's
+// largest-magnitude chunk (for this lane's accumulator token), sums the
+// slice's sub-block activation sums, table this lane's view of the format's
+// shared-memory table.  af[] are the f32 accumulators (rows g, g+8 x this
+// lane's two limb columns), am[] the min-term accumulators of rows g, g+8.
 template <class F>
 struct MmaFmt;
+
+// PRMT in its default mode.  CUDA's __byte_perm ignores bit 3 of each
+// selector nibble, so for a selector only known at run time the compiler
+// masks it first; the codebook nibbles here are 0..2 (bit 3 clear), where
+// both agree, so the mask is not needed.
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+    uint32_t r;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
+    return r;
+}
+
+// (a & b) | c as one LOP3 with all three operands in registers.
+__device__ __forceinline__ uint32_t and_or(uint32_t a, uint32_t b, uint32_t c) {
+    uint32_t r;
+    asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(r) : "r"(a), "r"(b), "r"(c));
+    return r;
+}
+
+// 32-bit load from a shared-memory address held as a 32-bit integer (no
+// generic-to-shared conversion per access).  Only for data that does not
+// change while the kernel runs after its initial barrier (the codebook).
+__device__ __forceinline__ uint32_t lds32_const(uint32_t addr) {
+    uint32_t v;
+    asm("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr));
+    return v;
+}
 
 template <>
 struct MmaFmt<FmtIQ1_S> {
     // Codebook as 8 nibbles g+1 (0..2) per entry, four interleaved copies:
     // copy c of entry i at byte 16*i + 4*c.  Lane t of a quad reads copy t,
     // so the 32 lanes of a lookup fall in four disjoint groups of 8 banks.
+    // (Eight copies, spreading also by row parity, measured no faster.)
     static constexpr int kTableBytes = 2048 * 16, kSubPerBlock = 8, kBlockBytes = 50;
     static constexpr bool kMins = false;
     static constexpr int kFR = 2;  // 16-row fragments per warp (independent work to hide latency)
@@ -107,32 +136,45 @@ struct MmaFmt<FmtIQ1_S> {
             *reinterpret_cast<uint4 *>(table + 16 * i) = make_uint4(v, v, v, v);
         }
     }
-    template <int C>
-    __device__ __forceinline__ static void chunk(const uint8_t *const (&p)[kFR][2], int t, const uint32_t (&b)[16][2],
-                                                 float xs, const float *, const uint8_t *table, float (&af)[kFR][4],
+    // This lane's copy of the codebook.
+    __device__ static const uint8_t *table_for_lane(const uint8_t *table, int lane) { return table + 4 * (lane & 3); }
+    template <int C, int NB>
+    __device__ __forceinline__ static void chunk(const uint8_t *const (&p)[kFR][2], int t, const uint32_t (&b)[NB][2],
+                                                 float xs, const float *, const uint8_t *tab, float (&af)[kFR][4],
                                                  float (&)[kFR][2]) {
-        const uint8_t *tab = table + 4 * t;
         const int sh = 3 * t;
+        constexpr uint32_t step = kLutMinus - kLutPlus;
+        const uint32_t k14 = 14u, k1 = 1u;
+        const uint32_t tab_s = smem_addr(tab);
+        const uint8_t *q[kFR][2], *qt[kFR][2];  // block C of rows g, g+8; its qs byte of group t
+#pragma unroll
+        for (int f = 0; f < kFR; ++f)
+#pragma unroll
+            for (int r = 0; r < 2; ++r) {
+                q[f][r] = p[f][r] + C * kBlockBytes;
+                qt[f][r] = q[f][r] + 2 + t;
+            }
         int ai[kFR][4] = {};
 #pragma unroll
         for (int s = 0; s < 8; ++s)
 #pragma unroll
         for (int f = 0; f < kFR; ++f) {
-            const uint8_t *q0 = p[f][0] + C * kBlockBytes, *q1 = p[f][1] + C * kBlockBytes;
-            const uint32_t h0 = u16(q0 + 34 + 2 * s), h1 = u16(q1 + 34 + 2 * s);
+            const uint32_t h0 = u16(q[f][0] + 34 + 2 * s), h1 = u16(q[f][1] + 34 + 2 * s);
             // index = qs | grid bits 3t..3t+2 of h at bits 8..10; h*256 moves
             // the field next to the byte (a multiply, off the logic pipe).
-            const uint32_t i0 = (((h0 * 256u) >> sh) & 0x700u) | q0[2 + 4 * s + t];
-            const uint32_t i1 = (((h1 * 256u) >> sh) & 0x700u) | q1[2 + 4 * s + t];
-            const uint32_t e0 = lds32(tab + 16 * i0), e1 = lds32(tab + 16 * i1);
+            const uint32_t i0 = (((h0 * 256u) >> sh) & 0x700u) | qt[f][0][4 * s];
+            const uint32_t i1 = (((h1 * 256u) >> sh) & 0x700u) | qt[f][1][4 * s];
+            const uint32_t e0 = lds32_const(tab_s + 16 * i0), e1 = lds32_const(tab_s + 16 * i1);
             // delta sign (bit 15) picks the byte table: P + sign * (M - P).
-            const uint32_t l0 = kLutPlus + (h0 >> 15) * (kLutMinus - kLutPlus);
-            const uint32_t l1 = kLutPlus + (h1 >> 15) * (kLutMinus - kLutPlus);
+            const uint32_t l0 = kLutPlus + (h0 >> 15) * step, l1 = kLutPlus + (h1 >> 15) * step;
             int c[4];
-            mma_s8s8(c, __byte_perm(l0, 0, e0), __byte_perm(l1, 0, e1), __byte_perm(l0, 0, __umulhi(e0, 65536u)),
-                     __byte_perm(l1, 0, __umulhi(e1, 65536u)), b[8 * C + s][0], b[8 * C + s][1]);
-            // 2s+1 from bits 12..14: ((h >> 11) & 14) | 1.
-            const int dl0 = static_cast<int>(((h0 >> 11) & 14u) | 1u), dl1 = static_cast<int>(((h1 >> 11) & 14u) | 1u);
+            // selector bits 16..31 are ignored: e for bytes 0..3, e >> 16 for 4..7
+            mma_s8s8(c, prmt(l0, 0, e0), prmt(l1, 0, e1), prmt(l0, 0, __umulhi(e0, 65536u)),
+                     prmt(l1, 0, __umulhi(e1, 65536u)), b[8 * C + s][0], b[8 * C + s][1]);
+            // 2s+1 from bits 12..14: ((h >> 11) & 14) | 1, one LOP3 with
+            // both constants in registers.
+            const int dl0 = static_cast<int>(and_or(h0 >> 11, k14, k1));
+            const int dl1 = static_cast<int>(and_or(h1 >> 11, k14, k1));
             ai[f][0] += dl0 * c[0];
             ai[f][1] += dl0 * c[1];
             ai[f][2] += dl1 * c[2];
@@ -156,11 +198,12 @@ struct MmaFmt<FmtQ8_0> {
     static constexpr bool kMins = false;
     static constexpr int kFR = 1;
     __device__ static void init_table(uint8_t *, int, int) {}
+    __device__ static const uint8_t *table_for_lane(const uint8_t *table, int) { return table; }
     // Eight 34-byte blocks.  A block at an even index within the slice starts
     // 4-byte aligned (its bytes follow a 2-byte scale), one at an odd index
     // 2 bytes past alignment, so its bytes are.
-    template <int C>
-    __device__ __forceinline__ static void chunk(const uint8_t *const (&p)[kFR][2], int t, const uint32_t (&b)[16][2],
+    template <int C, int NB>
+    __device__ __forceinline__ static void chunk(const uint8_t *const (&p)[kFR][2], int t, const uint32_t (&b)[NB][2],
                                                  float xs, const float *, const uint8_t *, float (&afr)[kFR][4],
                                                  float (&)[kFR][2]) {
         const uint8_t *p0 = p[0][0], *p1 = p[0][1];
@@ -200,13 +243,14 @@ struct MmaFmt<FmtQ4_K> {
     static constexpr bool kMins = true;
     static constexpr int kFR = 1;
     __device__ static void init_table(uint8_t *, int, int) {}
+    __device__ static const uint8_t *table_for_lane(const uint8_t *table, int) { return table; }
     // Byte j of the 6-bit scale (or min) words of a K-quant head, sub-blocks
     // 0..3 in `lo`, 4..7 in `hi` (kernels/packed.vx:107-120 on packed words).
     __device__ __forceinline__ static int sel6(uint32_t lo, uint32_t hi, int j) {
         return static_cast<int>(((j < 4 ? lo : hi) >> (8 * (j & 3))) & 0xffu);
     }
-    template <int C>
-    __device__ __forceinline__ static void chunk(const uint8_t *const (&p)[kFR][2], int t, const uint32_t (&b)[16][2],
+    template <int C, int NB>
+    __device__ __forceinline__ static void chunk(const uint8_t *const (&p)[kFR][2], int t, const uint32_t (&b)[NB][2],
                                                  float xs, const float *sums, const uint8_t *, float (&afr)[kFR][4],
                                                  float (&amr)[kFR][2]) {
         float(&af)[4] = afr[0];
@@ -331,8 +375,6 @@ __global__ void __launch_bounds__(256)
 
 // ----------------------------------------------------------------- kernel ---
 
-constexpr int kSliceSub = 16;  // 32-column sub-blocks per warp column slice (512 columns)
-
 __device__ __forceinline__ MmaJob job_at(const MmaJob &job0, const MmaJob *jobs, int j, int batch, int rows_per_job,
                                          size_t pstride) {
     if (jobs) return jobs[j];
@@ -348,7 +390,8 @@ __device__ __forceinline__ MmaJob job_at(const MmaJob &job0, const MmaJob *jobs,
     return r;
 }
 
-template <class F, int S, int RG>
+// W = 256-column chunks per warp column slice (1 or 2).
+template <class F, int S, int RG, int W>
 __global__ void __launch_bounds__((S * RG + 1) * 32, 1)
     mma_rows_kernel(MmaJob job0, const MmaJob *__restrict__ jobs, const int *njobs_dev, int max_jobs, int batch,
                     int rows_per_job, int cols, int row_bytes, int srow, int stages, int stage_stride,
@@ -436,11 +479,13 @@ __global__ void __launch_bounds__((S * RG + 1) * 32, 1)
 
     const int sw = warp % S, rg = warp / S;
     const int g = lane >> 2, t = lane & 3;
-    const int u0 = sw * kSliceSub;  // first sub-block of the slice
+    const uint8_t *ltab = MF::table_for_lane(table, lane);
+    constexpr int SUB = 8 * W;  // 32-column sub-blocks per slice
+    const int u0 = sw * SUB;    // first sub-block of the slice
     const size_t slice_off = static_cast<size_t>(u0 / MF::kSubPerBlock) * MF::kBlockBytes;
     const size_t scale_off = prep_scale_offset(cols), sums_off = prep_sums_offset(cols);
-    uint32_t b[kSliceSub][2];
-    float xs[2] = {0.0f, 0.0f}, down[2] = {0.0f, 0.0f};
+    uint32_t b[SUB][2];
+    float xs[W] = {}, down[2] = {0.0f, 0.0f};
     const float *sums = nullptr;
     MmaJob J{};
     int loaded = -1;
@@ -481,26 +526,30 @@ __global__ void __launch_bounds__((S * RG + 1) * 32, 1)
             }
             const uint8_t *xb = (g >> 2) ? J.xp[1] : J.xp[0];  // B column g: token g/4, limb g%4
 #pragma unroll
-            for (int u = 0; u < kSliceSub; ++u) {
+            for (int u = 0; u < SUB; ++u) {
                 uint2 v = make_uint2(0u, 0u);
                 if (xb) v = *reinterpret_cast<const uint2 *>(xb + static_cast<size_t>(g & 3) * cols + 32 * (u0 + u) + 8 * t);
                 b[u][0] = v.x;
                 b[u][1] = v.y;
             }
             const uint8_t *xa = (t >> 1) ? J.xp[1] : J.xp[0];  // accumulator columns 2t, 2t+1: token t/2
-            // Chunk c holds x*2^E_c.  Relative to Eref = min(E_0, E_1) (the
-            // chunk of larger magnitude) its scale is 2^(Eref - E_c) <= 1;
-            // the absolute 2^-Eref is applied once per tile in two exact steps.
-            // A chunk more than 2^126 below the other contributes nothing.
-            int e0 = 0, e1 = 0;
-            if (xa) {
-                e0 = reinterpret_cast<const int *>(xa + scale_off)[u0 / 8];
-                e1 = reinterpret_cast<const int *>(xa + scale_off)[u0 / 8 + 1];
+            // Chunk c holds x*2^E_c.  Relative to Eref = min over the slice's
+            // chunks (the one of largest magnitude) its scale is 2^(Eref - E_c)
+            // <= 1; the absolute 2^-Eref is applied once per tile in two exact
+            // steps.  A chunk more than 2^126 below another contributes nothing.
+            int e[W];
+            bool bad = false;
+#pragma unroll
+            for (int c = 0; c < W; ++c) {
+                e[c] = xa ? reinterpret_cast<const int *>(xa + scale_off)[u0 / 8 + c] : 0;
+                bad |= e[c] == kPrepNonFinite;
             }
-            const bool bad = e0 == kPrepNonFinite || e1 == kPrepNonFinite;
-            const int eref = bad ? 0 : min(e0, e1);
-            xs[0] = (xa && !bad && eref - e0 >= -126) ? pow2(eref - e0) : 0.0f;
-            xs[1] = (xa && !bad && eref - e1 >= -126) ? pow2(eref - e1) : 0.0f;
+            int eref = e[0];
+#pragma unroll
+            for (int c = 1; c < W; ++c) eref = min(eref, e[c]);
+            if (bad) eref = 0;
+#pragma unroll
+            for (int c = 0; c < W; ++c) xs[c] = (xa && !bad && eref - e[c] >= -126) ? pow2(eref - e[c]) : 0.0f;
             down[0] = bad ? __int_as_float(0x7fc00000) : pow2(-(eref / 2));
             down[1] = pow2(-(eref - eref / 2));
             sums = (MF::kMins && xa) ? reinterpret_cast<const float *>(xa + sums_off) + u0 : nullptr;
@@ -522,8 +571,8 @@ __global__ void __launch_bounds__((S * RG + 1) * 32, 1)
                           slice_off;
                 p[f][1] = p[f][0] + 8 * static_cast<size_t>(srow);
             }
-            MF::template chunk<0>(p, t, b, xs[0], sums, table, af, am);
-            MF::template chunk<1>(p, t, b, xs[1], sums, table, af, am);
+            MF::template chunk<0>(p, t, b, xs[0], sums, ltab, af, am);
+            if constexpr (W == 2) MF::template chunk<1>(p, t, b, xs[W - 1], sums, ltab, af, am);
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[s]);
         }
@@ -565,26 +614,47 @@ __global__ void __launch_bounds__((S * RG + 1) * 32, 1)
 // ------------------------------------------------------------------- host ---
 
 struct MmaPlan {
-    int S = 0, RG = 0, srow = 0, stages = 0, stage_stride = 0, grid = 0;
+    int S = 0, RG = 0, W = 0, srow = 0, stages = 0, stage_stride = 0, grid = 0;
     size_t smem = 0;
 };
 
-constexpr size_t kMmaSmemBudget = 220 * 1024;
+// Below the 227 KB opt-in limit of dynamic shared memory per block.
+constexpr size_t kMmaSmemBudget = 226 * 1024;
 
-// Row groups per CTA for S column slices: about twelve consumer warps.
-constexpr int mma_row_groups(int S) { return S >= 12 ? 1 : 12 / S; }
+// Row groups per CTA for S column slices of W chunks: about twelve consumer
+// warps with 512-column slices, twenty-four with 256-column ones (half the
+// B fragments per warp leave room for twice the warps).
+constexpr int mma_row_groups(int S, int W) {
+    return W == 2 ? (S >= 12 ? 1 : 12 / S) : (S >= 24 ? 1 : 24 / S);
+}
 
-constexpr bool mma_slices_ok(int S) {
-    return S == 1 || S == 2 || S == 3 || S == 4 || S == 6 || S == 8 || S == 12 || S == 16;
+constexpr bool mma_slices_ok(int S, int W) {
+    if (W == 2) return S == 1 || S == 2 || S == 3 || S == 4 || S == 6 || S == 8 || S == 12 || S == 16;
+    return S == 8 || S == 12 || S == 24;
+}
+
+// 256-column slices (W = 1) are built only with GLMVX_MMA_NARROW set (1:
+// IQ1_S, 2: every format); measured slower than 512-column slices with half
+// the warps for the IQ1_S decode on B200, so off by default.
+#ifndef GLMVX_MMA_NARROW
+#define GLMVX_MMA_NARROW 0
+#endif
+template <class F>
+static int mma_slice_chunks(int cols) {
+    const bool narrow = GLMVX_MMA_NARROW == 2 || (GLMVX_MMA_NARROW == 1 && std::is_same_v<F, FmtIQ1_S>);
+    if (narrow && cols % 256 == 0 && mma_slices_ok(cols / 256, 1)) return 1;
+    return 2;
 }
 
 template <class F>
 static bool plan_mma(int64_t max_rows, int64_t max_tiles_extra, int cols, int row_bytes, bool fused, MmaPlan &p) {
     using MF = MmaFmt<F>;
-    if (cols % 512 || row_bytes % 16) return false;
-    p.S = cols / 512;
-    if (!mma_slices_ok(p.S)) return false;
-    p.RG = mma_row_groups(p.S);
+    if (cols % 256 || row_bytes % 16) return false;
+    p.W = mma_slice_chunks<F>(cols);
+    if (cols % (256 * p.W)) return false;
+    p.S = cols / (256 * p.W);
+    if (!mma_slices_ok(p.S, p.W)) return false;
+    p.RG = mma_row_groups(p.S, p.W);
     const int R = 16 * MF::kFR * p.RG;
     // Shared-memory rows span an odd number of 16-byte units, so rows g = 0..7
     // of a fragment start in 8 different 4-bank groups.  Rows that already do
@@ -607,12 +677,12 @@ static bool plan_mma(int64_t max_rows, int64_t max_tiles_extra, int cols, int ro
     return true;
 }
 
-template <class F, int S>
+template <class F, int S, int W>
 static int32_t launch_mma(const MmaPlan &p, const MmaJob &job0, const MmaJob *jobs, const int *njobs_dev,
                           int max_jobs, int batch, int rows_per_job, int cols, int row_bytes, const float *x_raw,
                           cudaStream_t stream) {
-    constexpr int RG = mma_row_groups(S);
-    auto kern = mma_rows_kernel<F, S, RG>;
+    constexpr int RG = mma_row_groups(S, W);
+    auto kern = mma_rows_kernel<F, S, RG, W>;
     static size_t configured = 0;  // per instantiation
     if (p.smem > configured) {
         GLMVX_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(p.smem)));
@@ -637,19 +707,24 @@ template <class F>
 static int32_t launch_mma_s(const MmaPlan &p, const MmaJob &job0, const MmaJob *jobs, const int *njobs_dev,
                             int max_jobs, int batch, int rows_per_job, int cols, int row_bytes, const float *x_raw,
                             cudaStream_t stream) {
-#define GLMVX_MMA_CASE(s)                                                                                       \
-    case s:                                                                                                    \
-        return launch_mma<F, s>(p, job0, jobs, njobs_dev, max_jobs, batch, rows_per_job, cols, row_bytes, x_raw, \
-                                stream);
-    switch (p.S) {
-        GLMVX_MMA_CASE(1)
-        GLMVX_MMA_CASE(2)
-        GLMVX_MMA_CASE(3)
-        GLMVX_MMA_CASE(4)
-        GLMVX_MMA_CASE(6)
-        GLMVX_MMA_CASE(8)
-        GLMVX_MMA_CASE(12)
-        GLMVX_MMA_CASE(16)
+#define GLMVX_MMA_CASE(s, w)                                                                                 \
+    case 2 * (s) + (w) - 1:                                                                                 \
+        return launch_mma<F, s, w>(p, job0, jobs, njobs_dev, max_jobs, batch, rows_per_job, cols, row_bytes, \
+                                   x_raw, stream);
+    switch (2 * p.S + p.W - 1) {
+        GLMVX_MMA_CASE(1, 2)
+        GLMVX_MMA_CASE(2, 2)
+        GLMVX_MMA_CASE(3, 2)
+        GLMVX_MMA_CASE(4, 2)
+        GLMVX_MMA_CASE(6, 2)
+        GLMVX_MMA_CASE(8, 2)
+        GLMVX_MMA_CASE(12, 2)
+        GLMVX_MMA_CASE(16, 2)
+#if GLMVX_MMA_NARROW
+        GLMVX_MMA_CASE(8, 1)
+        GLMVX_MMA_CASE(12, 1)
+        GLMVX_MMA_CASE(24, 1)
+#endif
     default: set_error("mma: unsupported column count"); return kUnsupported;
     }
 #undef GLMVX_MMA_CASE
@@ -658,7 +733,7 @@ static int32_t launch_mma_s(const MmaPlan &p, const MmaJob &job0, const MmaJob *
 // Rows must be whole 16-byte units for the per-row bulk copies: always for
 // Q8_0 (cols % 256) and Q4_K, for IQ1_S when cols % 2048 == 0.
 bool mma_supported(int kind, int cols) {
-    if (cols <= 0 || cols % 512 || !mma_slices_ok(cols / 512)) return false;
+    if (cols <= 0 || cols % 512 || !mma_slices_ok(cols / 512, 2)) return false;
     return kind == 8 || kind == 12 || (kind == 19 && cols % 2048 == 0);
 }
 
