@@ -111,6 +111,11 @@ __device__ __forceinline__ uint32_t lds32_const(uint32_t addr) {
     return v;
 }
 
+// 2^(12-3t): (qh & 7 << 3t) * c_iq1s_hi_mul[t] = 4096 * (grid bits of group
+// t), the codebook offset of those bits, as one multiply-add.  Read from the
+// constant bank so the compiler keeps the multiply-add instead of a shift.
+__constant__ uint32_t c_iq1s_hi_mul[4] = {4096u, 512u, 64u, 8u};
+
 template <>
 struct MmaFmt<FmtIQ1_S> {
     // Codebook as 8 nibbles g+1 (0..2) per entry, four interleaved copies:
@@ -143,6 +148,7 @@ struct MmaFmt<FmtIQ1_S> {
                                                  float xs, const float *, const uint8_t *tab, float (&af)[kFR][4],
                                                  float (&)[kFR][2]) {
         const int sh = 3 * t;
+        const uint32_t hmask = 7u << sh, hmul = c_iq1s_hi_mul[t];
         constexpr uint32_t step = kLutMinus - kLutPlus;
         const uint32_t k14 = 14u, k1 = 1u;
         const uint32_t tab_s = smem_addr(tab);
@@ -160,11 +166,11 @@ struct MmaFmt<FmtIQ1_S> {
 #pragma unroll
         for (int f = 0; f < kFR; ++f) {
             const uint32_t h0 = u16(q[f][0] + 34 + 2 * s), h1 = u16(q[f][1] + 34 + 2 * s);
-            // index = qs | grid bits 3t..3t+2 of h at bits 8..10; h*256 moves
-            // the field next to the byte (a multiply, off the logic pipe).
-            const uint32_t i0 = (((h0 * 256u) >> sh) & 0x700u) | qt[f][0][4 * s];
-            const uint32_t i1 = (((h1 * 256u) >> sh) & 0x700u) | qt[f][1][4 * s];
-            const uint32_t e0 = lds32_const(tab_s + 16 * i0), e1 = lds32_const(tab_s + 16 * i1);
+            // entry (grid bits 3t..3t+2 of h, qs) at 4096*bits + 16*qs: index
+            // 256*bits + qs, the grid bits taken in place and scaled by a
+            // multiply-add rather than shifted into position
+            const uint32_t e0 = lds32_const((h0 & hmask) * hmul + (qt[f][0][4 * s] * 16u + tab_s));
+            const uint32_t e1 = lds32_const((h1 & hmask) * hmul + (qt[f][1][4 * s] * 16u + tab_s));
             // delta sign (bit 15) picks the byte table: P + sign * (M - P).
             const uint32_t l0 = kLutPlus + (h0 >> 15) * step, l1 = kLutPlus + (h1 >> 15) * step;
             int c[4];
