@@ -60,4 +60,15 @@ int32_t prep_rows_device(uint8_t *prep, const float *x, const float *x2, int row
 int32_t mma_gemv_device(int32_t kind, const MmaJob &job0, const MmaJob *jobs, const int *njobs_dev, int max_jobs,
                         int batch, int rows_per_job, int cols, cudaStream_t stream, const float *x_raw = nullptr);
 
+// f16 tensor-core GEMM for token batches (packed_gemm.cu): the weights are
+// decoded once per fragment for every token.  Q4_K, and IQ1_S with cols %
+// 2048 == 0; cols % 256 == 0; kGemmMinTokens..kGemmMaxTokens tokens; 16-byte
+// aligned w, x and scratch (gemm_f16_scratch_bytes).  kUnsupported when no
+// launch plan fits the shape.
+constexpr int kGemmMinTokens = 8, kGemmMaxTokens = 64;
+bool gemm_f16_supported(int kind, int cols, int batch);
+size_t gemm_f16_scratch_bytes(int cols, int batch);
+int32_t gemm_f16_device(int32_t kind, float *out, const uint8_t *w, const float *x, int rows, int cols, int batch,
+                        uint8_t *scratch, cudaStream_t stream);
+
 }  // namespace glmvx

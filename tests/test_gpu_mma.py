@@ -38,6 +38,15 @@ def _gemm(cuda_lib, kind, raw, rows, cols, x):
             b.close()
 
 
+PATH_GEMM = 6
+
+
+def _batch_path(kind, cols, batch):
+    """Tensor-core path taken for an aligned matrix: the f16 GEMM for 8..64
+    tokens of Q4_K and IQ1_S, the int8 GEMV kernel otherwise."""
+    return PATH_GEMM if kind in (12, 19) and 8 <= batch <= 64 and cols % 256 == 0 else PATH_MMA
+
+
 def _want(oracle, raw, kind, rows, cols, x):
     if x.shape[0] == 1:
         return oracle.packed_matvec(raw, kind, (rows, cols), x[0])[None]
@@ -54,8 +63,12 @@ def test_mma_matches_oracle(cuda_lib, oracle, kind, rows, cols, batch):
     x = np.random.default_rng(batch * 7 + cols).normal(size=(batch, cols)).astype(np.float32)
     got, path = _gemm(cuda_lib, kind, raw, rows, cols, x)
     # IQ1_S rows are whole 16-byte units only when cols % 2048 == 0; other
-    # widths keep the CUDA-core kernels.
-    assert (path == PATH_MMA) == (kind != 19 or cols % 2048 == 0)
+    # widths keep the CUDA-core kernels.  Eight or more tokens of Q4_K and
+    # IQ1_S take the f16 GEMM (test_gpu_gemm.py).
+    if kind != 19 or cols % 2048 == 0:
+        assert path == _batch_path(kind, cols, batch)
+    else:
+        assert path not in (PATH_MMA, PATH_GEMM)
     dec = unpack_for_validation(oracle.lib, raw, kind, (rows, cols))
     want = _want(oracle, raw, kind, rows, cols, x)
     for t in range(batch):
@@ -70,7 +83,7 @@ def test_mma_batches(cuda_lib, oracle, kind, batch):
     raw = payload(kind, blocks=rows * cols // block, seed=batch)
     x = np.random.default_rng(batch).normal(size=(batch, cols)).astype(np.float32)
     got, path = _gemm(cuda_lib, kind, raw, rows, cols, x)
-    assert path == PATH_MMA
+    assert path == _batch_path(kind, cols, batch)
     dec = unpack_for_validation(oracle.lib, raw, kind, (rows, cols))
     want = _want(oracle, raw, kind, rows, cols, x)
     for t in range(batch):
