@@ -324,9 +324,17 @@ def graph_time(rt, stream, fn, reps, ranks=None, clocks=None):
     return ms
 
 
+PATH_NAMES = {1: 'stream', 2: 'generic', 5: 'mma_int8', 6: 'gemm_f16'}
+
+
 def fused_gemv_sweep(rt, lib, dev, stream, steps, peak):
-    """Configs 0 and 1: GB/s of the fused dequant-GEMV/GEMM per launch."""
+    """Configs 0 and 1: GB/s of the fused dequant-GEMV/GEMM per launch; for
+    token batches on the f16 GEMM also the tensor-core rate (two limbs)."""
     res = {}
+    try:
+        bf16_peak = float(json.loads((ROOT / 'MEASURED_PEAKS.json').read_text())['bf16_tflops'])
+    except (OSError, KeyError, ValueError):
+        bf16_peak = 1590.0
     rng = np.random.default_rng(0)
     for name, kind, rows, cols, blk, size, batches in (('config0_q8_0_2048x6144', 8, 2048, 6144, 32, 34, (1,)),
                                                        ('config1_q4_k_6144x2048', 12, 6144, 2048, 256, 144,
@@ -354,8 +362,17 @@ def fused_gemv_sweep(rt, lib, dev, stream, steps, peak):
             for i in range(3):
                 launch(i)
             us = graph_time(rt, stream, launch, reps) / reps * 1e3
+            path = C.c_int32(-1)
+            rt.check(lib, lib.glmvx_packed_gemm_path(kind, od.ptr, wbuf.ptr, xd.ptr, rows, cols, b, stream.handle,
+                                                     C.byref(path)), 'glmvx_packed_gemm_path')
+            stream.synchronize()
             alg = wbytes + x.nbytes + 4 * b * rows
-            res[f'{name}_b{b}'] = {'us': us, 'gbs': alg / us / 1e3, 'frac_of_measured_hbm': alg / us / 1e3 / peak}
+            line = {'us': us, 'gbs': alg / us / 1e3, 'frac_of_measured_hbm': alg / us / 1e3 / peak,
+                    'path': PATH_NAMES.get(path.value, str(path.value)), 'gflops': 2 * rows * cols * b / us / 1e3}
+            if path.value == 6:  # f16 tensor-core GEMM: two f16 limbs per activation
+                tf = 2 * 2 * rows * cols * b / us / 1e6
+                line.update({'tensor_tflops': tf, 'frac_of_measured_bf16': tf / bf16_peak})
+            res[f'{name}_b{b}'] = line
             xd.close()
             od.close()
         wbuf.close()
@@ -529,7 +546,7 @@ def run_ours(args, ranks):
         'e2e': {'value': e2e_value, 'unit': 'tok/s', 'steps': e2e_steps,
                 'h2d_bytes_per_step': TOKENS * HIDDEN * 4, 'd2h_bytes_per_step': TOKENS * HIDDEN * 4 + 2 * TOKENS * TOPK * 4,
                 'api': 'gpu.moe.MoELayer.forward (host rows in, host rows + routing out)'},
-        'gpu_launches': 6 * args.steps,
+        'gpu_launches': 8 * args.steps,  # prep x, router logits, top-k, grouping, gate+up, prep h, down, combine
         'clocks': clocks.summary(),
     }
     if ranks.rank == 0 and ranks.world == 1 and not args.no_cpu_baseline:
