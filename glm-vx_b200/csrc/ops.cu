@@ -108,6 +108,10 @@ __global__ void __launch_bounds__(256)
 #pragma unroll
         for (int t = 0; t < TB; ++t) acc[e][t] = 0.0f;
     const int quads = cols >> 2;
+    // token tiles: two iterations' loads in flight per thread (the grid is
+    // one or two CTAs per SM, so memory latency is hidden within the thread)
+    constexpr int kUnroll = TB > 1 ? 2 : 1;
+#pragma unroll kUnroll
     for (int f = lane + 32 * warp; f < quads; f += 256) {
         float4 wv[EB], xv[TB];
 #pragma unroll
@@ -151,16 +155,17 @@ int32_t f32_rows(float *out, const float *w, const float *x, int rows, int cols,
                  cudaStream_t s) {
     if (rows == 0 || batch == 0) return kOk;
     const bool vec = ((reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(x)) & 15) == 0 && (cols & 3) == 0;
+    // Tiles of EB rows x TB tokens, sized so a 256-row router gives 128-256 CTAs.
     if (vec && batch <= 1) {
         f32_tile_kernel<2, 1><<<dim3((rows + 1) / 2, 1), 256, 0, s>>>(out, w, x, rows, cols, batch, token_major);
         return launch_status("f32_tile_kernel");
     }
     if (vec && batch <= 8) {
-        f32_tile_kernel<4, 8><<<dim3((rows + 3) / 4, 1), 256, 0, s>>>(out, w, x, rows, cols, batch, token_major);
+        f32_tile_kernel<2, 8><<<dim3((rows + 1) / 2, 1), 256, 0, s>>>(out, w, x, rows, cols, batch, token_major);
         return launch_status("f32_tile_kernel");
     }
     if (vec) {
-        f32_tile_kernel<8, 8><<<dim3((rows + 7) / 8, (batch + 7) / 8), 256, 0, s>>>(out, w, x, rows, cols, batch,
+        f32_tile_kernel<4, 8><<<dim3((rows + 3) / 4, (batch + 7) / 8), 256, 0, s>>>(out, w, x, rows, cols, batch,
                                                                                   token_major);
         return launch_status("f32_tile_kernel");
     }

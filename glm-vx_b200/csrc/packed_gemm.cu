@@ -474,13 +474,15 @@ struct GemmPlan {
 constexpr size_t kGemmSmemBudget = 226 * 1024;
 constexpr int kGemmMaxWarps = 12;
 
+// Plan for NTW 8-column tiles (4*NTW tokens) per warp; false if nothing fits.
 template <class F>
-bool plan_gemm(int rows, int cols, int batch, int row_bytes, GemmPlan &p) {
+bool plan_gemm_ntw(int ntw, int rows, int cols, int batch, int row_bytes, GemmPlan &p) {
     using GF = GemmFmt<F>;
     const int nt8 = (batch + 3) / 4;
-    p.ntw = nt8 > 4 ? 8 : (nt8 > 2 ? 4 : 2);
-    p.nt8 = (nt8 + p.ntw - 1) / p.ntw * p.ntw;
-    p.TG = p.nt8 / p.ntw;
+    p.ntw = ntw;
+    p.nt8 = (nt8 + ntw - 1) / ntw * ntw;
+    p.TG = p.nt8 / ntw;
+    if (p.TG > kGemmMaxWarps) return false;
     p.grid = std::max(1, std::min(sm_count(), (rows + 15) / 16));
     const int per_cta = (rows + p.grid - 1) / p.grid;
     p.srow = ((row_bytes >> 4) & 1) ? row_bytes : row_bytes + 16;
@@ -503,6 +505,22 @@ bool plan_gemm(int rows, int cols, int batch, int row_bytes, GemmPlan &p) {
         }
     }
     return false;
+}
+
+// The tile width that gives the most consumer warps (latency hiding for the
+// dependent tensor-core steps), the wider one on a tie (fewer decodes).
+template <class F>
+bool plan_gemm(int rows, int cols, int batch, int row_bytes, GemmPlan &p) {
+    const int nt8 = (batch + 3) / 4;
+    bool found = false;
+    for (int ntw = 8; ntw >= 2; ntw /= 2) {
+        if (ntw > 2 && ntw / 2 >= nt8) continue;  // a narrower tile covers the batch
+        GemmPlan c;
+        if (!plan_gemm_ntw<F>(ntw, rows, cols, batch, row_bytes, c)) continue;
+        if (!found || c.RG * c.TG * c.S > p.RG * p.TG * p.S) p = c;
+        found = true;
+    }
+    return found;
 }
 
 template <class F, int NTW>
@@ -583,10 +601,9 @@ int32_t gemm_f16_device(int32_t kind, float *out, const uint8_t *w, const float 
     return st;
 }
 
+// Enough for any tile width the planner picks (tokens padded to 32).
 size_t gemm_f16_scratch_bytes(int cols, int batch) {
-    const int nt8 = (batch + 3) / 4;
-    const int ntw = nt8 > 4 ? 8 : (nt8 > 2 ? 4 : 2);
-    const GemmRecord rec{(nt8 + ntw - 1) / ntw * ntw};
+    const GemmRecord rec{((batch + 3) / 4 + 7) / 8 * 8};
     return rec.bytes() * static_cast<size_t>(cols / 256);
 }
 

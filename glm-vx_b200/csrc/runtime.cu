@@ -234,6 +234,20 @@ GLMVX_EXPORT int32_t glmvx_graph_destroy(void *graph_exec) {
 
 // Reads and clears the current device's kernel error word.  *code is 0 when
 // no kernel reported a timeout; otherwise the first DeviceError recorded.
+// Device address of that word, so a caller can copy it back together with a
+// step's outputs (one transfer, one synchronisation) and call
+// glmvx_check_device_error only when it is nonzero.
+GLMVX_EXPORT int32_t glmvx_device_error_address(void **ptr) {
+    if (!ptr) {
+        set_error("device_error_address: null output pointer");
+        return kInvalid;
+    }
+    int *word = device_error_word();
+    if (!word) return cuda_fail(cudaGetLastError(), "cudaGetSymbolAddress(g_device_error)");
+    *ptr = word;
+    return kOk;
+}
+
 GLMVX_EXPORT int32_t glmvx_check_device_error(int32_t *code) {
     int *word = device_error_word();
     if (!word) return cuda_fail(cudaGetLastError(), "cudaGetSymbolAddress(g_device_error)");

@@ -143,6 +143,25 @@ class GPUBackend:
                 C.memmove(a.ctypes.data, self._host.ptr + o, a.nbytes)
         return arrays
 
+    def _fetch_checked(self, out_offsets, arrays, error_offset):
+        """_fetch plus the device error word, copied back in the same stream
+        pass into the arena at `error_offset` (reserved by _stage): one
+        synchronisation for outputs and error state; raises if a kernel
+        reported an expired bounded wait."""
+        if out_offsets:
+            lo = out_offsets[0]
+            hi = out_offsets[-1] + arrays[-1].nbytes
+            if hi > lo:
+                rt.call('glmvx_memcpy_dtoh', self._host.ptr + lo, self._dev.ptr + lo, hi - lo, self.stream.handle)
+        rt.call('glmvx_memcpy_dtoh', self._host.ptr + error_offset, self.device.error_address(), 4, self.stream.handle)
+        self.stream.synchronize()
+        for o, a in zip(out_offsets, arrays):
+            if a.nbytes:
+                C.memmove(a.ctypes.data, self._host.ptr + o, a.nbytes)
+        if C.c_int32.from_address(self._host.ptr + error_offset).value:
+            self.device.check_device_error()
+        return arrays
+
     # ----------------------------------------------------------- weights
     def resident(self, raw, kind, shape):
         """Upload a packed matrix once; the handle replaces `raw` in calls."""

@@ -66,8 +66,11 @@ class MoELayer:
         self._ws, self._ws_bytes, self._io = None, 0, None
 
     def workspace_bytes(self, tokens):
-        return int(self.backend.lib.glmvx_moe_workspace_bytes(tokens, self.hidden, self.inter, self.experts,
-                                                               self.top_k, int(self.shared[0] is not None)))
+        cache = self.__dict__.setdefault('_ws_need', {})
+        if tokens not in cache:
+            cache[tokens] = int(self.backend.lib.glmvx_moe_workspace_bytes(
+                tokens, self.hidden, self.inter, self.experts, self.top_k, int(self.shared[0] is not None)))
+        return cache[tokens]
 
     def _workspace(self, tokens):
         need = self.workspace_bytes(tokens)
@@ -101,10 +104,9 @@ class MoELayer:
         wts = np.empty((T, self.top_k), np.float32)
         if T == 0:
             return y, ids, wts
-        (xd,), (yd, idd, wd), offs = b._stage([x], [y.nbytes, ids.nbytes, wts.nbytes])
+        (xd,), (yd, idd, wd, _), offs = b._stage([x], [y.nbytes, ids.nbytes, wts.nbytes, 4])
         self.forward_device(yd, xd, T, idd, wd)
-        b._fetch(offs, [y, ids, wts])
-        b.device.check_device_error()
+        b._fetch_checked(offs[:3], [y, ids, wts], offs[3])
         if not np.isfinite(y).all():
             raise ValueError('nonfinite MoE output')
         return y, ids, wts

@@ -59,6 +59,7 @@ SIGNATURES = {
     'glmvx_graph_launch': ([_P, _P], _I32),
     'glmvx_graph_destroy': ([_P], _I32),
     'glmvx_check_device_error': ([_PI32], _I32),
+    'glmvx_device_error_address': ([C.POINTER(_P)], _I32),
     'glmvx_packed_gemv': ([_I32, _P, _P, _P, _I32, _I32, _P], _I32),
     'glmvx_packed_gemm': ([_I32, _P, _P, _P, _I32, _I32, _I32, _P], _I32),
     'glmvx_packed_gemm_path': ([_I32, _P, _P, _P, _I32, _I32, _I32, _P, _PI32], _I32),
@@ -164,6 +165,15 @@ class Device:
 
     def synchronize(self):
         call('glmvx_device_synchronize')
+
+    def error_address(self):
+        """Device address of the bounded-wait error word (copy it back with a
+        step's outputs; nonzero means call check_device_error)."""
+        if getattr(self, '_error_address', None) is None:
+            p = C.c_void_p()
+            call('glmvx_device_error_address', C.byref(p))
+            self._error_address = p.value
+        return self._error_address
 
     def check_device_error(self):
         """Raise if a kernel reported an expired bounded wait since the last check."""

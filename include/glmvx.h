@@ -123,6 +123,9 @@ int32_t glmvx_graph_launch(void *graph_exec, void *stream);
 int32_t glmvx_graph_destroy(void *graph_exec);
 /* Reads and clears the device word kernels set when a bounded wait expires. */
 int32_t glmvx_check_device_error(int32_t *code);
+/* Device address of that word (4 bytes), for an asynchronous copy back with a
+   step's outputs; nonzero means call glmvx_check_device_error. */
+int32_t glmvx_device_error_address(void **ptr);
 
 /* Fused packed dequant + matvec: out[rows] = W[rows,cols] . x[cols].
  * Replaces glm_vx_packed_<kind> (kernels/packed.vx:154-470) for resident
