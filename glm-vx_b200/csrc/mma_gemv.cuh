@@ -32,15 +32,19 @@ __host__ __device__ inline size_t prep_stride(int K) {
     return (prep_sums_offset(K) + 4ull * (K / 32) + 255) & ~static_cast<size_t>(255);
 }
 
-// One weight matrix applied to up to two prepared activation rows.
+// One weight matrix applied to up to four prepared activation rows (two
+// with pairs = 1, the slots 0 and 1).
+constexpr int kMmaSlots = 4;
 struct MmaJob {
-    const uint8_t *w;      // packed rows [rows_per_job][row_bytes], 16-byte aligned
-    const uint8_t *xp[2];  // prepared rows; nullptr marks an unused slot
-    float *out[2];         // out[s][r] for r < rows_per_job
+    const uint8_t *w;              // packed rows [rows_per_job][row_bytes], 16-byte aligned
+    const uint8_t *xp[kMmaSlots];  // prepared rows; nullptr marks an unused slot
+    float *out[kMmaSlots];         // out[s][r] for r < rows_per_job
 };
 
 // True when `kind` and the column count take the tensor-core path.
 bool mma_supported(int kind, int cols);
+// True when job lists of four tokens per job (pairs = 2) are built for it.
+bool mma_quad_supported(int kind, int cols);
 
 // Prepare `rows` activation rows x[r][0..cols) (x2 set: SwiGLU(x, x2) =
 // x*sigmoid(x)*x2 per element) into prep + r*prep_stride(cols).
@@ -50,6 +54,8 @@ int32_t prep_rows_device(uint8_t *prep, const float *x, const float *x2, int row
 //  * jobs != nullptr: device-resident descriptors; the job count is
 //    *njobs_dev when njobs_dev is set (read on the device after the previous
 //    kernel completes, clamped to max_jobs), else max_jobs.
+//  * pairs = 2 (job lists only, mma_quad_supported): each decoded weight
+//    fragment is multiplied into two token pairs, the job's slots 0-1 and 2-3.
 //  * jobs == nullptr: `batch` tokens against one matrix: job j applies job0.w
 //    to prepared rows 2j and 2j+1 of job0.xp[0] (stride prep_stride(cols))
 //    and writes rows of job0.out[0] (stride rows_per_job floats).  With
@@ -58,7 +64,8 @@ int32_t prep_rows_device(uint8_t *prep, const float *x, const float *x2, int row
 //    separate preparation or scratch is needed; returns kUnsupported when the
 //    shape leaves no room for that (use the prepared-row form then).
 int32_t mma_gemv_device(int32_t kind, const MmaJob &job0, const MmaJob *jobs, const int *njobs_dev, int max_jobs,
-                        int batch, int rows_per_job, int cols, cudaStream_t stream, const float *x_raw = nullptr);
+                        int batch, int rows_per_job, int cols, cudaStream_t stream, const float *x_raw = nullptr,
+                        int pairs = 1);
 
 // f16 tensor-core GEMM for token batches (packed_gemm.cu): the weights are
 // decoded once per fragment for every token.  Q4_K, and IQ1_S with cols %

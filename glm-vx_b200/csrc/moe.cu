@@ -23,7 +23,10 @@
 // token rows are prepared once (limbs) before step 1, the SwiGLU of each
 // pair's gate/up outputs is prepared after step 4, and each job applies one
 // expert matrix to TWO tokens routed to it, so an expert's weights are
-// decoded once per pair of its tokens.  Other formats run one streaming GEMV
+// decoded once per pair of its tokens; from 16 tokens per call, IQ1_S experts
+// routed three or more tokens and the shared expert go to a second job list
+// of FOUR tokens per job (its own launch of the same kernel with two token
+// pairs per decoded fragment).  Other formats run one streaming GEMV
 // job per pair (packed_gemv.cu) with SwiGLU fused into the activation load.
 // Jobs are ordered by expert so tokens sharing an expert stream its rows
 // close together in time (L2 reuse).
@@ -44,8 +47,9 @@ struct MoeWorkspace {
     float *combw;
     float *g_out, *u_out, *pair_out;
     uint8_t *xprep, *hprep;      // prepared token rows / SwiGLU inputs (tensor-core path)
-    MmaJob *gu_mjobs, *dn_mjobs;
-    int *counts;                 // [gate+up jobs, down jobs], written by the grouping kernel
+    MmaJob *gu_mjobs, *dn_mjobs;  // two tokens per job
+    MmaJob *gu_qjobs, *dn_qjobs;  // four tokens per job (experts with three or more)
+    int *counts;                  // [gate+up, down] jobs of each list, written by the grouping kernel
     size_t bytes;
 };
 
@@ -72,12 +76,14 @@ static MoeWorkspace carve(char *base, int T, int hidden, int inter, int E, int k
     w.hprep = reinterpret_cast<uint8_t *>(take(P * prep_stride(inter)));
     w.gu_mjobs = reinterpret_cast<MmaJob *>(take(sizeof(MmaJob) * 2 * P));
     w.dn_mjobs = reinterpret_cast<MmaJob *>(take(sizeof(MmaJob) * P));
-    w.counts = reinterpret_cast<int *>(take(2 * sizeof(int)));
+    w.gu_qjobs = reinterpret_cast<MmaJob *>(take(sizeof(MmaJob) * 2 * P));
+    w.dn_qjobs = reinterpret_cast<MmaJob *>(take(sizeof(MmaJob) * P));
+    w.counts = reinterpret_cast<int *>(take(4 * sizeof(int)));
     w.bytes = off;
     return w;
 }
 
-constexpr int kGroupThreads = 512, kMaxAssignments = 4096;
+constexpr int kGroupThreads = 512, kMaxAssignments = 4096, kQuadMinTokens = 16;
 
 // Inclusive prefix sum of v[0..n) in place (n <= kMaxAssignments), whole CTA.
 __device__ void block_inclusive_scan(int16_t *v, int n, int32_t *s_warp) {
@@ -108,39 +114,49 @@ __device__ void block_inclusive_scan(int16_t *v, int n, int32_t *s_warp) {
 // pair index, so pairs of one expert are contiguous and ordered by token.
 // With mjobs set (tensor-core path), consecutive pairs of one expert share a
 // job: the pair whose index within its expert's run is even opens a job,
-// the next one (if any) takes the job's second slot.
+// the next one (if any) takes the job's second slot.  With qjobs set too,
+// experts routed three or more pairs (and the shared expert, from three
+// tokens) go to the second list instead, four consecutive pairs per job
+// (slots 0..3), so their weights are decoded once per four tokens.
 __global__ void __launch_bounds__(kGroupThreads)
     moe_group_kernel(const int32_t *ids, const float *wts, int T, int k, int E, int shared, const uint8_t *gate,
                      const uint8_t *up, const uint8_t *down, size_t gu_stride, size_t dn_stride, const uint8_t *sgate,
                      const uint8_t *sup, const uint8_t *sdown, const float *x, int hidden, int inter, float *g_out,
                      float *u_out, float *pair_out, GemvJob *gu_jobs, GemvJob *dn_jobs, int32_t *comb, float *combw,
-                     int *bad, MmaJob *gu_m, MmaJob *dn_m, int *counts, const uint8_t *xprep, size_t xstride,
-                     const uint8_t *hprep, size_t hstride) {
-    __shared__ int32_t s_ids[kMaxAssignments];
-    __shared__ int32_t s_pair[kMaxAssignments];
-    __shared__ int16_t s_job[kMaxAssignments];  // per rank: opens a job (0/1), then the job id
+                     int *bad, MmaJob *gu_m, MmaJob *dn_m, MmaJob *gu_q, MmaJob *dn_q, int *counts,
+                     const uint8_t *xprep, size_t xstride, const uint8_t *hprep, size_t hstride) {
+    __shared__ int16_t s_ids[kMaxAssignments];   // expert ids (< 32768, checked by the host)
+    __shared__ int16_t s_pair[kMaxAssignments];  // rank of each assignment
+    __shared__ int16_t s_job[kMaxAssignments];   // per rank: opens a two-token job (0/1), then the job id + 1
+    __shared__ int16_t s_jobq[kMaxAssignments];  // per rank: opens a four-token job, then the job id + 1
+    __shared__ int8_t s_list[kMaxAssignments];   // per rank: 1 = four-token list
     __shared__ int32_t s_warp[kGroupThreads / 32];
     const int n = T * k;
     const int P = n + (shared ? T : 0);
     const bool mma = gu_m != nullptr;
+    const bool quad = mma && gu_q != nullptr;
     for (int a = threadIdx.x; a < n; a += blockDim.x) {
         const int e = ids[a];
-        s_ids[a] = e;
+        s_ids[a] = static_cast<int16_t>(min(max(e, 0), E - 1));
         if (e < 0 || e >= E) report_device_error(bad, kDevErrBadIndex);
     }
     __syncthreads();
     for (int a = threadIdx.x; a < n; a += blockDim.x) {
         const int e = s_ids[a];
-        int lt = 0, eq = 0;
+        int lt = 0, eq = 0, cnt = 0;
         for (int b = 0; b < n; ++b) {
             const int eb = s_ids[b];
             lt += eb < e;
             eq += (eb == e) & (b < a);
+            cnt += eb == e;
         }
         const int rank = lt + eq;
-        s_pair[a] = rank;
+        s_pair[a] = static_cast<int16_t>(rank);
         if (mma) {
-            s_job[rank] = static_cast<int16_t>((eq & 1) == 0);
+            const bool q4 = quad && cnt >= 3;
+            s_list[rank] = q4;
+            s_job[rank] = static_cast<int16_t>(!q4 && (eq & 1) == 0);
+            s_jobq[rank] = static_cast<int16_t>(q4 && (eq & 3) == 0);
             continue;
         }
         const int t = a / k;
@@ -163,49 +179,64 @@ __global__ void __launch_bounds__(kGroupThreads)
     }
     __syncthreads();
     if (mma) {
-        block_inclusive_scan(s_job, n, s_warp);  // s_job[r] = 1 + id of the job holding rank r
-        const int routed = n ? s_job[n - 1] : 0;
-        const int J = routed + (shared ? (T + 1) / 2 : 0);
-        // Pass 0 writes whole jobs from the pair in slot 0 (slot 1 empty),
-        // pass 1 fills slot 1.
+        block_inclusive_scan(s_job, n, s_warp);   // s_job[r] = 1 + id of the two-token job holding rank r
+        block_inclusive_scan(s_jobq, n, s_warp);  // s_jobq[r] = 1 + id of the four-token job holding rank r
+        const bool shared_q = quad;  // the host enables four-token jobs from 16 tokens
+        const int routed = n ? s_job[n - 1] : 0, routed_q = n ? s_jobq[n - 1] : 0;
+        const int J = routed + (shared && !shared_q ? (T + 1) / 2 : 0);
+        const int JQ = routed_q + (shared && shared_q ? (T + 3) / 4 : 0);
+        // Pass 0 writes whole jobs from the pair in slot 0 (other slots
+        // empty), pass 1 fills the other slots.
         for (int pass = 0; pass < 2; ++pass) {
             for (int a = threadIdx.x; a < n + (shared ? T : 0); a += blockDim.x) {
                 int e, t, r, j, slot;
+                bool q4;
                 const uint8_t *wg, *wu, *wd;
                 if (a < n) {
-                    e = min(max(s_ids[a], 0), E - 1);
+                    e = s_ids[a];
                     t = a / k;
                     r = s_pair[a];
-                    j = s_job[r] - 1;
-                    slot = (r > 0 && s_job[r - 1] == s_job[r]) ? 1 : 0;
+                    q4 = s_list[r];
+                    slot = 0;
+                    if (q4) {  // preceding ranks of the same four-token job
+                        j = s_jobq[r] - 1;
+                        for (int c = 1; c <= 3 && r - c >= 0 && s_list[r - c] && s_jobq[r - c] == s_jobq[r]; ++c)
+                            slot = c;
+                    } else {
+                        j = s_job[r] - 1;
+                        slot = (r > 0 && !s_list[r - 1] && s_job[r - 1] == s_job[r]) ? 1 : 0;
+                    }
                     wg = gate + e * gu_stride;
                     wu = up + e * gu_stride;
                     wd = down + e * dn_stride;
                 } else {
                     t = a - n;
                     r = n + t;
-                    j = routed + t / 2;
-                    slot = t & 1;
+                    q4 = shared_q;
+                    j = q4 ? routed_q + t / 4 : routed + t / 2;
+                    slot = q4 ? t & 3 : t & 1;
                     wg = sgate;
                     wu = sup;
                     wd = sdown;
                 }
-                if (slot != pass) continue;
+                if ((slot != 0) != (pass != 0)) continue;
                 const uint8_t *xp = xprep + static_cast<size_t>(t) * xstride;
                 const uint8_t *hp = hprep + static_cast<size_t>(r) * hstride;
                 float *go = g_out + static_cast<size_t>(r) * inter, *uo = u_out + static_cast<size_t>(r) * inter;
                 float *po = pair_out + static_cast<size_t>(r) * hidden;
+                MmaJob *gl = q4 ? gu_q : gu_m, *dl = q4 ? dn_q : dn_m;
+                const int Jl = q4 ? JQ : J;
                 if (slot == 0) {
-                    gu_m[j] = MmaJob{wg, {xp, nullptr}, {go, nullptr}};
-                    gu_m[J + j] = MmaJob{wu, {xp, nullptr}, {uo, nullptr}};
-                    dn_m[j] = MmaJob{wd, {hp, nullptr}, {po, nullptr}};
+                    gl[j] = MmaJob{wg, {xp}, {go}};
+                    gl[Jl + j] = MmaJob{wu, {xp}, {uo}};
+                    dl[j] = MmaJob{wd, {hp}, {po}};
                 } else {
-                    gu_m[j].xp[1] = xp;
-                    gu_m[j].out[1] = go;
-                    gu_m[J + j].xp[1] = xp;
-                    gu_m[J + j].out[1] = uo;
-                    dn_m[j].xp[1] = hp;
-                    dn_m[j].out[1] = po;
+                    gl[j].xp[slot] = xp;
+                    gl[j].out[slot] = go;
+                    gl[Jl + j].xp[slot] = xp;
+                    gl[Jl + j].out[slot] = uo;
+                    dl[j].xp[slot] = hp;
+                    dl[j].out[slot] = po;
                 }
             }
             __syncthreads();
@@ -213,6 +244,8 @@ __global__ void __launch_bounds__(kGroupThreads)
         if (threadIdx.x == 0) {
             counts[0] = 2 * J;
             counts[1] = J;
+            counts[2] = 2 * JQ;
+            counts[3] = JQ;
         }
     }
     // Each token's slots in ascending expert id (glm_vx/model.py:305-316).
@@ -265,7 +298,7 @@ static int32_t moe_ffn(float *y, const float *x, int32_t tokens, int32_t hidden,
                        int32_t *ids_out, float *weights_out, void *stream, void *const *events,
                        const int32_t *given_ids = nullptr) {
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    if (tokens < 0 || hidden <= 0 || inter <= 0 || experts <= 0 || top_k <= 0 || top_k > experts) {
+    if (tokens < 0 || hidden <= 0 || inter <= 0 || experts <= 0 || top_k <= 0 || top_k > experts || experts > 32767) {
         set_error("moe: invalid dimensions");
         return kInvalid;
     }
@@ -302,6 +335,11 @@ static int32_t moe_ffn(float *y, const float *x, int32_t tokens, int32_t hidden,
     auto a16 = [](const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
     const bool mma = mma_supported(kind, hidden) && mma_supported(kind, inter) && a16(x) && a16(gate) && a16(up) &&
                      a16(down) && (!shared || (a16(shared_gate) && a16(shared_up) && a16(shared_down)));
+    // Four-token jobs pay off from about 16 tokens (experts sharing three or
+    // more tokens, the shared expert); below, their two extra launches cost
+    // more than they save.
+    const bool quad = mma && tokens >= kQuadMinTokens && mma_quad_supported(kind, hidden) &&
+                      mma_quad_supported(kind, inter);
     int32_t st_ = mark(0);
     if (st_) return st_;
     if (mma && (st_ = prep_rows_device(w.xprep, x, nullptr, tokens, hidden, st))) return st_;
@@ -318,16 +356,21 @@ static int32_t moe_ffn(float *y, const float *x, int32_t tokens, int32_t hidden,
     moe_group_kernel<<<1, kGroupThreads, 0, st>>>(
         w.ids, w.wts, tokens, top_k, experts, shared, gate, up, down, gu_stride, dn_stride, shared_gate, shared_up,
         shared_down, x, hidden, inter, w.g_out, w.u_out, w.pair_out, w.gu_jobs, w.dn_jobs, w.comb, w.combw,
-        device_error_word(), mma ? w.gu_mjobs : nullptr, w.dn_mjobs, w.counts, w.xprep, prep_stride(hidden), w.hprep,
-        prep_stride(inter));
+        device_error_word(), mma ? w.gu_mjobs : nullptr, w.dn_mjobs, quad ? w.gu_qjobs : nullptr, w.dn_qjobs, w.counts,
+        w.xprep, prep_stride(hidden), w.hprep, prep_stride(inter));
     if ((st_ = launch_status("moe_group_kernel")) || (st_ = mark(3))) return st_;
     if (mma) {
         const MmaJob none{};
         if ((st_ = mma_gemv_device(kind, none, w.gu_mjobs, w.counts, 2 * P, 0, inter, hidden, st)) ||
+            (quad && (st_ = mma_gemv_device(kind, none, w.gu_qjobs, w.counts + 2, 2 * P, 0, inter, hidden, st,
+                                             nullptr, 2))) ||
             (st_ = mark(4)))
             return st_;
         if ((st_ = prep_rows_device(w.hprep, w.g_out, w.u_out, P, inter, st)) ||
-            (st_ = mma_gemv_device(kind, none, w.dn_mjobs, w.counts + 1, P, 0, hidden, inter, st)) || (st_ = mark(5)))
+            (st_ = mma_gemv_device(kind, none, w.dn_mjobs, w.counts + 1, P, 0, hidden, inter, st)) ||
+            (quad && (st_ = mma_gemv_device(kind, none, w.dn_qjobs, w.counts + 3, P, 0, hidden, inter, st, nullptr,
+                                             2))) ||
+            (st_ = mark(5)))
             return st_;
     } else {
         if ((st_ = gemv_jobs_device(kind, w.gu_jobs, 2 * P, inter, hidden, gate, x, st)) || (st_ = mark(4)))

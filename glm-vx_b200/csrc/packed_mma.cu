@@ -196,6 +196,52 @@ struct MmaFmt<FmtIQ1_S> {
             af[f][3] = fmaf(s1, static_cast<float>(ai[f][3]), af[f][3]);
         }
     }
+    // Two token pairs per job, one 16-row fragment (rows g, g+8 of p[0]):
+    // each decoded fragment feeds two MMAs.  Same arithmetic per pair as
+    // chunk(), so a token's result does not depend on the job it lands in.
+    template <int C, int NB>
+    __device__ __forceinline__ static void chunk2(const uint8_t *const (&p)[1][2], int t,
+                                                  const uint32_t (&b)[2][NB][2], float xs0, float xs1,
+                                                  const uint8_t *tab, float (&af)[2][1][4]) {
+        const int sh = 3 * t;
+        const uint32_t hmask = 7u << sh, hmul = c_iq1s_hi_mul[t];
+        constexpr uint32_t step = kLutMinus - kLutPlus;
+        const uint32_t k14 = 14u, k1 = 1u;
+        const uint32_t tab_s = smem_addr(tab);
+        const uint8_t *q0 = p[0][0] + C * kBlockBytes, *q1 = p[0][1] + C * kBlockBytes;
+        const uint8_t *qt0 = q0 + 2 + t, *qt1 = q1 + 2 + t;
+        int ai[2][4] = {};
+#pragma unroll
+        for (int s = 0; s < 8; ++s) {
+            const uint32_t h0 = u16(q0 + 34 + 2 * s), h1 = u16(q1 + 34 + 2 * s);
+            const uint32_t e0 = lds32_const((h0 & hmask) * hmul + (qt0[4 * s] * 16u + tab_s));
+            const uint32_t e1 = lds32_const((h1 & hmask) * hmul + (qt1[4 * s] * 16u + tab_s));
+            const uint32_t l0 = kLutPlus + (h0 >> 15) * step, l1 = kLutPlus + (h1 >> 15) * step;
+            const uint32_t a0 = prmt(l0, 0, e0), a1 = prmt(l1, 0, e1);
+            const uint32_t a2 = prmt(l0, 0, __umulhi(e0, 65536u)), a3 = prmt(l1, 0, __umulhi(e1, 65536u));
+            const int dl0 = static_cast<int>(and_or(h0 >> 11, k14, k1));
+            const int dl1 = static_cast<int>(and_or(h1 >> 11, k14, k1));
+#pragma unroll
+            for (int q = 0; q < 2; ++q) {
+                int c[4];
+                mma_s8s8(c, a0, a1, a2, a3, b[q][8 * C + s][0], b[q][8 * C + s][1]);
+                ai[q][0] += dl0 * c[0];
+                ai[q][1] += dl0 * c[1];
+                ai[q][2] += dl1 * c[2];
+                ai[q][3] += dl1 * c[3];
+            }
+        }
+        const float d0 = h2f(u16(q0)), d1 = h2f(u16(q1));
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+            const float xq = q ? xs1 : xs0;
+            const float s0 = d0 * (0.125f * xq), s1 = d1 * (0.125f * xq);
+            af[q][0][0] = fmaf(s0, static_cast<float>(ai[q][0]), af[q][0][0]);
+            af[q][0][1] = fmaf(s0, static_cast<float>(ai[q][1]), af[q][0][1]);
+            af[q][0][2] = fmaf(s1, static_cast<float>(ai[q][2]), af[q][0][2]);
+            af[q][0][3] = fmaf(s1, static_cast<float>(ai[q][3]), af[q][0][3]);
+        }
+    }
 };
 
 template <>
@@ -381,10 +427,21 @@ __global__ void __launch_bounds__(256)
 
 // ----------------------------------------------------------------- kernel ---
 
+// a[i] for a run-time i with constant-index reads (a dynamic index would
+// place the whole array in local memory).
+template <int N, class T>
+__device__ __forceinline__ T pick(const T (&a)[N], int i) {
+    T r = a[0];
+#pragma unroll
+    for (int c = 1; c < N; ++c)
+        if (i == c) r = a[c];
+    return r;
+}
+
 __device__ __forceinline__ MmaJob job_at(const MmaJob &job0, const MmaJob *jobs, int j, int batch, int rows_per_job,
                                          size_t pstride) {
     if (jobs) return jobs[j];
-    MmaJob r;
+    MmaJob r{};
     r.w = job0.w;
 #pragma unroll
     for (int s = 0; s < 2; ++s) {
@@ -396,14 +453,22 @@ __device__ __forceinline__ MmaJob job_at(const MmaJob &job0, const MmaJob *jobs,
     return r;
 }
 
-// W = 256-column chunks per warp column slice (1 or 2).
-template <class F, int S, int RG, int W>
+// W = 256-column chunks per warp column slice (1 or 2); NT = token pairs
+// per job (2: each decoded fragment is multiplied into two pairs, one 16-row
+// fragment per warp; job lists of IQ1_S only).
+template <class F, int NT>
+constexpr int mma_fragments() {
+    return NT == 2 ? 1 : MmaFmt<F>::kFR;
+}
+
+template <class F, int S, int RG, int W, int NT>
 __global__ void __launch_bounds__((S * RG + 1) * 32, 1)
     mma_rows_kernel(MmaJob job0, const MmaJob *__restrict__ jobs, const int *njobs_dev, int max_jobs, int batch,
                     int rows_per_job, int cols, int row_bytes, int srow, int stages, int stage_stride,
                     const float *__restrict__ x_raw, int *err) {
     using MF = MmaFmt<F>;
-    constexpr int FR = MF::kFR;
+    constexpr int FR = mma_fragments<F, NT>();
+    constexpr int NS = 2 * NT;                      // token slots per job
     constexpr int NW = S * RG, R = 16 * FR * RG;  // a warp owns FR 16-row fragments of the tile
     extern __shared__ __align__(128) uint8_t smem[];
     const size_t pstride = prep_stride(cols);
@@ -411,8 +476,8 @@ __global__ void __launch_bounds__((S * RG + 1) * 32, 1)
     // the two rows of each job it reaches into `bsm` itself.
     uint8_t *bsm = smem + static_cast<size_t>(stages) * stage_stride;
     uint8_t *table = bsm + (x_raw ? 2 * pstride : 0);
-    float *red = reinterpret_cast<float *>(table + MF::kTableBytes);  // [2][R][S][2]
-    uint64_t *full = reinterpret_cast<uint64_t *>(red + 2 * R * S * 2);
+    float *red = reinterpret_cast<float *>(table + MF::kTableBytes);  // [2][R][S][NS]
+    uint64_t *full = reinterpret_cast<uint64_t *>(red + 2 * R * S * NS);
     uint64_t *empty = full + stages;
     uint64_t *jobbar = empty + stages;  // consumer warps meet here around a job's preparation
     volatile int *abort_flag = reinterpret_cast<volatile int *>(jobbar + 1);  // [RG]
@@ -490,9 +555,9 @@ __global__ void __launch_bounds__((S * RG + 1) * 32, 1)
     const int u0 = sw * SUB;    // first sub-block of the slice
     const size_t slice_off = static_cast<size_t>(u0 / MF::kSubPerBlock) * MF::kBlockBytes;
     const size_t scale_off = prep_scale_offset(cols), sums_off = prep_sums_offset(cols);
-    uint32_t b[SUB][2];
-    float xs[W] = {}, down[2] = {0.0f, 0.0f};
-    const float *sums = nullptr;
+    uint32_t b[NT][SUB][2];
+    float xs[NT][W] = {}, down[NT][2] = {};
+    const float *sums[NT] = {};
     MmaJob J{};
     int loaded = -1;
     uint32_t jb_phase = 0;
@@ -530,35 +595,43 @@ __global__ void __launch_bounds__((S * RG + 1) * 32, 1)
                 J.xp[0] = bsm;
                 J.xp[1] = 2 * job + 1 < batch ? bsm + pstride : nullptr;
             }
-            const uint8_t *xb = (g >> 2) ? J.xp[1] : J.xp[0];  // B column g: token g/4, limb g%4
 #pragma unroll
-            for (int u = 0; u < SUB; ++u) {
-                uint2 v = make_uint2(0u, 0u);
-                if (xb) v = *reinterpret_cast<const uint2 *>(xb + static_cast<size_t>(g & 3) * cols + 32 * (u0 + u) + 8 * t);
-                b[u][0] = v.x;
-                b[u][1] = v.y;
+            for (int q = 0; q < NT; ++q) {
+                // pair q: B column g is token slot 2q + g/4, limb g%4
+                const uint8_t *xb = pick(J.xp, 2 * q + (g >> 2));
+#pragma unroll
+                for (int u = 0; u < SUB; ++u) {
+                    uint2 v = make_uint2(0u, 0u);
+                    if (xb)
+                        v = *reinterpret_cast<const uint2 *>(xb + static_cast<size_t>(g & 3) * cols + 32 * (u0 + u) +
+                                                             8 * t);
+                    b[q][u][0] = v.x;
+                    b[q][u][1] = v.y;
+                }
+                // accumulator columns 2t, 2t+1: token slot 2q + t/2
+                const uint8_t *xa = pick(J.xp, 2 * q + (t >> 1));
+                // Chunk c holds x*2^E_c.  Relative to Eref = min over the slice's
+                // chunks (the one of largest magnitude) its scale is 2^(Eref - E_c)
+                // <= 1; the absolute 2^-Eref is applied once per tile in two exact
+                // steps.  A chunk more than 2^126 below another contributes nothing.
+                int e[W];
+                bool bad = false;
+#pragma unroll
+                for (int c = 0; c < W; ++c) {
+                    e[c] = xa ? reinterpret_cast<const int *>(xa + scale_off)[u0 / 8 + c] : 0;
+                    bad |= e[c] == kPrepNonFinite;
+                }
+                int eref = e[0];
+#pragma unroll
+                for (int c = 1; c < W; ++c) eref = min(eref, e[c]);
+                if (bad) eref = 0;
+#pragma unroll
+                for (int c = 0; c < W; ++c)
+                    xs[q][c] = (xa && !bad && eref - e[c] >= -126) ? pow2(eref - e[c]) : 0.0f;
+                down[q][0] = bad ? __int_as_float(0x7fc00000) : pow2(-(eref / 2));
+                down[q][1] = pow2(-(eref - eref / 2));
+                sums[q] = (MF::kMins && xa) ? reinterpret_cast<const float *>(xa + sums_off) + u0 : nullptr;
             }
-            const uint8_t *xa = (t >> 1) ? J.xp[1] : J.xp[0];  // accumulator columns 2t, 2t+1: token t/2
-            // Chunk c holds x*2^E_c.  Relative to Eref = min over the slice's
-            // chunks (the one of largest magnitude) its scale is 2^(Eref - E_c)
-            // <= 1; the absolute 2^-Eref is applied once per tile in two exact
-            // steps.  A chunk more than 2^126 below another contributes nothing.
-            int e[W];
-            bool bad = false;
-#pragma unroll
-            for (int c = 0; c < W; ++c) {
-                e[c] = xa ? reinterpret_cast<const int *>(xa + scale_off)[u0 / 8 + c] : 0;
-                bad |= e[c] == kPrepNonFinite;
-            }
-            int eref = e[0];
-#pragma unroll
-            for (int c = 1; c < W; ++c) eref = min(eref, e[c]);
-            if (bad) eref = 0;
-#pragma unroll
-            for (int c = 0; c < W; ++c) xs[c] = (xa && !bad && eref - e[c] >= -126) ? pow2(eref - e[c]) : 0.0f;
-            down[0] = bad ? __int_as_float(0x7fc00000) : pow2(-(eref / 2));
-            down[1] = pow2(-(eref - eref / 2));
-            sums = (MF::kMins && xa) ? reinterpret_cast<const float *>(xa + sums_off) + u0 : nullptr;
         }
         const int s = k % stages;
         const bool ok = mbar_wait_bounded(&full[s], (k / stages) & 1);
@@ -567,7 +640,7 @@ __global__ void __launch_bounds__((S * RG + 1) * 32, 1)
             abort_flag[rg] = 1;
         }
         const int nr = tile_end(r0, r_end) - r0;
-        float af[FR][4] = {}, am[FR][2] = {};
+        float af[NT][FR][4] = {}, am[NT][FR][2] = {};
         const int rbase = 16 * FR * rg;  // first tile row of this warp's fragments
         if (ok) {
             const uint8_t *p[FR][2];
@@ -577,40 +650,47 @@ __global__ void __launch_bounds__((S * RG + 1) * 32, 1)
                           slice_off;
                 p[f][1] = p[f][0] + 8 * static_cast<size_t>(srow);
             }
-            MF::template chunk<0>(p, t, b, xs[0], sums, ltab, af, am);
-            if constexpr (W == 2) MF::template chunk<1>(p, t, b, xs[W - 1], sums, ltab, af, am);
+            if constexpr (NT == 1) {
+                MF::template chunk<0>(p, t, b[0], xs[0][0], sums[0], ltab, af[0], am[0]);
+                if constexpr (W == 2) MF::template chunk<1>(p, t, b[0], xs[0][W - 1], sums[0], ltab, af[0], am[0]);
+            } else {
+                MF::template chunk2<0>(p, t, b, xs[0][0], xs[1][0], ltab, af);
+                if constexpr (W == 2) MF::template chunk2<1>(p, t, b, xs[0][W - 1], xs[1][W - 1], ltab, af);
+            }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[s]);
         }
         // Recombine the limbs: lanes with even t hold limbs 0,1 (x 2^24, 2^16)
         // and subtract the min term, odd t limbs 2,3 (x 2^8, 1).
         const float whi = (t & 1) ? 256.0f : 16777216.0f, wlo = (t & 1) ? 1.0f : 65536.0f;
-        float *rb = red + static_cast<size_t>(k & 1) * R * S * 2;
+        float *rb = red + static_cast<size_t>(k & 1) * R * S * NS;
+#pragma unroll
+        for (int q = 0; q < NT; ++q)
 #pragma unroll
         for (int f = 0; f < FR; ++f) {
-            float v0 = fmaf(af[f][0], whi, af[f][1] * wlo) * down[0] * down[1];
-            float v1 = fmaf(af[f][2], whi, af[f][3] * wlo) * down[0] * down[1];
+            float v0 = fmaf(af[q][f][0], whi, af[q][f][1] * wlo) * down[q][0] * down[q][1];
+            float v1 = fmaf(af[q][f][2], whi, af[q][f][3] * wlo) * down[q][0] * down[q][1];
             if (MF::kMins && !(t & 1)) {
-                v0 -= am[f][0];
-                v1 -= am[f][1];
+                v0 -= am[q][f][0];
+                v1 -= am[q][f][1];
             }
             v0 += __shfl_xor_sync(0xffffffffu, v0, 1);
             v1 += __shfl_xor_sync(0xffffffffu, v1, 1);
             if (!(t & 1)) {
-                rb[((rbase + 16 * f + g) * S + sw) * 2 + (t >> 1)] = v0;
-                rb[((rbase + 16 * f + g + 8) * S + sw) * 2 + (t >> 1)] = v1;
+                rb[((rbase + 16 * f + g) * S + sw) * NS + 2 * q + (t >> 1)] = v0;
+                rb[((rbase + 16 * f + g + 8) * S + sw) * NS + 2 * q + (t >> 1)] = v1;
             }
         }
         named_barrier_sync(2 + rg, S * 32);
         if (abort_flag[rg]) break;
-        if (sw == 0) {  // 16*FR rows x 2 tokens: S partials each, in fixed order
+        if (sw == 0) {  // 16*FR rows x NS tokens: S partials each, in fixed order
 #pragma unroll
-            for (int o2 = lane; o2 < 32 * FR; o2 += 32) {
-                const int i = rbase + (o2 >> 1), slot = o2 & 1;
+            for (int o2 = lane; o2 < 16 * FR * NS; o2 += 32) {
+                const int i = rbase + o2 / NS, slot = o2 % NS;
                 float v = 0.0f;
 #pragma unroll
-                for (int q = 0; q < S; ++q) v += rb[(i * S + q) * 2 + slot];
-                float *o = slot ? J.out[1] : J.out[0];
+                for (int q = 0; q < S; ++q) v += rb[(i * S + q) * NS + slot];
+                float *o = pick(J.out, slot);
                 if (i < nr && o) o[(r0 + i) % rows_per_job] = v;
             }
         }
@@ -653,7 +733,8 @@ static int mma_slice_chunks(int cols) {
 }
 
 template <class F>
-static bool plan_mma(int64_t max_rows, int64_t max_tiles_extra, int cols, int row_bytes, bool fused, MmaPlan &p) {
+static bool plan_mma(int64_t max_rows, int64_t max_tiles_extra, int cols, int row_bytes, bool fused, int pairs,
+                     MmaPlan &p) {
     using MF = MmaFmt<F>;
     if (cols % 256 || row_bytes % 16) return false;
     p.W = mma_slice_chunks<F>(cols);
@@ -661,7 +742,7 @@ static bool plan_mma(int64_t max_rows, int64_t max_tiles_extra, int cols, int ro
     p.S = cols / (256 * p.W);
     if (!mma_slices_ok(p.S, p.W)) return false;
     p.RG = mma_row_groups(p.S, p.W);
-    const int R = 16 * MF::kFR * p.RG;
+    const int R = 16 * (pairs == 2 ? 1 : MF::kFR) * p.RG;
     // Shared-memory rows span an odd number of 16-byte units, so rows g = 0..7
     // of a fragment start in 8 different 4-bank groups.  Rows that already do
     // (IQ1_S: 400 or 1200 bytes) keep the global stride and arrive with one
@@ -670,7 +751,8 @@ static bool plan_mma(int64_t max_rows, int64_t max_tiles_extra, int cols, int ro
     // a row: the last block of a row has an odd index.)
     p.srow = ((row_bytes >> 4) & 1) ? row_bytes : row_bytes + 16;
     p.stage_stride = (R * p.srow + 127) & ~127;
-    const size_t fixed = (fused ? 2 * prep_stride(cols) : 0) + MF::kTableBytes + 2ull * R * p.S * 2 * 4 + 16 * 8 + 64;
+    const size_t fixed =
+        (fused ? 2 * prep_stride(cols) : 0) + MF::kTableBytes + 2ull * R * p.S * 2 * pairs * 4 + 16 * 8 + 64;
     const int fit = static_cast<int>((kMmaSmemBudget - std::min(fixed, kMmaSmemBudget)) / p.stage_stride);
     if (fit < 1) return false;
     const int64_t tiles = (max_rows + R - 1) / R + max_tiles_extra;
@@ -683,12 +765,12 @@ static bool plan_mma(int64_t max_rows, int64_t max_tiles_extra, int cols, int ro
     return true;
 }
 
-template <class F, int S, int W>
+template <class F, int S, int W, int NT>
 static int32_t launch_mma(const MmaPlan &p, const MmaJob &job0, const MmaJob *jobs, const int *njobs_dev,
                           int max_jobs, int batch, int rows_per_job, int cols, int row_bytes, const float *x_raw,
                           cudaStream_t stream) {
     constexpr int RG = mma_row_groups(S, W);
-    auto kern = mma_rows_kernel<F, S, RG, W>;
+    auto kern = mma_rows_kernel<F, S, RG, W, NT>;
     static size_t configured = 0;  // per instantiation
     if (p.smem > configured) {
         GLMVX_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(p.smem)));
@@ -709,14 +791,14 @@ static int32_t launch_mma(const MmaPlan &p, const MmaJob &job0, const MmaJob *jo
     return kOk;
 }
 
-template <class F>
+template <class F, int NT>
 static int32_t launch_mma_s(const MmaPlan &p, const MmaJob &job0, const MmaJob *jobs, const int *njobs_dev,
                             int max_jobs, int batch, int rows_per_job, int cols, int row_bytes, const float *x_raw,
                             cudaStream_t stream) {
-#define GLMVX_MMA_CASE(s, w)                                                                                 \
-    case 2 * (s) + (w) - 1:                                                                                 \
-        return launch_mma<F, s, w>(p, job0, jobs, njobs_dev, max_jobs, batch, rows_per_job, cols, row_bytes, \
-                                   x_raw, stream);
+#define GLMVX_MMA_CASE(s, w)                                                                                     \
+    case 2 * (s) + (w) - 1:                                                                                     \
+        return launch_mma<F, s, w, NT>(p, job0, jobs, njobs_dev, max_jobs, batch, rows_per_job, cols, row_bytes, \
+                                       x_raw, stream);
     switch (2 * p.S + p.W - 1) {
         GLMVX_MMA_CASE(1, 2)
         GLMVX_MMA_CASE(2, 2)
@@ -738,6 +820,9 @@ static int32_t launch_mma_s(const MmaPlan &p, const MmaJob &job0, const MmaJob *
 
 // Rows must be whole 16-byte units for the per-row bulk copies: always for
 // Q8_0 (cols % 256) and Q4_K, for IQ1_S when cols % 2048 == 0.
+// (Up to 12 column slices: with 16 the register budget of 17 warps spills.)
+bool mma_quad_supported(int kind, int cols) { return kind == 19 && mma_supported(kind, cols) && cols <= 6144; }
+
 bool mma_supported(int kind, int cols) {
     if (cols <= 0 || cols % 512 || !mma_slices_ok(cols / 512, 2)) return false;
     return kind == 8 || kind == 12 || (kind == 19 && cols % 2048 == 0);
@@ -765,7 +850,11 @@ int32_t prep_rows_device(uint8_t *prep, const float *x, const float *x2, int row
 }
 
 int32_t mma_gemv_device(int32_t kind, const MmaJob &job0, const MmaJob *jobs, const int *njobs_dev, int max_jobs,
-                        int batch, int rows_per_job, int cols, cudaStream_t stream, const float *x_raw) {
+                        int batch, int rows_per_job, int cols, cudaStream_t stream, const float *x_raw, int pairs) {
+    if (pairs != 1 && !(pairs == 2 && jobs && !x_raw && mma_quad_supported(kind, cols))) {
+        set_error("mma: two token pairs per job need a job list of a supported format");
+        return kInvalid;
+    }
     if (x_raw && (jobs || (reinterpret_cast<uintptr_t>(x_raw) & 15))) {
         set_error("mma: in-kernel preparation needs a single matrix and 16-byte aligned activations");
         return kInvalid;
@@ -786,13 +875,18 @@ int32_t mma_gemv_device(int32_t kind, const MmaJob &job0, const MmaJob *jobs, co
     dispatch_format(kind, [&]<class F>() {
         if constexpr (std::is_same_v<F, FmtQ8_0> || std::is_same_v<F, FmtQ4_K> || std::is_same_v<F, FmtIQ1_S>) {
             MmaPlan p;
-            if (!plan_mma<F>(max_rows, max_jobs, cols, row_bytes, x_raw != nullptr, p)) {
+            if (!plan_mma<F>(max_rows, max_jobs, cols, row_bytes, x_raw != nullptr, pairs, p)) {
                 set_error("mma: no launch plan for this shape");
                 st = kUnsupported;
                 return;
             }
-            st = launch_mma_s<F>(p, job0, jobs, njobs_dev, max_jobs, batch, rows_per_job, cols, row_bytes, x_raw,
-                                 stream);
+            if (pairs == 1) {
+                st = launch_mma_s<F, 1>(p, job0, jobs, njobs_dev, max_jobs, batch, rows_per_job, cols, row_bytes, x_raw,
+                                        stream);
+            } else if constexpr (std::is_same_v<F, FmtIQ1_S>) {
+                st = launch_mma_s<F, 2>(p, job0, jobs, njobs_dev, max_jobs, batch, rows_per_job, cols, row_bytes, x_raw,
+                                        stream);
+            }
         }
     });
     return st;

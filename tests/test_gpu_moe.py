@@ -117,11 +117,32 @@ def _check_layer(gpu_backend, oracle, E, H, I, K, T, kind, seed):
         moe.close()
 
 
-@pytest.mark.parametrize('T', [1, 2, 5, 9])
+@pytest.mark.parametrize('T', [1, 2, 5, 9, 17, 23])
 def test_moe_tokens_share_experts(gpu_backend, oracle, T):
     """4 experts, top-2: most experts serve several tokens, with odd and even
-    counts, so expert jobs take two tokens and some a single one."""
+    counts, so expert jobs take two tokens and some a single one; experts with
+    three or more tokens and the shared expert run as four-token jobs, full
+    and partial, from 16 tokens per call."""
     _check_layer(gpu_backend, oracle, 4, 2048, 2048, 2, T, 19, seed=30 + T)
+
+
+@pytest.mark.parametrize('T', [17, 23])
+def test_moe_result_independent_of_batch(gpu_backend, T):
+    """A token's output does not depend on the job it lands in (two- or
+    four-token jobs compute each token with the same arithmetic): the batch
+    equals token-by-token calls bit for bit."""
+    from gpu.moe import MoELayer
+    E, H, I, K = 4, 2048, 2048, 2
+    layer = synthetic_layer(E, H, I, seed=50 + T)
+    moe = MoELayer(gpu_backend, layer['router'], layer['bias'], 19, layer['gate'], layer['up'], layer['down'],
+                   H, I, K, 2.5, shared=layer['shared'])
+    try:
+        x = np.random.default_rng(60 + T).normal(size=(T, H)).astype(np.float32)
+        y, _, _ = moe.forward(x)
+        singles = np.stack([moe.forward(x[i:i + 1])[0][0] for i in range(T)])
+        assert y.tobytes() == singles.tobytes()
+    finally:
+        moe.close()
 
 
 @pytest.mark.parametrize('kind', [8, 12])
