@@ -539,14 +539,16 @@ def run_ours(args, ranks):
                    'l2_policy': 'inputs larger than L2: the layer streams 1.9 GB of resident experts',
                    'per_tokens': per_tokens},
         'roofline': {'bound': 'hbm', 'achieved': achieved, 'peak': peak, 'unit': 'GB/s', 'frac': achieved / peak,
-                     'traffic': NCU_TRAFFIC, 'kernel': 'mma_rows_kernel<IQ1_S> gate+up job list (tensor-core int8)',
+                     'traffic': NCU_TRAFFIC, 'kernel': 'mma_rows_kernel<IQ1_S> gate+up job lists (tensor-core int8; two- and four-token jobs, two launches)',
                      'algorithmic_bytes_per_launch': gu_bytes, 'avg_launch_us': gu_us, 'peak_source': peak_kind},
         'fused_gemv': gemv,
         **({'expert_parallel': ep} if ep else {}),
         'e2e': {'value': e2e_value, 'unit': 'tok/s', 'steps': e2e_steps,
                 'h2d_bytes_per_step': TOKENS * HIDDEN * 4, 'd2h_bytes_per_step': TOKENS * HIDDEN * 4 + 2 * TOKENS * TOPK * 4,
                 'api': 'gpu.moe.MoELayer.forward (host rows in, host rows + routing out)'},
-        'gpu_launches': 8 * args.steps,  # prep x, router logits, top-k, grouping, gate+up, prep h, down, combine
+        # prep x, router logits, top-k, grouping, gate+up (two-token and four-token job lists), prep h,
+        # down (both lists), combine
+        'gpu_launches': 10 * args.steps,
         'clocks': clocks.summary(),
     }
     if ranks.rank == 0 and ranks.world == 1 and not args.no_cpu_baseline:

@@ -83,7 +83,10 @@ static MoeWorkspace carve(char *base, int T, int hidden, int inter, int E, int k
     return w;
 }
 
-constexpr int kGroupThreads = 512, kMaxAssignments = 4096, kQuadMinTokens = 16;
+#ifndef GLMVX_QUAD_MIN_TOKENS
+#define GLMVX_QUAD_MIN_TOKENS 16
+#endif
+constexpr int kGroupThreads = 512, kMaxAssignments = 4096, kQuadMinTokens = GLMVX_QUAD_MIN_TOKENS;
 
 // Inclusive prefix sum of v[0..n) in place (n <= kMaxAssignments), whole CTA.
 __device__ void block_inclusive_scan(int16_t *v, int n, int32_t *s_warp) {
