@@ -513,15 +513,18 @@ def run_ours(args, ranks):
     achieved = gu_bytes / (gu_us * 1e-6) / 1e9
     dev.check_device_error()
 
-    # e2e through the public API: host token rows in, host outputs out.
+    # e2e through the public API: token rows in pinned host memory, copied to
+    # the device, the layer, outputs copied back to pinned host memory and
+    # checked there (MoELayer.forward_pinned), every step.
     e2e_steps = max(1, min(args.steps, 200))
+    np.copyto(moe.pinned_io(TOKENS)['x'], xs[TOKENS])
     for i in range(min(args.warmup, 3)):
-        moe.forward(xs[TOKENS])
+        moe.forward_pinned(TOKENS)
     ranks.barrier()
     t0 = time.perf_counter()
     w0 = time.time()
     for _ in range(e2e_steps):
-        moe.forward(xs[TOKENS])
+        moe.forward_pinned(TOKENS)
     e2e_s = ranks.max(time.perf_counter() - t0)
     clocks.window(w0, time.time())
     e2e_value = ranks.world * TOKENS * e2e_steps / e2e_s
@@ -545,7 +548,7 @@ def run_ours(args, ranks):
         **({'expert_parallel': ep} if ep else {}),
         'e2e': {'value': e2e_value, 'unit': 'tok/s', 'steps': e2e_steps,
                 'h2d_bytes_per_step': TOKENS * HIDDEN * 4, 'd2h_bytes_per_step': TOKENS * HIDDEN * 4 + 2 * TOKENS * TOPK * 4,
-                'api': 'gpu.moe.MoELayer.forward (host rows in, host rows + routing out)'},
+                'api': 'gpu.moe.MoELayer.forward_pinned (pinned host rows in, pinned host rows + routing out)'},
         # prep x, router logits, top-k, grouping, gate+up (two-token and four-token job lists), prep h,
         # down (both lists), combine
         'gpu_launches': 10 * args.steps,

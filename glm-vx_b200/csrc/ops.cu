@@ -293,7 +293,12 @@ __global__ void __launch_bounds__(256)
     __shared__ int ibest[8];
     __shared__ int chosen[kMaxRouterK];
     const float *lr = logits + static_cast<size_t>(blockIdx.x) * experts;
-    for (int e = threadIdx.x; e < experts; e += 256) score[e] = sigmoid_ref(lr[e]) + bias[e];
+    // A NaN score (non-finite activations) ranks as -inf, so every slot still
+    // names a distinct expert in range; the outputs are then non-finite.
+    for (int e = threadIdx.x; e < experts; e += 256) {
+        const float v = sigmoid_ref(lr[e]) + bias[e];
+        score[e] = isnan(v) ? -INFINITY : v;
+    }
     __syncthreads();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     for (int slot = 0; slot < k; ++slot) {
@@ -329,7 +334,7 @@ __global__ void __launch_bounds__(256)
                     i = ibest[q];
                 }
             chosen[slot] = i;
-            score[i] = -INFINITY;  // exclude from later slots
+            score[i] = NAN;  // excluded from later slots (never > or == anything)
         }
         __syncthreads();
     }

@@ -112,6 +112,16 @@ class GPUBackend:
                     b.close()
             self._dev, self._host, self._cap = rt.DeviceBuffer(cap), rt.HostBuffer(cap), cap
 
+    def _arena(self, input_bytes, output_bytes):
+        """Offsets (256-byte aligned) of inputs then outputs in the arena,
+        reserving it; no copies.  Returns (input offsets, output offsets)."""
+        offsets, off = [], 0
+        for nbytes in list(input_bytes) + list(output_bytes):
+            offsets.append(off)
+            off += (nbytes + 255) & ~255
+        self._reserve(max(off, 256))
+        return offsets[:len(input_bytes)], offsets[len(input_bytes):]
+
     def _stage(self, inputs, outputs):
         """Lay out inputs then outputs (256-byte aligned) in the arena, copy
         the inputs host->device in one transfer.  Returns device addresses of

@@ -77,9 +77,75 @@ class MoELayer:
         if need > self._ws_bytes:
             if self._ws is not None:
                 self.backend.stream.synchronize()
+                self._drop_graphs()
                 self._ws.close()
             self._ws, self._ws_bytes = rt.DeviceBuffer(need), need
         return self._ws.ptr
+
+    def _drop_graphs(self):
+        for g in self.__dict__.get('_graphs', {}).values():
+            g.close()
+        self._graphs = {}
+
+    def _io_layout(self, tokens):
+        """Byte offsets of x, y, ids, weights and the error word in the layer's
+        I/O buffers (pinned host + device, 256-byte aligned), grown on demand."""
+        sizes = [4 * tokens * self.hidden, 4 * tokens * self.hidden, 4 * tokens * self.top_k,
+                 4 * tokens * self.top_k, 4]
+        offs, off = [], 0
+        for n in sizes:
+            offs.append(off)
+            off += (n + 255) & ~255
+        if off > self.__dict__.get('_io_cap', 0):
+            self.backend.stream.synchronize()
+            self._drop_graphs()
+            for buf in self.__dict__.get('_io_bufs', ()):
+                buf.close()
+            self._io_bufs = (rt.HostBuffer(off), rt.DeviceBuffer(off))
+            self._io_cap = off
+        return offs
+
+    def pinned_io(self, tokens):
+        """Pinned host views for a `tokens`-row step: {'x', 'y', 'ids',
+        'weights'}.  Write the rows into 'x' and call forward_pinned(tokens);
+        the other views then hold its results until the next call."""
+        offs = self._io_layout(tokens)
+        host = self._io_bufs[0]
+        n, k = tokens * self.hidden, tokens * self.top_k
+        return {'x': host.view(np.float32, offs[0] // 4 + n)[offs[0] // 4:].reshape(tokens, self.hidden),
+                'y': host.view(np.float32, offs[1] // 4 + n)[offs[1] // 4:].reshape(tokens, self.hidden),
+                'ids': host.view(np.int32, offs[2] // 4 + k)[offs[2] // 4:].reshape(tokens, self.top_k),
+                'weights': host.view(np.float32, offs[3] // 4 + k)[offs[3] // 4:].reshape(tokens, self.top_k)}
+
+    def _step_graph(self, tokens):
+        """CUDA graph of one step on the I/O buffers: copy the token rows in,
+        the layer's launches, copy outputs and the device error word back.
+        Replayed per call so the GPU runs the step without host gaps;
+        captured again when the buffers or the workspace move."""
+        b = self.backend
+        offs = self._io_layout(tokens)
+        self._workspace(tokens)  # allocated before capture
+        host, dev = self._io_bufs
+        key = (tokens, host.ptr, dev.ptr, self._ws.ptr)
+        graphs = self.__dict__.setdefault('_graphs', {})
+        if key in graphs:
+            return graphs[key], offs
+        if any(k[1:] != key[1:] for k in graphs):
+            self._drop_graphs()
+            graphs = self._graphs
+        s = b.stream.handle
+        x_bytes, out_bytes = 4 * tokens * self.hidden, offs[3] + 4 * tokens * self.top_k - offs[1]
+        g = rt.Graph(b.stream)
+        g.begin()
+        try:
+            rt.call('glmvx_memcpy_htod', dev.ptr + offs[0], host.ptr + offs[0], x_bytes, s)
+            self.forward_device(dev.ptr + offs[1], dev.ptr + offs[0], tokens, dev.ptr + offs[2], dev.ptr + offs[3])
+            rt.call('glmvx_memcpy_dtoh', host.ptr + offs[1], dev.ptr + offs[1], out_bytes, s)
+            rt.call('glmvx_memcpy_dtoh', host.ptr + offs[4], b.device.error_address(), 4, s)
+        finally:
+            g.end()
+        graphs[key] = g
+        return g, offs
 
     def forward_device(self, y, x, tokens, ids=None, weights=None, stream=None):
         """Device pointers in and out; asynchronous on `stream` (default: the backend's)."""
@@ -89,30 +155,47 @@ class MoELayer:
             self.scale, self.kind, self.gate, self.up, self.down, *self.shared, ws, self._ws_bytes, ids, weights,
             stream if stream is not None else self.backend.stream.handle), 'glmvx_moe_ffn')
 
+    def forward_pinned(self, tokens):
+        """One step on the rows already in pinned_io(tokens)['x'] -> views
+        (y, ids, weights) of pinned_io(tokens), valid until the next call.
+        Raises like forward() on non-finite inputs or outputs."""
+        b = self.backend
+        b._begin()
+        io = self.pinned_io(tokens)
+        if tokens == 0:
+            return io['y'], io['ids'], io['weights']
+        g, offs = self._step_graph(tokens)
+        g.launch()
+        b.stream.synchronize()
+        if C.c_int32.from_address(self._io_bufs[0].ptr + offs[4]).value:
+            b.device.check_device_error()
+        # Non-finite inputs run safely (the router ranks NaN scores last) and
+        # give non-finite outputs, so one check after the step covers both.
+        if not np.isfinite(io['y']).all():
+            if not np.isfinite(io['x']).all():
+                raise ValueError('MoE input must be finite')
+            raise ValueError('nonfinite MoE output')
+        return io['y'], io['ids'], io['weights']
+
     def forward(self, x):
         """x [tokens, hidden] f32 -> (y [tokens, hidden], ids [tokens, k], weights [tokens, k])."""
         x = np.ascontiguousarray(x, dtype=np.float32)
         if x.ndim != 2 or x.shape[1] != self.hidden:
             raise ValueError('MoE input must be [tokens, hidden]')
-        if not np.isfinite(x).all():
-            raise ValueError('MoE input must be finite')
-        b = self.backend
-        b._begin()
         T = x.shape[0]
-        y = np.empty_like(x)
-        ids = np.empty((T, self.top_k), np.int32)
-        wts = np.empty((T, self.top_k), np.float32)
         if T == 0:
-            return y, ids, wts
-        (xd,), (yd, idd, wd, _), offs = b._stage([x], [y.nbytes, ids.nbytes, wts.nbytes, 4])
-        self.forward_device(yd, xd, T, idd, wd)
-        b._fetch_checked(offs[:3], [y, ids, wts], offs[3])
-        if not np.isfinite(y).all():
-            raise ValueError('nonfinite MoE output')
-        return y, ids, wts
+            return (np.empty_like(x), np.empty((0, self.top_k), np.int32), np.empty((0, self.top_k), np.float32))
+        self.backend._begin()
+        np.copyto(self.pinned_io(T)['x'], x)
+        y, ids, wts = self.forward_pinned(T)
+        return y.copy(), ids.copy(), wts.copy()
 
     def close(self):
         self.backend.stream.synchronize()
+        self._drop_graphs()
+        for buf in self.__dict__.pop('_io_bufs', ()):
+            buf.close()
+        self._io_cap = 0
         for buf in self._buffers + ([self._ws] if self._ws is not None else []):
             buf.close()
         self._buffers, self._ws = [], None

@@ -149,3 +149,37 @@ def test_moe_result_independent_of_batch(gpu_backend, T):
 def test_moe_other_formats(gpu_backend, oracle, kind):
     """Q8_0 and Q4_K expert stacks through the same layer (tensor-core path)."""
     _check_layer(gpu_backend, oracle, 8, 2048, 2048, 3, 4, kind, seed=kind)
+
+
+def test_moe_pinned_io_and_nonfinite_input(gpu_backend, oracle):
+    """forward_pinned on rows written into the layer's pinned buffers equals
+    forward; a non-finite activation runs safely (the router ranks NaN scores
+    last, every slot still a distinct expert in range) and is reported as
+    ValueError, after which the layer keeps working."""
+    from gpu.moe import MoELayer
+    E, H, I, K, T = 8, 2048, 2048, 4, 5
+    layer = synthetic_layer(E, H, I, seed=71)
+    moe = MoELayer(gpu_backend, layer['router'], layer['bias'], 19, layer['gate'], layer['up'], layer['down'],
+                   H, I, K, 2.5, shared=layer['shared'])
+    try:
+        x = np.random.default_rng(72).normal(size=(T, H)).astype(np.float32)
+        y, ids, w = moe.forward(x)
+        io = moe.pinned_io(T)
+        np.copyto(io['x'], x)
+        yp, idp, wp = moe.forward_pinned(T)
+        assert yp.tobytes() == y.tobytes() and idp.tolist() == ids.tolist() and wp.tobytes() == w.tobytes()
+        for bad in (np.nan, np.inf):
+            xb = x.copy()
+            xb[2, 10] = bad
+            with pytest.raises(ValueError, match='must be finite'):
+                moe.forward(xb)
+        xb = np.full_like(x, np.nan)
+        with pytest.raises(ValueError, match='must be finite'):
+            moe.forward(xb)
+        gpu_backend.device.check_device_error()
+        y2, _, _ = moe.forward(x)
+        assert y2.tobytes() == y.tobytes()
+        want, _ = reference_ffn(oracle, layer, x, E, H, I, K, 2.5)
+        assert np.linalg.norm(y - want) / np.linalg.norm(want) <= RTOL
+    finally:
+        moe.close()
