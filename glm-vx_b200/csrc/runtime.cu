@@ -147,56 +147,6 @@ GLMVX_EXPORT int32_t glmvx_memcpy_dtod(void *dst, const void *src, uint64_t byte
     return kOk;
 }
 
-// Device address of pinned host memory from glmvx_host_alloc (mapped into
-// the device's address space), for kernels that read or write it directly.
-GLMVX_EXPORT int32_t glmvx_host_device_pointer(void **dev, void *host) {
-    if (!dev || !host) {
-        set_error("host_device_pointer: null pointer");
-        return kInvalid;
-    }
-    *dev = nullptr;
-    GLMVX_CUDA(cudaHostGetDevicePointer(dev, host, 0));
-    return kOk;
-}
-
-// Copy by a kernel: 16-byte pieces over a grid-stride loop, then the tail
-// bytes.  With one side in mapped pinned host memory the transfer crosses
-// PCIe from the SMs' loads and stores, which for sub-megabyte transfers
-// avoids the copy engine's fixed start-up cost.
-__global__ void __launch_bounds__(256) copy_kernel(uint8_t *__restrict__ dst, const uint8_t *__restrict__ src,
-                                                   uint64_t bytes) {
-    grid_dependency_wait();
-    allow_dependent_launch();
-    const uint64_t n16 = bytes / 16;
-    const uint64_t stride = static_cast<uint64_t>(gridDim.x) * blockDim.x;
-    for (uint64_t i = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n16; i += stride)
-        reinterpret_cast<uint4 *>(dst)[i] = reinterpret_cast<const uint4 *>(src)[i];
-    const uint64_t tail = bytes - 16 * n16;
-    if (blockIdx.x == 0 && threadIdx.x < tail) dst[16 * n16 + threadIdx.x] = src[16 * n16 + threadIdx.x];
-}
-
-GLMVX_EXPORT int32_t glmvx_copy_kernel(void *dst, const void *src, uint64_t bytes, void *stream) {
-    if (!bytes) return kOk;
-    if (bytes >= 16 && ((reinterpret_cast<uintptr_t>(dst) | reinterpret_cast<uintptr_t>(src)) & 15)) {
-        set_error("copy_kernel: pointers must be 16-byte aligned (copies of 16 bytes or more)");
-        return kInvalid;
-    }
-    const uint64_t n16 = (bytes + 15) / 16;
-    const unsigned blocks = static_cast<unsigned>(std::min<uint64_t>((n16 + 255) / 256, 4ull * sm_count()));
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(std::max(1u, blocks));
-    cfg.blockDim = dim3(256);
-    cfg.stream = static_cast<cudaStream_t>(stream);
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    GLMVX_CUDA(cudaLaunchKernelEx(&cfg, copy_kernel, static_cast<uint8_t *>(dst), static_cast<const uint8_t *>(src),
-                                  bytes));
-    return kOk;
-}
-
 GLMVX_EXPORT int32_t glmvx_memset(void *dst, int32_t value, uint64_t bytes, void *stream) {
     if (bytes) GLMVX_CUDA(cudaMemsetAsync(dst, value, bytes, (cudaStream_t)stream));
     return kOk;

@@ -60,8 +60,6 @@ SIGNATURES = {
     'glmvx_graph_destroy': ([_P], _I32),
     'glmvx_check_device_error': ([_PI32], _I32),
     'glmvx_device_error_address': ([C.POINTER(_P)], _I32),
-    'glmvx_host_device_pointer': ([C.POINTER(_P), _P], _I32),
-    'glmvx_copy_kernel': ([_P, _P, _U64, _P], _I32),
     'glmvx_packed_gemv': ([_I32, _P, _P, _P, _I32, _I32, _P], _I32),
     'glmvx_packed_gemm': ([_I32, _P, _P, _P, _I32, _I32, _I32, _P], _I32),
     'glmvx_packed_gemm_path': ([_I32, _P, _P, _P, _I32, _I32, _I32, _P, _PI32], _I32),

@@ -126,12 +126,6 @@ int32_t glmvx_check_device_error(int32_t *code);
 /* Device address of that word (4 bytes), for an asynchronous copy back with a
    step's outputs; nonzero means call glmvx_check_device_error. */
 int32_t glmvx_device_error_address(void **ptr);
-/* Device address of pinned host memory from glmvx_host_alloc (mapped). */
-int32_t glmvx_host_device_pointer(void **dev, void *host);
-/* Asynchronous copy by a kernel (16-byte aligned pointers from 16 bytes on;
-   either side may be mapped pinned host memory: the transfer then crosses
-   PCIe from the SMs). */
-int32_t glmvx_copy_kernel(void *dst, const void *src, uint64_t bytes, void *stream);
 
 /* Fused packed dequant + matvec: out[rows] = W[rows,cols] . x[cols].
  * Replaces glm_vx_packed_<kind> (kernels/packed.vx:154-470) for resident
