@@ -124,7 +124,9 @@ struct MmaFmt<FmtIQ1_S> {
     // (Eight copies, spreading also by row parity, measured no faster.)
     static constexpr int kTableBytes = 2048 * 16, kSubPerBlock = 8, kBlockBytes = 50;
     static constexpr bool kMins = false;
-    static constexpr int kFR = 2;  // 16-row fragments per warp (independent work to hide latency)
+    // 16-row fragments per warp (independent work to hide latency); long job
+    // lists take kFRLong (fewer, larger tiles), short ones kFR (balance).
+    static constexpr int kFR = 2, kFRLong = 3;
     // Byte lookup words for PRMT: nibble n = g+1 selects 8*g+1 (delta = +1/8)
     // or 8*g-1 (delta = -1/8) as int8.
     static constexpr uint32_t kLutPlus = 0x000901F9u, kLutMinus = 0x0007FFF7u;
@@ -143,28 +145,28 @@ struct MmaFmt<FmtIQ1_S> {
     }
     // This lane's copy of the codebook.
     __device__ static const uint8_t *table_for_lane(const uint8_t *table, int lane) { return table + 4 * (lane & 3); }
-    template <int C, int NB>
-    __device__ __forceinline__ static void chunk(const uint8_t *const (&p)[kFR][2], int t, const uint32_t (&b)[NB][2],
-                                                 float xs, const float *, const uint8_t *tab, float (&af)[kFR][4],
-                                                 float (&)[kFR][2]) {
+    template <int C, int NB, int FR>
+    __device__ __forceinline__ static void chunk(const uint8_t *const (&p)[FR][2], int t, const uint32_t (&b)[NB][2],
+                                                 float xs, const float *, const uint8_t *tab, float (&af)[FR][4],
+                                                 float (&)[FR][2]) {
         const int sh = 3 * t;
         const uint32_t hmask = 7u << sh, hmul = c_iq1s_hi_mul[t];
         constexpr uint32_t step = kLutMinus - kLutPlus;
         const uint32_t k14 = 14u, k1 = 1u;
         const uint32_t tab_s = smem_addr(tab);
-        const uint8_t *q[kFR][2], *qt[kFR][2];  // block C of rows g, g+8; its qs byte of group t
+        const uint8_t *q[FR][2], *qt[FR][2];  // block C of rows g, g+8; its qs byte of group t
 #pragma unroll
-        for (int f = 0; f < kFR; ++f)
+        for (int f = 0; f < FR; ++f)
 #pragma unroll
             for (int r = 0; r < 2; ++r) {
                 q[f][r] = p[f][r] + C * kBlockBytes;
                 qt[f][r] = q[f][r] + 2 + t;
             }
-        int ai[kFR][4] = {};
+        int ai[FR][4] = {};
 #pragma unroll
         for (int s = 0; s < 8; ++s)
 #pragma unroll
-        for (int f = 0; f < kFR; ++f) {
+        for (int f = 0; f < FR; ++f) {
             const uint32_t h0 = u16(q[f][0] + 34 + 2 * s), h1 = u16(q[f][1] + 34 + 2 * s);
             // entry (grid bits 3t..3t+2 of h, qs) at 4096*bits + 16*qs: index
             // 256*bits + qs, the grid bits taken in place and scaled by a
@@ -187,7 +189,7 @@ struct MmaFmt<FmtIQ1_S> {
             ai[f][3] += dl1 * c[3];
         }
 #pragma unroll
-        for (int f = 0; f < kFR; ++f) {
+        for (int f = 0; f < FR; ++f) {
             const float s0 = h2f(u16(p[f][0] + C * kBlockBytes)) * (0.125f * xs);
             const float s1 = h2f(u16(p[f][1] + C * kBlockBytes)) * (0.125f * xs);
             af[f][0] = fmaf(s0, static_cast<float>(ai[f][0]), af[f][0]);
@@ -254,10 +256,11 @@ struct MmaFmt<FmtQ8_0> {
     // Eight 34-byte blocks.  A block at an even index within the slice starts
     // 4-byte aligned (its bytes follow a 2-byte scale), one at an odd index
     // 2 bytes past alignment, so its bytes are.
-    template <int C, int NB>
-    __device__ __forceinline__ static void chunk(const uint8_t *const (&p)[kFR][2], int t, const uint32_t (&b)[NB][2],
-                                                 float xs, const float *, const uint8_t *, float (&afr)[kFR][4],
-                                                 float (&)[kFR][2]) {
+    template <int C, int NB, int FR>
+    __device__ __forceinline__ static void chunk(const uint8_t *const (&p)[FR][2], int t, const uint32_t (&b)[NB][2],
+                                                 float xs, const float *, const uint8_t *, float (&afr)[FR][4],
+                                                 float (&)[FR][2]) {
+        static_assert(FR == 1, "one 16-row fragment per warp");
         const uint8_t *p0 = p[0][0], *p1 = p[0][1];
         float(&af)[4] = afr[0];
 #pragma unroll
@@ -301,10 +304,11 @@ struct MmaFmt<FmtQ4_K> {
     __device__ __forceinline__ static int sel6(uint32_t lo, uint32_t hi, int j) {
         return static_cast<int>(((j < 4 ? lo : hi) >> (8 * (j & 3))) & 0xffu);
     }
-    template <int C, int NB>
-    __device__ __forceinline__ static void chunk(const uint8_t *const (&p)[kFR][2], int t, const uint32_t (&b)[NB][2],
-                                                 float xs, const float *sums, const uint8_t *, float (&afr)[kFR][4],
-                                                 float (&amr)[kFR][2]) {
+    template <int C, int NB, int FR>
+    __device__ __forceinline__ static void chunk(const uint8_t *const (&p)[FR][2], int t, const uint32_t (&b)[NB][2],
+                                                 float xs, const float *sums, const uint8_t *, float (&afr)[FR][4],
+                                                 float (&amr)[FR][2]) {
+        static_assert(FR == 1, "one 16-row fragment per warp");
         float(&af)[4] = afr[0];
         float(&am)[2] = amr[0];
         const uint8_t *q0 = p[0][0] + C * kBlockBytes, *q1 = p[0][1] + C * kBlockBytes;
@@ -455,19 +459,13 @@ __device__ __forceinline__ MmaJob job_at(const MmaJob &job0, const MmaJob *jobs,
 
 // W = 256-column chunks per warp column slice (1 or 2); NT = token pairs
 // per job (2: each decoded fragment is multiplied into two pairs, one 16-row
-// fragment per warp; job lists of IQ1_S only).
-template <class F, int NT>
-constexpr int mma_fragments() {
-    return NT == 2 ? 1 : MmaFmt<F>::kFR;
-}
-
-template <class F, int S, int RG, int W, int NT>
+// fragment per warp; job lists of IQ1_S only); FR = 16-row fragments per warp.
+template <class F, int S, int RG, int W, int NT, int FR>
 __global__ void __launch_bounds__((S * RG + 1) * 32, 1)
     mma_rows_kernel(MmaJob job0, const MmaJob *__restrict__ jobs, const int *njobs_dev, int max_jobs, int batch,
                     int rows_per_job, int cols, int row_bytes, int srow, int stages, int stage_stride,
                     const float *__restrict__ x_raw, int *err) {
     using MF = MmaFmt<F>;
-    constexpr int FR = mma_fragments<F, NT>();
     constexpr int NS = 2 * NT;                      // token slots per job
     constexpr int NW = S * RG, R = 16 * FR * RG;  // a warp owns FR 16-row fragments of the tile
     extern __shared__ __align__(128) uint8_t smem[];
@@ -700,7 +698,7 @@ __global__ void __launch_bounds__((S * RG + 1) * 32, 1)
 // ------------------------------------------------------------------- host ---
 
 struct MmaPlan {
-    int S = 0, RG = 0, W = 0, srow = 0, stages = 0, stage_stride = 0, grid = 0;
+    int S = 0, RG = 0, W = 0, FR = 0, srow = 0, stages = 0, stage_stride = 0, grid = 0;
     size_t smem = 0;
 };
 
@@ -732,6 +730,18 @@ static int mma_slice_chunks(int cols) {
     return 2;
 }
 
+// Fragments per warp: one with two token pairs per job; for IQ1_S job lists
+// of at least kMmaLongRows rows the larger tiles of kFRLong (measured faster
+// on the 32-token MoE layer, slower at one token).
+constexpr int64_t kMmaLongRows = 150000;
+template <class F>
+static int mma_plan_fragments(int pairs, int64_t max_rows) {
+    if (pairs == 2) return 1;
+    if constexpr (std::is_same_v<F, FmtIQ1_S>)
+        if (max_rows >= kMmaLongRows) return MmaFmt<F>::kFRLong;
+    return MmaFmt<F>::kFR;
+}
+
 template <class F>
 static bool plan_mma(int64_t max_rows, int64_t max_tiles_extra, int cols, int row_bytes, bool fused, int pairs,
                      MmaPlan &p) {
@@ -742,7 +752,8 @@ static bool plan_mma(int64_t max_rows, int64_t max_tiles_extra, int cols, int ro
     p.S = cols / (256 * p.W);
     if (!mma_slices_ok(p.S, p.W)) return false;
     p.RG = mma_row_groups(p.S, p.W);
-    const int R = 16 * (pairs == 2 ? 1 : MF::kFR) * p.RG;
+    p.FR = mma_plan_fragments<F>(pairs, max_rows);
+    const int R = 16 * p.FR * p.RG;
     // Shared-memory rows span an odd number of 16-byte units, so rows g = 0..7
     // of a fragment start in 8 different 4-bank groups.  Rows that already do
     // (IQ1_S: 400 or 1200 bytes) keep the global stride and arrive with one
@@ -765,12 +776,12 @@ static bool plan_mma(int64_t max_rows, int64_t max_tiles_extra, int cols, int ro
     return true;
 }
 
-template <class F, int S, int W, int NT>
-static int32_t launch_mma(const MmaPlan &p, const MmaJob &job0, const MmaJob *jobs, const int *njobs_dev,
-                          int max_jobs, int batch, int rows_per_job, int cols, int row_bytes, const float *x_raw,
-                          cudaStream_t stream) {
+template <class F, int S, int W, int NT, int FR>
+static int32_t launch_mma_fr(const MmaPlan &p, const MmaJob &job0, const MmaJob *jobs, const int *njobs_dev,
+                             int max_jobs, int batch, int rows_per_job, int cols, int row_bytes, const float *x_raw,
+                             cudaStream_t stream) {
     constexpr int RG = mma_row_groups(S, W);
-    auto kern = mma_rows_kernel<F, S, RG, W, NT>;
+    auto kern = mma_rows_kernel<F, S, RG, W, NT, FR>;
     static size_t configured = 0;  // per instantiation
     if (p.smem > configured) {
         GLMVX_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(p.smem)));
@@ -789,6 +800,23 @@ static int32_t launch_mma(const MmaPlan &p, const MmaJob &job0, const MmaJob *jo
     GLMVX_CUDA(cudaLaunchKernelEx(&cfg, kern, job0, jobs, njobs_dev, max_jobs, batch, rows_per_job, cols, row_bytes,
                                   p.srow, p.stages, p.stage_stride, x_raw, device_error_word()));
     return kOk;
+}
+
+template <class F, int S, int W, int NT>
+static int32_t launch_mma(const MmaPlan &p, const MmaJob &job0, const MmaJob *jobs, const int *njobs_dev,
+                          int max_jobs, int batch, int rows_per_job, int cols, int row_bytes, const float *x_raw,
+                          cudaStream_t stream) {
+    if constexpr (NT == 2) {
+        return launch_mma_fr<F, S, W, 2, 1>(p, job0, jobs, njobs_dev, max_jobs, batch, rows_per_job, cols, row_bytes,
+                                            x_raw, stream);
+    } else {
+        if constexpr (std::is_same_v<F, FmtIQ1_S>)
+            if (p.FR == MmaFmt<F>::kFRLong)
+                return launch_mma_fr<F, S, W, 1, MmaFmt<F>::kFRLong>(p, job0, jobs, njobs_dev, max_jobs, batch,
+                                                                    rows_per_job, cols, row_bytes, x_raw, stream);
+        return launch_mma_fr<F, S, W, 1, MmaFmt<F>::kFR>(p, job0, jobs, njobs_dev, max_jobs, batch, rows_per_job,
+                                                          cols, row_bytes, x_raw, stream);
+    }
 }
 
 template <class F, int NT>
