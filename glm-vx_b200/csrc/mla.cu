@@ -1,0 +1,504 @@
+// Absorbed-MLA decode attention over DSA-selected compressed KV rows.
+//
+// Contract of the reference's fused entry (GLMKernels.mla_decode,
+// gpu/runtime.py:896-915, kernels glm_vx_gpu_mla_partial / _merge,
+// gpu/kernels.vx:204-310; model use glm_vx/model.py:209-221): for each head h
+//   s_j   = scale * (q_latent[h] . latent[t_j] + q_rope[h] . rope[t_j])
+//   out[h] = sum_j softmax(s)_j * latent[t_j]
+// over the selected token ids t_j = selected[h * selection_stride + j]
+// (j < count; ids outside [0, tokens) are skipped), the latent serving as
+// both key and value.  f32 throughout with an online (running max) softmax
+// per partition and a stable merge of the partitions.
+//
+// Layout here: a CTA takes a contiguous range (a split) of the selected ids;
+// the lanes of a warp hold interleaved columns of a head's query and running
+// output (column lane + 32i).  With one selection for all heads (the DSA
+// case: the indexer's top-k is per query token) mla_shared_kernel stages
+// tiles of the selected [latent | rope] rows in shared memory with cp.async,
+// three tiles in flight, and each of its 8 warps scores and accumulates two
+// heads against every staged row: a row crosses L2 once per 16 heads and
+// each shared-memory word read feeds two heads.  Per-head selections take
+// mla_partial_kernel, a warp per head reading its rows directly.  The merge
+// spreads each head over 32-column blocks and eight groups of splits.
+#include <algorithm>
+#include <cmath>
+
+#include "common.cuh"
+
+namespace glmvx {
+
+namespace {
+
+constexpr int kMlaHeadsPerCta = 8, kMlaMaxSplits = 64, kMlaBatch = 4;
+constexpr int kMlaTileRows = 8, kMlaStages = 3, kMlaMinRowsPerSplit = 16;
+constexpr int kMlaTargetCtas = 2 * 148;  // two CTAs per SM: one resident, one to follow
+constexpr int kMergeCols = 32, kMergeGroups = 8;
+
+__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async4(void *dst, const void *src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// Sums each of v[0..N) (N = 8 or 16) over the warp by halving exchanges (N
+// shuffles instead of 5N), then hands every lane all N totals.
+template <int N>
+__device__ __forceinline__ void warp_sum_n(float (&v)[N]) {
+    static_assert(N == 8 || N == 16, "8 or 16 values");
+    constexpr int kLow = N == 16 ? 2 : 4;  // lanes sharing one value after the halving
+    const int lane = threadIdx.x & 31;
+    constexpr int kSteps = N == 16 ? 4 : 3;
+#pragma unroll
+    for (int step = 0; step < kSteps; ++step) {
+        const int half = N >> (step + 1), bit = 16 >> step;
+        const bool up = lane & bit;
+#pragma unroll
+        for (int i = 0; i < half; ++i) {
+            const float send = up ? v[i] : v[i + half], keep = up ? v[i + half] : v[i];
+            v[i] = keep + __shfl_xor_sync(0xffffffffu, send, bit);
+        }
+    }
+#pragma unroll
+    for (int step = kSteps; step < 5; ++step) v[0] += __shfl_xor_sync(0xffffffffu, v[0], 16 >> step);
+    const float total = v[0];  // lane L: total of value L / kLow
+#pragma unroll
+    for (int i = 0; i < N; ++i) v[i] = __shfl_sync(0xffffffffu, total, kLow * i);
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// Cache row of selection position j of a shared list, -1 when j is past the
+// split or the id is outside [0, tokens).
+__device__ __forceinline__ int mla_row(const int32_t *selected, int j, int j1, int tokens) {
+    if (j >= j1) return -1;
+    const int t = selected ? __ldg(selected + j) : j;
+    return t >= 0 && t < tokens ? t : -1;
+}
+
+// One selection for all heads, rank <= 512.  RPL/PPL as below; HPW heads per
+// warp; VEC: rank and rope_dim multiples of 4 and both caches 16-byte
+// aligned (16-byte copies).  One CTA per SM: the compiler batches the
+// unrolled shared-memory loads, which needs more than 128 registers.
+template <int RPL, int PPL, int HPW, bool VEC>
+__global__ void __launch_bounds__(32 * kMlaHeadsPerCta, 1)
+    mla_shared_kernel(float *__restrict__ numerator, float *__restrict__ stats, const float *__restrict__ q_latent,
+                      const float *__restrict__ q_rope, const float *__restrict__ latent,
+                      const float *__restrict__ rope, const int32_t *__restrict__ selected, int heads, int rank,
+                      int rope_dim, int tokens, int count, int splits, float scale) {
+    constexpr int W = 32 * (RPL + PPL), kRowsFloats = kMlaTileRows * W;  // staged row: latent | rope
+    extern __shared__ __align__(16) float tile[];                       // [kMlaStages][kMlaTileRows][W]
+    grid_dependency_wait();
+    allow_dependent_launch();
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    constexpr int NV = kMlaTileRows * HPW;
+    int hs[HPW];
+#pragma unroll
+    for (int a = 0; a < HPW; ++a) hs[a] = static_cast<int>(blockIdx.y) * kMlaHeadsPerCta * HPW + kMlaHeadsPerCta * a + warp;
+    // Padding columns stay zero for the whole kernel.
+    for (int i = tid; i < kMlaStages * kRowsFloats; i += 32 * kMlaHeadsPerCta) tile[i] = 0.0f;
+    float q[HPW][RPL], qr[HPW][PPL], acc[HPW][RPL];
+#pragma unroll
+    for (int a = 0; a < HPW; ++a) {
+        const bool live = hs[a] < heads;
+#pragma unroll
+        for (int i = 0; i < RPL; ++i) {
+            const int d = lane + 32 * i;
+            q[a][i] = live && d < rank ? q_latent[static_cast<size_t>(hs[a]) * rank + d] : 0.0f;
+            acc[a][i] = 0.0f;
+        }
+#pragma unroll
+        for (int i = 0; i < PPL; ++i) {
+            const int d = lane + 32 * i;
+            qr[a][i] = live && d < rope_dim ? q_rope[static_cast<size_t>(hs[a]) * rope_dim + d] : 0.0f;
+        }
+    }
+    const int per = (count + splits - 1) / splits;
+    const int j0 = min(count, static_cast<int>(blockIdx.x) * per), j1 = min(count, j0 + per);
+    const int ntiles = (j1 - j0 + kMlaTileRows - 1) / kMlaTileRows;
+    __syncthreads();  // the zero fill lands before any copy into the tiles
+    // Stage tile tt: selected rows by copy, skipped rows (past the split, or
+    // ids out of range) as zeros so that stale values never meet a zero weight.
+    auto issue = [&](int tt) {
+        if (tt < ntiles) {
+            float *dst = tile + (tt % kMlaStages) * kRowsFloats;
+            const int jb = j0 + tt * kMlaTileRows;
+            const int unit = VEC ? 4 : 1, rq = rank / unit, cpr = rq + rope_dim / unit;
+            for (int c = tid; c < kMlaTileRows * cpr; c += 32 * kMlaHeadsPerCta) {
+                const int r = c / cpr, x = c - r * cpr;
+                const int t = mla_row(selected, jb + r, j1, tokens);
+                float *d = dst + r * W + (x < rq ? unit * x : 32 * RPL + unit * (x - rq));
+                const size_t row = static_cast<size_t>(max(t, 0));
+                const float *src = x < rq ? latent + row * rank + unit * x : rope + row * rope_dim + unit * (x - rq);
+                if (VEC) {
+                    if (t >= 0) cp_async16(d, src);
+                    else *reinterpret_cast<float4 *>(d) = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                } else {
+                    if (t >= 0) cp_async4(d, src);
+                    else *d = 0.0f;
+                }
+            }
+        }
+        cp_async_commit();
+    };
+#pragma unroll
+    for (int tt = 0; tt < kMlaStages - 1; ++tt) issue(tt);
+    float m[HPW], l[HPW];
+#pragma unroll
+    for (int a = 0; a < HPW; ++a) m[a] = -INFINITY, l[a] = 0.0f;
+    for (int tt = 0; tt < ntiles; ++tt) {
+        cp_async_wait<kMlaStages - 2>();
+        __syncthreads();  // tile tt complete for all threads; tile tt-1 no longer read
+        issue(tt + kMlaStages - 1);
+        const float *rows = tile + (tt % kMlaStages) * kRowsFloats;
+        const int jb = j0 + tt * kMlaTileRows;
+        float v[NV];  // v[8a + r]: head a . row r
+#pragma unroll
+        for (int r = 0; r < kMlaTileRows; ++r) {
+            float d[HPW];
+#pragma unroll
+            for (int a = 0; a < HPW; ++a) d[a] = 0.0f;
+#pragma unroll
+            for (int i = 0; i < RPL; ++i) {
+                const float x = rows[r * W + lane + 32 * i];
+#pragma unroll
+                for (int a = 0; a < HPW; ++a) d[a] = fmaf(q[a][i], x, d[a]);
+            }
+#pragma unroll
+            for (int i = 0; i < PPL; ++i) {
+                const float x = rows[r * W + 32 * RPL + lane + 32 * i];
+#pragma unroll
+                for (int a = 0; a < HPW; ++a) d[a] = fmaf(qr[a][i], x, d[a]);
+            }
+#pragma unroll
+            for (int a = 0; a < HPW; ++a) v[kMlaTileRows * a + r] = d[a];
+        }
+        warp_sum_n(v);
+        bool ok[kMlaTileRows];
+#pragma unroll
+        for (int r = 0; r < kMlaTileRows; ++r) ok[r] = mla_row(selected, jb + r, j1, tokens) >= 0;
+        float alpha[HPW], beta[HPW][kMlaTileRows];
+#pragma unroll
+        for (int a = 0; a < HPW; ++a) {
+            float mb = m[a];
+#pragma unroll
+            for (int r = 0; r < kMlaTileRows; ++r)
+                if (ok[r]) mb = fmaxf(mb, v[kMlaTileRows * a + r] * scale);
+            if (mb == -INFINITY) {  // nothing valid yet: no change
+                alpha[a] = 1.0f;
+#pragma unroll
+                for (int r = 0; r < kMlaTileRows; ++r) beta[a][r] = 0.0f;
+                continue;
+            }
+            alpha[a] = l[a] > 0.0f ? expf(m[a] - mb) : 0.0f;
+            float la = l[a] * alpha[a];
+#pragma unroll
+            for (int r = 0; r < kMlaTileRows; ++r) {
+                beta[a][r] = ok[r] ? expf(v[kMlaTileRows * a + r] * scale - mb) : 0.0f;
+                la += beta[a][r];
+            }
+            l[a] = la;
+            m[a] = mb;
+        }
+#pragma unroll
+        for (int i = 0; i < RPL; ++i) {
+            float x[kMlaTileRows];
+#pragma unroll
+            for (int r = 0; r < kMlaTileRows; ++r) x[r] = rows[r * W + lane + 32 * i];
+#pragma unroll
+            for (int a = 0; a < HPW; ++a) {
+                float y = acc[a][i] * alpha[a];
+#pragma unroll
+                for (int r = 0; r < kMlaTileRows; ++r) y = fmaf(beta[a][r], x[r], y);
+                acc[a][i] = y;
+            }
+        }
+    }
+    cp_async_wait<0>();
+#pragma unroll
+    for (int a = 0; a < HPW; ++a) {
+        if (hs[a] >= heads) continue;
+        const size_t task = static_cast<size_t>(blockIdx.x) * heads + hs[a];
+#pragma unroll
+        for (int i = 0; i < RPL; ++i) {
+            const int d = lane + 32 * i;
+            if (d < rank) numerator[task * rank + d] = acc[a][i];
+        }
+        if (lane == 0) {
+            stats[task * 2] = m[a];
+            stats[task * 2 + 1] = l[a];
+        }
+    }
+}
+
+// RPL = rank columns per lane (rank <= 32*RPL), PPL = rope columns per lane.
+template <int RPL, int PPL>
+__global__ void __launch_bounds__(32 * kMlaHeadsPerCta)
+    mla_partial_kernel(float *__restrict__ numerator, float *__restrict__ stats, const float *__restrict__ q_latent,
+                       const float *__restrict__ q_rope, const float *__restrict__ latent,
+                       const float *__restrict__ rope, const int32_t *__restrict__ selected, int heads, int rank,
+                       int rope_dim, int tokens, int count, int stride, int splits, float scale) {
+    grid_dependency_wait();
+    allow_dependent_launch();
+    const int lane = threadIdx.x & 31;
+    const int h = blockIdx.y * kMlaHeadsPerCta + (threadIdx.x >> 5);
+    const int split = blockIdx.x;
+    if (h >= heads) return;  // warp-uniform
+    float q[RPL], qr[PPL], acc[RPL];
+#pragma unroll
+    for (int i = 0; i < RPL; ++i) {
+        const int d = lane + 32 * i;
+        q[i] = d < rank ? q_latent[static_cast<size_t>(h) * rank + d] : 0.0f;
+        acc[i] = 0.0f;
+    }
+#pragma unroll
+    for (int i = 0; i < PPL; ++i) {
+        const int d = lane + 32 * i;
+        qr[i] = d < rope_dim ? q_rope[static_cast<size_t>(h) * rope_dim + d] : 0.0f;
+    }
+    const int per = (count + splits - 1) / splits;
+    const int j0 = split * per, j1 = min(count, j0 + per);
+    float m = -INFINITY, l = 0.0f;
+    for (int j = j0; j < j1; j += kMlaBatch) {
+        float lat[kMlaBatch][RPL], s[kMlaBatch];
+        bool ok[kMlaBatch];
+#pragma unroll
+        for (int b = 0; b < kMlaBatch; ++b) {
+            const int jj = j + b;
+            int t = -1;
+            if (jj < j1) t = selected ? selected[static_cast<size_t>(h) * stride + jj] : jj;
+            ok[b] = t >= 0 && t < tokens;  // uniform across the warp
+            float dot = 0.0f;
+#pragma unroll
+            for (int i = 0; i < RPL; ++i) {
+                const int d = lane + 32 * i;
+                lat[b][i] = ok[b] && d < rank ? latent[static_cast<size_t>(t) * rank + d] : 0.0f;
+                dot = fmaf(q[i], lat[b][i], dot);
+            }
+#pragma unroll
+            for (int i = 0; i < PPL; ++i) {
+                const int d = lane + 32 * i;
+                if (ok[b] && d < rope_dim) dot = fmaf(qr[i], rope[static_cast<size_t>(t) * rope_dim + d], dot);
+            }
+            s[b] = dot;
+        }
+#pragma unroll
+        for (int b = 0; b < kMlaBatch; ++b) s[b] = warp_sum(s[b]) * scale;
+        float mb = m;
+#pragma unroll
+        for (int b = 0; b < kMlaBatch; ++b)
+            if (ok[b]) mb = fmaxf(mb, s[b]);
+        if (mb == -INFINITY) continue;  // nothing valid yet
+        const float alpha = l > 0.0f ? expf(m - mb) : 0.0f;
+        float beta[kMlaBatch];
+#pragma unroll
+        for (int b = 0; b < kMlaBatch; ++b) beta[b] = ok[b] ? expf(s[b] - mb) : 0.0f;
+        l = l * alpha;
+#pragma unroll
+        for (int b = 0; b < kMlaBatch; ++b) l += beta[b];
+#pragma unroll
+        for (int i = 0; i < RPL; ++i) {
+            float v = acc[i] * alpha;
+#pragma unroll
+            for (int b = 0; b < kMlaBatch; ++b) v = fmaf(beta[b], lat[b][i], v);
+            acc[i] = v;
+        }
+        m = mb;
+    }
+    const size_t task = static_cast<size_t>(split) * heads + h;
+#pragma unroll
+    for (int i = 0; i < RPL; ++i) {
+        const int d = lane + 32 * i;
+        if (d < rank) numerator[task * rank + d] = acc[i];
+    }
+    if (lane == 0) {
+        stats[task * 2] = m;
+        stats[task * 2 + 1] = l;
+    }
+}
+
+// Grid (heads, rank / 32): per split a factor e^(m_s - max) over the splits
+// with mass (warp 0), then warp g sums splits g, g + 8, ... of 32 columns
+// and the eight partial sums are added in group order.
+__global__ void __launch_bounds__(32 * kMergeGroups)
+    mla_merge_kernel(float *__restrict__ out, const float *__restrict__ numerator, const float *__restrict__ stats,
+                     int heads, int rank, int splits) {
+    __shared__ float f[kMlaMaxSplits];
+    __shared__ float part[kMergeGroups][kMergeCols];
+    __shared__ float s_den;
+    grid_dependency_wait();
+    allow_dependent_launch();
+    const int h = blockIdx.x, tid = threadIdx.x, lane = tid & 31, g = tid >> 5;
+    if (g == 0) {
+        float mx = -INFINITY;
+        for (int s = lane; s < splits; s += 32) {
+            const size_t task = static_cast<size_t>(s) * heads + h;
+            if (stats[task * 2 + 1] > 0.0f) mx = fmaxf(mx, stats[task * 2]);
+        }
+        mx = warp_max(mx);
+        float den = 0.0f;
+        for (int s = lane; s < splits; s += 32) {
+            const size_t task = static_cast<size_t>(s) * heads + h;
+            const float ls = stats[task * 2 + 1];
+            const float e = ls > 0.0f ? expf(stats[task * 2] - mx) : -1.0f;  // -1: no mass
+            f[s] = e;
+            if (ls > 0.0f) den = fmaf(ls, e, den);
+        }
+        den = warp_sum(den);
+        if (lane == 0) s_den = den;
+    }
+    __syncthreads();
+    const int c = blockIdx.y * kMergeCols + lane;
+    float sum = 0.0f;
+    if (c < rank) {
+#pragma unroll 4
+        for (int s = g; s < splits; s += kMergeGroups)
+            if (f[s] >= 0.0f) sum = fmaf(numerator[(static_cast<size_t>(s) * heads + h) * rank + c], f[s], sum);
+    }
+    part[g][lane] = sum;
+    __syncthreads();
+    if (g == 0 && c < rank) {
+        float tot = 0.0f;
+#pragma unroll
+        for (int i = 0; i < kMergeGroups; ++i) tot += part[i][lane];
+        const float den = s_den;
+        out[static_cast<size_t>(h) * rank + c] = den > 0.0f ? tot / den : 0.0f;
+    }
+}
+
+// Heads per CTA: two per warp in the shared-selection kernel (rank <= 512),
+// one per warp in mla_partial_kernel.
+int mla_shared_heads(int rank) { return kMlaHeadsPerCta * (rank <= 512 ? 2 : 1); }
+
+// Splits: about two resident CTAs per SM over the head groups, at least
+// kMlaMinRowsPerSplit rows each, at most kMlaMaxSplits.
+int mla_splits(int heads, int rank, int count) {
+    const int per_cta = mla_shared_heads(rank);
+    const int groups = (heads + per_cta - 1) / per_cta;
+    const int want = (kMlaTargetCtas + groups - 1) / groups;
+    const int most = std::max(1, (count + kMlaMinRowsPerSplit - 1) / kMlaMinRowsPerSplit);
+    return std::max(1, std::min({kMlaMaxSplits, want, most}));
+}
+
+template <int RPL, int PPL, int HPW, bool VEC>
+int32_t launch_shared(dim3 grid, cudaStream_t st, float *numerator, float *stats, const float *q_latent,
+                      const float *q_rope, const float *latent, const float *rope, const int32_t *selected,
+                      int heads, int rank, int rope_dim, int tokens, int count, int splits, float scale) {
+    constexpr int bytes = kMlaStages * kMlaTileRows * 32 * (RPL + PPL) * 4;
+    static const cudaError_t attr =
+        cudaFuncSetAttribute(mla_shared_kernel<RPL, PPL, HPW, VEC>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (attr != cudaSuccess) return set_error("mla_shared smem: %s", cudaGetErrorString(attr)), kCudaError;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(32 * kMlaHeadsPerCta);
+    cfg.dynamicSmemBytes = bytes;
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    GLMVX_CUDA(cudaLaunchKernelEx(&cfg, mla_shared_kernel<RPL, PPL, HPW, VEC>, numerator, stats, q_latent, q_rope, latent,
+                                  rope, selected, heads, rank, rope_dim, tokens, count, splits, scale));
+    return kOk;
+}
+
+template <class K>
+int32_t launch_pdl(K kern, dim3 grid, dim3 block, cudaStream_t stream, auto... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    GLMVX_CUDA(cudaLaunchKernelEx(&cfg, kern, args...));
+    return kOk;
+}
+
+}  // namespace
+
+}  // namespace glmvx
+
+using namespace glmvx;
+
+// Scratch of glmvx_mla_decode: per (split, head) the partial output row and
+// its (max, mass).
+GLMVX_EXPORT int64_t glmvx_mla_scratch_bytes(int32_t heads, int32_t rank, int32_t count) {
+    if (heads <= 0 || rank <= 0 || count < 0) return -1;
+    const int64_t splits = mla_splits(heads, rank, count);
+    return 4 * splits * heads * (static_cast<int64_t>(rank) + 2);
+}
+
+// out[heads][rank]; q_latent [heads][rank], q_rope [heads][rope_dim], cache
+// rows latent [tokens][rank] and rope [tokens][rope_dim]; selected ids
+// [heads][selection_stride] (stride 0: one list for all heads; nullptr: the
+// first `count` tokens).  rank <= 1024, rope_dim <= 128.
+GLMVX_EXPORT int32_t glmvx_mla_decode(float *out, const float *q_latent, const float *q_rope,
+                                      const float *cache_latent, const float *cache_rope, const int32_t *selected,
+                                      int32_t heads, int32_t rank, int32_t rope_dim, int32_t tokens, int32_t count,
+                                      int32_t selection_stride, float scale, void *scratch, uint64_t scratch_bytes,
+                                      void *stream) {
+    if (heads <= 0 || rank <= 0 || rank > 1024 || rope_dim < 0 || rope_dim > 128 || tokens < 0 || count < 0 ||
+        selection_stride < 0 || !(scale > 0.0f) || !std::isfinite(scale)) {
+        set_error("mla_decode: invalid dimensions or scale");
+        return kInvalid;
+    }
+    if (!selected && count > tokens) {
+        set_error("mla_decode: count exceeds tokens without a selection");
+        return kInvalid;
+    }
+    const int splits = mla_splits(heads, rank, count);
+    const int64_t need = glmvx_mla_scratch_bytes(heads, rank, count);
+    if (!scratch || static_cast<int64_t>(scratch_bytes) < need || (reinterpret_cast<uintptr_t>(scratch) & 15)) {
+        set_error("mla_decode: scratch needs %lld bytes, 16-byte aligned", static_cast<long long>(need));
+        return kInvalid;
+    }
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    float *numerator = static_cast<float *>(scratch);
+    float *stats = numerator + static_cast<size_t>(splits) * heads * rank;
+    int32_t rc;
+    const int ppl = (rope_dim + 31) / 32;
+    if ((selection_stride == 0 || !selected) && rank <= 512) {  // one selection for every head
+        const int per_cta = mla_shared_heads(rank);
+        const dim3 grid(splits, (heads + per_cta - 1) / per_cta);
+        const bool vec = rank % 4 == 0 && rope_dim % 4 == 0 && (reinterpret_cast<uintptr_t>(cache_latent) & 15) == 0 &&
+                         (rope_dim == 0 || (reinterpret_cast<uintptr_t>(cache_rope) & 15) == 0);
+#define GLMVX_MLA_SHARED(R, P, H)                                                                                   \
+    (vec ? launch_shared<R, P, H, true>(grid, st, numerator, stats, q_latent, q_rope, cache_latent, cache_rope, selected, \
+                                     heads, rank, rope_dim, tokens, count, splits, scale)                           \
+         : launch_shared<R, P, H, false>(grid, st, numerator, stats, q_latent, q_rope, cache_latent, cache_rope,        \
+                                      selected, heads, rank, rope_dim, tokens, count, splits, scale))
+        rc = ppl <= 2 ? GLMVX_MLA_SHARED(16, 2, 2) : GLMVX_MLA_SHARED(16, 4, 2);
+#undef GLMVX_MLA_SHARED
+    } else {
+        const dim3 grid(splits, (heads + kMlaHeadsPerCta - 1) / kMlaHeadsPerCta), block(32 * kMlaHeadsPerCta);
+        if (rank <= 512) {
+            rc = ppl <= 2 ? launch_pdl(mla_partial_kernel<16, 2>, grid, block, st, numerator, stats, q_latent, q_rope,
+                                       cache_latent, cache_rope, selected, heads, rank, rope_dim, tokens, count,
+                                       selection_stride, splits, scale)
+                          : launch_pdl(mla_partial_kernel<16, 4>, grid, block, st, numerator, stats, q_latent, q_rope,
+                                       cache_latent, cache_rope, selected, heads, rank, rope_dim, tokens, count,
+                                       selection_stride, splits, scale);
+        } else {
+            rc = launch_pdl(mla_partial_kernel<32, 4>, grid, block, st, numerator, stats, q_latent, q_rope,
+                            cache_latent, cache_rope, selected, heads, rank, rope_dim, tokens, count, selection_stride,
+                            splits, scale);
+        }
+    }
+    if (rc) return rc;
+    return launch_pdl(mla_merge_kernel, dim3(heads, (rank + kMergeCols - 1) / kMergeCols), dim3(32 * kMergeGroups),
+                      st, out, const_cast<const float *>(numerator), const_cast<const float *>(stats), heads, rank,
+                      splits);
+}

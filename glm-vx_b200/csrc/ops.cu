@@ -397,23 +397,211 @@ __global__ void __launch_bounds__(1024)
     for (int i = threadIdx.x; i < k; i += blockDim.x) indices[i] = static_cast<int32_t>(keys[i] & 0xffffffffu);
 }
 
-// ---- DSA index scores (kernels/kernels.vx:404-421): one warp per token.
-__global__ void __launch_bounds__(256)
+// ---- top-k of many scores by radix selection (same order as topk_kernel):
+// the descending-score key of each score (topk_key's high word) is selected
+// 8 bits at a time down to the k-th smallest key T; the keys below T and the
+// lowest-index keys equal to T (stable ties) are gathered and sorted as
+// composite (key, index) words.  One CTA, k <= kTopkSelectMaxK.  With STAGED
+// the n keys are computed once into shared memory (n <= kTopkStagedScores)
+// and every pass reads them there; otherwise each pass re-reads the scores.
+constexpr int kTopkSelectMaxK = 4096, kTopkSelectThreads = 1024, kTopkStagedScores = 46 * 1024;
+
+__device__ __forceinline__ uint32_t topk_desc(float v) { return static_cast<uint32_t>(topk_key(v, 0) >> 32); }
+
+template <bool STAGED>
+__global__ void __launch_bounds__(kTopkSelectThreads)
+    topk_select_kernel(int32_t *indices, const float *scores, int n, int k) {
+    extern __shared__ uint32_t staged[];
+    __shared__ uint64_t sel[kTopkSelectMaxK];
+    __shared__ int hist[256];
+    __shared__ int s_warp[kTopkSelectThreads / 32];
+    __shared__ uint32_t s_prefix;
+    __shared__ int s_rank, s_below, s_ties;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const uint32_t lanes_below = (1u << lane) - 1u;
+    auto key_at = [&](int i) -> uint32_t { return STAGED ? staged[i] : topk_desc(__ldg(scores + i)); };
+    if (STAGED) {
+#pragma unroll 8
+        for (int i = tid; i < n; i += kTopkSelectThreads) staged[i] = topk_desc(__ldg(scores + i));
+    }
+    uint32_t prefix = 0, mask = 0;
+    int rank = k;  // 1-based position of the k-th key among those matching prefix
+    for (int shift = 24; shift >= 0; shift -= 8) {
+        if (tid < 256) hist[tid] = 0;
+        __syncthreads();
+        // Keys cluster in few digits (the exponent byte first): lanes with the
+        // same digit add together, one atomic per distinct digit per warp.
+        for (int i0 = tid - lane; i0 < n; i0 += kTopkSelectThreads) {
+            const int i = i0 + lane;
+            const uint32_t key = i < n ? key_at(i) : 0u;
+            const bool take = i < n && (key & mask) == prefix;
+            const int digit = take ? static_cast<int>((key >> shift) & 255) : 256;
+            const uint32_t same = __match_any_sync(0xffffffffu, digit);
+            if (take && lane == __ffs(same) - 1) atomicAdd(&hist[digit], __popc(same));
+        }
+        __syncthreads();
+        // The digit holding the rank-th key: a block scan of the 256 counts.
+        int count = 0, incl = 0;
+        if (tid < 256) {
+            count = incl = hist[tid];
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int y = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= o) incl += y;
+            }
+            if (lane == 31) s_warp[warp] = incl;
+        }
+        __syncthreads();
+        if (tid < 256) {
+            for (int w = 0; w < warp; ++w) incl += s_warp[w];
+            const int excl = incl - count;
+            if (excl < rank && rank <= incl) {  // exactly one digit: rank >= 1 and the total covers rank
+                s_prefix = prefix | (static_cast<uint32_t>(tid) << shift);
+                s_rank = rank - excl;
+            }
+        }
+        __syncthreads();
+        prefix = s_prefix;
+        rank = s_rank;
+        mask |= 255u << shift;
+    }
+    // prefix = T: the k - rank keys below T, then `rank` of the keys equal to
+    // T.  Positions within sel are arbitrary; the final sort orders them.
+    if (tid == 0) s_below = s_ties = 0;
+    __syncthreads();
+    int ties = 0;
+    for (int i0 = tid - lane; i0 < n; i0 += kTopkSelectThreads) {
+        const int i = i0 + lane;
+        const uint32_t key = i < n ? key_at(i) : ~0u;
+        const uint32_t below = __ballot_sync(0xffffffffu, i < n && key < prefix);
+        ties += i < n && key == prefix;
+        if (below) {
+            int base = 0;
+            if (lane == 0) base = atomicAdd(&s_below, __popc(below));
+            base = __shfl_sync(0xffffffffu, base, 0);
+            if (below >> lane & 1u)
+                sel[base + __popc(below & lanes_below)] = (static_cast<uint64_t>(key) << 32) | static_cast<uint32_t>(i);
+        }
+    }
+    ties = static_cast<int>(warp_sum(static_cast<float>(ties)));  // < 2^24: exact
+    if (lane == 0 && ties) atomicAdd(&s_ties, ties);
+    __syncthreads();
+    const uint64_t tkey = static_cast<uint64_t>(prefix) << 32;
+    if (s_ties == rank) {  // every key equal to T is taken
+        if (tid == 0) s_below = k - rank;
+        __syncthreads();
+        for (int i0 = tid - lane; i0 < n; i0 += kTopkSelectThreads) {
+            const int i = i0 + lane;
+            const uint32_t tie = __ballot_sync(0xffffffffu, i < n && key_at(i) == prefix);
+            if (tie) {
+                int base = 0;
+                if (lane == 0) base = atomicAdd(&s_below, __popc(tie));
+                base = __shfl_sync(0xffffffffu, base, 0);
+                if (tie >> lane & 1u) sel[base + __popc(tie & lanes_below)] = tkey | static_cast<uint32_t>(i);
+            }
+        }
+    } else {  // the lowest-index `rank` ties: chunks of the block in index order
+        int taken = 0;
+        for (int c0 = 0; c0 < n && taken < rank; c0 += kTopkSelectThreads) {
+            const int i = c0 + tid;
+            const bool is_tie = i < n && key_at(i) == prefix;
+            const uint32_t tie = __ballot_sync(0xffffffffu, is_tie);
+            if (lane == 0) s_warp[warp] = __popc(tie);
+            __syncthreads();
+            int before = taken + __popc(tie & lanes_below), total = 0;
+            for (int w = 0; w < kTopkSelectThreads / 32; ++w) {
+                before += w < warp ? s_warp[w] : 0;
+                total += s_warp[w];
+            }
+            if (is_tie && before < rank) sel[k - rank + before] = tkey | static_cast<uint32_t>(i);
+            taken += total;
+            __syncthreads();
+        }
+    }
+    int k2 = 1;
+    while (k2 < k) k2 <<= 1;
+    for (int i = k + tid; i < k2; i += kTopkSelectThreads) sel[i] = ~0ull;
+    __syncthreads();
+    bitonic_sort(sel, k2);
+    for (int i = tid; i < k; i += kTopkSelectThreads) indices[i] = static_cast<int32_t>(sel[i] & 0xffffffffu);
+}
+
+// ---- DSA index scores (kernels/kernels.vx:404-421): score_t = sum_h w_h *
+// relu(scale * q_h . k_t).  One thread per token: a block of 32 query heads x
+// up to 256 columns sits in shared memory (read as broadcasts, four columns
+// per load with VEC), each thread streams its key row in 16-column pieces and
+// keeps one running dot per head of the block in registers.  VEC: dim a
+// multiple of 16 and keys 16-byte aligned.
+constexpr int kIndexHeadBlock = 32, kIndexDimBlock = 256, kIndexThreads = 128;
+
+template <bool VEC>
+__global__ void __launch_bounds__(kIndexThreads)
     index_scores_kernel(float *out, const float *q, const float *keys, const float *w, int tokens, int heads,
                         int dim, float qk_scale) {
-    const int t = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
-    if (t >= tokens) return;
-    const float *kr = keys + static_cast<size_t>(t) * dim;
+    __shared__ __align__(16) float sq[kIndexHeadBlock * kIndexDimBlock];
+    const int t = blockIdx.x * kIndexThreads + threadIdx.x;
+    const bool live = t < tokens;
+    const float *kr = keys + static_cast<size_t>(live ? t : 0) * dim;
     float total = 0.0f;
-    for (int h = 0; h < heads; ++h) {
-        const float *qh = q + static_cast<size_t>(h) * dim;
-        float dot = 0.0f;
-        for (int d = lane; d < dim; d += 32) dot = fmaf(qh[d], kr[d], dot);
-        dot = warp_sum(dot);
-        const float s = dot * qk_scale;
-        if (s > 0.0f) total = fmaf(w[h], s, total);
+    for (int h0 = 0; h0 < heads; h0 += kIndexHeadBlock) {
+        const int nh = min(kIndexHeadBlock, heads - h0);
+        float dot[kIndexHeadBlock];
+#pragma unroll
+        for (int h = 0; h < kIndexHeadBlock; ++h) dot[h] = 0.0f;
+        for (int c0 = 0; c0 < dim; c0 += kIndexDimBlock) {
+            const int nc = min(kIndexDimBlock, dim - c0);
+            __syncthreads();  // the previous block of q is no longer read
+            for (int i = threadIdx.x; i < nh * nc; i += kIndexThreads) {
+                const int h = i / nc, c = i - h * nc;
+                sq[h * kIndexDimBlock + c] = q[static_cast<size_t>(h0 + h) * dim + c0 + c];
+            }
+            __syncthreads();
+            if (!live) continue;
+            for (int d = 0; d < nc; d += 16) {
+                float kv[16];
+                if (VEC) {
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const float4 v = __ldg(reinterpret_cast<const float4 *>(kr + c0 + d) + i);
+                        kv[4 * i] = v.x, kv[4 * i + 1] = v.y, kv[4 * i + 2] = v.z, kv[4 * i + 3] = v.w;
+                    }
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) kv[i] = d + i < nc ? __ldg(kr + c0 + d + i) : 0.0f;
+                }
+#pragma unroll
+                for (int h = 0; h < kIndexHeadBlock; ++h) {
+                    if (h < nh) {
+                        const float *qh = sq + h * kIndexDimBlock + d;
+                        float acc = dot[h];
+                        if (VEC) {
+#pragma unroll
+                            for (int i = 0; i < 4; ++i) {
+                                const float4 a = reinterpret_cast<const float4 *>(qh)[i];
+                                acc = fmaf(a.x, kv[4 * i], acc);
+                                acc = fmaf(a.y, kv[4 * i + 1], acc);
+                                acc = fmaf(a.z, kv[4 * i + 2], acc);
+                                acc = fmaf(a.w, kv[4 * i + 3], acc);
+                            }
+                        } else {
+#pragma unroll
+                            for (int i = 0; i < 16; ++i)
+                                if (d + i < nc) acc = fmaf(qh[i], kv[i], acc);
+                        }
+                        dot[h] = acc;
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int h = 0; h < kIndexHeadBlock; ++h) {
+            if (h < nh) {
+                const float s = dot[h] * qk_scale;
+                if (s > 0.0f) total = fmaf(__ldg(w + h0 + h), s, total);
+            }
+        }
     }
-    if (lane == 0) out[t] = total;
+    if (live) out[t] = total;
 }
 
 // ---- single-query attention over all or selected tokens
@@ -593,6 +781,17 @@ GLMVX_EXPORT int32_t glmvx_topk(int32_t *indices, const float *scores, int32_t n
     if (k == 0) return kOk;
     int n2 = 1;
     while (n2 < n) n2 <<= 1;
+    if (n2 > kTopkSmemKeys && k <= kTopkSelectMaxK) {  // many scores, bounded k: radix selection
+        if (n <= kTopkStagedScores) {
+            static const cudaError_t attr = cudaFuncSetAttribute(
+                topk_select_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTopkStagedScores * 4);
+            if (attr != cudaSuccess) return set_error("topk_select smem: %s", cudaGetErrorString(attr)), kCudaError;
+            topk_select_kernel<true><<<1, kTopkSelectThreads, n * 4, S_>>>(indices, scores, n, k);
+        } else {
+            topk_select_kernel<false><<<1, kTopkSelectThreads, 0, S_>>>(indices, scores, n, k);
+        }
+        return launch_status("topk_select_kernel");
+    }
     if (n2 > kTopkSmemKeys && !scratch) return set_error("topk needs scratch for n > %d", kTopkSmemKeys), kInvalid;
     topk_kernel<<<1, 1024, 0, S_>>>(indices, scores, n, k, static_cast<uint64_t *>(scratch), n2);
     return launch_status("topk_kernel");
@@ -601,7 +800,12 @@ GLMVX_EXPORT int32_t glmvx_topk(int32_t *indices, const float *scores, int32_t n
 GLMVX_EXPORT int32_t glmvx_index_scores(float *out, const float *q, const float *keys, const float *w,
                                         int32_t tokens, int32_t heads, int32_t dim, float qk_scale, void *stream) {
     if (tokens < 0 || heads <= 0 || dim <= 0) return set_error("index_scores dims"), kInvalid;
-    if (tokens) index_scores_kernel<<<(tokens + 7) / 8, 256, 0, S_>>>(out, q, keys, w, tokens, heads, dim, qk_scale);
+    if (tokens) {
+        const bool vec = dim % 16 == 0 && (reinterpret_cast<uintptr_t>(keys) & 15) == 0;
+        const int grid = (tokens + kIndexThreads - 1) / kIndexThreads;
+        if (vec) index_scores_kernel<true><<<grid, kIndexThreads, 0, S_>>>(out, q, keys, w, tokens, heads, dim, qk_scale);
+        else index_scores_kernel<false><<<grid, kIndexThreads, 0, S_>>>(out, q, keys, w, tokens, heads, dim, qk_scale);
+    }
     return launch_status("index_scores_kernel");
 }
 

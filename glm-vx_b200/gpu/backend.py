@@ -401,6 +401,37 @@ class GPUBackend:
         self._call('glmvx_index_scores', od, qd, kd, wd, tokens, heads, dim, scale, self.stream.handle)
         return self._fetch(offs, [out])[0]
 
+    def compressed_attention(self, q_latent, q_rope, latents, rope_keys, scale):
+        """Fused all-head attention over already-selected compressed KV rows,
+        the contract of the reference's GPUBackend.compressed_attention
+        (gpu/backend.py:233-254, used by glm_vx/model.py:209-221):
+        out[h] = softmax(scale * (q_latent[h] . latents^T + q_rope[h] .
+        rope_keys^T)) . latents, float32 [heads, rank]."""
+        arrs = [np.ascontiguousarray(a, dtype=np.float32) for a in (q_latent, q_rope, latents, rope_keys)]
+        q_latent, q_rope, latents, rope_keys = arrs
+        try:
+            scale = np.float32(scale)
+        except (TypeError, ValueError):
+            raise ValueError('MLA scale must be positive and finite') from None
+        if any(a.ndim != 2 for a in arrs):
+            raise ValueError('MLA expects matrices')
+        heads, rank = q_latent.shape
+        count, rdim = latents.shape[0], q_rope.shape[1]
+        if (rank > 1024 or rdim > 128 or q_rope.shape[0] != heads or latents.shape[1] != rank
+                or rope_keys.shape != (count, rdim)):
+            raise ValueError('MLA shape mismatch')
+        if not np.isfinite(scale) or scale <= 0:
+            raise ValueError('MLA scale must be positive and finite')
+        out = np.empty((heads, rank), np.float32)
+        if heads == 0 or rank == 0:
+            return out
+        self._begin()
+        need = int(self.lib.glmvx_mla_scratch_bytes(heads, rank, count))
+        (qd, rd, ld, kd), (od, sd), offs = self._stage(arrs, [out.nbytes, need])
+        self._call('glmvx_mla_decode', od, qd, rd, ld, kd, None, heads, rank, rdim, count, count, 0, float(scale), sd,
+                   need, self.stream.handle)
+        return self._fetch(offs[:1], [out])[0]
+
     def fp8_matvec(self, weight, scales, x):
         """FP8 E4M3FN block-scaled projection with the contract of the
         reference's GLMKernels.fp8_matvec (gpu/runtime.py:1031-1053):

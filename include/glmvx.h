@@ -171,6 +171,17 @@ int32_t glmvx_index_scores(float *out, const float *q, const float *keys, const 
 int32_t glmvx_attention(float *out, float *scratch, const float *q, const float *keys, const float *values,
                         const int32_t *selected, int32_t count, int32_t tokens, int32_t dim, int32_t value_dim,
                         float scale, int32_t *bad, void *stream);
+/* Absorbed-MLA decode over selected compressed KV rows, all heads
+   (GLMKernels.mla_decode, gpu/runtime.py:896-915; glm_vx/model.py:209-221):
+   out[h] = softmax_j(scale*(q_latent[h].latent[t_j] + q_rope[h].rope[t_j]))
+   . latent[t_j], t_j = selected[h*selection_stride + j] (ids outside
+   [0, tokens) skipped; selected NULL: t_j = j).  rank <= 1024, rope_dim <=
+   128; scratch of glmvx_mla_scratch_bytes(heads, rank, count) bytes. */
+int64_t glmvx_mla_scratch_bytes(int32_t heads, int32_t rank, int32_t count);
+int32_t glmvx_mla_decode(float *out, const float *q_latent, const float *q_rope, const float *cache_latent,
+                         const float *cache_rope, const int32_t *selected, int32_t heads, int32_t rank,
+                         int32_t rope_dim, int32_t tokens, int32_t count, int32_t selection_stride, float scale,
+                         void *scratch, uint64_t scratch_bytes, void *stream);
 
 /* Routed + shared MoE feed-forward layer (decode / small batches), device
  * pointers.  Replaces the per-expert Python loop of glm_vx/model.py:289-324

@@ -62,18 +62,29 @@ def test_f32_matvec_and_linear_batch(request, oracle, backend_name):
     np.testing.assert_allclose(b.linear_batch(w, x), oracle.linear_batch(w, x), **TOL)
 
 
-@pytest.mark.parametrize('n,k', [(4, 3), (100, 10), (4096, 2048), (40000, 2048)])
+@pytest.mark.parametrize('n,k', [(4, 3), (100, 10), (4096, 2048), (40000, 2048), (32768, 2048), (65536, 4096),
+                                 (5000, 1), (9000, 4097), (47104, 4096), (47105, 7)])
 def test_topk_exact(gpu_vx, oracle, n, k):
+    """Small inputs sort in shared memory; above 4096 scores (k <= 4096) the
+    radix selection runs, with the keys staged in shared memory up to 47104
+    scores and re-read from the scores above; all give the stable order of
+    the oracle."""
     rng = np.random.default_rng(n)
     scores = rng.integers(-50, 50, size=n).astype(np.float32)  # many ties
     assert gpu_vx.topk(scores, k).tolist() == oracle.topk(scores, k).tolist()
+    scores = rng.normal(size=n).astype(np.float32)
+    scores[::11] = 0.0
+    scores[::13] = -0.0  # -0 and +0 tie, lower index first
+    assert gpu_vx.topk(scores, k).tolist() == oracle.topk(scores, k).tolist()
 
 
-def test_index_scores(gpu_vx, oracle):
-    rng = np.random.default_rng(532)
-    q = rng.normal(size=(32, 128)).astype(np.float32)
-    keys = rng.normal(size=(777, 128)).astype(np.float32)
-    w = rng.normal(size=32).astype(np.float32) / 2
+@pytest.mark.parametrize('heads,dim', [(32, 128), (40, 100), (5, 300), (64, 64), (1, 1)])
+def test_index_scores(gpu_vx, oracle, heads, dim):
+    """Blocks of 32 heads x 256 columns, vector and scalar key loads."""
+    rng = np.random.default_rng(532 + heads + dim)
+    q = rng.normal(size=(heads, dim)).astype(np.float32)
+    keys = rng.normal(size=(777, dim)).astype(np.float32)
+    w = rng.normal(size=heads).astype(np.float32) / 2
     np.testing.assert_allclose(gpu_vx.index_scores(q, keys, w), oracle.index_scores(q, keys, w), **TOL)
 
 
