@@ -16,7 +16,9 @@ from DRAM.  Synthetic, seeded data: the reference publishes no dataset.
 Also reported (key `fused_gemv`): BASELINE config 0 (Q8_0 2048x6144, batch 1)
 and config 1 (Q4_K 6144x2048, batch 1/4/16/64) fused dequant-GEMV GB/s, and
 the FP8 E4M3 block-scaled projection (6144x6144, batch 1), rotating weight
-copies beyond L2.
+copies beyond L2.  Key `dsa_decode` (N=1): BASELINE config 3, the fused DSA
+decode attention (indexer over 32768 cached positions, top-2048, absorbed
+MLA with 64 heads x rank 512 + rope 64) for 1 and 16 queries.
 
 Arms:
   ours       device-resident timing (CUDA graph of the K timed steps, CUDA
@@ -406,6 +408,70 @@ def fused_gemv_sweep(rt, lib, dev, stream, steps, peak):
     return res
 
 
+DSA_CONTEXT, DSA_TOPK, DSA_HEADS, DSA_RANK, DSA_ROPE, DSA_IH, DSA_ID = 32768, 2048, 64, 512, 64, 32, 128
+
+
+def dsa_sweep(rt, lib, backend, stream, steps, peak):
+    """Config 3: fused DSA decode attention (gpu/dsa.py DSADecoder) for a
+    batch of 1 and 16 decode queries, each over its own resident compressed
+    cache of DSA_CONTEXT positions (f32 N(0,1)): indexer scores, stable
+    top-2048, absorbed MLA.  `us` is the device time of the fused decode
+    (a graph of launches, caches far beyond L2 for B=16; at B=1 the 23 MB of
+    keys and selected rows may partly stay in L2 between launches), `e2e_us`
+    one DSADecoder.step_pinned() call: inputs copied in from pinned memory,
+    the new rows appended, the decode, outputs copied back."""
+    from gpu.dsa import DSADecoder
+    rng = np.random.default_rng(3)
+    T = DSA_CONTEXT
+    lat = rng.normal(size=(T, DSA_RANK)).astype(np.float32)
+    rk = rng.normal(size=(T, DSA_ROPE)).astype(np.float32)
+    ik = rng.normal(size=(T, DSA_ID)).astype(np.float32)
+    # per query: every index key, the selected latent + rope rows, queries and outputs
+    per_query = 4 * (T * DSA_ID + DSA_TOPK * (DSA_RANK + DSA_ROPE) + DSA_HEADS * (2 * DSA_RANK + DSA_ROPE)
+                     + DSA_IH * (DSA_ID + 1) + T + DSA_TOPK)
+    fma_per_query = T * DSA_IH * DSA_ID + DSA_HEADS * DSA_TOPK * (2 * DSA_RANK + DSA_ROPE)
+    sm_clock = 1965e6
+    fp32_peak = backend.device.sm_count * 128 * 2 * sm_clock / 1e12  # nominal CUDA-core TFLOP/s
+    res = {}
+    for B in (1, 16):
+        dec = DSADecoder(backend, B, T)
+        warm = 3
+        reps = max(5, min(steps, 20))
+        n0 = T - (warm + reps + 2)
+        for i in range(B):
+            dec.load(i, lat[:n0], rk[:n0], ik[:n0])
+        io = dec.pinned_io()
+        for k in ('new_latent', 'new_rope', 'new_index_key', 'q_index'):
+            io[k][...] = rng.normal(size=io[k].shape)
+        io['q_latent'][...] = rng.normal(size=io['q_latent'].shape) * 0.05
+        io['q_rope'][...] = rng.normal(size=io['q_rope'].shape) * 0.05
+        io['head_weights'][...] = rng.normal(size=io['head_weights'].shape) * DSA_IH ** -0.5
+        for _ in range(warm):
+            dec.step_pinned()
+
+        def decode(i, dec=dec, B=B):
+            rt.check(lib, lib.glmvx_dsa_decode(
+                dec._ptr('out'), dec._ptr('selected'), dec._ptr('q_latent'), dec._ptr('q_rope'), dec._ptr('q_index'),
+                dec._ptr('head_weights'), dec.latents.ptr, dec.rope_keys.ptr, dec.index_keys.ptr, dec.lens_dev.ptr,
+                B, DSA_HEADS, DSA_RANK, DSA_ROPE, DSA_IH, DSA_ID, T, DSA_TOPK, dec.index_scale, dec.scale,
+                dec._scratch.ptr, dec._scratch_bytes, stream.handle), 'glmvx_dsa_decode')
+        us = graph_time(rt, stream, decode, reps) / reps * 1e3
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            dec.step_pinned()
+        e2e_us = (time.perf_counter() - t0) / reps * 1e6
+        backend.device.check_device_error()
+        alg = B * per_query
+        res[f'config3_b{B}'] = {
+            'us': us, 'queries_s': B / (us * 1e-6), 'e2e_us': e2e_us, 'e2e_queries_s': B / (e2e_us * 1e-6),
+            'gbs': alg / us / 1e3, 'frac_of_measured_hbm': alg / us / 1e3 / peak,
+            'fp32_tflops': 2 * B * fma_per_query / us / 1e6,
+            'frac_of_nominal_fp32': 2 * B * fma_per_query / us / 1e6 / fp32_peak,
+            'algorithmic_bytes': alg, 'context': T, 'topk': DSA_TOPK}
+        dec.close()
+    return res
+
+
 def expert_parallel_step(args, ranks, layer):
     """N>1: the same layer with its 256 experts sharded over the ranks
     (gpu/ep.py), TOKENS rows per rank; device time of the step (CUDA events on
@@ -530,6 +596,7 @@ def run_ours(args, ranks):
     e2e_value = ranks.world * TOKENS * e2e_steps / e2e_s
 
     gemv = fused_gemv_sweep(rt, lib, dev, stream, args.steps, peak)
+    dsa = dsa_sweep(rt, lib, backend, stream, args.steps, peak) if ranks.world == 1 else None
     ep = expert_parallel_step(args, ranks, layer) if ranks.world > 1 and EXPERTS % ranks.world == 0 else None
     line = {
         'metric': METRIC, 'value': value, 'unit': 'tok/s', 'n_gpus': ranks.world, 'steps': args.steps,
@@ -545,6 +612,7 @@ def run_ours(args, ranks):
                      'traffic': NCU_TRAFFIC, 'kernel': 'mma_rows_kernel<IQ1_S> gate+up job lists (tensor-core int8; two- and four-token jobs, two launches)',
                      'algorithmic_bytes_per_launch': gu_bytes, 'avg_launch_us': gu_us, 'peak_source': peak_kind},
         'fused_gemv': gemv,
+        **({'dsa_decode': dsa} if dsa else {}),
         **({'expert_parallel': ep} if ep else {}),
         'e2e': {'value': e2e_value, 'unit': 'tok/s', 'steps': e2e_steps,
                 'h2d_bytes_per_step': TOKENS * HIDDEN * 4, 'd2h_bytes_per_step': TOKENS * HIDDEN * 4 + 2 * TOKENS * TOPK * 4,

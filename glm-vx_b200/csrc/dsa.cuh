@@ -1,0 +1,20 @@
+// Batched DSA indexer launches (ops.cu) used by the fused decode in mla.cu.
+#pragma once
+#include <cstdint>
+
+#include <cuda_runtime.h>
+
+namespace glmvx {
+
+// scores[b][t] = sum_h w[b][h] relu(qk_scale q[b][h] . keys[b][t]) for t < lens[b]
+// (lens nullptr: `tokens` for every query); keys of query b at keys + b * key_stride.
+int32_t launch_index_scores_batch(float *out, const float *q, const float *keys, const float *w, int tokens,
+                                  int heads, int dim, float qk_scale, const int32_t *lens, int64_t key_stride,
+                                  int64_t out_stride, int batch, cudaStream_t stream);
+
+// indices[b][0:min(k, lens[b])] = stable descending top-k of scores[b][0:lens[b]],
+// the rest of indices[b][0:k] -1.  1 <= k <= 4096.
+int32_t launch_topk_batch(int32_t *indices, const float *scores, int n, int k, const int32_t *lens,
+                          int64_t score_stride, int out_stride, int batch, cudaStream_t stream);
+
+}  // namespace glmvx

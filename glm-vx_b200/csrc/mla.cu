@@ -24,6 +24,7 @@
 #include <cmath>
 
 #include "common.cuh"
+#include "dsa.cuh"
 
 namespace glmvx {
 
@@ -31,7 +32,7 @@ namespace {
 
 constexpr int kMlaHeadsPerCta = 8, kMlaMaxSplits = 64, kMlaBatch = 4;
 constexpr int kMlaTileRows = 8, kMlaStages = 3, kMlaMinRowsPerSplit = 16;
-constexpr int kMlaTargetCtas = 2 * 148;  // two CTAs per SM: one resident, one to follow
+constexpr int kMlaTargetCtas = 148;  // one wave: the shared kernel holds one CTA per SM
 constexpr int kMergeCols = 32, kMergeGroups = 8;
 
 __device__ __forceinline__ void cp_async16(void *dst, const void *src) {
@@ -77,6 +78,10 @@ __device__ __forceinline__ float warp_max(float v) {
     return v;
 }
 
+// Latent column of a lane's i-th value in mla_shared_kernel: four adjacent
+// columns per lane in each 128-column group, so rows are read as float4.
+__device__ __forceinline__ int latent_col(int i, int lane) { return 128 * (i >> 2) + 4 * lane + (i & 3); }
+
 // Cache row of selection position j of a shared list, -1 when j is past the
 // split or the id is outside [0, tokens).
 __device__ __forceinline__ int mla_row(const int32_t *selected, int j, int j1, int tokens) {
@@ -85,7 +90,9 @@ __device__ __forceinline__ int mla_row(const int32_t *selected, int j, int j1, i
     return t >= 0 && t < tokens ? t : -1;
 }
 
-// One selection for all heads, rank <= 512.  RPL/PPL as below; HPW heads per
+// One selection for all heads, rank <= 512.  RPL (a multiple of 4) latent
+// and PPL (2 or 4) rope values per lane, laid out as latent_col and
+// PPL * lane + i, read from the staged rows as float4 / float2; HPW heads per
 // warp; VEC: rank and rope_dim multiples of 4 and both caches 16-byte
 // aligned (16-byte copies).  One CTA per SM: the compiler batches the
 // unrolled shared-memory loads, which needs more than 128 registers.
@@ -94,11 +101,26 @@ __global__ void __launch_bounds__(32 * kMlaHeadsPerCta, 1)
     mla_shared_kernel(float *__restrict__ numerator, float *__restrict__ stats, const float *__restrict__ q_latent,
                       const float *__restrict__ q_rope, const float *__restrict__ latent,
                       const float *__restrict__ rope, const int32_t *__restrict__ selected, int heads, int rank,
-                      int rope_dim, int tokens, int count, int splits, float scale) {
+                      int rope_dim, int tokens, int count, int splits, float scale, const int32_t *__restrict__ lens,
+                      int64_t latent_stride, int64_t rope_stride, int64_t sel_stride) {
     constexpr int W = 32 * (RPL + PPL), kRowsFloats = kMlaTileRows * W;  // staged row: latent | rope
     extern __shared__ __align__(16) float tile[];                       // [kMlaStages][kMlaTileRows][W]
     grid_dependency_wait();
     allow_dependent_launch();
+    {  // query blockIdx.z of a batch: its own queries, cache rows, selection and length
+        const int bq = blockIdx.z;
+        if (lens) {
+            tokens = min(tokens, max(0, lens[bq]));
+            count = min(count, tokens);
+        }
+        q_latent += static_cast<size_t>(bq) * heads * rank;
+        q_rope += static_cast<size_t>(bq) * heads * rope_dim;
+        latent += bq * latent_stride;
+        rope += bq * rope_stride;
+        if (selected) selected += bq * sel_stride;
+        numerator += static_cast<size_t>(bq) * splits * heads * rank;
+        stats += static_cast<size_t>(bq) * splits * heads * 2;
+    }
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     constexpr int NV = kMlaTileRows * HPW;
     int hs[HPW];
@@ -112,13 +134,13 @@ __global__ void __launch_bounds__(32 * kMlaHeadsPerCta, 1)
         const bool live = hs[a] < heads;
 #pragma unroll
         for (int i = 0; i < RPL; ++i) {
-            const int d = lane + 32 * i;
+            const int d = latent_col(i, lane);
             q[a][i] = live && d < rank ? q_latent[static_cast<size_t>(hs[a]) * rank + d] : 0.0f;
             acc[a][i] = 0.0f;
         }
 #pragma unroll
         for (int i = 0; i < PPL; ++i) {
-            const int d = lane + 32 * i;
+            const int d = PPL * lane + i;
             qr[a][i] = live && d < rope_dim ? q_rope[static_cast<size_t>(hs[a]) * rope_dim + d] : 0.0f;
         }
     }
@@ -168,16 +190,25 @@ __global__ void __launch_bounds__(32 * kMlaHeadsPerCta, 1)
 #pragma unroll
             for (int a = 0; a < HPW; ++a) d[a] = 0.0f;
 #pragma unroll
-            for (int i = 0; i < RPL; ++i) {
-                const float x = rows[r * W + lane + 32 * i];
+            for (int g = 0; g < RPL / 4; ++g) {
+                const float4 x = *reinterpret_cast<const float4 *>(rows + r * W + 128 * g + 4 * lane);
 #pragma unroll
-                for (int a = 0; a < HPW; ++a) d[a] = fmaf(q[a][i], x, d[a]);
+                for (int a = 0; a < HPW; ++a) {
+                    d[a] = fmaf(q[a][4 * g], x.x, d[a]);
+                    d[a] = fmaf(q[a][4 * g + 1], x.y, d[a]);
+                    d[a] = fmaf(q[a][4 * g + 2], x.z, d[a]);
+                    d[a] = fmaf(q[a][4 * g + 3], x.w, d[a]);
+                }
             }
+            if constexpr (PPL == 2) {
+                const float2 x = *reinterpret_cast<const float2 *>(rows + r * W + 32 * RPL + 2 * lane);
 #pragma unroll
-            for (int i = 0; i < PPL; ++i) {
-                const float x = rows[r * W + 32 * RPL + lane + 32 * i];
+                for (int a = 0; a < HPW; ++a) d[a] = fmaf(qr[a][1], x.y, fmaf(qr[a][0], x.x, d[a]));
+            } else {
+                const float4 x = *reinterpret_cast<const float4 *>(rows + r * W + 32 * RPL + 4 * lane);
 #pragma unroll
-                for (int a = 0; a < HPW; ++a) d[a] = fmaf(qr[a][i], x, d[a]);
+                for (int a = 0; a < HPW; ++a)
+                    d[a] = fmaf(qr[a][3], x.w, fmaf(qr[a][2], x.z, fmaf(qr[a][1], x.y, fmaf(qr[a][0], x.x, d[a]))));
             }
 #pragma unroll
             for (int a = 0; a < HPW; ++a) v[kMlaTileRows * a + r] = d[a];
@@ -210,16 +241,23 @@ __global__ void __launch_bounds__(32 * kMlaHeadsPerCta, 1)
             m[a] = mb;
         }
 #pragma unroll
-        for (int i = 0; i < RPL; ++i) {
-            float x[kMlaTileRows];
+        for (int g = 0; g < RPL / 4; ++g) {
+            float4 x[kMlaTileRows];
 #pragma unroll
-            for (int r = 0; r < kMlaTileRows; ++r) x[r] = rows[r * W + lane + 32 * i];
+            for (int r = 0; r < kMlaTileRows; ++r)
+                x[r] = *reinterpret_cast<const float4 *>(rows + r * W + 128 * g + 4 * lane);
 #pragma unroll
             for (int a = 0; a < HPW; ++a) {
-                float y = acc[a][i] * alpha[a];
+                float y0 = acc[a][4 * g] * alpha[a], y1 = acc[a][4 * g + 1] * alpha[a];
+                float y2 = acc[a][4 * g + 2] * alpha[a], y3 = acc[a][4 * g + 3] * alpha[a];
 #pragma unroll
-                for (int r = 0; r < kMlaTileRows; ++r) y = fmaf(beta[a][r], x[r], y);
-                acc[a][i] = y;
+                for (int r = 0; r < kMlaTileRows; ++r) {
+                    y0 = fmaf(beta[a][r], x[r].x, y0);
+                    y1 = fmaf(beta[a][r], x[r].y, y1);
+                    y2 = fmaf(beta[a][r], x[r].z, y2);
+                    y3 = fmaf(beta[a][r], x[r].w, y3);
+                }
+                acc[a][4 * g] = y0, acc[a][4 * g + 1] = y1, acc[a][4 * g + 2] = y2, acc[a][4 * g + 3] = y3;
             }
         }
     }
@@ -230,7 +268,7 @@ __global__ void __launch_bounds__(32 * kMlaHeadsPerCta, 1)
         const size_t task = static_cast<size_t>(blockIdx.x) * heads + hs[a];
 #pragma unroll
         for (int i = 0; i < RPL; ++i) {
-            const int d = lane + 32 * i;
+            const int d = latent_col(i, lane);
             if (d < rank) numerator[task * rank + d] = acc[a][i];
         }
         if (lane == 0) {
@@ -337,6 +375,9 @@ __global__ void __launch_bounds__(32 * kMergeGroups)
     __shared__ float s_den;
     grid_dependency_wait();
     allow_dependent_launch();
+    out += static_cast<size_t>(blockIdx.z) * heads * rank;  // query of a batch
+    numerator += static_cast<size_t>(blockIdx.z) * splits * heads * rank;
+    stats += static_cast<size_t>(blockIdx.z) * splits * heads * 2;
     const int h = blockIdx.x, tid = threadIdx.x, lane = tid & 31, g = tid >> 5;
     if (g == 0) {
         float mx = -INFINITY;
@@ -379,12 +420,13 @@ __global__ void __launch_bounds__(32 * kMergeGroups)
 // one per warp in mla_partial_kernel.
 int mla_shared_heads(int rank) { return kMlaHeadsPerCta * (rank <= 512 ? 2 : 1); }
 
-// Splits: about two resident CTAs per SM over the head groups, at least
-// kMlaMinRowsPerSplit rows each, at most kMlaMaxSplits.
-int mla_splits(int heads, int rank, int count) {
+// Splits: as many as keep the head groups x queries x splits CTAs within
+// one wave (one CTA per SM; a partial second wave would cost a whole split's
+// time), at least kMlaMinRowsPerSplit rows each, at most kMlaMaxSplits.
+int mla_splits(int heads, int rank, int count, int batch = 1) {
     const int per_cta = mla_shared_heads(rank);
     const int groups = (heads + per_cta - 1) / per_cta;
-    const int want = (kMlaTargetCtas + groups - 1) / groups;
+    const int want = std::max(1, kMlaTargetCtas / (groups * batch));
     const int most = std::max(1, (count + kMlaMinRowsPerSplit - 1) / kMlaMinRowsPerSplit);
     return std::max(1, std::min({kMlaMaxSplits, want, most}));
 }
@@ -392,7 +434,8 @@ int mla_splits(int heads, int rank, int count) {
 template <int RPL, int PPL, int HPW, bool VEC>
 int32_t launch_shared(dim3 grid, cudaStream_t st, float *numerator, float *stats, const float *q_latent,
                       const float *q_rope, const float *latent, const float *rope, const int32_t *selected,
-                      int heads, int rank, int rope_dim, int tokens, int count, int splits, float scale) {
+                      int heads, int rank, int rope_dim, int tokens, int count, int splits, float scale,
+                      const int32_t *lens, int64_t latent_stride, int64_t rope_stride, int64_t sel_stride) {
     constexpr int bytes = kMlaStages * kMlaTileRows * 32 * (RPL + PPL) * 4;
     static const cudaError_t attr =
         cudaFuncSetAttribute(mla_shared_kernel<RPL, PPL, HPW, VEC>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
@@ -408,8 +451,31 @@ int32_t launch_shared(dim3 grid, cudaStream_t st, float *numerator, float *stats
     cfg.attrs = at;
     cfg.numAttrs = 1;
     GLMVX_CUDA(cudaLaunchKernelEx(&cfg, mla_shared_kernel<RPL, PPL, HPW, VEC>, numerator, stats, q_latent, q_rope, latent,
-                                  rope, selected, heads, rank, rope_dim, tokens, count, splits, scale));
+                                  rope, selected, heads, rank, rope_dim, tokens, count, splits, scale, lens,
+                                  latent_stride, rope_stride, sel_stride));
     return kOk;
+}
+
+// One CTA per query: copy its new rows to position lens[b] of each cache,
+// then lens[b] + 1.  A full cache (lens[b] == capacity) is left as it is
+// and flagged in *full.
+__global__ void __launch_bounds__(256)
+    dsa_append_kernel(float *latents, float *rope_keys, float *index_keys, int32_t *lens, const float *new_latent,
+                      const float *new_rope, const float *new_index, int capacity, int rank, int rope_dim,
+                      int index_dim, int32_t *full) {
+    const int b = blockIdx.x;
+    const int at = lens[b];
+    __syncthreads();  // every thread has read lens[b] before it moves
+    if (at < 0 || at >= capacity) {
+        if (threadIdx.x == 0) atomicExch(full, 1);
+        return;
+    }
+    const size_t row = static_cast<size_t>(b) * capacity + at;
+    for (int i = threadIdx.x; i < rank; i += blockDim.x) latents[row * rank + i] = new_latent[b * rank + i];
+    for (int i = threadIdx.x; i < rope_dim; i += blockDim.x) rope_keys[row * rope_dim + i] = new_rope[b * rope_dim + i];
+    for (int i = threadIdx.x; i < index_dim; i += blockDim.x)
+        index_keys[row * index_dim + i] = new_index[b * index_dim + i];
+    if (threadIdx.x == 0) lens[b] = at + 1;
 }
 
 template <class K>
@@ -477,9 +543,10 @@ GLMVX_EXPORT int32_t glmvx_mla_decode(float *out, const float *q_latent, const f
                          (rope_dim == 0 || (reinterpret_cast<uintptr_t>(cache_rope) & 15) == 0);
 #define GLMVX_MLA_SHARED(R, P, H)                                                                                   \
     (vec ? launch_shared<R, P, H, true>(grid, st, numerator, stats, q_latent, q_rope, cache_latent, cache_rope, selected, \
-                                     heads, rank, rope_dim, tokens, count, splits, scale)                           \
-         : launch_shared<R, P, H, false>(grid, st, numerator, stats, q_latent, q_rope, cache_latent, cache_rope,        \
-                                      selected, heads, rank, rope_dim, tokens, count, splits, scale))
+                                        heads, rank, rope_dim, tokens, count, splits, scale, nullptr, 0, 0, 0)       \
+         : launch_shared<R, P, H, false>(grid, st, numerator, stats, q_latent, q_rope, cache_latent, cache_rope,     \
+                                         selected, heads, rank, rope_dim, tokens, count, splits, scale, nullptr, 0, 0, \
+                                         0))
         rc = ppl <= 2 ? GLMVX_MLA_SHARED(16, 2, 2) : GLMVX_MLA_SHARED(16, 4, 2);
 #undef GLMVX_MLA_SHARED
     } else {
@@ -501,4 +568,107 @@ GLMVX_EXPORT int32_t glmvx_mla_decode(float *out, const float *q_latent, const f
     return launch_pdl(mla_merge_kernel, dim3(heads, (rank + kMergeCols - 1) / kMergeCols), dim3(32 * kMergeGroups),
                       st, out, const_cast<const float *>(numerator), const_cast<const float *>(stats), heads, rank,
                       splits);
+}
+
+// ---- Fused DSA decode for a batch of queries over device-resident
+// compressed caches (model.py:136-236 of the reference: `_index` then the
+// fused branch of `_attention`): per query b
+//   scores = sum_h head_weights[b][h] relu(index_scale q_index[b][h] . index_keys[b][t]), t < lens[b]
+//   sel    = stable descending top-min(topk, lens[b]) of scores
+//   out[b] = softmax-weighted latents over sel (the absorbed MLA above)
+// Three launches after one another on `stream` (index scores, top-k, MLA
+// partial + merge); lens lives on the device, so one captured graph serves
+// every step as the caches grow.
+
+// Scratch: scores [batch][capacity], selections [batch][topk], then the MLA
+// partials [batch][splits][heads][rank] and their (max, mass).
+GLMVX_EXPORT int64_t glmvx_dsa_scratch_bytes(int32_t batch, int32_t heads, int32_t rank, int32_t capacity,
+                                             int32_t topk) {
+    if (batch <= 0 || heads <= 0 || rank <= 0 || capacity <= 0 || topk <= 0) return -1;
+    const int64_t splits = mla_splits(heads, rank, topk, batch);
+    const auto up16 = [](int64_t b) { return (b + 15) / 16 * 16; };
+    return up16(4LL * batch * capacity) + up16(4LL * batch * topk) + 4LL * batch * splits * heads * (rank + 2);
+}
+
+// q_latent [batch][heads][rank], q_rope [batch][heads][rope_dim], q_index
+// [batch][index_heads][index_dim], head_weights [batch][index_heads];
+// caches latents [batch][capacity][rank], rope_keys [batch][capacity][rope_dim],
+// index_keys [batch][capacity][index_dim]; lens (device) [batch] valid rows
+// of each cache; out [batch][heads][rank]; selected_out, when given,
+// [batch][topk] (-1 past min(topk, lens[b])).  rank <= 512, rope_dim <= 128,
+// topk <= 4096.
+GLMVX_EXPORT int32_t glmvx_dsa_decode(float *out, int32_t *selected_out, const float *q_latent, const float *q_rope,
+                                      const float *q_index, const float *head_weights, const float *latents,
+                                      const float *rope_keys, const float *index_keys, const int32_t *lens,
+                                      int32_t batch, int32_t heads, int32_t rank, int32_t rope_dim,
+                                      int32_t index_heads, int32_t index_dim, int32_t capacity, int32_t topk,
+                                      float index_scale, float scale, void *scratch, uint64_t scratch_bytes,
+                                      void *stream) {
+    if (batch <= 0 || heads <= 0 || rank <= 0 || rank > 512 || rope_dim < 0 || rope_dim > 128 || index_heads <= 0 ||
+        index_dim <= 0 || capacity <= 0 || topk <= 0 || topk > 4096 || !(scale > 0.0f) || !std::isfinite(scale) ||
+        !std::isfinite(index_scale)) {
+        set_error("dsa_decode: invalid dimensions or scale");
+        return kInvalid;
+    }
+    if (!out || !q_latent || !q_index || !head_weights || !latents || !index_keys || !lens ||
+        (rope_dim && (!q_rope || !rope_keys))) {
+        set_error("dsa_decode: null pointer");
+        return kInvalid;
+    }
+    const int64_t need = glmvx_dsa_scratch_bytes(batch, heads, rank, capacity, topk);
+    if (!scratch || static_cast<int64_t>(scratch_bytes) < need || (reinterpret_cast<uintptr_t>(scratch) & 15)) {
+        set_error("dsa_decode: scratch needs %lld bytes, 16-byte aligned", static_cast<long long>(need));
+        return kInvalid;
+    }
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const auto up16 = [](int64_t b) { return (b + 15) / 16 * 16; };
+    char *base = static_cast<char *>(scratch);
+    float *scores = reinterpret_cast<float *>(base);
+    int32_t *sel = reinterpret_cast<int32_t *>(base + up16(4LL * batch * capacity));
+    float *numerator = reinterpret_cast<float *>(base + up16(4LL * batch * capacity) + up16(4LL * batch * topk));
+    const int splits = mla_splits(heads, rank, topk, batch);
+    float *stats = numerator + static_cast<size_t>(batch) * splits * heads * rank;
+    if (selected_out) sel = selected_out;
+    int32_t rc = launch_index_scores_batch(scores, q_index, index_keys, head_weights, capacity, index_heads, index_dim,
+                                           index_scale, lens, static_cast<int64_t>(capacity) * index_dim, capacity,
+                                           batch, st);
+    if (rc) return rc;
+    rc = launch_topk_batch(sel, scores, capacity, topk, lens, capacity, topk, batch, st);
+    if (rc) return rc;
+    const int per_cta = mla_shared_heads(rank);
+    const dim3 grid(splits, (heads + per_cta - 1) / per_cta, batch);
+    const int64_t lstride = static_cast<int64_t>(capacity) * rank, rstride = static_cast<int64_t>(capacity) * rope_dim;
+    const bool vec = rank % 4 == 0 && rope_dim % 4 == 0 && (reinterpret_cast<uintptr_t>(latents) & 15) == 0 &&
+                     (rope_dim == 0 || (reinterpret_cast<uintptr_t>(rope_keys) & 15) == 0);
+    const int ppl = (rope_dim + 31) / 32;
+#define GLMVX_DSA_SHARED(P)                                                                                       \
+    (vec ? launch_shared<16, P, 2, true>(grid, st, numerator, stats, q_latent, q_rope, latents, rope_keys, sel, heads, \
+                                         rank, rope_dim, capacity, topk, splits, scale, lens, lstride, rstride, topk) \
+         : launch_shared<16, P, 2, false>(grid, st, numerator, stats, q_latent, q_rope, latents, rope_keys, sel,      \
+                                          heads, rank, rope_dim, capacity, topk, splits, scale, lens, lstride, rstride, \
+                                          topk))
+    rc = ppl <= 2 ? GLMVX_DSA_SHARED(2) : GLMVX_DSA_SHARED(4);
+#undef GLMVX_DSA_SHARED
+    if (rc) return rc;
+    return launch_pdl(mla_merge_kernel, dim3(heads, (rank + kMergeCols - 1) / kMergeCols, batch),
+                      dim3(32 * kMergeGroups), st, out, const_cast<const float *>(numerator),
+                      const_cast<const float *>(stats), heads, rank, splits);
+}
+
+// Appends one row per query to the caches of glmvx_dsa_decode (device
+// pointers; new rows [batch][dim]); *full (device int32) is set to 1 for a
+// query whose cache already holds `capacity` rows, which is then unchanged.
+GLMVX_EXPORT int32_t glmvx_dsa_append(float *latents, float *rope_keys, float *index_keys, int32_t *lens,
+                                      const float *new_latent, const float *new_rope, const float *new_index,
+                                      int32_t batch, int32_t capacity, int32_t rank, int32_t rope_dim,
+                                      int32_t index_dim, int32_t *full, void *stream) {
+    if (batch < 0 || capacity <= 0 || rank <= 0 || rope_dim < 0 || index_dim <= 0 || !lens || !full) {
+        set_error("dsa_append: invalid arguments");
+        return kInvalid;
+    }
+    if (batch == 0) return kOk;
+    dsa_append_kernel<<<batch, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        latents, rope_keys, index_keys, lens, new_latent, new_rope, new_index, capacity, rank, rope_dim, index_dim, full);
+    GLMVX_CUDA(cudaGetLastError());
+    return kOk;
 }

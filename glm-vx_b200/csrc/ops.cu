@@ -398,165 +398,221 @@ __global__ void __launch_bounds__(1024)
 }
 
 // ---- top-k of many scores by radix selection (same order as topk_kernel):
-// the descending-score key of each score (topk_key's high word) is selected
-// 8 bits at a time down to the k-th smallest key T; the keys below T and the
-// lowest-index keys equal to T (stable ties) are gathered and sorted as
-// composite (key, index) words.  One CTA, k <= kTopkSelectMaxK.  With STAGED
-// the n keys are computed once into shared memory (n <= kTopkStagedScores)
-// and every pass reads them there; otherwise each pass re-reads the scores.
-constexpr int kTopkSelectMaxK = 4096, kTopkSelectThreads = 1024, kTopkStagedScores = 46 * 1024;
+// the descending-score key of each score (topk_key's high word) is resolved
+// 12, 12 and 8 bits at a time.  After a pass the keys whose resolved bits
+// are below the boundary digit are all in the top k; those equal to it are
+// candidates.  As soon as both groups fit in kTopkSelectMaxK and in no more
+// than the power of two the final sort needs anyway, they are gathered as
+// composite (key, index) words and sorted together, which also orders ties
+// by index; otherwise the three passes yield the k-th key T and the keys
+// below T plus the lowest-index keys equal to T are gathered and sorted.
+// One CTA, k <= kTopkSelectMaxK.  With STAGED the n keys are computed once
+// into shared memory (n <= kTopkStagedScores) and every pass reads them
+// there; otherwise each pass re-reads the scores.
+constexpr int kTopkSelectMaxK = 4096, kTopkSelectThreads = 1024, kTopkStagedScores = 44 * 1024;
+constexpr int kTopkBins = 4096;  // 12-bit digits
+constexpr int kTopkSelectSmem = kTopkSelectMaxK * 8 + kTopkBins * 4;  // sel + hist, before the staged keys
 
 __device__ __forceinline__ uint32_t topk_desc(float v) { return static_cast<uint32_t>(topk_key(v, 0) >> 32); }
 
+__host__ __device__ constexpr int topk_pow2(int m) {
+    int p = 1;
+    while (p < m) p <<= 1;
+    return p;
+}
+
+// Inclusive block scan of one int per thread (1024 threads).
+__device__ __forceinline__ int block_scan_incl(int v, int *s_warp) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, v, o);
+        if (lane >= o) v += y;
+    }
+    if (lane == 31) s_warp[warp] = v;
+    __syncthreads();
+    if (warp == 0) {
+        int t = s_warp[lane];
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, t, o);
+            if (lane >= o) t += y;
+        }
+        s_warp[lane] = t;
+    }
+    __syncthreads();
+    const int before = warp ? s_warp[warp - 1] : 0;
+    __syncthreads();  // s_warp reusable
+    return v + before;
+}
+
 template <bool STAGED>
 __global__ void __launch_bounds__(kTopkSelectThreads)
-    topk_select_kernel(int32_t *indices, const float *scores, int n, int k) {
-    extern __shared__ uint32_t staged[];
-    __shared__ uint64_t sel[kTopkSelectMaxK];
-    __shared__ int hist[256];
+    topk_select_kernel(int32_t *indices, const float *scores, int n, int k, const int32_t *lens, int64_t score_stride,
+                       int out_stride) {
+    extern __shared__ __align__(16) unsigned char topk_smem[];
+    uint64_t *sel = reinterpret_cast<uint64_t *>(topk_smem);
+    int *hist = reinterpret_cast<int *>(topk_smem + kTopkSelectMaxK * 8);
+    uint32_t *staged = reinterpret_cast<uint32_t *>(topk_smem + kTopkSelectSmem);
     __shared__ int s_warp[kTopkSelectThreads / 32];
-    __shared__ uint32_t s_prefix;
-    __shared__ int s_rank, s_below, s_ties;
+    __shared__ int s_digit, s_rank, s_bin, s_count, s_ties;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    // Query blockIdx.x of a batch: min(k, its length) positions, then -1.
+    scores += blockIdx.x * score_stride;
+    indices += static_cast<int64_t>(blockIdx.x) * out_stride;
+    if (lens) n = min(n, max(0, lens[blockIdx.x]));
+    for (int i = min(k, n) + tid; i < k; i += kTopkSelectThreads) indices[i] = -1;
+    k = min(k, n);
+    if (k == 0) return;
     const uint32_t lanes_below = (1u << lane) - 1u;
     auto key_at = [&](int i) -> uint32_t { return STAGED ? staged[i] : topk_desc(__ldg(scores + i)); };
     if (STAGED) {
 #pragma unroll 8
         for (int i = tid; i < n; i += kTopkSelectThreads) staged[i] = topk_desc(__ldg(scores + i));
     }
+    const int k2 = topk_pow2(k);
     uint32_t prefix = 0, mask = 0;
     int rank = k;  // 1-based position of the k-th key among those matching prefix
-    for (int shift = 24; shift >= 0; shift -= 8) {
-        if (tid < 256) hist[tid] = 0;
+    int bin = n;   // keys matching prefix
+    bool gathered = false;
+    for (int pass = 0; pass < 3; ++pass) {
+        const int bits = pass < 2 ? 12 : 8, shift = pass == 0 ? 20 : pass == 1 ? 8 : 0, nb = 1 << bits;
+        for (int i = tid; i < nb; i += kTopkSelectThreads) hist[i] = 0;
         __syncthreads();
-        // Keys cluster in few digits (the exponent byte first): lanes with the
-        // same digit add together, one atomic per distinct digit per warp.
-        for (int i0 = tid - lane; i0 < n; i0 += kTopkSelectThreads) {
-            const int i = i0 + lane;
-            const uint32_t key = i < n ? key_at(i) : 0u;
-            const bool take = i < n && (key & mask) == prefix;
-            const int digit = take ? static_cast<int>((key >> shift) & 255) : 256;
-            const uint32_t same = __match_any_sync(0xffffffffu, digit);
-            if (take && lane == __ffs(same) - 1) atomicAdd(&hist[digit], __popc(same));
+        for (int i = tid; i < n; i += kTopkSelectThreads) {
+            const uint32_t key = key_at(i);
+            if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & (nb - 1)], 1);
         }
         __syncthreads();
-        // The digit holding the rank-th key: a block scan of the 256 counts.
-        int count = 0, incl = 0;
-        if (tid < 256) {
-            count = incl = hist[tid];
-#pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-                const int y = __shfl_up_sync(0xffffffffu, incl, o);
-                if (lane >= o) incl += y;
-            }
-            if (lane == 31) s_warp[warp] = incl;
-        }
-        __syncthreads();
-        if (tid < 256) {
-            for (int w = 0; w < warp; ++w) incl += s_warp[w];
-            const int excl = incl - count;
-            if (excl < rank && rank <= incl) {  // exactly one digit: rank >= 1 and the total covers rank
-                s_prefix = prefix | (static_cast<uint32_t>(tid) << shift);
-                s_rank = rank - excl;
+        // The digit holding the rank-th key: each thread sums nb / 1024 bins.
+        const int per = nb / kTopkSelectThreads > 0 ? nb / kTopkSelectThreads : 1;
+        const int b0 = tid * per;
+        int local = 0;
+        for (int j = 0; j < per; ++j)
+            if (b0 + j < nb) local += hist[b0 + j];
+        int excl = block_scan_incl(local, s_warp) - local;
+        if (excl < rank && rank <= excl + local) {  // exactly one thread: rank >= 1 and the total covers rank
+            for (int j = 0; j < per; ++j) {
+                const int c = hist[b0 + j];
+                if (rank <= excl + c) {
+                    s_digit = b0 + j;
+                    s_rank = rank - excl;
+                    s_bin = c;
+                    break;
+                }
+                excl += c;
             }
         }
         __syncthreads();
-        prefix = s_prefix;
+        prefix |= static_cast<uint32_t>(s_digit) << shift;
+        mask |= static_cast<uint32_t>(nb - 1) << shift;
         rank = s_rank;
-        mask |= 255u << shift;
-    }
-    // prefix = T: the k - rank keys below T, then `rank` of the keys equal to
-    // T.  Positions within sel are arbitrary; the final sort orders them.
-    if (tid == 0) s_below = s_ties = 0;
-    __syncthreads();
-    int ties = 0;
-    for (int i0 = tid - lane; i0 < n; i0 += kTopkSelectThreads) {
-        const int i = i0 + lane;
-        const uint32_t key = i < n ? key_at(i) : ~0u;
-        const uint32_t below = __ballot_sync(0xffffffffu, i < n && key < prefix);
-        ties += i < n && key == prefix;
-        if (below) {
-            int base = 0;
-            if (lane == 0) base = atomicAdd(&s_below, __popc(below));
-            base = __shfl_sync(0xffffffffu, base, 0);
-            if (below >> lane & 1u)
-                sel[base + __popc(below & lanes_below)] = (static_cast<uint64_t>(key) << 32) | static_cast<uint32_t>(i);
+        bin = s_bin;
+        const int m = k - rank + bin;  // keys below the boundary digit + candidates
+        if (m <= kTopkSelectMaxK && (topk_pow2(m) == k2 || pass == 2)) {
+            gathered = true;
+            break;
         }
     }
-    ties = static_cast<int>(warp_sum(static_cast<float>(ties)));  // < 2^24: exact
-    if (lane == 0 && ties) atomicAdd(&s_ties, ties);
+    if (tid == 0) s_count = s_ties = 0;
     __syncthreads();
-    const uint64_t tkey = static_cast<uint64_t>(prefix) << 32;
-    if (s_ties == rank) {  // every key equal to T is taken
-        if (tid == 0) s_below = k - rank;
-        __syncthreads();
+    int m = k;  // sorted words
+    if (gathered) {  // every key with (key & mask) <= prefix, in any order
+        m = k - rank + bin;
         for (int i0 = tid - lane; i0 < n; i0 += kTopkSelectThreads) {
             const int i = i0 + lane;
-            const uint32_t tie = __ballot_sync(0xffffffffu, i < n && key_at(i) == prefix);
-            if (tie) {
+            const uint32_t key = i < n ? key_at(i) : ~0u;
+            const uint32_t take = __ballot_sync(0xffffffffu, i < n && (key & mask) <= prefix);
+            if (take) {
                 int base = 0;
-                if (lane == 0) base = atomicAdd(&s_below, __popc(tie));
+                if (lane == 0) base = atomicAdd(&s_count, __popc(take));
                 base = __shfl_sync(0xffffffffu, base, 0);
-                if (tie >> lane & 1u) sel[base + __popc(tie & lanes_below)] = tkey | static_cast<uint32_t>(i);
+                if (take >> lane & 1u)
+                    sel[base + __popc(take & lanes_below)] = (static_cast<uint64_t>(key) << 32) | static_cast<uint32_t>(i);
             }
         }
-    } else {  // the lowest-index `rank` ties: chunks of the block in index order
+    } else {
+        // prefix = T, with more keys equal to T than fit: the k - rank keys
+        // below T, then the lowest-index `rank` keys equal to T, chunks of the
+        // block in index order.
+        for (int i0 = tid - lane; i0 < n; i0 += kTopkSelectThreads) {
+            const int i = i0 + lane;
+            const uint32_t key = i < n ? key_at(i) : ~0u;
+            const uint32_t below = __ballot_sync(0xffffffffu, i < n && key < prefix);
+            if (below) {
+                int base = 0;
+                if (lane == 0) base = atomicAdd(&s_count, __popc(below));
+                base = __shfl_sync(0xffffffffu, base, 0);
+                if (below >> lane & 1u)
+                    sel[base + __popc(below & lanes_below)] = (static_cast<uint64_t>(key) << 32) | static_cast<uint32_t>(i);
+            }
+        }
+        const uint64_t tkey = static_cast<uint64_t>(prefix) << 32;
         int taken = 0;
         for (int c0 = 0; c0 < n && taken < rank; c0 += kTopkSelectThreads) {
             const int i = c0 + tid;
             const bool is_tie = i < n && key_at(i) == prefix;
-            const uint32_t tie = __ballot_sync(0xffffffffu, is_tie);
-            if (lane == 0) s_warp[warp] = __popc(tie);
-            __syncthreads();
-            int before = taken + __popc(tie & lanes_below), total = 0;
-            for (int w = 0; w < kTopkSelectThreads / 32; ++w) {
-                before += w < warp ? s_warp[w] : 0;
-                total += s_warp[w];
-            }
+            const int before = block_scan_incl(is_tie ? 1 : 0, s_warp) - (is_tie ? 1 : 0) + taken;
             if (is_tie && before < rank) sel[k - rank + before] = tkey | static_cast<uint32_t>(i);
-            taken += total;
+            if (tid == kTopkSelectThreads - 1) s_ties = before + (is_tie ? 1 : 0);
+            __syncthreads();
+            taken = s_ties;
             __syncthreads();
         }
     }
-    int k2 = 1;
-    while (k2 < k) k2 <<= 1;
-    for (int i = k + tid; i < k2; i += kTopkSelectThreads) sel[i] = ~0ull;
+    const int m2 = topk_pow2(m);
+    for (int i = m + tid; i < m2; i += kTopkSelectThreads) sel[i] = ~0ull;
     __syncthreads();
-    bitonic_sort(sel, k2);
+    bitonic_sort(sel, m2);
     for (int i = tid; i < k; i += kTopkSelectThreads) indices[i] = static_cast<int32_t>(sel[i] & 0xffffffffu);
 }
 
 // ---- DSA index scores (kernels/kernels.vx:404-421): score_t = sum_h w_h *
-// relu(scale * q_h . k_t).  One thread per token: a block of 32 query heads x
-// up to 256 columns sits in shared memory (read as broadcasts, four columns
-// per load with VEC), each thread streams its key row in 16-column pieces and
-// keeps one running dot per head of the block in registers.  VEC: dim a
+// relu(scale * q_h . k_t).  Four threads per token, each taking every
+// fourth head of a 32-head block (kIndexSplit-way split keeps ~28 warps per SM in flight
+// over the key stream): the block's queries, up to 128 columns at a time,
+// sit in shared memory (read as broadcasts, four columns per load with VEC);
+// each thread streams its token's key row in 16-column pieces (the four
+// threads of a token share the lines through L1) and keeps 8 running dots
+// in registers; the four partial totals meet by shuffles.  VEC: dim a
 // multiple of 16 and keys 16-byte aligned.
-constexpr int kIndexHeadBlock = 32, kIndexDimBlock = 256, kIndexThreads = 128;
+constexpr int kIndexHeadBlock = 32, kIndexDimBlock = 128, kIndexThreads = 128, kIndexSplit = 4;
+constexpr int kIndexHeadsPerThread = kIndexHeadBlock / kIndexSplit, kIndexTokensPerCta = kIndexThreads / kIndexSplit;
+constexpr int kIndexStride = kIndexDimBlock + 4;  // padded query row (floats)
 
 template <bool VEC>
-__global__ void __launch_bounds__(kIndexThreads)
+__global__ void __launch_bounds__(kIndexThreads, 8)
     index_scores_kernel(float *out, const float *q, const float *keys, const float *w, int tokens, int heads,
-                        int dim, float qk_scale) {
-    __shared__ __align__(16) float sq[kIndexHeadBlock * kIndexDimBlock];
-    const int t = blockIdx.x * kIndexThreads + threadIdx.x;
+                        int dim, float qk_scale, const int32_t *lens, int64_t key_stride, int64_t out_stride) {
+    __shared__ __align__(16) float sq[kIndexHeadBlock * kIndexStride];
+    const int b = blockIdx.y;  // query of a batch: its own keys, queries, weights and length
+    if (lens) tokens = min(tokens, max(0, lens[b]));
+    if (static_cast<int>(blockIdx.x) * kIndexTokensPerCta >= tokens) return;  // whole CTA past the keys
+    q += static_cast<size_t>(b) * heads * dim;
+    w += static_cast<size_t>(b) * heads;
+    keys += b * key_stride;
+    out += b * out_stride;
+    const int part = threadIdx.x % kIndexSplit;
+    const int t = blockIdx.x * kIndexTokensPerCta + threadIdx.x / kIndexSplit;
     const bool live = t < tokens;
     const float *kr = keys + static_cast<size_t>(live ? t : 0) * dim;
     float total = 0.0f;
     for (int h0 = 0; h0 < heads; h0 += kIndexHeadBlock) {
         const int nh = min(kIndexHeadBlock, heads - h0);
-        float dot[kIndexHeadBlock];
+        // This thread's heads within the block: part, part + 4, ... (the four
+        // threads of a token then read queries 16 bytes apart, no bank conflict).
+        float dot[kIndexHeadsPerThread];
 #pragma unroll
-        for (int h = 0; h < kIndexHeadBlock; ++h) dot[h] = 0.0f;
+        for (int h = 0; h < kIndexHeadsPerThread; ++h) dot[h] = 0.0f;
         for (int c0 = 0; c0 < dim; c0 += kIndexDimBlock) {
             const int nc = min(kIndexDimBlock, dim - c0);
             __syncthreads();  // the previous block of q is no longer read
             for (int i = threadIdx.x; i < nh * nc; i += kIndexThreads) {
                 const int h = i / nc, c = i - h * nc;
-                sq[h * kIndexDimBlock + c] = q[static_cast<size_t>(h0 + h) * dim + c0 + c];
+                sq[h * kIndexStride + c] = q[static_cast<size_t>(h0 + h) * dim + c0 + c];
             }
             __syncthreads();
-            if (!live) continue;
+            if (!live || part >= nh) continue;
             for (int d = 0; d < nc; d += 16) {
                 float kv[16];
                 if (VEC) {
@@ -570,9 +626,9 @@ __global__ void __launch_bounds__(kIndexThreads)
                     for (int i = 0; i < 16; ++i) kv[i] = d + i < nc ? __ldg(kr + c0 + d + i) : 0.0f;
                 }
 #pragma unroll
-                for (int h = 0; h < kIndexHeadBlock; ++h) {
-                    if (h < nh) {
-                        const float *qh = sq + h * kIndexDimBlock + d;
+                for (int h = 0; h < kIndexHeadsPerThread; ++h) {
+                    if (part + kIndexSplit * h < nh) {
+                        const float *qh = sq + (part + kIndexSplit * h) * kIndexStride + d;
                         float acc = dot[h];
                         if (VEC) {
 #pragma unroll
@@ -594,14 +650,17 @@ __global__ void __launch_bounds__(kIndexThreads)
             }
         }
 #pragma unroll
-        for (int h = 0; h < kIndexHeadBlock; ++h) {
-            if (h < nh) {
+        for (int h = 0; h < kIndexHeadsPerThread; ++h) {
+            if (part + kIndexSplit * h < nh) {
                 const float s = dot[h] * qk_scale;
-                if (s > 0.0f) total = fmaf(__ldg(w + h0 + h), s, total);
+                if (s > 0.0f) total = fmaf(__ldg(w + h0 + part + kIndexSplit * h), s, total);
             }
         }
     }
-    if (live) out[t] = total;
+    // The token's four partial totals, added in a fixed order.
+    total += __shfl_xor_sync(0xffffffffu, total, 1);
+    total += __shfl_xor_sync(0xffffffffu, total, 2);
+    if (live && part == 0) out[t] = total;
 }
 
 // ---- single-query attention over all or selected tokens
@@ -658,6 +717,44 @@ __global__ void __launch_bounds__(256)
 }
 
 static int ew_grid(int64_t n) { return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, 4 * 148 * 8))); }
+
+// Batched launches shared with the fused DSA decode (mla.cu); `batch`
+// queries along the grid's y (index scores) or x (top-k) dimension.
+int32_t launch_index_scores_batch(float *out, const float *q, const float *keys, const float *w, int tokens,
+                                  int heads, int dim, float qk_scale, const int32_t *lens, int64_t key_stride,
+                                  int64_t out_stride, int batch, cudaStream_t stream) {
+    if (tokens <= 0 || batch <= 0) return kOk;
+    const bool vec = dim % 16 == 0 && (reinterpret_cast<uintptr_t>(keys) & 15) == 0 && key_stride % 4 == 0;
+    const dim3 grid((tokens + kIndexTokensPerCta - 1) / kIndexTokensPerCta, batch);
+    if (vec)
+        index_scores_kernel<true><<<grid, kIndexThreads, 0, stream>>>(out, q, keys, w, tokens, heads, dim, qk_scale,
+                                                                      lens, key_stride, out_stride);
+    else
+        index_scores_kernel<false><<<grid, kIndexThreads, 0, stream>>>(out, q, keys, w, tokens, heads, dim,
+                                                                       qk_scale, lens, key_stride, out_stride);
+    return launch_status("index_scores_kernel");
+}
+
+int32_t launch_topk_batch(int32_t *indices, const float *scores, int n, int k, const int32_t *lens,
+                          int64_t score_stride, int out_stride, int batch, cudaStream_t stream) {
+    if (k <= 0 || k > kTopkSelectMaxK) return set_error("topk: 1 <= k <= %d", kTopkSelectMaxK), kInvalid;
+    if (batch <= 0) return kOk;
+    const bool staged = n <= kTopkStagedScores;
+    static const cudaError_t attr_staged = cudaFuncSetAttribute(
+        topk_select_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTopkSelectSmem + kTopkStagedScores * 4);
+    static const cudaError_t attr_plain = cudaFuncSetAttribute(
+        topk_select_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTopkSelectSmem);
+    const cudaError_t attr = staged ? attr_staged : attr_plain;
+    if (attr != cudaSuccess) return set_error("topk_select smem: %s", cudaGetErrorString(attr)), kCudaError;
+    const int smem = kTopkSelectSmem + (staged ? n * 4 : 0);
+    if (staged)
+        topk_select_kernel<true><<<batch, kTopkSelectThreads, smem, stream>>>(indices, scores, n, k, lens,
+                                                                             score_stride, out_stride);
+    else
+        topk_select_kernel<false><<<batch, kTopkSelectThreads, smem, stream>>>(indices, scores, n, k, lens,
+                                                                              score_stride, out_stride);
+    return launch_status("topk_select_kernel");
+}
 
 }  // namespace glmvx
 
@@ -782,15 +879,7 @@ GLMVX_EXPORT int32_t glmvx_topk(int32_t *indices, const float *scores, int32_t n
     int n2 = 1;
     while (n2 < n) n2 <<= 1;
     if (n2 > kTopkSmemKeys && k <= kTopkSelectMaxK) {  // many scores, bounded k: radix selection
-        if (n <= kTopkStagedScores) {
-            static const cudaError_t attr = cudaFuncSetAttribute(
-                topk_select_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTopkStagedScores * 4);
-            if (attr != cudaSuccess) return set_error("topk_select smem: %s", cudaGetErrorString(attr)), kCudaError;
-            topk_select_kernel<true><<<1, kTopkSelectThreads, n * 4, S_>>>(indices, scores, n, k);
-        } else {
-            topk_select_kernel<false><<<1, kTopkSelectThreads, 0, S_>>>(indices, scores, n, k);
-        }
-        return launch_status("topk_select_kernel");
+        return launch_topk_batch(indices, scores, n, k, nullptr, 0, 0, 1, S_);
     }
     if (n2 > kTopkSmemKeys && !scratch) return set_error("topk needs scratch for n > %d", kTopkSmemKeys), kInvalid;
     topk_kernel<<<1, 1024, 0, S_>>>(indices, scores, n, k, static_cast<uint64_t *>(scratch), n2);
@@ -800,13 +889,7 @@ GLMVX_EXPORT int32_t glmvx_topk(int32_t *indices, const float *scores, int32_t n
 GLMVX_EXPORT int32_t glmvx_index_scores(float *out, const float *q, const float *keys, const float *w,
                                         int32_t tokens, int32_t heads, int32_t dim, float qk_scale, void *stream) {
     if (tokens < 0 || heads <= 0 || dim <= 0) return set_error("index_scores dims"), kInvalid;
-    if (tokens) {
-        const bool vec = dim % 16 == 0 && (reinterpret_cast<uintptr_t>(keys) & 15) == 0;
-        const int grid = (tokens + kIndexThreads - 1) / kIndexThreads;
-        if (vec) index_scores_kernel<true><<<grid, kIndexThreads, 0, S_>>>(out, q, keys, w, tokens, heads, dim, qk_scale);
-        else index_scores_kernel<false><<<grid, kIndexThreads, 0, S_>>>(out, q, keys, w, tokens, heads, dim, qk_scale);
-    }
-    return launch_status("index_scores_kernel");
+    return launch_index_scores_batch(out, q, keys, w, tokens, heads, dim, qk_scale, nullptr, 0, 0, 1, S_);
 }
 
 // selected == nullptr attends to the first `count` tokens.  `bad` (device

@@ -182,6 +182,27 @@ int32_t glmvx_mla_decode(float *out, const float *q_latent, const float *q_rope,
                          const float *cache_rope, const int32_t *selected, int32_t heads, int32_t rank,
                          int32_t rope_dim, int32_t tokens, int32_t count, int32_t selection_stride, float scale,
                          void *scratch, uint64_t scratch_bytes, void *stream);
+/* Fused DSA decode for a batch of queries over device-resident compressed
+   caches (glm_vx/model.py:136-176 `_index` + :205-221 the fused attention
+   branch): per query b, indexer scores of its lens[b] cached keys
+   (index_scores), their stable top-min(topk, lens[b]) (topk), then the
+   absorbed MLA above over those rows.  Layouts [batch][...] as in
+   glmvx_index_scores / glmvx_mla_decode; caches [batch][capacity][dim];
+   lens on the device; selected_out optional [batch][topk] (-1 padded).
+   rank <= 512, rope_dim <= 128, topk <= 4096. */
+int64_t glmvx_dsa_scratch_bytes(int32_t batch, int32_t heads, int32_t rank, int32_t capacity, int32_t topk);
+int32_t glmvx_dsa_decode(float *out, int32_t *selected_out, const float *q_latent, const float *q_rope,
+                         const float *q_index, const float *head_weights, const float *latents,
+                         const float *rope_keys, const float *index_keys, const int32_t *lens, int32_t batch,
+                         int32_t heads, int32_t rank, int32_t rope_dim, int32_t index_heads, int32_t index_dim,
+                         int32_t capacity, int32_t topk, float index_scale, float scale, void *scratch,
+                         uint64_t scratch_bytes, void *stream);
+/* One decode step's new rows (model.py:176-181, 146-151: latent, rope key and
+   index key appended before indexing) written at lens[b] of each query's
+   caches, then lens[b] += 1; *full (device) set for a full cache. */
+int32_t glmvx_dsa_append(float *latents, float *rope_keys, float *index_keys, int32_t *lens, const float *new_latent,
+                         const float *new_rope, const float *new_index, int32_t batch, int32_t capacity, int32_t rank,
+                         int32_t rope_dim, int32_t index_dim, int32_t *full, void *stream);
 
 /* Routed + shared MoE feed-forward layer (decode / small batches), device
  * pointers.  Replaces the per-expert Python loop of glm_vx/model.py:289-324

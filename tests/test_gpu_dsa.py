@@ -1,0 +1,106 @@
+"""Fused batched DSA decode (csrc/mla.cu glmvx_dsa_append / glmvx_dsa_decode,
+gpu/dsa.py DSADecoder) against the reference's per-request semantics
+(glm_vx/model.py:136-176 `_index`, :205-221 fused attention): the new rows
+are appended before indexing, the selection is the stable descending top-k
+of the indexer scores over every cached position, and the attention is a
+float64 softmax over the selected rows.  The selection is checked exactly
+against the stable argsort of the same kernel's scores (glmvx_index_scores
+on the same rows), the attention within f32 tolerance."""
+import numpy as np
+import pytest
+
+from test_gpu_mla import mla_ref
+
+pytestmark = pytest.mark.gpu
+
+
+def _index_scores(gpu_backend, q, keys, w, scale):
+    return gpu_backend.index_scores(q, keys, w, scale)
+
+
+def _case(rng, B, T0, heads, rank, rdim, ih, idim):
+    caches = []
+    for b in range(B):
+        n = T0[b]
+        caches.append((rng.normal(size=(n, rank)).astype('f4'), rng.normal(size=(n, rdim)).astype('f4'),
+                       rng.normal(size=(n, idim)).astype('f4')))
+    step = dict(new_latent=rng.normal(size=(B, rank)).astype('f4'), new_rope=rng.normal(size=(B, rdim)).astype('f4'),
+                new_index_key=rng.normal(size=(B, idim)).astype('f4'),
+                q_latent=(rng.normal(size=(B, heads, rank)) * 0.05).astype('f4'),
+                q_rope=(rng.normal(size=(B, heads, rdim)) * 0.05).astype('f4'),
+                q_index=rng.normal(size=(B, ih, idim)).astype('f4'),
+                head_weights=(rng.normal(size=(B, ih)) * ih ** -0.5).astype('f4'))
+    return caches, step
+
+
+def _check(gpu_backend, dec, caches, step, out, sel):
+    for b, (lat, rk, ik) in enumerate(caches):
+        lat = np.vstack([lat, step['new_latent'][b:b + 1]])
+        rk = np.vstack([rk, step['new_rope'][b:b + 1]])
+        ik = np.vstack([ik, step['new_index_key'][b:b + 1]])
+        scores = _index_scores(gpu_backend, step['q_index'][b], ik, step['head_weights'][b], dec.index_scale)
+        count = min(dec.topk, lat.shape[0])
+        want = np.argsort(-scores, kind='stable')[:count]
+        assert sel[b, :count].tolist() == want.tolist()
+        assert np.all(sel[b, count:] == -1)
+        ref = mla_ref(step['q_latent'][b], step['q_rope'][b], lat, rk, dec.scale, [want] * dec.heads)
+        np.testing.assert_allclose(out[b], ref, rtol=5e-5, atol=3e-6)
+
+
+@pytest.mark.parametrize('lens', [(700, 0, 255, 256), (1,), (3000, 2999)])
+def test_dsa_decode_small(gpu_backend, lens):
+    from gpu.dsa import DSADecoder
+    rng = np.random.default_rng(sum(lens) + len(lens))
+    B, heads, rank, rdim, ih, idim, topk = len(lens), 20, 256, 32, 8, 64, 256
+    dec = DSADecoder(gpu_backend, B, 3100, heads=heads, rank=rank, rope_dim=rdim, index_heads=ih, index_dim=idim,
+                     topk=topk)
+    try:
+        caches, step = _case(rng, B, lens, heads, rank, rdim, ih, idim)
+        for b, c in enumerate(caches):
+            dec.load(b, *c)
+        out, sel = dec.step(**step)
+        _check(gpu_backend, dec, caches, step, out, sel)
+        # a second step appends after the first: the caches have grown by one
+        caches = [(np.vstack([c[0], step['new_latent'][b:b + 1]]), np.vstack([c[1], step['new_rope'][b:b + 1]]),
+                   np.vstack([c[2], step['new_index_key'][b:b + 1]])) for b, c in enumerate(caches)]
+        _, step2 = _case(rng, B, [0] * B, heads, rank, rdim, ih, idim)
+        out, sel = dec.step(**step2)
+        _check(gpu_backend, dec, caches, step2, out, sel)
+        assert dec.lens.tolist() == [n + 2 for n in lens]
+    finally:
+        dec.close()
+
+
+def test_dsa_decode_config3_shape(gpu_backend):
+    """64 heads, rank 512, rope 64, indexer 32 x 128, top-2048 over 32768
+    cached positions, two requests."""
+    from gpu.dsa import DSADecoder
+    rng = np.random.default_rng(33)
+    lens = (32767, 20000)
+    dec = DSADecoder(gpu_backend, 2, 32768)
+    try:
+        caches, step = _case(rng, 2, lens, 64, 512, 64, 32, 128)
+        for b, c in enumerate(caches):
+            dec.load(b, *c)
+        out, sel = dec.step(**step)
+        _check(gpu_backend, dec, caches, step, out, sel)
+        with pytest.raises(ValueError, match='full'):
+            dec.step(**step)  # request 0 now holds 32768 rows
+    finally:
+        dec.close()
+
+
+def test_dsa_validation(gpu_backend):
+    from gpu.dsa import DSADecoder
+    with pytest.raises(ValueError):
+        DSADecoder(gpu_backend, 1, 100, rank=1024)
+    with pytest.raises(ValueError):
+        DSADecoder(gpu_backend, 1, 100, topk=5000)
+    dec = DSADecoder(gpu_backend, 2, 10, heads=4, rank=64, rope_dim=8, index_heads=2, index_dim=16, topk=4)
+    try:
+        with pytest.raises(ValueError, match='capacity'):
+            dec.load(0, np.zeros((11, 64), 'f4'), np.zeros((11, 8), 'f4'), np.zeros((11, 16), 'f4'))
+        with pytest.raises(ValueError, match='request'):
+            dec.load(2, np.zeros((1, 64), 'f4'), np.zeros((1, 8), 'f4'), np.zeros((1, 16), 'f4'))
+    finally:
+        dec.close()
