@@ -1,0 +1,281 @@
+// Dense f32 GEMM C[M,N] = A[M,K] B[K,N], row-major, the contract of the
+// reference's resident GEMM (GEMMKernels.gemm, gpu/gemm.py:51-97; kernels
+// gpu/gemm.vx:14-73 tf32, :75ff f32):
+//   precision "tf32_rna": every multiplicand rounded to TF32 (nearest, ties
+//   away from zero), products accumulated in f32 on the tensor cores;
+//   precision "f32": f32 multiply-adds.
+// Any M, N, K >= 0 (K = 0 writes zeros), any 4-byte alignment.
+//
+// tf32_rna on the 5th-generation tensor cores: a CTA owns a 128 x 128 tile
+// of C whose f32 accumulators live in tensor memory (128 lanes x 128
+// columns).  Per 32-wide K block its 128 threads load A [128 x 32] and B
+// [32 x 128] from global memory, round them (cvt.rna.tf32) and store them in
+// shared memory as K-major 128-byte-swizzled tiles (row r of a tile at
+// (r/8)*1024 + (r%8)*128 bytes, 16-byte chunk c at position c ^ (r%8): the
+// canonical SWIZZLE_128B K-major layout of the UMMA descriptors); one thread
+// then issues four tcgen05.mma kind::tf32 (M=128, N=128, K=8) and commits
+// them to an mbarrier.  Two stages: the loads of block k+1 overlap the MMAs
+// of block k.  The epilogue reads the accumulators with tcgen05.ld (warp w
+// owns lanes 32w..32w+31, i.e. rows) and writes C.
+#include <cstdint>
+
+#include "common.cuh"
+
+namespace glmvx {
+
+namespace {
+
+constexpr int kGemmTile = 128, kGemmBK = 32, kGemmStages = 2, kGemmThreads = 128;
+constexpr int kGemmOperandBytes = kGemmTile * kGemmBK * 4;  // 16 KB: 128 rows x 128 bytes
+constexpr int kGemmStageBytes = 2 * kGemmOperandBytes;
+constexpr int kGemmSmem = kGemmStages * kGemmStageBytes + 1024;  // + alignment slack
+constexpr uint32_t kGemmTmemCols = 128;
+
+// Instruction descriptor, kind::tf32: D f32 (bits 4-5 = 1), A and B TF32
+// (bits 7-9, 10-12 = 2), both K-major (bits 15, 16 = 0), N >> 3 at bit 17,
+// M >> 4 at bit 24.
+constexpr uint32_t kGemmIdesc = (1u << 4) | (2u << 7) | (2u << 10) | ((kGemmTile >> 3) << 17) |
+                                ((kGemmTile >> 4) << 24);
+
+// Shared-memory matrix descriptor of a K-major SWIZZLE_128B tile at `addr`:
+// start address >> 4 (bits 0-13), leading byte offset 16 >> 4 (unused by
+// swizzled K-major layouts), stride byte offset 1024 >> 4 between 8-row
+// groups (bits 32-45), version 1 (bit 46), layout type 2 = SWIZZLE_128B
+// (bits 61-63).
+__device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t addr) {
+    return static_cast<uint64_t>((addr >> 4) & 0x3FFFu) | (1ull << 16) | (64ull << 32) | (1ull << 46) | (2ull << 61);
+}
+
+__device__ __forceinline__ uint32_t tf32_rna(float v) {
+    uint32_t r;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(v));
+    return r;
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void umma_tf32(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                          uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
+                 : "memory");
+}
+
+// 32 consecutive accumulator columns of this warp's 32 lanes.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]),
+          "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]),
+          "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Byte offset of 16-byte chunk `c` (K elements 4c..4c+3) of row r in a
+// K-major SWIZZLE_128B tile.
+__device__ __forceinline__ uint32_t sw128_offset(int r, int c) {
+    return static_cast<uint32_t>((r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4));
+}
+
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_tf32_kernel(float *__restrict__ C, const float *__restrict__ A, const float *__restrict__ B, int M, int N,
+                     int K, int *err) {
+    extern __shared__ uint8_t gemm_smem_raw[];
+    __shared__ uint64_t mma_done[kGemmStages];
+    __shared__ uint32_t tmem_slot;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const uint32_t raw = smem_addr(gemm_smem_raw);
+    const uint32_t pad = ((raw + 1023u) & ~1023u) - raw;  // the swizzle works on address bits: 1 KB-aligned tiles
+    uint8_t *tiles = gemm_smem_raw + pad;
+    const uint32_t tiles_s = raw + pad;
+    const int m0 = blockIdx.y * kGemmTile, n0 = blockIdx.x * kGemmTile;
+
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(&tmem_slot)),
+                     "r"(kGemmTmemCols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    if (tid == 0) {
+        for (int s = 0; s < kGemmStages; ++s) mbar_init(&mma_done[s], 1);
+        fence_mbar_init();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_slot;
+
+    const int nk = (K + kGemmBK - 1) / kGemmBK;
+    bool ok = true;
+    for (int kb = 0; kb < nk; ++kb) {
+        const int s = kb % kGemmStages;
+        if (kb >= kGemmStages) ok = mbar_wait_bounded(&mma_done[s], ((kb - kGemmStages) / kGemmStages) & 1);
+        if (!__syncthreads_and(ok)) {  // the stage is still read by MMAs that did not finish
+            if (tid == 0) report_device_error(err, kDevErrFullWait);
+            ok = false;
+            break;
+        }
+        uint8_t *as = tiles + s * kGemmStageBytes, *bs = as + kGemmOperandBytes;
+        const int k0 = kb * kGemmBK;
+        // A: row r = q / 8, K chunk c = q % 8 (four consecutive k).
+#pragma unroll 2
+        for (int q = tid; q < kGemmTile * 8; q += kGemmThreads) {
+            const int r = q >> 3, c = q & 7, m = m0 + r, k = k0 + 4 * c;
+            uint32_t v[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+                v[e] = (m < M && k + e < K) ? tf32_rna(__ldg(A + static_cast<int64_t>(m) * K + k + e)) : 0u;
+            *reinterpret_cast<uint4 *>(as + sw128_offset(r, c)) = make_uint4(v[0], v[1], v[2], v[3]);
+        }
+        // B as B^T, K-major: row n = tid (coalesced loads along n), chunk c.
+#pragma unroll 2
+        for (int c = 0; c < 8; ++c) {
+            const int n = n0 + tid, k = k0 + 4 * c;
+            uint32_t v[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+                v[e] = (n < N && k + e < K) ? tf32_rna(__ldg(B + static_cast<int64_t>(k + e) * N + n)) : 0u;
+            *reinterpret_cast<uint4 *>(bs + sw128_offset(tid, c)) = make_uint4(v[0], v[1], v[2], v[3]);
+        }
+        // Generic-proxy stores become visible to the tensor cores' async proxy.
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncthreads();
+        if (tid == 0) {
+            tc_fence_after();
+            const uint32_t a_s = tiles_s + s * kGemmStageBytes, b_s = a_s + kGemmOperandBytes;
+#pragma unroll
+            for (int kk = 0; kk < kGemmBK / 8; ++kk)  // K = 8 tf32 = 32 bytes per MMA
+                umma_tf32(tmem, umma_desc_sw128(a_s + 32 * kk), umma_desc_sw128(b_s + 32 * kk), kGemmIdesc,
+                          (kb > 0 || kk > 0) ? 1u : 0u);
+            umma_commit(&mma_done[s]);
+        }
+    }
+    if (ok && nk > 0) {
+        const int last = nk - 1;
+        ok = mbar_wait_bounded(&mma_done[last % kGemmStages], (last / kGemmStages) & 1);
+        if (!ok && lane == 0) report_device_error(err, kDevErrFullWait);
+    }
+    ok = __syncthreads_and(ok);
+    tc_fence_after();
+    // Epilogue: thread = row m0 + 32*warp + lane; zeros when K == 0.
+    const int row = m0 + 32 * warp + lane;
+#pragma unroll 1
+    for (int c0 = 0; c0 < kGemmTile; c0 += 32) {
+        uint32_t v[32];
+        if (nk > 0 && ok) {
+            tmem_ld32(tmem + (static_cast<uint32_t>(32 * warp) << 16) + c0, v);
+        } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = 0u;
+        }
+        if (row < M && ok) {
+            float *crow = C + static_cast<int64_t>(row) * N + n0 + c0;
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+                if (n0 + c0 + j < N) crow[j] = __uint_as_float(v[j]);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kGemmTmemCols)
+                     : "memory");
+}
+
+// precision "f32": 64 x 64 tile per CTA, 16 x 16 threads with 4 x 4
+// outputs each, K in blocks of 16 through shared memory; each output an
+// ordered chain of f32 fused multiply-adds over k.
+constexpr int kSgemmTile = 64, kSgemmBK = 16;
+
+__global__ void __launch_bounds__(256)
+    gemm_f32_kernel(float *__restrict__ C, const float *__restrict__ A, const float *__restrict__ B, int M, int N,
+                    int K) {
+    __shared__ float as[kSgemmBK][kSgemmTile + 4], bs[kSgemmBK][kSgemmTile + 4];
+    const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+    const int m0 = blockIdx.y * kSgemmTile, n0 = blockIdx.x * kSgemmTile;
+    float acc[4][4] = {};
+    for (int k0 = 0; k0 < K; k0 += kSgemmBK) {
+        for (int i = threadIdx.x; i < kSgemmTile * kSgemmBK; i += 256) {
+            const int r = i / kSgemmBK, k = i % kSgemmBK;  // A tile: row r, column k
+            as[k][r] = (m0 + r < M && k0 + k < K) ? __ldg(A + static_cast<int64_t>(m0 + r) * K + k0 + k) : 0.0f;
+            const int kb = i / kSgemmTile, n = i % kSgemmTile;  // B tile: row kb, column n
+            bs[kb][n] = (k0 + kb < K && n0 + n < N) ? __ldg(B + static_cast<int64_t>(k0 + kb) * N + n0 + n) : 0.0f;
+        }
+        __syncthreads();
+#pragma unroll
+        for (int k = 0; k < kSgemmBK; ++k) {
+            float a[4], b[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                a[i] = as[k][ty + 16 * i];
+                b[i] = bs[k][tx + 16 * i];
+            }
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int m = m0 + ty + 16 * i, n = n0 + tx + 16 * j;
+            if (m < M && n < N) C[static_cast<int64_t>(m) * N + n] = acc[i][j];
+        }
+}
+
+}  // namespace
+
+}  // namespace glmvx
+
+using namespace glmvx;
+
+// precision 0 = "f32", 1 = "tf32_rna" (gpu/gemm.py:24-47).  C must not
+// overlap A or B.  *err (device int32, the library's device error word when
+// NULL is not allowed) records a tensor-core wait that timed out.
+GLMVX_EXPORT int32_t glmvx_gemm(float *C, const float *A, const float *B, int32_t M, int32_t N, int32_t K,
+                                int32_t precision, int32_t *err, void *stream) {
+    if (M < 0 || N < 0 || K < 0) {
+        set_error("gemm: dimensions must be >= 0");
+        return kInvalid;
+    }
+    if (precision != 0 && precision != 1) {
+        set_error("precision must be 'f32' or explicit 'tf32_rna'");
+        return kInvalid;
+    }
+    if (M == 0 || N == 0) return kOk;
+    if (!C || (K > 0 && (!A || !B)) || (precision == 1 && !err)) {
+        set_error("gemm: null pointer");
+        return kInvalid;
+    }
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (precision == 0) {
+        const dim3 grid((N + kSgemmTile - 1) / kSgemmTile, (M + kSgemmTile - 1) / kSgemmTile);
+        gemm_f32_kernel<<<grid, 256, 0, st>>>(C, A, B, M, N, K);
+    } else {
+        static const cudaError_t attr =
+            cudaFuncSetAttribute(gemm_tf32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmem);
+        if (attr != cudaSuccess) {
+            set_error("gemm smem: %s", cudaGetErrorString(attr));
+            return kCudaError;
+        }
+        const dim3 grid((N + kGemmTile - 1) / kGemmTile, (M + kGemmTile - 1) / kGemmTile);
+        gemm_tf32_kernel<<<grid, kGemmThreads, kGemmSmem, st>>>(C, A, B, M, N, K, err);
+    }
+    GLMVX_CUDA(cudaGetLastError());
+    return kOk;
+}

@@ -432,6 +432,34 @@ class GPUBackend:
                    need, self.stream.handle)
         return self._fetch(offs[:1], [out])[0]
 
+    def gemm(self, a, b, precision='f32'):
+        """C = A @ B for float32 matrices A [M, K], B [K, N], the contract of
+        the reference's resident GEMM (GEMMKernels.gemm, gpu/gemm.py:51-97):
+        precision 'f32' multiplies and adds in f32; 'tf32_rna' rounds every
+        multiplicand to TF32 (nearest, ties away from zero) and accumulates
+        in f32 on the tensor cores (tcgen05, accumulators in tensor memory).
+        K = 0 gives zeros."""
+        if precision not in ('f32', 'tf32_rna'):
+            raise ValueError("precision must be 'f32' or explicit 'tf32_rna'")
+        a, b = (np.ascontiguousarray(x, dtype=np.float32) for x in (a, b))
+        if a.ndim != 2 or b.ndim != 2:
+            raise ValueError('A and B must be float32 matrices')
+        m, k = a.shape
+        if b.shape[0] != k:
+            raise ValueError('GEMM inner dimensions differ')
+        n = b.shape[1]
+        for value, name in ((m, 'M'), (n, 'N'), (k, 'K')):
+            if value >= 2 ** 31:
+                raise ValueError(f'{name} must fit in int32')
+        out = np.empty((m, n), np.float32)
+        if m == 0 or n == 0:
+            return out
+        self._begin()
+        (ad, bd), (od, ed), offs = self._stage([a, b], [out.nbytes, 4])
+        self._call('glmvx_gemm', od, ad, bd, m, n, k, 1 if precision == 'tf32_rna' else 0, self.device.error_address(),
+                   self.stream.handle)
+        return self._fetch_checked(offs[:1], [out], offs[1])[0]
+
     def fp8_matvec(self, weight, scales, x):
         """FP8 E4M3FN block-scaled projection with the contract of the
         reference's GLMKernels.fp8_matvec (gpu/runtime.py:1031-1053):

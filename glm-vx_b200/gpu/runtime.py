@@ -84,6 +84,7 @@ SIGNATURES = {
     'glmvx_dsa_scratch_bytes': ([_I32, _I32, _I32, _I32, _I32], _I64),
     'glmvx_dsa_decode': ([_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I32, _I32, _I32, _I32, _I32, _I32, _I32, _I32,
                           _F32, _F32, _P, _U64, _P], _I32),
+    'glmvx_gemm': ([_P, _P, _P, _I32, _I32, _I32, _I32, _P, _P], _I32),
     'glmvx_dsa_append': ([_P, _P, _P, _P, _P, _P, _P, _I32, _I32, _I32, _I32, _I32, _P, _P], _I32),
     'glmvx_moe_workspace_bytes': ([_I32, _I32, _I32, _I32, _I32, _I32], _I64),
     'glmvx_moe_ffn': ([_P, _P, _I32, _I32, _I32, _P, _P, _I32, _I32, _F32, _I32, _P, _P, _P, _P, _P, _P, _P, _U64,

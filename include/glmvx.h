@@ -204,6 +204,15 @@ int32_t glmvx_dsa_append(float *latents, float *rope_keys, float *index_keys, in
                          const float *new_rope, const float *new_index, int32_t batch, int32_t capacity, int32_t rank,
                          int32_t rope_dim, int32_t index_dim, int32_t *full, void *stream);
 
+/* Dense GEMM C[M,N] = A[M,K] B[K,N], row-major f32, the reference's resident
+   GEMM contract (GEMMKernels.gemm, gpu/gemm.py:51-97; gpu/gemm.vx):
+   precision 0 "f32" (f32 multiply-adds), 1 "tf32_rna" (multiplicands rounded
+   to TF32 nearest/ties-away, f32 accumulation on tcgen05 tensor cores with
+   TMEM accumulators).  K = 0 writes zeros; any 4-byte alignment; C must not
+   overlap A or B.  err: device int32 error word (required for precision 1). */
+int32_t glmvx_gemm(float *C, const float *A, const float *B, int32_t M, int32_t N, int32_t K, int32_t precision,
+                   int32_t *err, void *stream);
+
 /* Routed + shared MoE feed-forward layer (decode / small batches), device
  * pointers.  Replaces the per-expert Python loop of glm_vx/model.py:289-324
  * (and its grouped prefill form, glm_vx/prefill.py:44-81) for resident
