@@ -6,17 +6,19 @@
 //   precision "f32": f32 multiply-adds.
 // Any M, N, K >= 0 (K = 0 writes zeros), any 4-byte alignment.
 //
-// tf32_rna on the 5th-generation tensor cores: a CTA owns a 128 x 128 tile
-// of C whose f32 accumulators live in tensor memory (128 lanes x 128
-// columns).  Per 32-wide K block its 128 threads load A [128 x 32] and B
-// [32 x 128] from global memory, round them (cvt.rna.tf32) and store them in
-// shared memory as K-major 128-byte-swizzled tiles (row r of a tile at
-// (r/8)*1024 + (r%8)*128 bytes, 16-byte chunk c at position c ^ (r%8): the
-// canonical SWIZZLE_128B K-major layout of the UMMA descriptors); one thread
-// then issues four tcgen05.mma kind::tf32 (M=128, N=128, K=8) and commits
-// them to an mbarrier.  Two stages: the loads of block k+1 overlap the MMAs
-// of block k.  The epilogue reads the accumulators with tcgen05.ld (warp w
-// owns lanes 32w..32w+31, i.e. rows) and writes C.
+// tf32_rna on the 5th-generation tensor cores: a CTA owns a 128 x 256 tile
+// of C whose f32 accumulators live in tensor memory (128 lanes x 256
+// columns).  Per 32-wide K block its 256 threads load A [128 x 32] and B
+// [32 x 256] from global memory into registers (the next block's loads are
+// in flight while the current one is stored), round them (cvt.rna.tf32) and
+// store them in shared memory as K-major 128-byte-swizzled tiles (row r of a
+// tile at (r/8)*1024 + (r%8)*128 bytes, 16-byte chunk c at position
+// c ^ (r%8): the canonical SWIZZLE_128B K-major layout of the UMMA
+// descriptors; B is transposed on the way); one thread then issues four
+// tcgen05.mma kind::tf32 (M=128, N=256, K=8) and commits them to the stage's
+// mbarrier.  Three stages.  The epilogue reads the accumulators with
+// tcgen05.ld (warp w owns lanes 32*(w%4).. i.e. rows, and half the columns)
+// and writes C.
 #include <cstdint>
 
 #include "common.cuh"
@@ -25,17 +27,17 @@ namespace glmvx {
 
 namespace {
 
-constexpr int kGemmTile = 128, kGemmBK = 32, kGemmStages = 2, kGemmThreads = 128;
-constexpr int kGemmOperandBytes = kGemmTile * kGemmBK * 4;  // 16 KB: 128 rows x 128 bytes
-constexpr int kGemmStageBytes = 2 * kGemmOperandBytes;
+constexpr int kGemmBM = 128, kGemmBN = 256, kGemmBK = 32, kGemmStages = 3, kGemmThreads = 256;
+constexpr int kGemmABytes = kGemmBM * kGemmBK * 4, kGemmBBytes = kGemmBN * kGemmBK * 4;  // 16 KB, 32 KB
+constexpr int kGemmStageBytes = kGemmABytes + kGemmBBytes;
 constexpr int kGemmSmem = kGemmStages * kGemmStageBytes + 1024;  // + alignment slack
-constexpr uint32_t kGemmTmemCols = 128;
+constexpr uint32_t kGemmTmemCols = kGemmBN;
 
 // Instruction descriptor, kind::tf32: D f32 (bits 4-5 = 1), A and B TF32
 // (bits 7-9, 10-12 = 2), both K-major (bits 15, 16 = 0), N >> 3 at bit 17,
 // M >> 4 at bit 24.
-constexpr uint32_t kGemmIdesc = (1u << 4) | (2u << 7) | (2u << 10) | ((kGemmTile >> 3) << 17) |
-                                ((kGemmTile >> 4) << 24);
+constexpr uint32_t kGemmIdesc = (1u << 4) | (2u << 7) | (2u << 10) | ((kGemmBN >> 3) << 17) |
+                                ((kGemmBM >> 4) << 24);
 
 // Shared-memory matrix descriptor of a K-major SWIZZLE_128B tile at `addr`:
 // start address >> 4 (bits 0-13), leading byte offset 16 >> 4 (unused by
@@ -89,6 +91,74 @@ __device__ __forceinline__ uint32_t sw128_offset(int r, int c) {
     return static_cast<uint32_t>((r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4));
 }
 
+// One K block of a CTA's operands in registers: A chunks (row, 4 k) and B
+// blocks (4 k x 4 n), loaded while the previous block is stored and multiplied.
+// VEC: K and N multiples of 4 and A, B 16-byte aligned (float4 loads, whole
+// chunks in or out of range); otherwise scalar loads with per-element bounds.
+constexpr int kGemmAPer = kGemmBM * 8 / kGemmThreads, kGemmBPer = kGemmBN * 8 / (4 * kGemmThreads);
+
+template <bool VEC>
+__device__ __forceinline__ void gemm_load(float4 (&ra)[kGemmAPer], float4 (&rb)[kGemmBPer][4], const float *A,
+                                          const float *B, int M, int N, int K, int m0, int n0, int k0, int tid) {
+#pragma unroll
+    for (int i = 0; i < kGemmAPer; ++i) {
+        const int q = tid + kGemmThreads * i, r = q >> 3, c = q & 7, m = m0 + r, k = k0 + 4 * c;
+        const float *src = A + static_cast<int64_t>(m) * K + k;
+        if (VEC) {
+            ra[i] = (m < M && k < K) ? __ldg(reinterpret_cast<const float4 *>(src)) : make_float4(0.f, 0.f, 0.f, 0.f);
+        } else {
+            ra[i].x = (m < M && k < K) ? __ldg(src) : 0.0f;
+            ra[i].y = (m < M && k + 1 < K) ? __ldg(src + 1) : 0.0f;
+            ra[i].z = (m < M && k + 2 < K) ? __ldg(src + 2) : 0.0f;
+            ra[i].w = (m < M && k + 3 < K) ? __ldg(src + 3) : 0.0f;
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < kGemmBPer; ++i) {
+        // block (k quad kq, n quad nq): a warp covers 32 consecutive n quads of one k quad
+        const int q = tid + kGemmThreads * i, nq = q % (kGemmBN / 4), kq = q / (kGemmBN / 4);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const int k = k0 + 4 * kq + e, n = n0 + 4 * nq;
+            const float *src = B + static_cast<int64_t>(k) * N + n;
+            if (VEC) {
+                rb[i][e] = (k < K && n < N) ? __ldg(reinterpret_cast<const float4 *>(src))
+                                            : make_float4(0.f, 0.f, 0.f, 0.f);
+            } else {
+                rb[i][e].x = (k < K && n < N) ? __ldg(src) : 0.0f;
+                rb[i][e].y = (k < K && n + 1 < N) ? __ldg(src + 1) : 0.0f;
+                rb[i][e].z = (k < K && n + 2 < N) ? __ldg(src + 2) : 0.0f;
+                rb[i][e].w = (k < K && n + 3 < N) ? __ldg(src + 3) : 0.0f;
+            }
+        }
+    }
+}
+
+// Rounded to TF32 and stored as the stage's swizzled K-major tiles (B as B^T).
+__device__ __forceinline__ void gemm_store(uint8_t *as, uint8_t *bs, const float4 (&ra)[kGemmAPer],
+                                           const float4 (&rb)[kGemmBPer][4], int tid) {
+#pragma unroll
+    for (int i = 0; i < kGemmAPer; ++i) {
+        const int q = tid + kGemmThreads * i;
+        *reinterpret_cast<uint4 *>(as + sw128_offset(q >> 3, q & 7)) =
+            make_uint4(tf32_rna(ra[i].x), tf32_rna(ra[i].y), tf32_rna(ra[i].z), tf32_rna(ra[i].w));
+    }
+#pragma unroll
+    for (int i = 0; i < kGemmBPer; ++i) {
+        const int q = tid + kGemmThreads * i, nq = q % (kGemmBN / 4), kq = q / (kGemmBN / 4);
+        // column j of the 4x4 block is row n = 4nq + j of B^T, K chunk kq
+        *reinterpret_cast<uint4 *>(bs + sw128_offset(4 * nq, kq)) = make_uint4(
+            tf32_rna(rb[i][0].x), tf32_rna(rb[i][1].x), tf32_rna(rb[i][2].x), tf32_rna(rb[i][3].x));
+        *reinterpret_cast<uint4 *>(bs + sw128_offset(4 * nq + 1, kq)) = make_uint4(
+            tf32_rna(rb[i][0].y), tf32_rna(rb[i][1].y), tf32_rna(rb[i][2].y), tf32_rna(rb[i][3].y));
+        *reinterpret_cast<uint4 *>(bs + sw128_offset(4 * nq + 2, kq)) = make_uint4(
+            tf32_rna(rb[i][0].z), tf32_rna(rb[i][1].z), tf32_rna(rb[i][2].z), tf32_rna(rb[i][3].z));
+        *reinterpret_cast<uint4 *>(bs + sw128_offset(4 * nq + 3, kq)) = make_uint4(
+            tf32_rna(rb[i][0].w), tf32_rna(rb[i][1].w), tf32_rna(rb[i][2].w), tf32_rna(rb[i][3].w));
+    }
+}
+
+template <bool VEC>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_tf32_kernel(float *__restrict__ C, const float *__restrict__ A, const float *__restrict__ B, int M, int N,
                      int K, int *err) {
@@ -100,7 +170,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const uint32_t pad = ((raw + 1023u) & ~1023u) - raw;  // the swizzle works on address bits: 1 KB-aligned tiles
     uint8_t *tiles = gemm_smem_raw + pad;
     const uint32_t tiles_s = raw + pad;
-    const int m0 = blockIdx.y * kGemmTile, n0 = blockIdx.x * kGemmTile;
+    const int m0 = blockIdx.y * kGemmBM, n0 = blockIdx.x * kGemmBN;
 
     if (warp == 0) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(&tmem_slot)),
@@ -119,6 +189,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
     const int nk = (K + kGemmBK - 1) / kGemmBK;
     bool ok = true;
+    float4 ra[kGemmAPer], rb[kGemmBPer][4];
+    if (nk > 0) gemm_load<VEC>(ra, rb, A, B, M, N, K, m0, n0, 0, tid);
     for (int kb = 0; kb < nk; ++kb) {
         const int s = kb % kGemmStages;
         if (kb >= kGemmStages) ok = mbar_wait_bounded(&mma_done[s], ((kb - kGemmStages) / kGemmStages) & 1);
@@ -127,34 +199,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             ok = false;
             break;
         }
-        uint8_t *as = tiles + s * kGemmStageBytes, *bs = as + kGemmOperandBytes;
-        const int k0 = kb * kGemmBK;
-        // A: row r = q / 8, K chunk c = q % 8 (four consecutive k).
-#pragma unroll 2
-        for (int q = tid; q < kGemmTile * 8; q += kGemmThreads) {
-            const int r = q >> 3, c = q & 7, m = m0 + r, k = k0 + 4 * c;
-            uint32_t v[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e)
-                v[e] = (m < M && k + e < K) ? tf32_rna(__ldg(A + static_cast<int64_t>(m) * K + k + e)) : 0u;
-            *reinterpret_cast<uint4 *>(as + sw128_offset(r, c)) = make_uint4(v[0], v[1], v[2], v[3]);
-        }
-        // B as B^T, K-major: row n = tid (coalesced loads along n), chunk c.
-#pragma unroll 2
-        for (int c = 0; c < 8; ++c) {
-            const int n = n0 + tid, k = k0 + 4 * c;
-            uint32_t v[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e)
-                v[e] = (n < N && k + e < K) ? tf32_rna(__ldg(B + static_cast<int64_t>(k + e) * N + n)) : 0u;
-            *reinterpret_cast<uint4 *>(bs + sw128_offset(tid, c)) = make_uint4(v[0], v[1], v[2], v[3]);
-        }
+        uint8_t *as = tiles + s * kGemmStageBytes;
+        gemm_store(as, as + kGemmABytes, ra, rb, tid);
+        if (kb + 1 < nk) gemm_load<VEC>(ra, rb, A, B, M, N, K, m0, n0, (kb + 1) * kGemmBK, tid);
         // Generic-proxy stores become visible to the tensor cores' async proxy.
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         __syncthreads();
         if (tid == 0) {
             tc_fence_after();
-            const uint32_t a_s = tiles_s + s * kGemmStageBytes, b_s = a_s + kGemmOperandBytes;
+            const uint32_t a_s = tiles_s + s * kGemmStageBytes, b_s = a_s + kGemmABytes;
 #pragma unroll
             for (int kk = 0; kk < kGemmBK / 8; ++kk)  // K = 8 tf32 = 32 bytes per MMA
                 umma_tf32(tmem, umma_desc_sw128(a_s + 32 * kk), umma_desc_sw128(b_s + 32 * kk), kGemmIdesc,
@@ -169,22 +222,32 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     ok = __syncthreads_and(ok);
     tc_fence_after();
-    // Epilogue: thread = row m0 + 32*warp + lane; zeros when K == 0.
-    const int row = m0 + 32 * warp + lane;
+    // Epilogue: warp w reads tensor-memory lanes 32*(w%4).. (rows) and the
+    // column half w/4; zeros when K == 0.
+    const int row = m0 + 32 * (warp & 3) + lane, cbase = 128 * (warp >> 2);
+    const bool vec_out = VEC && (reinterpret_cast<uintptr_t>(C) & 15) == 0;
 #pragma unroll 1
-    for (int c0 = 0; c0 < kGemmTile; c0 += 32) {
+    for (int c0 = cbase; c0 < cbase + 128; c0 += 32) {
         uint32_t v[32];
         if (nk > 0 && ok) {
-            tmem_ld32(tmem + (static_cast<uint32_t>(32 * warp) << 16) + c0, v);
+            tmem_ld32(tmem + (static_cast<uint32_t>(32 * (warp & 3)) << 16) + c0, v);
         } else {
 #pragma unroll
             for (int j = 0; j < 32; ++j) v[j] = 0u;
         }
         if (row < M && ok) {
             float *crow = C + static_cast<int64_t>(row) * N + n0 + c0;
+            if (vec_out && n0 + c0 + 32 <= N) {
 #pragma unroll
-            for (int j = 0; j < 32; ++j)
-                if (n0 + c0 + j < N) crow[j] = __uint_as_float(v[j]);
+                for (int j = 0; j < 32; j += 4)
+                    *reinterpret_cast<float4 *>(crow + j) = make_float4(
+                        __uint_as_float(v[j]), __uint_as_float(v[j + 1]), __uint_as_float(v[j + 2]),
+                        __uint_as_float(v[j + 3]));
+            } else {
+#pragma unroll
+                for (int j = 0; j < 32; ++j)
+                    if (n0 + c0 + j < N) crow[j] = __uint_as_float(v[j]);
+            }
         }
     }
     tc_fence_before();
@@ -268,13 +331,18 @@ GLMVX_EXPORT int32_t glmvx_gemm(float *C, const float *A, const float *B, int32_
         gemm_f32_kernel<<<grid, 256, 0, st>>>(C, A, B, M, N, K);
     } else {
         static const cudaError_t attr =
-            cudaFuncSetAttribute(gemm_tf32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmem);
-        if (attr != cudaSuccess) {
-            set_error("gemm smem: %s", cudaGetErrorString(attr));
+            cudaFuncSetAttribute(gemm_tf32_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmem);
+        static const cudaError_t attr2 =
+            cudaFuncSetAttribute(gemm_tf32_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmem);
+        if (attr != cudaSuccess || attr2 != cudaSuccess) {
+            set_error("gemm smem: %s", cudaGetErrorString(attr != cudaSuccess ? attr : attr2));
             return kCudaError;
         }
-        const dim3 grid((N + kGemmTile - 1) / kGemmTile, (M + kGemmTile - 1) / kGemmTile);
-        gemm_tf32_kernel<<<grid, kGemmThreads, kGemmSmem, st>>>(C, A, B, M, N, K, err);
+        const bool vec = K % 4 == 0 && N % 4 == 0 &&
+                         ((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(B)) & 15) == 0;
+        const dim3 grid((N + kGemmBN - 1) / kGemmBN, (M + kGemmBM - 1) / kGemmBM);
+        if (vec) gemm_tf32_kernel<true><<<grid, kGemmThreads, kGemmSmem, st>>>(C, A, B, M, N, K, err);
+        else gemm_tf32_kernel<false><<<grid, kGemmThreads, kGemmSmem, st>>>(C, A, B, M, N, K, err);
     }
     GLMVX_CUDA(cudaGetLastError());
     return kOk;
