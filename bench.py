@@ -645,11 +645,17 @@ def run_ours(args, ranks):
 
 
 def run_profile_case(args):
-    """Small case for kernel captures: the config-2 layer shapes with only
-    PROFILE_EXPERTS experts (about 240 MB of IQ1_S, still above L2), TOKENS
-    rows, three untimed warm-up forwards then three more.  Prints one status
-    line; no benchmark numbers."""
+    """Small cases for kernel captures (one status line, no benchmark numbers).
+    moe: the config-2 layer shapes with only PROFILE_EXPERTS experts (about
+    240 MB of IQ1_S, still above L2), TOKENS rows, six forwards.
+    gemm: glmvx_gemm tf32_rna at 2048^3 (N(0,1) operands), three launches.
+    dsa: the config-3 fused DSA decode for 16 queries over caches of 32768
+    positions (DSADecoder.step_pinned), three steps."""
     use_ours()
+    if args.profile_case == 'gemm':
+        return profile_gemm()
+    if args.profile_case == 'dsa':
+        return profile_dsa()
     from gpu.backend import GPUBackend
     from gpu import runtime as rt
     from gpu.moe import MoELayer
@@ -672,6 +678,54 @@ def run_profile_case(args):
     return 0
 
 
+def profile_gemm(n=2048):
+    from gpu.backend import GPUBackend
+    from gpu import runtime as rt
+    backend = GPUBackend(0)
+    s = backend.stream.handle
+    a = np.random.default_rng(0).normal(size=(n, n)).astype(np.float32)
+    bufs = [rt.DeviceBuffer(a.nbytes) for _ in range(3)]
+    bufs[0].upload(a, s)
+    bufs[1].upload(a, s)
+    for _ in range(3):
+        rt.check(backend.lib, backend.lib.glmvx_gemm(bufs[2].ptr, bufs[0].ptr, bufs[1].ptr, n, n, n, 1,
+                                                     backend.device.error_address(), s), 'glmvx_gemm')
+    backend.stream.synchronize()
+    backend.device.check_device_error()
+    print(f'profile case ok: tf32 GEMM {n}^3, 3 launches', flush=True)
+    for b in bufs:
+        b.close()
+    backend.close()
+    return 0
+
+
+def profile_dsa(batch=16):
+    from gpu.backend import GPUBackend
+    from gpu.dsa import DSADecoder
+    backend = GPUBackend(0)
+    rng = np.random.default_rng(3)
+    T = DSA_CONTEXT
+    lat = rng.normal(size=(T - 8, DSA_RANK)).astype(np.float32)
+    rk = rng.normal(size=(T - 8, DSA_ROPE)).astype(np.float32)
+    ik = rng.normal(size=(T - 8, DSA_ID)).astype(np.float32)
+    dec = DSADecoder(backend, batch, T)
+    for i in range(batch):
+        dec.load(i, lat, rk, ik)
+    io = dec.pinned_io()
+    for k in ('new_latent', 'new_rope', 'new_index_key', 'q_index'):
+        io[k][...] = rng.normal(size=io[k].shape)
+    io['q_latent'][...] = rng.normal(size=io['q_latent'].shape) * 0.05
+    io['q_rope'][...] = rng.normal(size=io['q_rope'].shape) * 0.05
+    io['head_weights'][...] = rng.normal(size=io['head_weights'].shape) * DSA_IH ** -0.5
+    for _ in range(3):
+        dec.step_pinned()
+    backend.device.check_device_error()
+    print(f'profile case ok: DSA decode, {batch} queries x {T} positions, 3 steps', flush=True)
+    dec.close()
+    backend.close()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument('--gpus', type=int, default=1)
@@ -680,8 +734,8 @@ def main():
     ap.add_argument('--impl', choices=('ours', 'reference'), default='ours')
     ap.add_argument('--cpu-seconds', type=float, default=10.0)
     ap.add_argument('--no-cpu-baseline', action='store_true')
-    ap.add_argument('--profile-case', action='store_true',
-                    help='run the small kernel-capture case (one GPU) instead of the benchmark')
+    ap.add_argument('--profile-case', nargs='?', const='moe', choices=('moe', 'gemm', 'dsa'),
+                    help='run a small kernel-capture case (one GPU) instead of the benchmark')
     args = ap.parse_args()
     if args.profile_case:
         return run_profile_case(args)

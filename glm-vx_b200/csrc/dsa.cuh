@@ -12,6 +12,13 @@ int32_t launch_index_scores_batch(float *out, const float *q, const float *keys,
                                   int heads, int dim, float qk_scale, const int32_t *lens, int64_t key_stride,
                                   int64_t out_stride, int batch, cudaStream_t stream);
 
+// The same scores on the tensor cores (dsa_index.cu); kUnsupported when the
+// shape has no tensor-core kernel (more than 256 heads, or heads x columns
+// beyond its shared-memory budget).
+int32_t launch_index_scores_tc(float *out, const float *q, const float *keys, const float *w, int tokens, int heads,
+                               int dim, float qk_scale, const int32_t *lens, int64_t key_stride, int64_t out_stride,
+                               int batch, cudaStream_t stream);
+
 // indices[b][0:min(k, lens[b])] = stable descending top-k of scores[b][0:lens[b]],
 // the rest of indices[b][0:k] -1.  1 <= k <= 4096.
 int32_t launch_topk_batch(int32_t *indices, const float *scores, int n, int k, const int32_t *lens,

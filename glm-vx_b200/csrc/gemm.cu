@@ -22,6 +22,7 @@
 #include <cstdint>
 
 #include "common.cuh"
+#include "tcgen05.cuh"
 
 namespace glmvx {
 
@@ -33,63 +34,7 @@ constexpr int kGemmStageBytes = kGemmABytes + kGemmBBytes;
 constexpr int kGemmSmem = kGemmStages * kGemmStageBytes + 1024;  // + alignment slack
 constexpr uint32_t kGemmTmemCols = kGemmBN;
 
-// Instruction descriptor, kind::tf32: D f32 (bits 4-5 = 1), A and B TF32
-// (bits 7-9, 10-12 = 2), both K-major (bits 15, 16 = 0), N >> 3 at bit 17,
-// M >> 4 at bit 24.
-constexpr uint32_t kGemmIdesc = (1u << 4) | (2u << 7) | (2u << 10) | ((kGemmBN >> 3) << 17) |
-                                ((kGemmBM >> 4) << 24);
-
-// Shared-memory matrix descriptor of a K-major SWIZZLE_128B tile at `addr`:
-// start address >> 4 (bits 0-13), leading byte offset 16 >> 4 (unused by
-// swizzled K-major layouts), stride byte offset 1024 >> 4 between 8-row
-// groups (bits 32-45), version 1 (bit 46), layout type 2 = SWIZZLE_128B
-// (bits 61-63).
-__device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t addr) {
-    return static_cast<uint64_t>((addr >> 4) & 0x3FFFu) | (1ull << 16) | (64ull << 32) | (1ull << 46) | (2ull << 61);
-}
-
-__device__ __forceinline__ uint32_t tf32_rna(float v) {
-    uint32_t r;
-    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(v));
-    return r;
-}
-
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-
-__device__ __forceinline__ void umma_tf32(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                          uint32_t accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
-        : "memory");
-}
-
-__device__ __forceinline__ void umma_commit(uint64_t *bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
-                 : "memory");
-}
-
-// 32 consecutive accumulator columns of this warp's 32 lanes.
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
-        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
-        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
-          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]),
-          "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]),
-          "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
-        : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-}
-
-// Byte offset of 16-byte chunk `c` (K elements 4c..4c+3) of row r in a
-// K-major SWIZZLE_128B tile.
-__device__ __forceinline__ uint32_t sw128_offset(int r, int c) {
-    return static_cast<uint32_t>((r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4));
-}
+constexpr uint32_t kGemmIdesc = umma_idesc_tf32(kGemmBM, kGemmBN);
 
 // One K block of a CTA's operands in registers: A chunks (row, 4 k) and B
 // blocks (4 k x 4 n), loaded while the previous block is stored and multiplied.
@@ -173,10 +118,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int m0 = blockIdx.y * kGemmBM, n0 = blockIdx.x * kGemmBN;
 
     if (warp == 0) {
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(&tmem_slot)),
-                     "r"(kGemmTmemCols)
-                     : "memory");
-        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+        tmem_alloc(&tmem_slot, kGemmTmemCols);
     }
     if (tid == 0) {
         for (int s = 0; s < kGemmStages; ++s) mbar_init(&mma_done[s], 1);
@@ -203,7 +145,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         gemm_store(as, as + kGemmABytes, ra, rb, tid);
         if (kb + 1 < nk) gemm_load<VEC>(ra, rb, A, B, M, N, K, m0, n0, (kb + 1) * kGemmBK, tid);
         // Generic-proxy stores become visible to the tensor cores' async proxy.
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        fence_proxy_async_smem();
         __syncthreads();
         if (tid == 0) {
             tc_fence_after();
@@ -253,8 +195,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     tc_fence_before();
     __syncthreads();
     if (warp == 0)
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kGemmTmemCols)
-                     : "memory");
+        tmem_dealloc(tmem, kGemmTmemCols);
 }
 
 // precision "f32": 64 x 64 tile per CTA, 16 x 16 threads with 4 x 4
@@ -308,8 +249,8 @@ __global__ void __launch_bounds__(256)
 using namespace glmvx;
 
 // precision 0 = "f32", 1 = "tf32_rna" (gpu/gemm.py:24-47).  C must not
-// overlap A or B.  *err (device int32, the library's device error word when
-// NULL is not allowed) records a tensor-core wait that timed out.
+// overlap A or B.  *err (device int32; NULL: the library's device error
+// word) records a tensor-core wait that timed out.
 GLMVX_EXPORT int32_t glmvx_gemm(float *C, const float *A, const float *B, int32_t M, int32_t N, int32_t K,
                                 int32_t precision, int32_t *err, void *stream) {
     if (M < 0 || N < 0 || K < 0) {
@@ -321,7 +262,8 @@ GLMVX_EXPORT int32_t glmvx_gemm(float *C, const float *A, const float *B, int32_
         return kInvalid;
     }
     if (M == 0 || N == 0) return kOk;
-    if (!C || (K > 0 && (!A || !B)) || (precision == 1 && !err)) {
+    if (!err) err = device_error_word();
+    if (!C || (K > 0 && (!A || !B))) {
         set_error("gemm: null pointer");
         return kInvalid;
     }

@@ -11,6 +11,7 @@
 #include <cfloat>
 
 #include "common.cuh"
+#include "dsa.cuh"
 
 namespace glmvx {
 
@@ -724,6 +725,9 @@ int32_t launch_index_scores_batch(float *out, const float *q, const float *keys,
                                   int heads, int dim, float qk_scale, const int32_t *lens, int64_t key_stride,
                                   int64_t out_stride, int batch, cudaStream_t stream) {
     if (tokens <= 0 || batch <= 0) return kOk;
+    const int32_t tc = launch_index_scores_tc(out, q, keys, w, tokens, heads, dim, qk_scale, lens, key_stride,
+                                              out_stride, batch, stream);
+    if (tc != kUnsupported) return tc;
     const bool vec = dim % 16 == 0 && (reinterpret_cast<uintptr_t>(keys) & 15) == 0 && key_stride % 4 == 0;
     const dim3 grid((tokens + kIndexTokensPerCta - 1) / kIndexTokensPerCta, batch);
     if (vec)

@@ -209,7 +209,7 @@ int32_t glmvx_dsa_append(float *latents, float *rope_keys, float *index_keys, in
    precision 0 "f32" (f32 multiply-adds), 1 "tf32_rna" (multiplicands rounded
    to TF32 nearest/ties-away, f32 accumulation on tcgen05 tensor cores with
    TMEM accumulators).  K = 0 writes zeros; any 4-byte alignment; C must not
-   overlap A or B.  err: device int32 error word (required for precision 1). */
+   overlap A or B.  err: device int32 error word (NULL: the library's own). */
 int32_t glmvx_gemm(float *C, const float *A, const float *B, int32_t M, int32_t N, int32_t K, int32_t precision,
                    int32_t *err, void *stream);
 
