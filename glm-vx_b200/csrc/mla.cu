@@ -32,7 +32,17 @@ namespace {
 
 constexpr int kMlaHeadsPerCta = 8, kMlaMaxSplits = 64, kMlaBatch = 4;
 constexpr int kMlaTileRows = 8, kMlaStages = 3, kMlaMinRowsPerSplit = 16;
-constexpr int kMlaTargetCtas = 148;  // one wave: the shared kernel holds one CTA per SM
+constexpr int kMlaTargetCtas = 148;
+#ifndef GLMVX_MLA_TC
+#define GLMVX_MLA_TC 1
+#endif
+// Shared selections of up to 64 heads take the tensor-core partials
+// (mla_tc.cu) from kMlaTcMinRows selected rows per call (over all queries):
+// below that its few CTAs, each a chain of ~34 dependent load + MMA steps,
+// lose to the CUDA-core kernel's one CTA per SM (measured at 2048 rows per
+// query: 1 and 2 queries faster on CUDA cores, 4 and more on tensor cores).
+constexpr bool kMlaUseTensorCores = GLMVX_MLA_TC != 0;
+constexpr int64_t kMlaTcMinRows = 3 * 2048;  // one wave: the shared kernel holds one CTA per SM
 constexpr int kMergeCols = 32, kMergeGroups = 8;
 
 __device__ __forceinline__ void cp_async16(void *dst, const void *src) {
@@ -478,6 +488,12 @@ __global__ void __launch_bounds__(256)
     if (threadIdx.x == 0) lens[b] = at + 1;
 }
 
+// The merge kernel holds one factor per split in shared memory.
+int32_t check_merge_splits(int splits) {
+    if (splits < 1 || splits > kMlaMaxSplits) return set_error("mla merge: %d splits (1..%d)", splits, kMlaMaxSplits), kInvalid;
+    return kOk;
+}
+
 template <class K>
 int32_t launch_pdl(K kern, dim3 grid, dim3 block, cudaStream_t stream, auto... args) {
     cudaLaunchConfig_t cfg = {};
@@ -503,7 +519,7 @@ using namespace glmvx;
 // its (max, mass).
 GLMVX_EXPORT int64_t glmvx_mla_scratch_bytes(int32_t heads, int32_t rank, int32_t count) {
     if (heads <= 0 || rank <= 0 || count < 0) return -1;
-    const int64_t splits = mla_splits(heads, rank, count);
+    const int64_t splits = std::max(mla_splits(heads, rank, count), mla_tc_splits(count, 1));
     return 4 * splits * heads * (static_cast<int64_t>(rank) + 2);
 }
 
@@ -525,7 +541,10 @@ GLMVX_EXPORT int32_t glmvx_mla_decode(float *out, const float *q_latent, const f
         set_error("mla_decode: count exceeds tokens without a selection");
         return kInvalid;
     }
-    const int splits = mla_splits(heads, rank, count);
+    const bool shared_sel = selection_stride == 0 || !selected;
+    const bool tc = kMlaUseTensorCores && shared_sel && mla_tc_supported(heads, rank, rope_dim, count) &&
+                    count >= kMlaTcMinRows;
+    const int splits = tc ? mla_tc_splits(count, 1) : mla_splits(heads, rank, count);
     const int64_t need = glmvx_mla_scratch_bytes(heads, rank, count);
     if (!scratch || static_cast<int64_t>(scratch_bytes) < need || (reinterpret_cast<uintptr_t>(scratch) & 15)) {
         set_error("mla_decode: scratch needs %lld bytes, 16-byte aligned", static_cast<long long>(need));
@@ -536,7 +555,10 @@ GLMVX_EXPORT int32_t glmvx_mla_decode(float *out, const float *q_latent, const f
     float *stats = numerator + static_cast<size_t>(splits) * heads * rank;
     int32_t rc;
     const int ppl = (rope_dim + 31) / 32;
-    if ((selection_stride == 0 || !selected) && rank <= 512) {  // one selection for every head
+    if (tc) {
+        rc = launch_mla_tc(numerator, stats, q_latent, q_rope, cache_latent, cache_rope, selected, nullptr, heads, rank,
+                           rope_dim, tokens, count, splits, scale, 0, 0, 0, 1, st);
+    } else if (shared_sel && rank <= 512) {  // one selection for every head
         const int per_cta = mla_shared_heads(rank);
         const dim3 grid(splits, (heads + per_cta - 1) / per_cta);
         const bool vec = rank % 4 == 0 && rope_dim % 4 == 0 && (reinterpret_cast<uintptr_t>(cache_latent) & 15) == 0 &&
@@ -565,6 +587,7 @@ GLMVX_EXPORT int32_t glmvx_mla_decode(float *out, const float *q_latent, const f
         }
     }
     if (rc) return rc;
+    if (const int32_t bad = check_merge_splits(splits)) return bad;
     return launch_pdl(mla_merge_kernel, dim3(heads, (rank + kMergeCols - 1) / kMergeCols), dim3(32 * kMergeGroups),
                       st, out, const_cast<const float *>(numerator), const_cast<const float *>(stats), heads, rank,
                       splits);
@@ -585,7 +608,7 @@ GLMVX_EXPORT int32_t glmvx_mla_decode(float *out, const float *q_latent, const f
 GLMVX_EXPORT int64_t glmvx_dsa_scratch_bytes(int32_t batch, int32_t heads, int32_t rank, int32_t capacity,
                                              int32_t topk) {
     if (batch <= 0 || heads <= 0 || rank <= 0 || capacity <= 0 || topk <= 0) return -1;
-    const int64_t splits = mla_splits(heads, rank, topk, batch);
+    const int64_t splits = std::max(mla_splits(heads, rank, topk, batch), mla_tc_splits(topk, batch));
     const auto up16 = [](int64_t b) { return (b + 15) / 16 * 16; };
     return up16(4LL * batch * capacity) + up16(4LL * batch * topk) + 4LL * batch * splits * heads * (rank + 2);
 }
@@ -626,7 +649,9 @@ GLMVX_EXPORT int32_t glmvx_dsa_decode(float *out, int32_t *selected_out, const f
     float *scores = reinterpret_cast<float *>(base);
     int32_t *sel = reinterpret_cast<int32_t *>(base + up16(4LL * batch * capacity));
     float *numerator = reinterpret_cast<float *>(base + up16(4LL * batch * capacity) + up16(4LL * batch * topk));
-    const int splits = mla_splits(heads, rank, topk, batch);
+    const bool tc = kMlaUseTensorCores && mla_tc_supported(heads, rank, rope_dim, topk) &&
+                    static_cast<int64_t>(batch) * topk >= kMlaTcMinRows;
+    const int splits = tc ? mla_tc_splits(topk, batch) : mla_splits(heads, rank, topk, batch);
     float *stats = numerator + static_cast<size_t>(batch) * splits * heads * rank;
     if (selected_out) sel = selected_out;
     int32_t rc = launch_index_scores_batch(scores, q_index, index_keys, head_weights, capacity, index_heads, index_dim,
@@ -635,9 +660,18 @@ GLMVX_EXPORT int32_t glmvx_dsa_decode(float *out, int32_t *selected_out, const f
     if (rc) return rc;
     rc = launch_topk_batch(sel, scores, capacity, topk, lens, capacity, topk, batch, st);
     if (rc) return rc;
+    const int64_t lstride = static_cast<int64_t>(capacity) * rank, rstride = static_cast<int64_t>(capacity) * rope_dim;
+    if (tc) {
+        rc = launch_mla_tc(numerator, stats, q_latent, q_rope, latents, rope_keys, sel, lens, heads, rank, rope_dim,
+                           capacity, topk, splits, scale, lstride, rstride, topk, batch, st);
+        if (rc) return rc;
+        if (const int32_t bad = check_merge_splits(splits)) return bad;
+    return launch_pdl(mla_merge_kernel, dim3(heads, (rank + kMergeCols - 1) / kMergeCols, batch),
+                          dim3(32 * kMergeGroups), st, out, const_cast<const float *>(numerator),
+                          const_cast<const float *>(stats), heads, rank, splits);
+    }
     const int per_cta = mla_shared_heads(rank);
     const dim3 grid(splits, (heads + per_cta - 1) / per_cta, batch);
-    const int64_t lstride = static_cast<int64_t>(capacity) * rank, rstride = static_cast<int64_t>(capacity) * rope_dim;
     const bool vec = rank % 4 == 0 && rope_dim % 4 == 0 && (reinterpret_cast<uintptr_t>(latents) & 15) == 0 &&
                      (rope_dim == 0 || (reinterpret_cast<uintptr_t>(rope_keys) & 15) == 0);
     const int ppl = (rope_dim + 31) / 32;
@@ -650,6 +684,7 @@ GLMVX_EXPORT int32_t glmvx_dsa_decode(float *out, int32_t *selected_out, const f
     rc = ppl <= 2 ? GLMVX_DSA_SHARED(2) : GLMVX_DSA_SHARED(4);
 #undef GLMVX_DSA_SHARED
     if (rc) return rc;
+    if (const int32_t bad = check_merge_splits(splits)) return bad;
     return launch_pdl(mla_merge_kernel, dim3(heads, (rank + kMergeCols - 1) / kMergeCols, batch),
                       dim3(32 * kMergeGroups), st, out, const_cast<const float *>(numerator),
                       const_cast<const float *>(stats), heads, rank, splits);

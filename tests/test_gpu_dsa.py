@@ -104,3 +104,23 @@ def test_dsa_validation(gpu_backend):
             dec.load(2, np.zeros((1, 64), 'f4'), np.zeros((1, 8), 'f4'), np.zeros((1, 16), 'f4'))
     finally:
         dec.close()
+
+
+@pytest.mark.parametrize('B,lens,heads,rank,rdim,topk', [(4, (5000, 4096, 2047, 6000), 64, 512, 64, 2048),
+                                                         (8, (1500, 1024, 3, 900, 1400, 1100, 1023, 1499), 20, 256, 32,
+                                                          1024)])
+def test_dsa_decode_tensor_core_batches(gpu_backend, B, lens, heads, rank, rdim, topk):
+    """Batches of at least 6144 selected rows run the MLA partials on tcgen05."""
+    from gpu.dsa import DSADecoder
+    rng = np.random.default_rng(B * 7 + topk)
+    ih, idim = 32, 128
+    dec = DSADecoder(gpu_backend, B, max(lens) + 2, heads=heads, rank=rank, rope_dim=rdim, index_heads=ih,
+                     index_dim=idim, topk=topk)
+    try:
+        caches, step = _case(rng, B, lens, heads, rank, rdim, ih, idim)
+        for b, c in enumerate(caches):
+            dec.load(b, *c)
+        out, sel = dec.step(**step)
+        _check(gpu_backend, dec, caches, step, out, sel)
+    finally:
+        dec.close()

@@ -111,3 +111,21 @@ def test_empty_selection_and_validation(cuda_lib, gpu_backend):
                       ((q, qr, latent, rope, np.inf), 'positive')]:
         with pytest.raises(ValueError, match=msg):
             gpu_backend.compressed_attention(*args)
+
+
+@pytest.mark.parametrize('heads,rank,rdim,tokens,count', [(64, 512, 64, 9000, 6144), (17, 510, 62, 7000, 6200),
+                                                          (5, 96, 0, 6500, 6500), (64, 512, 64, 8192, 8192)])
+def test_tensor_core_partials(cuda_lib, heads, rank, rdim, tokens, count):
+    """From 6144 selected rows a shared selection takes the tcgen05 partials
+    (3xTF32 split): same contract, same tolerance; masked ids included."""
+    rng = np.random.default_rng(heads + rank + count)
+    q = (rng.normal(size=(heads, rank)) * 0.05).astype('f4')
+    qr = (rng.normal(size=(heads, rdim)) * 0.05).astype('f4')
+    latent = rng.normal(size=(tokens, rank)).astype('f4')
+    rope = rng.normal(size=(tokens, rdim)).astype('f4')
+    ids = rng.choice(tokens, count, replace=False).astype(np.int32)
+    ids[::13] = -1
+    ids[5::17] = tokens + 3
+    got = _device(cuda_lib, q, qr, latent, rope, ids, 0, count, (192 + 64) ** -0.5)
+    want = mla_ref(q, qr, latent, rope, (192 + 64) ** -0.5, [ids] * heads)
+    np.testing.assert_allclose(got, want, rtol=5e-5, atol=3e-6)
