@@ -19,7 +19,7 @@
 // heads against every staged row: a row crosses L2 once per 16 heads and
 // each shared-memory word read feeds two heads.  Per-head selections take
 // mla_partial_kernel, a warp per head reading its rows directly.  The merge
-// spreads each head over 32-column blocks and eight groups of splits.
+// takes one warp per head and 128-column block, a float4 of columns per lane.
 #include <algorithm>
 #include <cmath>
 
@@ -43,7 +43,7 @@ constexpr int kMlaTargetCtas = 148;
 // query: 1 and 2 queries faster on CUDA cores, 4 and more on tensor cores).
 constexpr bool kMlaUseTensorCores = GLMVX_MLA_TC != 0;
 constexpr int64_t kMlaTcMinRows = 3 * 2048;  // one wave: the shared kernel holds one CTA per SM
-constexpr int kMergeCols = 32, kMergeGroups = 8;
+constexpr int kMergeCols = 128;  // columns per merge warp
 
 __device__ __forceinline__ void cp_async16(void *dst, const void *src) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
@@ -374,56 +374,65 @@ __global__ void __launch_bounds__(32 * kMlaHeadsPerCta)
     }
 }
 
-// Grid (heads, rank / 32): per split a factor e^(m_s - max) over the splits
-// with mass (warp 0), then warp g sums splits g, g + 8, ... of 32 columns
-// and the eight partial sums are added in group order.
-__global__ void __launch_bounds__(32 * kMergeGroups)
+// Grid (heads, ceil(rank / 128), queries), one warp: the lanes turn the
+// splits' (max, mass) into factors e^(m_s - max) (splits with mass) and the
+// denominator; then each lane adds its float4 of the 128-column block over
+// the splits in split order (loads of 8 splits in flight).
+__global__ void __launch_bounds__(32)
     mla_merge_kernel(float *__restrict__ out, const float *__restrict__ numerator, const float *__restrict__ stats,
                      int heads, int rank, int splits) {
     __shared__ float f[kMlaMaxSplits];
-    __shared__ float part[kMergeGroups][kMergeCols];
-    __shared__ float s_den;
     grid_dependency_wait();
     allow_dependent_launch();
+    const int h = blockIdx.x, lane = threadIdx.x;
     out += static_cast<size_t>(blockIdx.z) * heads * rank;  // query of a batch
     numerator += static_cast<size_t>(blockIdx.z) * splits * heads * rank;
     stats += static_cast<size_t>(blockIdx.z) * splits * heads * 2;
-    const int h = blockIdx.x, tid = threadIdx.x, lane = tid & 31, g = tid >> 5;
-    if (g == 0) {
-        float mx = -INFINITY;
-        for (int s = lane; s < splits; s += 32) {
-            const size_t task = static_cast<size_t>(s) * heads + h;
-            if (stats[task * 2 + 1] > 0.0f) mx = fmaxf(mx, stats[task * 2]);
+    float mx = -INFINITY;
+    for (int s = lane; s < splits; s += 32) {
+        const size_t task = static_cast<size_t>(s) * heads + h;
+        if (stats[task * 2 + 1] > 0.0f) mx = fmaxf(mx, stats[task * 2]);
+    }
+    mx = warp_max(mx);
+    float den = 0.0f;
+    for (int s = lane; s < splits; s += 32) {
+        const size_t task = static_cast<size_t>(s) * heads + h;
+        const float ls = stats[task * 2 + 1];
+        const float e = ls > 0.0f ? expf(stats[task * 2] - mx) : -1.0f;  // -1: no mass
+        f[s] = e;
+        if (ls > 0.0f) den = fmaf(ls, e, den);
+    }
+    den = warp_sum(den);
+    __syncwarp();
+    const int c = 128 * blockIdx.y + 4 * lane;
+    if (c >= rank) return;
+    const bool vec = (rank & 3) == 0;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 8
+    for (int s = 0; s < splits; ++s) {
+        const float fs = f[s];
+        if (fs >= 0.0f) {
+            const float *row = numerator + (static_cast<size_t>(s) * heads + h) * rank + c;
+            float4 v;
+            if (vec) {
+                v = *reinterpret_cast<const float4 *>(row);
+            } else {
+                v.x = row[0];
+                v.y = c + 1 < rank ? row[1] : 0.0f;
+                v.z = c + 2 < rank ? row[2] : 0.0f;
+                v.w = c + 3 < rank ? row[3] : 0.0f;
+            }
+            acc.x = fmaf(v.x, fs, acc.x);
+            acc.y = fmaf(v.y, fs, acc.y);
+            acc.z = fmaf(v.z, fs, acc.z);
+            acc.w = fmaf(v.w, fs, acc.w);
         }
-        mx = warp_max(mx);
-        float den = 0.0f;
-        for (int s = lane; s < splits; s += 32) {
-            const size_t task = static_cast<size_t>(s) * heads + h;
-            const float ls = stats[task * 2 + 1];
-            const float e = ls > 0.0f ? expf(stats[task * 2] - mx) : -1.0f;  // -1: no mass
-            f[s] = e;
-            if (ls > 0.0f) den = fmaf(ls, e, den);
-        }
-        den = warp_sum(den);
-        if (lane == 0) s_den = den;
     }
-    __syncthreads();
-    const int c = blockIdx.y * kMergeCols + lane;
-    float sum = 0.0f;
-    if (c < rank) {
-#pragma unroll 4
-        for (int s = g; s < splits; s += kMergeGroups)
-            if (f[s] >= 0.0f) sum = fmaf(numerator[(static_cast<size_t>(s) * heads + h) * rank + c], f[s], sum);
-    }
-    part[g][lane] = sum;
-    __syncthreads();
-    if (g == 0 && c < rank) {
-        float tot = 0.0f;
-#pragma unroll
-        for (int i = 0; i < kMergeGroups; ++i) tot += part[i][lane];
-        const float den = s_den;
-        out[static_cast<size_t>(h) * rank + c] = den > 0.0f ? tot / den : 0.0f;
-    }
+    float *o = out + static_cast<size_t>(h) * rank + c;
+    o[0] = den > 0.0f ? acc.x / den : 0.0f;
+    if (c + 1 < rank) o[1] = den > 0.0f ? acc.y / den : 0.0f;
+    if (c + 2 < rank) o[2] = den > 0.0f ? acc.z / den : 0.0f;
+    if (c + 3 < rank) o[3] = den > 0.0f ? acc.w / den : 0.0f;
 }
 
 // Heads per CTA: two per warp in the shared-selection kernel (rank <= 512),
@@ -588,9 +597,8 @@ GLMVX_EXPORT int32_t glmvx_mla_decode(float *out, const float *q_latent, const f
     }
     if (rc) return rc;
     if (const int32_t bad = check_merge_splits(splits)) return bad;
-    return launch_pdl(mla_merge_kernel, dim3(heads, (rank + kMergeCols - 1) / kMergeCols), dim3(32 * kMergeGroups),
-                      st, out, const_cast<const float *>(numerator), const_cast<const float *>(stats), heads, rank,
-                      splits);
+    return launch_pdl(mla_merge_kernel, dim3(heads, (rank + kMergeCols - 1) / kMergeCols), dim3(32), st, out,
+                      const_cast<const float *>(numerator), const_cast<const float *>(stats), heads, rank, splits);
 }
 
 // ---- Fused DSA decode for a batch of queries over device-resident
@@ -666,9 +674,8 @@ GLMVX_EXPORT int32_t glmvx_dsa_decode(float *out, int32_t *selected_out, const f
                            capacity, topk, splits, scale, lstride, rstride, topk, batch, st);
         if (rc) return rc;
         if (const int32_t bad = check_merge_splits(splits)) return bad;
-    return launch_pdl(mla_merge_kernel, dim3(heads, (rank + kMergeCols - 1) / kMergeCols, batch),
-                          dim3(32 * kMergeGroups), st, out, const_cast<const float *>(numerator),
-                          const_cast<const float *>(stats), heads, rank, splits);
+        return launch_pdl(mla_merge_kernel, dim3(heads, (rank + kMergeCols - 1) / kMergeCols, batch), dim3(32), st, out,
+                          const_cast<const float *>(numerator), const_cast<const float *>(stats), heads, rank, splits);
     }
     const int per_cta = mla_shared_heads(rank);
     const dim3 grid(splits, (heads + per_cta - 1) / per_cta, batch);
@@ -685,9 +692,8 @@ GLMVX_EXPORT int32_t glmvx_dsa_decode(float *out, int32_t *selected_out, const f
 #undef GLMVX_DSA_SHARED
     if (rc) return rc;
     if (const int32_t bad = check_merge_splits(splits)) return bad;
-    return launch_pdl(mla_merge_kernel, dim3(heads, (rank + kMergeCols - 1) / kMergeCols, batch),
-                      dim3(32 * kMergeGroups), st, out, const_cast<const float *>(numerator),
-                      const_cast<const float *>(stats), heads, rank, splits);
+    return launch_pdl(mla_merge_kernel, dim3(heads, (rank + kMergeCols - 1) / kMergeCols, batch), dim3(32), st, out,
+                      const_cast<const float *>(numerator), const_cast<const float *>(stats), heads, rank, splits);
 }
 
 // Appends one row per query to the caches of glmvx_dsa_decode (device

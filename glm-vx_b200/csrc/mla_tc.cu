@@ -33,7 +33,7 @@ namespace glmvx {
 
 namespace {
 
-constexpr int kMtRows = 128, kMtThreads = 128, kMtChunk = 32, kMtMaxHeads = 64, kMtMaxRank = 512;
+constexpr int kMtRows = 128, kMtThreads = 256, kMtChunk = 32, kMtMaxHeads = 64, kMtMaxRank = 512;
 constexpr int kMtMaxRope = 64, kMtMaxSplits = 64;  // splits per query: the merge kernel's limit
 constexpr int kMtTile = kMtRows * kMtChunk * 4;        // 16 KB: one hi or lo operand tile of 128 rows
 constexpr int kMtQTile = kMtMaxHeads * kMtChunk * 4;   // 8 KB: a 32-column chunk of <= 64 query heads
@@ -90,7 +90,7 @@ __global__ void __launch_bounds__(kMtThreads, 1) mla_tc_kernel(MtArgs a) {
     __shared__ uint64_t phase_done;
     __shared__ uint32_t tmem_slot;
     __shared__ int s_ids[kMtRows];
-    __shared__ float s_red[2][kMtMaxHeads], s_mass[2][kMtMaxHeads];
+    __shared__ float s_red[4][kMtMaxHeads], s_mass[4][kMtMaxHeads];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int split = blockIdx.x, bq = blockIdx.z;
     int tokens = a.tokens, count = a.count;
@@ -121,7 +121,7 @@ __global__ void __launch_bounds__(kMtThreads, 1) mla_tc_kernel(MtArgs a) {
         mbar_init(&phase_done, 1);
         fence_mbar_init();
     }
-    {
+    if (tid < kMtRows) {
         const int j = j0 + tid;
         int id = -1;
         if (j < j1) {
@@ -141,62 +141,58 @@ __global__ void __launch_bounds__(kMtThreads, 1) mla_tc_kernel(MtArgs a) {
     bool ok = true;
     int done_phase = 0;  // completions of phase_done waited for
 
-    // Registers of one step: phase 1 K rows (8 float4) + Q heads (<= 4
-    // float4); phase 3 V rows (8 float4, 4 columns x 8 rows per thread).
-    float4 rk[8], rq[4];
-    auto load_step = [&](int st) {
+    // Registers of one step: phase 1 K rows (4 float4) + Q heads (2 float4);
+    // phase 3 V rows (4 float4: 4 columns x 4 rows per thread).  Two sets:
+    // the loads of steps st+1 and st+2 are in flight during step st.
+    float4 rk0[4], rq0[2], rk1[4], rq1[2];
+    auto load_step = [&](int st, float4 (&rk)[4], float4 (&rq)[2]) {
         if (st < nch) {  // K chunk st: row r = i >> 3, columns 4p.. (p = i & 7)
             const bool lat = st < cl;
             const int c0 = lat ? kMtChunk * st : kMtChunk * (st - cl), width = lat ? rank : rope_dim;
             const float *src_base = lat ? latent : rope;
 #pragma unroll
-            for (int jj = 0; jj < 8; ++jj) {
+            for (int jj = 0; jj < 4; ++jj) {
                 const int i = tid + kMtThreads * jj, r = i >> 3, d = c0 + 4 * (i & 7), id = s_ids[r];
                 rk[jj] = id >= 0 ? mt_ld4<VEC>(src_base + static_cast<int64_t>(id) * width + d, width - d)
                                  : make_float4(0.f, 0.f, 0.f, 0.f);
             }
             const float *qb = lat ? q_latent : q_rope;
 #pragma unroll
-            for (int jj = 0; jj < 4; ++jj) {
+            for (int jj = 0; jj < 2; ++jj) {
                 const int i = tid + kMtThreads * jj, h = i >> 3, d = c0 + 4 * (i & 7);
-                rq[jj] = (h < heads && jj < n_pad / 16) ? mt_ld4<VEC>(qb + static_cast<size_t>(h) * width + d, width - d)
-                                                        : make_float4(0.f, 0.f, 0.f, 0.f);
+                rq[jj] = h < heads ? mt_ld4<VEC>(qb + static_cast<size_t>(h) * width + d, width - d)
+                                   : make_float4(0.f, 0.f, 0.f, 0.f);
             }
-        } else {  // V^T block mb, rows 32kc + 8g .. + 7 (g = tid >> 5), columns 128mb + 4 (tid & 31) ..
+        } else {  // V^T block mb, rows 32kc + 4g .. + 3 (g = tid >> 5), columns 128mb + 4 lane ..
             const int k = st - nch, mb = k >> 2, kc = k & 3, g = tid >> 5, d = 128 * mb + 4 * lane;
 #pragma unroll
-            for (int jj = 0; jj < 8; ++jj) {
-                const int id = s_ids[32 * kc + 8 * g + jj];
+            for (int jj = 0; jj < 4; ++jj) {
+                const int id = s_ids[32 * kc + 4 * g + jj];
                 rk[jj] = id >= 0 ? mt_ld4<VEC>(latent + static_cast<int64_t>(id) * rank + d, rank - d)
                                  : make_float4(0.f, 0.f, 0.f, 0.f);
             }
         }
     };
-    auto store_step = [&](int st, uint8_t *stage) {
+    auto store_step = [&](int st, uint8_t *stage, const float4 (&rk)[4], const float4 (&rq)[2]) {
         uint8_t *t_hi = stage, *t_lo = stage + kMtTile;
         if (st < nch) {
 #pragma unroll
-            for (int jj = 0; jj < 8; ++jj) {
+            for (int jj = 0; jj < 4; ++jj) {
                 const int i = tid + kMtThreads * jj;
                 mt_store_split(t_hi, t_lo, sw128_offset(i >> 3, i & 7), rk[jj]);
             }
             uint8_t *q_hi = stage + 2 * kMtTile, *q_lo = q_hi + kMtQTile;
 #pragma unroll
-            for (int jj = 0; jj < 4; ++jj) {
+            for (int jj = 0; jj < 2; ++jj) {
                 const int i = tid + kMtThreads * jj;
-                if (jj < n_pad / 16) mt_store_split(q_hi, q_lo, sw128_offset(i >> 3, i & 7), rq[jj]);
+                if ((i >> 3) < n_pad) mt_store_split(q_hi, q_lo, sw128_offset(i >> 3, i & 7), rq[jj]);
             }
-        } else {  // transpose: column 4*lane + e of the block is row e of V^T, rows 8g..8g+7 two chunks
+        } else {  // transpose: column 4*lane + e of the block is row e of V^T; rows 4g..4g+3 are chunk g
             const int g = tid >> 5;
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const int row = 4 * lane + e;
-                const float *f = reinterpret_cast<const float *>(rk);  // rk[jj] component e: f[4 jj + e]
-                mt_store_split(t_hi, t_lo, sw128_offset(row, 2 * g),
-                               make_float4(f[e], f[4 + e], f[8 + e], f[12 + e]));
-                mt_store_split(t_hi, t_lo, sw128_offset(row, 2 * g + 1),
-                               make_float4(f[16 + e], f[20 + e], f[24 + e], f[28 + e]));
-            }
+            mt_store_split(t_hi, t_lo, sw128_offset(4 * lane, g), make_float4(rk[0].x, rk[1].x, rk[2].x, rk[3].x));
+            mt_store_split(t_hi, t_lo, sw128_offset(4 * lane + 1, g), make_float4(rk[0].y, rk[1].y, rk[2].y, rk[3].y));
+            mt_store_split(t_hi, t_lo, sw128_offset(4 * lane + 2, g), make_float4(rk[0].z, rk[1].z, rk[2].z, rk[3].z));
+            mt_store_split(t_hi, t_lo, sw128_offset(4 * lane + 3, g), make_float4(rk[0].w, rk[1].w, rk[2].w, rk[3].w));
         }
     };
     auto issue_step = [&](int st, uint32_t stage_s) {
@@ -232,42 +228,40 @@ __global__ void __launch_bounds__(kMtThreads, 1) mla_tc_kernel(MtArgs a) {
         return __syncthreads_and(w);
     };
 
-    load_step(0);
-    for (int st = 0; st < steps && ok; ++st) {
+    // One step on register set (rk, rq): false when a bounded wait expired.
+    auto step = [&](int st, float4 (&rk)[4], float4 (&rq)[2]) -> bool {
         const int s = st % kMtStages;
-        if (st >= kMtStages) ok = mbar_wait_bounded(&mma_done[s], ((st - kMtStages) / kMtStages) & 1);
-        if (!__syncthreads_and(ok)) {
-            ok = false;
-            break;
-        }
+        bool w = true;
+        if (st >= kMtStages) w = mbar_wait_bounded(&mma_done[s], ((st - kMtStages) / kMtStages) & 1);
+        if (!__syncthreads_and(w)) return false;
         if (st == nch) {
             // ---- phase 2: softmax of the split from S^T (all S MMAs committed below) ----
-            if (!wait_phase()) {
-                ok = false;
-                break;
-            }
+            if (!wait_phase()) return false;
             tc_fence_after();
-            const int r = 32 * warp + lane;
-            const bool valid = s_ids[r] >= 0;
-            for (int h0 = 0; h0 < n_pad; h0 += 32) {
-                uint32_t v[32];
-                tmem_ld32(tmem + (static_cast<uint32_t>(32 * warp) << 16) + kMtSCol + h0, v);
+            {  // warp w: rows 32 (w % 4) + lane, head columns 32 (w / 4) ..
+                const int r = 32 * (warp & 3) + lane, h0 = 32 * (warp >> 2);
+                const bool valid = s_ids[r] >= 0;
+                if (h0 < n_pad) {
+                    uint32_t v[32];
+                    tmem_ld32(tmem + (static_cast<uint32_t>(32 * (warp & 3)) << 16) + kMtSCol + h0, v);
 #pragma unroll
-                for (int j = 0; j < 32; ++j)
-                    if (h0 + j < n_pad) sbuf[r * kMtSStride + h0 + j] = valid ? __uint_as_float(v[j]) * a.scale : -INFINITY;
+                    for (int j = 0; j < 32; ++j)
+                        if (h0 + j < n_pad)
+                            sbuf[r * kMtSStride + h0 + j] = valid ? __uint_as_float(v[j]) * a.scale : -INFINITY;
+                }
             }
             __syncthreads();
-            const int h = tid & 63, half = tid >> 6;
+            const int h = tid & 63, qq = tid >> 6;  // head, quarter of the rows (32 rows = one P^T atom)
             float m = -INFINITY;
             if (h < n_pad)
-                for (int rr = 64 * half; rr < 64 * half + 64; ++rr) m = fmaxf(m, sbuf[rr * kMtSStride + h]);
-            s_red[half][h] = m;
+                for (int rr = 32 * qq; rr < 32 * qq + 32; ++rr) m = fmaxf(m, sbuf[rr * kMtSStride + h]);
+            s_red[qq][h] = m;
             __syncthreads();
-            m = fmaxf(s_red[0][h], s_red[1][h]);
+            m = fmaxf(fmaxf(s_red[0][h], s_red[1][h]), fmaxf(s_red[2][h], s_red[3][h]));
             float mass = 0.0f;
             if (h < n_pad) {
-                for (int c = 0; c < 16; ++c) {  // rows 64 half + 4c .. + 3: one 16-byte chunk of P^T row h
-                    const int r0 = 64 * half + 4 * c;
+                for (int c = 0; c < 8; ++c) {  // rows 32 qq + 4c .. + 3: chunk c of P^T row h in atom qq
+                    const int r0 = 32 * qq + 4 * c;
                     float4 p;
                     float *pp = &p.x;
 #pragma unroll
@@ -276,25 +270,24 @@ __global__ void __launch_bounds__(kMtThreads, 1) mla_tc_kernel(MtArgs a) {
                         pp[e] = sv == -INFINITY ? 0.0f : expf(sv - m);
                         mass += pp[e];
                     }
-                    const int atom = r0 >> 5, chunk = (r0 & 31) >> 2;
-                    mt_store_split(ph + atom * kMtPTile, pl + atom * kMtPTile, sw128_offset(h, chunk), p);
+                    mt_store_split(ph + qq * kMtPTile, pl + qq * kMtPTile, sw128_offset(h, c), p);
                 }
             }
-            s_mass[half][h] = mass;
+            s_mass[qq][h] = mass;
             fence_proxy_async_smem();
             tc_fence_before();
             __syncthreads();
             tc_fence_after();
             if (tid < heads) {
                 const size_t task = static_cast<size_t>(split) * heads + tid;
-                stats[task * 2] = s_red[0][tid] > s_red[1][tid] ? s_red[0][tid] : s_red[1][tid];
-                stats[task * 2 + 1] = s_mass[0][tid] + s_mass[1][tid];
+                stats[task * 2] = fmaxf(fmaxf(s_red[0][tid], s_red[1][tid]), fmaxf(s_red[2][tid], s_red[3][tid]));
+                stats[task * 2 + 1] = (s_mass[0][tid] + s_mass[1][tid]) + (s_mass[2][tid] + s_mass[3][tid]);
             }
             __syncthreads();  // the ring (sbuf) is free again
         }
         uint8_t *stage = base + s * kMtStage;
-        store_step(st, stage);
-        if (st + 1 < steps) load_step(st + 1);
+        store_step(st, stage, rk, rq);
+        if (st + 2 < steps) load_step(st + 2, rk, rq);
         fence_proxy_async_smem();
         __syncthreads();
         if (tid == 0) {
@@ -303,15 +296,23 @@ __global__ void __launch_bounds__(kMtThreads, 1) mla_tc_kernel(MtArgs a) {
             umma_commit(&mma_done[s]);
             if (st == nch - 1 || st == steps - 1) umma_commit(&phase_done);
         }
+        return true;
+    };
+    load_step(0, rk0, rq0);
+    if (steps > 1) load_step(1, rk1, rq1);
+    for (int st = 0; st < steps && ok; st += 2) {
+        ok = step(st, rk0, rq0);
+        if (ok && st + 1 < steps) ok = step(st + 1, rk1, rq1);
     }
     if (ok) ok = wait_phase();  // every O^T MMA
     if (ok) {
         tc_fence_after();
-        for (int mb = 0; mb < nb; ++mb) {
-            const int d = 128 * mb + 32 * warp + lane;  // latent column = tensor-memory lane of block mb
-            for (int h0 = 0; h0 < n_pad; h0 += 32) {
+        const int h0 = 32 * (warp >> 2);  // warp w: lanes 32 (w % 4) .. of each block, heads h0 ..
+        if (h0 < n_pad) {
+            for (int mb = 0; mb < nb; ++mb) {
+                const int d = 128 * mb + 32 * (warp & 3) + lane;  // latent column = tensor-memory lane of block mb
                 uint32_t v[32];
-                tmem_ld32(tmem + (static_cast<uint32_t>(32 * warp) << 16) + 64 * mb + h0, v);
+                tmem_ld32(tmem + (static_cast<uint32_t>(32 * (warp & 3)) << 16) + 64 * mb + h0, v);
                 if (d < rank) {
 #pragma unroll
                     for (int j = 0; j < 32; ++j)

@@ -410,9 +410,91 @@ __global__ void __launch_bounds__(1024)
 // One CTA, k <= kTopkSelectMaxK.  With STAGED the n keys are computed once
 // into shared memory (n <= kTopkStagedScores) and every pass reads them
 // there; otherwise each pass re-reads the scores.
-constexpr int kTopkSelectMaxK = 4096, kTopkSelectThreads = 1024, kTopkStagedScores = 44 * 1024;
+constexpr int kTopkSelectMaxK = 4096, kTopkSelectThreads = 1024, kTopkStagedScores = 36 * 1024;
 constexpr int kTopkBins = 4096;  // 12-bit digits
-constexpr int kTopkSelectSmem = kTopkSelectMaxK * 8 + kTopkBins * 4;  // sel + hist, before the staged keys
+// sel + the merge sort's second buffer + hist, before the staged keys
+constexpr int kTopkSelectSmem = 2 * kTopkSelectMaxK * 8 + kTopkBins * 4;
+
+__device__ __forceinline__ uint64_t shfl_xor_u64(uint64_t v, int m) {
+    const uint32_t lo = __shfl_xor_sync(0xffffffffu, static_cast<uint32_t>(v), m);
+    const uint32_t hi = __shfl_xor_sync(0xffffffffu, static_cast<uint32_t>(v >> 32), m);
+    return (static_cast<uint64_t>(hi) << 32) | lo;
+}
+
+// Ascending bitonic sort of the warp's 64 words, lane l holding positions
+// 2l (a) and 2l+1 (b): compare-exchanges across lanes by shuffles.
+__device__ __forceinline__ void warp_sort64(uint64_t &a, uint64_t &b) {
+    const int lane = threadIdx.x & 31;
+#pragma unroll
+    for (int size = 2; size <= 64; size <<= 1) {
+        const bool up = ((2 * lane) & size) == 0;
+#pragma unroll
+        for (int stride = size >> 1; stride > 0; stride >>= 1) {
+            if (stride == 1) {
+                if ((a > b) == up) {
+                    const uint64_t t = a;
+                    a = b;
+                    b = t;
+                }
+            } else {
+                const int ls = stride >> 1;
+                const uint64_t pa = shfl_xor_u64(a, ls), pb = shfl_xor_u64(b, ls);
+                const bool keep_min = ((lane & ls) == 0) == up;
+                a = keep_min ? (a < pa ? a : pa) : (a > pa ? a : pa);
+                b = keep_min ? (b < pb ? b : pb) : (b > pb ? b : pb);
+            }
+        }
+    }
+}
+
+// Ascending sort of n2 (a power of two) words of buf by warp-sorted runs of
+// 64 and log2(n2/64) merge levels: each word's place in the merged run is
+// its place in its own run plus its rank in the partner run (lower bound
+// from the left run, upper bound from the right, so equal words keep
+// distinct places).  tmp: n2 more words.  Returns the buffer holding the
+// result.  Every thread of the block calls it.
+__device__ uint64_t *block_merge_sort(uint64_t *buf, uint64_t *tmp, int n2) {
+    if (n2 < 64) {
+        bitonic_sort(buf, n2);
+        return buf;
+    }
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, warps = blockDim.x >> 5;
+    for (int run = warp; run < n2 / 64; run += warps) {
+        uint64_t a = buf[64 * run + 2 * lane], b = buf[64 * run + 2 * lane + 1];
+        warp_sort64(a, b);
+        buf[64 * run + 2 * lane] = a;
+        buf[64 * run + 2 * lane + 1] = b;
+    }
+    __syncthreads();
+    uint64_t *src = buf, *dst = tmp;
+    for (int len = 64; len < n2; len <<= 1) {
+        for (int i = threadIdx.x; i < n2; i += blockDim.x) {
+            const uint64_t x = src[i];
+            const int r = i / len, p = i - r * len;
+            const uint64_t *other = src + (r ^ 1) * len;
+            int lo = 0, hi = len;
+            if ((r & 1) == 0) {
+                while (lo < hi) {
+                    const int mid = (lo + hi) >> 1;
+                    if (other[mid] < x) lo = mid + 1;
+                    else hi = mid;
+                }
+            } else {
+                while (lo < hi) {
+                    const int mid = (lo + hi) >> 1;
+                    if (other[mid] <= x) lo = mid + 1;
+                    else hi = mid;
+                }
+            }
+            dst[(r & ~1) * len + p + lo] = x;
+        }
+        __syncthreads();
+        uint64_t *t = src;
+        src = dst;
+        dst = t;
+    }
+    return src;
+}
 
 __device__ __forceinline__ uint32_t topk_desc(float v) { return static_cast<uint32_t>(topk_key(v, 0) >> 32); }
 
@@ -448,12 +530,13 @@ __device__ __forceinline__ int block_scan_incl(int v, int *s_warp) {
 }
 
 template <bool STAGED>
-__global__ void __launch_bounds__(kTopkSelectThreads)
+__global__ void __launch_bounds__(kTopkSelectThreads, 1)
     topk_select_kernel(int32_t *indices, const float *scores, int n, int k, const int32_t *lens, int64_t score_stride,
                        int out_stride) {
     extern __shared__ __align__(16) unsigned char topk_smem[];
     uint64_t *sel = reinterpret_cast<uint64_t *>(topk_smem);
-    int *hist = reinterpret_cast<int *>(topk_smem + kTopkSelectMaxK * 8);
+    uint64_t *sort_tmp = sel + kTopkSelectMaxK;
+    int *hist = reinterpret_cast<int *>(topk_smem + 2 * kTopkSelectMaxK * 8);
     uint32_t *staged = reinterpret_cast<uint32_t *>(topk_smem + kTopkSelectSmem);
     __shared__ int s_warp[kTopkSelectThreads / 32];
     __shared__ int s_digit, s_rank, s_bin, s_count, s_ties;
@@ -564,8 +647,8 @@ __global__ void __launch_bounds__(kTopkSelectThreads)
     const int m2 = topk_pow2(m);
     for (int i = m + tid; i < m2; i += kTopkSelectThreads) sel[i] = ~0ull;
     __syncthreads();
-    bitonic_sort(sel, m2);
-    for (int i = tid; i < k; i += kTopkSelectThreads) indices[i] = static_cast<int32_t>(sel[i] & 0xffffffffu);
+    const uint64_t *sorted = block_merge_sort(sel, sort_tmp, m2);
+    for (int i = tid; i < k; i += kTopkSelectThreads) indices[i] = static_cast<int32_t>(sorted[i] & 0xffffffffu);
 }
 
 // ---- DSA index scores (kernels/kernels.vx:404-421): score_t = sum_h w_h *

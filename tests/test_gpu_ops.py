@@ -63,10 +63,10 @@ def test_f32_matvec_and_linear_batch(request, oracle, backend_name):
 
 
 @pytest.mark.parametrize('n,k', [(4, 3), (100, 10), (4096, 2048), (40000, 2048), (32768, 2048), (65536, 4096),
-                                 (5000, 1), (9000, 4097), (45056, 4096), (45057, 7), (20000, 2000)])
+                                 (5000, 1), (9000, 4097), (36864, 4096), (36865, 7), (20000, 2000), (4100, 33)])
 def test_topk_exact(gpu_vx, oracle, n, k):
     """Small inputs sort in shared memory; above 4096 scores (k <= 4096) the
-    radix selection runs, with the keys staged in shared memory up to 45056
+    radix selection runs, with the keys staged in shared memory up to 36864
     scores and re-read from the scores above; all give the stable order of
     the oracle."""
     rng = np.random.default_rng(n)
