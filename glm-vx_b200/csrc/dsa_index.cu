@@ -8,7 +8,7 @@
 // tf32_rna(x - hi)): q.k ~ qh.kh + ql.kh + qh.kl, each product exact in f32,
 // the dropped ql.kl below 2^-22 of |q||k|; accumulation in f32 in tensor
 // memory.  A CTA keeps one query's hi/lo heads in shared memory and walks
-// tiles of its keys (persistent over the tiles of one query): 256 threads
+// tiles of its keys (persistent over the tiles of one query): 128 threads
 // hold a tile's column chunk in registers (a warp reads 4 full 128-byte row
 // segments per load; the next chunk's loads are issued before this one's
 // MMAs), split it and store both halves as swizzled K-major tiles through a
@@ -27,7 +27,7 @@ namespace glmvx {
 
 namespace {
 
-constexpr int kIdxTile = 128, kIdxChunk = 32, kIdxThreads = 256, kIdxStages = 2;
+constexpr int kIdxTile = 128, kIdxChunk = 32, kIdxThreads = 128, kIdxStages = 2;
 constexpr int kIdxKeyBytes = kIdxTile * kIdxChunk * 4;  // 16 KB: hi or lo of one column chunk
 constexpr int kIdxStageBytes = 2 * kIdxKeyBytes;
 constexpr int kIdxMaxQRowChunks = 256;  // heads (rounded to 16) x column chunks: 64 KB of hi + lo
@@ -125,7 +125,6 @@ __global__ void __launch_bounds__(kIdxThreads, 2)
         const bool waited = mbar_wait_bounded(&tile_done[k & 1], (k >> 1) & 1);
         if (!__syncthreads_and(waited)) return false;  // uniform: every thread leaves together
         tc_fence_after();
-        if (warp >= 4) return true;  // warps 0-3 own the 128 lanes (keys)
         const int t = (static_cast<int>(blockIdx.x) + k * static_cast<int>(gridDim.x)) * kIdxTile + 32 * warp + lane;
         const uint32_t acc = tmem + (static_cast<uint32_t>(32 * warp) << 16) + (k & 1) * acc_cols;
         float total = 0.0f;
