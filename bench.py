@@ -470,11 +470,12 @@ def dsa_sweep(rt, lib, backend, stream, steps, peak):
     return res
 
 
-def expert_parallel_step(args, ranks, layer):
+def expert_parallel_step(args, ranks, layer, exchange='nccl'):
     """N>1: the same layer with its 256 experts sharded over the ranks
     (gpu/ep.py), TOKENS rows per rank; device time of the step (CUDA events on
-    the launching stream, host routing sync and NCCL exchanges inside), max
-    over ranks."""
+    the launching stream, host routing sync and the exchanges inside), max
+    over ranks.  exchange 'nccl' (all_to_all_single) or 'peer' (mailboxes
+    in peer memory, csrc/p2p.cu)."""
     import torch
     from gpu.ep import ExpertParallelMoE
     from kernels.packed import LAYOUTS
@@ -483,7 +484,7 @@ def expert_parallel_step(args, ranks, layer):
     sl = slice(ranks.rank * per * EXPERT_MATRIX_BYTES, (ranks.rank + 1) * per * EXPERT_MATRIX_BYTES)
     moe = ExpertParallelMoE(layer['router'], layer['bias'], KIND, layer['gate'][sl], layer['up'][sl],
                             layer['down'][sl], EXPERTS, HIDDEN, INTER, TOPK, SCALE, shared=layer['shared'],
-                            group=group)
+                            group=group, exchange=exchange, max_tokens=TOKENS)
     x = np.random.default_rng(300 + ranks.rank).normal(size=(TOKENS, HIDDEN)).astype(np.float32)
     xd = torch.from_numpy(x).cuda()
     from gpu.ep import ep_step
@@ -505,10 +506,15 @@ def expert_parallel_step(args, ranks, layer):
     torch.cuda.synchronize()
     ms = ranks.max(e0.elapsed_time(e1))
     ranks.barrier()
+    moe.close()
+    ranks.barrier()
     del moe
     return {'tok_s': ranks.world * TOKENS * steps / (ms * 1e-3), 'ms_per_step': ms / steps, 'steps': steps,
             'experts_per_gpu': per, 'tokens_per_rank': TOKENS,
-            'exchange': 'NCCL all_to_all_single: pair counts, token rows + expert ids out, pair outputs back'}
+            'exchange': ('NCCL all_to_all_single: pair counts, token rows + expert ids out, pair outputs back'
+                         if exchange == 'nccl' else
+                         'peer-memory mailboxes over NVLink (CUDA IPC): count matrix, token rows + expert ids out, '
+                         'pair outputs back; scatter / release-flag / bounded-wait kernels, no collective library')}
 
 
 def run_ours(args, ranks):
@@ -595,7 +601,9 @@ def run_ours(args, ranks):
 
     gemv = fused_gemv_sweep(rt, lib, dev, stream, args.steps, peak)
     dsa = dsa_sweep(rt, lib, backend, stream, args.steps, peak) if ranks.world == 1 else None
-    ep = expert_parallel_step(args, ranks, layer) if ranks.world > 1 and EXPERTS % ranks.world == 0 else None
+    ep_ok = ranks.world > 1 and EXPERTS % ranks.world == 0
+    ep = expert_parallel_step(args, ranks, layer) if ep_ok else None
+    ep_peer = expert_parallel_step(args, ranks, layer, 'peer') if ep_ok and ranks.world <= 8 else None
     line = {
         'metric': METRIC, 'value': value, 'unit': 'tok/s', 'n_gpus': ranks.world, 'steps': args.steps,
         'warmup': args.warmup, 'ms_per_step': total_ms / args.steps, 'higher_is_better': True, 'scaling': 'weak',
@@ -612,6 +620,7 @@ def run_ours(args, ranks):
         'fused_gemv': gemv,
         **({'dsa_decode': dsa} if dsa else {}),
         **({'expert_parallel': ep} if ep else {}),
+        **({'expert_parallel_peer': ep_peer} if ep_peer else {}),
         'e2e': {'value': e2e_value, 'unit': 'tok/s', 'steps': e2e_steps,
                 'h2d_bytes_per_step': TOKENS * HIDDEN * 4, 'd2h_bytes_per_step': TOKENS * HIDDEN * 4 + 2 * TOKENS * TOPK * 4,
                 'api': 'gpu.moe.MoELayer.forward_pinned (pinned host rows in, pinned host rows + routing out)'},

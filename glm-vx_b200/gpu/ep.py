@@ -22,6 +22,8 @@ supplied by the caller (`ExpertParallelMoE` uses the CUDA library; the CPU
 tests plug in the oracle).
 """
 
+import ctypes as C
+
 import numpy as np
 
 try:  # plumbing only: collectives and device tensors for the exchange buffers
@@ -80,6 +82,169 @@ class Exchange:
         dist.all_to_all_single(recv, send.contiguous(), [int(c) for c in recv_counts],
                                [int(c) for c in send_counts], group=self.group)
         return recv
+
+
+def peer_layout(M, send_counts, rank):
+    """Where this rank's rows land in a peer exchange, given the count matrix
+    M[s, d] (rows rank s sends to rank d in the forward direction):
+    (S, dst_rows, total) with S the matrix of this exchange (M forward, M.T
+    when the rows go back), dst_rows[d] the row of rank d's mailbox at which
+    this rank's rows start (the senders before it, in rank order -- the
+    concatenation order of all_to_all_single), total the rows this rank
+    receives."""
+    M = np.asarray(M, np.int64)
+    send_counts = np.asarray(send_counts, np.int64)
+    if np.array_equal(send_counts, M[rank]):
+        S = M
+    elif np.array_equal(send_counts, M[:, rank]):
+        S = M.T
+    else:
+        raise ValueError('rows() counts match neither direction of the last counts()')
+    dst_rows = [int(S[:rank, d].sum()) for d in range(S.shape[0])]
+    return S, dst_rows, int(S[:, rank].sum())
+
+
+class _DeviceView:
+    """Zero-copy torch view of raw device memory (__cuda_array_interface__)."""
+
+    def __init__(self, ptr, nbytes):
+        self.__cuda_array_interface__ = {'shape': (int(nbytes),), 'typestr': '|u1', 'data': (int(ptr), False),
+                                         'version': 3, 'strides': None}
+
+
+def _pad16(n):
+    return (int(n) + 15) // 16 * 16
+
+
+class PeerExchange:
+    """The interface of Exchange over peer memory instead of a collective
+    library (csrc/p2p.cu): every rank cudaMallocs a mailbox, the ranks swap
+    64-byte CUDA IPC handles once and map each other's mailboxes, and each
+    exchange is three launches on the current stream -- a scatter kernel
+    storing this rank's rows straight into the destinations' mailboxes over
+    NVLink, a signal kernel publishing the step's epoch in each destination's
+    flag slot for this rank (release, system scope), and a wait kernel
+    (acquire, bounded to 2 s) until every sender's flag reached the epoch.
+
+    counts() shares the whole send-count matrix (a row per rank, in every
+    mailbox) and returns it to the host, as all_to_all of the counts does;
+    rows() then knows every rank's offsets (peer_layout): forward rows land
+    in each destination in sender order, rows sent back (send counts = the
+    received counts) in each sender's order of destinations.  The rows
+    returned are a view of this rank's mailbox, valid until the next step's
+    counts() (every rank finishes a step before any rank's next counts()
+    completes).  Up to three rows() calls per counts(); at most `max_rows`
+    rows received per call, `row_bytes` bytes each (narrower rows are padded
+    to 16 bytes).  Plain peer stores: no multicast object."""
+
+    REGIONS = 3
+
+    def __init__(self, group, device, max_rows, row_bytes):
+        from . import runtime as rt
+        self.rt, self.lib, self.group, self.device = rt, rt.library(), group, device
+        self.world, self.rank = dist.get_world_size(group), dist.get_rank(group)
+        if self.world > 8:
+            raise ValueError('peer exchange supports up to 8 ranks')
+        rt.call('glmvx_set_device', device.index)
+        self.max_rows, self.row_cap = int(max_rows), _pad16(row_bytes)
+        W = self.world
+        self.count_row = _pad16(8 * W)
+        self.flags_off = (W * self.count_row + 255) // 256 * 256
+        self.data_off = (self.flags_off + (self.REGIONS + 1) * W * 4 + 255) // 256 * 256
+        self.region_bytes = (self.max_rows * self.row_cap + 255) // 256 * 256
+        total = self.data_off + self.REGIONS * self.region_bytes
+        self.mail = rt.DeviceBuffer(total)
+        rt.call('glmvx_memset', self.mail.ptr, 0, self.data_off, None)
+        rt.call('glmvx_device_synchronize')
+        handle = (C.c_uint8 * 64)()
+        rt.call('glmvx_ipc_handle', self.mail.ptr, handle)
+        handles = [None] * W
+        dist.all_gather_object(handles, bytes(handle), group=group)
+        self.base = []
+        for d in range(W):
+            if d == self.rank:
+                self.base.append(self.mail.ptr)
+            else:
+                p = C.c_void_p()
+                rt.call('glmvx_ipc_open', (C.c_uint8 * 64).from_buffer_copy(handles[d]), C.byref(p))
+                self.base.append(p.value)
+        self.view = torch.as_tensor(_DeviceView(self.mail.ptr, total), device=device)
+        self.stage = rt.DeviceBuffer(W * self.count_row)
+        self.epoch, self.call, self.M = 0, 0, None
+        dist.barrier(group)  # every mailbox zeroed and mapped before any store
+
+    def _stream(self):
+        return torch.cuda.current_stream(self.device).cuda_stream
+
+    def _ptrs(self, vals):
+        return (C.c_void_p * self.world)(*[int(v) for v in vals])
+
+    def _i64(self, vals):
+        return (C.c_int64 * self.world)(*[int(v) for v in vals])
+
+    def _exchange_done(self, region):
+        """Signal this rank's stores of `region` to every peer, then wait for
+        every sender's stores into this rank's mailbox."""
+        W, s = self.world, self._stream()
+        slots = [self.base[d] + self.flags_off + (region * W + self.rank) * 4 for d in range(W)]
+        self.rt.call('glmvx_p2p_signal', self._ptrs(slots), W, self.epoch, s)
+        self.rt.call('glmvx_p2p_wait', self.mail.ptr + self.flags_off + region * W * 4, W, self.epoch, s)
+
+    def counts(self, send_counts):
+        W, s = self.world, self._stream()
+        self.epoch = (self.epoch + 1) & 0xFFFFFFFF
+        self.call = 0
+        row = np.zeros(self.count_row // 8, np.int64)
+        row[:W] = np.asarray(send_counts, np.int64)
+        stage = np.ascontiguousarray(np.tile(row, (W, 1)))  # one copy of the row per destination
+        self.rt.call('glmvx_memcpy_htod', self.stage.ptr, stage.ctypes.data, stage.nbytes, s)
+        dst = [self.base[d] + self.rank * self.count_row for d in range(W)]
+        self.rt.call('glmvx_p2p_scatter', self.stage.ptr, self.count_row, self._ptrs(dst), self._i64([1] * W), None,
+                     W, s)
+        self._exchange_done(0)
+        m = np.empty((W, self.count_row // 8), np.int64)
+        self.rt.call('glmvx_memcpy_dtoh', m.ctypes.data, self.mail.ptr, m.nbytes, s)
+        torch.cuda.current_stream(self.device).synchronize()
+        code = C.c_int32(0)
+        self.rt.call('glmvx_check_device_error', C.byref(code))
+        if code.value:
+            raise RuntimeError('peer exchange: a rank did not deliver its counts in time')
+        self.M = m[:, :W].copy()  # M[s, d]: rows rank s sends to rank d
+        return self.M[:, self.rank].copy()
+
+    def rows(self, send, send_counts, recv_counts):
+        W, r = self.world, self.rank
+        S, dst_rows, total = peer_layout(self.M, send_counts, r)
+        if self.call >= self.REGIONS:
+            raise RuntimeError('more than three rows() exchanges after one counts()')
+        region, self.call = self.call, self.call + 1
+        n = int(send.shape[0])
+        rb = int(np.prod(send.shape[1:], dtype=np.int64)) * send.element_size()  # bytes per row
+        rb16 = _pad16(max(rb, 1))
+        if rb16 > self.row_cap or total > self.max_rows:
+            raise ValueError('peer exchange: more rows or wider rows than the mailbox holds')
+        off = self.data_off + region * self.region_bytes
+        if n:
+            flat = send.contiguous().view(torch.uint8).reshape(n, rb)
+            if rb16 != rb:
+                padded = torch.zeros((n, rb16), dtype=torch.uint8, device=send.device)
+                padded[:, :rb] = flat
+                flat = padded
+            dst = [self.base[d] + off for d in range(W)]
+            self.rt.call('glmvx_p2p_scatter', flat.data_ptr(), rb16, self._ptrs(dst),
+                         self._i64(np.asarray(send_counts, np.int64)), self._i64(dst_rows), W, self._stream())
+        self._exchange_done(region + 1)
+        recv = self.view[off:off + total * rb16].view(total, rb16)[:, :rb].contiguous()
+        return recv.view(send.dtype).reshape((total,) + tuple(send.shape[1:]))
+
+    def close(self):
+        for d, p in enumerate(getattr(self, 'base', [])):
+            if d != self.rank and p:
+                self.rt.call('glmvx_ipc_close', p)
+        self.base = []
+        for b in ('stage', 'mail'):
+            if getattr(self, b, None) is not None:
+                getattr(self, b).close()
 
 
 def ep_step(x, ids, wts, per_rank, exchange, ops):
@@ -169,7 +334,7 @@ class ExpertParallelMoE:
     bias and the shared expert are the full, replicated arrays."""
 
     def __init__(self, router_w, router_bias, kind, gate, up, down, experts, hidden, inter, top_k, scale,
-                 shared=None, group=None):
+                 shared=None, group=None, exchange='nccl', max_tokens=64):
         from . import runtime as rt
         from kernels.packed import LAYOUTS
         self.rt, self.lib = rt, rt.library()
@@ -179,6 +344,11 @@ class ExpertParallelMoE:
         # The library keeps its own CUDA runtime state: select the same device.
         rt.call('glmvx_set_device', torch.cuda.current_device())
         self.per_rank = experts_per_rank(self.experts, self.exchange.world)
+        if exchange == 'peer':  # rows over NVLink peer stores instead of NCCL (PeerExchange)
+            self.exchange = PeerExchange(group, self.exchange.device, self.exchange.world * max_tokens * self.top_k,
+                                         4 * self.hidden)
+        elif exchange != 'nccl':
+            raise ValueError("exchange must be 'nccl' or 'peer'")
         self.local_experts = self.per_rank
         block, size, _ = LAYOUTS[self.kind]
         one = self.inter * (self.hidden // block) * size
@@ -204,6 +374,12 @@ class ExpertParallelMoE:
 
     def _check(self, code, name):
         self.rt.check(self.lib, code, name)
+
+    def close(self):
+        """Unmap the peers' mailboxes and free this rank's (peer exchange);
+        call on every rank after its last step has finished."""
+        if hasattr(self.exchange, 'close'):
+            self.exchange.close()
 
     def route(self, x):
         """Replicated router on this rank's rows -> host ids, weights."""

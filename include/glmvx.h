@@ -254,6 +254,28 @@ int32_t glmvx_moe_experts(float *y, const float *x, const int32_t *expert_ids, i
 int32_t glmvx_moe_combine(float *y, const float *pair_out, const int32_t *comb, const float *combw,
                           const float *shared_rows, int32_t tokens, int32_t top_k, int32_t hidden, void *stream);
 int32_t glmvx_gather_rows(float *out, const float *x, const int32_t *idx, int32_t n, int32_t cols, void *stream);
+/* Peer-memory exchange between the GPUs of one node, the transport of the
+ * expert-parallel step without a collective library (replaces the
+ * all_to_all_single exchanges of glm-vx_b200/gpu/ep.py; the reference runs
+ * all experts in one process, glm_vx/model.py:289-324).  glmvx_ipc_handle /
+ * glmvx_ipc_open / glmvx_ipc_close: 64-byte CUDA IPC handles of cudaMalloc'd
+ * mailboxes and their mapping in a peer process.  glmvx_p2p_scatter: rows of
+ * src grouped by destination (counts[d] rows for rank d, rank order) stored
+ * from row dst_rows[d] (NULL: 0) of dst[d] -- own or mapped peer memory;
+ * row_bytes a multiple of 16, pointers 16-byte aligned, world <= 8.
+ * glmvx_p2p_signal: once this stream's earlier stores are visible
+ * system-wide, stores `epoch` (release, system scope) at flag_slots[d] (this
+ * rank's flag in rank d's mailbox).  glmvx_p2p_wait: waits on the device
+ * (acquire, system scope) until flags[s] reached epoch for every s < world;
+ * after 2 s it sets the device error word instead.  dst, counts, dst_rows
+ * and flag_slots are host arrays of `world` entries. */
+int32_t glmvx_ipc_handle(void *base, uint8_t *handle64);
+int32_t glmvx_ipc_open(const uint8_t *handle64, void **ptr);
+int32_t glmvx_ipc_close(void *ptr);
+int32_t glmvx_p2p_scatter(const void *src, int64_t row_bytes, void *const *dst, const int64_t *counts,
+                          const int64_t *dst_rows, int32_t world, void *stream);
+int32_t glmvx_p2p_signal(void *const *flag_slots, int32_t world, uint32_t epoch, void *stream);
+int32_t glmvx_p2p_wait(const uint32_t *flags, int32_t world, uint32_t epoch, void *stream);
 /* FP8 E4M3FN block-scaled projection, device pointers: out[rows] =
  * sum_c (decode(weight[r,c]) * scales[r/128, c/128]) * x[c], weight u8
  * [rows, cols], scales f32 [ceil(rows/128), ceil(cols/128)].  Replaces the

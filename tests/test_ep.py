@@ -132,3 +132,29 @@ def test_ep_step_over_gloo_matches_reference(tmp_path, oracle):
         want, want_ids = reference_ffn(oracle, layer, _tokens(rank), E, H, I, K, 2.5)
         assert got['ids'].tolist() == want_ids.tolist()
         assert got['y'].tobytes() == want.tobytes()
+
+
+def test_peer_layout_reproduces_all_to_all_order():
+    """Rows placed at peer_layout's offsets (the peer-memory exchange) land in
+    each receiver exactly as all_to_all_single concatenates them, forward and
+    back, for random count matrices."""
+    from gpu.ep import peer_layout
+    rng = np.random.default_rng(5)
+    for world in (1, 2, 3, 8):
+        M = rng.integers(0, 6, size=(world, world))
+        for direction in ('forward', 'back'):
+            S = M if direction == 'forward' else M.T
+            sends = {s: [(s, d, i) for d in range(world) for i in range(S[s, d])] for s in range(world)}
+            mail = {d: [None] * int(S[:, d].sum()) for d in range(world)}
+            for s in range(world):
+                _, dst_rows, _ = peer_layout(M, S[s], s)
+                k = 0
+                for d in range(world):
+                    for i in range(S[s, d]):
+                        assert mail[d][dst_rows[d] + i] is None
+                        mail[d][dst_rows[d] + i] = sends[s][k]
+                        k += 1
+            for d in range(world):
+                want = [row for s in range(world) for row in sends[s] if row[1] == d]  # sender order
+                assert mail[d] == want
+                assert peer_layout(M, S[d], d)[2] == len(want)

@@ -1,6 +1,7 @@
-"""Expert-parallel MoE layer (gpu/ep.py ExpertParallelMoE) on 2 GPUs over
-NCCL against the single-process reference layer (glm_vx/model.py:289-324)
-on the CPU oracle.  Runs as child processes, one per GPU; skipped when the
+"""Expert-parallel MoE layer (gpu/ep.py ExpertParallelMoE) on 2 GPUs, rows
+exchanged over NCCL or over the peer-memory mailboxes (PeerExchange,
+csrc/p2p.cu), against the single-process reference layer
+(glm_vx/model.py:289-324) on the CPU oracle.  Runs as child processes, one per GPU; skipped when the
 box has fewer than two GPUs."""
 import os
 import socket
@@ -32,7 +33,7 @@ def _tokens(rank):
     return np.random.default_rng(900 + rank).normal(size=(T, H)).astype(np.float32)
 
 
-def _rank_main(rank, world, port, out_dir):
+def _rank_main(rank, world, port, out_dir, exchange='nccl'):
     os.environ.update(MASTER_ADDR='127.0.0.1', MASTER_PORT=str(port), NCCL_NVLS_ENABLE='0')
     import torch
     import torch.distributed as dist
@@ -48,10 +49,12 @@ def _rank_main(rank, world, port, out_dir):
         lay, per = _layer(), E // world
         sl = slice(rank * per * one, (rank + 1) * per * one)
         moe = ExpertParallelMoE(lay['router'], lay['bias'], 19, lay['gate'][sl], lay['up'][sl], lay['down'][sl], E, H,
-                                I, K, 2.5, shared=lay['shared'])
+                                I, K, 2.5, shared=lay['shared'], exchange=exchange)
         y, ids, _ = moe.forward(_tokens(rank))
         y2, _, _ = moe.forward(_tokens(rank))
         torch.cuda.synchronize()
+        dist.barrier()  # both ranks' last steps have finished before the mailboxes go
+        moe.close()
         np.savez(os.path.join(out_dir, f'rank{rank}.npz'), y=y, y2=y2, ids=ids)
     finally:
         dist.destroy_process_group()
@@ -64,10 +67,12 @@ def _free_port():
 
 
 @pytest.mark.skipif(_gpus() < 2, reason='needs two GPUs')
-def test_expert_parallel_layer_on_two_gpus(tmp_path, oracle):
+@pytest.mark.parametrize('exchange', ['nccl', 'peer'])
+def test_expert_parallel_layer_on_two_gpus(tmp_path, oracle, exchange):
+    """Both transports: NCCL all_to_all and the peer-memory mailboxes."""
     import torch.multiprocessing as mp
     from test_gpu_moe import reference_ffn
-    mp.spawn(_rank_main, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=True)
+    mp.spawn(_rank_main, args=(2, _free_port(), str(tmp_path), exchange), nprocs=2, join=True)
     layer = _layer()
     for rank in range(2):
         got = np.load(tmp_path / f'rank{rank}.npz')
@@ -76,3 +81,18 @@ def test_expert_parallel_layer_on_two_gpus(tmp_path, oracle):
         err = np.linalg.norm(got['y'] - want) / np.linalg.norm(want)
         assert err <= RTOL, err
         assert got['y2'].tobytes() == got['y'].tobytes()
+
+
+def test_peer_exchange_single_rank(tmp_path, oracle):
+    """One rank: the peer exchange's scatter / signal / wait kernels run into
+    the rank's own mailbox (no IPC mapping), and the layer matches the
+    reference as with NCCL."""
+    import torch.multiprocessing as mp
+    from test_gpu_moe import reference_ffn
+    mp.spawn(_rank_main, args=(1, _free_port(), str(tmp_path), 'peer'), nprocs=1, join=True)
+    got = np.load(tmp_path / 'rank0.npz')
+    want, want_ids = reference_ffn(oracle, _layer(), _tokens(0), E, H, I, K, 2.5)
+    assert got['ids'].tolist() == want_ids.tolist()
+    err = np.linalg.norm(got['y'] - want) / np.linalg.norm(want)
+    assert err <= RTOL, err
+    assert got['y2'].tobytes() == got['y'].tobytes()
