@@ -917,6 +917,30 @@ GLMVX_EXPORT int32_t glmvx_add(float *out, const float *a, const float *b, int64
     return launch_status("add_kernel");
 }
 
+// *flag = 1 if any of x[0..n) is NaN or infinite, else 0: one CTA (no prior
+// zeroing needed), for a step's outputs already hot in L2.
+__global__ void __launch_bounds__(1024) nonfinite_kernel(const float *__restrict__ x, int64_t n, uint32_t *flag) {
+    bool bad = false;
+    if ((reinterpret_cast<uintptr_t>(x) & 15) == 0) {
+        const int64_t n4 = n / 4;
+        for (int64_t i = threadIdx.x; i < n4; i += blockDim.x) {
+            const float4 v = __ldg(reinterpret_cast<const float4 *>(x) + i);
+            bad |= !isfinite(v.x) || !isfinite(v.y) || !isfinite(v.z) || !isfinite(v.w);
+        }
+        for (int64_t i = 4 * n4 + threadIdx.x; i < n; i += blockDim.x) bad |= !isfinite(__ldg(x + i));
+    } else {
+        for (int64_t i = threadIdx.x; i < n; i += blockDim.x) bad |= !isfinite(__ldg(x + i));
+    }
+    bad = __syncthreads_or(bad);
+    if (threadIdx.x == 0) *flag = bad ? 1u : 0u;
+}
+
+GLMVX_EXPORT int32_t glmvx_nonfinite_flag(const float *x, int64_t n, uint32_t *flag, void *stream) {
+    if (n < 0 || !flag || (n && !x)) return set_error("nonfinite_flag: bad arguments"), kInvalid;
+    nonfinite_kernel<<<1, 1024, 0, S_>>>(x, n, flag);
+    return launch_status("nonfinite_kernel");
+}
+
 GLMVX_EXPORT int32_t glmvx_axpy(float *out, const float *x, float alpha, int64_t n, void *stream) {
     if (n < 0) return set_error("axpy n"), kInvalid;
     if (n) axpy_kernel<<<ew_grid(n), 256, 0, S_>>>(out, x, alpha, n);

@@ -88,10 +88,11 @@ class MoELayer:
         self._graphs = {}
 
     def _io_layout(self, tokens):
-        """Byte offsets of x, y, ids, weights and the error word in the layer's
-        I/O buffers (pinned host + device, 256-byte aligned), grown on demand."""
+        """Byte offsets of x, y, ids, weights, the error word and the
+        non-finite-output flag in the layer's I/O buffers (pinned host +
+        device, 256-byte aligned), grown on demand."""
         sizes = [4 * tokens * self.hidden, 4 * tokens * self.hidden, 4 * tokens * self.top_k,
-                 4 * tokens * self.top_k, 4]
+                 4 * tokens * self.top_k, 4, 4]
         offs, off = [], 0
         for n in sizes:
             offs.append(off)
@@ -119,7 +120,8 @@ class MoELayer:
 
     def _step_graph(self, tokens):
         """CUDA graph of one step on the I/O buffers: copy the token rows in,
-        the layer's launches, copy outputs and the device error word back.
+        the layer's launches, copy outputs, the device error word and the
+        non-finite-output flag back.
         Replayed per call so the GPU runs the step without host gaps;
         captured again when the buffers or the workspace move."""
         b = self.backend
@@ -142,6 +144,8 @@ class MoELayer:
             self.forward_device(dev.ptr + offs[1], dev.ptr + offs[0], tokens, dev.ptr + offs[2], dev.ptr + offs[3])
             rt.call('glmvx_memcpy_dtoh', host.ptr + offs[1], dev.ptr + offs[1], out_bytes, s)
             rt.call('glmvx_memcpy_dtoh', host.ptr + offs[4], b.device.error_address(), 4, s)
+            rt.call('glmvx_nonfinite_flag', dev.ptr + offs[1], tokens * self.hidden, dev.ptr + offs[5], s)
+            rt.call('glmvx_memcpy_dtoh', host.ptr + offs[5], dev.ptr + offs[5], 4, s)
         finally:
             g.end()
         graphs[key] = g
@@ -170,8 +174,9 @@ class MoELayer:
         if C.c_int32.from_address(self._io_bufs[0].ptr + offs[4]).value:
             b.device.check_device_error()
         # Non-finite inputs run safely (the router ranks NaN scores last) and
-        # give non-finite outputs, so one check after the step covers both.
-        if not np.isfinite(io['y']).all():
+        # give non-finite outputs, so one check after the step covers both;
+        # the step's last kernel flags a non-finite output on the device.
+        if C.c_uint32.from_address(self._io_bufs[0].ptr + offs[5]).value:
             if not np.isfinite(io['x']).all():
                 raise ValueError('MoE input must be finite')
             raise ValueError('nonfinite MoE output')

@@ -84,6 +84,7 @@ SIGNATURES = {
     'glmvx_dsa_scratch_bytes': ([_I32, _I32, _I32, _I32, _I32], _I64),
     'glmvx_dsa_decode': ([_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I32, _I32, _I32, _I32, _I32, _I32, _I32, _I32,
                           _F32, _F32, _P, _U64, _P], _I32),
+    'glmvx_nonfinite_flag': ([_P, _I64, _P, _P], _I32),
     'glmvx_ipc_handle': ([_P, _P], _I32),
     'glmvx_ipc_open': ([_P, C.POINTER(C.c_void_p)], _I32),
     'glmvx_ipc_close': ([_P], _I32),
