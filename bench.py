@@ -587,6 +587,7 @@ def run_ours(args, ranks):
     # the device, the layer, outputs copied back to pinned host memory and
     # checked there (MoELayer.forward_pinned), every step.
     e2e_steps = max(1, min(args.steps, 200))
+    e2e_h2d, e2e_d2h = moe.step_copy_bytes(TOKENS)
     np.copyto(moe.pinned_io(TOKENS)['x'], xs[TOKENS])
     for i in range(min(args.warmup, 3)):
         moe.forward_pinned(TOKENS)
@@ -622,7 +623,7 @@ def run_ours(args, ranks):
         **({'expert_parallel': ep} if ep else {}),
         **({'expert_parallel_peer': ep_peer} if ep_peer else {}),
         'e2e': {'value': e2e_value, 'unit': 'tok/s', 'steps': e2e_steps,
-                'h2d_bytes_per_step': TOKENS * HIDDEN * 4, 'd2h_bytes_per_step': TOKENS * HIDDEN * 4 + 2 * TOKENS * TOPK * 4,
+                'h2d_bytes_per_step': e2e_h2d, 'd2h_bytes_per_step': e2e_d2h,
                 'api': 'gpu.moe.MoELayer.forward_pinned (pinned host rows in, pinned host rows + routing out)'},
         # prep x, router logits, top-k, grouping, gate+up (two-token and four-token job lists), prep h,
         # down (both lists), combine

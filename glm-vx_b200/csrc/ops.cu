@@ -917,27 +917,35 @@ GLMVX_EXPORT int32_t glmvx_add(float *out, const float *a, const float *b, int64
     return launch_status("add_kernel");
 }
 
-// *flag = 1 if any of x[0..n) is NaN or infinite, else 0: one CTA (no prior
-// zeroing needed), for a step's outputs already hot in L2.
-__global__ void __launch_bounds__(1024) nonfinite_kernel(const float *__restrict__ x, int64_t n, uint32_t *flag) {
+constexpr int kFlagThreads = 256, kFlagVecPerThread = 4;
+
+// Sets *flag when a block sees a NaN or infinity; blocks that see none write
+// nothing, so the caller zeroes the flag (the write is the same 1 from every
+// block that writes).
+__global__ void __launch_bounds__(kFlagThreads) nonfinite_kernel(const float *__restrict__ x, int64_t n, uint32_t *flag) {
     bool bad = false;
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * kFlagThreads;
+    const int64_t first = static_cast<int64_t>(blockIdx.x) * kFlagThreads + threadIdx.x;
+    int64_t scalar_from = 0;
     if ((reinterpret_cast<uintptr_t>(x) & 15) == 0) {
         const int64_t n4 = n / 4;
-        for (int64_t i = threadIdx.x; i < n4; i += blockDim.x) {
+        for (int64_t i = first; i < n4; i += stride) {
             const float4 v = __ldg(reinterpret_cast<const float4 *>(x) + i);
             bad |= !isfinite(v.x) || !isfinite(v.y) || !isfinite(v.z) || !isfinite(v.w);
         }
-        for (int64_t i = 4 * n4 + threadIdx.x; i < n; i += blockDim.x) bad |= !isfinite(__ldg(x + i));
-    } else {
-        for (int64_t i = threadIdx.x; i < n; i += blockDim.x) bad |= !isfinite(__ldg(x + i));
+        scalar_from = 4 * n4;
     }
-    bad = __syncthreads_or(bad);
-    if (threadIdx.x == 0) *flag = bad ? 1u : 0u;
+    for (int64_t i = scalar_from + first; i < n; i += stride) bad |= !isfinite(__ldg(x + i));
+    if (__syncthreads_or(bad) && threadIdx.x == 0) *flag = 1u;
 }
 
 GLMVX_EXPORT int32_t glmvx_nonfinite_flag(const float *x, int64_t n, uint32_t *flag, void *stream) {
     if (n < 0 || !flag || (n && !x)) return set_error("nonfinite_flag: bad arguments"), kInvalid;
-    nonfinite_kernel<<<1, 1024, 0, S_>>>(x, n, flag);
+    if (n == 0) return kOk;
+    const int64_t units = (reinterpret_cast<uintptr_t>(x) & 15) ? n : n / 4 + 3;
+    const int64_t per_block = static_cast<int64_t>(kFlagThreads) * kFlagVecPerThread;
+    const int blocks = static_cast<int>(std::min<int64_t>((units + per_block - 1) / per_block, 4 * 148));
+    nonfinite_kernel<<<blocks, kFlagThreads, 0, S_>>>(x, n, flag);
     return launch_status("nonfinite_kernel");
 }
 

@@ -87,16 +87,20 @@ class MoELayer:
             g.close()
         self._graphs = {}
 
+    _IO_SLOTS = ('x', 'flag', 'y', 'ids', 'weights', 'err')
+
     def _io_layout(self, tokens):
-        """Byte offsets of x, y, ids, weights, the error word and the
-        non-finite-output flag in the layer's I/O buffers (pinned host +
-        device, 256-byte aligned), grown on demand."""
-        sizes = [4 * tokens * self.hidden, 4 * tokens * self.hidden, 4 * tokens * self.top_k,
-                 4 * tokens * self.top_k, 4, 4]
-        offs, off = [], 0
-        for n in sizes:
-            offs.append(off)
-            off += (n + 255) & ~255
+        """Byte offsets {'x', 'flag', 'y', 'ids', 'weights', 'err'} in the
+        layer's I/O buffers (pinned host + device, 256-byte aligned), grown on
+        demand.  The non-finite-output flag sits between the input rows and
+        the outputs: the step's one host-to-device copy (x and a zero flag)
+        clears it and its first device-to-host copy (flag to weights) returns
+        it."""
+        n, k = 4 * tokens * self.hidden, 4 * tokens * self.top_k
+        offs, off = {}, 0
+        for name, size in zip(self._IO_SLOTS, (n, 4, n, k, k, 4)):
+            offs[name] = off
+            off += (size + 255) & ~255
         if off > self.__dict__.get('_io_cap', 0):
             self.backend.stream.synchronize()
             self._drop_graphs()
@@ -104,24 +108,48 @@ class MoELayer:
                 buf.close()
             self._io_bufs = (rt.HostBuffer(off), rt.DeviceBuffer(off))
             self._io_cap = off
+            self._io_views = {}
         return offs
+
+    def step_copy_bytes(self, tokens):
+        """(host-to-device, device-to-host) bytes that one forward_pinned(tokens)
+        step copies: the rows and the flag in; the flag, outputs and routing,
+        then the device error word, out."""
+        o = self._io_layout(tokens)
+        return o['flag'] + 4 - o['x'], o['weights'] + 4 * tokens * self.top_k - o['flag'] + 4
 
     def pinned_io(self, tokens):
         """Pinned host views for a `tokens`-row step: {'x', 'y', 'ids',
         'weights'}.  Write the rows into 'x' and call forward_pinned(tokens);
         the other views then hold its results until the next call."""
+        return self._pinned(tokens)[0]
+
+    def _pinned(self, tokens):
+        """(pinned_io views, flag word, error word) of a `tokens`-row step,
+        made once per buffer layout."""
         offs = self._io_layout(tokens)
-        host = self._io_bufs[0]
-        n, k = tokens * self.hidden, tokens * self.top_k
-        return {'x': host.view(np.float32, offs[0] // 4 + n)[offs[0] // 4:].reshape(tokens, self.hidden),
-                'y': host.view(np.float32, offs[1] // 4 + n)[offs[1] // 4:].reshape(tokens, self.hidden),
-                'ids': host.view(np.int32, offs[2] // 4 + k)[offs[2] // 4:].reshape(tokens, self.top_k),
-                'weights': host.view(np.float32, offs[3] // 4 + k)[offs[3] // 4:].reshape(tokens, self.top_k)}
+        cached = self._io_views.get(tokens)
+        if cached is None:
+            host = self._io_bufs[0]
+            n, k = tokens * self.hidden, tokens * self.top_k
+
+            def view(name, dtype, count, shape):
+                o = offs[name] // 4
+                return host.view(dtype, o + count)[o:].reshape(shape)
+
+            views = {'x': view('x', np.float32, n, (tokens, self.hidden)),
+                     'y': view('y', np.float32, n, (tokens, self.hidden)),
+                     'ids': view('ids', np.int32, k, (tokens, self.top_k)),
+                     'weights': view('weights', np.float32, k, (tokens, self.top_k))}
+            cached = (views, C.c_uint32.from_address(host.ptr + offs['flag']),
+                      C.c_int32.from_address(host.ptr + offs['err']))
+            self._io_views[tokens] = cached
+        return cached
 
     def _step_graph(self, tokens):
-        """CUDA graph of one step on the I/O buffers: copy the token rows in,
-        the layer's launches, copy outputs, the device error word and the
-        non-finite-output flag back.
+        """CUDA graph of one step on the I/O buffers: copy the token rows (and
+        a zero flag) in, the layer's launches, flag a non-finite output, copy
+        the flag, outputs and routing back, then the device error word.
         Replayed per call so the GPU runs the step without host gaps;
         captured again when the buffers or the workspace move."""
         b = self.backend
@@ -131,25 +159,25 @@ class MoELayer:
         key = (tokens, host.ptr, dev.ptr, self._ws.ptr)
         graphs = self.__dict__.setdefault('_graphs', {})
         if key in graphs:
-            return graphs[key], offs
+            return graphs[key]
         if any(k[1:] != key[1:] for k in graphs):
             self._drop_graphs()
             graphs = self._graphs
         s = b.stream.handle
-        x_bytes, out_bytes = 4 * tokens * self.hidden, offs[3] + 4 * tokens * self.top_k - offs[1]
+        h2d, d2h = self.step_copy_bytes(tokens)
         g = rt.Graph(b.stream)
         g.begin()
         try:
-            rt.call('glmvx_memcpy_htod', dev.ptr + offs[0], host.ptr + offs[0], x_bytes, s)
-            self.forward_device(dev.ptr + offs[1], dev.ptr + offs[0], tokens, dev.ptr + offs[2], dev.ptr + offs[3])
-            rt.call('glmvx_memcpy_dtoh', host.ptr + offs[1], dev.ptr + offs[1], out_bytes, s)
-            rt.call('glmvx_memcpy_dtoh', host.ptr + offs[4], b.device.error_address(), 4, s)
-            rt.call('glmvx_nonfinite_flag', dev.ptr + offs[1], tokens * self.hidden, dev.ptr + offs[5], s)
-            rt.call('glmvx_memcpy_dtoh', host.ptr + offs[5], dev.ptr + offs[5], 4, s)
+            rt.call('glmvx_memcpy_htod', dev.ptr + offs['x'], host.ptr + offs['x'], h2d, s)
+            self.forward_device(dev.ptr + offs['y'], dev.ptr + offs['x'], tokens, dev.ptr + offs['ids'],
+                                dev.ptr + offs['weights'])
+            rt.call('glmvx_nonfinite_flag', dev.ptr + offs['y'], tokens * self.hidden, dev.ptr + offs['flag'], s)
+            rt.call('glmvx_memcpy_dtoh', host.ptr + offs['flag'], dev.ptr + offs['flag'], d2h - 4, s)
+            rt.call('glmvx_memcpy_dtoh', host.ptr + offs['err'], b.device.error_address(), 4, s)
         finally:
             g.end()
         graphs[key] = g
-        return g, offs
+        return g
 
     def forward_device(self, y, x, tokens, ids=None, weights=None, stream=None):
         """Device pointers in and out; asynchronous on `stream` (default: the backend's)."""
@@ -165,18 +193,19 @@ class MoELayer:
         Raises like forward() on non-finite inputs or outputs."""
         b = self.backend
         b._begin()
-        io = self.pinned_io(tokens)
+        io, flag, err = self._pinned(tokens)
         if tokens == 0:
             return io['y'], io['ids'], io['weights']
-        g, offs = self._step_graph(tokens)
+        g = self._step_graph(tokens)
+        flag.value = 0  # copied in with the rows
         g.launch()
         b.stream.synchronize()
-        if C.c_int32.from_address(self._io_bufs[0].ptr + offs[4]).value:
+        if err.value:
             b.device.check_device_error()
         # Non-finite inputs run safely (the router ranks NaN scores last) and
         # give non-finite outputs, so one check after the step covers both;
-        # the step's last kernel flags a non-finite output on the device.
-        if C.c_uint32.from_address(self._io_bufs[0].ptr + offs[5]).value:
+        # a kernel after the layer flags a non-finite output on the device.
+        if flag.value:
             if not np.isfinite(io['x']).all():
                 raise ValueError('MoE input must be finite')
             raise ValueError('nonfinite MoE output')
@@ -200,7 +229,7 @@ class MoELayer:
         self._drop_graphs()
         for buf in self.__dict__.pop('_io_bufs', ()):
             buf.close()
-        self._io_cap = 0
+        self._io_cap, self._io_views = 0, {}
         for buf in self._buffers + ([self._ws] if self._ws is not None else []):
             buf.close()
         self._buffers, self._ws = [], None

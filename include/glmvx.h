@@ -155,9 +155,10 @@ int32_t glmvx_layernorm(float *out, const float *x, const float *w, const float 
 int32_t glmvx_softmax(float *out, const float *x, int32_t rows, int32_t n, void *stream);
 int32_t glmvx_swiglu(float *out, const float *gate, const float *up, int64_t n, void *stream);
 int32_t glmvx_add(float *out, const float *a, const float *b, int64_t n, void *stream);
-/* *flag = 1 if any of x[0..n) is NaN or infinite, else 0 (device pointers;
-   lets a caller that copies a step's outputs back check them with one word;
-   no reference counterpart -- the reference checks on the host). */
+/* Sets *flag = 1 if any of x[0..n) is NaN or infinite and leaves it as it
+   was otherwise: the caller zeroes it first (device pointers; lets a caller
+   that copies a step's outputs back check them with one word; no reference
+   counterpart -- the reference checks on the host). */
 int32_t glmvx_nonfinite_flag(const float *x, int64_t n, uint32_t *flag, void *stream);
 int32_t glmvx_axpy(float *out, const float *x, float alpha, int64_t n, void *stream);
 int32_t glmvx_rope_offset(float *out, const float *x, const float *cosine, const float *sine, int32_t heads,

@@ -125,3 +125,39 @@ def test_mlp_resident(gpu_backend, oracle):
     x = rng.normal(size=48).astype(np.float32)
     want = oracle.matvec(down, oracle.swiglu(oracle.matvec(gate, x), oracle.matvec(up, x)))
     np.testing.assert_allclose(gpu_backend.mlp(gate, up, down, x), want, rtol=1e-4, atol=1e-4)
+
+
+@pytest.mark.parametrize('n', [1, 7, 4096, 4099, 1_000_003])
+@pytest.mark.parametrize('shift', [0, 1])
+def test_nonfinite_flag(gpu_backend, n, shift):
+    """glmvx_nonfinite_flag sets the flag for a NaN or infinity at the first,
+    a middle or the last element (16-byte aligned and unaligned starts, ragged
+    tails, one and many blocks) and leaves a zeroed flag at 0 otherwise."""
+    from gpu import runtime as rt
+    lib, s = gpu_backend.lib, gpu_backend.stream.handle
+    x = np.random.default_rng(n).normal(size=n + shift).astype(np.float32)
+    buf, flag = rt.DeviceBuffer(x.nbytes), rt.DeviceBuffer(16)
+    got = np.zeros(1, np.uint32)
+
+    def run(values):
+        buf.upload(values, s)
+        rt.call('glmvx_memset', flag.ptr, 0, 4, s)
+        rt.call('glmvx_nonfinite_flag', buf.ptr + 4 * shift, n, flag.ptr, s)
+        gpu_backend.stream.synchronize()
+        flag.download(got)
+        return int(got[0])
+
+    try:
+        assert run(x) == 0
+        for pos in {0, n // 2, n - 1}:
+            for bad in (np.nan, np.inf, -np.inf):
+                xb = x.copy()
+                xb[shift + pos] = bad
+                assert run(xb) == 1, (pos, bad)
+        if shift:  # a non-finite value just outside the range is not seen
+            xb = x.copy()
+            xb[0] = np.nan
+            assert run(xb) == 0
+    finally:
+        buf.close()
+        flag.close()
