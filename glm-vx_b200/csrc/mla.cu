@@ -628,13 +628,14 @@ GLMVX_EXPORT int64_t glmvx_dsa_scratch_bytes(int32_t batch, int32_t heads, int32
 // of each cache; out [batch][heads][rank]; selected_out, when given,
 // [batch][topk] (-1 past min(topk, lens[b])).  rank <= 512, rope_dim <= 128,
 // topk <= 4096.
-GLMVX_EXPORT int32_t glmvx_dsa_decode(float *out, int32_t *selected_out, const float *q_latent, const float *q_rope,
-                                      const float *q_index, const float *head_weights, const float *latents,
-                                      const float *rope_keys, const float *index_keys, const int32_t *lens,
-                                      int32_t batch, int32_t heads, int32_t rank, int32_t rope_dim,
-                                      int32_t index_heads, int32_t index_dim, int32_t capacity, int32_t topk,
-                                      float index_scale, float scale, void *scratch, uint64_t scratch_bytes,
-                                      void *stream) {
+namespace {
+
+int32_t dsa_decode(float *out, int32_t *selected_out, const float *q_latent, const float *q_rope, const float *q_index,
+                   const float *head_weights, const float *latents, const float *rope_keys, const float *index_keys,
+                   const int32_t *lens, int32_t batch, int32_t heads, int32_t rank, int32_t rope_dim,
+                   int32_t index_heads, int32_t index_dim, int32_t capacity, int32_t topk, float index_scale,
+                   float scale, void *scratch, uint64_t scratch_bytes, cudaEvent_t attention_inputs_ready,
+                   void *stream) {
     if (batch <= 0 || heads <= 0 || rank <= 0 || rank > 512 || rope_dim < 0 || rope_dim > 128 || index_heads <= 0 ||
         index_dim <= 0 || capacity <= 0 || topk <= 0 || topk > 4096 || !(scale > 0.0f) || !std::isfinite(scale) ||
         !std::isfinite(index_scale)) {
@@ -668,6 +669,7 @@ GLMVX_EXPORT int32_t glmvx_dsa_decode(float *out, int32_t *selected_out, const f
     if (rc) return rc;
     rc = launch_topk_batch(sel, scores, capacity, topk, lens, capacity, topk, batch, st);
     if (rc) return rc;
+    if (attention_inputs_ready) GLMVX_CUDA(cudaStreamWaitEvent(st, attention_inputs_ready, 0));
     const int64_t lstride = static_cast<int64_t>(capacity) * rank, rstride = static_cast<int64_t>(capacity) * rope_dim;
     if (tc) {
         rc = launch_mla_tc(numerator, stats, q_latent, q_rope, latents, rope_keys, sel, lens, heads, rank, rope_dim,
@@ -694,6 +696,36 @@ GLMVX_EXPORT int32_t glmvx_dsa_decode(float *out, int32_t *selected_out, const f
     if (const int32_t bad = check_merge_splits(splits)) return bad;
     return launch_pdl(mla_merge_kernel, dim3(heads, (rank + kMergeCols - 1) / kMergeCols, batch), dim3(32), st, out,
                       const_cast<const float *>(numerator), const_cast<const float *>(stats), heads, rank, splits);
+}
+
+}  // namespace
+
+GLMVX_EXPORT int32_t glmvx_dsa_decode(float *out, int32_t *selected_out, const float *q_latent, const float *q_rope,
+                                      const float *q_index, const float *head_weights, const float *latents,
+                                      const float *rope_keys, const float *index_keys, const int32_t *lens,
+                                      int32_t batch, int32_t heads, int32_t rank, int32_t rope_dim,
+                                      int32_t index_heads, int32_t index_dim, int32_t capacity, int32_t topk,
+                                      float index_scale, float scale, void *scratch, uint64_t scratch_bytes,
+                                      void *stream) {
+    return dsa_decode(out, selected_out, q_latent, q_rope, q_index, head_weights, latents, rope_keys, index_keys, lens,
+                      batch, heads, rank, rope_dim, index_heads, index_dim, capacity, topk, index_scale, scale, scratch,
+                      scratch_bytes, nullptr, stream);
+}
+
+// glmvx_dsa_decode whose attention stage (the first reader of q_latent and
+// q_rope) waits for `attention_inputs_ready` (a cudaEvent_t recorded after
+// the queries' copy, e.g. on a second stream): the indexer and top-k run
+// while those copies are still in flight.
+GLMVX_EXPORT int32_t glmvx_dsa_decode_wait(float *out, int32_t *selected_out, const float *q_latent,
+                                           const float *q_rope, const float *q_index, const float *head_weights,
+                                           const float *latents, const float *rope_keys, const float *index_keys,
+                                           const int32_t *lens, int32_t batch, int32_t heads, int32_t rank,
+                                           int32_t rope_dim, int32_t index_heads, int32_t index_dim, int32_t capacity,
+                                           int32_t topk, float index_scale, float scale, void *scratch,
+                                           uint64_t scratch_bytes, void *attention_inputs_ready, void *stream) {
+    return dsa_decode(out, selected_out, q_latent, q_rope, q_index, head_weights, latents, rope_keys, index_keys, lens,
+                      batch, heads, rank, rope_dim, index_heads, index_dim, capacity, topk, index_scale, scale, scratch,
+                      scratch_bytes, static_cast<cudaEvent_t>(attention_inputs_ready), stream);
 }
 
 // Appends one row per query to the caches of glmvx_dsa_decode (device

@@ -78,7 +78,12 @@ GLMVX_EXPORT int32_t glmvx_device_count(int32_t *count) {
     return kOk;
 }
 
+// Makes `device` current for this thread.  Callers activate their device
+// before every step; a device that is already current (cudaGetDevice reads
+// the runtime's thread state) is left alone.
 GLMVX_EXPORT int32_t glmvx_set_device(int32_t device) {
+    int current = -1;
+    if (cudaGetDevice(&current) == cudaSuccess && current == device) return kOk;
     GLMVX_CUDA(cudaSetDevice(device));
     return kOk;
 }

@@ -8,8 +8,11 @@ the caches of `batch` requests stay in HBM ([batch][capacity][dim] each,
 with per-request lengths on the device) and one decode step is one replayed
 CUDA graph: the step's inputs are copied in from pinned memory, the new
 rows are appended at each request's length (glmvx_dsa_append), the indexer
-scores, stable top-k and absorbed MLA run on the device (glmvx_dsa_decode),
-and the attended latents and selections are copied back.
+scores, stable top-k and absorbed MLA run on the device
+(glmvx_dsa_decode_wait), and the attended latents and selections are copied
+back.  The attention queries (most of the inbound bytes) travel on a second
+stream while the append, indexer and top-k run; the attention stage waits
+for them.
 
 Semantics per request (model.py:136-176 `_index`, :205-221 the fused
 attention branch): scores over all cached positions including the new one,
@@ -60,20 +63,23 @@ class DSADecoder:
         if need < 0:
             raise ValueError('DSA scratch size')
         self._scratch, self._scratch_bytes = dev(need), need
-        # I/O: inputs (new rows, queries), the overflow flag (sent as 0 and
-        # read back), then outputs (attended latents, selections).
+        # I/O: the attention queries (copied on a second stream while the
+        # append, indexer and top-k run), the append and indexer inputs and
+        # the overflow flag (sent as 0 and read back), then the outputs
+        # (attended latents, selections).
         H, R, P, IH, ID = self.heads, self.rank, self.rope_dim, self.index_heads, self.index_dim
-        shapes = [('new_latent', np.float32, (B, R)), ('new_rope', np.float32, (B, P)),
-                  ('new_index_key', np.float32, (B, ID)), ('q_latent', np.float32, (B, H, R)),
-                  ('q_rope', np.float32, (B, H, P)), ('q_index', np.float32, (B, IH, ID)),
+        shapes = [('q_latent', np.float32, (B, H, R)), ('q_rope', np.float32, (B, H, P)),
+                  ('new_latent', np.float32, (B, R)), ('new_rope', np.float32, (B, P)),
+                  ('new_index_key', np.float32, (B, ID)), ('q_index', np.float32, (B, IH, ID)),
                   ('head_weights', np.float32, (B, IH)), ('full', np.int32, (1,)),
                   ('out', np.float32, (B, H, R)), ('selected', np.int32, (B, self.topk))]
         self._offs, off = {}, 0
         for name, dt, shape in shapes:
             self._offs[name] = (off, dt, shape)
             off += (4 * int(np.prod(shape)) + 255) & ~255
-        self._in_bytes = self._offs['out'][0]  # inputs and the flag
         self._io_bytes = off
+        self._side, self._fork, self._queries_in = rt.Stream(), rt.Event(), rt.Event()
+        self._longest = 0  # max(self.lens)
         self._host, self._dev = rt.HostBuffer(off), dev(off)
         self._io = {}
         for name, (o, dt, shape) in self._offs.items():
@@ -111,6 +117,7 @@ class DSADecoder:
                 self._upload(self.rope_keys, rk, 4 * row * self.rope_dim)
             self._upload(self.index_keys, ik, 4 * row * self.index_dim)
         self.lens[b] = n
+        self._longest = int(self.lens.max())
         self._upload(self.lens_dev, self.lens.astype(np.int32))
 
     def pinned_io(self):
@@ -120,26 +127,34 @@ class DSADecoder:
         return {k: v for k, v in self._io.items() if k != 'full'}
 
     def _step_graph(self):
+        """The step as one graph: the append and indexer inputs (and a zero
+        overflow flag) copied in on the stream; the attention queries copied
+        in on a second stream, joined just before the attention stage; the
+        flag and outputs copied back."""
         if self._graph is not None:
             return self._graph
         s = self.backend.stream.handle
         lib, B, T = self.lib, self.batch, self.capacity
+        front, back = self._offs['new_latent'][0], self._offs['full'][0]
         g = rt.Graph(self.backend.stream)
         g.begin()
         try:
-            rt.call('glmvx_memcpy_htod', self._dev.ptr, self._host.ptr, self._in_bytes, s)
+            rt.call('glmvx_memcpy_htod', self._dev.ptr + front, self._host.ptr + front,
+                    self._offs['out'][0] - front, s)
+            self._fork.record(s)
+            self._side.wait_event(self._fork)
+            rt.call('glmvx_memcpy_htod', self._dev.ptr, self._host.ptr, front, self._side.handle)
+            self._queries_in.record(self._side)
             rt.check(lib, lib.glmvx_dsa_append(self.latents.ptr, self.rope_keys.ptr, self.index_keys.ptr,
                                                self.lens_dev.ptr, self._ptr('new_latent'), self._ptr('new_rope'),
                                                self._ptr('new_index_key'), B, T, self.rank, self.rope_dim,
                                                self.index_dim, self._ptr('full'), s), 'glmvx_dsa_append')
-            rt.check(lib, lib.glmvx_dsa_decode(self._ptr('out'), self._ptr('selected'), self._ptr('q_latent'),
-                                               self._ptr('q_rope'), self._ptr('q_index'), self._ptr('head_weights'),
-                                               self.latents.ptr, self.rope_keys.ptr, self.index_keys.ptr,
-                                               self.lens_dev.ptr, B, self.heads, self.rank, self.rope_dim,
-                                               self.index_heads, self.index_dim, T, self.topk, self.index_scale,
-                                               self.scale, self._scratch.ptr, self._scratch_bytes, s),
-                     'glmvx_dsa_decode')
-            back = self._offs['full'][0]
+            rt.check(lib, lib.glmvx_dsa_decode_wait(
+                self._ptr('out'), self._ptr('selected'), self._ptr('q_latent'), self._ptr('q_rope'),
+                self._ptr('q_index'), self._ptr('head_weights'), self.latents.ptr, self.rope_keys.ptr,
+                self.index_keys.ptr, self.lens_dev.ptr, B, self.heads, self.rank, self.rope_dim, self.index_heads,
+                self.index_dim, T, self.topk, self.index_scale, self.scale, self._scratch.ptr, self._scratch_bytes,
+                self._queries_in.handle, s), 'glmvx_dsa_decode_wait')
             rt.call('glmvx_memcpy_dtoh', self._host.ptr + back, self._dev.ptr + back, self._io_bytes - back, s)
         finally:
             g.end()
@@ -150,15 +165,17 @@ class DSADecoder:
         """One decode step for every request on the rows and queries already in
         pinned_io(): append, index, select, attend.  Returns the views
         (out [batch, heads, rank], selected [batch, topk], -1 padded)."""
-        if np.any(self.lens >= self.capacity):
+        if self._longest >= self.capacity:
             raise ValueError('a request cache is full')
         self.backend._begin()
-        self._io['full'][0] = 0
+        full = self._io['full']
+        full[0] = 0
         self._step_graph().launch()
         self.backend.stream.synchronize()
-        if self._io['full'][0]:
+        if full[0]:
             raise RuntimeError('DSA cache overflow on the device')
         self.lens += 1
+        self._longest += 1
         return self._io['out'], self._io['selected']
 
     def step(self, new_latent, new_rope, new_index_key, q_latent, q_rope, q_index, head_weights):
@@ -181,6 +198,8 @@ class DSADecoder:
             self._graph.close()
             self._graph = None
         self._host.close()
+        for h in (self._side, self._fork, self._queries_in):
+            h.close()
         for buf in self._bufs:
             buf.close()
         self._bufs = []

@@ -84,6 +84,8 @@ SIGNATURES = {
     'glmvx_dsa_scratch_bytes': ([_I32, _I32, _I32, _I32, _I32], _I64),
     'glmvx_dsa_decode': ([_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I32, _I32, _I32, _I32, _I32, _I32, _I32, _I32,
                           _F32, _F32, _P, _U64, _P], _I32),
+    'glmvx_dsa_decode_wait': ([_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I32, _I32, _I32, _I32, _I32, _I32, _I32,
+                               _I32, _F32, _F32, _P, _U64, _P, _P], _I32),
     'glmvx_nonfinite_flag': ([_P, _I64, _P, _P], _I32),
     'glmvx_ipc_handle': ([_P, _P], _I32),
     'glmvx_ipc_open': ([_P, C.POINTER(C.c_void_p)], _I32),
@@ -118,7 +120,15 @@ class CUDAUnavailable(RuntimeError):
 
 
 def library_path():
-    return Path(os.environ.get('GLM_VX_GPU_LIBRARY') or DEFAULT_LIBRARY).resolve()
+    return _resolved(os.environ.get('GLM_VX_GPU_LIBRARY') or str(DEFAULT_LIBRARY))
+
+
+@lru_cache(maxsize=None)
+def _resolved(path):
+    # Resolving walks the path with one system call per component; every
+    # runtime call looks the library up, so each configured path is resolved
+    # once.
+    return Path(path).resolve()
 
 
 @lru_cache(maxsize=None)

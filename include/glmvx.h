@@ -202,6 +202,18 @@ int32_t glmvx_dsa_decode(float *out, int32_t *selected_out, const float *q_laten
                          int32_t heads, int32_t rank, int32_t rope_dim, int32_t index_heads, int32_t index_dim,
                          int32_t capacity, int32_t topk, float index_scale, float scale, void *scratch,
                          uint64_t scratch_bytes, void *stream);
+/* glmvx_dsa_decode with the attention stage (the first reader of q_latent and
+   q_rope) waiting for `attention_inputs_ready` (a cudaEvent_t recorded after
+   those queries' copy, e.g. on a second stream), so the indexer and top-k
+   overlap the copy.  No reference counterpart: the reference's backend call
+   (gpu/backend.py:233-254) takes host arrays and copies them before any
+   kernel runs. */
+int32_t glmvx_dsa_decode_wait(float *out, int32_t *selected_out, const float *q_latent, const float *q_rope,
+                              const float *q_index, const float *head_weights, const float *latents,
+                              const float *rope_keys, const float *index_keys, const int32_t *lens, int32_t batch,
+                              int32_t heads, int32_t rank, int32_t rope_dim, int32_t index_heads, int32_t index_dim,
+                              int32_t capacity, int32_t topk, float index_scale, float scale, void *scratch,
+                              uint64_t scratch_bytes, void *attention_inputs_ready, void *stream);
 /* One decode step's new rows (model.py:176-181, 146-151: latent, rope key and
    index key appended before indexing) written at lens[b] of each query's
    caches, then lens[b] += 1; *full (device) set for a full cache. */
