@@ -122,12 +122,13 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def test_ep_step_over_gloo_matches_reference(tmp_path, oracle):
+@pytest.mark.parametrize('world', [2, 4])
+def test_ep_step_over_gloo_matches_reference(tmp_path, oracle, world):
     import torch.multiprocessing as mp
     from test_gpu_moe import reference_ffn
-    mp.spawn(_rank_main, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=True)
+    mp.spawn(_rank_main, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True)
     layer = _layer()
-    for rank in range(2):
+    for rank in range(world):
         got = np.load(tmp_path / f'rank{rank}.npz')
         want, want_ids = reference_ffn(oracle, layer, _tokens(rank), E, H, I, K, 2.5)
         assert got['ids'].tolist() == want_ids.tolist()
