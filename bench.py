@@ -662,8 +662,8 @@ def run_profile_case(args):
     use_ours()
     if args.profile_case == 'gemm':
         return profile_gemm()
-    if args.profile_case == 'dsa':
-        return profile_dsa()
+    if args.profile_case in ('dsa', 'dsa1'):  # 16 queries, or the single-query step
+        return profile_dsa(16 if args.profile_case == 'dsa' else 1)
     from gpu.backend import GPUBackend
     from gpu import runtime as rt
     from gpu.moe import MoELayer
@@ -742,7 +742,7 @@ def main():
     ap.add_argument('--impl', choices=('ours', 'reference'), default='ours')
     ap.add_argument('--cpu-seconds', type=float, default=10.0)
     ap.add_argument('--no-cpu-baseline', action='store_true')
-    ap.add_argument('--profile-case', nargs='?', const='moe', choices=('moe', 'gemm', 'dsa'),
+    ap.add_argument('--profile-case', nargs='?', const='moe', choices=('moe', 'gemm', 'dsa', 'dsa1'),
                     help='run a small kernel-capture case (one GPU) instead of the benchmark')
     args = ap.parse_args()
     if args.profile_case:
