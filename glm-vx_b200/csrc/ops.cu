@@ -601,19 +601,30 @@ __global__ void __launch_bounds__(kTopkSelectThreads, 1)
     if (tid == 0) s_count = s_ties = 0;
     __syncthreads();
     int m = k;  // sorted words
-    if (gathered) {  // every key with (key & mask) <= prefix, in any order
+    if (gathered) {  // every key with (key & mask) <= prefix, in index order
         m = k - rank + bin;
-        for (int i0 = tid - lane; i0 < n; i0 += kTopkSelectThreads) {
+        // Warp w takes a contiguous chunk of the keys: it counts its keys by
+        // ballots, the warps' counts give each warp its first slot, and it
+        // writes them there (no shared counter to contend on).
+        constexpr int kWarps = kTopkSelectThreads / 32;
+        const int chunk = ((n + kWarps - 1) / kWarps + 31) & ~31;
+        const int begin = warp * chunk, end = min(n, begin + chunk);
+        int count = 0;
+        for (int i0 = begin; i0 < end; i0 += 32) {
             const int i = i0 + lane;
-            const uint32_t key = i < n ? key_at(i) : ~0u;
-            const uint32_t take = __ballot_sync(0xffffffffu, i < n && (key & mask) <= prefix);
-            if (take) {
-                int base = 0;
-                if (lane == 0) base = atomicAdd(&s_count, __popc(take));
-                base = __shfl_sync(0xffffffffu, base, 0);
-                if (take >> lane & 1u)
-                    sel[base + __popc(take & lanes_below)] = (static_cast<uint64_t>(key) << 32) | static_cast<uint32_t>(i);
-            }
+            count += __popc(__ballot_sync(0xffffffffu, i < end && (key_at(i) & mask) <= prefix));
+        }
+        if (lane == 0) s_warp[warp] = count;
+        __syncthreads();
+        int base = 0;
+        for (int w = 0; w < warp; ++w) base += s_warp[w];
+        for (int i0 = begin; i0 < end; i0 += 32) {
+            const int i = i0 + lane;
+            const uint32_t key = i < end ? key_at(i) : ~0u;
+            const uint32_t take = __ballot_sync(0xffffffffu, i < end && (key & mask) <= prefix);
+            if (take >> lane & 1u)
+                sel[base + __popc(take & lanes_below)] = (static_cast<uint64_t>(key) << 32) | static_cast<uint32_t>(i);
+            base += __popc(take);
         }
     } else {
         // prefix = T, with more keys equal to T than fit: the k - rank keys
