@@ -550,10 +550,6 @@ __global__ void __launch_bounds__(kTopkSelectThreads, 1)
     if (k == 0) return;
     const uint32_t lanes_below = (1u << lane) - 1u;
     auto key_at = [&](int i) -> uint32_t { return STAGED ? staged[i] : topk_desc(__ldg(scores + i)); };
-    if (STAGED) {
-#pragma unroll 8
-        for (int i = tid; i < n; i += kTopkSelectThreads) staged[i] = topk_desc(__ldg(scores + i));
-    }
     const int k2 = topk_pow2(k);
     uint32_t prefix = 0, mask = 0;
     int rank = k;  // 1-based position of the k-th key among those matching prefix
@@ -563,9 +559,18 @@ __global__ void __launch_bounds__(kTopkSelectThreads, 1)
         const int bits = pass < 2 ? 12 : 8, shift = pass == 0 ? 20 : pass == 1 ? 8 : 0, nb = 1 << bits;
         for (int i = tid; i < nb; i += kTopkSelectThreads) hist[i] = 0;
         __syncthreads();
-        for (int i = tid; i < n; i += kTopkSelectThreads) {
-            const uint32_t key = key_at(i);
-            if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & (nb - 1)], 1);
+        if (STAGED && pass == 0) {  // the keys are staged while the first digit is counted (every key counts)
+#pragma unroll 8
+            for (int i = tid; i < n; i += kTopkSelectThreads) {
+                const uint32_t key = topk_desc(__ldg(scores + i));
+                staged[i] = key;
+                atomicAdd(&hist[key >> shift], 1);
+            }
+        } else {
+            for (int i = tid; i < n; i += kTopkSelectThreads) {
+                const uint32_t key = key_at(i);
+                if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & (nb - 1)], 1);
+            }
         }
         __syncthreads();
         // The digit holding the rank-th key: each thread sums nb / 1024 bins.
