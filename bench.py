@@ -59,9 +59,22 @@ TOKENS = 32
 PROFILE_EXPERTS = 32
 IQ1_BLOCK, IQ1_BYTES = 256, 50
 EXPERT_MATRIX_BYTES = INTER * (HIDDEN // IQ1_BLOCK) * IQ1_BYTES  # 2,457,600; gate, up and down are equal
-# dram bytes (read + write) per launch of the dominant kernel (gate+up), from the one-pass ncu
-# capture at this workload summarised in profiles/mma_rows_iq1_s_dram_full_config2.md.
-NCU_TRAFFIC = 906.5e6
+
+
+def traffic_row(workload):
+    """roofline.traffic for `workload` from profiles/traffic_per_launch.txt
+    (one-pass ncu captures): (bytes per launch, source) or (None, reason)."""
+    path = ROOT / 'profiles' / 'traffic_per_launch.txt'
+    try:
+        for line in path.read_text().splitlines():
+            if line.startswith('#') or not line.strip():
+                continue
+            cols = line.split('\t')
+            if cols[0] == workload:
+                return float(cols[2]), f'{path.relative_to(ROOT)} row {workload}: {cols[1]}; captured by: {cols[3]}'
+    except (OSError, IndexError, ValueError):
+        pass
+    return None, f'no ncu capture recorded for workload {workload}'
 
 
 def use_ours():
@@ -216,6 +229,10 @@ class _PackedLayerWeights:
         raw, kind, shape = self._packed(name)
         return backend.packed_matvec(raw, kind, shape, x)
 
+    def linear_batch(self, name, x, backend):
+        raw, kind, shape = self._packed(name)
+        return backend.packed_linear_batch(raw, kind, shape, x)
+
     def __call__(self, name):
         if name.endswith('e_score_correction_bias'):
             return self.layer['bias']
@@ -252,9 +269,24 @@ def oracle_ffn(cpu, layer, x):
     return result + mlp(*layer['shared'])
 
 
-def run_reference(args, ranks):
-    """The reference arm: the reference's own Python over the C oracle, host cores."""
-    if ranks.rank != 0:
+def workload_config():
+    """The config dict both arms print for the headline workload."""
+    return {'workload': 'config2_iq1_s_moe_decode_layer', 'experts': EXPERTS, 'shared_experts': 1,
+            'hidden': HIDDEN, 'moe_intermediate': INTER, 'top_k': TOPK, 'routed_scale': SCALE, 'format': 'IQ1_S',
+            'tokens_per_step': TOKENS}
+
+
+def run_reference(args):
+    """The reference arm: the reference's own Python over the C oracle, host cores.
+
+    A step is the headline's step: TOKENS token rows through one full config-2
+    layer, here by the reference's grouped path for a chunk of rows
+    (glm_vx/prefill.py:44-81 `_feed_forward`: batched router logits, rows
+    grouped by expert through packed_linear_batch / batch_v2, ascending-id
+    combine, shared expert over the whole chunk).  Under torchrun only rank 0
+    works; no process group is created, so no torch import can fix the
+    OpenMP runtime at one thread before the oracle library sets its count."""
+    if int(os.environ.get('RANK', 0)) != 0:
         return 0
     ref_root = ROOT / 'baseline' / '_ref'
     have_ref = (ref_root / 'glm_vx').exists()
@@ -265,32 +297,35 @@ def run_reference(args, ranks):
     os.environ['OMP_NUM_THREADS'] = str(cores)
     from oracle import loader
     lib = loader.parallel()
+    threads = int(C.CDLL(str(lib)).glm_vx_ref_set_threads(cores))
     layer = synthetic_layer(0)
     if have_ref:
+        from glm_vx import prefill
         model = reference_model(layer, lib)
-        run = lambda v: model._feed_forward(0, v)
-    else:  # reference Python not installed: the same semantics composed here
+        run = lambda v: prefill._feed_forward(model, 0, v)
+        source = 'baseline/_ref glm_vx.prefill._feed_forward + GlmMoeDsaModel + kernels.backend.VxBackend'
+    else:  # reference Python not installed: the same semantics composed here, token by token
         from kernels.backend import VxBackend
         cpu = VxBackend(str(lib))
-        run = lambda v: oracle_ffn(cpu, layer, v)
-    x = np.random.default_rng(1).normal(size=(args.steps + args.warmup, HIDDEN)).astype(np.float32)
+        run = lambda v: np.stack([oracle_ffn(cpu, layer, row) for row in v])
+        source = 'reference semantics composed over the oracle (baseline/_ref not installed)'
+    x = np.random.default_rng(1).normal(size=(args.steps + args.warmup, TOKENS, HIDDEN)).astype(np.float32)
     for i in range(args.warmup):
         run(x[i])
     t0 = time.perf_counter()
     for i in range(args.steps):
         run(x[args.warmup + i])
     secs = time.perf_counter() - t0
-    value = args.steps / secs
-    source = ('baseline/_ref glm_vx + kernels (GlmMoeDsaModel._feed_forward, VxBackend)' if have_ref
-              else 'reference semantics composed over the oracle (baseline/_ref not installed)')
+    value = TOKENS * args.steps / secs
     line = {
         'impl': 'reference', 'metric': METRIC, 'value': value, 'unit': 'tok/s', 'n_gpus': args.gpus,
         'steps': args.steps, 'warmup': args.warmup, 'ms_per_step': secs / args.steps * 1e3, 'higher_is_better': True,
         'scaling': 'weak', 'vs_baseline': None, 'dtype': 'f32', 'data': 'synthetic',
-        'config': {'workload': 'config2_iq1_s_moe_decode_layer', 'tokens_per_step': 1, 'parallelism': 'host cores'},
-        'cpu_baseline': {'value': value, 'unit': 'tok/s', 'cores': cores, 'kind': 'port',
-                         'sample': f'1 token per step through one full config-2 layer: {source} '
-                                   'over the OpenMP C restatement of the Vx kernels'},
+        'config': {**workload_config(), 'global_batch': TOKENS, 'parallelism': f'host cores ({threads} OpenMP threads)'},
+        'cpu_baseline': {'value': value, 'unit': 'tok/s', 'cores': threads, 'kind': 'port',
+                         'sample': f'{TOKENS} token rows per step through one full config-2 layer: {source} over '
+                                   f'the OpenMP C restatement of the Vx kernels ({threads} threads reported by the '
+                                   'library)'},
         'e2e': {'value': value, 'unit': 'tok/s', 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0},
     }
     print(json.dumps(line), flush=True)
@@ -581,12 +616,13 @@ def run_ours(args, ranks):
     gu_us = dom_t['stage_us']['gate_up']
     gu_bytes = (dom_t['unique_experts'] + 1) * 2 * EXPERT_MATRIX_BYTES + (TOKENS * TOPK + TOKENS) * 2 * INTER * 4
     achieved = gu_bytes / (gu_us * 1e-6) / 1e9
+    traffic = traffic_row(f'config2_t{TOKENS}_gate_up')
     dev.check_device_error()
 
     # e2e through the public API: token rows in pinned host memory, copied to
     # the device, the layer, outputs copied back to pinned host memory and
     # checked there (MoELayer.forward_pinned), every step.
-    e2e_steps = max(1, min(args.steps, 200))
+    e2e_steps = min(max(args.steps, 50), 200)
     e2e_h2d, e2e_d2h = moe.step_copy_bytes(TOKENS)
     np.copyto(moe.pinned_io(TOKENS)['x'], xs[TOKENS])
     for i in range(min(args.warmup, 3)):
@@ -616,7 +652,7 @@ def run_ours(args, ranks):
                    'l2_policy': 'inputs larger than L2: the layer streams 1.9 GB of resident experts',
                    'per_tokens': per_tokens},
         'roofline': {'bound': 'hbm', 'achieved': achieved, 'peak': peak, 'unit': 'GB/s', 'frac': achieved / peak,
-                     'traffic': NCU_TRAFFIC, 'kernel': 'mma_rows_kernel<IQ1_S> gate+up job lists (tensor-core int8; two- and four-token jobs, two launches)',
+                     'traffic': traffic[0], 'traffic_source': traffic[1], 'kernel': 'mma_rows_kernel<IQ1_S> gate+up job lists (tensor-core int8; two- and four-token jobs, two launches)',
                      'algorithmic_bytes_per_launch': gu_bytes, 'avg_launch_us': gu_us, 'peak_source': peak_kind},
         'fused_gemv': gemv,
         **({'dsa_decode': dsa} if dsa else {}),
@@ -737,7 +773,7 @@ def profile_dsa(batch=16):
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument('--gpus', type=int, default=1)
-    ap.add_argument('--steps', type=int, default=200)
+    ap.add_argument('--steps', type=int, default=20)
     ap.add_argument('--warmup', type=int, default=5)
     ap.add_argument('--impl', choices=('ours', 'reference'), default='ours')
     ap.add_argument('--cpu-seconds', type=float, default=10.0)
@@ -749,9 +785,11 @@ def main():
         return run_profile_case(args)
     if args.warmup < 3:
         ap.error('--warmup must be >= 3')
+    if args.impl == 'reference':
+        return run_reference(args)
     ranks = Ranks()
     try:
-        return run_reference(args, ranks) if args.impl == 'reference' else run_ours(args, ranks)
+        return run_ours(args, ranks)
     finally:
         ranks.close()
 

@@ -47,6 +47,16 @@ int *device_error_word();
 // SM count of the current device (cached per device).
 int sm_count();
 
+// Allows `kernel` (a __global__ function) `bytes` of dynamic shared memory on
+// the CURRENT device.  The attribute belongs to the function in one device's
+// context, so it is raised once per (device, kernel) and size, under a lock
+// (several host threads and several devices may launch the same kernel).
+int32_t allow_dynamic_smem(const void *kernel, size_t bytes, const char *name);
+template <class K>
+inline int32_t allow_dynamic_smem(K *kernel, size_t bytes, const char *name) {
+    return allow_dynamic_smem(reinterpret_cast<const void *>(kernel), bytes, name);
+}
+
 // ---------------------------------------------------------------- device ---
 
 // Error codes written into the device error word.

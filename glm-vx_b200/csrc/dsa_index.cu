@@ -218,14 +218,8 @@ int32_t launch_index_scores_tc(float *out, const float *q, const float *keys, co
     if (tokens <= 0 || batch <= 0) return kOk;
     uint32_t cols = 32;
     while (cols < static_cast<uint32_t>(n_pad)) cols <<= 1;
-    static const cudaError_t a1 =
-        cudaFuncSetAttribute(index_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kIdxSmem);
-    static const cudaError_t a2 =
-        cudaFuncSetAttribute(index_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kIdxSmem);
-    if (a1 != cudaSuccess || a2 != cudaSuccess) {
-        set_error("index_tc smem: %s", cudaGetErrorString(a1 != cudaSuccess ? a1 : a2));
-        return kCudaError;
-    }
+    if (const int32_t rc = allow_dynamic_smem(index_tc_kernel<true>, kIdxSmem, "index_tc smem")) return rc;
+    if (const int32_t rc = allow_dynamic_smem(index_tc_kernel<false>, kIdxSmem, "index_tc smem")) return rc;
     const int smem = kIdxStages * kIdxStageBytes + 2 * nchunks * n_pad * 128 + 1024;
     const int tiles = (tokens + kIdxTile - 1) / kIdxTile;
     const int per_query = std::max(1, std::min(tiles, (2 * 148 + batch - 1) / batch));  // ~two CTAs per SM

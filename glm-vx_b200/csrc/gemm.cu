@@ -272,14 +272,8 @@ GLMVX_EXPORT int32_t glmvx_gemm(float *C, const float *A, const float *B, int32_
         const dim3 grid((N + kSgemmTile - 1) / kSgemmTile, (M + kSgemmTile - 1) / kSgemmTile);
         gemm_f32_kernel<<<grid, 256, 0, st>>>(C, A, B, M, N, K);
     } else {
-        static const cudaError_t attr =
-            cudaFuncSetAttribute(gemm_tf32_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmem);
-        static const cudaError_t attr2 =
-            cudaFuncSetAttribute(gemm_tf32_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmem);
-        if (attr != cudaSuccess || attr2 != cudaSuccess) {
-            set_error("gemm smem: %s", cudaGetErrorString(attr != cudaSuccess ? attr : attr2));
-            return kCudaError;
-        }
+        if (const int32_t rc = allow_dynamic_smem(gemm_tf32_kernel<true>, kGemmSmem, "gemm smem")) return rc;
+        if (const int32_t rc = allow_dynamic_smem(gemm_tf32_kernel<false>, kGemmSmem, "gemm smem")) return rc;
         const bool vec = K % 4 == 0 && N % 4 == 0 &&
                          ((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(B)) & 15) == 0;
         const dim3 grid((N + kGemmBN - 1) / kGemmBN, (M + kGemmBM - 1) / kGemmBM);

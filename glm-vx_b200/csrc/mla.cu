@@ -456,9 +456,8 @@ int32_t launch_shared(dim3 grid, cudaStream_t st, float *numerator, float *stats
                       int heads, int rank, int rope_dim, int tokens, int count, int splits, float scale,
                       const int32_t *lens, int64_t latent_stride, int64_t rope_stride, int64_t sel_stride) {
     constexpr int bytes = kMlaStages * kMlaTileRows * 32 * (RPL + PPL) * 4;
-    static const cudaError_t attr =
-        cudaFuncSetAttribute(mla_shared_kernel<RPL, PPL, HPW, VEC>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
-    if (attr != cudaSuccess) return set_error("mla_shared smem: %s", cudaGetErrorString(attr)), kCudaError;
+    if (const int32_t rc = allow_dynamic_smem(mla_shared_kernel<RPL, PPL, HPW, VEC>, bytes, "mla_shared smem"))
+        return rc;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
     cfg.blockDim = dim3(32 * kMlaHeadsPerCta);
@@ -715,7 +714,9 @@ GLMVX_EXPORT int32_t glmvx_dsa_decode(float *out, int32_t *selected_out, const f
 // glmvx_dsa_decode whose attention stage (the first reader of q_latent and
 // q_rope) waits for `attention_inputs_ready` (a cudaEvent_t recorded after
 // the queries' copy, e.g. on a second stream): the indexer and top-k run
-// while those copies are still in flight.
+// while those copies are still in flight.  On every failure the stream still
+// waits for the event before the status is returned, so a stream capture
+// that forked the copy stays joined and ends with the original error.
 GLMVX_EXPORT int32_t glmvx_dsa_decode_wait(float *out, int32_t *selected_out, const float *q_latent,
                                            const float *q_rope, const float *q_index, const float *head_weights,
                                            const float *latents, const float *rope_keys, const float *index_keys,
@@ -723,9 +724,12 @@ GLMVX_EXPORT int32_t glmvx_dsa_decode_wait(float *out, int32_t *selected_out, co
                                            int32_t rope_dim, int32_t index_heads, int32_t index_dim, int32_t capacity,
                                            int32_t topk, float index_scale, float scale, void *scratch,
                                            uint64_t scratch_bytes, void *attention_inputs_ready, void *stream) {
-    return dsa_decode(out, selected_out, q_latent, q_rope, q_index, head_weights, latents, rope_keys, index_keys, lens,
-                      batch, heads, rank, rope_dim, index_heads, index_dim, capacity, topk, index_scale, scale, scratch,
-                      scratch_bytes, static_cast<cudaEvent_t>(attention_inputs_ready), stream);
+    const cudaEvent_t ready = static_cast<cudaEvent_t>(attention_inputs_ready);
+    const int32_t rc = dsa_decode(out, selected_out, q_latent, q_rope, q_index, head_weights, latents, rope_keys,
+                                  index_keys, lens, batch, heads, rank, rope_dim, index_heads, index_dim, capacity,
+                                  topk, index_scale, scale, scratch, scratch_bytes, ready, stream);
+    if (rc && ready) cudaStreamWaitEvent(static_cast<cudaStream_t>(stream), ready, 0);  // a second wait is harmless
+    return rc;
 }
 
 // Appends one row per query to the caches of glmvx_dsa_decode (device

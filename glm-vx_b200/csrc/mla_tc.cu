@@ -350,14 +350,8 @@ int32_t launch_mla_tc(float *numerator, float *stats, const float *q_latent, con
     if (!mla_tc_supported(heads, rank, rope_dim, count)) return kUnsupported;
     if (splits > kMtMaxSplits) return set_error("mla_tc: more than %d splits", kMtMaxSplits), kInvalid;
     if (batch <= 0 || splits <= 0) return kOk;
-    static const cudaError_t a1 =
-        cudaFuncSetAttribute(mla_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMtSmem);
-    static const cudaError_t a2 =
-        cudaFuncSetAttribute(mla_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMtSmem);
-    if (a1 != cudaSuccess || a2 != cudaSuccess) {
-        set_error("mla_tc smem: %s", cudaGetErrorString(a1 != cudaSuccess ? a1 : a2));
-        return kCudaError;
-    }
+    if (const int32_t rc = allow_dynamic_smem(mla_tc_kernel<true>, kMtSmem, "mla_tc smem")) return rc;
+    if (const int32_t rc = allow_dynamic_smem(mla_tc_kernel<false>, kMtSmem, "mla_tc smem")) return rc;
     MtArgs args{numerator, stats, q_latent, q_rope, latent, rope, selected, lens, heads, rank, rope_dim, tokens,
                 count, splits, (count + splits - 1) / splits, (heads + 15) / 16 * 16, scale, latent_stride,
                 rope_stride, sel_stride, device_error_word()};

@@ -294,6 +294,27 @@ GLMVX_EXPORT int64_t glmvx_moe_workspace_bytes(int32_t tokens, int32_t hidden, i
     return static_cast<int64_t>(carve(nullptr, tokens, hidden, inter, experts, top_k, has_shared != 0).bytes + 256);
 }
 
+// Job counts the last glmvx_moe_ffn / glmvx_moe_experts call on `workspace`
+// built (device -> host, synchronising `stream`): [0] gate+up and [1] down
+// jobs of two tokens, [2] gate+up and [3] down jobs of four tokens.  Zero
+// four-token jobs means that list was not used; the CUDA-core path (formats
+// without the tensor-core kernel) builds none of these lists.
+GLMVX_EXPORT int32_t glmvx_moe_job_counts(int32_t tokens, int32_t hidden, int32_t inter, int32_t experts,
+                                          int32_t top_k, int32_t has_shared, const void *workspace,
+                                          int32_t *counts4, void *stream) {
+    if (tokens <= 0 || hidden <= 0 || inter <= 0 || experts <= 0 || top_k <= 0 || !workspace || !counts4) {
+        set_error("moe job counts: invalid arguments");
+        return kInvalid;
+    }
+    const char *base = static_cast<const char *>(workspace);
+    base += (256 - (reinterpret_cast<uintptr_t>(base) & 255)) & 255;
+    const MoeWorkspace w = carve(const_cast<char *>(base), tokens, hidden, inter, experts, top_k, has_shared != 0);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    GLMVX_CUDA(cudaMemcpyAsync(counts4, w.counts, 4 * sizeof(int), cudaMemcpyDeviceToHost, st));
+    GLMVX_CUDA(cudaStreamSynchronize(st));
+    return kOk;
+}
+
 static int32_t moe_ffn(float *y, const float *x, int32_t tokens, int32_t hidden, int32_t inter, const float *router_w,
                        const float *router_bias, int32_t experts, int32_t top_k, float scale, int32_t kind,
                        const uint8_t *gate, const uint8_t *up, const uint8_t *down, const uint8_t *shared_gate,

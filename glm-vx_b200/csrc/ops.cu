@@ -843,13 +843,10 @@ int32_t launch_topk_batch(int32_t *indices, const float *scores, int n, int k, c
     if (k <= 0 || k > kTopkSelectMaxK) return set_error("topk: 1 <= k <= %d", kTopkSelectMaxK), kInvalid;
     if (batch <= 0) return kOk;
     const bool staged = n <= kTopkStagedScores;
-    static const cudaError_t attr_staged = cudaFuncSetAttribute(
-        topk_select_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTopkSelectSmem + kTopkStagedScores * 4);
-    static const cudaError_t attr_plain = cudaFuncSetAttribute(
-        topk_select_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTopkSelectSmem);
-    const cudaError_t attr = staged ? attr_staged : attr_plain;
-    if (attr != cudaSuccess) return set_error("topk_select smem: %s", cudaGetErrorString(attr)), kCudaError;
     const int smem = kTopkSelectSmem + (staged ? n * 4 : 0);
+    if (const int32_t rc = staged ? allow_dynamic_smem(topk_select_kernel<true>, smem, "topk_select smem")
+                                  : allow_dynamic_smem(topk_select_kernel<false>, smem, "topk_select smem"))
+        return rc;
     if (staged)
         topk_select_kernel<true><<<batch, kTopkSelectThreads, smem, stream>>>(indices, scores, n, k, lens,
                                                                              score_stride, out_stride);
@@ -1002,6 +999,7 @@ GLMVX_EXPORT int32_t glmvx_router(int32_t *ids, float *weights, const float *log
 
 // Scratch bytes glmvx_topk needs for n scores (0 when it sorts in shared memory).
 GLMVX_EXPORT int64_t glmvx_topk_scratch_bytes(int32_t n) {
+    if (n > (1 << 30)) return -1;
     int64_t n2 = 1;
     while (n2 < n) n2 <<= 1;
     return n2 <= kTopkSmemKeys ? 0 : n2 * 8;
@@ -1010,8 +1008,9 @@ GLMVX_EXPORT int64_t glmvx_topk_scratch_bytes(int32_t n) {
 GLMVX_EXPORT int32_t glmvx_topk(int32_t *indices, const float *scores, int32_t n, int32_t k, void *scratch,
                                 void *stream) {
     if (n < 0 || k < 0 || n < k) return set_error("topk n/k"), kInvalid;
+    if (n > (1 << 30)) return set_error("topk: at most 2^30 scores"), kInvalid;
     if (k == 0) return kOk;
-    int n2 = 1;
+    int64_t n2 = 1;
     while (n2 < n) n2 <<= 1;
     if (n2 > kTopkSmemKeys && k <= kTopkSelectMaxK) {  // many scores, bounded k: radix selection
         return launch_topk_batch(indices, scores, n, k, nullptr, 0, 0, 1, S_);

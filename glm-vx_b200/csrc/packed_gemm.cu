@@ -527,11 +527,7 @@ template <class F, int NTW>
 int32_t launch_gemm(const GemmPlan &p, float *out, const uint8_t *w, const uint8_t *rec, int rows, int cols, int batch,
                     int row_bytes, cudaStream_t stream) {
     auto kern = gemm_f16_kernel<F, NTW>;
-    static size_t configured = 0;
-    if (p.smem > configured) {
-        GLMVX_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(p.smem)));
-        configured = p.smem;
-    }
+    if (const int32_t rc = allow_dynamic_smem(kern, p.smem, "packed_gemm smem")) return rc;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(p.grid);
     cfg.blockDim = dim3((p.RG * p.TG * p.S + 1) * 32);

@@ -782,11 +782,7 @@ static int32_t launch_mma_fr(const MmaPlan &p, const MmaJob &job0, const MmaJob 
                              cudaStream_t stream) {
     constexpr int RG = mma_row_groups(S, W);
     auto kern = mma_rows_kernel<F, S, RG, W, NT, FR>;
-    static size_t configured = 0;  // per instantiation
-    if (p.smem > configured) {
-        GLMVX_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(p.smem)));
-        configured = p.smem;
-    }
+    if (const int32_t rc = allow_dynamic_smem(kern, p.smem, "packed_mma smem")) return rc;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(p.grid);
     cfg.blockDim = dim3((S * RG + 1) * 32);

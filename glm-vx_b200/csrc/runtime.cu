@@ -5,7 +5,9 @@
 #include <algorithm>
 #include <cstdarg>
 #include <cstdio>
+#include <map>
 #include <mutex>
+#include <utility>
 
 #include "common.cuh"
 
@@ -55,6 +57,22 @@ int sm_count() {
         cached[dev] = n > 0 ? n : 148;
     }
     return cached[dev];
+}
+
+int32_t allow_dynamic_smem(const void *kernel, size_t bytes, const char *name) {
+    if (bytes <= 48 * 1024) return kOk;  // below the default limit nothing needs raising
+    int dev = 0;
+    GLMVX_CUDA(cudaGetDevice(&dev));
+    static std::mutex mu;
+    static std::map<std::pair<int, const void *>, size_t> raised;  // (device, kernel) -> bytes allowed
+    std::lock_guard<std::mutex> lock(mu);
+    size_t &have = raised[{dev, kernel}];
+    if (have >= bytes) return kOk;
+    const cudaError_t e =
+        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes));
+    if (e != cudaSuccess) return cuda_fail(e, name);
+    have = bytes;
+    return kOk;
 }
 
 }  // namespace glmvx
@@ -114,6 +132,15 @@ GLMVX_EXPORT int32_t glmvx_malloc(void **ptr, uint64_t bytes) {
     *ptr = nullptr;
     if (bytes == 0) return kOk;
     GLMVX_CUDA(cudaMalloc(ptr, bytes));
+    return kOk;
+}
+
+// Free and total bytes of device memory on the current device (cudaMemGetInfo).
+GLMVX_EXPORT int32_t glmvx_mem_get_info(uint64_t *free_bytes, uint64_t *total_bytes) {
+    size_t f = 0, t = 0;
+    GLMVX_CUDA(cudaMemGetInfo(&f, &t));
+    if (free_bytes) *free_bytes = f;
+    if (total_bytes) *total_bytes = t;
     return kOk;
 }
 

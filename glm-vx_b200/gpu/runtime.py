@@ -104,6 +104,8 @@ SIGNATURES = {
     'glmvx_moe_experts': ([_P, _P, _P, _I32, _I32, _I32, _I32, _I32, _P, _P, _P, _P, _U64, _P], _I32),
     'glmvx_moe_combine': ([_P, _P, _P, _P, _P, _I32, _I32, _I32, _P], _I32),
     'glmvx_gather_rows': ([_P, _P, _P, _I32, _I32, _P], _I32),
+    'glmvx_mem_get_info': ([C.POINTER(_U64), C.POINTER(_U64)], _I32),
+    'glmvx_moe_job_counts': ([_I32, _I32, _I32, _I32, _I32, _I32, _P, _PI32, _P], _I32),
 }
 
 

@@ -101,6 +101,10 @@ int32_t glmvx_device_info(int32_t device, char *name, int32_t name_len, int32_t 
                           int64_t *l2_bytes, int64_t *total_mem, int32_t *smem_optin);
 int32_t glmvx_malloc(void **ptr, uint64_t bytes);
 int32_t glmvx_free(void *ptr);
+/* Free / total device memory of the current device (cudaMemGetInfo; the
+ * reference runtime's CUDAContext has no counterpart, tests use it to show
+ * that an entry point allocates nothing). */
+int32_t glmvx_mem_get_info(uint64_t *free_bytes, uint64_t *total_bytes);
 int32_t glmvx_host_alloc(void **ptr, uint64_t bytes); /* pinned host memory */
 int32_t glmvx_host_free(void *ptr);
 int32_t glmvx_memcpy_htod(void *dst, const void *src, uint64_t bytes, void *stream);
@@ -257,6 +261,12 @@ int32_t glmvx_moe_ffn_profiled(float *y, const float *x, int32_t tokens, int32_t
                                float scale, int32_t kind, const uint8_t *gate, const uint8_t *up, const uint8_t *down,
                                const uint8_t *shared_gate, const uint8_t *shared_up, const uint8_t *shared_down,
                                void *workspace, uint64_t workspace_bytes, void *const *events, void *stream);
+/* The job counts the last glmvx_moe_ffn / glmvx_moe_experts call on
+ * `workspace` built, copied to counts4 (host) after synchronising `stream`:
+ * two-token gate+up, two-token down, four-token gate+up, four-token down.
+ * Diagnostic (which job lists a layer call used); no reference counterpart. */
+int32_t glmvx_moe_job_counts(int32_t tokens, int32_t hidden, int32_t inter, int32_t experts, int32_t top_k,
+                             int32_t has_shared, const void *workspace, int32_t *counts4, void *stream);
 /* Expert-parallel building blocks (the reference runs all experts in one
  * process; these split glm_vx/model.py:289-324 between the rank that routes a
  * token and the rank that owns its expert).  glmvx_moe_experts: routed experts

@@ -19,6 +19,25 @@
 #endif
 #define EXPORT __attribute__((visibility("default")))
 
+#if defined(_OPENMP)
+#include <omp.h>
+#endif
+
+/* Thread control of the OpenMP build (no reference counterpart): the timed
+ * CPU legs set the thread count through the library itself, so an OpenMP
+ * runtime that another module initialised earlier (with OMP_NUM_THREADS=1,
+ * as torchrun exports) cannot pin it to one thread.  The serial build reports
+ * one thread and ignores the request. */
+EXPORT int32_t glm_vx_ref_set_threads(int32_t n) {
+#if defined(_OPENMP)
+    if (n > 0) omp_set_num_threads(n);
+    return omp_get_max_threads();
+#else
+    (void)n;
+    return 1;
+#endif
+}
+
 /* Sign-split logistic (kernels/kernels.vx:8-15). */
 static float sigmoid_f32(float x) {
     if (x >= 0.0f) return 1.0f / (1.0f + expf(0.0f - x));

@@ -78,27 +78,58 @@ def test_moe_small(gpu_backend, oracle, tokens, H, I):
         moe.close()
 
 
-def test_moe_config2_full_width(gpu_backend):
-    """BASELINE config 2 shapes: 256 experts + shared, hidden 6144, inter 2048, IQ1_S, top-8, scale 2.5."""
+@pytest.fixture(scope='module')
+def config2_layer(gpu_backend):
+    """BASELINE config 2 at full width: 256 experts + shared, hidden 6144,
+    inter 2048, IQ1_S, top-8, scale 2.5 (the benchmarked layer's shapes)."""
     from gpu.moe import MoELayer
-    from oracle import loader
-    from kernels.backend import VxBackend
-    cpu = VxBackend(str(loader.parallel()))
     E, H, I, K = 256, 6144, 2048, 8
     layer = synthetic_layer(E, H, I, seed=2)
     moe = MoELayer(gpu_backend, layer['router'], layer['bias'], 19, layer['gate'], layer['up'], layer['down'],
                    H, I, K, 2.5, shared=layer['shared'])
-    try:
-        x = np.random.default_rng(7).normal(size=(2, H)).astype(np.float32)
-        y, ids, _ = moe.forward(x)
-        want, want_ids = reference_ffn(cpu, layer, x, E, H, I, K, 2.5)
-        assert ids.tolist() == want_ids.tolist()
-        assert np.linalg.norm(y - want) / np.linalg.norm(want) <= RTOL
-        # deterministic across calls
-        y2, _, _ = moe.forward(x)
-        assert y2.tobytes() == y.tobytes()
-    finally:
-        moe.close()
+    yield layer, moe
+    moe.close()
+
+
+def _job_counts(moe, tokens):
+    import ctypes as C
+    counts = (C.c_int32 * 4)()
+    moe.backend.lib.glmvx_moe_job_counts(tokens, moe.hidden, moe.inter, moe.experts, moe.top_k, 1, moe._ws.ptr,
+                                         counts, moe.backend.stream.handle)
+    return list(counts)
+
+
+@pytest.mark.parametrize('T', [1, 2, 8, 32])
+def test_moe_config2_full_width(config2_layer, T):
+    """The benchmarked layer (config 2, full width) at 1, 2, 8 and 32 tokens
+    against the reference's sparse feed-forward (glm_vx/model.py:289-324) on
+    the CPU oracle: identical routing, outputs within 1e-5.  At 32 tokens the
+    IQ1_S experts routed three or more tokens and the shared expert run in
+    the four-token job list (mma_rows_kernel<IQ1_S, S=12> with two token pairs
+    per fragment), the path the headline number times; the job counts show
+    both lists were used.  Repeated calls are bit-identical."""
+    from oracle import loader
+    from kernels.backend import VxBackend
+    layer, moe = config2_layer
+    cpu = VxBackend(str(loader.parallel()))
+    E, H, I, K = 256, 6144, 2048, 8
+    x = np.random.default_rng(7 + T).normal(size=(T, H)).astype(np.float32)
+    y, ids, _ = moe.forward(x)
+    counts = _job_counts(moe, T)
+    want, want_ids = reference_ffn(cpu, layer, x, E, H, I, K, 2.5)
+    assert ids.tolist() == want_ids.tolist()
+    err = np.linalg.norm(y - want) / np.linalg.norm(want)
+    assert err <= RTOL, err
+    row_err = np.linalg.norm(y - want, axis=1) / np.linalg.norm(want, axis=1)
+    assert row_err.max() <= RTOL, row_err.max()
+    assert counts[0] == 2 * counts[1] and counts[2] == 2 * counts[3]
+    if T >= 16:
+        # the shared expert alone fills ceil(T/4) four-token jobs
+        assert counts[3] >= (T + 3) // 4, counts
+    else:
+        assert counts[3] == 0, counts
+    y2, _, _ = moe.forward(x)
+    assert y2.tobytes() == y.tobytes()
 
 
 def _check_layer(gpu_backend, oracle, E, H, I, K, T, kind, seed):

@@ -1,6 +1,12 @@
 """glmvx_moe_ffn_static (scratch in a file-scope device array, no workspace
 argument) against glmvx_moe_ffn (caller workspace) on the same resident layer.
 
+The static entry is for callers that cannot allocate device memory -- a host
+runtime whose allocator already owns the device's whole memory budget, or a
+decode loop that must keep a fixed footprint.  Both entries run the same
+kernels on the same data, so their outputs must agree byte for byte; and the
+device's free memory must not change across two calls of the static entry.
+
 Collected last on purpose: it must also pass after every other GPU test has
 run in the same process (the static array is then set up on a device that has
 already done other work)."""
@@ -44,12 +50,25 @@ def test_static_scratch_matches_workspace_entry(gpu_backend):
         yd.download(want_y)
         idd.download(want_ids)
         wd.download(want_w)
-        for _ in range(2):  # two calls in a row through the same static scratch
-            for b in (yd, idd, wd):
-                rt.call('glmvx_memset', b.ptr, 0, b.nbytes, stream.handle)
+        def call_static():
             code = fn(yd.ptr, xd.ptr, T, H, I, moe.router_w, moe.router_bias, E, K, scale, 19, moe.gate, moe.up,
                       moe.down, *moe.shared, idd.ptr, wd.ptr, stream.handle)
             rt.check(lib, code, 'glmvx_moe_ffn_static')
+
+        def free_bytes():
+            free, total = C.c_uint64(), C.c_uint64()
+            rt.check(lib, lib.glmvx_mem_get_info(C.byref(free), C.byref(total)), 'glmvx_mem_get_info')
+            return free.value
+
+        # The first call on a device looks the array's address up (which can
+        # load the library's module data); measure the calls after it.
+        call_static()
+        stream.synchronize()
+        free_before = free_bytes()
+        for _ in range(2):  # two calls in a row through the same static scratch
+            for b in (yd, idd, wd):
+                rt.call('glmvx_memset', b.ptr, 0, b.nbytes, stream.handle)
+            call_static()
             y, ids, w = np.empty_like(x), np.empty((T, K), np.int32), np.empty((T, K), np.float32)
             stream.synchronize()
             yd.download(y)
@@ -57,9 +76,12 @@ def test_static_scratch_matches_workspace_entry(gpu_backend):
             wd.download(w)
             gpu_backend.device.check_device_error()
             assert ids.tolist() == want_ids.tolist()
-            np.testing.assert_allclose(w, want_w, rtol=RTOL, atol=0)
+            assert w.tobytes() == want_w.tobytes()
+            assert y.tobytes() == want_y.tobytes()
             err = np.linalg.norm(y - want_y) / np.linalg.norm(want_y)
             assert err <= RTOL, err
+        assert free_bytes() == free_before, 'the static entry allocated device memory'
+
     finally:
         stream.synchronize()
         for b in bufs:
