@@ -35,6 +35,7 @@
 #include "codecs.cuh"
 #include "gemv_jobs.cuh"
 #include "mma_gemv.cuh"
+#include "moe_jobs.cuh"
 
 namespace glmvx {
 
@@ -86,41 +87,33 @@ static MoeWorkspace carve(char *base, int T, int hidden, int inter, int E, int k
 #ifndef GLMVX_QUAD_MIN_TOKENS
 #define GLMVX_QUAD_MIN_TOKENS 16
 #endif
-constexpr int kGroupThreads = 512, kMaxAssignments = 4096, kQuadMinTokens = GLMVX_QUAD_MIN_TOKENS;
+constexpr int kQuadMinTokens = GLMVX_QUAD_MIN_TOKENS;
 
-// Inclusive prefix sum of v[0..n) in place (n <= kMaxAssignments), whole CTA.
-__device__ void block_inclusive_scan(int16_t *v, int n, int32_t *s_warp) {
-    const int per = (n + kGroupThreads - 1) / kGroupThreads;
-    const int b0 = min(static_cast<int>(threadIdx.x) * per, n), b1 = min(b0 + per, n);
-    int sum = 0;
-    for (int i = b0; i < b1; ++i) sum += v[i];
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    int incl = sum;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-        const int y = __shfl_up_sync(0xffffffffu, incl, o);
-        if (lane >= o) incl += y;
-    }
-    if (lane == 31) s_warp[warp] = incl;
-    __syncthreads();
-    int before = 0;
-    for (int w = 0; w < warp; ++w) before += s_warp[w];
-    int run = before + incl - sum;
-    for (int i = b0; i < b1; ++i) {
-        run += v[i];
-        v[i] = static_cast<int16_t>(run);
-    }
-    __syncthreads();
-}
+// Addresses of the single-GPU layer's assignments for form_mma_jobs:
+// assignment a is token a / k; every pair's down output is row r of pair_out.
+struct LocalJobSrc {
+    const uint8_t *gate, *up, *down, *sgate, *sup, *sdown, *xprep;
+    size_t gu_stride, dn_stride, xstride;
+    float *pair_out;
+    int k, hidden;
+    __device__ const uint8_t *wg(int e) const { return gate + e * gu_stride; }
+    __device__ const uint8_t *wu(int e) const { return up + e * gu_stride; }
+    __device__ const uint8_t *wd(int e) const { return down + e * dn_stride; }
+    __device__ const uint8_t *sg() const { return sgate; }
+    __device__ const uint8_t *su() const { return sup; }
+    __device__ const uint8_t *sd() const { return sdown; }
+    __device__ const uint8_t *xp(int a) const { return xprep + static_cast<size_t>(a / k) * xstride; }
+    __device__ float *out(int, int r) const { return pair_out + static_cast<size_t>(r) * hidden; }
+    __device__ const uint8_t *xp_shared(int t) const { return xprep + static_cast<size_t>(t) * xstride; }
+    __device__ float *out_shared(int, int r) const { return pair_out + static_cast<size_t>(r) * hidden; }
+};
 
 // Rank each (token, slot) assignment by (expert id, token): the rank is its
 // pair index, so pairs of one expert are contiguous and ordered by token.
-// With mjobs set (tensor-core path), consecutive pairs of one expert share a
-// job: the pair whose index within its expert's run is even opens a job,
-// the next one (if any) takes the job's second slot.  With qjobs set too,
-// experts routed three or more pairs (and the shared expert, from three
-// tokens) go to the second list instead, four consecutive pairs per job
-// (slots 0..3), so their weights are decoded once per four tokens.
+// With mjobs set (tensor-core path) the job lists come from form_mma_jobs
+// (moe_jobs.cuh): two tokens per job, and with qjobs set too experts routed
+// three or more pairs and the shared expert in a list of four tokens per job.
+// Otherwise one streaming GEMV job per pair (GemvJob).
 __global__ void __launch_bounds__(kGroupThreads)
     moe_group_kernel(const int32_t *ids, const float *wts, int T, int k, int E, int shared, const uint8_t *gate,
                      const uint8_t *up, const uint8_t *down, size_t gu_stride, size_t dn_stride, const uint8_t *sgate,
@@ -128,136 +121,61 @@ __global__ void __launch_bounds__(kGroupThreads)
                      float *u_out, float *pair_out, GemvJob *gu_jobs, GemvJob *dn_jobs, int32_t *comb, float *combw,
                      int *bad, MmaJob *gu_m, MmaJob *dn_m, MmaJob *gu_q, MmaJob *dn_q, int *counts,
                      const uint8_t *xprep, size_t xstride, const uint8_t *hprep, size_t hstride) {
-    __shared__ int16_t s_ids[kMaxAssignments];   // expert ids (< 32768, checked by the host)
-    __shared__ int16_t s_pair[kMaxAssignments];  // rank of each assignment
-    __shared__ int16_t s_job[kMaxAssignments];   // per rank: opens a two-token job (0/1), then the job id + 1
-    __shared__ int16_t s_jobq[kMaxAssignments];  // per rank: opens a four-token job, then the job id + 1
-    __shared__ int8_t s_list[kMaxAssignments];   // per rank: 1 = four-token list
-    __shared__ int32_t s_warp[kGroupThreads / 32];
+    __shared__ GroupSmem g;
     const int n = T * k;
     const int P = n + (shared ? T : 0);
     const bool mma = gu_m != nullptr;
-    const bool quad = mma && gu_q != nullptr;
     for (int a = threadIdx.x; a < n; a += blockDim.x) {
         const int e = ids[a];
-        s_ids[a] = static_cast<int16_t>(min(max(e, 0), E - 1));
+        g.ids[a] = static_cast<int16_t>(min(max(e, 0), E - 1));
         if (e < 0 || e >= E) report_device_error(bad, kDevErrBadIndex);
     }
     __syncthreads();
-    for (int a = threadIdx.x; a < n; a += blockDim.x) {
-        const int e = s_ids[a];
-        int lt = 0, eq = 0, cnt = 0;
-        for (int b = 0; b < n; ++b) {
-            const int eb = s_ids[b];
-            lt += eb < e;
-            eq += (eb == e) & (b < a);
-            cnt += eb == e;
-        }
-        const int rank = lt + eq;
-        s_pair[a] = static_cast<int16_t>(rank);
-        if (mma) {
-            const bool q4 = quad && cnt >= 3;
-            s_list[rank] = q4;
-            s_job[rank] = static_cast<int16_t>(!q4 && (eq & 1) == 0);
-            s_jobq[rank] = static_cast<int16_t>(q4 && (eq & 3) == 0);
-            continue;
-        }
-        const int t = a / k;
-        const int ec = min(max(e, 0), E - 1);  // never form an out-of-range pointer
-        gu_jobs[rank] = GemvJob{gate + ec * gu_stride, x + static_cast<size_t>(t) * hidden, nullptr,
-                                g_out + static_cast<size_t>(rank) * inter};
-        gu_jobs[P + rank] = GemvJob{up + ec * gu_stride, x + static_cast<size_t>(t) * hidden, nullptr,
-                                    u_out + static_cast<size_t>(rank) * inter};
-        dn_jobs[rank] = GemvJob{down + ec * dn_stride, g_out + static_cast<size_t>(rank) * inter,
-                                u_out + static_cast<size_t>(rank) * inter, pair_out + static_cast<size_t>(rank) * hidden};
-    }
-    if (shared && !mma) {
-        for (int t = threadIdx.x; t < T; t += blockDim.x) {
-            const int p = n + t;
-            gu_jobs[p] = GemvJob{sgate, x + static_cast<size_t>(t) * hidden, nullptr, g_out + static_cast<size_t>(p) * inter};
-            gu_jobs[P + p] = GemvJob{sup, x + static_cast<size_t>(t) * hidden, nullptr, u_out + static_cast<size_t>(p) * inter};
-            dn_jobs[p] = GemvJob{sdown, g_out + static_cast<size_t>(p) * inter, u_out + static_cast<size_t>(p) * inter,
-                                 pair_out + static_cast<size_t>(p) * hidden};
-        }
-    }
-    __syncthreads();
     if (mma) {
-        block_inclusive_scan(s_job, n, s_warp);   // s_job[r] = 1 + id of the two-token job holding rank r
-        block_inclusive_scan(s_jobq, n, s_warp);  // s_jobq[r] = 1 + id of the four-token job holding rank r
-        const bool shared_q = quad;  // the host enables four-token jobs from 16 tokens
-        const int routed = n ? s_job[n - 1] : 0, routed_q = n ? s_jobq[n - 1] : 0;
-        const int J = routed + (shared && !shared_q ? (T + 1) / 2 : 0);
-        const int JQ = routed_q + (shared && shared_q ? (T + 3) / 4 : 0);
-        // Pass 0 writes whole jobs from the pair in slot 0 (other slots
-        // empty), pass 1 fills the other slots.
-        for (int pass = 0; pass < 2; ++pass) {
-            for (int a = threadIdx.x; a < n + (shared ? T : 0); a += blockDim.x) {
-                int e, t, r, j, slot;
-                bool q4;
-                const uint8_t *wg, *wu, *wd;
-                if (a < n) {
-                    e = s_ids[a];
-                    t = a / k;
-                    r = s_pair[a];
-                    q4 = s_list[r];
-                    slot = 0;
-                    if (q4) {  // preceding ranks of the same four-token job
-                        j = s_jobq[r] - 1;
-                        for (int c = 1; c <= 3 && r - c >= 0 && s_list[r - c] && s_jobq[r - c] == s_jobq[r]; ++c)
-                            slot = c;
-                    } else {
-                        j = s_job[r] - 1;
-                        slot = (r > 0 && !s_list[r - 1] && s_job[r - 1] == s_job[r]) ? 1 : 0;
-                    }
-                    wg = gate + e * gu_stride;
-                    wu = up + e * gu_stride;
-                    wd = down + e * dn_stride;
-                } else {
-                    t = a - n;
-                    r = n + t;
-                    q4 = shared_q;
-                    j = q4 ? routed_q + t / 4 : routed + t / 2;
-                    slot = q4 ? t & 3 : t & 1;
-                    wg = sgate;
-                    wu = sup;
-                    wd = sdown;
-                }
-                if ((slot != 0) != (pass != 0)) continue;
-                const uint8_t *xp = xprep + static_cast<size_t>(t) * xstride;
-                const uint8_t *hp = hprep + static_cast<size_t>(r) * hstride;
-                float *go = g_out + static_cast<size_t>(r) * inter, *uo = u_out + static_cast<size_t>(r) * inter;
-                float *po = pair_out + static_cast<size_t>(r) * hidden;
-                MmaJob *gl = q4 ? gu_q : gu_m, *dl = q4 ? dn_q : dn_m;
-                const int Jl = q4 ? JQ : J;
-                if (slot == 0) {
-                    gl[j] = MmaJob{wg, {xp}, {go}};
-                    gl[Jl + j] = MmaJob{wu, {xp}, {uo}};
-                    dl[j] = MmaJob{wd, {hp}, {po}};
-                } else {
-                    gl[j].xp[slot] = xp;
-                    gl[j].out[slot] = go;
-                    gl[Jl + j].xp[slot] = xp;
-                    gl[Jl + j].out[slot] = uo;
-                    dl[j].xp[slot] = hp;
-                    dl[j].out[slot] = po;
-                }
+        const LocalJobSrc src{gate, up, down, sgate, sup, sdown, xprep, gu_stride, dn_stride, xstride, pair_out, k,
+                              hidden};
+        form_mma_jobs(src, g, n, shared ? T : 0, gu_q != nullptr, g_out, u_out, hprep, hstride, inter, gu_m, dn_m,
+                      gu_q, dn_q, counts);
+    } else {
+        for (int a = threadIdx.x; a < n; a += blockDim.x) {
+            const int e = g.ids[a];
+            int lt = 0, eq = 0;
+            for (int b = 0; b < n; ++b) {
+                const int eb = g.ids[b];
+                lt += eb < e;
+                eq += (eb == e) & (b < a);
             }
-            __syncthreads();
+            const int rank = lt + eq;
+            g.pair[a] = static_cast<int16_t>(rank);
+            const int t = a / k;
+            gu_jobs[rank] = GemvJob{gate + e * gu_stride, x + static_cast<size_t>(t) * hidden, nullptr,
+                                    g_out + static_cast<size_t>(rank) * inter};
+            gu_jobs[P + rank] = GemvJob{up + e * gu_stride, x + static_cast<size_t>(t) * hidden, nullptr,
+                                        u_out + static_cast<size_t>(rank) * inter};
+            dn_jobs[rank] = GemvJob{down + e * dn_stride, g_out + static_cast<size_t>(rank) * inter,
+                                    u_out + static_cast<size_t>(rank) * inter,
+                                    pair_out + static_cast<size_t>(rank) * hidden};
         }
-        if (threadIdx.x == 0) {
-            counts[0] = 2 * J;
-            counts[1] = J;
-            counts[2] = 2 * JQ;
-            counts[3] = JQ;
+        if (shared) {
+            for (int t = threadIdx.x; t < T; t += blockDim.x) {
+                const int p = n + t;
+                gu_jobs[p] = GemvJob{sgate, x + static_cast<size_t>(t) * hidden, nullptr,
+                                     g_out + static_cast<size_t>(p) * inter};
+                gu_jobs[P + p] = GemvJob{sup, x + static_cast<size_t>(t) * hidden, nullptr,
+                                         u_out + static_cast<size_t>(p) * inter};
+                dn_jobs[p] = GemvJob{sdown, g_out + static_cast<size_t>(p) * inter,
+                                     u_out + static_cast<size_t>(p) * inter, pair_out + static_cast<size_t>(p) * hidden};
+            }
         }
+        __syncthreads();
     }
     // Each token's slots in ascending expert id (glm_vx/model.py:305-316).
     for (int t = threadIdx.x; t < T; t += blockDim.x) {
         for (int i = 0; i < k; ++i) {
-            const int a = t * k + i, e = s_ids[a];
+            const int a = t * k + i, e = g.ids[a];
             int pos = 0;
-            for (int j = 0; j < k; ++j) pos += s_ids[t * k + j] < e;
-            comb[t * k + pos] = s_pair[a];
+            for (int j = 0; j < k; ++j) pos += g.ids[t * k + j] < e;
+            comb[t * k + pos] = g.pair[a];
             combw[t * k + pos] = wts[a];
         }
     }
