@@ -32,11 +32,15 @@ Arms:
              baseline/_ref) over the OpenMP C restatement of its uncompilable
              Vx kernels, one token per step, all host cores.
 
-Multi-GPU: each rank runs an independent replica of the layer on its own
-token batch (the headline, "replicas"); torch.distributed over gloo carries
-only barriers and the max of device times.  With N>1 the line also carries
-`expert_parallel`: the same layer with its experts sharded over the N GPUs
-(gpu/ep.py), exchanging (token, expert) rows with NCCL all-to-all.
+Multi-GPU (N>1, one process per GPU under torchrun): the headline is the
+same layer EXPERT-PARALLEL over the N GPUs (gpu/ep.py, csrc/ep.cu): 256/N
+experts per GPU, router and shared expert replicated, TOKENS rows per GPU
+per step, token rows and expert outputs moved by this library's kernels over
+peer memory (NVLink), one captured graph of K steps per rank, max over
+ranks.  Its line carries the per-rank parity against the full single-GPU
+layer (bit-identical expected).  The N independent replicas are reported
+beside it (`replicas`).  torch.distributed over gloo carries only barriers,
+the max of device times and the one-time swap of IPC handles.
 """
 import argparse
 import ctypes as C
@@ -184,13 +188,6 @@ class Ranks:
         t = torch.tensor([float(value)], dtype=torch.float64)
         self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
         return float(t.item())
-
-    def nccl_group(self):
-        """A second group over NCCL (the expert-parallel exchange); the
-        default gloo group keeps carrying barriers and max-reductions."""
-        import torch
-        torch.cuda.set_device(self.local)
-        return self.dist.new_group(backend='nccl')
 
     def close(self):
         if self.dist:
@@ -505,51 +502,118 @@ def dsa_sweep(rt, lib, backend, stream, steps, peak):
     return res
 
 
-def expert_parallel_step(args, ranks, layer, exchange='nccl'):
-    """N>1: the same layer with its 256 experts sharded over the ranks
-    (gpu/ep.py), TOKENS rows per rank; device time of the step (CUDA events on
-    the launching stream, host routing sync and the exchanges inside), max
-    over ranks.  exchange 'nccl' (all_to_all_single) or 'peer' (mailboxes
-    in peer memory, csrc/p2p.cu)."""
-    import torch
-    from gpu.ep import ExpertParallelMoE
-    from kernels.packed import LAYOUTS
-    group = ranks.nccl_group()
-    per = EXPERTS // ranks.world
-    sl = slice(ranks.rank * per * EXPERT_MATRIX_BYTES, (ranks.rank + 1) * per * EXPERT_MATRIX_BYTES)
-    moe = ExpertParallelMoE(layer['router'], layer['bias'], KIND, layer['gate'][sl], layer['up'][sl],
-                            layer['down'][sl], EXPERTS, HIDDEN, INTER, TOPK, SCALE, shared=layer['shared'],
-                            group=group, exchange=exchange, max_tokens=TOKENS)
-    x = np.random.default_rng(300 + ranks.rank).normal(size=(TOKENS, HIDDEN)).astype(np.float32)
-    xd = torch.from_numpy(x).cuda()
-    from gpu.ep import ep_step
+def expert_parallel_step(args, ranks, backend, layer, moe, x, clocks):
+    """N>1 headline: the config-2 layer with its 256 experts sharded over the
+    N GPUs (gpu/ep.py, csrc/ep.cu: 256/N experts per GPU, router and shared
+    expert replicated), TOKENS rows per GPU per step.  Each rank captures K
+    steps in one CUDA graph; the ranks' graphs run together (the steps pace
+    each other through the mailbox flags); device time per rank from CUDA
+    events on the launching stream, max over ranks.  Also: the per-rank
+    output against the full single-GPU layer (bit-identical expected), the
+    end-to-end rate through ExpertParallelLayer.forward_pinned, per-phase
+    times of one un-graphed step, and the bytes that cross NVLink."""
+    from gpu import runtime as rt
+    from gpu.ep import ExpertParallelLayer, split_layer
+    N, r = ranks.world, ranks.rank
+    stream = backend.stream
+    g, u, d = split_layer(layer, N, r)
+    ep = ExpertParallelLayer(backend, r, N, layer['router'], layer['bias'], KIND, g, u, d, EXPERTS, HIDDEN, INTER,
+                             TOPK, SCALE, shared=layer['shared'], max_tokens=TOKENS)
 
-    def step():
-        ids, wts = moe.route(xd)
-        return ep_step(xd, ids, wts, moe.per_rank, moe.exchange, moe.ops)
+    def allgather(data):
+        out = [None] * N
+        ranks.dist.all_gather_object(out, data)
+        return out
 
+    ep.connect_ipc(allgather)
+    xd, yd, idd = rt.DeviceBuffer(x.nbytes), rt.DeviceBuffer(x.nbytes), rt.DeviceBuffer(4 * TOKENS * TOPK)
+    xd.upload(x, stream.handle)
+    stream.synchronize()
+    ranks.barrier()
     for _ in range(args.warmup):
-        step()
-    torch.cuda.synchronize()
-    steps = max(5, min(args.steps, 50))
+        ep.forward_device(yd.ptr, xd.ptr, TOKENS)
+    stream.synchronize()
+    backend.device.check_device_error()
+    ms = ranks.max(graph_time(rt, stream, lambda i: ep.forward_device(yd.ptr, xd.ptr, TOKENS), args.steps, ranks,
+                              clocks))
+    backend.device.check_device_error()
+    value = N * TOKENS * args.steps / (ms * 1e-3)
+
+    # parity: this rank's rows through the expert-parallel step and through
+    # the full single-GPU layer (same kernels per token: bytes must agree)
+    io = ep.pinned_io(TOKENS)
+    np.copyto(io['x'], x)
+    y_ep, ids_ep, _ = (a.copy() for a in ep.forward_pinned(TOKENS))
+    y_1, ids_1, _ = moe.forward(x)
+    rel = float(np.linalg.norm(y_ep - y_1) / np.linalg.norm(y_1))
+    mism = float(ids_ep.tolist() != ids_1.tolist()) + float(y_ep.tobytes() != y_1.tobytes())
+    worst_rel, worst_mism = ranks.max(rel), ranks.max(mism)
+
+    # end to end through the public API: pinned rows in, pinned outputs out
+    e2e_steps = min(max(args.steps, 50), 200)
+    for _ in range(3):
+        ep.forward_pinned(TOKENS)
     ranks.barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(steps):
-        step()
-    e1.record()
-    torch.cuda.synchronize()
-    ms = ranks.max(e0.elapsed_time(e1))
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        ep.forward_pinned(TOKENS)
+    e2e_s = ranks.max(time.perf_counter() - t0)
+    h2d, d2h = ep.step_copy_bytes(TOKENS)
+
+    # phases of one un-graphed step (events between them; the wait for the
+    # slowest peer lands in the phase that waits)
+    ev = [rt.Event() for _ in range(4)]
+    sums = np.zeros(3)
+    reps = 10
     ranks.barrier()
-    moe.close()
+    for _ in range(reps):
+        ev[0].record(stream)
+        ep.dispatch(xd.ptr, TOKENS, idd.ptr)
+        ev[1].record(stream)
+        ep.run_experts(TOKENS)
+        ev[2].record(stream)
+        ep.combine(yd.ptr, TOKENS)
+        ev[3].record(stream)
+        ev[3].synchronize()
+        sums += [ev[i].elapsed_ms(ev[i + 1]) for i in range(3)]
+    backend.device.check_device_error()
+    phases = dict(zip(('route_and_dispatch', 'experts_and_return', 'wait_and_combine'), (sums / reps * 1e3).tolist()))
+
+    # bytes per step: this rank's pairs to other ranks (prepared rows out,
+    # f32 rows back), and the owner's expert weights (distinct local experts
+    # routed by all ranks + the shared expert) read from HBM
+    ids = np.empty(TOKENS * TOPK, np.int32)
+    idd.download(ids)
+    per = EXPERTS // N
+    remote = int(np.sum(ids // per != r))
+    xstride = ((4 * HIDDEN + 4 * (HIDDEN // 256) + 15) // 16 * 16 + 4 * (HIDDEN // 32) + 255) // 256 * 256
+    nvlink = remote * (xstride + 4 * HIDDEN)
+    all_ids = allgather(ids.tobytes())
+    routed = np.concatenate([np.frombuffer(b, np.int32) for b in all_ids])
+    local = len(np.unique(routed[routed // per == r]))
+    weight_bytes = (local + 1) * 3 * EXPERT_MATRIX_BYTES + EXPERTS * HIDDEN * 4
+    step_s = ms * 1e-3 / args.steps
+    res = {'tok_s': value, 'ms_per_step': ms / args.steps, 'steps': args.steps, 'experts_per_gpu': per,
+           'tokens_per_gpu': TOKENS,
+           'parity': {'max_rel_err_vs_single_gpu_layer': worst_rel, 'ranks_not_bit_identical': worst_mism,
+                      'reference': 'gpu.moe.MoELayer (full 256-expert layer on the same rows; pinned to the oracle '
+                                   'by tests/test_gpu_moe.py)'},
+           'e2e': {'value': N * TOKENS * e2e_steps / e2e_s, 'unit': 'tok/s', 'steps': e2e_steps,
+                   'h2d_bytes_per_step': h2d, 'd2h_bytes_per_step': d2h,
+                   'api': 'gpu.ep.ExpertParallelLayer.forward_pinned (pinned rows in, pinned outputs + routing out)'},
+           'phase_us_rank0_view': phases,
+           'nvlink_bytes_per_step_per_gpu': {'out': nvlink - remote * 4 * HIDDEN, 'back': remote * 4 * HIDDEN},
+           'owner_distinct_experts': local,
+           'hbm_bytes_per_step_per_gpu': weight_bytes,
+           'hbm_gbs_per_gpu': weight_bytes / step_s / 1e9,
+           'transport': 'own kernels over peer memory: prepared rows stored into the owners\' IPC-mapped mailboxes, '
+                        'down-GEMV outputs stored straight back into the senders\' mailboxes, epoch flags with '
+                        'system-scope release/acquire (bounded 2 s waits); no NCCL, no host round trip'}
     ranks.barrier()
-    del moe
-    return {'tok_s': ranks.world * TOKENS * steps / (ms * 1e-3), 'ms_per_step': ms / steps, 'steps': steps,
-            'experts_per_gpu': per, 'tokens_per_rank': TOKENS,
-            'exchange': ('NCCL all_to_all_single: pair counts, token rows + expert ids out, pair outputs back'
-                         if exchange == 'nccl' else
-                         'peer-memory mailboxes over NVLink (CUDA IPC): count matrix, token rows + expert ids out, '
-                         'pair outputs back; scatter / release-flag / bounded-wait kernels, no collective library')}
+    for b in (xd, yd, idd):
+        b.close()
+    ep.close(barrier=ranks.barrier)
+    return res
 
 
 def run_ours(args, ranks):
@@ -638,32 +702,51 @@ def run_ours(args, ranks):
 
     gemv = fused_gemv_sweep(rt, lib, dev, stream, args.steps, peak)
     dsa = dsa_sweep(rt, lib, backend, stream, args.steps, peak) if ranks.world == 1 else None
-    ep_ok = ranks.world > 1 and EXPERTS % ranks.world == 0
-    ep = expert_parallel_step(args, ranks, layer) if ep_ok else None
-    ep_peer = expert_parallel_step(args, ranks, layer, 'peer') if ep_ok and ranks.world <= 8 else None
+    ep = (expert_parallel_step(args, ranks, backend, layer, moe, xs[TOKENS], clocks)
+          if ranks.world > 1 and EXPERTS % ranks.world == 0 else None)
+    single = {'tok_s': value, 'ms_per_step': total_ms / args.steps,
+              'e2e': {'value': e2e_value, 'unit': 'tok/s', 'steps': e2e_steps, 'h2d_bytes_per_step': e2e_h2d,
+                      'd2h_bytes_per_step': e2e_d2h,
+                      'api': 'gpu.moe.MoELayer.forward_pinned (pinned host rows in, pinned host rows + routing out)'}}
+    roofline = {'bound': 'hbm', 'achieved': achieved, 'peak': peak, 'unit': 'GB/s', 'frac': achieved / peak,
+                'traffic': traffic[0], 'traffic_source': traffic[1],
+                'kernel': 'mma_rows_kernel<IQ1_S> gate+up job lists of the single-GPU layer (tensor-core int8; '
+                          'two- and four-token jobs, two launches)',
+                'algorithmic_bytes_per_launch': gu_bytes, 'avg_launch_us': gu_us, 'peak_source': peak_kind}
+    config = {**workload_config(), 'global_batch': TOKENS * ranks.world,
+              'l2_policy': 'inputs larger than L2: every step streams its experts from HBM (1.2 GB per GPU at N=1)',
+              'per_tokens': per_tokens}
+    if ep:
+        # N > 1: the expert-parallel step is the headline; replicas beside it
+        config['parallelism'] = f'expert x{ranks.world} ({EXPERTS // ranks.world} experts per GPU, router and ' \
+                                'shared expert replicated)'
+        headline = {'value': ep['tok_s'], 'ms_per_step': ep['ms_per_step'], 'e2e': ep['e2e'],
+                    # prep x, router logits, top-k, dispatch, grouping, gate+up (two lists), prep h, down (two
+                    # lists), return signal, combine
+                    'gpu_launches': 12 * args.steps}
+        ep_roof = {'bound': 'hbm', 'achieved': ep['hbm_gbs_per_gpu'], 'peak': peak, 'unit': 'GB/s',
+                   'frac': ep['hbm_gbs_per_gpu'] / peak, 'traffic': None,
+                   'traffic_source': 'no ncu capture of a multi-rank step (ncu runs on one GPU only)',
+                   'kernel': 'whole expert-parallel step per GPU: owner expert weights (distinct local experts + '
+                             'shared) + router over the step time',
+                   'algorithmic_bytes_per_step': ep['hbm_bytes_per_step_per_gpu'], 'peak_source': peak_kind}
+        extra = {'expert_parallel': ep, 'replicas': single, 'single_gpu_roofline': roofline}
+        roofline = ep_roof
+    else:
+        config['parallelism'] = 'single GPU'
+        headline = {'value': value, 'ms_per_step': total_ms / args.steps, 'e2e': single['e2e'],
+                    # prep x, router logits, top-k, grouping, gate+up (two lists), prep h, down (two lists), combine
+                    'gpu_launches': 10 * args.steps}
+        extra = {}
     line = {
-        'metric': METRIC, 'value': value, 'unit': 'tok/s', 'n_gpus': ranks.world, 'steps': args.steps,
-        'warmup': args.warmup, 'ms_per_step': total_ms / args.steps, 'higher_is_better': True, 'scaling': 'weak',
-        'vs_baseline': None, 'dtype': 'f32', 'data': 'synthetic',
-        'config': {'workload': 'config2_iq1_s_moe_decode_layer', 'experts': EXPERTS, 'shared_experts': 1,
-                   'hidden': HIDDEN, 'moe_intermediate': INTER, 'top_k': TOPK, 'routed_scale': SCALE,
-                   'format': 'IQ1_S', 'tokens_per_step': TOKENS, 'global_batch': TOKENS * ranks.world,
-                   'parallelism': f'replicas x{ranks.world}',
-                   'l2_policy': 'inputs larger than L2: the layer streams 1.9 GB of resident experts',
-                   'per_tokens': per_tokens},
-        'roofline': {'bound': 'hbm', 'achieved': achieved, 'peak': peak, 'unit': 'GB/s', 'frac': achieved / peak,
-                     'traffic': traffic[0], 'traffic_source': traffic[1], 'kernel': 'mma_rows_kernel<IQ1_S> gate+up job lists (tensor-core int8; two- and four-token jobs, two launches)',
-                     'algorithmic_bytes_per_launch': gu_bytes, 'avg_launch_us': gu_us, 'peak_source': peak_kind},
+        'metric': METRIC, 'value': headline['value'], 'unit': 'tok/s', 'n_gpus': ranks.world, 'steps': args.steps,
+        'warmup': args.warmup, 'ms_per_step': headline['ms_per_step'], 'higher_is_better': True, 'scaling': 'weak',
+        'vs_baseline': None, 'dtype': 'f32', 'data': 'synthetic', 'config': config, 'roofline': roofline,
         'fused_gemv': gemv,
         **({'dsa_decode': dsa} if dsa else {}),
-        **({'expert_parallel': ep} if ep else {}),
-        **({'expert_parallel_peer': ep_peer} if ep_peer else {}),
-        'e2e': {'value': e2e_value, 'unit': 'tok/s', 'steps': e2e_steps,
-                'h2d_bytes_per_step': e2e_h2d, 'd2h_bytes_per_step': e2e_d2h,
-                'api': 'gpu.moe.MoELayer.forward_pinned (pinned host rows in, pinned host rows + routing out)'},
-        # prep x, router logits, top-k, grouping, gate+up (two-token and four-token job lists), prep h,
-        # down (both lists), combine
-        'gpu_launches': 10 * args.steps,
+        **extra,
+        'e2e': headline['e2e'],
+        'gpu_launches': headline['gpu_launches'],
         'clocks': clocks.summary(),
     }
     if ranks.rank == 0 and ranks.world == 1 and not args.no_cpu_baseline:

@@ -47,8 +47,11 @@ bool mma_supported(int kind, int cols);
 bool mma_quad_supported(int kind, int cols);
 
 // Prepare `rows` activation rows x[r][0..cols) (x2 set: SwiGLU(x, x2) =
-// x*sigmoid(x)*x2 per element) into prep + r*prep_stride(cols).
-int32_t prep_rows_device(uint8_t *prep, const float *x, const float *x2, int rows, int cols, cudaStream_t stream);
+// x*sigmoid(x)*x2 per element) into prep + r*prep_stride(cols).  With
+// rows_dev set, only the first min(*rows_dev, rows) rows (a count written on
+// the device by an earlier kernel; `rows` is then the capacity).
+int32_t prep_rows_device(uint8_t *prep, const float *x, const float *x2, int rows, int cols, cudaStream_t stream,
+                         const int *rows_dev = nullptr);
 
 // Tensor-core packed GEMV over a job list.
 //  * jobs != nullptr: device-resident descriptors; the job count is

@@ -417,9 +417,10 @@ __device__ __forceinline__ void prep_chunk(uint8_t *out, const float *x, const f
 // One warp per (row, 256-column chunk).
 __global__ void __launch_bounds__(256)
     prep_rows_kernel(uint8_t *__restrict__ prep, const float *__restrict__ x, const float *__restrict__ x2, int rows,
-                     int cols) {
+                     int cols, const int *rows_dev) {
     grid_dependency_wait();
     allow_dependent_launch();
+    if (rows_dev) rows = min(max(*rows_dev, 0), rows);
     const int chunks = cols >> 8;
     const int64_t wid = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
@@ -852,7 +853,8 @@ bool mma_supported(int kind, int cols) {
     return kind == 8 || kind == 12 || (kind == 19 && cols % 2048 == 0);
 }
 
-int32_t prep_rows_device(uint8_t *prep, const float *x, const float *x2, int rows, int cols, cudaStream_t stream) {
+int32_t prep_rows_device(uint8_t *prep, const float *x, const float *x2, int rows, int cols, cudaStream_t stream,
+                         const int *rows_dev) {
     if (rows <= 0) return kOk;
     if (cols % 256 || (reinterpret_cast<uintptr_t>(prep) & 15) || (reinterpret_cast<uintptr_t>(x) & 15) ||
         (reinterpret_cast<uintptr_t>(x2) & 15)) {
@@ -869,7 +871,7 @@ int32_t prep_rows_device(uint8_t *prep, const float *x, const float *x2, int row
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    GLMVX_CUDA(cudaLaunchKernelEx(&cfg, prep_rows_kernel, prep, x, x2, rows, cols));
+    GLMVX_CUDA(cudaLaunchKernelEx(&cfg, prep_rows_kernel, prep, x, x2, rows, cols, rows_dev));
     return kOk;
 }
 

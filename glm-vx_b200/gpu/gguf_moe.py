@@ -100,11 +100,12 @@ def expert_slice(array, experts_total, first, count):
     return array[first * per:(first + count) * per]
 
 
-def expert_parallel_layer(source, layer, rank, world, *, top_k=None, scale=None, group=None):
-    """ExpertParallelMoE (gpu/ep.py) holding this rank's experts
-    [rank*E/world, (rank+1)*E/world) of GGUF block `layer`; router, bias and
-    shared expert replicated.  torch.cuda's device must already be selected."""
-    from .ep import ExpertParallelMoE, experts_per_rank
+def expert_parallel_layer(source, layer, rank, world, backend, *, top_k=None, scale=None, max_tokens=32):
+    """ExpertParallelLayer (gpu/ep.py) holding this rank's experts
+    [rank*E/world, (rank+1)*E/world) of GGUF block `layer` on `backend`'s
+    device; router, bias and shared expert replicated.  Connect it to the
+    other ranks (connect_ipc) before its first step."""
+    from .ep import ExpertParallelLayer, experts_per_rank
     reader = open_reader(source)
     t = layer_tensors(reader, layer)
     kind, E, hidden, inter = _check(t)
@@ -113,5 +114,5 @@ def expert_parallel_layer(source, layer, rank, world, *, top_k=None, scale=None,
     scale = float(scale if scale is not None else _field(reader, 'glm-dsa.expert_weights_scale'))
     part = {p: expert_slice(t[p][0], E, rank * per, per) for p in ('gate', 'up', 'down')}
     shared = tuple(t[p][0] for p in ('shared_gate', 'shared_up', 'shared_down')) if 'shared_gate' in t else None
-    return ExpertParallelMoE(t['router'][0], t['bias'][0], kind, part['gate'], part['up'], part['down'], E, hidden,
-                             inter, top_k, scale, shared=shared, group=group)
+    return ExpertParallelLayer(backend, rank, world, t['router'][0], t['bias'][0], kind, part['gate'], part['up'],
+                               part['down'], E, hidden, inter, top_k, scale, shared=shared, max_tokens=max_tokens)

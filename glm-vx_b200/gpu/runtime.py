@@ -90,9 +90,6 @@ SIGNATURES = {
     'glmvx_ipc_handle': ([_P, _P], _I32),
     'glmvx_ipc_open': ([_P, C.POINTER(C.c_void_p)], _I32),
     'glmvx_ipc_close': ([_P], _I32),
-    'glmvx_p2p_scatter': ([_P, _I64, _P, _P, _P, _I32, _P], _I32),
-    'glmvx_p2p_signal': ([_P, _I32, C.c_uint32, _P], _I32),
-    'glmvx_p2p_wait': ([_P, _I32, C.c_uint32, _P], _I32),
     'glmvx_gemm': ([_P, _P, _P, _I32, _I32, _I32, _I32, _P, _P], _I32),
     'glmvx_dsa_append': ([_P, _P, _P, _P, _P, _P, _P, _I32, _I32, _I32, _I32, _I32, _P, _P], _I32),
     'glmvx_moe_workspace_bytes': ([_I32, _I32, _I32, _I32, _I32, _I32], _I64),
@@ -105,6 +102,15 @@ SIGNATURES = {
     'glmvx_moe_combine': ([_P, _P, _P, _P, _P, _I32, _I32, _I32, _P], _I32),
     'glmvx_gather_rows': ([_P, _P, _P, _I32, _I32, _P], _I32),
     'glmvx_mem_get_info': ([C.POINTER(_U64), C.POINTER(_U64)], _I32),
+    'glmvx_ep_create': ([C.POINTER(_P), _I32, _I32, _I32, _I32, _I32, _I32, _I32, _F32, _I32, _P, _P, _P, _P, _P,
+                         _P, _P, _P], _I32),
+    'glmvx_ep_mailbox': ([_P, C.POINTER(_P), C.POINTER(_U64)], _I32),
+    'glmvx_ep_connect': ([_P, _P], _I32),
+    'glmvx_ep_dispatch': ([_P, _P, _I32, _P, _P, _P], _I32),
+    'glmvx_ep_experts': ([_P, _I32, _P], _I32),
+    'glmvx_ep_combine': ([_P, _P, _I32, _P], _I32),
+    'glmvx_ep_step': ([_P, _P, _P, _I32, _P, _P, _P], _I32),
+    'glmvx_ep_destroy': ([_P], _I32),
     'glmvx_moe_job_counts': ([_I32, _I32, _I32, _I32, _I32, _I32, _P, _PI32, _P], _I32),
 }
 

@@ -281,28 +281,53 @@ int32_t glmvx_moe_experts(float *y, const float *x, const int32_t *expert_ids, i
 int32_t glmvx_moe_combine(float *y, const float *pair_out, const int32_t *comb, const float *combw,
                           const float *shared_rows, int32_t tokens, int32_t top_k, int32_t hidden, void *stream);
 int32_t glmvx_gather_rows(float *out, const float *x, const int32_t *idx, int32_t n, int32_t cols, void *stream);
-/* Peer-memory exchange between the GPUs of one node, the transport of the
- * expert-parallel step without a collective library (replaces the
- * all_to_all_single exchanges of glm-vx_b200/gpu/ep.py; the reference runs
- * all experts in one process, glm_vx/model.py:289-324).  glmvx_ipc_handle /
- * glmvx_ipc_open / glmvx_ipc_close: 64-byte CUDA IPC handles of cudaMalloc'd
- * mailboxes and their mapping in a peer process.  glmvx_p2p_scatter: rows of
- * src grouped by destination (counts[d] rows for rank d, rank order) stored
- * from row dst_rows[d] (NULL: 0) of dst[d] -- own or mapped peer memory;
- * row_bytes a multiple of 16, pointers 16-byte aligned, world <= 8.
- * glmvx_p2p_signal: once this stream's earlier stores are visible
- * system-wide, stores `epoch` (release, system scope) at flag_slots[d] (this
- * rank's flag in rank d's mailbox).  glmvx_p2p_wait: waits on the device
- * (acquire, system scope) until flags[s] reached epoch for every s < world;
- * after 2 s it sets the device error word instead.  dst, counts, dst_rows
- * and flag_slots are host arrays of `world` entries. */
+/* CUDA IPC mapping of cudaMalloc'd allocations between the rank processes of
+ * one node (the expert-parallel mailboxes below): glmvx_ipc_handle writes the
+ * 64-byte handle of a base pointer, glmvx_ipc_open maps a peer's handle
+ * (peer access enabled on first use), glmvx_ipc_close unmaps it.  The
+ * reference's runtime has no multi-process mapping (gpu/runtime.py). */
 int32_t glmvx_ipc_handle(void *base, uint8_t *handle64);
 int32_t glmvx_ipc_open(const uint8_t *handle64, void **ptr);
 int32_t glmvx_ipc_close(void *ptr);
-int32_t glmvx_p2p_scatter(const void *src, int64_t row_bytes, void *const *dst, const int64_t *counts,
-                          const int64_t *dst_rows, int32_t world, void *stream);
-int32_t glmvx_p2p_signal(void *const *flag_slots, int32_t world, uint32_t epoch, void *stream);
-int32_t glmvx_p2p_wait(const uint32_t *flags, int32_t world, uint32_t epoch, void *stream);
+/* Expert-parallel sparse layer, one rank per GPU of a node (replaces the
+ * NCCL all-to-all dispatch/combine the survey proposed as glmvx_ep_init /
+ * dispatch / combine; the reference runs all experts in one process,
+ * glm_vx/model.py:289-324).  Routed expert e lives on rank
+ * e / (experts / world); router and shared expert are replicated.  Each rank
+ * owns a mailbox that the other ranks store into over NVLink: prepared token
+ * rows go to the expert's owner, whose down GEMV stores each output row
+ * straight back into the sender's mailbox; epoch flags (system-scope
+ * release / acquire, waits bounded to 2 s, then the device error word) order
+ * the steps.  No host round trip inside a step; a step is capturable.
+ *   glmvx_ep_create   this rank's layer: `gate`/`up`/`down` hold its own
+ *                     experts/world experts, router / bias / shared expert
+ *                     the full arrays (device pointers, 16-byte aligned,
+ *                     kept by the caller); allocates the mailbox + scratch.
+ *                     world <= 8, world * max_tokens * top_k <= 4096,
+ *                     formats and widths of the tensor-core path.
+ *   glmvx_ep_mailbox  this rank's mailbox (cudaMalloc'd: share it with
+ *                     glmvx_ipc_handle) and its size.
+ *   glmvx_ep_connect  every rank's mailbox in rank order as this process
+ *                     addresses it (own included).
+ *   glmvx_ep_dispatch / _experts / _combine  the three phases of a step
+ *                     (route + store rows to owners; owner's experts +
+ *                     return; wait + ordered combine); glmvx_ep_step = all
+ *                     three.  Every rank runs every step (tokens may be 0).
+ *   glmvx_ep_destroy  after every rank's last step and after the peers
+ *                     unmapped this mailbox. */
+int32_t glmvx_ep_create(void **layer, int32_t rank, int32_t world, int32_t max_tokens, int32_t hidden, int32_t inter,
+                        int32_t experts, int32_t top_k, float scale, int32_t kind, const float *router_w,
+                        const float *router_bias, const uint8_t *gate, const uint8_t *up, const uint8_t *down,
+                        const uint8_t *shared_gate, const uint8_t *shared_up, const uint8_t *shared_down);
+int32_t glmvx_ep_mailbox(void *layer, void **base, uint64_t *bytes);
+int32_t glmvx_ep_connect(void *layer, void *const *mailboxes);
+int32_t glmvx_ep_dispatch(void *layer, const float *x, int32_t tokens, int32_t *ids_out, float *weights_out,
+                          void *stream);
+int32_t glmvx_ep_experts(void *layer, int32_t tokens, void *stream);
+int32_t glmvx_ep_combine(void *layer, float *y, int32_t tokens, void *stream);
+int32_t glmvx_ep_step(void *layer, float *y, const float *x, int32_t tokens, int32_t *ids_out, float *weights_out,
+                      void *stream);
+int32_t glmvx_ep_destroy(void *layer);
 /* FP8 E4M3FN block-scaled projection, device pointers: out[rows] =
  * sum_c (decode(weight[r,c]) * scales[r/128, c/128]) * x[c], weight u8
  * [rows, cols], scales f32 [ceil(rows/128), ceil(cols/128)].  Replaces the

@@ -1,7 +1,8 @@
-"""Expert-parallel MoE protocol (gpu/ep.py) on CPU: dispatch/combine planning,
-and a full layer step over a 2-rank gloo group with the CPU oracle as the
-expert compute, which must reproduce the single-process reference layer
-(glm_vx/model.py:289-324) bit for bit."""
+"""Expert-parallel MoE protocol on CPU (tests/ep_model.py, the host model of
+the device protocol in csrc/ep.cu): dispatch/combine planning, the device
+mailbox plan, and a full layer step over 2- and 4-rank gloo groups with the
+CPU oracle as the expert compute, which must reproduce the single-process
+reference layer (glm_vx/model.py:289-324) bit for bit."""
 import os
 import socket
 
@@ -12,7 +13,7 @@ from kernels.packed import LAYOUTS
 
 
 def test_dispatch_plan_groups_pairs_by_owner():
-    from gpu.ep import dispatch_plan
+    from ep_model import dispatch_plan
     ids = np.array([[5, 0, 7], [2, 6, 1]], np.int32)  # 8 experts over 2 ranks: 0-3 on rank 0
     order, counts = dispatch_plan(ids, 4, 2)
     assert counts.tolist() == [3, 3]
@@ -22,7 +23,7 @@ def test_dispatch_plan_groups_pairs_by_owner():
 
 
 def test_combine_plan_is_ascending_expert_order():
-    from gpu.ep import combine_plan, dispatch_plan
+    from ep_model import combine_plan, dispatch_plan
     ids = np.array([[5, 0, 7], [2, 6, 1]], np.int32)
     wts = np.array([[0.5, 0.25, 0.125], [1.0, 2.0, 3.0]], np.float32)
     order, _ = dispatch_plan(ids, 4, 2)
@@ -33,7 +34,7 @@ def test_combine_plan_is_ascending_expert_order():
         assert experts.tolist() == sorted(ids[t].tolist())
         assert combw[t].tolist() == [float(wts[t][list(ids[t]).index(e)]) for e in experts]
     with pytest.raises(ValueError, match='evenly'):
-        from gpu.ep import experts_per_rank
+        from ep_model import experts_per_rank
         experts_per_rank(10, 4)
 
 
@@ -100,7 +101,7 @@ def _rank_main(rank, world, port, out_dir):
     try:
         from oracle import loader
         from kernels.backend import VxBackend
-        from gpu.ep import Exchange, ep_step
+        from ep_model import Exchange, ep_step
         cpu = VxBackend(str(loader.serial()))
         layer, x = _layer(), _tokens(rank)
         ids, wts = [], []
@@ -135,27 +136,25 @@ def test_ep_step_over_gloo_matches_reference(tmp_path, oracle, world):
         assert got['y'].tobytes() == want.tobytes()
 
 
-def test_peer_layout_reproduces_all_to_all_order():
-    """Rows placed at peer_layout's offsets (the peer-memory exchange) land in
-    each receiver exactly as all_to_all_single concatenates them, forward and
-    back, for random count matrices."""
-    from gpu.ep import peer_layout
-    rng = np.random.default_rng(5)
-    for world in (1, 2, 3, 8):
-        M = rng.integers(0, 6, size=(world, world))
-        for direction in ('forward', 'back'):
-            S = M if direction == 'forward' else M.T
-            sends = {s: [(s, d, i) for d in range(world) for i in range(S[s, d])] for s in range(world)}
-            mail = {d: [None] * int(S[:, d].sum()) for d in range(world)}
-            for s in range(world):
-                _, dst_rows, _ = peer_layout(M, S[s], s)
-                k = 0
-                for d in range(world):
-                    for i in range(S[s, d]):
-                        assert mail[d][dst_rows[d] + i] is None
-                        mail[d][dst_rows[d] + i] = sends[s][k]
-                        k += 1
-            for d in range(world):
-                want = [row for s in range(world) for row in sends[s] if row[1] == d]  # sender order
-                assert mail[d] == want
-                assert peer_layout(M, S[d], d)[2] == len(want)
+def test_mailbox_plan_matches_host_plan():
+    """The device dispatch (ep_dispatch_kernel) places pair a of destination d
+    at position pos[a] of d's region for this sender, in (token, slot) order,
+    and the combine reads owner * cap + pos in ascending expert id: the same
+    pairs, order and combine sequence as the host plan (all_to_all order)."""
+    from ep_model import combine_plan, dispatch_plan, mailbox_plan
+    rng = np.random.default_rng(9)
+    for world, experts, k, T in ((1, 8, 2, 3), (2, 16, 4, 5), (4, 256, 8, 32), (8, 256, 8, 32)):
+        per = experts // world
+        ids = np.stack([rng.choice(experts, size=k, replace=False) for _ in range(T)]).astype(np.int32)
+        wts = rng.random((T, k)).astype(np.float32)
+        cap = T * k
+        dest, pos, counts, rows = mailbox_plan(ids, per, world, cap)
+        order, host_counts = dispatch_plan(ids, per, world)
+        assert counts.tolist() == host_counts.tolist()
+        starts = np.concatenate([[0], np.cumsum(host_counts)[:-1]])
+        # position in the all_to_all send order = start of the destination + position in it
+        assert (starts[dest] + pos)[order].tolist() == list(range(T * k))
+        comb, _ = combine_plan(ids, wts, order)
+        # the same pair behind every combine slot
+        flat_of_row = {int(dest[a] * cap + pos[a]): a for a in range(T * k)}
+        assert [[flat_of_row[int(r)] for r in row] for row in rows] == order[comb].tolist()
