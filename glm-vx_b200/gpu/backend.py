@@ -27,7 +27,7 @@ import hashlib
 import numpy as np
 
 from . import runtime as rt
-from kernels.backend import _cached_rope_coefficients, _make_rope_coefficients
+from kernels.backend import _rope_table, _rope_table_cached
 from kernels.packed import LAYOUTS, _buffers, batch_input
 
 _MAX = 2**31 - 1
@@ -349,7 +349,7 @@ class GPUBackend:
         d = x.shape[-1]
         if not d or d % 2 or not np.isfinite(position) or not np.isfinite(theta) or theta <= 0:
             raise ValueError('invalid RoPE parameters')
-        coefficients = _cached_rope_coefficients if d <= 4096 else _make_rope_coefficients
+        coefficients = _rope_table_cached if d <= 4096 else _rope_table
         cosine, sine = coefficients(d, float(position), float(theta))
         return self._unary_rows('glmvx_rope_glm', x, [cosine, sine], lambda a: (a.size // d, d))
 

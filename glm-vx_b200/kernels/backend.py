@@ -1,16 +1,20 @@
-"""Model-facing backend over the reference's C ABI, executed on the B200.
+"""VxBackend: the reference's model-facing kernel interface, executed by the
+B200 library through the reference C ABI (host pointers).
 
-Mirrors the reference class kernels/backend.py:48-237 (VxBackend) of
-gakonst/glm-vx: same methods, argument checks and ValueError wording, so
-glm_vx/model.py, glm_vx/prefill.py and glm_vx/gguf_checkpoint.py can use it
-unchanged.  The difference is the library behind it: by default this loads
-libglmvx_cuda.so, whose glm_vx_* exports stage host buffers onto the GPU and
-run the sm_100a kernels.  GLM_VX_LIBRARY (or `library=`) selects another
-library exporting the same ABI.  There is no numerical fallback: a missing
-library raises RuntimeError.
+Interface kept from the reference class (kernels/backend.py:48-237 of
+gakonst/glm-vx): the method names and arguments glm_vx/model.py,
+glm_vx/prefill.py and glm_vx/gguf_checkpoint.py call, the ValueError texts
+their tests match, the RuntimeError when the library is missing (no
+numerical fallback), and the library choice -- `library=`, else
+$GLM_VX_LIBRARY, else libglmvx_cuda.so next to this package.  Each call
+stages its operands on the GPU inside the library (abi_host.cu) and copies
+the result back; for weights that should stay in HBM across calls use
+gpu.backend.GPUBackend.
 
-For weights that should stay resident in HBM across calls use
-gpu.backend.GPUBackend instead; this class uploads its operands per call.
+Structure: `_Abi` loads the library and binds every entry point this class
+uses from a signature table spelled after include/glmvx.h; the `_need_*`
+checks hold the argument rules; ops over the final axis of N-D inputs
+(rmsnorm, layernorm, softmax) go through one row driver.
 """
 import ctypes as C
 import os
@@ -19,221 +23,249 @@ from pathlib import Path
 
 import numpy as np
 
-_F = C.POINTER(C.c_float)
-_I = C.POINTER(C.c_int32)
-_S = C.c_int32
-_R = C.c_float
-_MAX = np.iinfo(np.int32).max
 DEFAULT_LIBRARY = Path(__file__).resolve().parents[1] / 'libglmvx_cuda.so'
+INT32_LIMIT = np.iinfo(np.int32).max
+
+# Entry points (prefix glm_vx_) and their C parameters, one letter each:
+# f = float*, i = int32*, n = int32 count, s = float scalar.
+_ABI_TABLE = {
+    'matvec': 'fffnn',          # out, w, x, rows, cols
+    'matmul_nt': 'fffnnn',      # out, x, w, batch, rows, cols
+    'rmsnorm': 'fffns',         # out, x, w, n, eps
+    'layernorm': 'ffffns',      # out, x, w, bias, n, eps
+    'softmax': 'ffn',           # out, x, n
+    'swiglu': 'fffn',           # out, gate, up, n
+    'rope_glm': 'ffffnn',       # out, x, cos, sin, rows, d
+    'router': 'ifffnns',        # ids, weights, logits, bias, experts, k, scale
+    'topk': 'ifnn',             # ids, scores, n, k
+    'index_scores': 'ffffnnns',  # out, q, keys, w, tokens, heads, dim, scale
+}
+_CTYPES = {'f': C.POINTER(C.c_float), 'i': C.POINTER(C.c_int32), 'n': C.c_int32, 's': C.c_float}
 
 
-def _array(value, name):
-    out = np.asarray(value, dtype=np.float32)
-    if out.ndim == 0:
-        raise ValueError(f'{name} must have at least one dimension')
-    if out.size > _MAX or any(d > _MAX for d in out.shape):
-        raise ValueError(f'{name} exceeds Vx int32 indexing capacity')
-    return np.ascontiguousarray(out)
+class _Abi:
+    """The loaded library with its entry points bound; `run` converts
+    arrays to pointers and turns a nonzero status into ValueError."""
 
-
-def _pointer(value):
-    return value.ctypes.data_as(_I if value.dtype == np.int32 else _F)
-
-
-def _make_rope_coefficients(d, position, theta):
-    """cos/sin per rotated pair at `position`, in the model's f32 precision
-    (reference kernels/backend.py:32-39)."""
-    angles = position * np.power(theta, -np.arange(0, d, 2, dtype=np.float32) / d)
-    cosine = np.ascontiguousarray(np.cos(angles), dtype=np.float32)
-    sine = np.ascontiguousarray(np.sin(angles), dtype=np.float32)
-    cosine.flags.writeable = False
-    sine.flags.writeable = False
-    return cosine, sine
-
-
-@lru_cache(maxsize=128)
-def _cached_rope_coefficients(d, position, theta):
-    # Callers use the cache only for d <= 4096 (<= 2 MiB of payload overall).
-    return _make_rope_coefficients(d, position, theta)
-
-
-class VxBackend:
-    """f32 backend with explicit buffer/shape validation (reference contract)."""
-    name = 'vx-b200-f32'
-
-    _SIGNATURES = {
-        'layernorm': [_F, _F, _F, _F, _S, _R],
-        'topk': [_I, _F, _S, _S],
-        'index_scores': [_F, _F, _F, _F, _S, _S, _S, _R],
-        'matvec': [_F, _F, _F, _S, _S],
-        'matmul_nt': [_F, _F, _F, _S, _S, _S],
-        'rmsnorm': [_F, _F, _F, _S, _R],
-        'rope_glm': [_F, _F, _F, _F, _S, _S],
-        'softmax': [_F, _F, _S],
-        'swiglu': [_F, _F, _F, _S],
-        'router': [_I, _F, _F, _F, _S, _S, _R],
-    }
-
-    def __init__(self, library=None):
-        self.library_path = Path(library or os.environ.get('GLM_VX_LIBRARY') or DEFAULT_LIBRARY).resolve()
+    def __init__(self, path):
+        self.path = Path(path).resolve()
         try:
-            self.lib = C.CDLL(str(self.library_path))
+            self.lib = C.CDLL(str(self.path))
         except OSError as exc:
-            raise RuntimeError(f'Cannot load the kernel library at {self.library_path}; build it with '
+            raise RuntimeError(f'Cannot load the kernel library at {self.path}; build it with '
                                'python glm-vx_b200/build.py. No numerical fallback is enabled.') from exc
-        for op, args in self._SIGNATURES.items():
+        self.fns = {}
+        for op, spec in _ABI_TABLE.items():
             fn = getattr(self.lib, 'glm_vx_' + op)
-            fn.argtypes, fn.restype = args, _S
+            fn.argtypes, fn.restype = [_CTYPES[c] for c in spec], C.c_int32
+            self.fns[op] = fn
 
-    def _call(self, op, *args):
-        status = getattr(self.lib, 'glm_vx_' + op)(*[_pointer(a) if isinstance(a, np.ndarray) else a for a in args])
+    def run(self, op, *args):
+        spec = _ABI_TABLE[op]
+        conv = [a.ctypes.data_as(_CTYPES[c]) if c in 'fi' else a for c, a in zip(spec, args)]
+        status = self.fns[op](*conv)
         if status:
             raise ValueError(f'Vx {op} rejected arguments (status {status})')
 
+
+# ------------------------------------------------------------ argument rules
+def _need_f32(value, name):
+    """C-contiguous float32 copy/view with at least one axis, every extent
+    (and the size) addressable with int32."""
+    arr = np.ascontiguousarray(np.asarray(value, dtype=np.float32))
+    if arr.ndim == 0:
+        raise ValueError(f'{name} must have at least one dimension')
+    if arr.size > INT32_LIMIT or max(arr.shape) > INT32_LIMIT:
+        raise ValueError(f'{name} exceeds Vx int32 indexing capacity')
+    return arr
+
+
+def _need_eps(eps, op):
+    eps = float(eps)
+    if not (np.isfinite(eps) and eps > 0):
+        raise ValueError(f'{op} epsilon must be finite and positive')
+    return eps
+
+
+def _need_row_params(x, params, op, what):
+    """Per-row parameter vectors (weight, bias) matching the final axis."""
+    width = x.shape[-1]
+    if not width or any(p.ndim != 1 or p.size != width for p in params):
+        raise ValueError(f'{op} {what} must match the nonempty final input axis')
+    return width
+
+
+def _rows(abi, op, x, width, params=(), scalars=()):
+    """Apply a one-row entry point to every row along the final axis."""
+    out = np.empty_like(x)
+    src, dst = x.reshape(-1, width), out.reshape(-1, width)
+    for i in range(src.shape[0]):
+        abi.run(op, dst[i], src[i], *params, width, *scalars)
+    return out
+
+
+# ------------------------------------------------------------ RoPE tables
+def _rope_table(d, position, theta):
+    """cos/sin of the rotated pairs at `position`, read-only float32.  The
+    arithmetic is the reference model's own (kernels/backend.py:32-39):
+    float32 exponents arange(0, d, 2)/d, numpy power and cos/sin, so the
+    rotated values match it bit for bit."""
+    angles = position * np.power(theta, -np.arange(0, d, 2, dtype=np.float32) / d)
+    table = (np.ascontiguousarray(np.cos(angles), dtype=np.float32),
+             np.ascontiguousarray(np.sin(angles), dtype=np.float32))
+    for t in table:
+        t.flags.writeable = False
+    return table
+
+
+_rope_table_cached = lru_cache(maxsize=128)(_rope_table)  # used for d <= 4096: at most 2 MiB in total
+
+
+class VxBackend:
+    """float32 kernel backend with explicit shape and value validation."""
+    name = 'vx-b200-f32'
+
+    def __init__(self, library=None):
+        self._abi = _Abi(library or os.environ.get('GLM_VX_LIBRARY') or DEFAULT_LIBRARY)
+        self.library_path, self.lib = self._abi.path, self._abi.lib
+
+    # ---------------------------------------------------------- projections
     def matvec(self, w, x):
-        w, x = _array(w, 'weight'), _array(x, 'input')
-        if w.ndim != 2 or x.ndim != 1 or w.shape[1] != x.size:
+        w, x = _need_f32(w, 'weight'), _need_f32(x, 'input')
+        if not (w.ndim == 2 and x.ndim == 1 and w.shape[1] == x.size):
             raise ValueError('matvec expects weight[rows,cols] and input[cols]')
-        out = np.empty(w.shape[0], dtype=np.float32)
-        self._call('matvec', out, w, x, *w.shape)
+        out = np.empty(w.shape[0], np.float32)
+        self._abi.run('matvec', out, w, x, w.shape[0], w.shape[1])
         return out
 
     def linear_batch(self, w, x):
-        """X[batch,input] @ W[output,input]^T."""
-        w, x = _array(w, 'weight'), _array(x, 'input')
-        if w.ndim != 2 or x.ndim != 2 or w.shape[1] != x.shape[1]:
+        """x[batch, input] @ w[output, input]^T."""
+        w, x = _need_f32(w, 'weight'), _need_f32(x, 'input')
+        if not (w.ndim == 2 and x.ndim == 2 and w.shape[1] == x.shape[1]):
             raise ValueError('linear_batch expects weight[output,input] and input[batch,input]')
-        if w.shape[0] * x.shape[0] > _MAX:
+        if w.shape[0] * x.shape[0] > INT32_LIMIT:
             raise ValueError('linear_batch output exceeds Vx int32 indexing capacity')
-        out = np.empty((x.shape[0], w.shape[0]), dtype=np.float32)
-        self._call('matmul_nt', out, x, w, x.shape[0], w.shape[0], w.shape[1])
+        out = np.empty((x.shape[0], w.shape[0]), np.float32)
+        self._abi.run('matmul_nt', out, x, w, x.shape[0], w.shape[0], w.shape[1])
         return out
 
     def supports_packed(self, kind):
         from .packed import supports
         return supports(self.lib, kind)
 
-    def packed_matvec(self, raw, kind, shape, x):
-        """Borrowed contiguous GGUF bytes times an f32 activation vector."""
-        from .packed import _buffers, matvec
-        if int(kind) != 0:
-            return matvec(self.lib, raw, kind, shape, x)
-        _buffers(raw, kind, shape)
-        x = _array(x, 'input')
-        if not np.isfinite(x).all():
-            raise ValueError('packed input must be finite')
-        out = self.matvec(raw.view(np.float32).reshape(shape), x)
+    @staticmethod
+    def _f32_packed(raw, shape):
+        """A kind-0 (F32) GGUF tensor's bytes viewed as its weight matrix."""
+        return raw.view(np.float32).reshape(shape)
+
+    @staticmethod
+    def _finite_output(out):
         if not np.isfinite(out).all():
             raise ValueError('nonfinite packed GGUF output')
         return out
+
+    def packed_matvec(self, raw, kind, shape, x):
+        """Borrowed contiguous GGUF bytes times an f32 activation vector."""
+        from .packed import _buffers, matvec
+        if int(kind):
+            return matvec(self.lib, raw, kind, shape, x)
+        _buffers(raw, kind, shape)
+        x = _need_f32(x, 'input')
+        if not np.isfinite(x).all():
+            raise ValueError('packed input must be finite')
+        return self._finite_output(self.matvec(self._f32_packed(raw, shape), x))
 
     def packed_linear_batch(self, raw, kind, shape, x):
         """Batched projection straight from borrowed GGUF bytes."""
         from .packed import batch_input, matmul
-        if int(kind) != 0:
+        if int(kind):
             return matmul(self.lib, raw, kind, shape, x)
-        rows, cols, suffix, x = batch_input(raw, kind, shape, x)
-        if len(x) == 0 or rows == 0:
-            return np.empty((len(x), rows), dtype=np.float32)
-        out = self.linear_batch(raw.view(np.float32).reshape(shape), x)
-        if not np.isfinite(out).all():
-            raise ValueError('nonfinite packed GGUF output')
-        return out
+        rows, _, _, x = batch_input(raw, kind, shape, x)
+        if rows == 0 or len(x) == 0:
+            return np.empty((len(x), rows), np.float32)
+        return self._finite_output(self.linear_batch(self._f32_packed(raw, shape), x))
 
+    # ---------------------------------------------------- per-row primitives
     def rmsnorm(self, x, w, eps):
-        x, w = _array(x, 'input'), _array(w, 'weight')
-        if w.ndim != 1 or w.size != x.shape[-1] or not w.size:
-            raise ValueError('rmsnorm weight must match the nonempty final input axis')
-        eps = float(eps)
-        if not np.isfinite(eps) or eps <= 0:
-            raise ValueError('rmsnorm epsilon must be finite and positive')
-        out = np.empty_like(x)
-        for src, dst in zip(x.reshape(-1, w.size), out.reshape(-1, w.size)):
-            self._call('rmsnorm', dst, src, w, w.size, eps)
-        return out
+        x, w = _need_f32(x, 'input'), _need_f32(w, 'weight')
+        width = _need_row_params(x, (w,), 'rmsnorm', 'weight')
+        return _rows(self._abi, 'rmsnorm', x, width, (w,), (_need_eps(eps, 'rmsnorm'),))
 
-    def rope(self, x, position, theta):
-        x = _array(x, 'input')
-        d = x.shape[-1]
-        if not d or d % 2:
-            raise ValueError('RoPE final dimension must be positive and even')
-        position, theta = float(position), float(theta)
-        if not np.isfinite(position) or not np.isfinite(theta) or theta <= 0:
-            raise ValueError('RoPE requires finite position and positive finite theta')
-        coefficients = _cached_rope_coefficients if d <= 4096 else _make_rope_coefficients
-        cosine, sine = coefficients(d, position, theta)
-        out = np.empty_like(x)
-        self._call('rope_glm', out, x, cosine, sine, x.size // d, d)
-        return out
+    def layernorm(self, x, w, bias, eps=1e-6):
+        """Affine LayerNorm along the final axis (the indexer's k_norm)."""
+        x, w, bias = _need_f32(x, 'input'), _need_f32(w, 'weight'), _need_f32(bias, 'bias')
+        width = _need_row_params(x, (w, bias), 'layernorm', 'weight/bias')
+        return _rows(self._abi, 'layernorm', x, width, (w, bias), (_need_eps(eps, 'layernorm'),))
 
     def softmax(self, x):
-        x = _array(x, 'input')
-        n = x.shape[-1]
-        if not n:
+        x = _need_f32(x, 'input')
+        width = x.shape[-1]
+        if not width:
             raise ValueError('softmax final axis must be nonempty')
-        rows = x.reshape(-1, n)
-        if np.isnan(rows).any() or np.isposinf(rows).any() or not np.isfinite(rows).any(axis=-1).all():
+        flat = x.reshape(-1, width)
+        if np.isnan(flat).any() or np.isposinf(flat).any() or not np.isfinite(flat).any(axis=-1).all():
             raise ValueError('softmax needs one finite score per row and no NaN/+inf')
-        out = np.empty_like(x)
-        for src, dst in zip(rows, out.reshape(-1, n)):
-            self._call('softmax', dst, src, n)
-        return out
+        return _rows(self._abi, 'softmax', x, width)
 
+    # ------------------------------------------------------------ elementwise
     def swiglu(self, gate, up):
-        gate, up = _array(gate, 'gate'), _array(up, 'up')
+        gate, up = _need_f32(gate, 'gate'), _need_f32(up, 'up')
         if gate.shape != up.shape:
             raise ValueError('SwiGLU gate and up shapes must match')
         out = np.empty_like(gate)
-        self._call('swiglu', out, gate, up, gate.size)
+        self._abi.run('swiglu', out, gate, up, gate.size)
         return out
 
+    def rope(self, x, position, theta):
+        x = _need_f32(x, 'input')
+        d = x.shape[-1]
+        if d == 0 or d % 2:
+            raise ValueError('RoPE final dimension must be positive and even')
+        position, theta = float(position), float(theta)
+        if not (np.isfinite(position) and np.isfinite(theta) and theta > 0):
+            raise ValueError('RoPE requires finite position and positive finite theta')
+        cos, sin = (_rope_table_cached if d <= 4096 else _rope_table)(d, position, theta)
+        out = np.empty_like(x)
+        self._abi.run('rope_glm', out, x, cos, sin, x.size // d, d)
+        return out
+
+    # ---------------------------------------------------- routing and DSA
     def route(self, logits, bias, k, scale):
-        logits, bias = _array(logits, 'logits'), _array(bias, 'bias')
+        logits, bias = _need_f32(logits, 'logits'), _need_f32(bias, 'bias')
         if logits.ndim != 1 or bias.shape != logits.shape:
             raise ValueError('route expects equal one-dimensional logits and bias')
-        if not isinstance(k, (int, np.integer)) or not 0 < k <= logits.size:
+        if not (isinstance(k, (int, np.integer)) and 0 < k <= logits.size):
             raise ValueError('route k must be an integer in [1, experts]')
-        if not np.isfinite(logits).all() or not np.isfinite(bias).all() or not np.isfinite(scale):
+        if not (np.isfinite(logits).all() and np.isfinite(bias).all() and np.isfinite(scale)):
             raise ValueError('route inputs and scale must be finite')
         ids, weights = np.empty(k, np.int32), np.empty(k, np.float32)
-        self._call('router', ids, weights, logits, bias, logits.size, k, float(scale))
+        self._abi.run('router', ids, weights, logits, bias, logits.size, k, float(scale))
         return ids, weights
 
-    def layernorm(self, x, w, bias, eps=1e-6):
-        """Affine LayerNorm along the final axis (indexer k_norm)."""
-        x, w, bias = _array(x, 'input'), _array(w, 'weight'), _array(bias, 'bias')
-        if w.ndim != 1 or bias.shape != w.shape or w.size != x.shape[-1] or not w.size:
-            raise ValueError('layernorm weight/bias must match the nonempty final input axis')
-        eps = float(eps)
-        if not np.isfinite(eps) or eps <= 0:
-            raise ValueError('layernorm epsilon must be finite and positive')
-        out = np.empty_like(x)
-        for src, dst in zip(x.reshape(-1, w.size), out.reshape(-1, w.size)):
-            self._call('layernorm', dst, src, w, bias, w.size, eps)
-        return out
-
     def topk(self, scores, k):
-        """Descending finite scores, ties by smaller index; int32 ids."""
-        scores = _array(scores, 'scores')
+        """Indices of the k largest finite scores, descending, ties by the
+        smaller index (int32)."""
+        scores = _need_f32(scores, 'scores')
         if scores.ndim != 1 or not np.isfinite(scores).all():
             raise ValueError('topk expects finite one-dimensional scores')
-        if not isinstance(k, (int, np.integer)) or not 0 <= k <= scores.size:
+        if not (isinstance(k, (int, np.integer)) and 0 <= k <= scores.size):
             raise ValueError('topk k must be an integer in [0, scores.size]')
         ids = np.empty(k, np.int32)
-        self._call('topk', ids, scores, scores.size, k)
+        self._abi.run('topk', ids, scores, scores.size, k)
         return ids
 
     def index_scores(self, q, keys, weights, scale=None):
-        """DSA score per token: sum_h weights[h]*relu(dot(q[h],keys[t])*scale)."""
-        q, keys, weights = _array(q, 'query'), _array(keys, 'keys'), _array(weights, 'weights')
-        if q.ndim != 2 or keys.ndim != 2 or weights.ndim != 1:
+        """DSA score of every cached token t: sum_h weights[h] *
+        relu(dot(q[h], keys[t]) * scale)."""
+        q, keys, weights = _need_f32(q, 'query'), _need_f32(keys, 'keys'), _need_f32(weights, 'weights')
+        if (q.ndim, keys.ndim, weights.ndim) != (2, 2, 1):
             raise ValueError('index_scores expects query[heads,dim], keys[tokens,dim], weights[heads]')
         heads, dim = q.shape
-        if not heads or not dim or keys.shape[1] != dim or weights.size != heads:
+        if 0 in (heads, dim) or keys.shape[1] != dim or weights.size != heads:
             raise ValueError('index_scores dimensions do not match')
         scale = dim ** -0.5 if scale is None else float(scale)
         if not np.isfinite(scale):
             raise ValueError('index_scores scale must be finite')
         out = np.empty(keys.shape[0], np.float32)
-        self._call('index_scores', out, q, keys, weights, keys.shape[0], heads, dim, scale)
+        self._abi.run('index_scores', out, q, keys, weights, keys.shape[0], heads, dim, scale)
         return out

@@ -16,6 +16,7 @@ import hashlib
 import sys
 from functools import lru_cache
 from pathlib import Path
+from typing import NamedTuple
 
 import numpy as np
 
@@ -57,32 +58,47 @@ def supports(lib, kind):
     return kind in LAYOUTS and hasattr(lib, 'glm_vx_packed_' + LAYOUTS[kind][2])
 
 
-def _geometry(kind):
-    return (1, 4, 'f32') if kind == 0 else LAYOUTS[kind]
+class _Matrix(NamedTuple):
+    """A packed weight matrix's geometry after its format and shape checks."""
+    rows: int
+    cols: int
+    suffix: str
+    nbytes: int
+
+
+def _matrix(kind, shape):
+    """Format and shape rules (before the bytes are looked at)."""
+    kind = int(kind)
+    if kind != 0 and kind not in LAYOUTS:
+        raise ValueError('unsupported packed GGML format')
+    if len(shape) != 2 or any(type(n) is not int for n in shape):
+        raise ValueError('packed weight shape must be two Python integer dimensions')
+    rows, cols = shape
+    block, size, suffix = (1, 4, 'f32') if kind == 0 else LAYOUTS[kind]
+    if rows < 0 or cols <= 0 or cols % block:
+        raise ValueError('packed matrix must have nonnegative rows and positive block-aligned cols')
+    nbytes = rows * (cols // block) * size
+    # The int32 ABI indexes F32 matrices by element and quantized ones by byte.
+    if max(rows, cols, rows * cols) > INT32_MAX or (kind != 0 and nbytes > INT32_MAX):
+        raise ValueError('packed matrix exceeds Vx int32 indexing capacity')
+    return _Matrix(rows, cols, suffix, nbytes)
+
+
+def _bytes_match(raw, kind, m):
+    """Rules on the borrowed bytes themselves."""
+    if not (isinstance(raw, np.ndarray) and raw.dtype == np.uint8 and raw.flags.c_contiguous):
+        raise ValueError('packed bytes must be a contiguous uint8 array')
+    if raw.nbytes != m.nbytes:
+        raise ValueError('packed byte count does not match shape/format')
+    if int(kind) == 0 and raw.ctypes.data % np.dtype(np.float32).alignment:
+        raise ValueError('F32 packed bytes must be aligned for float loads')
 
 
 def _buffers(raw, kind, shape):
     """Validate a borrowed packed matrix; returns (rows, cols, suffix)."""
-    kind = int(kind)
-    if kind != 0 and kind not in LAYOUTS:
-        raise ValueError('unsupported packed GGML format')
-    if len(shape) != 2 or not all(type(n) is int for n in shape):
-        raise ValueError('packed weight shape must be two Python integer dimensions')
-    rows, cols = shape
-    block, size, suffix = _geometry(kind)
-    if rows < 0 or cols <= 0 or cols % block:
-        raise ValueError('packed matrix must have nonnegative rows and positive block-aligned cols')
-    # F32 indexes float elements; quantized codecs index bytes (int32 ABI).
-    nbytes = rows * (cols // block) * size
-    if rows > INT32_MAX or cols > INT32_MAX or rows * cols > INT32_MAX or (kind != 0 and nbytes > INT32_MAX):
-        raise ValueError('packed matrix exceeds Vx int32 indexing capacity')
-    if not isinstance(raw, np.ndarray) or raw.dtype != np.uint8 or not raw.flags.c_contiguous:
-        raise ValueError('packed bytes must be a contiguous uint8 array')
-    if raw.nbytes != nbytes:
-        raise ValueError('packed byte count does not match shape/format')
-    if kind == 0 and raw.ctypes.data % np.dtype(np.float32).alignment:
-        raise ValueError('F32 packed bytes must be aligned for float loads')
-    return rows, cols, suffix
+    m = _matrix(kind, shape)
+    _bytes_match(raw, kind, m)
+    return m.rows, m.cols, m.suffix
 
 
 def _status(code, what):
@@ -121,16 +137,20 @@ def unpack_for_validation(lib, raw, kind, shape):
     return out
 
 
+MAX_BATCH = 64
+
+
 def batch_input(raw, kind, shape, x):
-    """Validate a bounded token batch before any allocation or transpose."""
+    """Validate a bounded token batch before any allocation or transpose:
+    returns (rows, cols, suffix, x as float32 [batch, cols])."""
     rows, cols, suffix = _buffers(raw, kind, shape)
     x = np.asarray(x, dtype=np.float32)
-    if x.ndim != 2 or x.shape[1] != cols:
+    if x.shape[1:] != (cols,) or x.ndim != 2:
         raise ValueError('packed batch input must be [batch,weight columns]')
-    batch = x.shape[0]
-    if batch > 64:
-        raise ValueError('packed batch supports at most 64 tokens')
-    if batch * cols > INT32_MAX or batch * rows > INT32_MAX:
+    batch = len(x)
+    if batch > MAX_BATCH:
+        raise ValueError(f'packed batch supports at most {MAX_BATCH} tokens')
+    if batch * max(cols, rows) > INT32_MAX:
         raise ValueError('packed batch exceeds Vx int32 indexing capacity')
     if not np.isfinite(x).all():
         raise ValueError('packed input must be finite')
