@@ -65,6 +65,18 @@ IQ1_BLOCK, IQ1_BYTES = 256, 50
 EXPERT_MATRIX_BYTES = INTER * (HIDDEN // IQ1_BLOCK) * IQ1_BYTES  # 2,457,600; gate, up and down are equal
 
 
+# the full synthetic GLM-MoE-DSA decoder.  Widths from the
+# BASELINE line; the remaining architecture fields (DSA indexer every fourth
+# layer after the first three, RoPE theta) from the reference's model config.
+CONFIG4 = dict(num_hidden_layers=78, first_k_dense_replace=3, hidden_size=6144, vocab_size=154880,
+               num_attention_heads=64, q_lora_rank=2048, kv_lora_rank=512, qk_nope_head_dim=192,
+               qk_rope_head_dim=64, v_head_dim=256, index_n_heads=32, index_head_dim=128, index_topk=2048,
+               index_topk_freq=4, index_skip_topk_offset=3, intermediate_size=12288, moe_intermediate_size=2048,
+               n_routed_experts=256, n_shared_experts=1, num_experts_per_tok=8, routed_scaling_factor=2.5,
+               rms_norm_eps=1e-5, rope_parameters={'rope_theta': 8000000, 'rope_type': 'default'},
+               attention_bias=False, tie_word_embeddings=False)
+
+
 def traffic_row(workload):
     """roofline.traffic for `workload` from profiles/traffic_per_launch.txt
     (one-pass ncu captures): (bytes per launch, source) or (None, reason)."""
@@ -502,6 +514,48 @@ def dsa_sweep(rt, lib, backend, stream, steps, peak):
     return res
 
 
+def decoder_sweep(rt, backend, steps):
+    """Config 4 on one GPU: the resident batched greedy decoder (gpu/decoder.py)
+    at BASELINE config-4 widths, B=64 sequences whose caches hold 4096
+    synthetic positions (a stand-in for prefilling the 4096-token prompts),
+    device-generated random weights (IQ1_S experts, Q4_K attention, Q8_0
+    embedding / lm_head).  The 78-layer model (~150 GB of experts plus
+    ~58 GB of caches) does not fit one GPU, so the step is measured at 4
+    layers (3 dense + 1 sparse) and 6 (3 dense + 3 sparse): the sparse layer's
+    time is the difference / 2 and the 78-layer step is extrapolated as
+    t(4) + 74 * t_sparse (labelled as such)."""
+    from gpu.decoder import ResidentDecoder, SyntheticWeights
+    B, ctx = 64, 4096
+    reps = max(3, min(steps, 10))
+    out = {}
+    for L in (4, 6):
+        dec = ResidentDecoder(backend, CONFIG4, SyntheticWeights(CONFIG4, seed=44), batch=B, capacity=ctx + 16 + reps,
+                              layers=L)
+        try:
+            dec.fill_caches(ctx)
+            dec.set_tokens(np.random.default_rng(L).integers(0, CONFIG4['vocab_size'], B))
+            for _ in range(3):
+                dec.step()
+            dec.check()
+            e0, e1 = rt.Event(), rt.Event()
+            e0.record(backend.stream)
+            for _ in range(reps):
+                dec.step()
+            e1.record(backend.stream)
+            e1.synchronize()
+            dec.check()
+            out[L] = e0.elapsed_ms(e1) / reps
+        finally:
+            dec.close()
+    t_sparse = (out[6] - out[4]) / 2
+    t78 = out[4] + 74 * t_sparse
+    return {'batch': B, 'context': ctx, 'ms_per_step_4_layers': out[4], 'ms_per_step_6_layers': out[6],
+            'tok_s_6_layers': B / (out[6] * 1e-3), 'sparse_layer_ms': t_sparse,
+            'extrapolated_78_layer_ms_per_step': t78, 'extrapolated_78_layer_tok_s': B / (t78 * 1e-3),
+            'note': 'measured at 4 and 6 layers (3 dense + 1 or 3 sparse) on one GPU; 78 layers extrapolated '
+                    '(the full model does not fit one GPU); caches filled synthetically, weights random'}
+
+
 def expert_parallel_step(args, ranks, backend, layer, moe, x, clocks):
     """N>1 headline: the config-2 layer with its 256 experts sharded over the
     N GPUs (gpu/ep.py, csrc/ep.cu: 256/N experts per GPU, router and shared
@@ -702,6 +756,7 @@ def run_ours(args, ranks):
 
     gemv = fused_gemv_sweep(rt, lib, dev, stream, args.steps, peak)
     dsa = dsa_sweep(rt, lib, backend, stream, args.steps, peak) if ranks.world == 1 else None
+    decoder = decoder_sweep(rt, backend, args.steps) if ranks.world == 1 and not args.no_decoder else None
     ep = (expert_parallel_step(args, ranks, backend, layer, moe, xs[TOKENS], clocks)
           if ranks.world > 1 and EXPERTS % ranks.world == 0 else None)
     single = {'tok_s': value, 'ms_per_step': total_ms / args.steps,
@@ -744,6 +799,7 @@ def run_ours(args, ranks):
         'vs_baseline': None, 'dtype': 'f32', 'data': 'synthetic', 'config': config, 'roofline': roofline,
         'fused_gemv': gemv,
         **({'dsa_decode': dsa} if dsa else {}),
+        **({'full_decoder_config4': decoder} if decoder else {}),
         **extra,
         'e2e': headline['e2e'],
         'gpu_launches': headline['gpu_launches'],
@@ -861,6 +917,7 @@ def main():
     ap.add_argument('--impl', choices=('ours', 'reference'), default='ours')
     ap.add_argument('--cpu-seconds', type=float, default=10.0)
     ap.add_argument('--no-cpu-baseline', action='store_true')
+    ap.add_argument('--no-decoder', action='store_true', help='skip the config-4 decoder measurement')
     ap.add_argument('--profile-case', nargs='?', const='moe', choices=('moe', 'gemm', 'dsa', 'dsa1'),
                     help='run a small kernel-capture case (one GPU) instead of the benchmark')
     args = ap.parse_args()

@@ -629,6 +629,11 @@ GLMVX_EXPORT int64_t glmvx_dsa_scratch_bytes(int32_t batch, int32_t heads, int32
 // topk <= 4096.
 namespace {
 
+int32_t dsa_mla_stage(float *out, const int32_t *sel, const float *q_latent, const float *q_rope, const float *latents,
+                      const float *rope_keys, const int32_t *lens, int32_t batch, int32_t heads, int32_t rank,
+                      int32_t rope_dim, int32_t capacity, int32_t topk, float scale, float *numerator, float *stats,
+                      int splits, bool tc, cudaStream_t st);
+
 int32_t dsa_decode(float *out, int32_t *selected_out, const float *q_latent, const float *q_rope, const float *q_index,
                    const float *head_weights, const float *latents, const float *rope_keys, const float *index_keys,
                    const int32_t *lens, int32_t batch, int32_t heads, int32_t rank, int32_t rope_dim,
@@ -669,6 +674,18 @@ int32_t dsa_decode(float *out, int32_t *selected_out, const float *q_latent, con
     rc = launch_topk_batch(sel, scores, capacity, topk, lens, capacity, topk, batch, st);
     if (rc) return rc;
     if (attention_inputs_ready) GLMVX_CUDA(cudaStreamWaitEvent(st, attention_inputs_ready, 0));
+    return dsa_mla_stage(out, sel, q_latent, q_rope, latents, rope_keys, lens, batch, heads, rank, rope_dim, capacity,
+                         topk, scale, numerator, stats, splits, tc, st);
+}
+
+// The attention stage of the DSA decode: absorbed MLA of every query over its
+// selection sel [batch][topk] (ids outside [0, lens[b]) skipped), split
+// partials into numerator/stats, then the ordered merge into out.
+int32_t dsa_mla_stage(float *out, const int32_t *sel, const float *q_latent, const float *q_rope, const float *latents,
+                      const float *rope_keys, const int32_t *lens, int32_t batch, int32_t heads, int32_t rank,
+                      int32_t rope_dim, int32_t capacity, int32_t topk, float scale, float *numerator, float *stats,
+                      int splits, bool tc, cudaStream_t st) {
+    int32_t rc = kOk;
     const int64_t lstride = static_cast<int64_t>(capacity) * rank, rstride = static_cast<int64_t>(capacity) * rope_dim;
     if (tc) {
         rc = launch_mla_tc(numerator, stats, q_latent, q_rope, latents, rope_keys, sel, lens, heads, rank, rope_dim,
@@ -732,6 +749,39 @@ GLMVX_EXPORT int32_t glmvx_dsa_decode_wait(float *out, int32_t *selected_out, co
     return rc;
 }
 
+// The attention stage of glmvx_dsa_decode alone, over selections given by
+// the caller (a DSA layer that reuses the previous layer's top-k,
+// glm_vx/model.py:197-204): selected [batch][topk], -1 padded; each query
+// attends to its ids in [0, lens[b]).  Scratch as glmvx_dsa_scratch_bytes.
+GLMVX_EXPORT int32_t glmvx_dsa_attend(float *out, const int32_t *selected, const float *q_latent, const float *q_rope,
+                                      const float *latents, const float *rope_keys, const int32_t *lens, int32_t batch,
+                                      int32_t heads, int32_t rank, int32_t rope_dim, int32_t capacity, int32_t topk,
+                                      float scale, void *scratch, uint64_t scratch_bytes, void *stream) {
+    if (batch <= 0 || heads <= 0 || rank <= 0 || rank > 512 || rope_dim < 0 || rope_dim > 128 || capacity <= 0 ||
+        topk <= 0 || topk > 4096 || !(scale > 0.0f) || !std::isfinite(scale)) {
+        set_error("dsa_attend: invalid dimensions or scale");
+        return kInvalid;
+    }
+    if (!out || !selected || !q_latent || !latents || !lens || (rope_dim && (!q_rope || !rope_keys))) {
+        set_error("dsa_attend: null pointer");
+        return kInvalid;
+    }
+    const int64_t need = glmvx_dsa_scratch_bytes(batch, heads, rank, capacity, topk);
+    if (!scratch || static_cast<int64_t>(scratch_bytes) < need || (reinterpret_cast<uintptr_t>(scratch) & 15)) {
+        set_error("dsa_attend: scratch needs %lld bytes, 16-byte aligned", static_cast<long long>(need));
+        return kInvalid;
+    }
+    const auto up16 = [](int64_t b) { return (b + 15) / 16 * 16; };
+    float *numerator = reinterpret_cast<float *>(static_cast<char *>(scratch) + up16(4LL * batch * capacity) +
+                                                 up16(4LL * batch * topk));
+    const bool tc = kMlaUseTensorCores && mla_tc_supported(heads, rank, rope_dim, topk) &&
+                    static_cast<int64_t>(batch) * topk >= kMlaTcMinRows;
+    const int splits = tc ? mla_tc_splits(topk, batch) : mla_splits(heads, rank, topk, batch);
+    float *stats = numerator + static_cast<size_t>(batch) * splits * heads * rank;
+    return dsa_mla_stage(out, selected, q_latent, q_rope, latents, rope_keys, lens, batch, heads, rank, rope_dim,
+                         capacity, topk, scale, numerator, stats, splits, tc, static_cast<cudaStream_t>(stream));
+}
+
 // Appends one row per query to the caches of glmvx_dsa_decode (device
 // pointers; new rows [batch][dim]); *full (device int32) is set to 1 for a
 // query whose cache already holds `capacity` rows, which is then unchanged.
@@ -739,7 +789,8 @@ GLMVX_EXPORT int32_t glmvx_dsa_append(float *latents, float *rope_keys, float *i
                                       const float *new_latent, const float *new_rope, const float *new_index,
                                       int32_t batch, int32_t capacity, int32_t rank, int32_t rope_dim,
                                       int32_t index_dim, int32_t *full, void *stream) {
-    if (batch < 0 || capacity <= 0 || rank <= 0 || rope_dim < 0 || index_dim <= 0 || !lens || !full) {
+    if (batch < 0 || capacity <= 0 || rank <= 0 || rope_dim < 0 || index_dim < 0 || !lens || !full ||
+        (index_dim && (!index_keys || !new_index))) {
         set_error("dsa_append: invalid arguments");
         return kInvalid;
     }

@@ -14,6 +14,7 @@
 //                                     token's 32-column sums
 //   IQ1_S  w = d*(2s+1)*(g + delta)   A = (2s+1)*(8g +- 1) (integers <= 135,
 //                                     exact in f16); per block D*d/8
+//   Q8_0   w = d*q                    A = q (exact in f16); d per 32 columns
 //
 // The activations enter as two f16 limbs.  Per 256-column chunk of a token,
 // x*2^E (largest magnitude in [2^14, 2^15)) = hi + lo with hi = f16(x*2^E),
@@ -341,6 +342,79 @@ struct GemmFmt<FmtIQ1_S> {
     }
 };
 
+// Signed int8 bytes of a word, pairs (0,1) and (2,3), to f16x2: the bytes
+// biased by 128 go into the mantissa of 1024 (f16 0x64xx = 1024 + byte),
+// one exact half2 subtraction of 1152 leaves q.
+__device__ __forceinline__ uint32_t s8pair_to_f16x2(uint32_t biased_word, uint32_t sel) {
+    uint32_t r;
+    asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(prmt(biased_word, 0x64646464u, sel)), "r"(0x64806480u));
+    return r;
+}
+
+template <>
+struct GemmFmt<FmtQ8_0> {
+    // Eight 34-byte blocks per 256 columns; A = q (int8, exact in f16), the
+    // block scale d applied per 32 columns (two k16 steps) in f32.
+    static constexpr int kChunkBytes = 8 * 34, kTableBytes = 0;
+    __device__ static void init_table(uint8_t *, int, int) {}
+    template <int NTW>
+    __device__ __forceinline__ static void chunk(const uint8_t *r0, const uint8_t *r1, const uint8_t *rec, int nt8,
+                                                 int tq0, int lane, uint32_t, float (&tot)[NTW][2]) {
+        const int t = lane & 3;
+        const uint2 *bf = reinterpret_cast<const uint2 *>(rec) + tq0 * 32 + lane;
+        float ctot[NTW][2];
+#pragma unroll
+        for (int q = 0; q < NTW; ++q) ctot[q][0] = ctot[q][1] = 0.0f;
+#pragma unroll
+        for (int b = 0; b < 8; ++b) {
+            float acc[NTW][4];
+#pragma unroll
+            for (int q = 0; q < NTW; ++q) acc[q][0] = acc[q][1] = acc[q][2] = acc[q][3] = 0.0f;
+#pragma unroll
+            for (int hs = 0; hs < 2; ++hs) {
+                // bytes 4t..4t+3 of the block's 16-column half hs; a block at an
+                // odd index starts 2 bytes past a 4-byte boundary, so its quant
+                // bytes are aligned, an even one's straddle two words
+                const int off = 34 * b + 2 + 16 * hs + 4 * t;
+                uint32_t w0, w1;
+                if (b & 1) {
+                    w0 = lds32(r0 + off);
+                    w1 = lds32(r1 + off);
+                } else {
+                    w0 = __funnelshift_r(lds32(r0 + off - 2), lds32(r0 + off + 2), 16);
+                    w1 = __funnelshift_r(lds32(r1 + off - 2), lds32(r1 + off + 2), 16);
+                }
+                w0 ^= 0x80808080u;
+                w1 ^= 0x80808080u;
+                const uint32_t a0 = s8pair_to_f16x2(w0, 0x4140), a2 = s8pair_to_f16x2(w0, 0x4342);
+                const uint32_t a1 = s8pair_to_f16x2(w1, 0x4140), a3 = s8pair_to_f16x2(w1, 0x4342);
+                const int st = 2 * b + hs;
+#pragma unroll
+                for (int q = 0; q < NTW; ++q) {
+                    const uint2 bb = bf[(st * nt8 + q) * 32];
+                    mma_f16(acc[q], a0, a1, a2, a3, bb.x, bb.y);
+                }
+            }
+            const float d0 = h2f(u16(r0 + 34 * b)), d1 = h2f(u16(r1 + 34 * b));
+#pragma unroll
+            for (int q = 0; q < NTW; ++q) {
+                ctot[q][0] = fmaf(acc[q][0] + acc[q][1], d0, ctot[q][0]);
+                ctot[q][1] = fmaf(acc[q][2] + acc[q][3], d1, ctot[q][1]);
+            }
+        }
+        const GemmRecord R{nt8};
+        const int *ex = reinterpret_cast<const int *>(rec + R.exps_off());
+#pragma unroll
+        for (int q = 0; q < NTW; ++q) {
+            const int E = ex[4 * (tq0 + q) + t];
+            const bool bad = E == kPrepNonFinite;
+            const float f1 = bad ? __int_as_float(0x7fc00000) : pow2(-(E / 2)), f2 = bad ? 1.0f : pow2(-(E - E / 2));
+            tot[q][0] += (ctot[q][0] * f1) * f2;
+            tot[q][1] += (ctot[q][1] * f1) * f2;
+        }
+    }
+};
+
 // ----------------------------------------------------------------- kernel ---
 
 template <class F, int NTW>
@@ -487,8 +561,11 @@ bool plan_gemm_ntw(int ntw, int rows, int cols, int batch, int row_bytes, GemmPl
     const int per_cta = (rows + p.grid - 1) / p.grid;
     p.srow = ((row_bytes >> 4) & 1) ? row_bytes : row_bytes + 16;
     p.RG = std::max(1, std::min((per_cta + 15) / 16, kGemmMaxWarps / p.TG));
-    while (p.RG > 1 && static_cast<size_t>(16 * p.RG) * p.srow > 100 * 1024) --p.RG;
-    if (static_cast<size_t>(16 * p.RG) * p.srow > 100 * 1024) return false;
+    // Q8_0 rows are long (6528 bytes at 6144 columns): one 16-row tile may
+    // take a little more of the budget.
+    const size_t a_cap = (std::is_same_v<F, FmtQ8_0> ? 112 : 100) * 1024;
+    while (p.RG > 1 && static_cast<size_t>(16 * p.RG) * p.srow > a_cap) --p.RG;
+    if (static_cast<size_t>(16 * p.RG) * p.srow > a_cap) return false;
     const GemmRecord rec{p.nt8};
     p.rec_stride = static_cast<int>((rec.bytes() + 127) & ~size_t(127));
     p.a_bytes = static_cast<int>((static_cast<size_t>(16 * p.RG) * p.srow + 127) & ~size_t(127));
@@ -547,7 +624,7 @@ int32_t launch_gemm(const GemmPlan &p, float *out, const uint8_t *w, const uint8
 
 bool gemm_f16_supported(int kind, int cols, int batch) {
     if (batch < kGemmMinTokens || batch > kGemmMaxTokens || cols <= 0 || cols % 256) return false;
-    return kind == 12 || (kind == 19 && cols % 2048 == 0);
+    return kind == 12 || kind == 8 || (kind == 19 && cols % 2048 == 0);
 }
 
 int32_t gemm_f16_device(int32_t kind, float *out, const uint8_t *w, const float *x, int rows, int cols, int batch,
@@ -565,9 +642,19 @@ int32_t gemm_f16_device(int32_t kind, float *out, const uint8_t *w, const float 
     const int row_bytes = cols / blk * bytes;
     int32_t st = kUnsupported;
     dispatch_format(kind, [&]<class F>() {
-        if constexpr (std::is_same_v<F, FmtQ4_K> || std::is_same_v<F, FmtIQ1_S>) {
+        if constexpr (std::is_same_v<F, FmtQ4_K> || std::is_same_v<F, FmtIQ1_S> || std::is_same_v<F, FmtQ8_0>) {
             GemmPlan p;
             if (!plan_gemm<F>(rows, cols, batch, row_bytes, p)) {
+                // Long rows with many tokens may not fit one CTA's shared
+                // memory: run the batch as halves (the weights stream twice).
+                if (batch >= 2 * kGemmMinTokens) {
+                    const int h = (batch + 1) / 2;
+                    st = gemm_f16_device(kind, out, w, x, rows, cols, h, scratch, stream);
+                    if (!st)
+                        st = gemm_f16_device(kind, out + static_cast<size_t>(h) * rows, w,
+                                             x + static_cast<size_t>(h) * cols, rows, cols, batch - h, scratch, stream);
+                    return;
+                }
                 set_error("gemm: no launch plan for this shape");
                 return;
             }

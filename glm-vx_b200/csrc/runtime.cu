@@ -53,7 +53,10 @@ int sm_count() {
     std::lock_guard<std::mutex> lock(mu);
     if (!cached[dev]) {
         int n = 0;
+        cudaStreamCaptureMode mode = cudaStreamCaptureModeRelaxed;  // the first query may come during a capture
+        cudaThreadExchangeStreamCaptureMode(&mode);
         cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        cudaThreadExchangeStreamCaptureMode(&mode);
         cached[dev] = n > 0 ? n : 148;
     }
     return cached[dev];
@@ -68,8 +71,13 @@ int32_t allow_dynamic_smem(const void *kernel, size_t bytes, const char *name) {
     std::lock_guard<std::mutex> lock(mu);
     size_t &have = raised[{dev, kernel}];
     if (have >= bytes) return kOk;
+    // The first launch may happen while this thread captures a graph: let
+    // this one non-stream call through (relaxed mode) without invalidating it.
+    cudaStreamCaptureMode mode = cudaStreamCaptureModeRelaxed;
+    cudaThreadExchangeStreamCaptureMode(&mode);
     const cudaError_t e =
         cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes));
+    cudaThreadExchangeStreamCaptureMode(&mode);
     if (e != cudaSuccess) return cuda_fail(e, name);
     have = bytes;
     return kOk;

@@ -111,6 +111,16 @@ SIGNATURES = {
     'glmvx_ep_combine': ([_P, _P, _I32, _P], _I32),
     'glmvx_ep_step': ([_P, _P, _P, _I32, _P, _P, _P], _I32),
     'glmvx_ep_destroy': ([_P], _I32),
+    'glmvx_embed_rows': ([_P, _P, _I32, _P, _I32, _I32, _I32, _P], _I32),
+    'glmvx_rope_rows': ([_P, _P, _P, _P, _P, _I32, _I32, _I32, _I32, _I64, _I32, _I32, _I64, _I32, _I32, _I32, _P],
+                        _I32),
+    'glmvx_rmsnorm_rows': ([_P, _P, _P, _I32, _I32, _I64, _I64, _F32, _P], _I32),
+    'glmvx_absorb_query': ([_P, _P, _P, _I32, _I32, _I32, _I32, _I32, _I32, _P], _I32),
+    'glmvx_absorb_value': ([_P, _P, _P, _I32, _I32, _I32, _I32, _P], _I32),
+    'glmvx_scale': ([_P, _P, _F32, _I64, _P], _I32),
+    'glmvx_argmax_rows': ([_P, _P, _I32, _I32, _P], _I32),
+    'glmvx_fill_random': ([_P, _I32, _I64, _U64, _F32, _I32, _P], _I32),
+    'glmvx_dsa_attend': ([_P, _P, _P, _P, _P, _P, _P, _I32, _I32, _I32, _I32, _I32, _I32, _F32, _P, _U64, _P], _I32),
     'glmvx_moe_job_counts': ([_I32, _I32, _I32, _I32, _I32, _I32, _P, _PI32, _P], _I32),
 }
 

@@ -328,6 +328,47 @@ int32_t glmvx_ep_combine(void *layer, float *y, int32_t tokens, void *stream);
 int32_t glmvx_ep_step(void *layer, float *y, const float *x, int32_t tokens, int32_t *ids_out, float *weights_out,
                       void *stream);
 int32_t glmvx_ep_destroy(void *layer);
+/* Batched decode-step pieces of the GLM-MoE-DSA model (one token for each of
+ * `tokens` sequences, device pointers; the reference runs them per token on
+ * the host, glm_vx/model.py:96-237, 359-392).
+ *   glmvx_embed_rows   x[b] = row ids[b] of an F32 (kind 0) or Q8_0 (8) table
+ *   glmvx_rope_rows    the reference rope (kernels/kernels.vx:425-441, pairs
+ *                      rotated, output half-split) of `d` elements of `heads`
+ *                      strided rows per sequence at position pos[b], cos/sin
+ *                      from [max_pos][d/2] tables, plus `tail` copied elements
+ *   glmvx_rmsnorm_rows rmsnorm of strided rows (kernels/kernels.vx:17-27)
+ *   glmvx_absorb_query q_latent[b,h] = kv_b[h,:nope]^T query[b,h,:nope],
+ *                      kv_b [heads][nope+vdim][rank], serial f32 sums
+ *   glmvx_absorb_value out[b,h*vdim+i] = sum_r kvbo_t[h][r][i] att[b,h,r]
+ *                      (kv_b's value half transposed), serial f32 sums
+ *   glmvx_scale        out = x * s
+ *   glmvx_argmax_rows  first index of each row's maximum (numpy argmax)
+ *   glmvx_fill_random  seeded synthetic weights: f32 N(0,1)*scale (or ones),
+ *                      or Q8_0 / Q4_K / IQ1_S blocks of random bytes with
+ *                      |N(0,1)|*scale fp16 block scales
+ *   glmvx_dsa_attend   glmvx_dsa_decode's attention stage alone over given
+ *                      selections [batch][topk] (-1 padded), for DSA layers
+ *                      that reuse the previous layer's top-k (model.py:197-204) */
+int32_t glmvx_embed_rows(float *out, const void *table, int32_t kind, const int32_t *ids, int32_t rows, int32_t vocab,
+                         int32_t hidden, void *stream);
+int32_t glmvx_rope_rows(float *out, const float *x, const float *cos_tab, const float *sin_tab, const int32_t *pos,
+                        int32_t tokens, int32_t heads, int32_t d, int32_t tail, int64_t x_tok, int32_t x_head,
+                        int32_t x_off, int64_t out_tok, int32_t out_head, int32_t out_off, int32_t max_pos,
+                        void *stream);
+int32_t glmvx_rmsnorm_rows(float *out, const float *x, const float *w, int32_t rows, int32_t n, int64_t x_stride,
+                           int64_t out_stride, float eps, void *stream);
+int32_t glmvx_absorb_query(float *q_latent, const float *query, const float *kvb, int32_t tokens, int32_t heads,
+                           int32_t nope, int32_t qk_head, int32_t rank, int32_t vdim, void *stream);
+int32_t glmvx_absorb_value(float *out, const float *att, const float *kvbo_t, int32_t tokens, int32_t heads,
+                           int32_t rank, int32_t vdim, void *stream);
+int32_t glmvx_scale(float *out, const float *x, float s, int64_t n, void *stream);
+int32_t glmvx_argmax_rows(int32_t *ids, const float *logits, int32_t rows, int32_t n, void *stream);
+int32_t glmvx_fill_random(void *out, int32_t kind, int64_t count, uint64_t seed, float scale, int32_t ones,
+                          void *stream);
+int32_t glmvx_dsa_attend(float *out, const int32_t *selected, const float *q_latent, const float *q_rope,
+                         const float *latents, const float *rope_keys, const int32_t *lens, int32_t batch,
+                         int32_t heads, int32_t rank, int32_t rope_dim, int32_t capacity, int32_t topk, float scale,
+                         void *scratch, uint64_t scratch_bytes, void *stream);
 /* FP8 E4M3FN block-scaled projection, device pointers: out[rows] =
  * sum_c (decode(weight[r,c]) * scales[r/128, c/128]) * x[c], weight u8
  * [rows, cols], scales f32 [ceil(rows/128), ceil(cols/128)].  Replaces the

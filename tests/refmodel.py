@@ -172,6 +172,14 @@ class PackedCheckpoint:
             return self.dense[name]
         raise KeyError(name)
 
+    def packed_tensor(self, name):
+        """(raw bytes, kind, shape) of a projection (gpu.decoder source protocol)."""
+        return self.packed[name]
+
+    def dense_tensor(self, name):
+        """float32 array of a norm, bias, kv_b or the F32 embedding."""
+        return self.dense[name]
+
     def kinds(self):
         return sorted({k for _, k, _ in self.packed.values()})
 

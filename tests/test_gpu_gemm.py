@@ -1,6 +1,6 @@
 """f16 tensor-core GEMM for token batches (csrc/packed_gemm.cu, path 6)
 against the CPU oracle's batched packed kernels (the reference's batch_v2
-contract, kernels/packed.vx:473ff): Q4_K and IQ1_S at 8..64 tokens, shapes
+contract, kernels/packed.vx:473ff): Q4_K, IQ1_S and Q8_0 at 8..64 tokens, shapes
 with one and several row tiles and column slices, ragged row counts,
 activation ranges far from N(0,1), a non-finite token, determinism."""
 import numpy as np
@@ -23,7 +23,8 @@ def _case(kind, rows, cols, batch, seed):
 
 @pytest.mark.parametrize('kind,rows,cols,batch', [
     (12, 6144, 2048, 16), (12, 6144, 2048, 64), (12, 300, 4096, 9), (12, 16, 256, 8), (12, 777, 2048, 33),
-    (12, 2048, 6144, 24), (19, 2048, 6144, 32), (19, 6144, 2048, 8), (19, 130, 2048, 64), (19, 4100, 4096, 12)])
+    (12, 2048, 6144, 24), (19, 2048, 6144, 32), (19, 6144, 2048, 8), (19, 130, 2048, 64), (19, 4100, 4096, 12),
+    (8, 2048, 6144, 16), (8, 2048, 6144, 64), (8, 300, 4096, 9), (8, 1000, 256, 8), (8, 4099, 2048, 40)])
 def test_gemm_matches_oracle(cuda_lib, oracle, kind, rows, cols, batch):
     raw, x = _case(kind, rows, cols, batch, rows + batch)
     got, path = _device_gemm(cuda_lib, kind, raw, rows, cols, x)
@@ -33,7 +34,7 @@ def test_gemm_matches_oracle(cuda_lib, oracle, kind, rows, cols, batch):
     assert_close_dot(got, want, dec, x)
 
 
-@pytest.mark.parametrize('kind', [12, 19])
+@pytest.mark.parametrize('kind', [12, 19, 8])
 def test_gemm_activation_ranges(cuda_lib, oracle, kind):
     """Each token's chunks are scaled separately: tiny, huge, mixed and zero
     chunks keep the relative accuracy of the others."""
@@ -54,7 +55,7 @@ def test_gemm_activation_ranges(cuda_lib, oracle, kind):
     assert_close_dot(got, want, dec, x)
 
 
-@pytest.mark.parametrize('kind', [12, 19])
+@pytest.mark.parametrize('kind', [12, 19, 8])
 def test_gemm_nonfinite_token(cuda_lib, kind):
     """A non-finite activation makes that token's outputs NaN and leaves the
     other tokens finite."""
