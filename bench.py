@@ -514,7 +514,7 @@ def dsa_sweep(rt, lib, backend, stream, steps, peak):
     return res
 
 
-def decoder_sweep(rt, backend, steps):
+def decoder_sweep(rt, backend, steps, ranks=None):
     """Config 4 on one GPU: the resident batched greedy decoder (gpu/decoder.py)
     at BASELINE config-4 widths, B=64 sequences whose caches hold 4096
     synthetic positions (a stand-in for prefilling the 4096-token prompts),
@@ -524,19 +524,31 @@ def decoder_sweep(rt, backend, steps):
     layers (3 dense + 1 sparse) and 6 (3 dense + 3 sparse): the sparse layer's
     time is the difference / 2 and the 78-layer step is extrapolated as
     t(4) + 74 * t_sparse (labelled as such)."""
-    from gpu.decoder import ResidentDecoder, SyntheticWeights
+    from gpu.decoder import ResidentDecoder, SyntheticWeights, expert_parallel_moe
     B, ctx = 64, 4096
+    N = ranks.world if ranks else 1
+    local = B // N
     reps = max(3, min(steps, 10))
     out = {}
+
+    def allgather(data):
+        got = [None] * N
+        ranks.dist.all_gather_object(got, data)
+        return got
+
     for L in (4, 6):
-        dec = ResidentDecoder(backend, CONFIG4, SyntheticWeights(CONFIG4, seed=44), batch=B, capacity=ctx + 16 + reps,
-                              layers=L)
+        factory = expert_parallel_moe(ranks.rank, N, allgather) if N > 1 else None
+        dec = ResidentDecoder(backend, CONFIG4, SyntheticWeights(CONFIG4, seed=44), batch=local,
+                              capacity=ctx + 16 + reps, layers=L, moe_layer_factory=factory)
         try:
-            dec.fill_caches(ctx)
-            dec.set_tokens(np.random.default_rng(L).integers(0, CONFIG4['vocab_size'], B))
+            dec.fill_caches(ctx, seed=1 + (ranks.rank if ranks else 0))
+            dec.set_tokens(np.random.default_rng(L * 100 + (ranks.rank if ranks else 0)).integers(
+                0, CONFIG4['vocab_size'], local))
             for _ in range(3):
                 dec.step()
             dec.check()
+            if ranks:
+                ranks.barrier()
             e0, e1 = rt.Event(), rt.Event()
             e0.record(backend.stream)
             for _ in range(reps):
@@ -544,16 +556,20 @@ def decoder_sweep(rt, backend, steps):
             e1.record(backend.stream)
             e1.synchronize()
             dec.check()
-            out[L] = e0.elapsed_ms(e1) / reps
+            ms = e0.elapsed_ms(e1) / reps
+            out[L] = ranks.max(ms) if ranks else ms
         finally:
-            dec.close()
+            dec.close(barrier=ranks.barrier if N > 1 else None)
     t_sparse = (out[6] - out[4]) / 2
     t78 = out[4] + 74 * t_sparse
-    return {'batch': B, 'context': ctx, 'ms_per_step_4_layers': out[4], 'ms_per_step_6_layers': out[6],
-            'tok_s_6_layers': B / (out[6] * 1e-3), 'sparse_layer_ms': t_sparse,
+    return {'batch': B, 'sequences_per_gpu': local, 'context': ctx, 'ms_per_step_4_layers': out[4],
+            'ms_per_step_6_layers': out[6], 'tok_s_6_layers': B / (out[6] * 1e-3), 'sparse_layer_ms': t_sparse,
             'extrapolated_78_layer_ms_per_step': t78, 'extrapolated_78_layer_tok_s': B / (t78 * 1e-3),
-            'note': 'measured at 4 and 6 layers (3 dense + 1 or 3 sparse) on one GPU; 78 layers extrapolated '
-                    '(the full model does not fit one GPU); caches filled synthetically, weights random'}
+            'parallelism': (f'expert x{N} for the sparse layers ({CONFIG4["n_routed_experts"] // N} experts per GPU), '
+                            f'data-parallel attention ({local} sequences per GPU)') if N > 1 else 'single GPU',
+            'note': 'measured at 4 and 6 layers (3 dense + 1 or 3 sparse); 78 layers extrapolated as '
+                    't(4) + 74 * (t(6) - t(4)) / 2 (the full model does not fit one GPU); caches filled '
+                    'synthetically, weights random'}
 
 
 def expert_parallel_step(args, ranks, backend, layer, moe, x, clocks):
@@ -756,7 +772,8 @@ def run_ours(args, ranks):
 
     gemv = fused_gemv_sweep(rt, lib, dev, stream, args.steps, peak)
     dsa = dsa_sweep(rt, lib, backend, stream, args.steps, peak) if ranks.world == 1 else None
-    decoder = decoder_sweep(rt, backend, args.steps) if ranks.world == 1 and not args.no_decoder else None
+    decoder = (decoder_sweep(rt, backend, args.steps, ranks if ranks.world > 1 else None)
+               if not args.no_decoder and 64 % ranks.world == 0 else None)
     ep = (expert_parallel_step(args, ranks, backend, layer, moe, xs[TOKENS], clocks)
           if ranks.world > 1 and EXPERTS % ranks.world == 0 else None)
     single = {'tok_s': value, 'ms_per_step': total_ms / args.steps,
@@ -839,6 +856,8 @@ def run_profile_case(args):
         return profile_gemm()
     if args.profile_case in ('dsa', 'dsa1'):  # 16 queries, or the single-query step
         return profile_dsa(16 if args.profile_case == 'dsa' else 1)
+    if args.profile_case == 'decoder':
+        return profile_decoder()
     from gpu.backend import GPUBackend
     from gpu import runtime as rt
     from gpu.moe import MoELayer
@@ -857,6 +876,26 @@ def run_profile_case(args):
     xd.close()
     yd.close()
     moe.close()
+    backend.close()
+    return 0
+
+
+def profile_decoder(layers=4, steps=2):
+    """The config-4 resident decoder at 4 layers (3 dense + 1 sparse), 64
+    sequences over 4096 synthetic cache rows: `steps` eager (un-graphed)
+    steps, so a launch list shows every kernel of a step."""
+    from gpu.backend import GPUBackend
+    from gpu.decoder import ResidentDecoder, SyntheticWeights
+    backend = GPUBackend(0)
+    dec = ResidentDecoder(backend, CONFIG4, SyntheticWeights(CONFIG4, seed=44), batch=64, capacity=4096 + 16,
+                          layers=layers)
+    dec.fill_caches(4096)
+    dec.set_tokens(np.arange(64) * 7)
+    for _ in range(steps):
+        dec._step_launches()
+    dec.check()
+    print(f'profile case ok: config-4 decoder, {layers} layers, 64 sequences, {steps} steps', flush=True)
+    dec.close()
     backend.close()
     return 0
 
@@ -918,7 +957,7 @@ def main():
     ap.add_argument('--cpu-seconds', type=float, default=10.0)
     ap.add_argument('--no-cpu-baseline', action='store_true')
     ap.add_argument('--no-decoder', action='store_true', help='skip the config-4 decoder measurement')
-    ap.add_argument('--profile-case', nargs='?', const='moe', choices=('moe', 'gemm', 'dsa', 'dsa1'),
+    ap.add_argument('--profile-case', nargs='?', const='moe', choices=('moe', 'gemm', 'dsa', 'dsa1', 'decoder'),
                     help='run a small kernel-capture case (one GPU) instead of the benchmark')
     args = ap.parse_args()
     if args.profile_case:

@@ -32,6 +32,7 @@ on the device instead (counter-based, seeded), for configurations too large
 to build on the host.
 """
 import ctypes as C
+import hashlib
 import math
 
 import numpy as np
@@ -78,6 +79,14 @@ class SyntheticWeights:
 
     def __init__(self, config, seed=0):
         self.config, self.seed = dict(config), int(seed)
+
+    def fill(self, lib, ptr, kind, count, scale, key, ones, stream):
+        """Generate tensor `key` at device address ptr (its seed is a hash of
+        the model seed and the tensor name, so every rank and every
+        configuration derives the same bytes for the same tensor)."""
+        digest = hashlib.sha256(f'{self.seed}:{key}'.encode()).digest()
+        rt.check(lib, lib.glmvx_fill_random(ptr, kind, count, int.from_bytes(digest[:8], 'little'), scale,
+                                            int(ones), stream), 'glmvx_fill_random')
 
     def kind(self, name, shape):
         if name in ('lm_head', 'model.embed_tokens'):
@@ -150,12 +159,10 @@ class ResidentDecoder:
         buf.upload(array, self.s)
         return buf.ptr
 
-    def _fill(self, kind, nbytes, count, scale, ones=False):
-        """Device buffer of synthetic weights (see SyntheticWeights)."""
+    def _fill(self, kind, nbytes, count, scale, key, ones=False):
+        """Device buffer of synthetic weights for tensor `key` (see SyntheticWeights)."""
         buf = self._dev(nbytes)
-        self._seq = getattr(self, '_seq', 0) + 1
-        rt.check(self.lib, self.lib.glmvx_fill_random(buf.ptr, kind, count, self.source.seed * 1000003 + self._seq,
-                                                      scale, int(ones), self.s), 'glmvx_fill_random')
+        self.source.fill(self.lib, buf.ptr, kind, count, scale, key, ones, self.s)
         return buf.ptr
 
     def _proj(self, name, rows, cols):
@@ -164,7 +171,7 @@ class ResidentDecoder:
             kind = self.source.kind(name, (rows, cols))
             block, size, _ = LAYOUTS[kind] if kind else (1, 4, 'f32')
             count = rows * cols // block
-            return self._fill(kind, count * size, count, self.source.scale(kind, cols)), kind, rows, cols
+            return self._fill(kind, count * size, count, self.source.scale(kind, cols), name), kind, rows, cols
         raw, kind, shape = self.source.packed_tensor(name + '.weight')
         if tuple(shape) != (rows, cols):
             raise ValueError(f'{name}: shape {shape}, expected {(rows, cols)}')
@@ -172,7 +179,7 @@ class ResidentDecoder:
 
     def _vec(self, name, n, ones=True):
         if self._synthetic:  # norms 1, biases N(0, 0.01)
-            return self._fill(0, 4 * n, n, 0.01, ones=ones)
+            return self._fill(0, 4 * n, n, 0.01, name, ones=ones)
         a = np.asarray(self.source.dense_tensor(name), np.float32)
         if a.shape != (n,):
             raise ValueError(f'{name}: shape {a.shape}, expected ({n},)')
@@ -205,9 +212,9 @@ class ResidentDecoder:
             # value half transposed to [heads][rank][v] for coalesced reads.
             if self._synthetic:
                 n = self.heads * (self.nope + self.vdim) * self.rank
-                kvb = self._fill(0, 4 * n, n, 1.0 / math.sqrt(self.rank))
+                kvb = self._fill(0, 4 * n, n, 1.0 / math.sqrt(self.rank), a + '.kv_b_proj')
                 nv = self.heads * self.rank * self.vdim  # the value half, already transposed
-                kvbo = self._fill(0, 4 * nv, nv, 1.0 / math.sqrt(self.rank))
+                kvbo = self._fill(0, 4 * nv, nv, 1.0 / math.sqrt(self.rank), a + '.kv_b_proj.value_t')
             else:
                 w = np.asarray(self.source.dense_tensor(a + '.kv_b_proj.weight'), np.float32)
                 w = w.reshape(self.heads, self.nope + self.vdim, self.rank)
@@ -232,6 +239,19 @@ class ResidentDecoder:
             self.layers.append(L)
         self.backend.stream.synchronize()
 
+    def synthetic_experts(self, m, part, first, count, rows, cols):
+        """Device stack of experts [first, first + count) of projection `part`
+        of sparse layer `m`, each expert generated from its own name, so a
+        rank's slice holds the same bytes as the whole stack would."""
+        kind = self.source.kind(m + '.experts', (rows, cols))
+        block, size, _ = LAYOUTS[kind]
+        blocks = rows * cols // block
+        buf = self._dev(count * blocks * size)
+        for i, e in enumerate(range(first, first + count)):
+            self.source.fill(self.lib, buf.ptr + i * blocks * size, kind, blocks, self.source.scale(kind, cols),
+                             f'{m}.experts.{e}.{part}', False, self.s)
+        return buf.ptr
+
     def _local_moe(self, m):
         c, H = self.config, self.hidden
         E, I = int(c['n_routed_experts']), int(c['moe_intermediate_size'])
@@ -243,9 +263,7 @@ class ResidentDecoder:
         for part, (rows, cols) in (('gate_proj', (I, H)), ('up_proj', (I, H)), ('down_proj', (H, I))):
             if self._synthetic:
                 kind = self.source.kind(m + '.experts', (rows, cols))
-                block, size, _ = LAYOUTS[kind]
-                count = E * rows * cols // block
-                stacks.append((self._fill(kind, count * size, count, self.source.scale(kind, cols)), kind))
+                stacks.append((self.synthetic_experts(m, part, 0, E, rows, cols), kind))
             else:
                 raws = [self.source.packed_tensor(f'{m}.experts.{e}.{part}.weight') for e in range(E)]
                 kinds = {r[1] for r in raws}
@@ -498,7 +516,10 @@ class ResidentDecoder:
             L['lens'].upload(lens, self.s)
         self.backend.stream.synchronize()
 
-    def close(self):
+    def close(self, barrier=None):
+        """Free everything; with expert-parallel sparse layers pass the ranks'
+        `barrier` (each layer's mailbox is freed only after every rank has
+        unmapped it)."""
         self.backend.stream.synchronize()
         if self._graph is not None:
             self._graph.close()
@@ -506,13 +527,54 @@ class ResidentDecoder:
         for L in getattr(self, 'layers', []):
             m = L.get('moe')
             if m is not None and hasattr(m, 'close'):
-                m.close()
+                m.close(barrier=barrier) if barrier is not None else m.close()
         if getattr(self, 'host_tokens', None) is not None:
             self.host_tokens.close()
             self.host_tokens = None
         for b in self._bufs:
             b.close()
         self._bufs = []
+
+
+def expert_parallel_moe(rank, world, allgather):
+    """moe_layer_factory for ResidentDecoder: every sparse layer as an
+    ExpertParallelLayer (gpu/ep.py) holding this rank's experts
+    [rank*E/world, (rank+1)*E/world) with the router and shared expert
+    replicated, connected to the other ranks' layers through `allgather`
+    (bytes -> [bytes per rank]).  Each rank decodes its own sequences (data-
+    parallel attention); the ranks step together."""
+    def factory(i, dec):
+        from .ep import ExpertParallelLayer, experts_per_rank
+        c, H = dec.config, dec.hidden
+        E, I = int(c['n_routed_experts']), int(c['moe_intermediate_size'])
+        per = experts_per_rank(E, world)
+        m = f'model.layers.{i}.mlp'
+        router = dec._proj(m + '.gate', E, H)
+        if router[1] != 0:
+            raise ValueError('the router must be F32')
+        bias = dec._vec(m + '.gate.e_score_correction_bias', E, ones=False)
+        stacks, kind = [], None
+        for part, (rows, cols) in (('gate_proj', (I, H)), ('up_proj', (I, H)), ('down_proj', (H, I))):
+            if dec._synthetic:
+                kind = dec.source.kind(m + '.experts', (rows, cols))
+                stacks.append(dec.synthetic_experts(m, part, rank * per, per, rows, cols))
+            else:
+                raws = [dec.source.packed_tensor(f'{m}.experts.{e}.{part}.weight') for e in range(rank * per,
+                                                                                              (rank + 1) * per)]
+                kind = raws[0][1]
+                stacks.append(dec._put(np.concatenate([np.ascontiguousarray(r[0]).view(np.uint8) for r in raws])))
+        shared = None
+        if int(c.get('n_shared_experts', 1)) > 0:
+            SI = I * int(c.get('n_shared_experts', 1))
+            shared = tuple(dec._proj(f'{m}.shared_experts.{part}', rows, cols)[0]
+                           for part, (rows, cols) in (('gate_proj', (SI, H)), ('up_proj', (SI, H)),
+                                                     ('down_proj', (H, SI))))
+        dec.backend.stream.synchronize()
+        layer = ExpertParallelLayer(dec.backend, rank, world, router[0], bias, kind, *stacks, E, H, I, dec.k,
+                                    dec.scale_r, shared=shared, max_tokens=dec.B, device_weights=True)
+        layer.connect_ipc(allgather)
+        return layer
+    return factory
 
 
 class _LocalMoE:

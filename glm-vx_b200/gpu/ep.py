@@ -82,12 +82,22 @@ class ExpertParallelLayer:
     token rows per rank (world * max_tokens * top_k <= 4096)."""
 
     def __init__(self, backend, rank, world, router_w, router_bias, kind, gate, up, down, experts, hidden, inter,
-                 top_k, scale, shared=None, max_tokens=32):
+                 top_k, scale, shared=None, max_tokens=32, device_weights=False):
+        """device_weights: router_w, router_bias, gate, up, down and shared
+        are device addresses (ints) of resident arrays the caller keeps alive,
+        laid out as the host arrays would be; nothing is uploaded."""
         self.backend, self.lib = backend, backend.lib
         self.rank, self.world = int(rank), int(world)
         self.kind, self.experts, self.hidden, self.inter = int(kind), int(experts), int(hidden), int(inter)
         self.top_k, self.scale, self.max_tokens = int(top_k), float(scale), int(max_tokens)
         self.per_rank = experts_per_rank(self.experts, self.world)
+        self._buffers = []
+        if device_weights:
+            self.router_w, self.router_bias = int(router_w), int(router_bias)
+            self.gate, self.up, self.down = int(gate), int(up), int(down)
+            self.shared = tuple(int(p) for p in shared) if shared is not None else (None, None, None)
+            self._create()
+            return
         block, size, _ = LAYOUTS[self.kind]
         if self.hidden % block or self.inter % block:
             raise ValueError('hidden and intermediate sizes must be block-aligned')
@@ -101,7 +111,6 @@ class ExpertParallelLayer:
             raise ValueError('router weight must be [experts, hidden] and bias [experts]')
         backend._begin()
         s = backend.stream.handle
-        self._buffers = []
 
         def upload(arr):
             arr = np.ascontiguousarray(arr)
@@ -121,6 +130,9 @@ class ExpertParallelLayer:
         else:
             self.shared = (None, None, None)
         backend.stream.synchronize()
+        self._create()
+
+    def _create(self):
         handle = C.c_void_p()
         rt.check(self.lib, self.lib.glmvx_ep_create(
             C.byref(handle), self.rank, self.world, self.max_tokens, self.hidden, self.inter, self.experts, self.top_k,

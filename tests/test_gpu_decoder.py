@@ -93,3 +93,62 @@ def test_synthetic_config4_shapes_run(gpu_backend):
         finally:
             dec.close()
     assert outs[0].tolist() == outs[1].tolist()
+
+
+EP_PROMPTS = PROMPTS + [[7, 8, 9, 10, 11, 12]]
+
+
+def _gpus():
+    from gpu import runtime
+    try:
+        return runtime.device_count()
+    except Exception:
+        return 0
+
+
+def _ep_rank_main(rank, world, boot_dir, out_path):
+    import sys
+    from pathlib import Path
+    root = Path(__file__).resolve().parents[1]
+    sys.path[:0] = [str(root), str(root / 'glm-vx_b200'), str(root / 'tests')]
+    import refmodel as R
+    from gpu.backend import GPUBackend
+    from gpu.decoder import ResidentDecoder, expert_parallel_moe
+    from gpu.ep import FileBootstrap
+    backend = GPUBackend(rank)
+    boot = FileBootstrap(boot_dir, rank, world)
+    config = R.dropin_config()
+    ckpt = R.PackedCheckpoint(config, seed=1)
+    per = len(EP_PROMPTS) // world
+    dec = ResidentDecoder(backend, config, ckpt, batch=per, capacity=32,
+                          moe_layer_factory=expert_parallel_moe(rank, world, boot.allgather))
+    tokens, _ = dec.generate(np.array(EP_PROMPTS[rank * per:(rank + 1) * per]), NEW_TOKENS)
+    dec.close(barrier=boot.barrier)
+    backend.close()
+    np.save(out_path, tokens)
+
+
+@pytest.mark.skipif(_gpus() < 2, reason='needs two GPUs')
+def test_expert_parallel_decoder_on_two_gpus(tmp_path):
+    """Two processes, one GPU each: each decodes two of the four prompts
+    (data-parallel attention) while the sparse layers' experts are split
+    between the GPUs (gpu/ep.py over IPC mailboxes); every sequence's greedy
+    tokens equal the reference model's own decode on the oracle."""
+    import multiprocessing as mp
+    refmodel.ref_glm_vx()
+    from glm_vx.model import GlmMoeDsaModel
+    from oracle import loader
+    config = refmodel.dropin_config()
+    ckpt = refmodel.PackedCheckpoint(config, seed=1)
+    model = GlmMoeDsaModel(config, ckpt, refmodel.ref_vx_backend(loader.serial()), packed_weights=True)
+    want = [refmodel.greedy(model, p, NEW_TOKENS, grouped_prefill=False)[0] for p in EP_PROMPTS]
+    ctx = mp.get_context('spawn')
+    procs = [ctx.Process(target=_ep_rank_main, args=(r, 2, str(tmp_path / 'boot'), str(tmp_path / f'r{r}.npy')))
+             for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+        assert p.exitcode == 0
+    got = np.concatenate([np.load(tmp_path / f'r{r}.npy') for r in range(2)])
+    assert got.tolist() == want
