@@ -561,11 +561,10 @@ bool plan_gemm_ntw(int ntw, int rows, int cols, int batch, int row_bytes, GemmPl
     const int per_cta = (rows + p.grid - 1) / p.grid;
     p.srow = ((row_bytes >> 4) & 1) ? row_bytes : row_bytes + 16;
     p.RG = std::max(1, std::min((per_cta + 15) / 16, kGemmMaxWarps / p.TG));
-    // Q8_0 rows are long (6528 bytes at 6144 columns): one 16-row tile may
-    // take a little more of the budget.
-    const size_t a_cap = (std::is_same_v<F, FmtQ8_0> ? 112 : 100) * 1024;
-    while (p.RG > 1 && static_cast<size_t>(16 * p.RG) * p.srow > a_cap) --p.RG;
-    if (static_cast<size_t>(16 * p.RG) * p.srow > a_cap) return false;
+    // Tiles of several row groups stay within 100 KB; a single 16-row tile
+    // of long rows (Q8_0 at 6144 columns, Q4_K at 16384) may take more, as
+    // long as the whole plan fits the budget (checked below).
+    while (p.RG > 1 && static_cast<size_t>(16 * p.RG) * p.srow > 100 * 1024) --p.RG;
     const GemmRecord rec{p.nt8};
     p.rec_stride = static_cast<int>((rec.bytes() + 127) & ~size_t(127));
     p.a_bytes = static_cast<int>((static_cast<size_t>(16 * p.RG) * p.srow + 127) & ~size_t(127));

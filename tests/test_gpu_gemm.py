@@ -24,7 +24,8 @@ def _case(kind, rows, cols, batch, seed):
 @pytest.mark.parametrize('kind,rows,cols,batch', [
     (12, 6144, 2048, 16), (12, 6144, 2048, 64), (12, 300, 4096, 9), (12, 16, 256, 8), (12, 777, 2048, 33),
     (12, 2048, 6144, 24), (19, 2048, 6144, 32), (19, 6144, 2048, 8), (19, 130, 2048, 64), (19, 4100, 4096, 12),
-    (8, 2048, 6144, 16), (8, 2048, 6144, 64), (8, 300, 4096, 9), (8, 1000, 256, 8), (8, 4099, 2048, 40)])
+    (8, 2048, 6144, 16), (8, 2048, 6144, 64), (8, 300, 4096, 9), (8, 1000, 256, 8), (8, 4099, 2048, 40),
+    (8, 200, 8192, 8), (12, 640, 16384, 64), (12, 100, 16384, 13)])
 def test_gemm_matches_oracle(cuda_lib, oracle, kind, rows, cols, batch):
     raw, x = _case(kind, rows, cols, batch, rows + batch)
     got, path = _device_gemm(cuda_lib, kind, raw, rows, cols, x)

@@ -45,11 +45,7 @@ def _batch_path(kind, cols, batch):
     """Tensor-core path taken for an aligned matrix: the f16 GEMM for 8..64
     tokens of Q4_K, Q8_0 and IQ1_S (IQ1_S rows of 2048-column multiples), the
     int8 GEMV kernel otherwise."""
-    # Q8_0 needs a 16-row tile of its long rows (padded to an odd number of
-    # 16-byte units) within 112 KB of shared memory: up to 6656 columns.
-    q8_fits = 16 * (cols // 32 * 34 + 16) <= 112 * 1024
-    gemm = 8 <= batch <= 64 and cols % 256 == 0 and (kind == 12 or (kind == 8 and q8_fits) or
-                                                     (kind == 19 and cols % 2048 == 0))
+    gemm = 8 <= batch <= 64 and cols % 256 == 0 and (kind in (8, 12) or (kind == 19 and cols % 2048 == 0))
     return PATH_GEMM if gemm else PATH_MMA
 
 
