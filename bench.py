@@ -858,6 +858,8 @@ def run_profile_case(args):
         return profile_dsa(16 if args.profile_case == 'dsa' else 1)
     if args.profile_case == 'decoder':
         return profile_decoder()
+    if args.profile_case == 'packed_gemm':
+        return profile_packed_gemm()
     from gpu.backend import GPUBackend
     from gpu import runtime as rt
     from gpu.moe import MoELayer
@@ -896,6 +898,36 @@ def profile_decoder(layers=4, steps=2):
     dec.check()
     print(f'profile case ok: config-4 decoder, {layers} layers, 64 sequences, {steps} steps', flush=True)
     dec.close()
+    backend.close()
+    return 0
+
+
+def profile_packed_gemm():
+    """The f16 tensor-core packed GEMM on BASELINE config 1 at 64 tokens (Q4_K
+    6144 x 2048) and on the config-4 lm_head shape at 32 tokens (Q8_0
+    154880 x 6144, 1 GB, larger than L2): three launches each."""
+    from gpu.backend import GPUBackend
+    from gpu import runtime as rt
+    backend = GPUBackend(0)
+    s = backend.stream.handle
+    rng = np.random.default_rng(0)
+    for kind, rows, cols, batch in ((12, 6144, 2048, 64), (8, 154880, 6144, 32)):
+        blk, size = (256, 144) if kind == 12 else (32, 34)
+        nb = rows * cols // blk
+        w = rt.DeviceBuffer(nb * size)
+        rt.check(backend.lib, backend.lib.glmvx_fill_random(w.ptr, kind, nb, 7, 0.01, 0, s), 'glmvx_fill_random')
+        x = rng.normal(size=(batch, cols)).astype(np.float32)
+        xd, od = rt.DeviceBuffer(x.nbytes), rt.DeviceBuffer(4 * batch * rows)
+        xd.upload(x, s)
+        for _ in range(3):
+            rt.check(backend.lib, backend.lib.glmvx_packed_gemm(kind, od.ptr, w.ptr, xd.ptr, rows, cols, batch, s),
+                     'glmvx_packed_gemm')
+        backend.stream.synchronize()
+        for b in (w, xd, od):
+            b.close()
+    backend.device.check_device_error()
+    print('profile case ok: packed f16 GEMM, config-1 Q4_K x64 and config-4 lm_head Q8_0 x32, 3 launches each',
+          flush=True)
     backend.close()
     return 0
 
@@ -957,7 +989,7 @@ def main():
     ap.add_argument('--cpu-seconds', type=float, default=10.0)
     ap.add_argument('--no-cpu-baseline', action='store_true')
     ap.add_argument('--no-decoder', action='store_true', help='skip the config-4 decoder measurement')
-    ap.add_argument('--profile-case', nargs='?', const='moe', choices=('moe', 'gemm', 'dsa', 'dsa1', 'decoder'),
+    ap.add_argument('--profile-case', nargs='?', const='moe', choices=('moe', 'gemm', 'dsa', 'dsa1', 'decoder', 'packed_gemm'),
                     help='run a small kernel-capture case (one GPU) instead of the benchmark')
     args = ap.parse_args()
     if args.profile_case:

@@ -49,16 +49,18 @@ def ref_vx_backend(library):
     return ref_kernels().backend.VxBackend(str(library))
 
 
-def dropin_config(layers=4):
+def dropin_config(layers=4, width=256):
     """The reference's tiny GLM-MoE-DSA config (glm_vx/tiny.py) widened so
-    every projection is block-aligned for the packed formats: hidden 256
-    (IQ1_S / Q4_K rows), 8 routed experts + 1 shared, top-2, first layer
-    dense, the last layer sharing the previous indexer selection."""
+    every projection is block-aligned for the packed formats: hidden and
+    intermediate sizes `width` (256: IQ1_S / Q4_K rows; 2048: the tensor-core
+    widths the expert-parallel layer needs), 8 routed experts + 1 shared,
+    top-2, first layer dense, the last layer sharing the previous indexer
+    selection."""
     from glm_vx.tiny import tiny_config
     c = tiny_config()
-    c.update(hidden_size=256, vocab_size=512, num_hidden_layers=layers, num_attention_heads=4,
+    c.update(hidden_size=width, vocab_size=512, num_hidden_layers=layers, num_attention_heads=4,
              num_key_value_heads=4, q_lora_rank=64, kv_lora_rank=32, qk_nope_head_dim=16, qk_rope_head_dim=8,
-             qk_head_dim=24, v_head_dim=16, intermediate_size=256, moe_intermediate_size=256, n_routed_experts=8,
+             qk_head_dim=24, v_head_dim=16, intermediate_size=width, moe_intermediate_size=width, n_routed_experts=8,
              num_experts_per_tok=2, index_head_dim=16, index_n_heads=4, index_topk=4,
              mlp_layer_types=['dense'] + ['sparse'] * (layers - 1),
              indexer_types=['full'] * (layers - 1) + ['shared'])

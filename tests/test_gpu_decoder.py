@@ -23,14 +23,15 @@ PROMPTS = [[37, 401, 5, 260, 118, 77], [3, 3, 3, 500, 12, 9], [255, 0, 511, 64, 
 NEW_TOKENS = 8
 
 
-@pytest.fixture(scope='module')
-def reference_runs():
+@pytest.fixture(scope='module', params=[256, 2048], ids=['w256', 'w2048'])
+def reference_runs(request):
+    """Width 256 runs the CUDA-core expert jobs, 2048 the tensor-core ones."""
     refmodel.ref_glm_vx()
     from glm_vx.model import GlmMoeDsaModel
     from oracle import loader
-    config = refmodel.dropin_config()
+    config = refmodel.dropin_config(width=request.param)
     ckpt = refmodel.PackedCheckpoint(config, seed=1)
-    model = GlmMoeDsaModel(config, ckpt, refmodel.ref_vx_backend(loader.serial()), packed_weights=True)
+    model = GlmMoeDsaModel(config, ckpt, refmodel.ref_vx_backend(loader.parallel()), packed_weights=True)
     runs = [refmodel.greedy(model, p, NEW_TOKENS, grouped_prefill=False) for p in PROMPTS]
     return config, ckpt, runs
 
@@ -117,7 +118,7 @@ def _ep_rank_main(rank, world, boot_dir, out_path):
     from gpu.ep import FileBootstrap
     backend = GPUBackend(rank)
     boot = FileBootstrap(boot_dir, rank, world)
-    config = R.dropin_config()
+    config = R.dropin_config(width=2048)
     ckpt = R.PackedCheckpoint(config, seed=1)
     per = len(EP_PROMPTS) // world
     dec = ResidentDecoder(backend, config, ckpt, batch=per, capacity=32,
@@ -138,9 +139,9 @@ def test_expert_parallel_decoder_on_two_gpus(tmp_path):
     refmodel.ref_glm_vx()
     from glm_vx.model import GlmMoeDsaModel
     from oracle import loader
-    config = refmodel.dropin_config()
+    config = refmodel.dropin_config(width=2048)  # the expert-parallel layer runs the tensor-core widths
     ckpt = refmodel.PackedCheckpoint(config, seed=1)
-    model = GlmMoeDsaModel(config, ckpt, refmodel.ref_vx_backend(loader.serial()), packed_weights=True)
+    model = GlmMoeDsaModel(config, ckpt, refmodel.ref_vx_backend(loader.parallel()), packed_weights=True)
     want = [refmodel.greedy(model, p, NEW_TOKENS, grouped_prefill=False)[0] for p in EP_PROMPTS]
     ctx = mp.get_context('spawn')
     procs = [ctx.Process(target=_ep_rank_main, args=(r, 2, str(tmp_path / 'boot'), str(tmp_path / f'r{r}.npy')))
