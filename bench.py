@@ -514,6 +514,59 @@ def dsa_sweep(rt, lib, backend, stream, steps, peak):
     return res
 
 
+def attention_config3(rt, backend, steps, peak):
+    """Config 3 with its projections: one DSA attention sub-step of the
+    resident decoder (gpu/decoder.py) at config-3 widths (64 heads, q_lora
+    2048, kv_lora 512, rope 64, nope 192, v 256, indexer 32 x 128 top-2048,
+    RoPE theta 1e6) with Q8_0 random projections (q_a, q_b, kv_a, o_proj,
+    indexer wq_b / wk; the indexer head weights F32 and kv_b F32 as the
+    reference model keeps them), 1 and 16 queries over 32768 cached
+    positions: rmsnorm, projections, indexer, append, top-2048, absorbed MLA,
+    o_proj, residual, as a graph replayed per step."""
+    from gpu.decoder import ResidentDecoder, SyntheticWeights
+    cfg = dict(CONFIG4, num_hidden_layers=1, first_k_dense_replace=1,
+               rope_parameters={'rope_theta': 1000000, 'rope_type': 'default'})
+    ctx = DSA_CONTEXT
+    res = {}
+    for B in (1, 16):
+        reps = max(3, min(steps, 10))
+        dec = ResidentDecoder(backend, cfg, SyntheticWeights(cfg, seed=33, attention_kind=8), batch=B,
+                              capacity=ctx + 8 + reps, layers=1)
+        try:
+            dec.fill_caches(ctx)
+            dec.set_tokens(np.arange(B) * 11)
+            rt.check(backend.lib, backend.lib.glmvx_embed_rows(dec.x, dec.embed[0], dec.embed[1], dec.tokens, B,
+                                                               dec.vocab, dec.hidden, dec.s), 'glmvx_embed_rows')
+            g = dec.attention_graph(0)
+            for _ in range(3):
+                g.launch()
+            dec.check()
+            e0, e1 = rt.Event(), rt.Event()
+            e0.record(backend.stream)
+            for _ in range(reps):
+                g.launch()
+            e1.record(backend.stream)
+            e1.synchronize()
+            dec.check()
+            us = e0.elapsed_ms(e1) / reps * 1e3
+            g.close()
+        finally:
+            dec.close()
+        H, Q = cfg['hidden_size'], cfg['q_lora_rank']
+        heads, R, P, N, V = 64, 512, 64, 192, 256
+        q8 = lambda r, c: r * c // 32 * 34
+        proj = (q8(Q, H) + q8(heads * (N + P), Q) + q8(R + P, H) + q8(H, heads * V) + q8(32 * 128, Q) + q8(128, H)
+                + 4 * 32 * H + 4 * heads * (N + V) * R)
+        per_query = 4 * (ctx * 128 + DSA_TOPK * (R + P))
+        alg = proj + B * per_query
+        res[f'config3_b{B}'] = {'us': us, 'queries_s': B / (us * 1e-6), 'algorithmic_bytes': alg,
+                                'gbs': alg / us / 1e3, 'frac_of_measured_hbm': alg / us / 1e3 / peak,
+                                'projection_bytes': proj, 'context': ctx, 'topk': DSA_TOPK}
+    res['note'] = ('one attention sub-step of the resident decoder with Q8_0 projections (kv_b and the indexer head '
+                   'weights F32 as the reference model keeps them); graph-timed, caches synthetic')
+    return res
+
+
 def decoder_sweep(rt, backend, steps, ranks=None):
     """Config 4 on one GPU: the resident batched greedy decoder (gpu/decoder.py)
     at BASELINE config-4 widths, B=64 sequences whose caches hold 4096
@@ -772,6 +825,8 @@ def run_ours(args, ranks):
 
     gemv = fused_gemv_sweep(rt, lib, dev, stream, args.steps, peak)
     dsa = dsa_sweep(rt, lib, backend, stream, args.steps, peak) if ranks.world == 1 else None
+    if dsa is not None:
+        dsa['with_projections'] = attention_config3(rt, backend, args.steps, peak)
     decoder = (decoder_sweep(rt, backend, args.steps, ranks if ranks.world > 1 else None)
                if not args.no_decoder and 64 % ranks.world == 0 else None)
     ep = (expert_parallel_step(args, ranks, backend, layer, moe, xs[TOKENS], clocks)

@@ -153,6 +153,13 @@ __device__ __forceinline__ void report_device_error(int *err, int code) {
 __device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void allow_dependent_launch() { asm volatile("griddepcontrol.launch_dependents;"); }
 
+// The reference's branch-stable logistic (kernels/kernels.vx:8-15).
+__device__ __forceinline__ float sigmoid_ref(float x) {
+    if (x >= 0.0f) return 1.0f / (1.0f + expf(0.0f - x));
+    const float z = expf(x);
+    return z / (1.0f + z);
+}
+
 // SwiGLU element x*sigmoid(x)*u with the reference's branch-stable sigmoid
 // and rounding order (kernels/kernels.vx:8-15,56-60).
 __device__ __forceinline__ float silu_mul(float g, float u) {

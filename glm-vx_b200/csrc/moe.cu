@@ -30,6 +30,7 @@
 // job per pair (packed_gemv.cu) with SwiGLU fused into the activation load.
 // Jobs are ordered by expert so tokens sharing an expert stream its rows
 // close together in time (L2 reuse).
+#include <climits>
 #include <mutex>
 
 #include "codecs.cuh"
@@ -108,23 +109,91 @@ struct LocalJobSrc {
     __device__ float *out_shared(int, int r) const { return pair_out + static_cast<size_t>(r) * hidden; }
 };
 
+// One warp routes one token over experts <= 256 (expert e = 32 j + lane, j <
+// 8, in registers), with router_kernel's rules exactly (ops.cu,
+// kernels/kernels.vx:252-279): score sigmoid(logit) + bias, a NaN score
+// ranked -inf; k rounds of the largest score, the lower id on ties, the
+// chosen expert removed; weights = the chosen sigmoids over their sum in
+// selection order + 1e-20, times scale.  Ids and weights are bit-identical
+// to router_kernel's.
+constexpr int kWarpRouteExperts = 256, kWarpRouteMaxTokens = 64;
+__device__ void route_token_warp(const float *lr, const float *bias, int E, int k, float scale, int32_t *ids_out,
+                                 float *w_out, int lane) {
+    float sc[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const int e = 32 * j + lane;
+        if (e < E) {
+            const float v = sigmoid_ref(lr[e]) + bias[e];
+            sc[j] = isnan(v) ? -INFINITY : v;
+        } else {
+            sc[j] = __int_as_float(0x7fc00000);  // beyond the experts: never chosen
+        }
+    }
+    float total = 0.0f;
+    for (int slot = 0; slot < k; ++slot) {
+        float bv = -INFINITY;
+        int bi = INT_MAX;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int e = 32 * j + lane;
+            if (sc[j] > bv || (sc[j] == bv && e < bi)) {
+                bv = sc[j];
+                bi = e;
+            }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (ov > bv || (ov == bv && oi < bi)) {
+                bv = ov;
+                bi = oi;
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+            if (32 * j + lane == bi) sc[j] = __int_as_float(0x7fc00000);
+        if (lane == 0) {
+            const float p = sigmoid_ref(lr[bi]);
+            ids_out[slot] = bi;
+            w_out[slot] = p;
+            total = total + p;
+        }
+    }
+    if (lane == 0) {
+        total = total + 1e-20f;
+        for (int slot = 0; slot < k; ++slot) w_out[slot] = w_out[slot] / total * scale;
+    }
+}
+
 // Rank each (token, slot) assignment by (expert id, token): the rank is its
 // pair index, so pairs of one expert are contiguous and ordered by token.
+// With `logits` set the kernel first routes every token itself (a warp per
+// token, route_token_warp), writing ids / wts.
 // With mjobs set (tensor-core path) the job lists come from form_mma_jobs
 // (moe_jobs.cuh): two tokens per job, and with qjobs set too experts routed
 // three or more pairs and the shared expert in a list of four tokens per job.
 // Otherwise one streaming GEMV job per pair (GemvJob).
 __global__ void __launch_bounds__(kGroupThreads)
-    moe_group_kernel(const int32_t *ids, const float *wts, int T, int k, int E, int shared, const uint8_t *gate,
+    moe_group_kernel(int32_t *ids, float *wts, int T, int k, int E, int shared, const uint8_t *gate,
                      const uint8_t *up, const uint8_t *down, size_t gu_stride, size_t dn_stride, const uint8_t *sgate,
                      const uint8_t *sup, const uint8_t *sdown, const float *x, int hidden, int inter, float *g_out,
                      float *u_out, float *pair_out, GemvJob *gu_jobs, GemvJob *dn_jobs, int32_t *comb, float *combw,
                      int *bad, MmaJob *gu_m, MmaJob *dn_m, MmaJob *gu_q, MmaJob *dn_q, int *counts,
-                     const uint8_t *xprep, size_t xstride, const uint8_t *hprep, size_t hstride) {
+                     const uint8_t *xprep, size_t xstride, const uint8_t *hprep, size_t hstride, const float *logits,
+                     const float *bias, float scale) {
     __shared__ GroupSmem g;
     const int n = T * k;
     const int P = n + (shared ? T : 0);
     const bool mma = gu_m != nullptr;
+    if (logits) {
+        const int lane = threadIdx.x & 31;
+        for (int t = threadIdx.x >> 5; t < T; t += kGroupThreads / 32)
+            route_token_warp(logits + static_cast<size_t>(t) * E, bias, E, k, scale, ids + static_cast<size_t>(t) * k,
+                             wts + static_cast<size_t>(t) * k, lane);
+        __syncthreads();  // the block's writes to ids / wts are visible to every thread
+    }
     for (int a = threadIdx.x; a < n; a += blockDim.x) {
         const int e = ids[a];
         g.ids[a] = static_cast<int16_t>(min(max(e, 0), E - 1));
@@ -282,6 +351,9 @@ static int32_t moe_ffn(float *y, const float *x, int32_t tokens, int32_t hidden,
     // more than they save.
     const bool quad = mma && tokens >= kQuadMinTokens && mma_quad_supported(kind, hidden) &&
                       mma_quad_supported(kind, inter);
+    // Up to 64 tokens over up to 256 experts: the grouping kernel routes the
+    // tokens itself (a warp per token) instead of a separate router launch.
+    const bool fused_route = !given_ids && experts <= kWarpRouteExperts && tokens <= kWarpRouteMaxTokens;
     int32_t st_ = mark(0);
     if (st_) return st_;
     if (mma && (st_ = prep_rows_device(w.xprep, x, nullptr, tokens, hidden, st))) return st_;
@@ -292,14 +364,17 @@ static int32_t moe_ffn(float *y, const float *x, int32_t tokens, int32_t hidden,
     } else {
         st_ = glmvx_matmul_nt(w.logits, x, router_w, tokens, experts, hidden, st);
         if (st_ || (st_ = mark(1))) return st_;
-        st_ = glmvx_router(w.ids, w.wts, w.logits, router_bias, tokens, experts, top_k, scale, st);
-        if (st_ || (st_ = mark(2))) return st_;
+        if (!fused_route) {
+            st_ = glmvx_router(w.ids, w.wts, w.logits, router_bias, tokens, experts, top_k, scale, st);
+            if (st_) return st_;
+        }
+        if ((st_ = mark(2))) return st_;
     }
     moe_group_kernel<<<1, kGroupThreads, 0, st>>>(
         w.ids, w.wts, tokens, top_k, experts, shared, gate, up, down, gu_stride, dn_stride, shared_gate, shared_up,
         shared_down, x, hidden, inter, w.g_out, w.u_out, w.pair_out, w.gu_jobs, w.dn_jobs, w.comb, w.combw,
         device_error_word(), mma ? w.gu_mjobs : nullptr, w.dn_mjobs, quad ? w.gu_qjobs : nullptr, w.dn_qjobs, w.counts,
-        w.xprep, prep_stride(hidden), w.hprep, prep_stride(inter));
+        w.xprep, prep_stride(hidden), w.hprep, prep_stride(inter), fused_route ? w.logits : nullptr, router_bias, scale);
     if ((st_ = launch_status("moe_group_kernel")) || (st_ = mark(3))) return st_;
     if (mma) {
         const MmaJob none{};

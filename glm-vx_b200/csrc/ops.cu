@@ -15,11 +15,6 @@
 
 namespace glmvx {
 
-__device__ __forceinline__ float sigmoid_ref(float x) {  // kernels/kernels.vx:8-15
-    if (x >= 0.0f) return 1.0f / (1.0f + expf(0.0f - x));
-    const float z = expf(x);
-    return z / (1.0f + z);
-}
 
 // Block-wide sum for blockDim.x == 256 (8 warps); result broadcast to all.
 __device__ __forceinline__ float block_sum_256(float v, float *scratch) {
@@ -111,7 +106,7 @@ __global__ void __launch_bounds__(256)
     const int quads = cols >> 2;
     // token tiles: two iterations' loads in flight per thread (the grid is
     // one or two CTAs per SM, so memory latency is hidden within the thread)
-    constexpr int kUnroll = TB > 1 ? 2 : 1;
+    constexpr int kUnroll = TB > 1 ? 2 : 4;
 #pragma unroll kUnroll
     for (int f = lane + 32 * warp; f < quads; f += 256) {
         float4 wv[EB], xv[TB];
@@ -158,8 +153,8 @@ int32_t f32_rows(float *out, const float *w, const float *x, int rows, int cols,
     const bool vec = ((reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(x)) & 15) == 0 && (cols & 3) == 0;
     // Tiles of EB rows x TB tokens, sized so a 256-row router gives 128-512
     // CTAs (two rows per CTA measured ~3 us faster than four at 32 tokens).
-    if (vec && batch <= 1) {
-        f32_tile_kernel<2, 1><<<dim3((rows + 1) / 2, 1), 256, 0, s>>>(out, w, x, rows, cols, batch, token_major);
+    if (vec && batch <= 1) {  // one row per CTA: a 256-row router spreads over the SMs
+        f32_tile_kernel<1, 1><<<dim3(rows, 1), 256, 0, s>>>(out, w, x, rows, cols, batch, token_major);
         return launch_status("f32_tile_kernel");
     }
     if (vec && batch <= 8) {

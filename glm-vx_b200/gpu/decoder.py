@@ -77,8 +77,10 @@ class SyntheticWeights:
     dense MLP, Q4_K attention projections, Q8_0 embedding and lm_head, F32
     routers, indexer head weights and kv_b."""
 
-    def __init__(self, config, seed=0):
-        self.config, self.seed = dict(config), int(seed)
+    def __init__(self, config, seed=0, attention_kind=None):
+        """attention_kind: GGML kind of the attention projections (default
+        Q4_K where the width allows, as config 4; 8 for config 3's Q8_0)."""
+        self.config, self.seed, self.attention_kind = dict(config), int(seed), attention_kind
 
     def fill(self, lib, ptr, kind, count, scale, key, ones, stream):
         """Generate tensor `key` at device address ptr (its seed is a hash of
@@ -95,6 +97,8 @@ class SyntheticWeights:
             return 0
         if '.mlp.' in name:
             return 19
+        if self.attention_kind is not None:
+            return self.attention_kind
         return 12 if shape[1] % 256 == 0 else 8
 
     @staticmethod
@@ -408,6 +412,20 @@ class ResidentDecoder:
             L['moe'].forward_device(self.ffn, self.n, B)
         self._check(self.lib.glmvx_add(self.x, self.x, self.ffn, B * H, self.s), 'glmvx_add')
 
+    def attention_graph(self, layer=0):
+        """A CUDA graph of layer `layer`'s attention sub-step alone (rmsnorm,
+        projections, indexer, cache append, DSA attention, o_proj, residual)
+        on the current hidden rows, for measuring it apart from the step."""
+        L = self.layers[layer]
+        g = rt.Graph(self.backend.stream)
+        g.begin()
+        try:
+            self._rmsnorm(self.n, self.x, L['in_norm'], self.hidden, self.eps)
+            self._attention(layer, L, None)
+        finally:
+            g.end()
+        return g
+
     def _step_launches(self):
         """One decode step on the device: embed self.tokens, the layers, the
         logits, the argmax written back into self.tokens."""
@@ -491,6 +509,13 @@ class ResidentDecoder:
                 self.step()
         self.check()
         return np.stack(out, axis=1), (np.stack(logits, axis=1) if with_logits else None)
+
+    def reset_slot(self, b):
+        """Empty sequence b's caches in every layer (its length to 0)."""
+        if not 0 <= b < self.B:
+            raise ValueError('slot outside the batch')
+        for L in self.layers:
+            rt.call('glmvx_memset', L['lens'].ptr + 4 * b, 0, 4, self.s)
 
     def reset(self):
         """Empty every cache (lengths to 0)."""

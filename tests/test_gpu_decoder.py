@@ -153,3 +153,41 @@ def test_expert_parallel_decoder_on_two_gpus(tmp_path):
         assert p.exitcode == 0
     got = np.concatenate([np.load(tmp_path / f'r{r}.npy') for r in range(2)])
     assert got.tolist() == want
+
+
+def test_batch_scheduler_matches_reference(gpu_backend, reference_runs):
+    """gpu/serving.py over 2 decoder slots, 4 requests (slots reused after a
+    request leaves): every greedy request's tokens equal the reference
+    model's own greedy decode of its prompt; a sampled request (temperature
+    > 0) is reproducible from its seed; status and the reference's
+    validation messages hold."""
+    from gpu.decoder import ResidentDecoder
+    from gpu.serving import BatchScheduler, BusyError, collect
+    config, ckpt, runs = reference_runs
+    dec = ResidentDecoder(gpu_backend, config, ckpt, batch=2, capacity=32)
+    sched = BatchScheduler(dec)
+    try:
+        with pytest.raises(ValueError, match='nonempty'):
+            sched.submit([], 4)
+        with pytest.raises(ValueError, match='context'):
+            sched.submit([1] * 30, 8)
+        reqs = [sched.submit(list(PROMPTS[0]), NEW_TOKENS), sched.submit(list(PROMPTS[1]), NEW_TOKENS)]
+        with pytest.raises(BusyError):
+            sched.submit([1, 2], 2)  # both slots taken
+        out = [collect(r) for r in reqs]
+        for (tokens, done), want in zip(out, runs[:2]):
+            assert done['reason'] == 'length' and done['completion_tokens'] == NEW_TOKENS
+            assert tokens == want[0]
+        r2 = sched.submit(list(PROMPTS[2]), NEW_TOKENS)
+        s1 = sched.submit(list(PROMPTS[0]), 5, temperature=0.7, seed=11)
+        t2, _ = collect(r2)
+        assert t2 == runs[2][0]
+        ts1, _ = collect(s1)
+        s2 = sched.submit(list(PROMPTS[0]), 5, temperature=0.7, seed=11)
+        ts2, _ = collect(s2)
+        assert ts1 == ts2 and len(ts1) == 5
+        assert sched.status()['error'] is None and sched.status()['active_requests'] == 0
+    finally:
+        sched.close()
+        dec.check()
+        dec.close()

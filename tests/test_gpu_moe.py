@@ -214,3 +214,44 @@ def test_moe_pinned_io_and_nonfinite_input(gpu_backend, oracle):
         assert np.linalg.norm(y - want) / np.linalg.norm(want) <= RTOL
     finally:
         moe.close()
+
+
+@pytest.mark.parametrize('T', [1, 5, 32, 64, 65])
+def test_layer_routing_equals_router_kernel(gpu_backend, T):
+    """Up to 64 tokens over up to 256 experts the grouping kernel routes the
+    tokens itself (a warp per token); beyond, the separate router kernel
+    runs.  Either way the layer's ids and weights are byte-identical to
+    glmvx_router on the same logits (glmvx_matmul_nt of the same rows)."""
+    import ctypes as C
+    from gpu import runtime as rt
+    from gpu.moe import MoELayer
+    E, H, I, K = 256, 2048, 2048, 8
+    layer = synthetic_layer(E, H, I, seed=90)
+    # ties and extremes in the router: duplicate expert rows tie their scores
+    layer['router'][7] = layer['router'][3]
+    layer['bias'][7] = layer['bias'][3]
+    moe = MoELayer(gpu_backend, layer['router'], layer['bias'], 19, layer['gate'], layer['up'], layer['down'],
+                   H, I, K, 2.5, shared=layer['shared'])
+    lib, s = gpu_backend.lib, gpu_backend.stream.handle
+    x = np.random.default_rng(T).normal(size=(T, H)).astype(np.float32)
+    x[0] = layer['router'][3] * 40.0  # a token that favours the tied pair
+    bufs = [rt.DeviceBuffer(n) for n in (x.nbytes, 4 * T * E, 4 * T * K, 4 * T * K)]
+    try:
+        y, ids, w = moe.forward(x)
+        xd, ld, idd, wd = bufs
+        xd.upload(x, s)
+        rt.check(lib, lib.glmvx_matmul_nt(ld.ptr, xd.ptr, moe.router_w, T, E, H, s), 'matmul_nt')
+        rt.check(lib, lib.glmvx_router(idd.ptr, wd.ptr, ld.ptr, moe.router_bias, T, E, K, C.c_float(2.5), s),
+                 'router')
+        want_ids, want_w = np.empty((T, K), np.int32), np.empty((T, K), np.float32)
+        gpu_backend.stream.synchronize()
+        idd.download(want_ids)
+        wd.download(want_w)
+        assert ids.tolist() == want_ids.tolist()
+        assert w.tobytes() == want_w.tobytes()
+        assert 3 in ids[0] and 7 in ids[0] and list(ids[0]).index(3) < list(ids[0]).index(7)
+    finally:
+        gpu_backend.stream.synchronize()
+        for b in bufs:
+            b.close()
+        moe.close()
