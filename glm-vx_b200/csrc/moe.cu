@@ -109,68 +109,20 @@ struct LocalJobSrc {
     __device__ float *out_shared(int, int r) const { return pair_out + static_cast<size_t>(r) * hidden; }
 };
 
-// One warp routes one token over experts <= 256 (expert e = 32 j + lane, j <
-// 8, in registers), with router_kernel's rules exactly (ops.cu,
-// kernels/kernels.vx:252-279): score sigmoid(logit) + bias, a NaN score
-// ranked -inf; k rounds of the largest score, the lower id on ties, the
-// chosen expert removed; weights = the chosen sigmoids over their sum in
-// selection order + 1e-20, times scale.  Ids and weights are bit-identical
-// to router_kernel's.
-constexpr int kWarpRouteExperts = 256, kWarpRouteMaxTokens = 64;
-__device__ void route_token_warp(const float *lr, const float *bias, int E, int k, float scale, int32_t *ids_out,
-                                 float *w_out, int lane) {
-    float sc[8];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-        const int e = 32 * j + lane;
-        if (e < E) {
-            const float v = sigmoid_ref(lr[e]) + bias[e];
-            sc[j] = isnan(v) ? -INFINITY : v;
-        } else {
-            sc[j] = __int_as_float(0x7fc00000);  // beyond the experts: never chosen
-        }
-    }
-    float total = 0.0f;
-    for (int slot = 0; slot < k; ++slot) {
-        float bv = -INFINITY;
-        int bi = INT_MAX;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            const int e = 32 * j + lane;
-            if (sc[j] > bv || (sc[j] == bv && e < bi)) {
-                bv = sc[j];
-                bi = e;
-            }
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-            if (ov > bv || (ov == bv && oi < bi)) {
-                bv = ov;
-                bi = oi;
-            }
-        }
-#pragma unroll
-        for (int j = 0; j < 8; ++j)
-            if (32 * j + lane == bi) sc[j] = __int_as_float(0x7fc00000);
-        if (lane == 0) {
-            const float p = sigmoid_ref(lr[bi]);
-            ids_out[slot] = bi;
-            w_out[slot] = p;
-            total = total + p;
-        }
-    }
-    if (lane == 0) {
-        total = total + 1e-20f;
-        for (int slot = 0; slot < k; ++slot) w_out[slot] = w_out[slot] / total * scale;
-    }
-}
+// Small batches are routed inside the grouping kernel (one launch less on
+// the latency-bound decode path), with router_kernel's rules exactly (ops.cu,
+// kernels/kernels.vx:252-279): score = sigmoid(logit) + bias, a NaN score
+// ranked -inf; the experts ranked 0..k-1 by (larger score, then lower id) are
+// the k picks in selection order; weight = the pick's sigmoid over the picks'
+// sigmoids summed in that order + 1e-20, times scale.  Every (token, expert)
+// is ranked by one thread against the token's row of scores in shared
+// memory, so the ids and weights are byte-identical to router_kernel's.
+constexpr int kFusedRouteExperts = 256, kFusedRouteTokens = 2;
 
 // Rank each (token, slot) assignment by (expert id, token): the rank is its
 // pair index, so pairs of one expert are contiguous and ordered by token.
-// With `logits` set the kernel first routes every token itself (a warp per
-// token, route_token_warp), writing ids / wts.
+// With `logits` set the kernel first routes every token itself (small
+// batches, see kFusedRouteTokens), writing ids / wts.
 // With mjobs set (tensor-core path) the job lists come from form_mma_jobs
 // (moe_jobs.cuh): two tokens per job, and with qjobs set too experts routed
 // three or more pairs and the shared expert in a list of four tokens per job.
@@ -184,14 +136,38 @@ __global__ void __launch_bounds__(kGroupThreads)
                      const uint8_t *xprep, size_t xstride, const uint8_t *hprep, size_t hstride, const float *logits,
                      const float *bias, float scale) {
     __shared__ GroupSmem g;
+    __shared__ float route_score[kFusedRouteTokens * kFusedRouteExperts];
     const int n = T * k;
     const int P = n + (shared ? T : 0);
     const bool mma = gu_m != nullptr;
-    if (logits) {
-        const int lane = threadIdx.x & 31;
-        for (int t = threadIdx.x >> 5; t < T; t += kGroupThreads / 32)
-            route_token_warp(logits + static_cast<size_t>(t) * E, bias, E, k, scale, ids + static_cast<size_t>(t) * k,
-                             wts + static_cast<size_t>(t) * k, lane);
+    if (logits) {  // T <= kFusedRouteTokens, E <= kFusedRouteExperts (host-checked)
+        for (int i = threadIdx.x; i < T * E; i += blockDim.x) {
+            const int e = i % E;
+            const float v = sigmoid_ref(logits[i]) + bias[e];
+            route_score[i] = isnan(v) ? -INFINITY : v;
+        }
+        __syncthreads();
+        for (int i = threadIdx.x; i < T * E; i += blockDim.x) {
+            const int t = i / E, e = i % E;
+            const float *row = route_score + t * E;
+            const float v = row[e];
+            int rank = 0;
+            for (int f = 0; f < E; ++f) {
+                const float u = row[f];
+                rank += (u > v) | ((u == v) & (f < e));
+            }
+            if (rank < k) {
+                ids[t * k + rank] = e;
+                wts[t * k + rank] = sigmoid_ref(logits[i]);
+            }
+        }
+        __syncthreads();
+        for (int t = threadIdx.x; t < T; t += blockDim.x) {
+            float total = 0.0f;
+            for (int s = 0; s < k; ++s) total = total + wts[t * k + s];
+            total = total + 1e-20f;
+            for (int s = 0; s < k; ++s) wts[t * k + s] = wts[t * k + s] / total * scale;
+        }
         __syncthreads();  // the block's writes to ids / wts are visible to every thread
     }
     for (int a = threadIdx.x; a < n; a += blockDim.x) {
@@ -353,7 +329,7 @@ static int32_t moe_ffn(float *y, const float *x, int32_t tokens, int32_t hidden,
                       mma_quad_supported(kind, inter);
     // Up to 64 tokens over up to 256 experts: the grouping kernel routes the
     // tokens itself (a warp per token) instead of a separate router launch.
-    const bool fused_route = !given_ids && experts <= kWarpRouteExperts && tokens <= kWarpRouteMaxTokens;
+    const bool fused_route = !given_ids && experts <= kFusedRouteExperts && tokens <= kFusedRouteTokens;
     int32_t st_ = mark(0);
     if (st_) return st_;
     if (mma && (st_ = prep_rows_device(w.xprep, x, nullptr, tokens, hidden, st))) return st_;

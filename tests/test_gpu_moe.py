@@ -216,11 +216,11 @@ def test_moe_pinned_io_and_nonfinite_input(gpu_backend, oracle):
         moe.close()
 
 
-@pytest.mark.parametrize('T', [1, 5, 32, 64, 65])
+@pytest.mark.parametrize('T', [1, 2, 3, 32, 65])
 def test_layer_routing_equals_router_kernel(gpu_backend, T):
-    """Up to 64 tokens over up to 256 experts the grouping kernel routes the
-    tokens itself (a warp per token); beyond, the separate router kernel
-    runs.  Either way the layer's ids and weights are byte-identical to
+    """Up to 2 tokens over up to 256 experts the grouping kernel routes the
+    tokens itself (every (token, expert) score ranked by one thread); beyond,
+    the separate router kernel runs.  Either way the layer's ids and weights are byte-identical to
     glmvx_router on the same logits (glmvx_matmul_nt of the same rows)."""
     import ctypes as C
     from gpu import runtime as rt
