@@ -370,7 +370,7 @@ def graph_time(rt, stream, fn, reps, ranks=None, clocks=None):
     return ms
 
 
-PATH_NAMES = {1: 'stream', 2: 'generic', 5: 'mma_int8', 6: 'gemm_f16'}
+PATH_NAMES = {1: 'stream', 2: 'generic', 5: 'mma_int8', 6: 'gemm_f16', 7: 'mma_int8_col_segments', 8: 'gemm_f16_col_segments'}
 
 
 def fused_gemv_sweep(rt, lib, dev, stream, steps, peak):
@@ -915,6 +915,8 @@ def run_profile_case(args):
         return profile_decoder()
     if args.profile_case == 'packed_gemm':
         return profile_packed_gemm()
+    if args.profile_case in ('attention3', 'attention3_16'):
+        return profile_attention3(16 if args.profile_case == 'attention3_16' else 1)
     from gpu.backend import GPUBackend
     from gpu import runtime as rt
     from gpu.moe import MoELayer
@@ -952,6 +954,34 @@ def profile_decoder(layers=4, steps=2):
         dec._step_launches()
     dec.check()
     print(f'profile case ok: config-4 decoder, {layers} layers, 64 sequences, {steps} steps', flush=True)
+    dec.close()
+    backend.close()
+    return 0
+
+
+def profile_attention3(B, steps=2):
+    """Config 3's attention sub-step with its Q8_0 projections (the resident
+    decoder's layer-0 attention at config-3 widths, B queries over 32768
+    synthetic cache rows), `steps` eager passes so a launch list shows every
+    kernel."""
+    from gpu.backend import GPUBackend
+    from gpu.decoder import ResidentDecoder, SyntheticWeights
+    backend = GPUBackend(0)
+    cfg = dict(CONFIG4, num_hidden_layers=1, first_k_dense_replace=1,
+               rope_parameters={'rope_theta': 1000000, 'rope_type': 'default'})
+    dec = ResidentDecoder(backend, cfg, SyntheticWeights(cfg, seed=33, attention_kind=8), batch=B,
+                          capacity=DSA_CONTEXT + 8 + steps, layers=1)
+    dec.fill_caches(DSA_CONTEXT)
+    dec.set_tokens(np.arange(B) * 11)
+    from gpu import runtime as rt
+    rt.check(backend.lib, backend.lib.glmvx_embed_rows(dec.x, dec.embed[0], dec.embed[1], dec.tokens, B, dec.vocab,
+                                                       dec.hidden, dec.s), 'glmvx_embed_rows')
+    L = dec.layers[0]
+    for _ in range(steps):
+        dec._rmsnorm(dec.n, dec.x, L['in_norm'], dec.hidden, dec.eps)
+        dec._attention(0, L, None)
+    dec.check()
+    print(f'profile case ok: config-3 attention with projections, {B} queries, {steps} steps', flush=True)
     dec.close()
     backend.close()
     return 0
@@ -1044,7 +1074,8 @@ def main():
     ap.add_argument('--cpu-seconds', type=float, default=10.0)
     ap.add_argument('--no-cpu-baseline', action='store_true')
     ap.add_argument('--no-decoder', action='store_true', help='skip the config-4 decoder measurement')
-    ap.add_argument('--profile-case', nargs='?', const='moe', choices=('moe', 'gemm', 'dsa', 'dsa1', 'decoder', 'packed_gemm'),
+    ap.add_argument('--profile-case', nargs='?', const='moe', choices=('moe', 'gemm', 'dsa', 'dsa1', 'decoder', 'packed_gemm',
+                                                                 'attention3', 'attention3_16'),
                     help='run a small kernel-capture case (one GPU) instead of the benchmark')
     args = ap.parse_args()
     if args.profile_case:

@@ -31,6 +31,9 @@ namespace glmvx {
 namespace {
 
 constexpr int kDecThreads = 256;
+// Loads a thread issues before it consumes any of them: a strided row loop
+// written plainly waits out one memory latency per element.
+constexpr int kRowBatch = 8;
 
 __global__ void embed_rows_kernel(float *out, const uint8_t *table, int kind, const int32_t *ids, int vocab,
                                   int hidden, int *err) {
@@ -41,16 +44,34 @@ __global__ void embed_rows_kernel(float *out, const uint8_t *table, int kind, co
         id = min(max(id, 0), vocab - 1);
     }
     float *o = out + static_cast<size_t>(b) * hidden;
+    const int step = blockDim.x;
     if (kind == 0) {
         const float *row = reinterpret_cast<const float *>(table) + static_cast<size_t>(id) * hidden;
-        for (int i = threadIdx.x; i < hidden; i += blockDim.x) o[i] = row[i];
+        int i = threadIdx.x;
+        for (; i + (kRowBatch - 1) * step < hidden; i += kRowBatch * step) {
+            float v[kRowBatch];
+#pragma unroll
+            for (int u = 0; u < kRowBatch; ++u) v[u] = row[i + u * step];
+#pragma unroll
+            for (int u = 0; u < kRowBatch; ++u) o[i + u * step] = v[u];
+        }
+        for (; i < hidden; i += step) o[i] = row[i];
         return;
     }
     const uint8_t *row = table + static_cast<size_t>(id) * (hidden / 32) * 34;  // Q8_0
-    for (int i = threadIdx.x; i < hidden; i += blockDim.x) {
+    auto elem = [&](int i) {
         const uint8_t *blk = row + (i / 32) * 34;
-        o[i] = h2f(u16(blk)) * static_cast<float>(static_cast<int8_t>(blk[2 + i % 32]));
+        return h2f(u16(blk)) * static_cast<float>(static_cast<int8_t>(blk[2 + i % 32]));
+    };
+    int i = threadIdx.x;
+    for (; i + (kRowBatch - 1) * step < hidden; i += kRowBatch * step) {
+        float v[kRowBatch];
+#pragma unroll
+        for (int u = 0; u < kRowBatch; ++u) v[u] = elem(i + u * step);
+#pragma unroll
+        for (int u = 0; u < kRowBatch; ++u) o[i + u * step] = v[u];
     }
+    for (; i < hidden; i += step) o[i] = elem(i);
 }
 
 struct RopeRows {
@@ -93,69 +114,141 @@ __global__ void rmsnorm_rows_kernel(float *out, const float *x, const float *w, 
     __shared__ float partial[kDecThreads / 32];
     const float *xr = x + blockIdx.x * x_stride;
     float *orow = out + blockIdx.x * out_stride;
+    const int step = blockDim.x;
     float ss = 0.0f;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) ss = fmaf(xr[i], xr[i], ss);
+    int i = threadIdx.x;
+    for (; i + (kRowBatch - 1) * step < n; i += kRowBatch * step) {  // same order as one element at a time
+        float v[kRowBatch];
+#pragma unroll
+        for (int u = 0; u < kRowBatch; ++u) v[u] = xr[i + u * step];
+#pragma unroll
+        for (int u = 0; u < kRowBatch; ++u) ss = fmaf(v[u], v[u], ss);
+    }
+    for (; i < n; i += step) ss = fmaf(xr[i], xr[i], ss);
     ss = warp_sum(ss);
     if ((threadIdx.x & 31) == 0) partial[threadIdx.x >> 5] = ss;
     __syncthreads();
     float tot = 0.0f;
-    for (int i = 0; i < kDecThreads / 32; ++i) tot += partial[i];
+    for (int k = 0; k < kDecThreads / 32; ++k) tot += partial[k];
     const float inv = 1.0f / sqrtf(tot / static_cast<float>(n) + eps);
-    for (int i = threadIdx.x; i < n; i += blockDim.x) orow[i] = __fmul_rn(__fmul_rn(xr[i], inv), w[i]);
+    i = threadIdx.x;
+    for (; i + (kRowBatch - 1) * step < n; i += kRowBatch * step) {
+        float v[kRowBatch], g[kRowBatch];
+#pragma unroll
+        for (int u = 0; u < kRowBatch; ++u) {
+            v[u] = xr[i + u * step];
+            g[u] = w[i + u * step];
+        }
+#pragma unroll
+        for (int u = 0; u < kRowBatch; ++u) orow[i + u * step] = __fmul_rn(__fmul_rn(v[u], inv), g[u]);
+    }
+    for (; i < n; i += step) orow[i] = __fmul_rn(__fmul_rn(xr[i], inv), w[i]);
 }
 
 // q_latent[b][h][r] = sum_j kv_b[h][j][r] * query[b][h][j], j < nope, serial
-// in j.  CTA: one head, kTok sequences, threads over r.
-constexpr int kAbsorbTok = 8;
-__global__ void __launch_bounds__(kDecThreads)
-    absorb_query_kernel(float *q_latent, const float *query, const float *kvb, int tokens, int heads, int nope,
-                        int qk_head, int rank, int vdim) {
-    extern __shared__ float qs[];  // [kAbsorbTok][nope]
-    const int h = blockIdx.x, b0 = blockIdx.y * kAbsorbTok;
-    const int nb = min(kAbsorbTok, tokens - b0);
-    for (int i = threadIdx.x; i < nb * nope; i += blockDim.x) {
-        const int tb = i / nope, j = i % nope;
-        qs[tb * nope + j] = query[(static_cast<size_t>(b0 + tb) * heads + h) * qk_head + j];
-    }
-    __syncthreads();
-    const float *w = kvb + static_cast<size_t>(h) * (nope + vdim) * rank;
-    for (int r = threadIdx.x; r < rank; r += blockDim.x) {
-        float acc[kAbsorbTok];
+// in j.  A thread owns one r of one head for KT sequences (the weight read
+// once for all of them); it loads U weights of its column before it adds
+// any, so the loads of a column overlap while the sum keeps its order.
+// Grid: (rank / kAbsorbThreads, heads, sequence groups of KT).
+constexpr int kAbsorbThreads = 128, kAbsorbTok = 8;
+
+// v[u] = p[u * stride] for u < U, all U loads issued before any is used: the
+// loads are volatile PTX in program order, and the empty statements that
+// read and rewrite the values keep every use behind the last load.
+template <int U>
+__device__ __forceinline__ void load_column(float (&v)[U], const float *p, size_t stride) {
+    static_assert(U % 8 == 0, "loads in groups of eight");
 #pragma unroll
-        for (int tb = 0; tb < kAbsorbTok; ++tb) acc[tb] = 0.0f;
-        for (int j = 0; j < nope; ++j) {
-            const float wv = w[static_cast<size_t>(j) * rank + r];
+    for (int u = 0; u < U; ++u) asm volatile("ld.global.nc.f32 %0, [%1];" : "=f"(v[u]) : "l"(p + u * stride));
 #pragma unroll
-            for (int tb = 0; tb < kAbsorbTok; ++tb) acc[tb] = __fadd_rn(acc[tb], __fmul_rn(wv, qs[tb * nope + j]));
-        }
-        for (int tb = 0; tb < nb; ++tb) q_latent[(static_cast<size_t>(b0 + tb) * heads + h) * rank + r] = acc[tb];
-    }
+    for (int u = 0; u < U; u += 8)
+        asm volatile("" : "+f"(v[u]), "+f"(v[u + 1]), "+f"(v[u + 2]), "+f"(v[u + 3]), "+f"(v[u + 4]), "+f"(v[u + 5]),
+                     "+f"(v[u + 6]), "+f"(v[u + 7]));
 }
 
-// out[b][h*vdim + i] = sum_r kvbo_t[h][r][i] * att[b][h][r], serial in r;
-// kvbo_t is kv_b[h, nope:] transposed to [heads][rank][vdim] at load time.
-__global__ void __launch_bounds__(kDecThreads)
-    absorb_value_kernel(float *out, const float *att, const float *kvbo_t, int tokens, int heads, int rank, int vdim) {
-    extern __shared__ float as[];  // [kAbsorbTok][rank]
-    const int h = blockIdx.x, b0 = blockIdx.y * kAbsorbTok;
-    const int nb = min(kAbsorbTok, tokens - b0);
-    for (int i = threadIdx.x; i < nb * rank; i += blockDim.x) {
-        const int tb = i / rank, r = i % rank;
-        as[tb * rank + r] = att[(static_cast<size_t>(b0 + tb) * heads + h) * rank + r];
+template <int KT, int U>
+__global__ void __launch_bounds__(kAbsorbThreads)
+    absorb_query_kernel(float *q_latent, const float *query, const float *kvb, int tokens, int heads, int nope,
+                        int qk_head, int rank, int vdim) {
+    extern __shared__ float qs[];  // [KT][nope]
+    const int h = blockIdx.y, b0 = blockIdx.z * KT;
+    const int nb = min(KT, tokens - b0);
+    for (int i = threadIdx.x; i < KT * nope; i += blockDim.x) {
+        const int tb = i / nope, j = i % nope;
+        qs[i] = tb < nb ? query[(static_cast<size_t>(b0 + tb) * heads + h) * qk_head + j] : 0.0f;
     }
     __syncthreads();
-    const float *w = kvbo_t + static_cast<size_t>(h) * rank * vdim;
-    for (int i = threadIdx.x; i < vdim; i += blockDim.x) {
-        float acc[kAbsorbTok];
+    const int r = blockIdx.x * blockDim.x + threadIdx.x;
+    if (r >= rank) return;
+    const float *w = kvb + static_cast<size_t>(h) * (nope + vdim) * rank + r;
+    float acc[KT];
 #pragma unroll
-        for (int tb = 0; tb < kAbsorbTok; ++tb) acc[tb] = 0.0f;
-        for (int r = 0; r < rank; ++r) {
-            const float wv = w[static_cast<size_t>(r) * vdim + i];
+    for (int tb = 0; tb < KT; ++tb) acc[tb] = 0.0f;
+    int j = 0;
+    for (; j + U <= nope; j += U) {
+        float wv[U];
+        load_column(wv, w + static_cast<size_t>(j) * rank, rank);
 #pragma unroll
-            for (int tb = 0; tb < kAbsorbTok; ++tb) acc[tb] = __fadd_rn(acc[tb], __fmul_rn(wv, as[tb * rank + r]));
-        }
-        for (int tb = 0; tb < nb; ++tb) out[static_cast<size_t>(b0 + tb) * heads * vdim + h * vdim + i] = acc[tb];
+        for (int u = 0; u < U; ++u)
+#pragma unroll
+            for (int tb = 0; tb < KT; ++tb) acc[tb] = __fadd_rn(acc[tb], __fmul_rn(wv[u], qs[tb * nope + j + u]));
     }
+    for (; j < nope; ++j) {
+        const float wv = __ldg(w + static_cast<size_t>(j) * rank);
+#pragma unroll
+        for (int tb = 0; tb < KT; ++tb) acc[tb] = __fadd_rn(acc[tb], __fmul_rn(wv, qs[tb * nope + j]));
+    }
+#pragma unroll
+    for (int tb = 0; tb < KT; ++tb)
+        if (tb < nb) q_latent[(static_cast<size_t>(b0 + tb) * heads + h) * rank + r] = acc[tb];
+}
+
+// out[b][h*vdim + i] = sum_r kv_b[h][nope + i][r] * att[b][h][r], serial in
+// r.  A thread owns output column i of one head for KT sequences and reads
+// its contiguous kv_b row as float4s, U4 of them (4*U4 weights) issued
+// before any is added.  Grid: (vdim / kAbsorbThreads, heads, groups of KT).
+template <int KT, int U4>
+__global__ void __launch_bounds__(kAbsorbThreads)
+    absorb_value_kernel(float *out, const float *att, const float *kvb, int tokens, int heads, int nope, int rank,
+                        int vdim) {
+    extern __shared__ float as[];  // [KT][rank]
+    const int h = blockIdx.y, b0 = blockIdx.z * KT;
+    const int nb = min(KT, tokens - b0);
+    for (int i = threadIdx.x; i < KT * rank; i += blockDim.x) {
+        const int tb = i / rank, r = i % rank;
+        as[i] = tb < nb ? att[(static_cast<size_t>(b0 + tb) * heads + h) * rank + r] : 0.0f;
+    }
+    __syncthreads();
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= vdim) return;
+    const float *w = kvb + (static_cast<size_t>(h) * (nope + vdim) + nope + i) * rank;
+    float acc[KT];
+#pragma unroll
+    for (int tb = 0; tb < KT; ++tb) acc[tb] = 0.0f;
+    auto add = [&](float wv, int r) {
+#pragma unroll
+        for (int tb = 0; tb < KT; ++tb) acc[tb] = __fadd_rn(acc[tb], __fmul_rn(wv, as[tb * rank + r]));
+    };
+    int r = 0;
+    if ((rank & 3) == 0) {  // rows start 16-byte aligned
+        const float4 *w4 = reinterpret_cast<const float4 *>(w);
+        for (; r + 4 * U4 <= rank; r += 4 * U4) {
+            float4 v[U4];
+#pragma unroll
+            for (int u = 0; u < U4; ++u) v[u] = __ldg(w4 + r / 4 + u);
+#pragma unroll
+            for (int u = 0; u < U4; ++u) {
+                add(v[u].x, r + 4 * u);
+                add(v[u].y, r + 4 * u + 1);
+                add(v[u].z, r + 4 * u + 2);
+                add(v[u].w, r + 4 * u + 3);
+            }
+        }
+    }
+    for (; r < rank; ++r) add(__ldg(w + r), r);
+#pragma unroll
+    for (int tb = 0; tb < KT; ++tb)
+        if (tb < nb) out[static_cast<size_t>(b0 + tb) * heads * vdim + h * vdim + i] = acc[tb];
 }
 
 __global__ void scale_kernel(float *out, const float *x, float s, int64_t n) {
@@ -165,28 +258,44 @@ __global__ void scale_kernel(float *out, const float *x, float s, int64_t n) {
 }
 
 // One CTA per row: the largest value, ties to the smallest index; a NaN
-// anywhere makes its first index the answer (numpy argmax).
-__global__ void argmax_rows_kernel(int32_t *ids, const float *logits, int n) {
-    __shared__ float sv[kDecThreads / 32];
-    __shared__ int si[kDecThreads / 32];
+// anywhere makes its first index the answer (numpy argmax).  Each thread
+// scans its indices in increasing order, kRowBatch loads at a time.
+constexpr int kArgmaxThreads = 1024;
+
+// (v, j) replaces (best, bi) under the rule above.
+__device__ __forceinline__ bool argmax_takes(float v, int j, float best, int bi) {
+    const bool vn = v != v, bn = best != best;
+    return (vn && !bn) || (vn == bn && (vn ? j < bi : (v > best || (v == best && j < bi))));
+}
+
+__global__ void __launch_bounds__(kArgmaxThreads) argmax_rows_kernel(int32_t *ids, const float *logits, int n) {
+    __shared__ float sv[kArgmaxThreads / 32];
+    __shared__ int si[kArgmaxThreads / 32];
     const float *row = logits + static_cast<size_t>(blockIdx.x) * n;
+    const int step = blockDim.x;
     float best = -INFINITY;
     int bi = n;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) {
-        const float v = row[i];
+    auto scan = [&](float v, int i) {
         const bool nan = v != v, bnan = best != best;
         if ((nan && !bnan) || (!bnan && v > best)) {  // strictly better, or the first NaN
             best = v;
             bi = i;
         }
+    };
+    int i = threadIdx.x;
+    for (; i + (kRowBatch - 1) * step < n; i += kRowBatch * step) {
+        float v[kRowBatch];
+#pragma unroll
+        for (int u = 0; u < kRowBatch; ++u) v[u] = row[i + u * step];
+#pragma unroll
+        for (int u = 0; u < kRowBatch; ++u) scan(v[u], i + u * step);
     }
+    for (; i < n; i += step) scan(row[i], i);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
         const float v = __shfl_xor_sync(0xffffffffu, best, o);
         const int j = __shfl_xor_sync(0xffffffffu, bi, o);
-        const bool vn = v != v, bn = best != best;
-        const bool take = (vn && !bn) || (vn == bn && (vn ? j < bi : (v > best || (v == best && j < bi))));
-        if (take) {
+        if (argmax_takes(v, j, best, bi)) {
             best = v;
             bi = j;
         }
@@ -197,13 +306,10 @@ __global__ void argmax_rows_kernel(int32_t *ids, const float *logits, int n) {
     }
     __syncthreads();
     if (threadIdx.x == 0) {
-        for (int w = 1; w < kDecThreads / 32; ++w) {
-            const float v = sv[w];
-            const int j = si[w];
-            const bool vn = v != v, bn = best != best;
-            if ((vn && !bn) || (vn == bn && (vn ? j < bi : (v > best || (v == best && j < bi))))) {
-                best = v;
-                bi = j;
+        for (int w = 1; w < static_cast<int>(blockDim.x) / 32; ++w) {
+            if (argmax_takes(sv[w], si[w], best, bi)) {
+                best = sv[w];
+                bi = si[w];
             }
         }
         ids[blockIdx.x] = bi < n ? bi : 0;
@@ -308,25 +414,41 @@ GLMVX_EXPORT int32_t glmvx_rmsnorm_rows(float *out, const float *x, const float 
 GLMVX_EXPORT int32_t glmvx_absorb_query(float *q_latent, const float *query, const float *kvb, int32_t tokens,
                                         int32_t heads, int32_t nope, int32_t qk_head, int32_t rank, int32_t vdim,
                                         void *stream) {
-    if (tokens < 0 || heads <= 0 || nope <= 0 || qk_head < nope || rank <= 0 || vdim < 0 ||
+    if (tokens < 0 || heads <= 0 || heads > 65535 || nope <= 0 || qk_head < nope || rank <= 0 || vdim < 0 ||
         nope * kAbsorbTok * 4 > 48 * 1024)
         return set_error("absorb_query: invalid dimensions"), kInvalid;
     if (!tokens) return kOk;
-    const dim3 grid(heads, (tokens + kAbsorbTok - 1) / kAbsorbTok);
-    absorb_query_kernel<<<grid, kDecThreads, kAbsorbTok * nope * 4, static_cast<cudaStream_t>(stream)>>>(
-        q_latent, query, kvb, tokens, heads, nope, qk_head, rank, vdim);
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const unsigned cols = (rank + kAbsorbThreads - 1) / kAbsorbThreads;
+    if (tokens == 1) {
+        absorb_query_kernel<1, 64><<<dim3(cols, heads, 1), kAbsorbThreads, nope * 4, st>>>(q_latent, query, kvb,
+                                                                                          tokens, heads, nope,
+                                                                                          qk_head, rank, vdim);
+    } else {
+        const dim3 grid(cols, heads, (tokens + kAbsorbTok - 1) / kAbsorbTok);
+        absorb_query_kernel<kAbsorbTok, 16><<<grid, kAbsorbThreads, kAbsorbTok * nope * 4, st>>>(
+            q_latent, query, kvb, tokens, heads, nope, qk_head, rank, vdim);
+    }
     return launch_status("absorb_query_kernel");
 }
 
-// att [tokens][heads][rank], kvbo_t [heads][rank][vdim] -> out [tokens][heads * vdim].
-GLMVX_EXPORT int32_t glmvx_absorb_value(float *out, const float *att, const float *kvbo_t, int32_t tokens,
-                                        int32_t heads, int32_t rank, int32_t vdim, void *stream) {
-    if (tokens < 0 || heads <= 0 || rank <= 0 || vdim <= 0 || rank * kAbsorbTok * 4 > 48 * 1024)
+// att [tokens][heads][rank], kvb [heads][nope + vdim][rank] -> out [tokens][heads * vdim].
+GLMVX_EXPORT int32_t glmvx_absorb_value(float *out, const float *att, const float *kvb, int32_t tokens, int32_t heads,
+                                        int32_t nope, int32_t rank, int32_t vdim, void *stream) {
+    if (tokens < 0 || heads <= 0 || heads > 65535 || nope < 0 || rank <= 0 || vdim <= 0 ||
+        rank * kAbsorbTok * 4 > 48 * 1024)
         return set_error("absorb_value: invalid dimensions"), kInvalid;
     if (!tokens) return kOk;
-    const dim3 grid(heads, (tokens + kAbsorbTok - 1) / kAbsorbTok);
-    absorb_value_kernel<<<grid, kDecThreads, kAbsorbTok * rank * 4, static_cast<cudaStream_t>(stream)>>>(
-        out, att, kvbo_t, tokens, heads, rank, vdim);
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const unsigned cols = (vdim + kAbsorbThreads - 1) / kAbsorbThreads;
+    if (tokens == 1) {
+        absorb_value_kernel<1, 8><<<dim3(cols, heads, 1), kAbsorbThreads, rank * 4, st>>>(out, att, kvb, tokens, heads,
+                                                                                         nope, rank, vdim);
+    } else {
+        const dim3 grid(cols, heads, (tokens + kAbsorbTok - 1) / kAbsorbTok);
+        absorb_value_kernel<kAbsorbTok, 4><<<grid, kAbsorbThreads, kAbsorbTok * rank * 4, st>>>(
+            out, att, kvb, tokens, heads, nope, rank, vdim);
+    }
     return launch_status("absorb_value_kernel");
 }
 
@@ -360,6 +482,6 @@ GLMVX_EXPORT int32_t glmvx_fill_random(void *out, int32_t kind, int64_t count, u
 GLMVX_EXPORT int32_t glmvx_argmax_rows(int32_t *ids, const float *logits, int32_t rows, int32_t n, void *stream) {
     if (rows < 0 || n <= 0) return set_error("argmax_rows: invalid dimensions"), kInvalid;
     if (!rows) return kOk;
-    argmax_rows_kernel<<<rows, kDecThreads, 0, static_cast<cudaStream_t>(stream)>>>(ids, logits, n);
+    argmax_rows_kernel<<<rows, kArgmaxThreads, 0, static_cast<cudaStream_t>(stream)>>>(ids, logits, n);
     return launch_status("argmax_rows_kernel");
 }

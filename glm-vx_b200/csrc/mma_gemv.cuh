@@ -41,6 +41,17 @@ struct MmaJob {
     float *out[kMmaSlots];         // out[s][r] for r < rows_per_job
 };
 
+// A column segment of a longer matrix (rows too long for one tensor-core
+// plan run as equal column segments): the weights' global row pitch in
+// bytes (0: the segment's own row length), the f32 activation row stride in
+// floats (0: cols), and whether results add onto `out` (later segments, in
+// segment order) instead of replacing it.
+struct ColSegment {
+    int64_t pitch = 0;
+    int xstride = 0;
+    bool accumulate = false;
+};
+
 // True when `kind` and the column count take the tensor-core path.
 bool mma_supported(int kind, int cols);
 // True when job lists of four tokens per job (pairs = 2) are built for it.
@@ -51,7 +62,7 @@ bool mma_quad_supported(int kind, int cols);
 // rows_dev set, only the first min(*rows_dev, rows) rows (a count written on
 // the device by an earlier kernel; `rows` is then the capacity).
 int32_t prep_rows_device(uint8_t *prep, const float *x, const float *x2, int rows, int cols, cudaStream_t stream,
-                         const int *rows_dev = nullptr);
+                         const int *rows_dev = nullptr, int xstride = 0);
 
 // Tensor-core packed GEMV over a job list.
 //  * jobs != nullptr: device-resident descriptors; the job count is
@@ -66,9 +77,10 @@ int32_t prep_rows_device(uint8_t *prep, const float *x, const float *x2, int row
 //    prepares the rows of the jobs it reaches in shared memory, so no
 //    separate preparation or scratch is needed; returns kUnsupported when the
 //    shape leaves no room for that (use the prepared-row form then).
+//  * seg: single-matrix calls only (jobs == nullptr).
 int32_t mma_gemv_device(int32_t kind, const MmaJob &job0, const MmaJob *jobs, const int *njobs_dev, int max_jobs,
                         int batch, int rows_per_job, int cols, cudaStream_t stream, const float *x_raw = nullptr,
-                        int pairs = 1);
+                        int pairs = 1, const ColSegment &seg = {});
 
 // f16 tensor-core GEMM for token batches (packed_gemm.cu): the weights are
 // decoded once per fragment for every token.  Q4_K, and IQ1_S with cols %
@@ -79,6 +91,6 @@ constexpr int kGemmMinTokens = 8, kGemmMaxTokens = 64;
 bool gemm_f16_supported(int kind, int cols, int batch);
 size_t gemm_f16_scratch_bytes(int cols, int batch);
 int32_t gemm_f16_device(int32_t kind, float *out, const uint8_t *w, const float *x, int rows, int cols, int batch,
-                        uint8_t *scratch, cudaStream_t stream);
+                        uint8_t *scratch, cudaStream_t stream, const ColSegment &seg = {});
 
 }  // namespace glmvx

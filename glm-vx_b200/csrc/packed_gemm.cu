@@ -115,7 +115,8 @@ struct GemmRecord {
 
 // One warp per (token, chunk), 8 columns per lane.
 __global__ void __launch_bounds__(256)
-    prep_f16_kernel(uint8_t *__restrict__ rec, const float *__restrict__ x, int T, int T4, int cols, int nt8) {
+    prep_f16_kernel(uint8_t *__restrict__ rec, const float *__restrict__ x, int T, int T4, int cols, int nt8,
+                    int xstride) {
     grid_dependency_wait();
     allow_dependent_launch();
     const int chunks = cols >> 8;
@@ -127,7 +128,7 @@ __global__ void __launch_bounds__(256)
     uint8_t *out = rec + static_cast<size_t>(chunk) * R.bytes();
     float v[8] = {0, 0, 0, 0, 0, 0, 0, 0};
     if (tok < T) {
-        const float4 *xr = reinterpret_cast<const float4 *>(x + static_cast<size_t>(tok) * cols + chunk * 256 + lane * 8);
+        const float4 *xr = reinterpret_cast<const float4 *>(x + static_cast<size_t>(tok) * xstride + chunk * 256 + lane * 8);
         const float4 lo = __ldg(xr), hi = __ldg(xr + 1);
         v[0] = lo.x, v[1] = lo.y, v[2] = lo.z, v[3] = lo.w, v[4] = hi.x, v[5] = hi.y, v[6] = hi.z, v[7] = hi.w;
     }
@@ -421,7 +422,7 @@ template <class F, int NTW>
 __global__ void __launch_bounds__(13 * 32, 1)
     gemm_f16_kernel(float *__restrict__ out, const uint8_t *__restrict__ w, const uint8_t *__restrict__ rec, int rows,
                     int cols, int T, int nt8, int row_bytes, int srow, int RG, int TG, int S, int nst,
-                    int rec_stride, int a_bytes, int *err) {
+                    int rec_stride, int a_bytes, int64_t pitch, int accumulate, int *err) {
     using GF = GemmFmt<F>;
     extern __shared__ __align__(128) uint8_t smem[];
     const int NW = RG * TG * S, R = 16 * RG, T4 = 4 * nt8;
@@ -467,7 +468,7 @@ __global__ void __launch_bounds__(13 * 32, 1)
             if (lane == 0) mbar_arrive_expect_tx(a_full, static_cast<uint32_t>(nr) * row_bytes);
             __syncwarp();
             for (int r = lane; r < nr; r += 32)
-                bulk_g2s(atile + static_cast<size_t>(r) * srow, w + static_cast<size_t>(r0 + r) * row_bytes, row_bytes,
+                bulk_g2s(atile + static_cast<size_t>(r) * srow, w + static_cast<size_t>(r0 + r) * pitch, row_bytes,
                          a_full);
             for (int c = 0; c < C; ++c) {
                 const int k = i * C + c, s = k % nst;
@@ -530,7 +531,8 @@ __global__ void __launch_bounds__(13 * 32, 1)
             const int tok = idx / nr, r = idx % nr;
             float v = 0.0f;
             for (int q = 0; q < S; ++q) v += red[(static_cast<size_t>(q) * R + r) * T4 + tok];
-            out[static_cast<size_t>(tok) * rows + r0 + r] = v;
+            float *d = out + static_cast<size_t>(tok) * rows + r0 + r;
+            *d = accumulate ? *d + v : v;
         }
         named_barrier_sync(2, NW * 32);  // red is rewritten by the next tile
     }
@@ -601,7 +603,7 @@ bool plan_gemm(int rows, int cols, int batch, int row_bytes, GemmPlan &p) {
 
 template <class F, int NTW>
 int32_t launch_gemm(const GemmPlan &p, float *out, const uint8_t *w, const uint8_t *rec, int rows, int cols, int batch,
-                    int row_bytes, cudaStream_t stream) {
+                    int row_bytes, const ColSegment &seg, cudaStream_t stream) {
     auto kern = gemm_f16_kernel<F, NTW>;
     if (const int32_t rc = allow_dynamic_smem(kern, p.smem, "packed_gemm smem")) return rc;
     cudaLaunchConfig_t cfg = {};
@@ -615,7 +617,8 @@ int32_t launch_gemm(const GemmPlan &p, float *out, const uint8_t *w, const uint8
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     GLMVX_CUDA(cudaLaunchKernelEx(&cfg, kern, out, w, rec, rows, cols, batch, p.nt8, row_bytes, p.srow, p.RG, p.TG, p.S,
-                                  p.nst, p.rec_stride, p.a_bytes, device_error_word()));
+                                  p.nst, p.rec_stride, p.a_bytes, seg.pitch ? seg.pitch : row_bytes,
+                                  static_cast<int>(seg.accumulate), device_error_word()));
     return kOk;
 }
 
@@ -627,7 +630,7 @@ bool gemm_f16_supported(int kind, int cols, int batch) {
 }
 
 int32_t gemm_f16_device(int32_t kind, float *out, const uint8_t *w, const float *x, int rows, int cols, int batch,
-                        uint8_t *scratch, cudaStream_t stream) {
+                        uint8_t *scratch, cudaStream_t stream, const ColSegment &seg) {
     if (!gemm_f16_supported(kind, cols, batch) || rows <= 0) {
         set_error("gemm: unsupported format or shape");
         return kUnsupported;
@@ -639,6 +642,11 @@ int32_t gemm_f16_device(int32_t kind, float *out, const uint8_t *w, const float 
     int blk = 0, bytes = 0;
     reference_layout(kind, blk, bytes);
     const int row_bytes = cols / blk * bytes;
+    if ((seg.pitch && (seg.pitch < row_bytes || seg.pitch % 16)) || (seg.xstride && seg.xstride < cols)) {
+        set_error("gemm: a column segment needs a 16-byte row pitch and strides >= its width");
+        return kInvalid;
+    }
+    const int xstride = seg.xstride ? seg.xstride : cols;
     int32_t st = kUnsupported;
     dispatch_format(kind, [&]<class F>() {
         if constexpr (std::is_same_v<F, FmtQ4_K> || std::is_same_v<F, FmtIQ1_S> || std::is_same_v<F, FmtQ8_0>) {
@@ -648,10 +656,11 @@ int32_t gemm_f16_device(int32_t kind, float *out, const uint8_t *w, const float 
                 // memory: run the batch as halves (the weights stream twice).
                 if (batch >= 2 * kGemmMinTokens) {
                     const int h = (batch + 1) / 2;
-                    st = gemm_f16_device(kind, out, w, x, rows, cols, h, scratch, stream);
+                    st = gemm_f16_device(kind, out, w, x, rows, cols, h, scratch, stream, seg);
                     if (!st)
                         st = gemm_f16_device(kind, out + static_cast<size_t>(h) * rows, w,
-                                             x + static_cast<size_t>(h) * cols, rows, cols, batch - h, scratch, stream);
+                                             x + static_cast<size_t>(h) * xstride, rows, cols, batch - h, scratch,
+                                             stream, seg);
                     return;
                 }
                 set_error("gemm: no launch plan for this shape");
@@ -668,15 +677,15 @@ int32_t gemm_f16_device(int32_t kind, float *out, const uint8_t *w, const float 
             attr[0].val.programmaticStreamSerializationAllowed = 1;
             cfg.attrs = attr;
             cfg.numAttrs = 1;
-            const cudaError_t e = cudaLaunchKernelEx(&cfg, prep_f16_kernel, scratch, x, batch, T4, cols, p.nt8);
+            const cudaError_t e = cudaLaunchKernelEx(&cfg, prep_f16_kernel, scratch, x, batch, T4, cols, p.nt8, xstride);
             if (e != cudaSuccess) {
                 st = cuda_fail(e, "prep_f16_kernel");
                 return;
             }
             switch (p.ntw) {
-            case 2: st = launch_gemm<F, 2>(p, out, w, scratch, rows, cols, batch, row_bytes, stream); break;
-            case 4: st = launch_gemm<F, 4>(p, out, w, scratch, rows, cols, batch, row_bytes, stream); break;
-            default: st = launch_gemm<F, 8>(p, out, w, scratch, rows, cols, batch, row_bytes, stream); break;
+            case 2: st = launch_gemm<F, 2>(p, out, w, scratch, rows, cols, batch, row_bytes, seg, stream); break;
+            case 4: st = launch_gemm<F, 4>(p, out, w, scratch, rows, cols, batch, row_bytes, seg, stream); break;
+            default: st = launch_gemm<F, 8>(p, out, w, scratch, rows, cols, batch, row_bytes, seg, stream); break;
             }
         }
     });

@@ -417,7 +417,7 @@ __device__ __forceinline__ void prep_chunk(uint8_t *out, const float *x, const f
 // One warp per (row, 256-column chunk).
 __global__ void __launch_bounds__(256)
     prep_rows_kernel(uint8_t *__restrict__ prep, const float *__restrict__ x, const float *__restrict__ x2, int rows,
-                     int cols, const int *rows_dev) {
+                     int cols, const int *rows_dev, int xstride) {
     grid_dependency_wait();
     allow_dependent_launch();
     if (rows_dev) rows = min(max(*rows_dev, 0), rows);
@@ -426,8 +426,8 @@ __global__ void __launch_bounds__(256)
     const int lane = threadIdx.x & 31;
     if (wid >= static_cast<int64_t>(rows) * chunks) return;  // warp-uniform
     const int row = static_cast<int>(wid / chunks), chunk = static_cast<int>(wid % chunks);
-    prep_chunk(prep + static_cast<size_t>(row) * prep_stride(cols), x + static_cast<size_t>(row) * cols,
-               x2 ? x2 + static_cast<size_t>(row) * cols : nullptr, cols, chunk, lane);
+    prep_chunk(prep + static_cast<size_t>(row) * prep_stride(cols), x + static_cast<size_t>(row) * xstride,
+               x2 ? x2 + static_cast<size_t>(row) * xstride : nullptr, cols, chunk, lane);
 }
 
 // ----------------------------------------------------------------- kernel ---
@@ -465,7 +465,7 @@ template <class F, int S, int RG, int W, int NT, int FR>
 __global__ void __launch_bounds__((S * RG + 1) * 32, 1)
     mma_rows_kernel(MmaJob job0, const MmaJob *__restrict__ jobs, const int *njobs_dev, int max_jobs, int batch,
                     int rows_per_job, int cols, int row_bytes, int srow, int stages, int stage_stride,
-                    const float *__restrict__ x_raw, int *err) {
+                    const float *__restrict__ x_raw, int64_t pitch, int xstride, int accumulate, int *err) {
     using MF = MmaFmt<F>;
     constexpr int NS = 2 * NT;                      // token slots per job
     constexpr int NW = S * RG, R = 16 * FR * RG;  // a warp owns FR 16-row fragments of the tile
@@ -524,8 +524,8 @@ __global__ void __launch_bounds__((S * RG + 1) * 32, 1)
             const int nr = tile_end(r0, r_end) - r0;
             const MmaJob j = job_at(job0, jobs, r0 / rows_per_job, batch, rows_per_job, pstride);
             uint8_t *stage = smem + static_cast<size_t>(s) * stage_stride;
-            const uint8_t *src = j.w + static_cast<size_t>(r0 % rows_per_job) * row_bytes;
-            if (srow == row_bytes) {  // rows already bank-spread: the tile is one contiguous copy
+            const uint8_t *src = j.w + static_cast<size_t>(r0 % rows_per_job) * pitch;
+            if (srow == row_bytes && pitch == row_bytes) {  // rows already bank-spread: one contiguous copy
                 if (lane == 0) {
                     mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(nr) * row_bytes);
                     bulk_g2s(stage, src, static_cast<uint32_t>(nr) * row_bytes, &full[s]);
@@ -534,7 +534,7 @@ __global__ void __launch_bounds__((S * RG + 1) * 32, 1)
                 if (lane == 0) mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(nr) * row_bytes);
                 __syncwarp();
                 for (int i = lane; i < nr; i += 32)
-                    bulk_g2s(stage + static_cast<size_t>(i) * srow, src + static_cast<size_t>(i) * row_bytes, row_bytes,
+                    bulk_g2s(stage + static_cast<size_t>(i) * srow, src + static_cast<size_t>(i) * pitch, row_bytes,
                              &full[s]);
             }
         }
@@ -584,7 +584,7 @@ __global__ void __launch_bounds__((S * RG + 1) * 32, 1)
                 for (int c = warp; c < 2 * chunks; c += NW) {
                     const int slot = c / chunks, tok = 2 * job + slot;
                     if (tok < batch)
-                        prep_chunk(bsm + slot * pstride, x_raw + static_cast<size_t>(tok) * cols, nullptr, cols,
+                        prep_chunk(bsm + slot * pstride, x_raw + static_cast<size_t>(tok) * xstride, nullptr, cols,
                                    c % chunks, lane);
                 }
                 if (!job_sync()) {
@@ -690,7 +690,10 @@ __global__ void __launch_bounds__((S * RG + 1) * 32, 1)
 #pragma unroll
                 for (int q = 0; q < S; ++q) v += rb[(i * S + q) * NS + slot];
                 float *o = pick(J.out, slot);
-                if (i < nr && o) o[(r0 + i) % rows_per_job] = v;
+                if (i < nr && o) {
+                    float *d = o + (r0 + i) % rows_per_job;
+                    *d = accumulate ? *d + v : v;
+                }
             }
         }
     }
@@ -780,7 +783,7 @@ static bool plan_mma(int64_t max_rows, int64_t max_tiles_extra, int cols, int ro
 template <class F, int S, int W, int NT, int FR>
 static int32_t launch_mma_fr(const MmaPlan &p, const MmaJob &job0, const MmaJob *jobs, const int *njobs_dev,
                              int max_jobs, int batch, int rows_per_job, int cols, int row_bytes, const float *x_raw,
-                             cudaStream_t stream) {
+                             const ColSegment &seg, cudaStream_t stream) {
     constexpr int RG = mma_row_groups(S, W);
     auto kern = mma_rows_kernel<F, S, RG, W, NT, FR>;
     if (const int32_t rc = allow_dynamic_smem(kern, p.smem, "packed_mma smem")) return rc;
@@ -794,36 +797,39 @@ static int32_t launch_mma_fr(const MmaPlan &p, const MmaJob &job0, const MmaJob 
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
+    const int64_t pitch = seg.pitch ? seg.pitch : row_bytes;
+    const int xstride = seg.xstride ? seg.xstride : cols;
     GLMVX_CUDA(cudaLaunchKernelEx(&cfg, kern, job0, jobs, njobs_dev, max_jobs, batch, rows_per_job, cols, row_bytes,
-                                  p.srow, p.stages, p.stage_stride, x_raw, device_error_word()));
+                                  p.srow, p.stages, p.stage_stride, x_raw, pitch, xstride,
+                                  static_cast<int>(seg.accumulate), device_error_word()));
     return kOk;
 }
 
 template <class F, int S, int W, int NT>
 static int32_t launch_mma(const MmaPlan &p, const MmaJob &job0, const MmaJob *jobs, const int *njobs_dev,
                           int max_jobs, int batch, int rows_per_job, int cols, int row_bytes, const float *x_raw,
-                          cudaStream_t stream) {
+                          const ColSegment &seg, cudaStream_t stream) {
     if constexpr (NT == 2) {
         return launch_mma_fr<F, S, W, 2, 1>(p, job0, jobs, njobs_dev, max_jobs, batch, rows_per_job, cols, row_bytes,
-                                            x_raw, stream);
+                                            x_raw, seg, stream);
     } else {
         if constexpr (std::is_same_v<F, FmtIQ1_S>)
             if (p.FR == MmaFmt<F>::kFRLong)
                 return launch_mma_fr<F, S, W, 1, MmaFmt<F>::kFRLong>(p, job0, jobs, njobs_dev, max_jobs, batch,
-                                                                    rows_per_job, cols, row_bytes, x_raw, stream);
+                                                                    rows_per_job, cols, row_bytes, x_raw, seg, stream);
         return launch_mma_fr<F, S, W, 1, MmaFmt<F>::kFR>(p, job0, jobs, njobs_dev, max_jobs, batch, rows_per_job,
-                                                          cols, row_bytes, x_raw, stream);
+                                                          cols, row_bytes, x_raw, seg, stream);
     }
 }
 
 template <class F, int NT>
 static int32_t launch_mma_s(const MmaPlan &p, const MmaJob &job0, const MmaJob *jobs, const int *njobs_dev,
                             int max_jobs, int batch, int rows_per_job, int cols, int row_bytes, const float *x_raw,
-                            cudaStream_t stream) {
+                            const ColSegment &seg, cudaStream_t stream) {
 #define GLMVX_MMA_CASE(s, w)                                                                                     \
     case 2 * (s) + (w) - 1:                                                                                     \
         return launch_mma<F, s, w, NT>(p, job0, jobs, njobs_dev, max_jobs, batch, rows_per_job, cols, row_bytes, \
-                                       x_raw, stream);
+                                       x_raw, seg, stream);
     switch (2 * p.S + p.W - 1) {
         GLMVX_MMA_CASE(1, 2)
         GLMVX_MMA_CASE(2, 2)
@@ -854,7 +860,7 @@ bool mma_supported(int kind, int cols) {
 }
 
 int32_t prep_rows_device(uint8_t *prep, const float *x, const float *x2, int rows, int cols, cudaStream_t stream,
-                         const int *rows_dev) {
+                         const int *rows_dev, int xstride) {
     if (rows <= 0) return kOk;
     if (cols % 256 || (reinterpret_cast<uintptr_t>(prep) & 15) || (reinterpret_cast<uintptr_t>(x) & 15) ||
         (reinterpret_cast<uintptr_t>(x2) & 15)) {
@@ -871,12 +877,13 @@ int32_t prep_rows_device(uint8_t *prep, const float *x, const float *x2, int row
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    GLMVX_CUDA(cudaLaunchKernelEx(&cfg, prep_rows_kernel, prep, x, x2, rows, cols, rows_dev));
+    GLMVX_CUDA(cudaLaunchKernelEx(&cfg, prep_rows_kernel, prep, x, x2, rows, cols, rows_dev, xstride ? xstride : cols));
     return kOk;
 }
 
 int32_t mma_gemv_device(int32_t kind, const MmaJob &job0, const MmaJob *jobs, const int *njobs_dev, int max_jobs,
-                        int batch, int rows_per_job, int cols, cudaStream_t stream, const float *x_raw, int pairs) {
+                        int batch, int rows_per_job, int cols, cudaStream_t stream, const float *x_raw, int pairs,
+                        const ColSegment &seg) {
     if (pairs != 1 && !(pairs == 2 && jobs && !x_raw && mma_quad_supported(kind, cols))) {
         set_error("mma: two token pairs per job need a job list of a supported format");
         return kInvalid;
@@ -896,6 +903,11 @@ int32_t mma_gemv_device(int32_t kind, const MmaJob &job0, const MmaJob *jobs, co
     int blk = 0, bytes = 0;
     reference_layout(kind, blk, bytes);
     const int row_bytes = cols / blk * bytes;
+    if ((seg.pitch || seg.xstride || seg.accumulate) &&
+        (jobs || (seg.pitch && (seg.pitch < row_bytes || seg.pitch % 16)) || (seg.xstride && seg.xstride < cols))) {
+        set_error("mma: a column segment needs a single matrix, a 16-byte row pitch and strides >= its width");
+        return kInvalid;
+    }
     const int64_t max_rows = static_cast<int64_t>(rows_per_job) * max_jobs;
     int32_t st = kUnsupported;
     dispatch_format(kind, [&]<class F>() {
@@ -908,10 +920,10 @@ int32_t mma_gemv_device(int32_t kind, const MmaJob &job0, const MmaJob *jobs, co
             }
             if (pairs == 1) {
                 st = launch_mma_s<F, 1>(p, job0, jobs, njobs_dev, max_jobs, batch, rows_per_job, cols, row_bytes, x_raw,
-                                        stream);
+                                        seg, stream);
             } else if constexpr (std::is_same_v<F, FmtIQ1_S>) {
                 st = launch_mma_s<F, 2>(p, job0, jobs, njobs_dev, max_jobs, batch, rows_per_job, cols, row_bytes, x_raw,
-                                        stream);
+                                        seg, stream);
             }
         }
     });

@@ -212,19 +212,16 @@ class ResidentDecoder:
                  'kv_a': self._proj(a + '.kv_a_proj_with_mqa', self.rank + self.rot, H),
                  'kv_a_norm': self._vec(a + '.kv_a_layernorm.weight', self.rank),
                  'o': self._proj(a + '.o_proj', H, self.heads * self.vdim)}
-            # kv_b [heads][nope + v][rank] f32: the latent-query half as is, the
-            # value half transposed to [heads][rank][v] for coalesced reads.
+            # kv_b [heads][nope + v][rank] f32, as the reference keeps it: the
+            # query absorption reads its first nope rows of each head, the
+            # value absorption the last v rows.
             if self._synthetic:
                 n = self.heads * (self.nope + self.vdim) * self.rank
                 kvb = self._fill(0, 4 * n, n, 1.0 / math.sqrt(self.rank), a + '.kv_b_proj')
-                nv = self.heads * self.rank * self.vdim  # the value half, already transposed
-                kvbo = self._fill(0, 4 * nv, nv, 1.0 / math.sqrt(self.rank), a + '.kv_b_proj.value_t')
             else:
                 w = np.asarray(self.source.dense_tensor(a + '.kv_b_proj.weight'), np.float32)
-                w = w.reshape(self.heads, self.nope + self.vdim, self.rank)
-                kvb = self._put(w)
-                kvbo = self._put(np.ascontiguousarray(w[:, self.nope:, :].transpose(0, 2, 1)))
-            L['kvb'], L['kvbo_t'] = kvb, kvbo
+                kvb = self._put(w.reshape(self.heads, self.nope + self.vdim, self.rank))
+            L['kvb'] = kvb
             if self.indexer_types[i] == 'full':
                 L['wq_b'] = self._proj(a + '.indexer.wq_b', self.ih * self.idim, self.q_lora)
                 L['wk'] = self._proj(a + '.indexer.wk', self.idim, H)
@@ -393,7 +390,7 @@ class ResidentDecoder:
                 self.capacity, self.topk, C.c_float(scale), self.dsa_scratch, self.dsa_bytes, self.s),
                 'glmvx_dsa_attend')
             sel = sel_prev
-        self._check(self.lib.glmvx_absorb_value(self.vout, self.att, L['kvbo_t'], B, heads, R, V, self.s),
+        self._check(self.lib.glmvx_absorb_value(self.vout, self.att, L['kvb'], B, heads, N, R, V, self.s),
                     'glmvx_absorb_value')
         self._linear(self.ffn, self.vout, L['o'])  # attention output (ffn buffer reused)
         self._check(self.lib.glmvx_add(self.x, self.x, self.ffn, B * H, self.s), 'glmvx_add')

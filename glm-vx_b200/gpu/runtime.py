@@ -116,7 +116,7 @@ SIGNATURES = {
                         _I32),
     'glmvx_rmsnorm_rows': ([_P, _P, _P, _I32, _I32, _I64, _I64, _F32, _P], _I32),
     'glmvx_absorb_query': ([_P, _P, _P, _I32, _I32, _I32, _I32, _I32, _I32, _P], _I32),
-    'glmvx_absorb_value': ([_P, _P, _P, _I32, _I32, _I32, _I32, _P], _I32),
+    'glmvx_absorb_value': ([_P, _P, _P, _I32, _I32, _I32, _I32, _I32, _P], _I32),
     'glmvx_scale': ([_P, _P, _F32, _I64, _P], _I32),
     'glmvx_argmax_rows': ([_P, _P, _I32, _I32, _P], _I32),
     'glmvx_fill_random': ([_P, _I32, _I64, _U64, _F32, _I32, _P], _I32),

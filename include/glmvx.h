@@ -141,7 +141,9 @@ int32_t glmvx_packed_gemv(int32_t kind, float *out, const uint8_t *w, const floa
 int32_t glmvx_packed_gemm(int32_t kind, float *out, const uint8_t *w, const float *x, int32_t rows, int32_t cols,
                           int32_t batch, void *stream);
 /* As glmvx_packed_gemm; *path reports the kernel taken
- * (1 stream GEMV, 2 generic, 3 F16 element path, 5 tensor-core int8 path). */
+ * (1 stream GEMV, 2 generic, 3 F16 element path, 5 tensor-core int8 path,
+ * 6 f16 tensor-core GEMM, 7 / 8 the int8 path / f16 GEMM over equal column
+ * segments of rows too long for one plan, later segments adding in order). */
 int32_t glmvx_packed_gemm_path(int32_t kind, float *out, const uint8_t *w, const float *x, int32_t rows,
                                int32_t cols, int32_t batch, void *stream, int32_t *path);
 /* Diagnostic decode of `blocks` reference blocks (F16: elements) to f32.
@@ -339,8 +341,8 @@ int32_t glmvx_ep_destroy(void *layer);
  *   glmvx_rmsnorm_rows rmsnorm of strided rows (kernels/kernels.vx:17-27)
  *   glmvx_absorb_query q_latent[b,h] = kv_b[h,:nope]^T query[b,h,:nope],
  *                      kv_b [heads][nope+vdim][rank], serial f32 sums
- *   glmvx_absorb_value out[b,h*vdim+i] = sum_r kvbo_t[h][r][i] att[b,h,r]
- *                      (kv_b's value half transposed), serial f32 sums
+ *   glmvx_absorb_value out[b,h*vdim+i] = sum_r kv_b[h][nope+i][r] att[b,h,r],
+ *                      kv_b [heads][nope+vdim][rank], serial f32 sums
  *   glmvx_scale        out = x * s
  *   glmvx_argmax_rows  first index of each row's maximum (numpy argmax)
  *   glmvx_fill_random  seeded synthetic weights: f32 N(0,1)*scale (or ones),
@@ -359,8 +361,8 @@ int32_t glmvx_rmsnorm_rows(float *out, const float *x, const float *w, int32_t r
                            int64_t out_stride, float eps, void *stream);
 int32_t glmvx_absorb_query(float *q_latent, const float *query, const float *kvb, int32_t tokens, int32_t heads,
                            int32_t nope, int32_t qk_head, int32_t rank, int32_t vdim, void *stream);
-int32_t glmvx_absorb_value(float *out, const float *att, const float *kvbo_t, int32_t tokens, int32_t heads,
-                           int32_t rank, int32_t vdim, void *stream);
+int32_t glmvx_absorb_value(float *out, const float *att, const float *kvb, int32_t tokens, int32_t heads,
+                           int32_t nope, int32_t rank, int32_t vdim, void *stream);
 int32_t glmvx_scale(float *out, const float *x, float s, int64_t n, void *stream);
 int32_t glmvx_argmax_rows(int32_t *ids, const float *logits, int32_t rows, int32_t n, void *stream);
 int32_t glmvx_fill_random(void *out, int32_t kind, int64_t count, uint64_t seed, float scale, int32_t ones,

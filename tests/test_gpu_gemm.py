@@ -95,3 +95,21 @@ def test_gemm_full_size_normwise(gpu_vx):
     want = ref.packed_linear_batch(raw, 12, (6144, 2048), x)
     err = np.linalg.norm(got.astype(np.float64) - want) / np.linalg.norm(want.astype(np.float64))
     assert err <= RTOL, err
+
+
+@pytest.mark.parametrize('kind,rows,cols,batch,path', [
+    (8, 512, 16384, 1, 7), (8, 300, 16384, 2, 7), (8, 6144, 16384, 1, 7), (8, 700, 16384, 16, 8),
+    (8, 130, 24576, 8, 8), (12, 256, 16384, 1, 7), (12, 100, 32768, 3, 7), (19, 256, 16384, 1, 7),
+    (19, 96, 65536, 9, 8)])
+def test_long_rows_in_column_segments(cuda_lib, oracle, kind, rows, cols, batch, path):
+    """Rows too long for one tensor-core plan (config 3's Q8_0 o_proj reads
+    16384 columns) run as equal column segments, later ones adding onto the
+    output in segment order; same tolerance against the oracle as one pass."""
+    raw, x = _case(kind, rows, cols, batch, rows + cols + batch)
+    got, p = _device_gemm(cuda_lib, kind, raw, rows, cols, x)
+    assert p == path
+    want = oracle.packed_linear_batch(raw, kind, (rows, cols), x)
+    dec = unpack_for_validation(oracle.lib, raw, kind, (rows, cols))
+    assert_close_dot(got, want, dec, x)
+    again, _ = _device_gemm(cuda_lib, kind, raw, rows, cols, x)
+    assert again.tobytes() == got.tobytes()
