@@ -370,7 +370,8 @@ def graph_time(rt, stream, fn, reps, ranks=None, clocks=None):
     return ms
 
 
-PATH_NAMES = {1: 'stream', 2: 'generic', 5: 'mma_int8', 6: 'gemm_f16', 7: 'mma_int8_col_segments', 8: 'gemm_f16_col_segments'}
+PATH_NAMES = {1: 'stream', 2: 'generic', 5: 'mma_int8', 6: 'gemm_f16', 7: 'mma_int8_col_segments', 8: 'gemm_f16_col_segments',
+              9: 'gemm_tcgen05_bf16x3'}
 
 
 def fused_gemv_sweep(rt, lib, dev, stream, steps, peak):
@@ -915,6 +916,8 @@ def run_profile_case(args):
         return profile_decoder()
     if args.profile_case == 'packed_gemm':
         return profile_packed_gemm()
+    if args.profile_case == 'packed_gemm_tc':
+        return profile_packed_gemm('glmvx_packed_gemm_tc')
     if args.profile_case in ('attention3', 'attention3_16'):
         return profile_attention3(16 if args.profile_case == 'attention3_16' else 1)
     from gpu.backend import GPUBackend
@@ -987,10 +990,12 @@ def profile_attention3(B, steps=2):
     return 0
 
 
-def profile_packed_gemm():
-    """The f16 tensor-core packed GEMM on BASELINE config 1 at 64 tokens (Q4_K
-    6144 x 2048) and on the config-4 lm_head shape at 32 tokens (Q8_0
-    154880 x 6144, 1 GB, larger than L2): three launches each."""
+def profile_packed_gemm(entry='glmvx_packed_gemm'):
+    """The packed GEMM for token batches (`entry`: the dispatching
+    glmvx_packed_gemm, or glmvx_packed_gemm_tc for the tcgen05 kernel) on
+    BASELINE config 1 at 64 tokens (Q4_K 6144 x 2048) and on the config-4
+    lm_head shape at 32 tokens (Q8_0 154880 x 6144, 1 GB, larger than L2):
+    three launches each."""
     from gpu.backend import GPUBackend
     from gpu import runtime as rt
     backend = GPUBackend(0)
@@ -1005,14 +1010,13 @@ def profile_packed_gemm():
         xd, od = rt.DeviceBuffer(x.nbytes), rt.DeviceBuffer(4 * batch * rows)
         xd.upload(x, s)
         for _ in range(3):
-            rt.check(backend.lib, backend.lib.glmvx_packed_gemm(kind, od.ptr, w.ptr, xd.ptr, rows, cols, batch, s),
-                     'glmvx_packed_gemm')
+            rt.check(backend.lib, getattr(backend.lib, entry)(kind, od.ptr, w.ptr, xd.ptr, rows, cols, batch, s),
+                     entry)
         backend.stream.synchronize()
         for b in (w, xd, od):
             b.close()
     backend.device.check_device_error()
-    print('profile case ok: packed f16 GEMM, config-1 Q4_K x64 and config-4 lm_head Q8_0 x32, 3 launches each',
-          flush=True)
+    print(f'profile case ok: {entry}, config-1 Q4_K x64 and config-4 lm_head Q8_0 x32, 3 launches each', flush=True)
     backend.close()
     return 0
 
@@ -1075,7 +1079,7 @@ def main():
     ap.add_argument('--no-cpu-baseline', action='store_true')
     ap.add_argument('--no-decoder', action='store_true', help='skip the config-4 decoder measurement')
     ap.add_argument('--profile-case', nargs='?', const='moe', choices=('moe', 'gemm', 'dsa', 'dsa1', 'decoder', 'packed_gemm',
-                                                                 'attention3', 'attention3_16'),
+                                                                 'attention3', 'attention3_16', 'packed_gemm_tc'),
                     help='run a small kernel-capture case (one GPU) instead of the benchmark')
     args = ap.parse_args()
     if args.profile_case:

@@ -129,6 +129,19 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity
     }
 }
 
+// As mbar_wait_bounded, polling without the suspend hint: for hand-offs on
+// the critical path of a pipeline whose every stage waits on the previous
+// one (a suspended thread resumes later than a polling one notices).
+__device__ __forceinline__ bool mbar_wait_spin_bounded(uint64_t *bar, uint32_t parity,
+                                                       uint64_t limit_ns = 2000000000ull) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t start = globaltimer_ns();
+    for (uint32_t i = 1;; ++i) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((i & 63u) == 0 && globaltimer_ns() - start > limit_ns) return false;
+    }
+}
+
 // 1-D bulk copy global -> shared (TMA engine), completing `bytes` of
 // transaction count on `bar`.  dst/src 16-byte aligned, bytes % 16 == 0.
 // No cluster multicast: this is a plain per-CTA load.

@@ -1,0 +1,608 @@
+// Packed-GGUF GEMM for token batches on the 5th-generation tensor cores
+// (tcgen05), the batch_v2 contract (kernels/packed.vx:473ff):
+// out[t][r] = sum_j w[r][j] * x[t][j] in f32 with w decoded per GGML block.
+//
+// Numerics.  Every weight is decoded to the f32 value the reference computes
+// (Q8_0 and Q4_K by their own 16-weight decoders, the other formats by their
+// `octet`, codecs.cuh) and split exactly into three bf16 limbs (w = a1 + a2 +
+// a3: the top 8 significant bits, the next 8, the rest); the activations are
+// split the same way (b1 + b2 + b3) by prep_tc_kernel.  bf16 keeps f32's
+// exponent range, so nothing is scaled, and every limb product is exact in
+// f32.  Three kind::f16 (bf16) MMAs per K step of 16 columns, a1 x [b1 | b2 |
+// b3], a2 x [b1 | b2] and a3 x b1, accumulate the whole row in f32 in tensor
+// memory; the epilogue adds the b1, b2 and b3 columns.  The dropped a2*b3,
+// a3*b2, a3*b3 are below 2^-23 |w x|.  A non-finite activation turns its own
+// token's outputs NaN only (columns are tokens).
+//
+// Kernel (gemm_tc_kernel<F>): one CTA per 128-row tile, 18 warps.
+//   warp 0   producer: per chunk of `chunk_cols` columns one 2-D tiled TMA
+//            copy of the tile's raw packed bytes (128 rows x the chunk's
+//            bytes, the tensor map's rows past the matrix read as zeros)
+//            into a ring of one or two stages -- one multi-KB copy instead
+//            of 128 row copies of 144-880 bytes, which measured ~1 us per
+//            32 columns; per 32-column atom one 1-D bulk copy of the
+//            prepared activation limbs (already in the operand layout);
+//   warp 1   allocates tensor memory; lane 0 issues the MMAs of each atom
+//            (2 K steps x 3, M = 128) and commits them to the atom slot's
+//            mbarrier;
+//   warps 2-17 decode in two groups of 8 taking alternate atoms: per atom
+//            128 rows x 32 columns, a thread 16 weights of one row, into
+//            the three K-major A limb tiles (8 x 16-byte core matrices, no
+//            swizzle) of the atom's slot;
+//   warps 2-5 (one per lane quarter) read the accumulators at the end
+//            (tcgen05.ld) and store out[t][row].
+// Every mbarrier wait is bounded (2 s): on expiry the kernel records the
+// device error word and returns after freeing its tensor memory.
+//
+// Measured costs that shape it: a tcgen05.mma of M = 128 and N <= 64 takes
+// ~25 ns back to back whatever N (K = 8 TF32 or K = 16 f16/bf16), so few,
+// wide MMAs -- bf16 limbs give twice the K of TF32 per MMA and half the
+// operand bytes; per-row bulk copies of a few hundred bytes cost ~1 us per 32
+// columns, hence the 2-D tensor-map copy.
+#include <algorithm>
+#include <type_traits>
+
+#include <cuda.h>
+
+#include "codecs.cuh"
+#include "mma_gemv.cuh"
+#include "tcgen05.cuh"
+
+namespace glmvx {
+
+namespace {
+
+constexpr int kTcRows = 128;                    // weight rows per CTA (UMMA M)
+constexpr int kTcAtomCols = 32;                 // columns per atom (one A slot, 2 K steps)
+constexpr int kTcLimbs = 3;                     // bf16 limbs per operand (8 + 8 + 8 bits)
+constexpr int kTcRowBytes = kTcAtomCols * 2;    // one row of one limb of an atom: 64 bytes
+constexpr int kTcATile = kTcRows * kTcRowBytes; // one limb of one atom: 8 KB
+constexpr int kTcGroupWarps = 8;                // a decode group: 8 warps, one atom at a time
+// Threads of a CTA with NG decode groups: producer + MMA warps + groups.
+__host__ __device__ constexpr int tc_threads(int ng) { return (2 + ng * kTcGroupWarps) * 32; }
+// Shared memory of a CTA that shares its SM with another (one decode group):
+// half the opt-in maximum less the per-CTA reservation.
+constexpr int kTcSmemHalf = 112 * 1024;
+constexpr int kTcSmemBudget = 226 * 1024;
+constexpr int kTcMaxTokens = 64;
+
+constexpr uint32_t kHi16 = 0xFFFF0000u;
+
+// Columns per raw stage: the smallest multiple of 256 (and of the block)
+// whose packed bytes per row are a multiple of 16, at most 2048.
+__host__ __device__ constexpr int tc_chunk_cols(int blk, int bytes) {
+    for (int c = 256; c <= 2048; c += 256)
+        if (c % blk == 0 && (c / blk * bytes) % 16 == 0) return c;
+    return 0;
+}
+
+// f32 -> three bf16 limbs, exactly: l1 = v truncated to bf16, l2 = (v - l1)
+// truncated, l3 = the rest (at most 8 significant bits, a bf16 value).  Each
+// limb is returned as the f32 bit pattern whose low 16 bits are zero.
+__device__ __forceinline__ void bf16_limbs(float v, uint32_t &l1, uint32_t &l2, uint32_t &l3) {
+    l1 = __float_as_uint(v) & kHi16;
+    const float r1 = v - __uint_as_float(l1);
+    l2 = __float_as_uint(r1) & kHi16;
+    l3 = __float_as_uint(r1 - __uint_as_float(l2));
+}
+
+// Two limb values (low 16 bits zero) as one bf16x2 word, element 0 low.
+__device__ __forceinline__ uint32_t pack_bf16(uint32_t e0, uint32_t e1) { return __byte_perm(e0, e1, 0x7632); }
+
+// Instruction descriptor, kind::f16 with BF16 A and B (bits 7-9, 10-12 = 1),
+// f32 accumulation (bits 4-5 = 1), both K-major, N >> 3 at bit 17, M >> 4 at 24.
+__host__ __device__ constexpr uint32_t umma_idesc_bf16(int m, int n) {
+    return (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(n >> 3) << 17) |
+           (static_cast<uint32_t>(m >> 4) << 24);
+}
+
+__device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                          uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// K-major operand tiles without swizzle, as core matrices of 8 rows x 16
+// bytes (128 contiguous bytes): 16-byte chunk c (bf16 k = 8c..8c+7) of row r
+// of a `rows`-row atom sits in K step c/2 (one MMA, K = 16), core matrix c%2
+// of 8-row group r/8.  Per K step the tile is rows*32 contiguous bytes, so an
+// MMA reads exactly its operands.
+__host__ __device__ __forceinline__ uint32_t kmajor_offset(int r, int c, int rows) {
+    return static_cast<uint32_t>((c >> 1) * rows * 32 + (r >> 3) * 256 + (c & 1) * 128 + (r & 7) * 16);
+}
+
+// UMMA shared-memory descriptor of a K-major SWIZZLE_NONE tile: leading
+// byte offset 128 (between the two core matrices of a K step), stride byte
+// offset 256 (between 8-row groups), version 1, layout type 0.
+__device__ __forceinline__ uint64_t umma_desc_kmajor(uint32_t addr) {
+    return static_cast<uint64_t>((addr >> 4) & 0x3FFFu) | (8ull << 16) | (16ull << 32) | (1ull << 46);
+}
+
+// Byte k of u as the float 2^23 + byte: the byte permuted into the mantissa.
+template <int K>
+__device__ __forceinline__ float byte_biased(uint32_t u) {
+    return __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7650u | K));
+}
+
+// The 16 weights of tile row `rc` (its bytes in the raw stage) at chunk
+// columns a*32 + 16h .. +15, as the reference computes them in f32.
+// Generic: two octets of the format's decoder.
+template <class F>
+struct TcDecode {
+    __device__ __forceinline__ static void run(const uint8_t *rc, int a, int h, float (&w)[16]) {
+#pragma unroll
+        for (int o = 0; o < 2; ++o) {
+            const int col = a * kTcAtomCols + 16 * h + 8 * o;
+            F::octet(rc + (col / F::kBlk) * F::kBytes, col % F::kBlk, w + 8 * o);
+        }
+    }
+};
+
+// Q8_0 (kernels/packed.vx:28-31, w = d*q): atom a is block a of the chunk;
+// its 16 bytes come in four 32-bit loads (odd a: 4-byte aligned) or five
+// and funnel shifts (even a: 2 bytes past alignment); q + 128 enters the
+// mantissa of 2^23 and one subtraction gives q exactly.
+template <>
+struct TcDecode<FmtQ8_0> {
+    __device__ __forceinline__ static void run(const uint8_t *rc, int a, int h, float (&w)[16]) {
+        const uint8_t *blk = rc + a * FmtQ8_0::kBytes;
+        const float d = h2f(u16(blk));
+        uint32_t v[4];
+        if (a & 1) {
+            const uint32_t *p = reinterpret_cast<const uint32_t *>(blk + 2 + 16 * h);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) v[i] = p[i];
+        } else {
+            const uint32_t *p = reinterpret_cast<const uint32_t *>(blk + 16 * h);
+            uint32_t x[5];
+#pragma unroll
+            for (int i = 0; i < 5; ++i) x[i] = p[i];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) v[i] = __funnelshift_r(x[i], x[i + 1], 16);
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const uint32_t u = v[i] ^ 0x80808080u;
+            w[4 * i + 0] = __fmul_rn(d, byte_biased<0>(u) - 8388736.0f);
+            w[4 * i + 1] = __fmul_rn(d, byte_biased<1>(u) - 8388736.0f);
+            w[4 * i + 2] = __fmul_rn(d, byte_biased<2>(u) - 8388736.0f);
+            w[4 * i + 3] = __fmul_rn(d, byte_biased<3>(u) - 8388736.0f);
+        }
+    }
+};
+
+// Q4_K (kernels/packed.vx:121-130, w = (d*sc)*q - dmin*m): the chunk is one
+// superblock, atom a its sub-block a; the 16 nibble bytes in one 16-byte load.
+template <>
+struct TcDecode<FmtQ4_K> {
+    __device__ __forceinline__ static void run(const uint8_t *rc, int a, int h, float (&w)[16]) {
+        const float dl = __fmul_rn(h2f(u16(rc)), static_cast<float>(k4_scale(rc + 4, a)));
+        const float ml = __fmul_rn(h2f(u16(rc + 2)), static_cast<float>(k4_min(rc + 4, a)));
+        const uint4 q = *reinterpret_cast<const uint4 *>(rc + 16 + 32 * (a >> 1) + 16 * h);
+        const int shift = 4 * (a & 1);
+        const uint32_t v[4] = {(q.x >> shift) & 0x0F0F0F0Fu, (q.y >> shift) & 0x0F0F0F0Fu, (q.z >> shift) & 0x0F0F0F0Fu,
+                               (q.w >> shift) & 0x0F0F0F0Fu};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            w[4 * i + 0] = __fsub_rn(__fmul_rn(dl, byte_biased<0>(v[i]) - 8388608.0f), ml);
+            w[4 * i + 1] = __fsub_rn(__fmul_rn(dl, byte_biased<1>(v[i]) - 8388608.0f), ml);
+            w[4 * i + 2] = __fsub_rn(__fmul_rn(dl, byte_biased<2>(v[i]) - 8388608.0f), ml);
+            w[4 * i + 3] = __fsub_rn(__fmul_rn(dl, byte_biased<3>(v[i]) - 8388608.0f), ml);
+        }
+    }
+};
+
+// 2-D tiled TMA load (box of the tensor map at element (x, y)) into shared
+// memory, completing its bytes on `bar`.  No multicast.
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
+            "r"(smem_addr(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_addr(bar))
+        : "memory");
+}
+
+// A bounded wait whose outcome is the same for every lane of the warp (the
+// tensor-memory loads after it are warp-collective).
+__device__ __forceinline__ bool warp_wait(uint64_t *bar, uint32_t parity) {
+    const bool ok = mbar_wait_bounded(bar, parity);
+    return __all_sync(0xffffffffu, ok);
+}
+
+// Shared-memory layout of a CTA (offsets from the 1 KB-aligned base).
+struct TcLayout {
+    int npad, chunk_cols, chunk_bytes, slots, raw_stages;
+    __host__ __device__ int b_tile() const { return npad * kTcRowBytes; }     // one limb of one atom
+    __host__ __device__ int slot_bytes() const { return kTcLimbs * (kTcATile + b_tile()); }
+    __host__ __device__ int raw_stage() const { return kTcRows * chunk_bytes; }
+    __host__ __device__ int raw_off() const { return slots * slot_bytes(); }
+    __host__ __device__ int bar_off() const { return (raw_off() + raw_stages * raw_stage() + 15) & ~15; }
+    // raw_full[2], raw_empty[2], a_full[slots], b_full[slots], op_empty[slots], acc_full, tmem slot
+    __host__ __device__ int bytes() const { return bar_off() + 8 * (4 + 3 * slots + 1) + 16; }
+};
+
+}  // namespace
+
+// Prepared activation limbs for the tensor-core GEMM: per 32-column atom a one
+// K-major core-matrix tile of 3*npad rows of 64 bytes (32 bf16), row
+// l*npad + n the bf16 limb l of token n (zeros past `tokens`), at
+// a * 3*npad*64.  One thread per (atom, token row, 16-byte chunk of 8 columns).
+__global__ void __launch_bounds__(256)
+    prep_tc_kernel(uint8_t *__restrict__ rec, const float *__restrict__ x, int tokens, int npad, int cols,
+                   int xstride) {
+    grid_dependency_wait();
+    allow_dependent_launch();
+    const int64_t id = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const int atoms = cols / kTcAtomCols;
+    if (id >= static_cast<int64_t>(atoms) * npad * 4) return;
+    const int c = static_cast<int>(id & 3), n = static_cast<int>((id >> 2) % npad);
+    const int a = static_cast<int>((id >> 2) / npad);
+    float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    if (n < tokens) {
+        const float4 *src = reinterpret_cast<const float4 *>(x + static_cast<size_t>(n) * xstride + a * kTcAtomCols + 8 * c);
+        const float4 lo4 = __ldg(src), hi4 = __ldg(src + 1);
+        v[0] = lo4.x, v[1] = lo4.y, v[2] = lo4.z, v[3] = lo4.w, v[4] = hi4.x, v[5] = hi4.y, v[6] = hi4.z, v[7] = hi4.w;
+    }
+    uint32_t l[3][8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) bf16_limbs(v[e], l[0][e], l[1][e], l[2][e]);
+    uint8_t *atom = rec + static_cast<size_t>(a) * kTcLimbs * npad * kTcRowBytes;
+#pragma unroll
+    for (int k = 0; k < kTcLimbs; ++k)
+        *reinterpret_cast<uint4 *>(atom + kmajor_offset(k * npad + n, c, kTcLimbs * npad)) =
+            make_uint4(pack_bf16(l[k][0], l[k][1]), pack_bf16(l[k][2], l[k][3]), pack_bf16(l[k][4], l[k][5]),
+                       pack_bf16(l[k][6], l[k][7]));
+}
+
+namespace {
+
+template <class F, int NG>
+__global__ void __launch_bounds__(tc_threads(NG), NG == 1 ? 2 : 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap wmap, float *__restrict__ out, const uint8_t *__restrict__ rec,
+                   int rows, int cols, int tokens, int npad, int chunk_cols, int chunk_bytes, int slots, int raw_stages,
+                   int accumulate, int *err) {
+    extern __shared__ uint8_t tc_smem_raw[];
+    const uint32_t raw_s = smem_addr(tc_smem_raw);
+    const uint32_t pad = ((raw_s + 1023u) & ~1023u) - raw_s;  // swizzled tiles: 1 KB-aligned addresses
+    uint8_t *base = tc_smem_raw + pad;
+    const uint32_t base_s = raw_s + pad;
+    const TcLayout L{npad, chunk_cols, chunk_bytes, slots, raw_stages};
+    uint64_t *bars = reinterpret_cast<uint64_t *>(base + L.bar_off());
+    uint64_t *raw_full = bars, *raw_empty = bars + 2, *a_full = bars + 4;
+    uint64_t *b_full = a_full + slots, *op_empty = b_full + slots, *acc_full = op_empty + slots;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_full + 1);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int row0 = blockIdx.x * kTcRows;
+    const int nrows = min(kTcRows, rows - row0);
+    const int atoms = cols / kTcAtomCols, chunks = cols / chunk_cols, apc = chunk_cols / kTcAtomCols;
+    // 2 npad accumulator columns; the epilogue reads 32-column groups at 0 ..
+    // npad and npad .. 2 npad, so at least npad + 32 columns are allocated.
+    const int need = max(kTcLimbs * npad, 2 * npad + 32);
+    const uint32_t tmem_cols = need <= 32 ? 32u : (need <= 64 ? 64u : (need <= 128 ? 128u : 256u));
+    const uint32_t idesc1 = umma_idesc_bf16(kTcRows, npad), idesc2 = umma_idesc_bf16(kTcRows, 2 * npad),
+                   idesc3 = umma_idesc_bf16(kTcRows, 3 * npad);
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&raw_full[i], 1);
+            mbar_init(&raw_empty[i], NG * kTcGroupWarps);
+        }
+        for (int i = 0; i < slots; ++i) {
+            mbar_init(&a_full[i], kTcGroupWarps);
+            mbar_init(&b_full[i], 1);
+            mbar_init(&op_empty[i], 1);
+        }
+        mbar_init(acc_full, 1);
+        fence_mbar_init();
+    }
+    if (warp == 1) tmem_alloc(tmem_slot, tmem_cols);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    allow_dependent_launch();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {  // producer
+        bool ok = true;
+        for (int c = 0; c < chunks && ok; ++c) {
+            const int s = c % raw_stages;
+            int good = 1;
+            if (lane == 0) good = mbar_wait_bounded(&raw_empty[s], ((c / raw_stages) & 1) ^ 1);
+            good = __shfl_sync(0xffffffffu, good, 0);
+            if (!good) {
+                if (lane == 0) report_device_error(err, kDevErrEmptyWait);
+                break;
+            }
+            uint8_t *stage = base + L.raw_off() + s * L.raw_stage();
+            if (lane == 0) {
+                mbar_arrive_expect_tx(&raw_full[s], static_cast<uint32_t>(kTcRows * chunk_bytes));
+                tma_load_2d(stage, &wmap, c * (chunk_bytes / 4), row0, &raw_full[s]);
+            }
+            __syncwarp();
+            if (c == 0) grid_dependency_wait();  // the activation limbs come from the previous kernel
+            for (int a = 0; a < apc; ++a) {
+                const int g = c * apc + a, slot = g % slots;
+                if (lane == 0) {
+                    if (!mbar_wait_bounded(&op_empty[slot], ((g / slots) & 1) ^ 1)) {
+                        report_device_error(err, kDevErrEmptyWait);
+                        good = 0;
+                    } else {
+                        uint8_t *b = base + slot * L.slot_bytes() + kTcLimbs * kTcATile;
+                        mbar_arrive_expect_tx(&b_full[slot], static_cast<uint32_t>(kTcLimbs * L.b_tile()));
+                        bulk_g2s(b, rec + static_cast<size_t>(g) * kTcLimbs * L.b_tile(),
+                                 static_cast<uint32_t>(kTcLimbs * L.b_tile()),
+                                 &b_full[slot]);
+                    }
+                }
+                good = __shfl_sync(0xffffffffu, good, 0);
+                if (!good) {
+                    ok = false;
+                    break;
+                }
+            }
+        }
+    } else if (warp == 1) {  // MMA issue
+        if (lane == 0) {
+            bool ok = true;
+            for (int g = 0; g < atoms; ++g) {
+                const int slot = g % slots;
+                const uint32_t ph = (g / slots) & 1;
+                if (!mbar_wait_spin_bounded(&a_full[slot], ph) || !mbar_wait_spin_bounded(&b_full[slot], ph)) {
+                    report_device_error(err, kDevErrFullWait);
+                    ok = false;
+                    break;
+                }
+                // (No tcgen05 fence here: the tiles were published through the
+                // async proxy -- TMA, or fence.proxy.async before the arrive.)
+                // Descriptors of the slot's tiles; a K step adds its offset >> 4
+                // to the start-address field (no carry: shared addresses < 256 KB).
+                // Per K step (16 columns): a1 x [b1 | b2 | b3], a2 x [b1 | b2],
+                // a3 x b1 -- B rows 0 .. k*npad of the stacked limb tile -- into
+                // accumulator columns 0 .. 3 npad.
+                const uint64_t da = umma_desc_kmajor(base_s + slot * L.slot_bytes());
+                const uint64_t db = da + ((kTcLimbs * kTcATile) >> 4);
+#pragma unroll
+                for (int kk = 0; kk < kTcAtomCols / 16; ++kk) {  // K = 16 bf16 = 32 bytes per MMA
+                    const uint64_t oa = (kk * kTcRows * 32) >> 4, ob = static_cast<uint64_t>(kk * kTcLimbs * npad * 2);
+                    umma_bf16(tmem, da + oa, db + ob, idesc3, (g > 0 || kk > 0) ? 1u : 0u);
+                    umma_bf16(tmem, da + (kTcATile >> 4) + oa, db + ob, idesc2, 1u);
+                    umma_bf16(tmem, da + ((2 * kTcATile) >> 4) + oa, db + ob, idesc1, 1u);
+                }
+                umma_commit(&op_empty[slot]);
+            }
+            if (ok) umma_commit(acc_full);
+        }
+        __syncwarp();
+    } else {  // decode (two groups of 8 warps, alternate atoms), then (warps 2-5) the epilogue
+        const int grp = (warp - 2) / kTcGroupWarps, gt = threadIdx.x - 64 - grp * kTcGroupWarps * 32;
+        const int r = gt >> 1, h = gt & 1;  // a thread: 16 weights of one tile row
+        bool ok = true;
+        for (int c = 0; c < chunks && ok; ++c) {
+            const int s = c % raw_stages;
+            if (!warp_wait(&raw_full[s], (c / raw_stages) & 1)) {
+                if (lane == 0) report_device_error(err, kDevErrFullWait);
+                ok = false;
+                break;
+            }
+            const uint8_t *rc = base + L.raw_off() + s * L.raw_stage() + r * chunk_bytes;
+            for (int a = grp; a < apc; a += NG) {
+                const int g = c * apc + a, slot = g % slots;
+                if (!warp_wait(&op_empty[slot], ((g / slots) & 1) ^ 1)) {
+                    if (lane == 0) report_device_error(err, kDevErrEmptyWait);
+                    ok = false;
+                    break;
+                }
+                float v[16];
+                if (r < nrows) {
+                    TcDecode<F>::run(rc, a, h, v);
+                } else {
+#pragma unroll
+                    for (int e = 0; e < 16; ++e) v[e] = 0.0f;
+                }
+                uint8_t *at = base + slot * L.slot_bytes();
+#pragma unroll
+                for (int i = 0; i < 2; ++i) {  // 8 weights -> one 16-byte chunk per limb
+                    uint32_t l[3][8];
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) bf16_limbs(v[8 * i + e], l[0][e], l[1][e], l[2][e]);
+                    const uint32_t off = kmajor_offset(r, 2 * h + i, kTcRows);
+#pragma unroll
+                    for (int k = 0; k < kTcLimbs; ++k)
+                        *reinterpret_cast<uint4 *>(at + k * kTcATile + off) =
+                            make_uint4(pack_bf16(l[k][0], l[k][1]), pack_bf16(l[k][2], l[k][3]),
+                                       pack_bf16(l[k][4], l[k][5]), pack_bf16(l[k][6], l[k][7]));
+                }
+                fence_proxy_async_smem();  // generic-proxy stores -> the tensor cores' async proxy
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&a_full[slot]);
+            }
+            __syncwarp();
+            if (lane == 0 && ok) mbar_arrive(&raw_empty[s]);
+        }
+        if (warp < 6) {  // one warp per tensor-memory lane quarter: rows 32*(warp%4) ..
+            const bool got = ok && warp_wait(acc_full, 0);
+            if (ok && !got && lane == 0) report_device_error(err, kDevErrFullWait);
+            tc_fence_after();
+            grid_dependency_wait();  // `out` may be read or written by the previous kernel
+            const int q = warp & 3, r = 32 * q + lane;
+            for (int c0 = 0; c0 < npad && got; c0 += 32) {
+                // columns t (a1 b1 + a2 b1 + a3 b1), npad + t (a1 b2 + a2 b2), 2 npad + t (a1 b3)
+                float v[32];
+                uint32_t u[32];
+                tmem_ld32(tmem + (static_cast<uint32_t>(32 * q) << 16) + static_cast<uint32_t>(c0), u);
+#pragma unroll
+                for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(u[j]);
+                tmem_ld32(tmem + (static_cast<uint32_t>(32 * q) << 16) + static_cast<uint32_t>(npad + c0), u);
+#pragma unroll
+                for (int j = 0; j < 32; ++j) v[j] += __uint_as_float(u[j]);
+                tmem_ld32(tmem + (static_cast<uint32_t>(32 * q) << 16) + static_cast<uint32_t>(2 * npad + c0), u);
+#pragma unroll
+                for (int j = 0; j < 32; ++j) v[j] += __uint_as_float(u[j]);
+                if (r < nrows) {
+                    float *o = out + row0 + r;
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        const int t = c0 + j;
+                        if (t < tokens) {
+                            float *d = o + static_cast<size_t>(t) * rows;
+                            const float val = v[j];
+                            *d = accumulate ? *d + val : val;
+                        }
+                    }
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) tmem_dealloc(tmem, tmem_cols);
+}
+
+}  // namespace
+
+namespace {
+
+// budget: kTcSmemBudget (one CTA per SM, two decode groups) or kTcSmemHalf
+// (two CTAs per SM, one group each).
+template <class F>
+bool plan_tc(int cols, int batch, TcLayout &L, size_t &smem, int budget = kTcSmemBudget) {
+    const int chunk = tc_chunk_cols(F::kBlk, F::kBytes);
+    if (!chunk || cols <= 0 || cols % chunk || batch < 1 || batch > kTcMaxTokens) return false;
+    L.npad = (batch + 15) / 16 * 16;
+    L.chunk_cols = chunk;
+    L.chunk_bytes = chunk / F::kBlk * F::kBytes;
+    // Two raw stages (loads overlap decoding) where they fit, else one.
+    for (int rs = 2; rs >= 1; --rs)
+        for (int sl = 4; sl >= 2; --sl) {
+            L.slots = sl;
+            L.raw_stages = rs;
+            if (static_cast<size_t>(L.bytes()) + 1024 <= static_cast<size_t>(budget)) {
+                smem = static_cast<size_t>(L.bytes()) + 1024;  // + alignment slack of the 1 KB base
+                return true;
+            }
+        }
+    return false;
+}
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                   const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+// The driver's cuTensorMapEncodeTiled through the runtime (the library links
+// no libcuda); looked up once, in relaxed capture mode (safe during a graph
+// capture).
+EncodeTiledFn encode_tiled() {
+    static const EncodeTiledFn fn = [] {
+        cudaStreamCaptureMode mode = cudaStreamCaptureModeRelaxed;
+        cudaThreadExchangeStreamCaptureMode(&mode);
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+        const cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q);
+        cudaThreadExchangeStreamCaptureMode(&mode);
+        return (e == cudaSuccess && q == cudaDriverEntryPointSuccess) ? reinterpret_cast<EncodeTiledFn>(p) : nullptr;
+    }();
+    return fn;
+}
+
+}  // namespace
+
+bool gemm_tc_supported(int kind, int cols, int batch) {
+    bool ok = false;
+    dispatch_format(kind, [&]<class F>() {
+        TcLayout L{};
+        size_t smem = 0;
+        ok = plan_tc<F>(cols, batch, L, smem);
+    });
+    return ok;
+}
+
+size_t gemm_tc_scratch_bytes(int cols, int batch) {
+    const size_t npad = static_cast<size_t>((batch + 15) / 16 * 16);
+    return static_cast<size_t>(cols / kTcAtomCols) * kTcLimbs * npad * kTcRowBytes;
+}
+
+int32_t gemm_tc_device(int32_t kind, float *out, const uint8_t *w, const float *x, int rows, int cols, int batch,
+                       uint8_t *scratch, cudaStream_t stream, const ColSegment &seg) {
+    int blk = 0, bytes = 0;
+    if (!reference_layout(kind, blk, bytes) || rows <= 0 || cols <= 0 || cols % blk) {
+        set_error("gemm_tc: unsupported format or shape");
+        return kUnsupported;
+    }
+    const int64_t row_bytes = static_cast<int64_t>(cols / blk) * bytes;
+    const int64_t pitch = seg.pitch ? seg.pitch : row_bytes;
+    const int xstride = seg.xstride ? seg.xstride : cols;
+    if ((reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(scratch)) & 15 ||
+        pitch % 16 || pitch < row_bytes || xstride < cols || xstride % 4) {
+        set_error("gemm_tc: weights, activations and scratch 16-byte aligned, row pitch a multiple of 16");
+        return kInvalid;
+    }
+    int32_t st = kUnsupported;
+    dispatch_format(kind, [&]<class F>() {
+        // Two CTAs per SM with one decode group each where their shared memory
+        // fits half an SM (two MMA-issuing threads keep the tensor core busier
+        // than one), else one CTA with two groups.
+        TcLayout L{};
+        size_t smem = 0;
+        const bool pair = plan_tc<F>(cols, batch, L, smem, kTcSmemHalf);
+        if (!pair && !plan_tc<F>(cols, batch, L, smem)) {
+            set_error("gemm_tc: no launch plan for this shape");
+            return;
+        }
+        // The weights as a 2-D tensor of 4-byte elements: rows x (row bytes / 4),
+        // row pitch `pitch` bytes; one box = 128 rows x one chunk's bytes.
+        const EncodeTiledFn encode = encode_tiled();
+        if (!encode) {
+            set_error("gemm_tc: cuTensorMapEncodeTiled is not available");
+            st = kUnsupported;
+            return;
+        }
+        CUtensorMap wmap;
+        const cuuint64_t dims[2] = {static_cast<cuuint64_t>(row_bytes / 4), static_cast<cuuint64_t>(rows)};
+        const cuuint64_t strides[1] = {static_cast<cuuint64_t>(pitch)};
+        const cuuint32_t box[2] = {static_cast<cuuint32_t>(L.chunk_bytes / 4), static_cast<cuuint32_t>(kTcRows)};
+        const cuuint32_t estr[2] = {1, 1};
+        const CUresult ce = encode(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<uint8_t *>(w), dims, strides,
+                                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (ce != CUDA_SUCCESS) {
+            set_error("gemm_tc: cuTensorMapEncodeTiled failed (%d)", static_cast<int>(ce));
+            st = kInvalid;
+            return;
+        }
+        auto kern = pair ? gemm_tc_kernel<F, 1> : gemm_tc_kernel<F, 2>;
+        if ((st = allow_dynamic_smem(kern, smem, "gemm_tc smem"))) return;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        const int64_t threads = static_cast<int64_t>(cols / kTcAtomCols) * L.npad * 4;
+        cudaLaunchConfig_t pc = {};
+        pc.gridDim = dim3(static_cast<unsigned>((threads + 255) / 256));
+        pc.blockDim = dim3(256);
+        pc.stream = stream;
+        pc.attrs = attr;
+        pc.numAttrs = 1;
+        cudaError_t e = cudaLaunchKernelEx(&pc, prep_tc_kernel, scratch, x, batch, L.npad, cols, xstride);
+        if (e != cudaSuccess) {
+            st = cuda_fail(e, "prep_tc_kernel");
+            return;
+        }
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(static_cast<unsigned>((rows + kTcRows - 1) / kTcRows));
+        cfg.blockDim = dim3(tc_threads(pair ? 1 : 2));
+        cfg.dynamicSmemBytes = smem;
+        cfg.stream = stream;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        e = cudaLaunchKernelEx(&cfg, kern, wmap, out, static_cast<const uint8_t *>(scratch), rows, cols, batch, L.npad,
+                               L.chunk_cols, L.chunk_bytes, L.slots, L.raw_stages, static_cast<int>(seg.accumulate),
+                               device_error_word());
+        st = e == cudaSuccess ? kOk : cuda_fail(e, "gemm_tc_kernel");
+    });
+    return st;
+}
+
+}  // namespace glmvx

@@ -63,6 +63,7 @@ SIGNATURES = {
     'glmvx_packed_gemv': ([_I32, _P, _P, _P, _I32, _I32, _P], _I32),
     'glmvx_packed_gemm': ([_I32, _P, _P, _P, _I32, _I32, _I32, _P], _I32),
     'glmvx_packed_gemm_path': ([_I32, _P, _P, _P, _I32, _I32, _I32, _P, _PI32], _I32),
+    'glmvx_packed_gemm_tc': ([_I32, _P, _P, _P, _I32, _I32, _I32, _P], _I32),
     'glmvx_unpack': ([_I32, _P, _P, _I64, _P], _I32),
     'glmvx_matvec_f32': ([_P, _P, _P, _I32, _I32, _P], _I32),
     'glmvx_matmul_nt': ([_P, _P, _P, _I32, _I32, _I32, _P], _I32),

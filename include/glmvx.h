@@ -140,10 +140,18 @@ int32_t glmvx_packed_gemv(int32_t kind, float *out, const uint8_t *w, const floa
  * Replaces glm_vx_packed_batch_v2_<kind> (kernels/packed.vx:473ff). */
 int32_t glmvx_packed_gemm(int32_t kind, float *out, const uint8_t *w, const float *x, int32_t rows, int32_t cols,
                           int32_t batch, void *stream);
+/* The tcgen05 packed GEMM alone: weights decoded to f32 and split into two
+ * TF32 limbs in shared memory, three kind::tf32 MMAs per K step accumulating in
+ * tensor memory; any format, batch 1..64, cols a multiple of the format's raw
+ * chunk (256 columns for Q8_0/Q4_K, 2048 for IQ1_S), 16-byte aligned w and x. */
+int32_t glmvx_packed_gemm_tc(int32_t kind, float *out, const uint8_t *w, const float *x, int32_t rows, int32_t cols,
+                             int32_t batch, void *stream);
 /* As glmvx_packed_gemm; *path reports the kernel taken
  * (1 stream GEMV, 2 generic, 3 F16 element path, 5 tensor-core int8 path,
  * 6 f16 tensor-core GEMM, 7 / 8 the int8 path / f16 GEMM over equal column
- * segments of rows too long for one plan, later segments adding in order). */
+ * segments of rows too long for one plan, later segments adding in order,
+ * 9 the tcgen05 GEMM of glmvx_packed_gemm_tc, taken from 65536 rows and 17
+ * tokens). */
 int32_t glmvx_packed_gemm_path(int32_t kind, float *out, const uint8_t *w, const float *x, int32_t rows,
                                int32_t cols, int32_t batch, void *stream, int32_t *path);
 /* Diagnostic decode of `blocks` reference blocks (F16: elements) to f32.
