@@ -95,12 +95,13 @@ int32_t gemm_f16_device(int32_t kind, float *out, const uint8_t *w, const float 
 
 // tcgen05 packed GEMM for token batches (packed_gemm_tc.cu): weights decoded
 // to f32 and split into two TF32 limbs in shared memory, activations split
-// likewise by a preparation kernel into `scratch` (gemm_tc_scratch_bytes),
+// likewise by a preparation kernel into `scratch` (gemm_tc_scratch_bytes:
+// the prepared limbs, plus the partial sums when a tile's columns are split),
 // three kind::tf32 MMAs per K step accumulating each row in tensor memory.
 // Any format, 1..64 tokens, cols a multiple of the format's raw chunk (256
 // columns for Q8_0 / Q4_K, 2048 for IQ1_S); 16-byte aligned w, x, scratch.
 bool gemm_tc_supported(int kind, int cols, int batch);
-size_t gemm_tc_scratch_bytes(int cols, int batch);
+size_t gemm_tc_scratch_bytes(int32_t kind, int rows, int cols, int batch);
 int32_t gemm_tc_device(int32_t kind, float *out, const uint8_t *w, const float *x, int rows, int cols, int batch,
                        uint8_t *scratch, cudaStream_t stream, const ColSegment &seg = {});
 

@@ -264,7 +264,7 @@ template <class F, int NG>
 __global__ void __launch_bounds__(tc_threads(NG), NG == 1 ? 2 : 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap wmap, float *__restrict__ out, const uint8_t *__restrict__ rec,
                    int rows, int cols, int tokens, int npad, int chunk_cols, int chunk_bytes, int slots, int raw_stages,
-                   int accumulate, int *err) {
+                   int accumulate, float *__restrict__ partial, int *err) {
     extern __shared__ uint8_t tc_smem_raw[];
     const uint32_t raw_s = smem_addr(tc_smem_raw);
     const uint32_t pad = ((raw_s + 1023u) & ~1023u) - raw_s;  // swizzled tiles: 1 KB-aligned addresses
@@ -278,7 +278,12 @@ __global__ void __launch_bounds__(tc_threads(NG), NG == 1 ? 2 : 1)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int row0 = blockIdx.x * kTcRows;
     const int nrows = min(kTcRows, rows - row0);
-    const int atoms = cols / kTcAtomCols, chunks = cols / chunk_cols, apc = chunk_cols / kTcAtomCols;
+    const int chunks_all = cols / chunk_cols, apc = chunk_cols / kTcAtomCols;
+    // K split (grid.y > 1): this CTA's chunks [c_begin, c_end) of the row;
+    // its sums go to partial[split][token][row] for the reduction kernel.
+    const int c_begin = static_cast<int>(static_cast<int64_t>(chunks_all) * blockIdx.y / gridDim.y);
+    const int c_end = static_cast<int>(static_cast<int64_t>(chunks_all) * (blockIdx.y + 1) / gridDim.y);
+    const int chunks = c_end - c_begin, atoms = chunks * apc;
     // 2 npad accumulator columns; the epilogue reads 32-column groups at 0 ..
     // npad and npad .. 2 npad, so at least npad + 32 columns are allocated.
     const int need = max(kTcLimbs * npad, 2 * npad + 32);
@@ -320,7 +325,7 @@ __global__ void __launch_bounds__(tc_threads(NG), NG == 1 ? 2 : 1)
             uint8_t *stage = base + L.raw_off() + s * L.raw_stage();
             if (lane == 0) {
                 mbar_arrive_expect_tx(&raw_full[s], static_cast<uint32_t>(kTcRows * chunk_bytes));
-                tma_load_2d(stage, &wmap, c * (chunk_bytes / 4), row0, &raw_full[s]);
+                tma_load_2d(stage, &wmap, (c_begin + c) * (chunk_bytes / 4), row0, &raw_full[s]);
             }
             __syncwarp();
             if (c == 0) grid_dependency_wait();  // the activation limbs come from the previous kernel
@@ -333,7 +338,7 @@ __global__ void __launch_bounds__(tc_threads(NG), NG == 1 ? 2 : 1)
                     } else {
                         uint8_t *b = base + slot * L.slot_bytes() + kTcLimbs * kTcATile;
                         mbar_arrive_expect_tx(&b_full[slot], static_cast<uint32_t>(kTcLimbs * L.b_tile()));
-                        bulk_g2s(b, rec + static_cast<size_t>(g) * kTcLimbs * L.b_tile(),
+                        bulk_g2s(b, rec + static_cast<size_t>(c_begin * apc + g) * kTcLimbs * L.b_tile(),
                                  static_cast<uint32_t>(kTcLimbs * L.b_tile()),
                                  &b_full[slot]);
                     }
@@ -443,14 +448,21 @@ __global__ void __launch_bounds__(tc_threads(NG), NG == 1 ? 2 : 1)
 #pragma unroll
                 for (int j = 0; j < 32; ++j) v[j] += __uint_as_float(u[j]);
                 if (r < nrows) {
-                    float *o = out + row0 + r;
+                    if (gridDim.y > 1) {
+                        float *o = partial + static_cast<size_t>(blockIdx.y) * tokens * rows + row0 + r;
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) {
-                        const int t = c0 + j;
-                        if (t < tokens) {
-                            float *d = o + static_cast<size_t>(t) * rows;
-                            const float val = v[j];
-                            *d = accumulate ? *d + val : val;
+                        for (int j = 0; j < 32; ++j)
+                            if (c0 + j < tokens) o[static_cast<size_t>(c0 + j) * rows] = v[j];
+                    } else {
+                        float *o = out + row0 + r;
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) {
+                            const int t = c0 + j;
+                            if (t < tokens) {
+                                float *d = o + static_cast<size_t>(t) * rows;
+                                const float val = v[j];
+                                *d = accumulate ? *d + val : val;
+                            }
                         }
                     }
                 }
@@ -460,6 +472,20 @@ __global__ void __launch_bounds__(tc_threads(NG), NG == 1 ? 2 : 1)
     tc_fence_before();
     __syncthreads();
     if (warp == 1) tmem_dealloc(tmem, tmem_cols);
+}
+
+// out[t][r] (+)= sum over splits, in split order, of partial[split][t][r].
+__global__ void __launch_bounds__(256)
+    tc_split_reduce_kernel(float *__restrict__ out, const float *__restrict__ partial, int64_t n, int splits,
+                           int accumulate) {
+    grid_dependency_wait();
+    allow_dependent_launch();
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        float v = partial[i];
+        for (int k = 1; k < splits; ++k) v += partial[static_cast<int64_t>(k) * n + i];
+        out[i] = accumulate ? out[i] + v : v;
+    }
 }
 
 }  // namespace
@@ -520,9 +546,41 @@ bool gemm_tc_supported(int kind, int cols, int batch) {
     return ok;
 }
 
-size_t gemm_tc_scratch_bytes(int cols, int batch) {
-    const size_t npad = static_cast<size_t>((batch + 15) / 16 * 16);
-    return static_cast<size_t>(cols / kTcAtomCols) * kTcLimbs * npad * kTcRowBytes;
+namespace {
+
+// Launch shape: two CTAs per SM (one decode group) where shared memory
+// allows, else one with two groups; when the 128-row tiles leave SMs idle,
+// each tile's chunks are split over grid.y CTAs (at least two chunks each)
+// whose partial sums a reduction adds in split order.
+struct TcShape {
+    TcLayout L{};
+    size_t smem = 0;
+    bool pair = false;
+    int splits = 1;
+    size_t rec_bytes = 0, scratch_bytes = 0;
+};
+
+template <class F>
+bool shape_tc(int rows, int cols, int batch, TcShape &sh) {
+    sh.pair = plan_tc<F>(cols, batch, sh.L, sh.smem, kTcSmemHalf);
+    if (!sh.pair && !plan_tc<F>(cols, batch, sh.L, sh.smem)) return false;
+    const int tiles = (rows + kTcRows - 1) / kTcRows, chunks = cols / sh.L.chunk_cols;
+    const int slots = sm_count() * (sh.pair ? 2 : 1);
+    sh.splits = std::max(1, std::min(chunks / 2, slots / std::max(tiles, 1)));
+    sh.rec_bytes = (static_cast<size_t>(cols / kTcAtomCols) * kTcLimbs * sh.L.npad * kTcRowBytes + 255) & ~size_t(255);
+    sh.scratch_bytes = sh.rec_bytes + (sh.splits > 1 ? static_cast<size_t>(sh.splits) * batch * rows * 4 : 0);
+    return true;
+}
+
+}  // namespace
+
+size_t gemm_tc_scratch_bytes(int32_t kind, int rows, int cols, int batch) {
+    size_t bytes = 0;
+    dispatch_format(kind, [&]<class F>() {
+        TcShape sh;
+        if (shape_tc<F>(rows, cols, batch, sh)) bytes = sh.scratch_bytes;
+    });
+    return bytes;
 }
 
 int32_t gemm_tc_device(int32_t kind, float *out, const uint8_t *w, const float *x, int rows, int cols, int batch,
@@ -544,14 +602,15 @@ int32_t gemm_tc_device(int32_t kind, float *out, const uint8_t *w, const float *
     dispatch_format(kind, [&]<class F>() {
         // Two CTAs per SM with one decode group each where their shared memory
         // fits half an SM (two MMA-issuing threads keep the tensor core busier
-        // than one), else one CTA with two groups.
-        TcLayout L{};
-        size_t smem = 0;
-        const bool pair = plan_tc<F>(cols, batch, L, smem, kTcSmemHalf);
-        if (!pair && !plan_tc<F>(cols, batch, L, smem)) {
+        // than one), else one CTA with two groups; K split over idle SMs.
+        TcShape sh;
+        if (!shape_tc<F>(rows, cols, batch, sh)) {
             set_error("gemm_tc: no launch plan for this shape");
             return;
         }
+        const TcLayout &L = sh.L;
+        const size_t smem = sh.smem;
+        const bool pair = sh.pair;
         // The weights as a 2-D tensor of 4-byte elements: rows x (row bytes / 4),
         // row pitch `pitch` bytes; one box = 128 rows x one chunk's bytes.
         const EncodeTiledFn encode = encode_tiled();
@@ -591,7 +650,7 @@ int32_t gemm_tc_device(int32_t kind, float *out, const uint8_t *w, const float *
             return;
         }
         cudaLaunchConfig_t cfg = {};
-        cfg.gridDim = dim3(static_cast<unsigned>((rows + kTcRows - 1) / kTcRows));
+        cfg.gridDim = dim3(static_cast<unsigned>((rows + kTcRows - 1) / kTcRows), static_cast<unsigned>(sh.splits));
         cfg.blockDim = dim3(tc_threads(pair ? 1 : 2));
         cfg.dynamicSmemBytes = smem;
         cfg.stream = stream;
@@ -599,8 +658,28 @@ int32_t gemm_tc_device(int32_t kind, float *out, const uint8_t *w, const float *
         cfg.numAttrs = 1;
         e = cudaLaunchKernelEx(&cfg, kern, wmap, out, static_cast<const uint8_t *>(scratch), rows, cols, batch, L.npad,
                                L.chunk_cols, L.chunk_bytes, L.slots, L.raw_stages, static_cast<int>(seg.accumulate),
-                               device_error_word());
-        st = e == cudaSuccess ? kOk : cuda_fail(e, "gemm_tc_kernel");
+                               reinterpret_cast<float *>(scratch + sh.rec_bytes), device_error_word());
+        if (e != cudaSuccess) {
+            st = cuda_fail(e, "gemm_tc_kernel");
+            return;
+        }
+        if (sh.splits > 1) {
+            const int64_t n = static_cast<int64_t>(batch) * rows;
+            cudaLaunchConfig_t rc = {};
+            rc.gridDim = dim3(static_cast<unsigned>(std::min<int64_t>((n + 255) / 256, 4 * sm_count())));
+            rc.blockDim = dim3(256);
+            rc.stream = stream;
+            rc.attrs = attr;
+            rc.numAttrs = 1;
+            e = cudaLaunchKernelEx(&rc, tc_split_reduce_kernel, out,
+                                   reinterpret_cast<const float *>(scratch + sh.rec_bytes), n, sh.splits,
+                                   static_cast<int>(seg.accumulate));
+            if (e != cudaSuccess) {
+                st = cuda_fail(e, "tc_split_reduce_kernel");
+                return;
+            }
+        }
+        st = kOk;
     });
     return st;
 }

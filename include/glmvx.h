@@ -150,8 +150,9 @@ int32_t glmvx_packed_gemm_tc(int32_t kind, float *out, const uint8_t *w, const f
  * (1 stream GEMV, 2 generic, 3 F16 element path, 5 tensor-core int8 path,
  * 6 f16 tensor-core GEMM, 7 / 8 the int8 path / f16 GEMM over equal column
  * segments of rows too long for one plan, later segments adding in order,
- * 9 the tcgen05 GEMM of glmvx_packed_gemm_tc, taken from 65536 rows and 17
- * tokens). */
+ * 9 the tcgen05 GEMM of glmvx_packed_gemm_tc, taken where it measured faster:
+ * 33..64 tokens on long rows or many tiles, 17..32 tokens on 16384+ columns or
+ * 65536+ rows). */
 int32_t glmvx_packed_gemm_path(int32_t kind, float *out, const uint8_t *w, const float *x, int32_t rows,
                                int32_t cols, int32_t batch, void *stream, int32_t *path);
 /* Diagnostic decode of `blocks` reference blocks (F16: elements) to f32.

@@ -13,6 +13,7 @@ from test_gpu_packed import _device_gemm
 pytestmark = pytest.mark.gpu
 
 PATH_GEMM = 6
+PATH_TC = 9
 
 
 def _case(kind, rows, cols, batch, seed):
@@ -29,7 +30,10 @@ def _case(kind, rows, cols, batch, seed):
 def test_gemm_matches_oracle(cuda_lib, oracle, kind, rows, cols, batch):
     raw, x = _case(kind, rows, cols, batch, rows + batch)
     got, path = _device_gemm(cuda_lib, kind, raw, rows, cols, x)
-    assert path == PATH_GEMM
+    # long rows at 33..64 tokens take the tcgen05 GEMM (path 9, its own tests
+    # in test_gpu_packed_tc.py); the rest the f16 GEMM
+    long_rows = cols >= (12288 if kind == 19 else 6144)
+    assert path == (PATH_TC if batch > 32 and (long_rows or rows >= 16384) else PATH_GEMM)
     want = oracle.packed_linear_batch(raw, kind, (rows, cols), x)
     dec = unpack_for_validation(oracle.lib, raw, kind, (rows, cols))
     assert_close_dot(got, want, dec, x)
