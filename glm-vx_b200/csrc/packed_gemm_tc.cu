@@ -550,8 +550,8 @@ namespace {
 
 // Launch shape: two CTAs per SM (one decode group) where shared memory
 // allows, else one with two groups; when the 128-row tiles leave SMs idle,
-// each tile's chunks are split over grid.y CTAs (at least two chunks each)
-// whose partial sums a reduction adds in split order.
+// each tile's chunks are split over grid.y CTAs (whole chunks, at least 512
+// columns each) whose partial sums a reduction adds in split order.
 struct TcShape {
     TcLayout L{};
     size_t smem = 0;
@@ -566,7 +566,20 @@ bool shape_tc(int rows, int cols, int batch, TcShape &sh) {
     if (!sh.pair && !plan_tc<F>(cols, batch, sh.L, sh.smem)) return false;
     const int tiles = (rows + kTcRows - 1) / kTcRows, chunks = cols / sh.L.chunk_cols;
     const int slots = sm_count() * (sh.pair ? 2 : 1);
-    sh.splits = std::max(1, std::min(chunks / 2, slots / std::max(tiles, 1)));
+    // Whole chunks, at least 16 atoms (512 columns) per split; the split count
+    // minimising waves x atoms per CTA (a CTA's time is its chain of atoms).
+    // Only when the tiles leave CTA slots idle (the partial sums cost a
+    // write and a read of splits x tokens x rows floats).
+    const int by_atoms = tiles >= slots ? 1 : std::max(1, std::min(chunks, cols / kTcAtomCols / 16));
+    int64_t best = -1;
+    for (int sp = 1; sp <= by_atoms; ++sp) {
+        const int64_t waves = (static_cast<int64_t>(tiles) * sp + slots - 1) / slots;
+        const int64_t cost = waves * ((chunks + sp - 1) / sp);
+        if (best < 0 || cost < best) {
+            best = cost;
+            sh.splits = sp;
+        }
+    }
     sh.rec_bytes = (static_cast<size_t>(cols / kTcAtomCols) * kTcLimbs * sh.L.npad * kTcRowBytes + 255) & ~size_t(255);
     sh.scratch_bytes = sh.rec_bytes + (sh.splits > 1 ? static_cast<size_t>(sh.splits) * batch * rows * 4 : 0);
     return true;
