@@ -133,6 +133,7 @@ __device__ __forceinline__ float byte_biased(uint32_t u) {
 // Generic: two octets of the format's decoder.
 template <class F>
 struct TcDecode {
+    static constexpr bool kWords = false;
     __device__ __forceinline__ static void run(const uint8_t *rc, int a, int h, float (&w)[16]) {
 #pragma unroll
         for (int o = 0; o < 2; ++o) {
@@ -148,6 +149,32 @@ struct TcDecode {
 // mantissa of 2^23 and one subtraction gives q exactly.
 template <>
 struct TcDecode<FmtQ8_0> {
+    static constexpr bool kWords = true;
+    // Words q and q + 4 (weights 4q..4q+3 and 16+4q..16+4q+3) of atom a of
+    // row `rc`: the lanes of a warp, 8 rows x 4 quarters, read 32 different
+    // banks (rows are 68 words apart).
+    __device__ __forceinline__ static void words(const uint8_t *rc, int a, int q, float (&w)[8]) {
+        const uint8_t *blk = rc + a * FmtQ8_0::kBytes;
+        const float d = h2f(u16(blk));
+        uint32_t x[2];
+        if (a & 1) {  // the block's bytes start 4-byte aligned
+            const uint32_t *p = reinterpret_cast<const uint32_t *>(blk + 2);
+            x[0] = p[q];
+            x[1] = p[q + 4];
+        } else {  // 2 bytes past alignment: join aligned neighbours
+            const uint32_t *p = reinterpret_cast<const uint32_t *>(blk);
+            x[0] = __funnelshift_r(p[q], p[q + 1], 16);
+            x[1] = __funnelshift_r(p[q + 4], p[q + 5], 16);
+        }
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            const uint32_t u = x[i] ^ 0x80808080u;
+            w[4 * i + 0] = __fmul_rn(d, byte_biased<0>(u) - 8388736.0f);
+            w[4 * i + 1] = __fmul_rn(d, byte_biased<1>(u) - 8388736.0f);
+            w[4 * i + 2] = __fmul_rn(d, byte_biased<2>(u) - 8388736.0f);
+            w[4 * i + 3] = __fmul_rn(d, byte_biased<3>(u) - 8388736.0f);
+        }
+    }
     __device__ __forceinline__ static void run(const uint8_t *rc, int a, int h, float (&w)[16]) {
         const uint8_t *blk = rc + a * FmtQ8_0::kBytes;
         const float d = h2f(u16(blk));
@@ -179,6 +206,22 @@ struct TcDecode<FmtQ8_0> {
 // superblock, atom a its sub-block a; the 16 nibble bytes in one 16-byte load.
 template <>
 struct TcDecode<FmtQ4_K> {
+    static constexpr bool kWords = true;
+    // As TcDecode<FmtQ8_0>::words (rows 36 words apart).
+    __device__ __forceinline__ static void words(const uint8_t *rc, int a, int q, float (&w)[8]) {
+        const float dl = __fmul_rn(h2f(u16(rc)), static_cast<float>(k4_scale(rc + 4, a)));
+        const float ml = __fmul_rn(h2f(u16(rc + 2)), static_cast<float>(k4_min(rc + 4, a)));
+        const uint32_t *p = reinterpret_cast<const uint32_t *>(rc + 16 + 32 * (a >> 1));
+        const int shift = 4 * (a & 1);
+        const uint32_t x[2] = {(p[q] >> shift) & 0x0F0F0F0Fu, (p[q + 4] >> shift) & 0x0F0F0F0Fu};
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            w[4 * i + 0] = __fsub_rn(__fmul_rn(dl, byte_biased<0>(x[i]) - 8388608.0f), ml);
+            w[4 * i + 1] = __fsub_rn(__fmul_rn(dl, byte_biased<1>(x[i]) - 8388608.0f), ml);
+            w[4 * i + 2] = __fsub_rn(__fmul_rn(dl, byte_biased<2>(x[i]) - 8388608.0f), ml);
+            w[4 * i + 3] = __fsub_rn(__fmul_rn(dl, byte_biased<3>(x[i]) - 8388608.0f), ml);
+        }
+    }
     __device__ __forceinline__ static void run(const uint8_t *rc, int a, int h, float (&w)[16]) {
         const float dl = __fmul_rn(h2f(u16(rc)), static_cast<float>(k4_scale(rc + 4, a)));
         const float ml = __fmul_rn(h2f(u16(rc + 2)), static_cast<float>(k4_min(rc + 4, a)));
@@ -401,25 +444,56 @@ __global__ void __launch_bounds__(tc_threads(NG), NG == 1 ? 2 : 1)
                     ok = false;
                     break;
                 }
-                float v[16];
-                if (r < nrows) {
-                    TcDecode<F>::run(rc, a, h, v);
-                } else {
-#pragma unroll
-                    for (int e = 0; e < 16; ++e) v[e] = 0.0f;
-                }
                 uint8_t *at = base + slot * L.slot_bytes();
+                if constexpr (TcDecode<F>::kWords) {
+                    // lane = (row j, quarter q) of 8 rows per warp, two passes of
+                    // 64 rows: conflict-free 4-byte raw loads and 8-byte stores
+                    // (a half-warp covers 8 rows x both word parities)
+                    const int wj = lane & 7, wq = lane >> 3, wg = (warp - 2) % kTcGroupWarps;
+                    const uint8_t *stage = rc - r * chunk_bytes;
 #pragma unroll
-                for (int i = 0; i < 2; ++i) {  // 8 weights -> one 16-byte chunk per limb
-                    uint32_t l[3][8];
+                    for (int pass = 0; pass < 2; ++pass) {
+                        const int rr = pass * 64 + wg * 8 + wj;
+                        float v[8];
+                        if (rr < nrows) {
+                            TcDecode<F>::words(stage + rr * chunk_bytes, a, wq, v);
+                        } else {
 #pragma unroll
-                    for (int e = 0; e < 8; ++e) bf16_limbs(v[8 * i + e], l[0][e], l[1][e], l[2][e]);
-                    const uint32_t off = kmajor_offset(r, 2 * h + i, kTcRows);
+                            for (int e = 0; e < 8; ++e) v[e] = 0.0f;
+                        }
 #pragma unroll
-                    for (int k = 0; k < kTcLimbs; ++k)
-                        *reinterpret_cast<uint4 *>(at + k * kTcATile + off) =
-                            make_uint4(pack_bf16(l[k][0], l[k][1]), pack_bf16(l[k][2], l[k][3]),
-                                       pack_bf16(l[k][4], l[k][5]), pack_bf16(l[k][6], l[k][7]));
+                        for (int hw = 0; hw < 2; ++hw) {  // word wq, then wq + 4
+                            const int wd = wq + 4 * hw;   // K positions 4wd .. 4wd+3
+                            uint32_t l[3][4];
+#pragma unroll
+                            for (int e = 0; e < 4; ++e) bf16_limbs(v[4 * hw + e], l[0][e], l[1][e], l[2][e]);
+                            const uint32_t off = kmajor_offset(rr, wd >> 1, kTcRows) + 8 * (wd & 1);
+#pragma unroll
+                            for (int k = 0; k < kTcLimbs; ++k)
+                                *reinterpret_cast<uint2 *>(at + k * kTcATile + off) =
+                                    make_uint2(pack_bf16(l[k][0], l[k][1]), pack_bf16(l[k][2], l[k][3]));
+                        }
+                    }
+                } else {
+                    float v[16];
+                    if (r < nrows) {
+                        TcDecode<F>::run(rc, a, h, v);
+                    } else {
+#pragma unroll
+                        for (int e = 0; e < 16; ++e) v[e] = 0.0f;
+                    }
+#pragma unroll
+                    for (int i = 0; i < 2; ++i) {  // 8 weights -> one 16-byte chunk per limb
+                        uint32_t l[3][8];
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) bf16_limbs(v[8 * i + e], l[0][e], l[1][e], l[2][e]);
+                        const uint32_t off = kmajor_offset(r, 2 * h + i, kTcRows);
+#pragma unroll
+                        for (int k = 0; k < kTcLimbs; ++k)
+                            *reinterpret_cast<uint4 *>(at + k * kTcATile + off) =
+                                make_uint4(pack_bf16(l[k][0], l[k][1]), pack_bf16(l[k][2], l[k][3]),
+                                           pack_bf16(l[k][4], l[k][5]), pack_bf16(l[k][6], l[k][7]));
+                    }
                 }
                 fence_proxy_async_smem();  // generic-proxy stores -> the tensor cores' async proxy
                 __syncwarp();
