@@ -173,6 +173,24 @@ class GPUBackend:
         return arrays
 
     # ----------------------------------------------------------- weights
+    def unpack(self, raw, kind, blocks):
+        """Decode `blocks` GGML blocks (F16: elements) of `raw` to f32 on the
+        device (glmvx_unpack) and return them as a host array."""
+        raw = np.ascontiguousarray(raw).view(np.uint8).reshape(-1)
+        block = 1 if int(kind) == 1 else LAYOUTS[int(kind)][0]
+        n = int(blocks) * block
+        src, dst = rt.DeviceBuffer(max(raw.nbytes, 16)), rt.DeviceBuffer(max(4 * n, 16))
+        try:
+            src.upload(raw, self.stream.handle)
+            rt.call('glmvx_unpack', int(kind), dst.ptr, src.ptr, int(blocks), self.stream.handle)
+            out = np.empty(n, np.float32)
+            dst.download(out, self.stream.handle)
+            self.stream.synchronize()
+            return out
+        finally:
+            src.close()
+            dst.close()
+
     def resident(self, raw, kind, shape):
         """Upload a packed matrix once; the handle replaces `raw` in calls."""
         self._begin()

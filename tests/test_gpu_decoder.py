@@ -107,7 +107,7 @@ def _gpus():
         return 0
 
 
-def _ep_rank_main(rank, world, boot_dir, out_path):
+def _ep_rank_main(rank, world, boot_dir, out_path, gguf_path=None):
     import sys
     from pathlib import Path
     root = Path(__file__).resolve().parents[1]
@@ -119,7 +119,11 @@ def _ep_rank_main(rank, world, boot_dir, out_path):
     backend = GPUBackend(rank)
     boot = FileBootstrap(boot_dir, rank, world)
     config = R.dropin_config(width=2048)
-    ckpt = R.PackedCheckpoint(config, seed=1)
+    if gguf_path:  # this rank's experts read straight from the split GGUF files
+        from gpu.gguf_source import GGUFSource
+        ckpt = GGUFSource(gguf_path, config, backend)
+    else:
+        ckpt = R.PackedCheckpoint(config, seed=1)
     per = len(EP_PROMPTS) // world
     dec = ResidentDecoder(backend, config, ckpt, batch=per, capacity=32,
                           moe_layer_factory=expert_parallel_moe(rank, world, boot.allgather))
@@ -130,11 +134,14 @@ def _ep_rank_main(rank, world, boot_dir, out_path):
 
 
 @pytest.mark.skipif(_gpus() < 2, reason='needs two GPUs')
-def test_expert_parallel_decoder_on_two_gpus(tmp_path):
+@pytest.mark.parametrize('source', ['packed', 'gguf'])
+def test_expert_parallel_decoder_on_two_gpus(tmp_path, source):
     """Two processes, one GPU each: each decodes two of the four prompts
     (data-parallel attention) while the sparse layers' experts are split
     between the GPUs (gpu/ep.py over IPC mailboxes); every sequence's greedy
-    tokens equal the reference model's own decode on the oracle."""
+    tokens equal the reference model's own decode on the oracle.  With
+    source 'gguf' the ranks load the checkpoint from split GGUF files, each
+    uploading only its own experts' slices."""
     import multiprocessing as mp
     refmodel.ref_glm_vx()
     from glm_vx.model import GlmMoeDsaModel
@@ -143,8 +150,13 @@ def test_expert_parallel_decoder_on_two_gpus(tmp_path):
     ckpt = refmodel.PackedCheckpoint(config, seed=1)
     model = GlmMoeDsaModel(config, ckpt, refmodel.ref_vx_backend(loader.parallel()), packed_weights=True)
     want = [refmodel.greedy(model, p, NEW_TOKENS, grouped_prefill=False)[0] for p in EP_PROMPTS]
+    gguf_path = None
+    if source == 'gguf':
+        import gguf_fixture
+        gguf_path = str(gguf_fixture.write_checkpoint(ckpt, config, tmp_path / 'glm.gguf', split_max_tensors=24)[0])
     ctx = mp.get_context('spawn')
-    procs = [ctx.Process(target=_ep_rank_main, args=(r, 2, str(tmp_path / 'boot'), str(tmp_path / f'r{r}.npy')))
+    procs = [ctx.Process(target=_ep_rank_main,
+                         args=(r, 2, str(tmp_path / 'boot'), str(tmp_path / f'r{r}.npy'), gguf_path))
              for r in range(2)]
     for p in procs:
         p.start()
