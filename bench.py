@@ -448,7 +448,27 @@ def fused_gemv_sweep(rt, lib, dev, stream, steps, peak):
     us = graph_time(rt, stream, launch8, reps) / reps * 1e3
     alg = wbytes + sc.nbytes + x.nbytes + 4 * rows
     res['fp8_e4m3_6144x6144_b1'] = {'us': us, 'gbs': alg / us / 1e3, 'frac_of_measured_hbm': alg / us / 1e3 / peak}
-    for b in (wbuf, sd, xd, od):
+    for b in (xd, od):
+        b.close()
+    # The same weights for 16 and 32 tokens through glmvx_fp8_gemm (tcgen05).
+    for b in (16, 32):
+        xb = rng.normal(size=(b, cols)).astype(np.float32)
+        xd, od, path = rt.DeviceBuffer(xb.nbytes), rt.DeviceBuffer(4 * rows * b), C.c_int32(-1)
+        xd.upload(xb, stream.handle)
+
+        def launch8b(i):
+            rt.check(lib, lib.glmvx_fp8_gemm(od.ptr, wbuf.ptr + (i % copies) * stride, sd.ptr, xd.ptr, rows, cols, b,
+                                             C.byref(path), stream.handle), 'glmvx_fp8_gemm')
+        for i in range(3):
+            launch8b(i)
+        us = graph_time(rt, stream, launch8b, reps) / reps * 1e3
+        alg = wbytes + sc.nbytes + xb.nbytes + 4 * rows * b
+        res[f'fp8_e4m3_6144x6144_b{b}'] = {'us': us, 'gbs': alg / us / 1e3, 'frac_of_measured_hbm': alg / us / 1e3 / peak,
+                                          'path': PATH_NAMES.get(path.value, str(path.value)),
+                                          'us_per_token_gemv': res['fp8_e4m3_6144x6144_b1']['us']}
+        xd.close()
+        od.close()
+    for b in (wbuf, sd):
         b.close()
     return res
 

@@ -20,6 +20,7 @@
 #include <cuda_fp8.h>
 
 #include "common.cuh"
+#include "mma_gemv.cuh"
 
 namespace glmvx {
 
@@ -150,6 +151,37 @@ __global__ void __launch_bounds__(kFp8Threads)
         for (int p = 0; p < split; ++p) total += part_sum[warp + p][lane];
         out[row0 + lane] = total;
     }
+}
+
+
+// Batched: out[t][r] for tokens t < batch, x[t][cols] row-major.  Columns a
+// multiple of 256 and 2..64 tokens go to the tcgen05 GEMM (weights times
+// their tile scale in f32, three bf16 limbs); otherwise one GEMV per token.
+GLMVX_EXPORT int32_t glmvx_fp8_gemm(float *out, const uint8_t *weight, const float *scales, const float *x,
+                                    int32_t rows, int32_t cols, int32_t batch, int32_t *path, void *stream) {
+    if (rows < 1 || cols < 0 || batch < 0 || !out || !weight || !scales || (cols && batch && !x)) {
+        set_error("fp8 gemm: rows must be >= 1, cols and batch >= 0 and pointers set");
+        return kInvalid;
+    }
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (batch >= 2 && fp8_gemm_tc_supported(cols, batch) &&
+        ((reinterpret_cast<uintptr_t>(weight) | reinterpret_cast<uintptr_t>(x)) & 15) == 0) {
+        if (path) *path = 9;
+        keep_pool_memory();
+        void *scratch = nullptr;
+        GLMVX_CUDA(cudaMallocAsync(&scratch, fp8_gemm_tc_scratch_bytes(rows, cols, batch), st));
+        const int32_t rc = fp8_gemm_tc_device(out, weight, scales, x, rows, cols, batch,
+                                              static_cast<uint8_t *>(scratch), st);
+        const cudaError_t fe = cudaFreeAsync(scratch, st);
+        if (rc) return rc;
+        return fe == cudaSuccess ? kOk : cuda_fail(fe, "cudaFreeAsync");
+    }
+    if (path) *path = 1;
+    for (int t = 0; t < batch; ++t)
+        if (const int32_t rc = glmvx_fp8_matvec(out + static_cast<int64_t>(t) * rows, weight, scales,
+                                                x + static_cast<int64_t>(t) * cols, rows, cols, stream))
+            return rc;
+    return kOk;
 }
 
 }  // namespace glmvx

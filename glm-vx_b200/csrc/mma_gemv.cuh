@@ -105,4 +105,17 @@ size_t gemm_tc_scratch_bytes(int32_t kind, int rows, int cols, int batch);
 int32_t gemm_tc_device(int32_t kind, float *out, const uint8_t *w, const float *x, int rows, int cols, int batch,
                        uint8_t *scratch, cudaStream_t stream, const ColSegment &seg = {});
 
+// The same kernel for FP8 E4M3FN weights with f32 scales per 128 x 128 tile
+// (the gpu/fp8.vx contract): out[t][r] = sum_c (decode(w[r][c]) *
+// s[r/128][c/128]) * x[t][c]; cols a multiple of 256, 1..64 tokens.
+// Keep freed blocks of the device's default stream-ordered pool (the
+// tensor-core paths' scratch) instead of releasing them at every
+// synchronisation; once per device, safe inside a graph capture.
+void keep_pool_memory();
+
+bool fp8_gemm_tc_supported(int cols, int batch);
+size_t fp8_gemm_tc_scratch_bytes(int rows, int cols, int batch);
+int32_t fp8_gemm_tc_device(float *out, const uint8_t *w, const float *scales, const float *x, int rows, int cols,
+                           int batch, uint8_t *scratch, cudaStream_t stream);
+
 }  // namespace glmvx

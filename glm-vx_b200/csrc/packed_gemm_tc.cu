@@ -43,6 +43,7 @@
 #include <type_traits>
 
 #include <cuda.h>
+#include <cuda_fp8.h>
 
 #include "codecs.cuh"
 #include "mma_gemv.cuh"
@@ -153,7 +154,7 @@ struct TcDecode<FmtQ8_0> {
     // Words q and q + 4 (weights 4q..4q+3 and 16+4q..16+4q+3) of atom a of
     // row `rc`: the lanes of a warp, 8 rows x 4 quarters, read 32 different
     // banks (rows are 68 words apart).
-    __device__ __forceinline__ static void words(const uint8_t *rc, int a, int q, float (&w)[8]) {
+    __device__ __forceinline__ static void words(const uint8_t *rc, int a, int q, float, float (&w)[8]) {
         const uint8_t *blk = rc + a * FmtQ8_0::kBytes;
         const float d = h2f(u16(blk));
         uint32_t x[2];
@@ -208,7 +209,7 @@ template <>
 struct TcDecode<FmtQ4_K> {
     static constexpr bool kWords = true;
     // As TcDecode<FmtQ8_0>::words (rows 36 words apart).
-    __device__ __forceinline__ static void words(const uint8_t *rc, int a, int q, float (&w)[8]) {
+    __device__ __forceinline__ static void words(const uint8_t *rc, int a, int q, float, float (&w)[8]) {
         const float dl = __fmul_rn(h2f(u16(rc)), static_cast<float>(k4_scale(rc + 4, a)));
         const float ml = __fmul_rn(h2f(u16(rc + 2)), static_cast<float>(k4_min(rc + 4, a)));
         const uint32_t *p = reinterpret_cast<const uint32_t *>(rc + 16 + 32 * (a >> 1));
@@ -249,6 +250,35 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, i
         : "memory");
 }
 
+// FP8 E4M3FN weights with f32 scales per 128 x 128 tile (gpu/fp8.vx:20-38):
+// w = decode(byte) * scale, one byte per weight; only this kernel uses it.
+struct FmtFP8 {
+    static constexpr int kBlk = 1, kBytes = 1;
+};
+
+template <>
+struct TcDecode<FmtFP8> {
+    static constexpr bool kWords = true;
+    // Bytes of words q and q + 4 of atom a (32 bytes) through the hardware
+    // E4M3x2 -> f16x2 conversion (exact, NaN codes to NaN), times the tile's
+    // scale in f32 as the reference multiplies them.
+    __device__ __forceinline__ static void words(const uint8_t *rc, int a, int q, float scale, float (&w)[8]) {
+        const uint32_t *p = reinterpret_cast<const uint32_t *>(rc + a * kTcAtomCols);
+        const uint32_t x[2] = {p[q], p[q + 4]};
+#pragma unroll
+        for (int i = 0; i < 2; ++i)
+#pragma unroll
+            for (int k = 0; k < 2; ++k) {
+                const __half2_raw h = __nv_cvt_fp8x2_to_halfraw2(
+                    static_cast<__nv_fp8x2_storage_t>((x[i] >> (16 * k)) & 0xffffu), __NV_E4M3);
+                const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&h));
+                w[4 * i + 2 * k] = __fmul_rn(f.x, scale);
+                w[4 * i + 2 * k + 1] = __fmul_rn(f.y, scale);
+            }
+    }
+    __device__ __forceinline__ static void run(const uint8_t *, int, int, float (&)[16]) {}
+};
+
 // A bounded wait whose outcome is the same for every lane of the warp (the
 // tensor-memory loads after it are warp-collective).
 __device__ __forceinline__ bool warp_wait(uint64_t *bar, uint32_t parity) {
@@ -259,9 +289,13 @@ __device__ __forceinline__ bool warp_wait(uint64_t *bar, uint32_t parity) {
 // Shared-memory layout of a CTA (offsets from the 1 KB-aligned base).
 struct TcLayout {
     int npad, chunk_cols, chunk_bytes, slots, raw_stages;
+    // Raw stage row pitch: the chunk's bytes, plus 16 when they are a multiple
+    // of 128 (otherwise every row of the box would start in the same bank);
+    // the TMA box then reads 16 bytes of the next chunk (or zeros past the row).
+    __host__ __device__ int raw_row() const { return chunk_bytes + ((chunk_bytes % 128) == 0 ? 16 : 0); }
     __host__ __device__ int b_tile() const { return npad * kTcRowBytes; }     // one limb of one atom
     __host__ __device__ int slot_bytes() const { return kTcLimbs * (kTcATile + b_tile()); }
-    __host__ __device__ int raw_stage() const { return kTcRows * chunk_bytes; }
+    __host__ __device__ int raw_stage() const { return kTcRows * raw_row(); }
     __host__ __device__ int raw_off() const { return slots * slot_bytes(); }
     __host__ __device__ int bar_off() const { return (raw_off() + raw_stages * raw_stage() + 15) & ~15; }
     // raw_full[2], raw_empty[2], a_full[slots], b_full[slots], op_empty[slots], acc_full, tmem slot
@@ -307,7 +341,8 @@ template <class F, int NG>
 __global__ void __launch_bounds__(tc_threads(NG), NG == 1 ? 2 : 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap wmap, float *__restrict__ out, const uint8_t *__restrict__ rec,
                    int rows, int cols, int tokens, int npad, int chunk_cols, int chunk_bytes, int slots, int raw_stages,
-                   int accumulate, float *__restrict__ partial, int *err) {
+                   int accumulate, float *__restrict__ partial, const float *__restrict__ scales, int scale_cols,
+                   int *err) {
     extern __shared__ uint8_t tc_smem_raw[];
     const uint32_t raw_s = smem_addr(tc_smem_raw);
     const uint32_t pad = ((raw_s + 1023u) & ~1023u) - raw_s;  // swizzled tiles: 1 KB-aligned addresses
@@ -367,7 +402,7 @@ __global__ void __launch_bounds__(tc_threads(NG), NG == 1 ? 2 : 1)
             }
             uint8_t *stage = base + L.raw_off() + s * L.raw_stage();
             if (lane == 0) {
-                mbar_arrive_expect_tx(&raw_full[s], static_cast<uint32_t>(kTcRows * chunk_bytes));
+                mbar_arrive_expect_tx(&raw_full[s], static_cast<uint32_t>(kTcRows * L.raw_row()));
                 tma_load_2d(stage, &wmap, (c_begin + c) * (chunk_bytes / 4), row0, &raw_full[s]);
             }
             __syncwarp();
@@ -436,7 +471,8 @@ __global__ void __launch_bounds__(tc_threads(NG), NG == 1 ? 2 : 1)
                 ok = false;
                 break;
             }
-            const uint8_t *rc = base + L.raw_off() + s * L.raw_stage() + r * chunk_bytes;
+            const int raw_row = L.raw_row();
+            const uint8_t *rc = base + L.raw_off() + s * L.raw_stage() + r * raw_row;
             for (int a = grp; a < apc; a += NG) {
                 const int g = c * apc + a, slot = g % slots;
                 if (!warp_wait(&op_empty[slot], ((g / slots) & 1) ^ 1)) {
@@ -445,18 +481,22 @@ __global__ void __launch_bounds__(tc_threads(NG), NG == 1 ? 2 : 1)
                     break;
                 }
                 uint8_t *at = base + slot * L.slot_bytes();
+                float scale = 1.0f;  // FP8: this tile's scale (rows 128*blockIdx.x.., columns of the atom)
+                if constexpr (std::is_same_v<F, FmtFP8>)
+                    scale = __ldg(scales + static_cast<size_t>(blockIdx.x) * scale_cols +
+                                  ((c_begin + c) * chunk_cols + a * kTcAtomCols) / 128);
                 if constexpr (TcDecode<F>::kWords) {
                     // lane = (row j, quarter q) of 8 rows per warp, two passes of
                     // 64 rows: conflict-free 4-byte raw loads and 8-byte stores
                     // (a half-warp covers 8 rows x both word parities)
                     const int wj = lane & 7, wq = lane >> 3, wg = (warp - 2) % kTcGroupWarps;
-                    const uint8_t *stage = rc - r * chunk_bytes;
+                    const uint8_t *stage = rc - r * raw_row;
 #pragma unroll
                     for (int pass = 0; pass < 2; ++pass) {
                         const int rr = pass * 64 + wg * 8 + wj;
                         float v[8];
                         if (rr < nrows) {
-                            TcDecode<F>::words(stage + rr * chunk_bytes, a, wq, v);
+                            TcDecode<F>::words(stage + rr * raw_row, a, wq, scale, v);
                         } else {
 #pragma unroll
                             for (int e = 0; e < 8; ++e) v[e] = 0.0f;
@@ -670,6 +710,87 @@ size_t gemm_tc_scratch_bytes(int32_t kind, int rows, int cols, int batch) {
     return bytes;
 }
 
+namespace {
+
+// Prepare the activation limbs and launch the GEMM (plus the split
+// reduction) for format F; `scales` / `scale_cols` for FmtFP8 only.
+template <class F>
+int32_t launch_tc(float *out, const uint8_t *w, const float *x, int rows, int cols, int batch, uint8_t *scratch,
+                  cudaStream_t stream, int64_t row_bytes, int64_t pitch, int xstride, bool accumulate,
+                  const float *scales, int scale_cols) {
+    // Two CTAs per SM with one decode group each where their shared memory
+    // fits half an SM (two MMA-issuing threads keep the tensor core busier
+    // than one), else one CTA with two groups; K split over idle SMs.
+    TcShape sh;
+    if (!shape_tc<F>(rows, cols, batch, sh)) {
+        set_error("gemm_tc: no launch plan for this shape");
+        return kUnsupported;
+    }
+    const TcLayout &L = sh.L;
+    // The weights as a 2-D tensor of 4-byte elements: rows x (row bytes / 4),
+    // row pitch `pitch` bytes; one box = 128 rows x one raw stage row.
+    const EncodeTiledFn encode = encode_tiled();
+    if (!encode) {
+        set_error("gemm_tc: cuTensorMapEncodeTiled is not available");
+        return kUnsupported;
+    }
+    CUtensorMap wmap;
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(row_bytes / 4), static_cast<cuuint64_t>(rows)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(pitch)};
+    const cuuint32_t box[2] = {static_cast<cuuint32_t>(L.raw_row() / 4), static_cast<cuuint32_t>(kTcRows)};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult ce = encode(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<uint8_t *>(w), dims, strides, box,
+                               estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (ce != CUDA_SUCCESS) {
+        set_error("gemm_tc: cuTensorMapEncodeTiled failed (%d)", static_cast<int>(ce));
+        return kInvalid;
+    }
+    auto kern = sh.pair ? gemm_tc_kernel<F, 1> : gemm_tc_kernel<F, 2>;
+    if (const int32_t rc = allow_dynamic_smem(kern, sh.smem, "gemm_tc smem")) return rc;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    const int64_t threads = static_cast<int64_t>(cols / kTcAtomCols) * L.npad * 4;
+    cudaLaunchConfig_t pc = {};
+    pc.gridDim = dim3(static_cast<unsigned>((threads + 255) / 256));
+    pc.blockDim = dim3(256);
+    pc.stream = stream;
+    pc.attrs = attr;
+    pc.numAttrs = 1;
+    GLMVX_CUDA(cudaLaunchKernelEx(&pc, prep_tc_kernel, scratch, x, batch, L.npad, cols, xstride));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>((rows + kTcRows - 1) / kTcRows), static_cast<unsigned>(sh.splits));
+    cfg.blockDim = dim3(tc_threads(sh.pair ? 1 : 2));
+    cfg.dynamicSmemBytes = sh.smem;
+    cfg.stream = stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    GLMVX_CUDA(cudaLaunchKernelEx(&cfg, kern, wmap, out, static_cast<const uint8_t *>(scratch), rows, cols, batch, L.npad,
+                                  L.chunk_cols, L.chunk_bytes, L.slots, L.raw_stages, static_cast<int>(accumulate),
+                                  reinterpret_cast<float *>(scratch + sh.rec_bytes), scales, scale_cols,
+                                  device_error_word()));
+    if (sh.splits > 1) {
+        const int64_t n = static_cast<int64_t>(batch) * rows;
+        cudaLaunchConfig_t rc = {};
+        rc.gridDim = dim3(static_cast<unsigned>(std::min<int64_t>((n + 255) / 256, 4 * sm_count())));
+        rc.blockDim = dim3(256);
+        rc.stream = stream;
+        rc.attrs = attr;
+        rc.numAttrs = 1;
+        GLMVX_CUDA(cudaLaunchKernelEx(&rc, tc_split_reduce_kernel, out,
+                                      reinterpret_cast<const float *>(scratch + sh.rec_bytes), n, sh.splits,
+                                      static_cast<int>(accumulate)));
+    }
+    return kOk;
+}
+
+bool aligned16(const void *a, const void *b, const void *c) {
+    return ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b) | reinterpret_cast<uintptr_t>(c)) & 15) == 0;
+}
+
+}  // namespace
+
 int32_t gemm_tc_device(int32_t kind, float *out, const uint8_t *w, const float *x, int rows, int cols, int batch,
                        uint8_t *scratch, cudaStream_t stream, const ColSegment &seg) {
     int blk = 0, bytes = 0;
@@ -680,95 +801,40 @@ int32_t gemm_tc_device(int32_t kind, float *out, const uint8_t *w, const float *
     const int64_t row_bytes = static_cast<int64_t>(cols / blk) * bytes;
     const int64_t pitch = seg.pitch ? seg.pitch : row_bytes;
     const int xstride = seg.xstride ? seg.xstride : cols;
-    if ((reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(scratch)) & 15 ||
-        pitch % 16 || pitch < row_bytes || xstride < cols || xstride % 4) {
+    if (!aligned16(w, x, scratch) || pitch % 16 || pitch < row_bytes || xstride < cols || xstride % 4) {
         set_error("gemm_tc: weights, activations and scratch 16-byte aligned, row pitch a multiple of 16");
         return kInvalid;
     }
     int32_t st = kUnsupported;
     dispatch_format(kind, [&]<class F>() {
-        // Two CTAs per SM with one decode group each where their shared memory
-        // fits half an SM (two MMA-issuing threads keep the tensor core busier
-        // than one), else one CTA with two groups; K split over idle SMs.
-        TcShape sh;
-        if (!shape_tc<F>(rows, cols, batch, sh)) {
-            set_error("gemm_tc: no launch plan for this shape");
-            return;
-        }
-        const TcLayout &L = sh.L;
-        const size_t smem = sh.smem;
-        const bool pair = sh.pair;
-        // The weights as a 2-D tensor of 4-byte elements: rows x (row bytes / 4),
-        // row pitch `pitch` bytes; one box = 128 rows x one chunk's bytes.
-        const EncodeTiledFn encode = encode_tiled();
-        if (!encode) {
-            set_error("gemm_tc: cuTensorMapEncodeTiled is not available");
-            st = kUnsupported;
-            return;
-        }
-        CUtensorMap wmap;
-        const cuuint64_t dims[2] = {static_cast<cuuint64_t>(row_bytes / 4), static_cast<cuuint64_t>(rows)};
-        const cuuint64_t strides[1] = {static_cast<cuuint64_t>(pitch)};
-        const cuuint32_t box[2] = {static_cast<cuuint32_t>(L.chunk_bytes / 4), static_cast<cuuint32_t>(kTcRows)};
-        const cuuint32_t estr[2] = {1, 1};
-        const CUresult ce = encode(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<uint8_t *>(w), dims, strides,
-                                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-                                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-        if (ce != CUDA_SUCCESS) {
-            set_error("gemm_tc: cuTensorMapEncodeTiled failed (%d)", static_cast<int>(ce));
-            st = kInvalid;
-            return;
-        }
-        auto kern = pair ? gemm_tc_kernel<F, 1> : gemm_tc_kernel<F, 2>;
-        if ((st = allow_dynamic_smem(kern, smem, "gemm_tc smem"))) return;
-        cudaLaunchAttribute attr[1];
-        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-        attr[0].val.programmaticStreamSerializationAllowed = 1;
-        const int64_t threads = static_cast<int64_t>(cols / kTcAtomCols) * L.npad * 4;
-        cudaLaunchConfig_t pc = {};
-        pc.gridDim = dim3(static_cast<unsigned>((threads + 255) / 256));
-        pc.blockDim = dim3(256);
-        pc.stream = stream;
-        pc.attrs = attr;
-        pc.numAttrs = 1;
-        cudaError_t e = cudaLaunchKernelEx(&pc, prep_tc_kernel, scratch, x, batch, L.npad, cols, xstride);
-        if (e != cudaSuccess) {
-            st = cuda_fail(e, "prep_tc_kernel");
-            return;
-        }
-        cudaLaunchConfig_t cfg = {};
-        cfg.gridDim = dim3(static_cast<unsigned>((rows + kTcRows - 1) / kTcRows), static_cast<unsigned>(sh.splits));
-        cfg.blockDim = dim3(tc_threads(pair ? 1 : 2));
-        cfg.dynamicSmemBytes = smem;
-        cfg.stream = stream;
-        cfg.attrs = attr;
-        cfg.numAttrs = 1;
-        e = cudaLaunchKernelEx(&cfg, kern, wmap, out, static_cast<const uint8_t *>(scratch), rows, cols, batch, L.npad,
-                               L.chunk_cols, L.chunk_bytes, L.slots, L.raw_stages, static_cast<int>(seg.accumulate),
-                               reinterpret_cast<float *>(scratch + sh.rec_bytes), device_error_word());
-        if (e != cudaSuccess) {
-            st = cuda_fail(e, "gemm_tc_kernel");
-            return;
-        }
-        if (sh.splits > 1) {
-            const int64_t n = static_cast<int64_t>(batch) * rows;
-            cudaLaunchConfig_t rc = {};
-            rc.gridDim = dim3(static_cast<unsigned>(std::min<int64_t>((n + 255) / 256, 4 * sm_count())));
-            rc.blockDim = dim3(256);
-            rc.stream = stream;
-            rc.attrs = attr;
-            rc.numAttrs = 1;
-            e = cudaLaunchKernelEx(&rc, tc_split_reduce_kernel, out,
-                                   reinterpret_cast<const float *>(scratch + sh.rec_bytes), n, sh.splits,
-                                   static_cast<int>(seg.accumulate));
-            if (e != cudaSuccess) {
-                st = cuda_fail(e, "tc_split_reduce_kernel");
-                return;
-            }
-        }
-        st = kOk;
+        st = launch_tc<F>(out, w, x, rows, cols, batch, scratch, stream, row_bytes, pitch, xstride, seg.accumulate,
+                          nullptr, 0);
     });
     return st;
+}
+
+bool fp8_gemm_tc_supported(int cols, int batch) {
+    TcShape sh;
+    return cols % 256 == 0 && shape_tc<FmtFP8>(128, cols, batch, sh);
+}
+
+size_t fp8_gemm_tc_scratch_bytes(int rows, int cols, int batch) {
+    TcShape sh;
+    return shape_tc<FmtFP8>(rows, cols, batch, sh) ? sh.scratch_bytes : 0;
+}
+
+int32_t fp8_gemm_tc_device(float *out, const uint8_t *w, const float *scales, const float *x, int rows, int cols,
+                           int batch, uint8_t *scratch, cudaStream_t stream) {
+    if (rows <= 0 || cols <= 0 || cols % 256 || batch < 1 || batch > kTcMaxTokens) {
+        set_error("fp8 gemm: rows >= 1, columns a multiple of 256, 1..64 tokens");
+        return kUnsupported;
+    }
+    if (!aligned16(w, x, scratch) || (reinterpret_cast<uintptr_t>(scales) & 3)) {
+        set_error("fp8 gemm: weights, activations and scratch 16-byte aligned");
+        return kInvalid;
+    }
+    return launch_tc<FmtFP8>(out, w, x, rows, cols, batch, scratch, stream, cols, cols, cols, false, scales,
+                             (cols + 127) / 128);
 }
 
 }  // namespace glmvx

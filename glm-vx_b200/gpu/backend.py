@@ -478,15 +478,8 @@ class GPUBackend:
                    self.stream.handle)
         return self._fetch_checked(offs[:1], [out], offs[1])[0]
 
-    def fp8_matvec(self, weight, scales, x):
-        """FP8 E4M3FN block-scaled projection with the contract of the
-        reference's GLMKernels.fp8_matvec (gpu/runtime.py:1031-1053):
-        weight uint8 [rows, cols], scales float32 [ceil(rows/128),
-        ceil(cols/128)], x float32 [cols] -> float32 [rows],
-        out[r] = sum_c (decode(w[r,c]) * scales[r//128, c//128]) * x[c].
-        As there, non-finite inputs and the E4M3 NaN encodings are outside the
-        finite-input contract and are not screened."""
-        self._begin()
+    @staticmethod
+    def _fp8_args(weight, scales, x, batched):
         weight, scales, x = np.asarray(weight), np.asarray(scales), np.asarray(x)
         for name, arr, dtype in (('weight', weight, np.uint8), ('scales', scales, np.float32), ('x', x, np.float32)):
             if arr.dtype != dtype:
@@ -499,12 +492,39 @@ class GPUBackend:
                 raise ValueError(f'{name} must be between {minimum} and {_MAX}')
         if scales.shape != ((rows + 127) // 128, (cols + 127) // 128):
             raise ValueError(f'scales has incompatible shape {scales.shape}')
-        if x.shape != (cols,):
+        if x.shape[-1:] != (cols,) or x.ndim != (2 if batched else 1):
             raise ValueError(f'x has incompatible shape {x.shape}')
-        weight, scales, x = (np.ascontiguousarray(a) for a in (weight, scales, x))
+        return tuple(np.ascontiguousarray(a) for a in (weight, scales, x))
+
+    def fp8_matvec(self, weight, scales, x):
+        """FP8 E4M3FN block-scaled projection with the contract of the
+        reference's GLMKernels.fp8_matvec (gpu/runtime.py:1031-1053):
+        weight uint8 [rows, cols], scales float32 [ceil(rows/128),
+        ceil(cols/128)], x float32 [cols] -> float32 [rows],
+        out[r] = sum_c (decode(w[r,c]) * scales[r//128, c//128]) * x[c].
+        As there, non-finite inputs and the E4M3 NaN encodings are outside the
+        finite-input contract and are not screened."""
+        self._begin()
+        weight, scales, x = self._fp8_args(weight, scales, x, False)
+        rows, cols = weight.shape
         out = np.empty(rows, np.float32)
         (wd, sd, xd), (od,), offs = self._stage([weight, scales, x], [out.nbytes])
         self._call('glmvx_fp8_matvec', od, wd, sd, xd, rows, cols, self.stream.handle)
+        return self._fetch(offs, [out])[0]
+
+    def fp8_matmul(self, weight, scales, x):
+        """fp8_matvec for a batch of tokens: x float32 [batch, cols] ->
+        float32 [batch, rows] (row t = fp8_matvec(weight, scales, x[t])),
+        through glmvx_fp8_gemm (the tcgen05 GEMM for 2..64 tokens and
+        columns a multiple of 256, else one GEMV per token)."""
+        self._begin()
+        weight, scales, x = self._fp8_args(weight, scales, x, True)
+        rows, cols = weight.shape
+        out = np.empty((len(x), rows), np.float32)
+        if len(x) == 0:
+            return out
+        (wd, sd, xd), (od,), offs = self._stage([weight, scales, x], [out.nbytes])
+        self._call('glmvx_fp8_gemm', od, wd, sd, xd, rows, cols, len(x), None, self.stream.handle)
         return self._fetch(offs, [out])[0]
 
     def mlp(self, gate, up, down, x):

@@ -99,6 +99,7 @@ SIGNATURES = {
     'glmvx_moe_ffn_profiled': ([_P, _P, _I32, _I32, _I32, _P, _P, _I32, _I32, _F32, _I32, _P, _P, _P, _P, _P, _P, _P,
                                 _U64, _P, _P], _I32),
     'glmvx_fp8_matvec': ([_P, _P, _P, _P, _I32, _I32, _P], _I32),
+    'glmvx_fp8_gemm': ([_P, _P, _P, _P, _I32, _I32, _I32, _P, _P], _I32),
     'glmvx_moe_experts': ([_P, _P, _P, _I32, _I32, _I32, _I32, _I32, _P, _P, _P, _P, _U64, _P], _I32),
     'glmvx_moe_combine': ([_P, _P, _P, _P, _P, _I32, _I32, _I32, _P], _I32),
     'glmvx_gather_rows': ([_P, _P, _P, _I32, _I32, _P], _I32),

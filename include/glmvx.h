@@ -140,9 +140,10 @@ int32_t glmvx_packed_gemv(int32_t kind, float *out, const uint8_t *w, const floa
  * Replaces glm_vx_packed_batch_v2_<kind> (kernels/packed.vx:473ff). */
 int32_t glmvx_packed_gemm(int32_t kind, float *out, const uint8_t *w, const float *x, int32_t rows, int32_t cols,
                           int32_t batch, void *stream);
-/* The tcgen05 packed GEMM alone: weights decoded to f32 and split into two
- * TF32 limbs in shared memory, three kind::tf32 MMAs per K step accumulating in
- * tensor memory; any format, batch 1..64, cols a multiple of the format's raw
+/* The tcgen05 packed GEMM alone: weights and activations split exactly into
+ * three bf16 limbs in shared memory, six products (those above 2^-24 of the
+ * leading term) in three kind::f16 MMAs per K step accumulating in f32 tensor
+ * memory; any format, batch 1..64, cols a multiple of the format's raw
  * chunk (256 columns for Q8_0/Q4_K, 2048 for IQ1_S), 16-byte aligned w and x. */
 int32_t glmvx_packed_gemm_tc(int32_t kind, float *out, const uint8_t *w, const float *x, int32_t rows, int32_t cols,
                              int32_t batch, void *stream);
@@ -387,6 +388,15 @@ int32_t glmvx_dsa_attend(float *out, const int32_t *selected, const float *q_lat
  * GLMKernels.fp8_matvec (gpu/runtime.py:1031-1053).  rows >= 1, cols >= 0. */
 int32_t glmvx_fp8_matvec(float *out, const uint8_t *weight, const float *scales, const float *x, int32_t rows,
                          int32_t cols, void *stream);
+/* The same projection for a batch of tokens: out[t][r], x[t][cols] row-major.
+ * 2..64 tokens with cols a multiple of 256 and 16-byte aligned weight and x
+ * run on the tcgen05 GEMM (*path = 9: each weight times its tile scale in f32,
+ * split exactly into three bf16 limbs, six kind::f16 MMAs per K step);
+ * otherwise one glmvx_fp8_matvec per token (*path = 1).  path may be NULL.
+ * The reference multiplies one token at a time (GLMKernels.fp8_matvec,
+ * gpu/runtime.py:1031-1053); results agree within the f32 dot-product bound. */
+int32_t glmvx_fp8_gemm(float *out, const uint8_t *weight, const float *scales, const float *x, int32_t rows,
+                       int32_t cols, int32_t batch, int32_t *path, void *stream);
 /* glmvx_moe_ffn without a caller workspace, for callers that cannot allocate
  * device memory (an embedding runtime that owns the whole memory budget, a
  * decode loop with a fixed footprint).  No counterpart in the reference.

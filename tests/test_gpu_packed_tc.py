@@ -1,8 +1,8 @@
 """tcgen05 packed GEMM (csrc/packed_gemm_tc.cu, glmvx_packed_gemm_tc) against
 the CPU oracle's batched packed kernels (the reference's batch_v2 contract,
-kernels/packed.vx:473ff): weights decoded to f32 and split into two TF32
-limbs, three kind::tf32 MMAs per K step; every format, 1..64 tokens, partial
-128-row tiles, activation ranges, a non-finite token, determinism."""
+kernels/packed.vx:473ff): weights and activations split exactly into three
+bf16 limbs, three kind::f16 MMAs per K step; every format, 1..64 tokens,
+partial 128-row tiles, activation ranges, a non-finite token, determinism."""
 import ctypes as C
 
 import numpy as np
@@ -56,7 +56,7 @@ def test_gemm_tc_matches_oracle(cuda_lib, oracle, kind, rows, cols, batch):
 
 
 def test_gemm_tc_activation_ranges_and_nonfinite(cuda_lib, oracle):
-    """TF32 limbs keep f32's exponent range: tiny, huge and mixed chunks need
+    """bf16 limbs keep f32's exponent range: tiny, huge and mixed chunks need
     no scaling; an infinite activation makes only its own token NaN."""
     kind, rows, cols, batch = 8, 192, 2048, 16
     raw, x = _case(kind, rows, cols, batch, 5)
