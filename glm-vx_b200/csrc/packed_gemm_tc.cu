@@ -260,9 +260,10 @@ template <>
 struct TcDecode<FmtFP8> {
     static constexpr bool kWords = true;
     // Bytes of words q and q + 4 of atom a (32 bytes) through the hardware
-    // E4M3x2 -> f16x2 conversion (exact, NaN codes to NaN), times the tile's
-    // scale in f32 as the reference multiplies them.
-    __device__ __forceinline__ static void words(const uint8_t *rc, int a, int q, float scale, float (&w)[8]) {
+    // E4M3x2 -> f16x2 conversion (exact, NaN codes to NaN).  The values have
+    // at most 4 significant bits, so one bf16 limb holds them exactly; the
+    // tile's scale goes into the activation limbs.
+    __device__ __forceinline__ static void words(const uint8_t *rc, int a, int q, float, float (&w)[8]) {
         const uint32_t *p = reinterpret_cast<const uint32_t *>(rc + a * kTcAtomCols);
         const uint32_t x[2] = {p[q], p[q + 4]};
 #pragma unroll
@@ -272,8 +273,8 @@ struct TcDecode<FmtFP8> {
                 const __half2_raw h = __nv_cvt_fp8x2_to_halfraw2(
                     static_cast<__nv_fp8x2_storage_t>((x[i] >> (16 * k)) & 0xffffu), __NV_E4M3);
                 const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&h));
-                w[4 * i + 2 * k] = __fmul_rn(f.x, scale);
-                w[4 * i + 2 * k + 1] = __fmul_rn(f.y, scale);
+                w[4 * i + 2 * k] = f.x;
+                w[4 * i + 2 * k + 1] = f.y;
             }
     }
     __device__ __forceinline__ static void run(const uint8_t *, int, int, float (&)[16]) {}
@@ -289,12 +290,15 @@ __device__ __forceinline__ bool warp_wait(uint64_t *bar, uint32_t parity) {
 // Shared-memory layout of a CTA (offsets from the 1 KB-aligned base).
 struct TcLayout {
     int npad, chunk_cols, chunk_bytes, slots, raw_stages;
+    // Weight limbs per slot (3; FP8 values are exact in one bf16).
+    int a_limbs = kTcLimbs;
     // Raw stage row pitch: the chunk's bytes, plus 16 when they are a multiple
     // of 128 (otherwise every row of the box would start in the same bank);
     // the TMA box then reads 16 bytes of the next chunk (or zeros past the row).
     __host__ __device__ int raw_row() const { return chunk_bytes + ((chunk_bytes % 128) == 0 ? 16 : 0); }
     __host__ __device__ int b_tile() const { return npad * kTcRowBytes; }     // one limb of one atom
-    __host__ __device__ int slot_bytes() const { return kTcLimbs * (kTcATile + b_tile()); }
+    __host__ __device__ int b_off() const { return a_limbs * kTcATile; }  // B tile within a slot
+    __host__ __device__ int slot_bytes() const { return b_off() + kTcLimbs * b_tile(); }
     __host__ __device__ int raw_stage() const { return kTcRows * raw_row(); }
     __host__ __device__ int raw_off() const { return slots * slot_bytes(); }
     __host__ __device__ int bar_off() const { return (raw_off() + raw_stages * raw_stage() + 15) & ~15; }
@@ -340,6 +344,7 @@ namespace {
 template <class F, int NG>
 __global__ void __launch_bounds__(tc_threads(NG), NG == 1 ? 2 : 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap wmap, float *__restrict__ out, const uint8_t *__restrict__ rec,
+                   const float *__restrict__ x, int xstride,
                    int rows, int cols, int tokens, int npad, int chunk_cols, int chunk_bytes, int slots, int raw_stages,
                    int accumulate, float *__restrict__ partial, const float *__restrict__ scales, int scale_cols,
                    int *err) {
@@ -348,7 +353,11 @@ __global__ void __launch_bounds__(tc_threads(NG), NG == 1 ? 2 : 1)
     const uint32_t pad = ((raw_s + 1023u) & ~1023u) - raw_s;  // swizzled tiles: 1 KB-aligned addresses
     uint8_t *base = tc_smem_raw + pad;
     const uint32_t base_s = raw_s + pad;
-    const TcLayout L{npad, chunk_cols, chunk_bytes, slots, raw_stages};
+    // FP8: one weight limb; the decode warps split the activations, times
+    // the tile's scale, into limbs themselves (x read from L2 one atom ahead).
+    constexpr bool kFP8 = std::is_same_v<F, FmtFP8>;
+    constexpr int kAL = kFP8 ? 1 : kTcLimbs;
+    const TcLayout L{npad, chunk_cols, chunk_bytes, slots, raw_stages, kAL};
     uint64_t *bars = reinterpret_cast<uint64_t *>(base + L.bar_off());
     uint64_t *raw_full = bars, *raw_empty = bars + 2, *a_full = bars + 4;
     uint64_t *b_full = a_full + slots, *op_empty = b_full + slots, *acc_full = op_empty + slots;
@@ -391,10 +400,13 @@ __global__ void __launch_bounds__(tc_threads(NG), NG == 1 ? 2 : 1)
 
     if (warp == 0) {  // producer
         bool ok = true;
+        int slot = 0;
+        uint32_t ph = 0;  // slot and phase of atom g (counters: no division by `slots`)
         for (int c = 0; c < chunks && ok; ++c) {
-            const int s = c % raw_stages;
+            const int s = raw_stages == 1 ? 0 : (c & 1);
+            const uint32_t rph = raw_stages == 1 ? (c & 1) : ((c >> 1) & 1);
             int good = 1;
-            if (lane == 0) good = mbar_wait_bounded(&raw_empty[s], ((c / raw_stages) & 1) ^ 1);
+            if (lane == 0) good = mbar_wait_bounded(&raw_empty[s], rph ^ 1);
             good = __shfl_sync(0xffffffffu, good, 0);
             if (!good) {
                 if (lane == 0) report_device_error(err, kDevErrEmptyWait);
@@ -406,15 +418,16 @@ __global__ void __launch_bounds__(tc_threads(NG), NG == 1 ? 2 : 1)
                 tma_load_2d(stage, &wmap, (c_begin + c) * (chunk_bytes / 4), row0, &raw_full[s]);
             }
             __syncwarp();
+            if constexpr (kFP8) continue;  // no prepared activation records
             if (c == 0) grid_dependency_wait();  // the activation limbs come from the previous kernel
             for (int a = 0; a < apc; ++a) {
-                const int g = c * apc + a, slot = g % slots;
+                const int g = c * apc + a;
                 if (lane == 0) {
-                    if (!mbar_wait_bounded(&op_empty[slot], ((g / slots) & 1) ^ 1)) {
+                    if (!mbar_wait_bounded(&op_empty[slot], ph ^ 1)) {
                         report_device_error(err, kDevErrEmptyWait);
                         good = 0;
                     } else {
-                        uint8_t *b = base + slot * L.slot_bytes() + kTcLimbs * kTcATile;
+                        uint8_t *b = base + slot * L.slot_bytes() + L.b_off();
                         mbar_arrive_expect_tx(&b_full[slot], static_cast<uint32_t>(kTcLimbs * L.b_tile()));
                         bulk_g2s(b, rec + static_cast<size_t>(c_begin * apc + g) * kTcLimbs * L.b_tile(),
                                  static_cast<uint32_t>(kTcLimbs * L.b_tile()),
@@ -426,15 +439,20 @@ __global__ void __launch_bounds__(tc_threads(NG), NG == 1 ? 2 : 1)
                     ok = false;
                     break;
                 }
+                if (++slot == slots) {
+                    slot = 0;
+                    ph ^= 1;
+                }
             }
         }
     } else if (warp == 1) {  // MMA issue
         if (lane == 0) {
             bool ok = true;
+            int slot = 0;
+            uint32_t ph = 0;
             for (int g = 0; g < atoms; ++g) {
-                const int slot = g % slots;
-                const uint32_t ph = (g / slots) & 1;
-                if (!mbar_wait_spin_bounded(&a_full[slot], ph) || !mbar_wait_spin_bounded(&b_full[slot], ph)) {
+                // (FP8: the decode warps consumed b_full and built B before a_full)
+                if (!mbar_wait_spin_bounded(&a_full[slot], ph) || (!kFP8 && !mbar_wait_spin_bounded(&b_full[slot], ph))) {
                     report_device_error(err, kDevErrFullWait);
                     ok = false;
                     break;
@@ -447,15 +465,21 @@ __global__ void __launch_bounds__(tc_threads(NG), NG == 1 ? 2 : 1)
                 // a3 x b1 -- B rows 0 .. k*npad of the stacked limb tile -- into
                 // accumulator columns 0 .. 3 npad.
                 const uint64_t da = umma_desc_kmajor(base_s + slot * L.slot_bytes());
-                const uint64_t db = da + ((kTcLimbs * kTcATile) >> 4);
+                const uint64_t db = da + (L.b_off() >> 4);
 #pragma unroll
                 for (int kk = 0; kk < kTcAtomCols / 16; ++kk) {  // K = 16 bf16 = 32 bytes per MMA
                     const uint64_t oa = (kk * kTcRows * 32) >> 4, ob = static_cast<uint64_t>(kk * kTcLimbs * npad * 2);
                     umma_bf16(tmem, da + oa, db + ob, idesc3, (g > 0 || kk > 0) ? 1u : 0u);
-                    umma_bf16(tmem, da + (kTcATile >> 4) + oa, db + ob, idesc2, 1u);
-                    umma_bf16(tmem, da + ((2 * kTcATile) >> 4) + oa, db + ob, idesc1, 1u);
+                    if constexpr (!kFP8) {
+                        umma_bf16(tmem, da + (kTcATile >> 4) + oa, db + ob, idesc2, 1u);
+                        umma_bf16(tmem, da + ((2 * kTcATile) >> 4) + oa, db + ob, idesc1, 1u);
+                    }
                 }
                 umma_commit(&op_empty[slot]);
+                if (++slot == slots) {
+                    slot = 0;
+                    ph ^= 1;
+                }
             }
             if (ok) umma_commit(acc_full);
         }
@@ -464,9 +488,36 @@ __global__ void __launch_bounds__(tc_threads(NG), NG == 1 ? 2 : 1)
         const int grp = (warp - 2) / kTcGroupWarps, gt = threadIdx.x - 64 - grp * kTcGroupWarps * 32;
         const int r = gt >> 1, h = gt & 1;  // a thread: 16 weights of one tile row
         bool ok = true;
+        int slot = grp;  // slot and phase of this group's atom g = grp, grp + NG, ... (NG <= slots)
+        uint32_t ph = 0;
+        // FP8: activations (token xn, columns 8 xq .. 8 xq + 7 of the atom; zeros
+        // past the tokens) and the atom's scale, fetched one atom ahead.  A
+        // quarter-warp takes 8 consecutive tokens of one column quarter, so its
+        // 16-byte limb stores fill one 128-byte core matrix (no bank conflict).
+        const int xn = (gt & 7) | ((gt >> 5) << 3), xq = (gt >> 3) & 3;
+        const bool xact = kFP8 && gt < npad * 4 && xn < tokens;
+        float4 xr0 = make_float4(0.f, 0.f, 0.f, 0.f), xr1 = xr0;
+        float scr = 0.0f;
+        auto fetch = [&](int g) {
+            if constexpr (kFP8) {
+                if (g < atoms) {
+                    const int col = (c_begin * apc + g) * kTcAtomCols;
+                    scr = __ldg(scales + static_cast<size_t>(blockIdx.x) * scale_cols + col / 128);
+                    if (xact) {
+                        const float4 *src = reinterpret_cast<const float4 *>(x + static_cast<size_t>(xn) * xstride + col + 8 * xq);
+                        xr0 = __ldg(src);
+                        xr1 = __ldg(src + 1);
+                    }
+                }
+            }
+        };
+        if constexpr (kFP8) {
+            grid_dependency_wait();  // x comes from the previous kernel
+            fetch(grp);
+        }
         for (int c = 0; c < chunks && ok; ++c) {
-            const int s = c % raw_stages;
-            if (!warp_wait(&raw_full[s], (c / raw_stages) & 1)) {
+            const int s = raw_stages == 1 ? 0 : (c & 1);
+            if (!warp_wait(&raw_full[s], raw_stages == 1 ? (c & 1) : ((c >> 1) & 1))) {
                 if (lane == 0) report_device_error(err, kDevErrFullWait);
                 ok = false;
                 break;
@@ -474,17 +525,16 @@ __global__ void __launch_bounds__(tc_threads(NG), NG == 1 ? 2 : 1)
             const int raw_row = L.raw_row();
             const uint8_t *rc = base + L.raw_off() + s * L.raw_stage() + r * raw_row;
             for (int a = grp; a < apc; a += NG) {
-                const int g = c * apc + a, slot = g % slots;
-                if (!warp_wait(&op_empty[slot], ((g / slots) & 1) ^ 1)) {
+                const int g = c * apc + a;
+                const float4 x0 = xr0, x1 = xr1;
+                const float scale = scr;  // FP8: this tile's scale (rows 128*blockIdx.x.., the atom's columns)
+                fetch(g + NG);
+                if (!warp_wait(&op_empty[slot], ph ^ 1)) {
                     if (lane == 0) report_device_error(err, kDevErrEmptyWait);
                     ok = false;
                     break;
                 }
                 uint8_t *at = base + slot * L.slot_bytes();
-                float scale = 1.0f;  // FP8: this tile's scale (rows 128*blockIdx.x.., columns of the atom)
-                if constexpr (std::is_same_v<F, FmtFP8>)
-                    scale = __ldg(scales + static_cast<size_t>(blockIdx.x) * scale_cols +
-                                  ((c_begin + c) * chunk_cols + a * kTcAtomCols) / 128);
                 if constexpr (TcDecode<F>::kWords) {
                     // lane = (row j, quarter q) of 8 rows per warp, two passes of
                     // 64 rows: conflict-free 4-byte raw loads and 8-byte stores
@@ -509,7 +559,7 @@ __global__ void __launch_bounds__(tc_threads(NG), NG == 1 ? 2 : 1)
                             for (int e = 0; e < 4; ++e) bf16_limbs(v[4 * hw + e], l[0][e], l[1][e], l[2][e]);
                             const uint32_t off = kmajor_offset(rr, wd >> 1, kTcRows) + 8 * (wd & 1);
 #pragma unroll
-                            for (int k = 0; k < kTcLimbs; ++k)
+                            for (int k = 0; k < kAL; ++k)
                                 *reinterpret_cast<uint2 *>(at + k * kTcATile + off) =
                                     make_uint2(pack_bf16(l[k][0], l[k][1]), pack_bf16(l[k][2], l[k][3]));
                         }
@@ -529,8 +579,25 @@ __global__ void __launch_bounds__(tc_threads(NG), NG == 1 ? 2 : 1)
                         for (int e = 0; e < 8; ++e) bf16_limbs(v[8 * i + e], l[0][e], l[1][e], l[2][e]);
                         const uint32_t off = kmajor_offset(r, 2 * h + i, kTcRows);
 #pragma unroll
-                        for (int k = 0; k < kTcLimbs; ++k)
+                        for (int k = 0; k < kAL; ++k)
                             *reinterpret_cast<uint4 *>(at + k * kTcATile + off) =
+                                make_uint4(pack_bf16(l[k][0], l[k][1]), pack_bf16(l[k][2], l[k][3]),
+                                           pack_bf16(l[k][4], l[k][5]), pack_bf16(l[k][6], l[k][7]));
+                    }
+                }
+                if constexpr (kFP8) {
+                    // B = (x * scale) in three bf16 limbs, stacked as the prepared
+                    // records of prep_tc_kernel: one (token, 8 columns) per thread
+                    // (npad * 4 <= 256 threads).
+                    if (gt < npad * 4) {
+                        const float xv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+                        uint32_t l[3][8];
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) bf16_limbs(__fmul_rn(xv[e], scale), l[0][e], l[1][e], l[2][e]);
+                        uint8_t *bt = at + L.b_off();
+#pragma unroll
+                        for (int k = 0; k < kTcLimbs; ++k)
+                            *reinterpret_cast<uint4 *>(bt + kmajor_offset(k * npad + xn, xq, kTcLimbs * npad)) =
                                 make_uint4(pack_bf16(l[k][0], l[k][1]), pack_bf16(l[k][2], l[k][3]),
                                            pack_bf16(l[k][4], l[k][5]), pack_bf16(l[k][6], l[k][7]));
                     }
@@ -538,6 +605,10 @@ __global__ void __launch_bounds__(tc_threads(NG), NG == 1 ? 2 : 1)
                 fence_proxy_async_smem();  // generic-proxy stores -> the tensor cores' async proxy
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&a_full[slot]);
+                if ((slot += NG) >= slots) {
+                    slot -= slots;
+                    ph ^= 1;
+                }
             }
             __syncwarp();
             if (lane == 0 && ok) mbar_arrive(&raw_empty[s]);
@@ -613,6 +684,7 @@ bool plan_tc(int cols, int batch, TcLayout &L, size_t &smem, int budget = kTcSme
     const int chunk = tc_chunk_cols(F::kBlk, F::kBytes);
     if (!chunk || cols <= 0 || cols % chunk || batch < 1 || batch > kTcMaxTokens) return false;
     L.npad = (batch + 15) / 16 * 16;
+    L.a_limbs = std::is_same_v<F, FmtFP8> ? 1 : kTcLimbs;
     L.chunk_cols = chunk;
     L.chunk_bytes = chunk / F::kBlk * F::kBytes;
     // Two raw stages (loads overlap decoding) where they fit, else one.
@@ -694,7 +766,9 @@ bool shape_tc(int rows, int cols, int batch, TcShape &sh) {
             sh.splits = sp;
         }
     }
-    sh.rec_bytes = (static_cast<size_t>(cols / kTcAtomCols) * kTcLimbs * sh.L.npad * kTcRowBytes + 255) & ~size_t(255);
+    sh.rec_bytes = std::is_same_v<F, FmtFP8>
+                       ? 0  // FP8 builds its activation limbs in the kernel
+                       : (static_cast<size_t>(cols / kTcAtomCols) * kTcLimbs * sh.L.npad * kTcRowBytes + 255) & ~size_t(255);
     sh.scratch_bytes = sh.rec_bytes + (sh.splits > 1 ? static_cast<size_t>(sh.splits) * batch * rows * 4 : 0);
     return true;
 }
@@ -746,6 +820,7 @@ int32_t launch_tc(float *out, const uint8_t *w, const float *x, int rows, int co
         set_error("gemm_tc: cuTensorMapEncodeTiled failed (%d)", static_cast<int>(ce));
         return kInvalid;
     }
+    constexpr bool kFP8 = std::is_same_v<F, FmtFP8>;
     auto kern = sh.pair ? gemm_tc_kernel<F, 1> : gemm_tc_kernel<F, 2>;
     if (const int32_t rc = allow_dynamic_smem(kern, sh.smem, "gemm_tc smem")) return rc;
     cudaLaunchAttribute attr[1];
@@ -758,7 +833,7 @@ int32_t launch_tc(float *out, const uint8_t *w, const float *x, int rows, int co
     pc.stream = stream;
     pc.attrs = attr;
     pc.numAttrs = 1;
-    GLMVX_CUDA(cudaLaunchKernelEx(&pc, prep_tc_kernel, scratch, x, batch, L.npad, cols, xstride));
+    if constexpr (!kFP8) GLMVX_CUDA(cudaLaunchKernelEx(&pc, prep_tc_kernel, scratch, x, batch, L.npad, cols, xstride));
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(static_cast<unsigned>((rows + kTcRows - 1) / kTcRows), static_cast<unsigned>(sh.splits));
     cfg.blockDim = dim3(tc_threads(sh.pair ? 1 : 2));
@@ -766,7 +841,8 @@ int32_t launch_tc(float *out, const uint8_t *w, const float *x, int rows, int co
     cfg.stream = stream;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    GLMVX_CUDA(cudaLaunchKernelEx(&cfg, kern, wmap, out, static_cast<const uint8_t *>(scratch), rows, cols, batch, L.npad,
+    GLMVX_CUDA(cudaLaunchKernelEx(&cfg, kern, wmap, out, static_cast<const uint8_t *>(scratch), x, xstride, rows, cols,
+                                  batch, L.npad,
                                   L.chunk_cols, L.chunk_bytes, L.slots, L.raw_stages, static_cast<int>(accumulate),
                                   reinterpret_cast<float *>(scratch + sh.rec_bytes), scales, scale_cols,
                                   device_error_word()));
