@@ -104,20 +104,26 @@ __global__ void __launch_bounds__(256)
 #pragma unroll
         for (int t = 0; t < TB; ++t) acc[e][t] = 0.0f;
     const int quads = cols >> 2;
-    // token tiles: two iterations' loads in flight per thread (the grid is
-    // one or two CTAs per SM, so memory latency is hidden within the thread)
-    constexpr int kUnroll = TB > 1 ? 2 : 4;
-#pragma unroll kUnroll
-    for (int f = lane + 32 * warp; f < quads; f += 256) {
-        float4 wv[EB], xv[TB];
+    // The thread's quads f0, f0 + 256, ... (n of them), U at a time: U
+    // iterations' loads are issued before the first is used, with no bounds
+    // test between them (a guarded loop cannot move a load above the test
+    // that ends it, which leaves one iteration's loads in flight).
+    constexpr int U = TB > 1 ? 2 : 4;
+    const int f0 = lane + 32 * warp;
+    const int n = f0 < quads ? (quads - f0 + 255) / 256 : 0;
+    auto load_w = [&](int f, float4 (&wv)[EB]) {
 #pragma unroll
         for (int e = 0; e < EB; ++e)
             wv[e] = e < nr ? __ldg(reinterpret_cast<const float4 *>(wt + static_cast<size_t>(r0 + e) * cols) + f)
                            : make_float4(0.f, 0.f, 0.f, 0.f);
+    };
+    auto load_x = [&](int f, float4 (&xv)[TB]) {
 #pragma unroll
         for (int t = 0; t < TB; ++t)
             xv[t] = t < nt ? __ldg(reinterpret_cast<const float4 *>(x + static_cast<size_t>(t0 + t) * cols) + f)
                            : make_float4(0.f, 0.f, 0.f, 0.f);
+    };
+    auto fma_tile = [&](const float4 (&wv)[EB], const float4 (&xv)[TB]) {
 #pragma unroll
         for (int e = 0; e < EB; ++e)
 #pragma unroll
@@ -127,6 +133,23 @@ __global__ void __launch_bounds__(256)
                 acc[e][t] = fmaf(wv[e].z, xv[t].z, acc[e][t]);
                 acc[e][t] = fmaf(wv[e].w, xv[t].w, acc[e][t]);
             }
+    };
+    int i = 0;
+    for (; i + U <= n; i += U) {
+        float4 wv[U][EB], xv[U][TB];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            load_w(f0 + 256 * (i + u), wv[u]);
+            load_x(f0 + 256 * (i + u), xv[u]);
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) fma_tile(wv[u], xv[u]);
+    }
+    for (; i < n; ++i) {
+        float4 wv[EB], xv[TB];
+        load_w(f0 + 256 * i, wv);
+        load_x(f0 + 256 * i, xv);
+        fma_tile(wv, xv);
     }
 #pragma unroll
     for (int e = 0; e < EB; ++e)
