@@ -938,6 +938,8 @@ def run_profile_case(args):
         return profile_packed_gemm()
     if args.profile_case == 'fp8_gemm':
         return profile_fp8_gemm()
+    if args.profile_case == 'fp8_matvec':
+        return profile_fp8_matvec()
     if args.profile_case == 'packed_gemm_tc':
         return profile_packed_gemm('glmvx_packed_gemm_tc')
     if args.profile_case in ('attention3', 'attention3_16'):
@@ -1043,6 +1045,33 @@ def profile_packed_gemm(entry='glmvx_packed_gemm'):
     return 0
 
 
+def profile_fp8_matvec(rows=16384, cols=6144):
+    """glmvx_fp8_matvec on a 16384 x 6144 FP8 projection (100 MB, larger than
+    L2): three launches."""
+    from gpu.backend import GPUBackend
+    from gpu import runtime as rt
+    backend = GPUBackend(0)
+    s = backend.stream.handle
+    rng = np.random.default_rng(0)
+    w8 = rng.integers(0, 256, size=rows * cols, dtype=np.uint8)
+    w8[(w8 & 0x7F) == 0x7F] = 0x3C
+    sc = (np.abs(rng.normal(size=(rows // 128) * (cols // 128))) * 0.02 + 1e-3).astype(np.float32)
+    x = rng.normal(size=cols).astype(np.float32)
+    bufs = [rt.DeviceBuffer(a.nbytes) for a in (w8, sc, x)] + [rt.DeviceBuffer(4 * rows)]
+    for b, a in zip(bufs, (w8, sc, x)):
+        b.upload(a, s)
+    for _ in range(3):
+        rt.check(backend.lib, backend.lib.glmvx_fp8_matvec(bufs[3].ptr, bufs[0].ptr, bufs[1].ptr, bufs[2].ptr, rows,
+                                                           cols, s), 'glmvx_fp8_matvec')
+    backend.stream.synchronize()
+    for b in bufs:
+        b.close()
+    backend.device.check_device_error()
+    print(f'profile case ok: glmvx_fp8_matvec {rows} x {cols}, 3 launches', flush=True)
+    backend.close()
+    return 0
+
+
 def profile_fp8_gemm():
     """glmvx_fp8_gemm (tcgen05) at 32 tokens on the bench's FP8 6144 x 6144
     projection and on 24576 x 6144 (151 MB, larger than L2): three launches
@@ -1131,7 +1160,7 @@ def main():
     ap.add_argument('--cpu-seconds', type=float, default=10.0)
     ap.add_argument('--no-cpu-baseline', action='store_true')
     ap.add_argument('--no-decoder', action='store_true', help='skip the config-4 decoder measurement')
-    ap.add_argument('--profile-case', nargs='?', const='moe', choices=('moe', 'gemm', 'dsa', 'dsa1', 'decoder', 'packed_gemm', 'fp8_gemm',
+    ap.add_argument('--profile-case', nargs='?', const='moe', choices=('moe', 'gemm', 'dsa', 'dsa1', 'decoder', 'packed_gemm', 'fp8_gemm', 'fp8_matvec',
                                                                  'attention3', 'attention3_16', 'packed_gemm_tc'),
                     help='run a small kernel-capture case (one GPU) instead of the benchmark')
     args = ap.parse_args()
