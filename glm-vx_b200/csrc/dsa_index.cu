@@ -222,7 +222,10 @@ int32_t launch_index_scores_tc(float *out, const float *q, const float *keys, co
     if (const int32_t rc = allow_dynamic_smem(index_tc_kernel<false>, kIdxSmem, "index_tc smem")) return rc;
     const int smem = kIdxStages * kIdxStageBytes + 2 * nchunks * n_pad * 128 + 1024;
     const int tiles = (tokens + kIdxTile - 1) / kIdxTile;
-    const int per_query = std::max(1, std::min(tiles, (2 * 148 + batch - 1) / batch));  // ~two CTAs per SM
+    // Two CTAs per SM, all resident at once: per query the floor of the
+    // slots over the queries (the ceiling put CTAs into a second wave, e.g.
+    // 19 x 16 = 304 > 296 at 16 queries: 180 -> 120 us for the indexer).
+    const int per_query = std::max(1, std::min(tiles, 2 * sm_count() / batch));
     const dim3 grid(per_query, batch);
     const bool vec = dim % 4 == 0 && key_stride % 4 == 0 && (reinterpret_cast<uintptr_t>(keys) & 15) == 0;
     if (vec)
