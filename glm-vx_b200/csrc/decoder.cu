@@ -466,12 +466,11 @@ GLMVX_EXPORT int32_t glmvx_scale(float *out, const float *x, float s, int64_t n,
 // scales |N(0,1)|*scale (Q4_K: d and dmin).  Deterministic in `seed`.
 GLMVX_EXPORT int32_t glmvx_fill_random(void *out, int32_t kind, int64_t count, uint64_t seed, float scale,
                                        int32_t ones, void *stream) {
-    int blk = 1, bytes = 4, scale_bytes = 0;
-    if (kind == 8) bytes = 34, scale_bytes = 2, blk = 32;
-    else if (kind == 12) bytes = 144, scale_bytes = 4, blk = 256;
-    else if (kind == 19) bytes = 50, scale_bytes = 2, blk = 256;
+    int bytes = 4, scale_bytes = 0;  // per element (kind 0) or per block
+    if (kind == 8) bytes = 34, scale_bytes = 2;
+    else if (kind == 12) bytes = 144, scale_bytes = 4;
+    else if (kind == 19) bytes = 50, scale_bytes = 2;
     else if (kind != 0) return set_error("fill_random: kind 0, 8, 12 or 19"), kInvalid;
-    (void)blk;
     if (count < 0) return set_error("fill_random: negative count"), kInvalid;
     if (!count) return kOk;
     fill_random_kernel<<<8 * sm_count(), kDecThreads, 0, static_cast<cudaStream_t>(stream)>>>(
