@@ -59,8 +59,11 @@ def test_all_encodings_decode(gpu_backend, ops_golden):
 
 
 @pytest.mark.parametrize('rows,cols', [(1, 128), (7, 4), (130, 512), (300, 1000), (257, 6144), (64, 7168),
-                                       (3, 13000), (5, 13001)])
+                                       (3, 13000), (5, 13001), (4100, 1024), (4097, 1040)])
 def test_matvec_matches_oracle(gpu_backend, ops_golden, rows, cols):
+    """Below 4096 rows four warps per row; above, one row per warp with the
+    word mapping (widths a multiple of 512: 4100 x 1024, a partial last CTA)
+    or 16 bytes per lane (4097 x 1040)."""
     weight, scales, x = _case(rows, cols, rows + cols)
     got = gpu_backend.fp8_matvec(weight, scales, x)
     assert_close_dot(got, _want(weight, scales, x), _decoded(weight, scales, ops_golden), x)
